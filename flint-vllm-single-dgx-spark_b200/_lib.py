@@ -1,0 +1,91 @@
+"""ctypes binding of ``libflint_b200.so`` (the C ABI in ``include/flint_b200.h``).
+
+There is no fallback: if the library is missing or no sm_100 device is present, the ops raise.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libflint_b200.so")
+
+_lock = threading.Lock()
+_lib = None
+
+P = ctypes.c_void_p
+I64 = ctypes.c_int64
+I32 = ctypes.c_int
+F32 = ctypes.c_float
+
+# name -> (restype, argtypes); every symbol declared in include/flint_b200.h
+SIGNATURES: dict[str, tuple] = {
+    "flint_version": (I32, []),
+    "flint_error_string": (ctypes.c_char_p, [I32]),
+    "flint_lm_head_workspace_bytes": (I64, []),
+    "flint_lm_head_nv4": (I32, [P, I64, I64, P, P, F32, I64, I64, P, I64, P, P, I32, P]),
+}
+
+
+class FlintError(RuntimeError):
+    pass
+
+
+def lib() -> ctypes.CDLL:
+    """Load (once) the in-tree library.  Raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise FlintError(f"{LIB_PATH} is missing: build it with __graft_entry__.build() "
+                                 f"(or python flint-vllm-single-dgx-spark_b200/build.py)")
+            h = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(h, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = h
+    return _lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = lib().flint_error_string(rc).decode()
+        raise FlintError(f"{what} failed: {msg} (code {rc})")
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def require_cuda(t: torch.Tensor, what: str) -> None:
+    if not t.is_cuda:
+        raise FlintError(f"{what}: tensors must be on a CUDA device (no CPU path)")
+
+
+# ---------------------------------------------------------------------------------------------------------
+# Persistent workspaces: one zero-filled buffer per (device, kind), allocated before any CUDA graph capture
+# (the kernels leave them zeroed, so captured graphs keep valid, reusable pointers).
+# ---------------------------------------------------------------------------------------------------------
+_workspaces: dict[tuple[int, str], torch.Tensor] = {}
+
+
+def workspace(device: torch.device, kind: str, nbytes: int) -> torch.Tensor:
+    key = (device.index if device.index is not None else torch.cuda.current_device(), kind)
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < nbytes:
+        if torch.cuda.is_current_stream_capturing():
+            raise FlintError(f"workspace '{kind}' must be created before CUDA graph capture "
+                             f"(run the op once eagerly first)")
+        ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+        _workspaces[key] = ws
+    return ws

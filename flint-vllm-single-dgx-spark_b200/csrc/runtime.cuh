@@ -1,0 +1,32 @@
+// Host-side launch helpers shared by the entry points.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/flint_b200.h"
+
+namespace flint {
+
+// SM count of the current device (cached), or -1 if there is none / it is not sm_10x.
+int num_sms(int* dev_out = nullptr);
+
+inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Launch with optional programmatic dependent launch (PDL); returns FLINT_OK / FLINT_ERR_LAUNCH.
+template <typename... KArgs, typename... Args>
+int launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, void* stream, int pdl, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+  return e == cudaSuccess ? FLINT_OK : FLINT_ERR_LAUNCH;
+}
+
+}  // namespace flint

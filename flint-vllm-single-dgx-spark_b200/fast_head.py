@@ -1,0 +1,138 @@
+"""NVFP4 LM head for decode -- drop-in for the reference's ``fast/fast_head.py`` (nv4 mode).
+
+Same entry points and argument meaning as the reference:
+
+* ``nv4_logits_fma(x, P, S, gs, out)`` / ``nv4_logits(x, P, S, gs, out)`` (fast/fast_head.py:118-129):
+  fp32 logits ``gs * x @ dequant(P, S)^T`` into ``out``; tuning keywords are accepted and ignored.
+* ``FastHead(weight, scale, mode, nv4)`` (fast/fast_head.py:182-215) with ``__call__(x) -> logits``.
+* ``compute_logits(model, hidden_states)`` (fast/fast_head.py:360-381): logits or ``None`` for the caller's
+  stock path, env-gated by ``FLINT_FAST_HEAD`` / ``FLINT_FAST_HEAD_MAX_M``.
+
+Additions for the fused path: ``FastHead.greedy(x)`` (logits + argmax in the same pass) and
+``FastHead.sample(...)`` (top-k -> top-p -> seeded draw without materialising the logits).
+The reference's inexact ``int2`` mode (coarse INT2 logits + top-C refine) is not provided.
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import torch
+
+from . import ops as _ops
+
+ENABLED = os.environ.get("FLINT_FAST_HEAD", "0") == "1"
+MAX_M = int(os.environ.get("FLINT_FAST_HEAD_MAX_M", "8"))
+MODE = os.environ.get("FLINT_FAST_HEAD_MODE", "nv4")
+GROUP = 16
+_EMPTY: dict[torch.device, tuple[torch.Tensor, torch.Tensor]] = {}
+
+
+def _dummies(dev: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
+    d = _EMPTY.get(dev)
+    if d is None:
+        d = _EMPTY[dev] = (torch.empty((1, 1), dtype=torch.float32, device=dev),
+                           torch.empty((1,), dtype=torch.int32, device=dev))
+    return d
+
+
+def _scale_value(gs) -> float:
+    return float(gs.item()) if isinstance(gs, torch.Tensor) else float(gs)
+
+
+def nv4_logits_fma(x, P, S, gs, out, BN=None, BK=None, nw=None, stages=None):
+    """M == 1 exact NVFP4 head (reference: fast/fast_head.py:95-121).  Returns ``out``."""
+    return nv4_logits(x, P, S, gs, out)
+
+
+def nv4_logits(x, P, S, gs, out, BN=None, BK=None, nw=None, stages=None):
+    """M <= 8 exact NVFP4 head (reference: fast/fast_head.py:68-90,124-129).  Returns ``out``."""
+    x = x.contiguous()
+    _, tok = _dummies(x.device)
+    torch.ops.flint_b200.lm_head_nv4(x, P, S.view(torch.uint8), _scale_value(gs), out, tok, True, False)
+    return out
+
+
+class FastHead:
+    """NVFP4 LM head (reference: fast/fast_head.py:182-215, mode ``nv4`` only).
+
+    weight: the head's bf16 weight (kept for the caller, unused by the kernels) or None;
+    scale: fp32 global scale applied to the fp32 logits (``lm_head.weight_scale_2``);
+    nv4: (P u8 [V, K/2], S E4M3 [V, K/16]) ModelOpt tensors."""
+
+    def __init__(self, weight, scale, mode="nv4", nv4=None):
+        if mode != "nv4":
+            raise NotImplementedError("only the exact 'nv4' head is provided (the inexact 'int2' mode is not)")
+        if nv4 is None:
+            raise ValueError("FastHead(mode='nv4') needs nv4=(P, S)")
+        self.W = weight
+        self.scale = _scale_value(scale)
+        self.P = nv4[0].contiguous()
+        self.S = nv4[1].contiguous().view(torch.uint8)
+        self.V, self.K = self.P.shape[0], self.P.shape[1] * 2
+        self.mode = mode
+
+    def __call__(self, x):
+        m = x.shape[0]
+        out = torch.empty((m, self.V), dtype=torch.float32, device=x.device)
+        return nv4_logits(x, self.P, self.S, self.scale, out)
+
+    def greedy(self, x, want_logits: bool = False):
+        """-> (token ids int32 [M], logits fp32 [M, V] or None), one pass over the head."""
+        x = x.contiguous()
+        m = x.shape[0]
+        tok = torch.empty((m,), dtype=torch.int32, device=x.device)
+        if want_logits:
+            out = torch.empty((m, self.V), dtype=torch.float32, device=x.device)
+        else:
+            out = _dummies(x.device)[0]
+        torch.ops.flint_b200.lm_head_nv4(x, self.P, self.S, self.scale, out, tok, want_logits, True)
+        return tok, (out if want_logits else None)
+
+
+# ---------------------------------------------------------------------------------------------------------
+# integration hook (reference: fast/fast_head.py:285-312,360-381)
+# ---------------------------------------------------------------------------------------------------------
+_state = {"head": None, "failed": False, "bypass": 0}
+
+
+def _log(msg):
+    print(f"[flint-fast-head] {msg}", file=sys.stderr, flush=True)
+
+
+def _build(model):
+    """The model exposes its NVFP4 head as ``model.lm_head.{weight (u8), weight_scale (E4M3), weight_scale_2}``
+    and an optional ``model.logits_processor.scale`` (fp32, multiplies the logits)."""
+    lm = model.lm_head
+    P = getattr(lm, "weight", None)
+    S = getattr(lm, "weight_scale", None)
+    gs = getattr(lm, "weight_scale_2", None)
+    ok = (P is not None and S is not None and gs is not None and P.dtype == torch.uint8 and P.dim() == 2
+          and S.shape[0] == P.shape[0] and getattr(lm, "tp_size", 1) == 1)
+    if not ok:
+        _log("fast head disabled: unsupported lm_head")
+        _state["failed"] = True
+        return
+    lp = getattr(model, "logits_processor", None)
+    scale = _scale_value(gs) * float(getattr(lp, "scale", 1.0) if lp is not None else 1.0)
+    _state["head"] = FastHead(None, scale, "nv4", (P, S))
+    _state["org_vocab"] = int(getattr(lp, "org_vocab_size", P.shape[0]) if lp is not None else P.shape[0])
+
+
+def compute_logits(model, hidden_states):
+    """Returns logits (fp32, [M, org_vocab]) or None to let the caller use the stock path."""
+    if _state["bypass"] > 0:
+        return None
+    m = hidden_states.shape[0]
+    if m < 1 or m > MAX_M:
+        return None
+    if not ENABLED or _state["failed"]:
+        return None
+    if _state["head"] is None:
+        if torch.cuda.is_current_stream_capturing():
+            return None
+        _build(model)
+        if _state["head"] is None:
+            return None
+    out = _state["head"](hidden_states)
+    return out[:, :_state["org_vocab"]]
