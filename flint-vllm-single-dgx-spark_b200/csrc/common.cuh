@@ -30,11 +30,6 @@ __device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
   return r;
 }
-__device__ __forceinline__ uint32_t ldg_stream_u16(const void* p) {
-  unsigned short r;
-  asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(r) : "l"(p));
-  return r;
-}
 __device__ __forceinline__ uint32_t ldg_stream_u32(const void* p) {
   uint32_t r;
   asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
@@ -114,17 +109,16 @@ __device__ __forceinline__ unsigned long long shfl_xor_u64(unsigned long long v,
 }
 
 // ------------------------------------------------------------------------------------------------------------
-// Activation staging: x bf16 [M, K] (row stride ldx) -> f16 in shared memory, rescaled per token by 2^shift[m]
-// and permuted so that the mma B fragments of a warp are bank-conflict free:
-//   k = 128*c + 32*t + 4*j + e   (chunk c, thread-in-quad t, mma step j, element e)  ->  128*c + 16*j + 4*t + e
-// Row stride is K + 16 halves.  Rows M..7 are never read (B fragments of lanes with g >= M are zero).
+// Activation staging: x bf16 [M, K] (row stride ldx) -> f16 in shared memory, rescaled per token by 2^shift[m].
+// Lane quad t of a warp consumes k = 128*c + 32*t + v (v = 0..31) of chunk c as four 16-byte units q = v/8; unit q of
+// lanes t = 2, 3 is stored at q ^ 2, and rows are K + 8 halves apart, so each 128-bit B-fragment read of a warp
+// (up to 2 token rows per quarter-warp) is bank-conflict free.  Rows M..7 are never read.
 // ------------------------------------------------------------------------------------------------------------
-__host__ __device__ constexpr int xs_stride(int K) { return K + 16; }
+__host__ __device__ constexpr int xs_stride(int K) { return K + 8; }
 
 __device__ __forceinline__ int xs_perm(int k) {
-  const int c = k >> 7, r = k & 127;
-  const int t = r >> 5, j = (r >> 2) & 7, e = r & 3;
-  return (c << 7) + (j << 4) + (t << 2) + e;
+  const int t = (k >> 5) & 3, q = (k >> 3) & 3;
+  return (k & ~31) + ((q ^ ((t >> 1) << 1)) << 3) + (k & 7);
 }
 
 // All threads of the block call this.  red must hold >= blockDim/32 * 8 floats.
@@ -156,66 +150,6 @@ __device__ __forceinline__ void stage_x_f16(const bf16* __restrict__ x, int64_t 
     for (int k = tid; k < K; k += nt) row[xs_perm(k)] = __float2half_rn(ldexpf(__bfloat162float(x[m * ldx + k]), s));
   }
   __syncthreads();
-}
-
-// ------------------------------------------------------------------------------------------------------------
-// Warp tile: 16 weight rows (g and g+8 per lane) x 128-k chunks, streamed through registers.
-// Lane (g = lane/4, t = lane%4) holds, per chunk, 16 bytes of codes of each of its two rows (k = 32t .. 32t+31
-// of the chunk) and the 2 E4M3 scales of those k (blocks 2t, 2t+1 of the chunk).
-// ------------------------------------------------------------------------------------------------------------
-template <int CPS>
-struct WStage {
-  uint4 q[CPS][2];
-  uint32_t s[CPS];
-};
-
-template <int CPS>
-__device__ __forceinline__ void load_stage(WStage<CPS>& st, const uint8_t* __restrict__ wg, const uint8_t* __restrict__ wg8,
-                                           const uint8_t* __restrict__ sg, const uint8_t* __restrict__ sg8, int chunk0, int t) {
-#pragma unroll
-  for (int c = 0; c < CPS; ++c) {
-    const int ch = chunk0 + c;
-    st.q[c][0] = ldg_stream_v4(wg + ch * 64 + t * 16);
-    st.q[c][1] = ldg_stream_v4(wg8 + ch * 64 + t * 16);
-    st.s[c] = ldg_stream_u16(sg + ch * 8 + 2 * t) | (ldg_stream_u16(sg8 + ch * 8 + 2 * t) << 16);
-  }
-}
-
-// acc[2][4]: two independent accumulator sets (even / odd mma steps) to halve the mma dependency chain.
-// xrow: this lane's token row of the staged activations (nullptr-equivalent handled by `active`).
-template <int CPS>
-__device__ __forceinline__ void compute_stage(const WStage<CPS>& st, const __half* xrow, bool active, int chunk0, int t,
-                                              float (&acc)[2][4]) {
-#pragma unroll
-  for (int c = 0; c < CPS; ++c) {
-    const int ch = chunk0 + c;
-    const uint32_t sc_g = e4m3x2_to_f16x2(st.s[c] & 0xFFFFu);
-    const uint32_t sc_g8 = e4m3x2_to_f16x2(st.s[c] >> 16);
-    const uint32_t sa_g = bcast_lo(sc_g), sb_g = bcast_hi(sc_g);
-    const uint32_t sa_g8 = bcast_lo(sc_g8), sb_g8 = bcast_hi(sc_g8);
-    const uint32_t wg[4] = {st.q[c][0].x, st.q[c][0].y, st.q[c][0].z, st.q[c][0].w};
-    const uint32_t wg8[4] = {st.q[c][1].x, st.q[c][1].y, st.q[c][1].z, st.q[c][1].w};
-#pragma unroll
-    for (int wd = 0; wd < 4; ++wd) {
-      uint32_t dg[4], dg8[4];
-      e2m1x8_to_f16x2(wg[wd], dg);
-      e2m1x8_to_f16x2(wg8[wd], dg8);
-      const uint32_t s_g = wd < 2 ? sa_g : sb_g;     // values 8wd .. 8wd+7: block 2t for wd < 2, else 2t+1
-      const uint32_t s_g8 = wd < 2 ? sa_g8 : sb_g8;
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {                  // mma step j = 2*wd + h: bytes 2h, 2h+1 of the word
-        const int j = 2 * wd + h;
-        uint32_t a[4];
-        a[0] = hmul2(dg[2 * h], s_g);
-        a[1] = hmul2(dg8[2 * h], s_g8);
-        a[2] = hmul2(dg[2 * h + 1], s_g);
-        a[3] = hmul2(dg8[2 * h + 1], s_g8);
-        uint2 b = make_uint2(0u, 0u);
-        if (active) b = *reinterpret_cast<const uint2*>(xrow + ch * 128 + 16 * j + 4 * t);
-        mma_f16(acc[j & 1], a, b.x, b.y);
-      }
-    }
-  }
 }
 
 }  // namespace flint

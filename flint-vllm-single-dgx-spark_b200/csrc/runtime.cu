@@ -1,5 +1,8 @@
 // Library-wide host helpers: version, error strings, per-device properties.
 #include "runtime.cuh"
+#include "tma.cuh"
+
+#include <cudaTypedefs.h>
 
 namespace flint {
 
@@ -17,6 +20,35 @@ int num_sms(int* dev_out) {
     cache[dev] = n;
   }
   return cache[dev];
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+int encode_u8_2d(CUtensorMap* map, const void* base, uint64_t cols_bytes, uint64_t rows, uint64_t row_stride_bytes,
+                 uint32_t box_cols, uint32_t box_rows, bool swizzle128) {
+  auto fn = get_encode_fn();
+  if (!fn) return FLINT_ERR_DEVICE;
+  if (!aligned(base, 16) || row_stride_bytes % 16 != 0) return FLINT_ERR_ALIGN;
+  cuuint64_t dims[2] = {cols_bytes, rows};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? FLINT_OK : FLINT_ERR_ALIGN;
 }
 
 }  // namespace flint

@@ -1,0 +1,72 @@
+// TMA (cp.async.bulk.tensor) + mbarrier helpers for the weight-streaming kernels.
+//
+// Weights are fetched as 2-D tiles of their row-major byte image: codes [rows, K/2] u8 in boxes of 128 B x 128 rows
+// with the 128-byte swizzle (16-byte unit u of row r lands at unit u ^ (r & 7)), and block scales [rows, K/16] u8
+// in boxes of 16 B x 128 rows without swizzle.  No multicast is used anywhere.
+// Every wait is bounded: after FLINT_WAIT_LIMIT polls the waiter records an error and stops waiting.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/flint_b200.h"
+
+#ifndef FLINT_WAIT_LIMIT
+#define FLINT_WAIT_LIMIT (1u << 22)
+#endif
+
+namespace flint {
+
+// status word bits written by kernels into their workspace (0 = healthy)
+enum : unsigned { STATUS_WAIT_TIMEOUT = 1u };
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n.reg .pred p;\n"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase of the given parity; returns false (and sets *status) on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, unsigned* status) {
+  for (unsigned i = 0; i < FLINT_WAIT_LIMIT; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  if (status) atomicOr(status, STATUS_WAIT_TIMEOUT);
+  return false;
+}
+
+// 2-D tensor tile load into shared memory, completion counted on `bar` (transaction bytes).
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ---- host: tensor-map encoding through the driver entry point (no libcuda link needed) ----
+int encode_u8_2d(CUtensorMap* map, const void* base, uint64_t cols_bytes, uint64_t rows, uint64_t row_stride_bytes,
+                 uint32_t box_cols, uint32_t box_rows, bool swizzle128);
+
+}  // namespace flint

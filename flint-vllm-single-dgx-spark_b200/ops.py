@@ -44,7 +44,7 @@ def lm_head_nv4(x: torch.Tensor, P: torch.Tensor, S: torch.Tensor, gs: float, lo
         raise _lib.FlintError("lm_head_nv4: logits must be fp32 [M, V]")
     if write_tokens and (tokens.dtype != torch.int32 or tokens.numel() < M):
         raise _lib.FlintError("lm_head_nv4: tokens must be int32 [M]")
-    ws = _lib.workspace(x.device, "lm_head", lib().flint_lm_head_workspace_bytes()) if write_tokens else None
+    ws = _lib.workspace(x.device, "lm_head", lib().flint_lm_head_workspace_bytes())
     rc = lib().flint_lm_head_nv4(ptr(x), x.stride(0), M, ptr(_u8(P)), ptr(_u8(S)), float(gs), V, K,
                                  ptr(logits) if write_logits else None, logits.stride(0) if write_logits else 0,
                                  ptr(tokens) if write_tokens else None, ptr(ws), 0, stream_ptr(x.device))

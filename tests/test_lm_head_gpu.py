@@ -51,7 +51,7 @@ def check(got_logits, got_tok, ref):
 
 @needs_cuda
 @pytest.mark.parametrize("V,K,M", [(1000, 2048, 1), (4096, 2048, 8), (333, 256, 3), (2048, 4096, 2), (160, 768, 1),
-                                   (16, 128, 5)])
+                                   (16, 256, 5)])
 def test_head_small(fb, V, K, M):
     rng = np.random.default_rng(V * 7 + K + M)
     P, S, gs = make_head(rng, V, K)
