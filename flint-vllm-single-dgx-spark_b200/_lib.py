@@ -27,6 +27,19 @@ SIGNATURES: dict[str, tuple] = {
     "flint_error_string": (ctypes.c_char_p, [I32]),
     "flint_lm_head_workspace_bytes": (I64, []),
     "flint_lm_head_nv4": (I32, [P, I64, I64, P, P, F32, I64, I64, P, I64, P, P, I32, P]),
+    "flint_moe_workspace_bytes": (I64, [I64]),
+    "flint_moe_route": (I32, [P, I64, P, P, F32, P, I64, I64, I64, I64, I32, P, P, P, P, P, P, I32, P]),
+    "flint_moe_up": (I32, [P, I64, I64, P, I64, P, P, P, I64, I64, I64, P, P, I32, P]),
+    "flint_moe_down": (I32, [P, I64, P, P, I64, P, P, P, I64, I64, I64, P, P, I32, P]),
+    "flint_moe_align": (I32, [P, I64, I64, I64, P, I64, P, I64, P, P, I32, P]),
+    "flint_attn_proj_workspace_bytes": (I64, []),
+    "flint_attn_qkv": (I32, [P, I64, P, P, F32, P, P, P, I64, I64, I64, I64, I64, I32, P, P, F32, P, P, I64, P, P, I64,
+                             I64, I64, I64, P, P, P, P, P, I32, P]),
+    "flint_attn_o": (I32, [P, I64, I64, P, P, P, I64, I64, P, P, I32, P]),
+    "flint_decode_attention_splits": (I64, [I64, I64]),
+    "flint_decode_attention_workspace_bytes": (I64, [I64, I64, I64]),
+    "flint_decode_attention": (I32, [P, I64, P, I64, I64, I64, I64, P, I64, I64, P, P, I64, F32, I64, I64, P, I64, I64, P,
+                                     I32, P]),
 }
 
 
@@ -77,6 +90,7 @@ def require_cuda(t: torch.Tensor, what: str) -> None:
 # (the kernels leave them zeroed, so captured graphs keep valid, reusable pointers).
 # ---------------------------------------------------------------------------------------------------------
 _workspaces: dict[tuple[int, str], torch.Tensor] = {}
+_retired: list[torch.Tensor] = []     # grown-out workspaces stay alive: captured graphs may still point at them
 
 
 def workspace(device: torch.device, kind: str, nbytes: int) -> torch.Tensor:
@@ -86,6 +100,8 @@ def workspace(device: torch.device, kind: str, nbytes: int) -> torch.Tensor:
         if torch.cuda.is_current_stream_capturing():
             raise FlintError(f"workspace '{kind}' must be created before CUDA graph capture "
                              f"(run the op once eagerly first)")
+        if ws is not None:
+            _retired.append(ws)
         ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
         _workspaces[key] = ws
     return ws

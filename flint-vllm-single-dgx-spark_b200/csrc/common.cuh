@@ -121,35 +121,126 @@ __device__ __forceinline__ int xs_perm(int k) {
   return (k & ~31) + ((q ^ ((t >> 1) << 1)) << 3) + (k & 7);
 }
 
-// All threads of the block call this.  red must hold >= blockDim/32 * 8 floats.
+// Stage `rows` activation rows (src + r*ld, bf16, K columns, 16-byte aligned rows) as f16 into xs (row stride
+// xs_stride(K)) with a per-row power-of-two rescale shift[r].  Called by threads [0, nthreads) of the block (a multiple
+// of 32), which synchronise on named barrier `bar` (0 = __syncthreads when nthreads == blockDim.x).
+// One global pass: raw bf16 goes to its permuted place in xs while the row maxima accumulate (shared atomicMax on
+// the non-negative float bits), then each element is converted in place.  red: >= rows floats.
+__device__ __forceinline__ void stage_rows_f16(const bf16* __restrict__ src, int64_t ld, int rows, int K, __half* xs,
+                                               int* shift, float* red, int nthreads, int bar) {
+  const int tid = threadIdx.x;
+  const int K8 = K >> 3, n = rows * K8;
+  auto sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthreads) : "memory"); };
+  int* redi = reinterpret_cast<int*>(red);
+  for (int r = tid; r < rows; r += nthreads) redi[r] = 0;
+  sync();
+  for (int idx = tid; idx < n; idx += nthreads) {
+    const int r = idx / K8, k8 = idx - r * K8;
+    const uint4 v = reinterpret_cast<const uint4*>(src + r * ld)[k8];
+    float f[8];
+    bf16x8_to_f32(v, f);
+    float mx = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(f[j]));
+    atomicMax(&redi[r], __float_as_int(mx));
+    *reinterpret_cast<uint4*>(xs + r * xs_stride(K) + xs_perm(k8 * 8)) = v;   // 8 consecutive k: one 16-byte unit
+  }
+  sync();
+  for (int r = tid; r < rows; r += nthreads) {
+    const float mx = __int_as_float(redi[r]);
+    int s = 0;
+    if (mx > 0.f && !(mx != mx) && mx <= 3.0e38f) s = 14 - ((int)((__float_as_uint(mx) >> 23) & 0xFF) - 127);
+    shift[r] = s;
+  }
+  sync();
+  for (int idx = tid; idx < n; idx += nthreads) {
+    const int r = idx / K8, k8 = idx - r * K8;
+    uint4* p = reinterpret_cast<uint4*>(xs + r * xs_stride(K) + xs_perm(k8 * 8));
+    float f[8];
+    bf16x8_to_f32(*p, f);
+    const int s = shift[r];
+    uint32_t h[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __half2 v = __floats2half2_rn(ldexpf(f[2 * j], s), ldexpf(f[2 * j + 1], s));
+      h[j] = *reinterpret_cast<uint32_t*>(&v);
+    }
+    *p = make_uint4(h[0], h[1], h[2], h[3]);
+  }
+  sync();
+}
+
+// s = x (+ res) in fp32; res_out = bf16(s) (global, optional); xn = bf16(s * rsqrt(mean(s^2) + eps) * w) into shared
+// memory (w == nullptr: xn = bf16(s)).  Threads [0, nthreads) with named barrier `bar`.  The sum of squares is
+// reduced in a fixed order (per-thread chains, xor butterfly, warps in order), identical in every CTA that runs it.
+// sbuf: fp32 shared scratch [M][H]; red: >= (nthreads/32) * 8 floats; M <= 8; rows of x / res 16-byte aligned.
+__device__ __forceinline__ void add_rmsnorm_smem(const bf16* x, int64_t ldx, const bf16* res, const bf16* __restrict__ w,
+                                                 float eps, int M, int H, float* sbuf, bf16* xn, bf16* res_out, float* red,
+                                                 int nthreads, int bar) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = nthreads >> 5, H8 = H >> 3;
+  auto sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthreads) : "memory"); };
+  float ss[8];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    ss[m] = 0.f;
+    if (m < M) {
+      for (int k8 = tid; k8 < H8; k8 += nthreads) {
+        float a[8];
+        bf16x8_to_f32(reinterpret_cast<const uint4*>(x + m * ldx)[k8], a);
+        if (res) {
+          float b[8];
+          bf16x8_to_f32(reinterpret_cast<const uint4*>(res + m * ldx)[k8], b);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) a[j] += b[j];
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss[m] = fmaf(a[j], a[j], ss[m]);
+        float4* d = reinterpret_cast<float4*>(sbuf + m * H + k8 * 8);
+        d[0] = make_float4(a[0], a[1], a[2], a[3]);
+        d[1] = make_float4(a[4], a[5], a[6], a[7]);
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    float v = ss[m];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[warp * 8 + m] = v;
+  }
+  sync();
+  for (int idx = tid; idx < M * H8; idx += nthreads) {
+    const int m = idx / H8, k8 = idx - m * H8;
+    float rs = 1.f;
+    if (w) {
+      float tot = 0.f;
+      for (int ww = 0; ww < nw; ++ww) tot += red[ww * 8 + m];
+      rs = rsqrtf(tot / (float)H + eps);
+    }
+    const float4* sp = reinterpret_cast<const float4*>(sbuf + m * H + k8 * 8);
+    const float4 s0 = sp[0], s1 = sp[1];
+    const float a[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    float wf[8];
+    if (w) bf16x8_to_f32(reinterpret_cast<const uint4*>(w)[k8], wf);
+    uint32_t pk[4], rk[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __nv_bfloat162 n2 = w ? __floats2bfloat162_rn(a[2 * j] * rs * wf[2 * j], a[2 * j + 1] * rs * wf[2 * j + 1])
+                            : __floats2bfloat162_rn(a[2 * j], a[2 * j + 1]);
+      pk[j] = *reinterpret_cast<uint32_t*>(&n2);
+      __nv_bfloat162 r2 = __floats2bfloat162_rn(a[2 * j], a[2 * j + 1]);
+      rk[j] = *reinterpret_cast<uint32_t*>(&r2);
+    }
+    reinterpret_cast<uint4*>(xn + m * H)[k8] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    if (res_out) reinterpret_cast<uint4*>(res_out + m * H)[k8] = make_uint4(rk[0], rk[1], rk[2], rk[3]);
+  }
+  sync();
+}
+
+// Whole-block variant (the LM head): all threads, __syncthreads.
 __device__ __forceinline__ void stage_x_f16(const bf16* __restrict__ x, int64_t ldx, int M, int K, __half* xs,
                                             int* shift, float* red) {
-  const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5, nw = nt >> 5;
-  for (int m = 0; m < M; ++m) {
-    float mx = 0.f;
-    for (int k = tid; k < K; k += nt) mx = fmaxf(mx, fabsf(__bfloat162float(x[m * ldx + k])));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (lane == 0) red[warp * 8 + m] = mx;
-  }
-  __syncthreads();
-  if (tid < M) {
-    float mx = 0.f;
-    for (int w = 0; w < nw; ++w) mx = fmaxf(mx, red[w * 8 + tid]);
-    int s = 0;
-    if (mx > 0.f && !(mx != mx) && mx <= 3.0e38f) {
-      const int e = (int)((__float_as_uint(mx) >> 23) & 0xFF) - 127;   // bf16 inputs are never subnormal here
-      s = 14 - e;
-    }
-    shift[tid] = s;
-  }
-  __syncthreads();
-  for (int m = 0; m < M; ++m) {
-    const int s = shift[m];
-    __half* row = xs + m * xs_stride(K);
-    for (int k = tid; k < K; k += nt) row[xs_perm(k)] = __float2half_rn(ldexpf(__bfloat162float(x[m * ldx + k]), s));
-  }
-  __syncthreads();
+  stage_rows_f16(x, ldx, M, K, xs, shift, red, blockDim.x, 0);
 }
 
 }  // namespace flint

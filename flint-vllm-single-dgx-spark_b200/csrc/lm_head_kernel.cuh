@@ -31,7 +31,7 @@ lm_head_kernel(const __grid_constant__ CUtensorMap map_codes, const __grid_const
   uint8_t* ring_scales = smem + NS * G::code_bytes;
   __half* xs = reinterpret_cast<__half*>(smem + NS * G::bytes);
   __shared__ uint64_t bar_full[NS], bar_empty[NS];
-  __shared__ float red[(NW + 1) * 8];
+  __shared__ float red[(NW + 1) * 8];   // stage_rows_f16 scratch: warps x tokens
   __shared__ int shift[8];
   __shared__ unsigned long long wbest[NW][8];
   __shared__ int s_last;

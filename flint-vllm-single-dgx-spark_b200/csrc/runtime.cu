@@ -51,6 +51,23 @@ int encode_u8_2d(CUtensorMap* map, const void* base, uint64_t cols_bytes, uint64
   return r == CUDA_SUCCESS ? FLINT_OK : FLINT_ERR_ALIGN;
 }
 
+int encode_bf16_4d(CUtensorMap* map, const void* base, const uint64_t dims[4], const uint64_t strides_bytes[3],
+                   const uint32_t box[4]) {
+  auto fn = get_encode_fn();
+  if (!fn) return FLINT_ERR_DEVICE;
+  if (!aligned(base, 16)) return FLINT_ERR_ALIGN;
+  for (int i = 0; i < 3; ++i)
+    if (strides_bytes[i] % 16 != 0) return FLINT_ERR_ALIGN;
+  cuuint64_t d[4] = {dims[0], dims[1], dims[2], dims[3]};
+  cuuint64_t s[3] = {strides_bytes[0], strides_bytes[1], strides_bytes[2]};
+  cuuint32_t b[4] = {box[0], box[1], box[2], box[3]};
+  cuuint32_t e[4] = {1, 1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), d, s, b, e,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? FLINT_OK : FLINT_ERR_ALIGN;
+}
+
 }  // namespace flint
 
 extern "C" int flint_version(void) { return 100; }

@@ -29,4 +29,26 @@ int launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, void* str
   return e == cudaSuccess ? FLINT_OK : FLINT_ERR_LAUNCH;
 }
 
+// Launch with a thread-block cluster of `cluster` CTAs along x (grid.x must be a multiple), optional PDL.
+template <typename... KArgs, typename... Args>
+int launch_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, void* stream, int pdl, int cluster,
+                   Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = cluster;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 2 : 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+  return e == cudaSuccess ? FLINT_OK : FLINT_ERR_LAUNCH;
+}
+
 }  // namespace flint

@@ -61,6 +61,13 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
 }
+// 4-D tensor tile load (x, y, z, w) into shared memory.
+__device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* map, int x, int y, int z, int w, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];"
+      ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+      : "memory");
+}
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -68,5 +75,8 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
 // ---- host: tensor-map encoding through the driver entry point (no libcuda link needed) ----
 int encode_u8_2d(CUtensorMap* map, const void* base, uint64_t cols_bytes, uint64_t rows, uint64_t row_stride_bytes,
                  uint32_t box_cols, uint32_t box_rows, bool swizzle128);
+// bf16 4-D map (dims innermost first, strides in bytes for dims 1..3), 128-byte swizzle.
+int encode_bf16_4d(CUtensorMap* map, const void* base, const uint64_t dims[4], const uint64_t strides_bytes[3],
+                   const uint32_t box[4]);
 
 }  // namespace flint

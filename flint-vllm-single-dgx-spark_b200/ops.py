@@ -54,3 +54,191 @@ def lm_head_nv4(x: torch.Tensor, P: torch.Tensor, S: torch.Tensor, gs: float, lo
 @lm_head_nv4.register_fake
 def _(x, P, S, gs, logits, tokens, write_logits, write_tokens):
     return None
+
+
+# ------------------------------------------------------------------------------------------------------------
+# (1) MoE decode and (2) deterministic align
+# ------------------------------------------------------------------------------------------------------------
+def _moe_ws(device: torch.device, H: int) -> torch.Tensor:
+    return _lib.workspace(device, "moe", lib().flint_moe_workspace_bytes(H))
+
+
+def _bf16_2d(t: torch.Tensor, what: str) -> None:
+    if t.dtype != torch.bfloat16 or t.dim() != 2 or t.stride(1) != 1:
+        raise _lib.FlintError(f"{what}: expected a bf16 matrix with unit inner stride, got {t.dtype} {tuple(t.shape)}")
+
+
+@torch.library.custom_op(f"{NS}::moe_route", mutates_args=("logits", "topk_ids", "topk_weights", "xn", "res_out"))
+def moe_route(x: torch.Tensor, res: torch.Tensor | None, norm_w: torch.Tensor | None, eps: float, gate_w: torch.Tensor,
+              topk: int, score_fn: int, logits: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
+              xn: torch.Tensor, res_out: torch.Tensor, write_xn: bool, write_res: bool) -> None:
+    """Router: (residual add +) RMSNorm, bf16 logits, top-k (softmax: score_fn 0, sigmoid: 1), renormalised weights."""
+    _lib.require_cuda(x, "moe_route")
+    _bf16_2d(x, "moe_route x")
+    M, H = x.shape
+    E = gate_w.shape[0]
+    if gate_w.dtype != torch.bfloat16 or gate_w.shape[1] != H or not gate_w.is_contiguous():
+        raise _lib.FlintError("moe_route: gate_w must be contiguous bf16 [E, H]")
+    if res is not None and (res.shape != x.shape or res.stride() != x.stride() or res.dtype != torch.bfloat16):
+        raise _lib.FlintError("moe_route: res must match x")
+    rc = lib().flint_moe_route(ptr(x), x.stride(0), ptr(res), ptr(norm_w), float(eps), ptr(gate_w), M, H, E, topk,
+                               score_fn, ptr(logits), ptr(topk_ids), ptr(topk_weights), ptr(xn) if write_xn else None,
+                               ptr(res_out) if write_res else None, ptr(_moe_ws(x.device, H)), 0, stream_ptr(x.device))
+    check(rc, "flint_moe_route")
+
+
+@moe_route.register_fake
+def _(x, res, norm_w, eps, gate_w, topk, score_fn, logits, topk_ids, topk_weights, xn, res_out, write_xn, write_res):
+    return None
+
+
+@torch.library.custom_op(f"{NS}::moe_up", mutates_args=("act",))
+def moe_up(xn: torch.Tensor, topk_ids: torch.Tensor, w13: torch.Tensor, s13: torch.Tensor, g13: torch.Tensor,
+           act: torch.Tensor) -> None:
+    """act[m*topk+s] = bf16(silu(g) * u) of expert topk_ids[m, s] (NVFP4 gate/up rows [0:I] / [I:2I])."""
+    _lib.require_cuda(xn, "moe_up")
+    _bf16_2d(xn, "moe_up xn")
+    M, H = xn.shape
+    E, I2, Hh = w13.shape
+    topk = topk_ids.shape[-1]
+    if Hh * 2 != H or s13.shape != (E, I2, H // 16) or g13.numel() != E or act.shape != (M * topk, I2 // 2):
+        raise _lib.FlintError("moe_up: weight / activation shapes mismatch")
+    rc = lib().flint_moe_up(ptr(xn), xn.stride(0), M, ptr(topk_ids), topk, ptr(_u8(w13)), ptr(_u8(s13)), ptr(g13), E,
+                            I2 // 2, H, ptr(act), ptr(_moe_ws(xn.device, H)), 0, stream_ptr(xn.device))
+    check(rc, "flint_moe_up")
+
+
+@moe_up.register_fake
+def _(xn, topk_ids, w13, s13, g13, act):
+    return None
+
+
+@torch.library.custom_op(f"{NS}::moe_down", mutates_args=("out",))
+def moe_down(act: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor, w2: torch.Tensor, s2: torch.Tensor,
+             g2: torch.Tensor, out: torch.Tensor) -> None:
+    """out[m] = bf16(sum_s topk_weights[m, s] * bf16(act[m*topk+s] . W2[e] * g2[e]))."""
+    _lib.require_cuda(act, "moe_down")
+    E, H, Ih = w2.shape
+    M, topk = topk_ids.shape
+    if act.shape != (M * topk, Ih * 2) or s2.shape != (E, H, Ih // 8) or g2.numel() != E or out.shape != (M, H):
+        raise _lib.FlintError("moe_down: weight / activation shapes mismatch")
+    rc = lib().flint_moe_down(ptr(act), M, ptr(topk_ids), ptr(topk_weights), topk, ptr(_u8(w2)), ptr(_u8(s2)), ptr(g2), E,
+                              Ih * 2, H, ptr(out), ptr(_moe_ws(act.device, H)), 0, stream_ptr(act.device))
+    check(rc, "flint_moe_down")
+
+
+@moe_down.register_fake
+def _(act, topk_ids, topk_weights, w2, s2, g2, out):
+    return None
+
+
+@torch.library.custom_op(f"{NS}::moe_align", mutates_args=("sorted_ids", "expert_ids", "num_tokens_post_pad"))
+def moe_align(topk_ids: torch.Tensor, num_experts: int, block_size: int, sorted_ids: torch.Tensor,
+              expert_ids: torch.Tensor, num_tokens_post_pad: torch.Tensor) -> None:
+    """Deterministic moe_align_block_size (routes of an expert in ascending route order)."""
+    _lib.require_cuda(topk_ids, "moe_align")
+    ids = topk_ids if topk_ids.dtype == torch.int32 and topk_ids.is_contiguous() else topk_ids.contiguous().to(torch.int32)
+    status = _lib.workspace(topk_ids.device, "align_status", 4)
+    rc = lib().flint_moe_align(ptr(ids), ids.numel(), num_experts, block_size, ptr(sorted_ids), sorted_ids.numel(),
+                               ptr(expert_ids), expert_ids.numel(), ptr(num_tokens_post_pad), ptr(status), 0,
+                               stream_ptr(topk_ids.device))
+    check(rc, "flint_moe_align")
+
+
+@moe_align.register_fake
+def _(topk_ids, num_experts, block_size, sorted_ids, expert_ids, num_tokens_post_pad):
+    return None
+
+
+# ------------------------------------------------------------------------------------------------------------
+# (3) attention block
+# ------------------------------------------------------------------------------------------------------------
+def _proj_ws(device):
+    return _lib.workspace(device, "attn_proj", lib().flint_attn_proj_workspace_bytes())
+
+
+@torch.library.custom_op(f"{NS}::attn_qkv", mutates_args=("q_out", "qkv_out", "res_out", "k_cache", "v_cache"))
+def attn_qkv(x: torch.Tensor, res: torch.Tensor | None, norm_w: torch.Tensor, eps: float, W: torch.Tensor,
+             S: torch.Tensor, gs: torch.Tensor, num_q_heads: int, num_kv_heads: int, head_mode: bool,
+             q_norm_w: torch.Tensor | None, k_norm_w: torch.Tensor | None, eps_head: float,
+             positions: torch.Tensor | None, cos_sin: torch.Tensor | None, k_cache: torch.Tensor, v_cache: torch.Tensor,
+             slots: torch.Tensor | None, q_out: torch.Tensor, qkv_out: torch.Tensor, res_out: torch.Tensor,
+             write_res: bool) -> None:
+    """Fused (add +) RMSNorm + NVFP4 QKV GEMV (+ q/k norm, RoPE and paged KV write when head_mode)."""
+    _lib.require_cuda(x, "attn_qkv")
+    _bf16_2d(x, "attn_qkv x")
+    N, K = _check_nvfp4(W, S, "attn_qkv")
+    M, H = x.shape
+    if H != K or qkv_out.shape != (M, N) or (res is not None and res.stride() != x.stride()):
+        raise _lib.FlintError("attn_qkv: shape mismatch")
+    if head_mode and (k_cache.dim() != 4 or k_cache.stride(3) != 1 or v_cache.stride() != k_cache.stride()):
+        raise _lib.FlintError("attn_qkv: caches must be [blocks, block_size, kv_heads, head_dim] views, unit inner stride")
+    if head_mode and positions is not None and positions.dtype != torch.int64:
+        raise _lib.FlintError("attn_qkv: positions must be int64")
+    if head_mode and slots is not None and slots.dtype != torch.int64:
+        raise _lib.FlintError("attn_qkv: slots must be int64")
+    cs = cos_sin if (head_mode and cos_sin is not None) else None
+    rc = lib().flint_attn_qkv(
+        ptr(x), x.stride(0), ptr(res), ptr(norm_w), float(eps), ptr(_u8(W)), ptr(_u8(S)), ptr(gs), M, H, N, num_q_heads,
+        num_kv_heads, 1 if head_mode else 0, ptr(q_norm_w), ptr(k_norm_w), float(eps_head), ptr(positions), ptr(cs),
+        cs.stride(0) if cs is not None else 0, ptr(k_cache) if head_mode else None, ptr(v_cache) if head_mode else None,
+        k_cache.stride(0) if head_mode else 0, k_cache.stride(1) if head_mode else 0, k_cache.stride(2) if head_mode else 0,
+        k_cache.shape[1] if head_mode else 1, ptr(slots), ptr(q_out) if head_mode else None, ptr(qkv_out),
+        ptr(res_out) if write_res else None, ptr(_proj_ws(x.device)), 0, stream_ptr(x.device))
+    check(rc, "flint_attn_qkv")
+
+
+@attn_qkv.register_fake
+def _(x, res, norm_w, eps, W, S, gs, num_q_heads, num_kv_heads, head_mode, q_norm_w, k_norm_w, eps_head, positions,
+      cos_sin, k_cache, v_cache, slots, q_out, qkv_out, res_out, write_res):
+    return None
+
+
+@torch.library.custom_op(f"{NS}::attn_o", mutates_args=("y",))
+def attn_o(a: torch.Tensor, W: torch.Tensor, S: torch.Tensor, gs: torch.Tensor, y: torch.Tensor) -> None:
+    """y = bf16(gs * a @ dequant(W, S)^T)."""
+    _lib.require_cuda(a, "attn_o")
+    _bf16_2d(a, "attn_o a")
+    N, K = _check_nvfp4(W, S, "attn_o")
+    M = a.shape[0]
+    if a.shape[1] != K or y.shape != (M, N):
+        raise _lib.FlintError("attn_o: shape mismatch")
+    rc = lib().flint_attn_o(ptr(a), a.stride(0), M, ptr(_u8(W)), ptr(_u8(S)), ptr(gs), N, K, ptr(y),
+                            ptr(_proj_ws(a.device)), 0, stream_ptr(a.device))
+    check(rc, "flint_attn_o")
+
+
+@attn_o.register_fake
+def _(a, W, S, gs, y):
+    return None
+
+
+def attention_splits(batch: int, num_kv_heads: int) -> int:
+    return int(lib().flint_decode_attention_splits(batch, num_kv_heads))
+
+
+@torch.library.custom_op(f"{NS}::decode_attention", mutates_args=("out",))
+def decode_attention(q: torch.Tensor, kv_cache: torch.Tensor, block_tables: torch.Tensor, seq_lens: torch.Tensor,
+                     sinks: torch.Tensor | None, window: int, scale: float, out: torch.Tensor, splits: int) -> None:
+    """Paged split-K decode attention (HND bf16 cache [blocks, kv_heads, 16, 2*128])."""
+    _lib.require_cuda(q, "decode_attention")
+    B, Hq, D = q.shape
+    nblk, Hkv, page, D2 = kv_cache.shape
+    if D != 128 or page != 16 or D2 != 256 or kv_cache.stride(3) != 1 or kv_cache.stride(2) != 256:
+        raise _lib.FlintError("decode_attention: kv_cache must be HND bf16 [blocks, kv_heads, 16, 256]")
+    if q.stride(2) != 1 or q.stride(1) != D or out.stride(2) != 1 or out.stride(1) != D:
+        raise _lib.FlintError("decode_attention: q / out must be [B, heads, 128] with contiguous heads")
+    if block_tables.dtype != torch.int32 or seq_lens.dtype != torch.int32:
+        raise _lib.FlintError("decode_attention: block_tables / seq_lens must be int32")
+    nbytes = lib().flint_decode_attention_workspace_bytes(B, Hkv, splits)
+    ws = _lib.workspace(q.device, "decode_attention", nbytes)
+    rc = lib().flint_decode_attention(ptr(q), q.stride(0), ptr(kv_cache), nblk, Hkv, kv_cache.stride(0),
+                                      kv_cache.stride(1), ptr(block_tables), block_tables.stride(0),
+                                      block_tables.shape[1], ptr(seq_lens), ptr(sinks), int(window), float(scale), B, Hq,
+                                      ptr(out), out.stride(0), splits, ptr(ws), 0, stream_ptr(q.device))
+    check(rc, "flint_decode_attention")
+
+
+@decode_attention.register_fake
+def _(q, kv_cache, block_tables, seq_lens, sinks, window, scale, out, splits):
+    return None

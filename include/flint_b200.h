@@ -59,6 +59,98 @@ int flint_lm_head_nv4(const void* x, int64_t ldx, int64_t M, const void* P, cons
                       int64_t K, float* logits, int64_t ld_logits, int32_t* token_ids, void* workspace, int pdl,
                       void* stream);
 
+/* ------------------------------------------------------------------------------------------------
+ * (1) MoE decode, 1..8 tokens.  Replaces fast/fp4moe_mar.cu (route_kernel 243-303, route_norm_kernel
+ * 311-417, up_mar 67-152, down_mar 157-233) behind fast/fp4moe_decode.py route / route_norm / moe_up /
+ * moe_down (lines 61-95), for any expert count / top-k / sizes (the reference hard-codes E=256, k=6).
+ * One workspace of flint_moe_workspace_bytes(H) serves all three kernels of a layer (and every layer,
+ * launches being stream ordered).
+ * ------------------------------------------------------------------------------------------------ */
+int64_t flint_moe_workspace_bytes(int64_t H);
+
+/* Router with the (residual add +) RMSNorm fused in (fp4moe_mar.cu:311-417 / fp4moe_decode.py:61-79):
+ *   s = x + res (res may be NULL), res_out = bf16(s) (NULL to skip), xn = bf16(s * rsqrt(mean(s^2)+eps) * w)
+ *   (norm_w NULL: xn = bf16(s), no norm), logits[m, e] = bf16(xn[m] . gate_w[e]) stored as fp32,
+ *   top-k on the logits (score_fn 0 = softmax) or sigmoid scores (score_fn 1), ties -> lowest expert,
+ *   weights renormalised over the chosen experts.
+ * x, res, xn_out, res_out bf16 [M, H] (row stride ldx for x/res, H for outputs); gate_w bf16 [E, H];
+ * logits fp32 [M, E]; topk_ids int32 [M, topk]; topk_weights fp32 [M, topk].  H in {2048, 4096},
+ * E % 32 == 0, E <= 512, M <= 8, M * topk <= 64. */
+int flint_moe_route(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, const void* gate_w,
+                    int64_t M, int64_t H, int64_t E, int64_t topk, int score_fn, float* logits, int32_t* topk_ids,
+                    float* topk_weights, void* xn_out, void* res_out, void* workspace, int pdl, void* stream);
+
+/* Expert gate/up GEMV + SwiGLU (fp4moe_mar.cu:67-152):  act[m*topk+s, :] = bf16(silu(g) * u) with
+ * g, u = xn[m] . W13[e, 0:I] * gs13[e], xn[m] . W13[e, I:2I] * gs13[e], e = topk_ids[m, s].
+ * xn bf16 [M, H] (stride ldx); w13 u8 [E, 2I, H/2]; s13 E4M3 [E, 2I, H/16]; g13 fp32 [E]; act bf16 [M*topk, I]. */
+int flint_moe_up(const void* xn, int64_t ldx, int64_t M, const int32_t* topk_ids, int64_t topk, const void* w13,
+                 const void* s13, const float* g13, int64_t E, int64_t I, int64_t H, void* act, void* workspace, int pdl,
+                 void* stream);
+
+/* Expert down GEMV + weighted sum (fp4moe_mar.cu:157-233):  y = bf16(act[r] . W2[e] * gs2[e]) per route,
+ * out[m] = bf16(sum_s topk_weights[m, s] * y[m*topk+s]) (slot order, fp32).
+ * act bf16 [M*topk, I]; w2 u8 [E, H, I/2]; s2 E4M3 [E, H, I/16]; g2 fp32 [E]; out bf16 [M, H]. */
+int flint_moe_down(const void* act, int64_t M, const int32_t* topk_ids, const float* topk_weights, int64_t topk,
+                   const void* w2, const void* s2, const float* g2, int64_t E, int64_t I, int64_t H, void* out,
+                   void* workspace, int pdl, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * (2) Deterministic moe_align_block_size.  Replaces fast/patch_align.py:11-30 (_deterministic_align), the
+ * vLLM call-site contract of moe_align_block_size (same buffers, same outputs): routes of each expert in
+ * ascending route order, each expert padded to block_size, unused slots = numel, expert_ids[blk] = expert
+ * of block blk or -1 past the last, num_tokens_post_pad = padded total.  Buffers must be at least as long
+ * as vLLM allocates (numel + E*(B-1), or min(numel*B, that) when numel < E).  status: int32 device word,
+ * OR-ed with 1 when an id is outside [0, E) (that route is skipped).
+ * ------------------------------------------------------------------------------------------------ */
+int flint_moe_align(const int32_t* topk_ids, int64_t numel, int64_t num_experts, int64_t block_size, int32_t* sorted_ids,
+                    int64_t n_sorted, int32_t* expert_ids, int64_t n_blocks, int32_t* num_tokens_post_pad,
+                    int32_t* status, int pdl, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * (3) Decode attention block: QKV projection (+ q/k norm, RoPE, paged KV write), paged split-K GQA decode
+ * attention, O projection.  Replaces fast/attn_gemv2.cu (qkv_gemv_kernel 101-150, qkv_head_kernel
+ * 170-265, o_gemv_kernel 268-289) behind fast/attn_gemv.py qkv_gemv / qkv_head / o_gemv (lines 24-58),
+ * and the Flint PR's flint_decode_attention (patch:2539-2605).  1..8 tokens.
+ * ------------------------------------------------------------------------------------------------ */
+int64_t flint_attn_proj_workspace_bytes(void);
+
+/* s = x + res (res may be NULL), res_out = bf16(s) (may be NULL), xn = bf16(s*rsqrt(mean(s^2)+eps)*norm_w),
+ * qkv_out[m] = bf16(gs * xn[m] . dequant(W, S)^T)  (W u8 [N, H/2], S E4M3 [N, H/16], gs fp32 device scalar,
+ * N = (num_q_heads + 2*num_kv_heads) * 128).
+ * head_mode 1 (qkv_head): per q/k head n = bf16(y * rsqrt(mean(y^2)+eps_head) * q_norm_w|k_norm_w), NeoX RoPE
+ * from cos_sin fp32 [max_pos, 128] (cos | sin; NULL = no RoPE) at positions[m] (int64), q heads to q_out bf16
+ * [M, num_q_heads*128], k heads back into qkv_out and to k_cache, v heads (unnormalised) to v_cache, at
+ * element offset (slot/block_size)*stride_block + (slot%block_size)*stride_slot + kv_head*stride_head of
+ * slots[m] (int64; < 0 skips the write).  H % 512 == 0. */
+int flint_attn_qkv(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, const void* W, const void* S,
+                   const float* gs, int64_t M, int64_t H, int64_t N, int64_t num_q_heads, int64_t num_kv_heads,
+                   int head_mode, const void* q_norm_w, const void* k_norm_w, float eps_head, const int64_t* positions,
+                   const float* cos_sin, int64_t cos_sin_stride, void* k_cache, void* v_cache, int64_t stride_block,
+                   int64_t stride_slot, int64_t stride_head, int64_t block_size, const int64_t* slots, void* q_out,
+                   void* qkv_out, void* res_out, void* workspace, int pdl, void* stream);
+
+/* y[m] = bf16(gs * a[m] . dequant(W, S)^T);  a bf16 [M, K] (stride lda), W u8 [N, K/2], S E4M3 [N, K/16].
+ * K % 1024 == 0, N % 64 == 0. */
+int flint_attn_o(const void* a, int64_t lda, int64_t M, const void* W, const void* S, const float* gs, int64_t N, int64_t K,
+                 void* y, void* workspace, int pdl, void* stream);
+
+/* Paged decode attention with optional sinks and sliding window, one query token per request:
+ * q bf16 [batch, num_q_heads, 128] (request stride q_stride_b elements); kv_cache bf16 HND
+ * [num_blocks, num_kv_heads, 16, 256] (K in [..., :128], V in [..., 128:], element strides stride_block /
+ * stride_head, 256-element token rows); block_tables int32 [batch, max_blocks] (row stride bt_stride);
+ * seq_lens int32 [batch] (KV length including the current token; 0 writes zeros); sinks fp32 [num_q_heads]
+ * or NULL; window 0 = full attention, else the last `window` positions; out bf16 [batch, num_q_heads, 128].
+ * num_q_heads / num_kv_heads <= 8.  splits: flint_decode_attention_splits(batch, kv_heads) (any value in
+ * 1..256 works; the workspace must match).  block_tables / seq_lens are read before the PDL wait: they must
+ * not be written by the kernel launched just before this one. */
+int64_t flint_decode_attention_splits(int64_t batch, int64_t num_kv_heads);
+int64_t flint_decode_attention_workspace_bytes(int64_t batch, int64_t num_kv_heads, int64_t splits);
+int flint_decode_attention(const void* q, int64_t q_stride_b, const void* kv_cache, int64_t num_blocks,
+                           int64_t num_kv_heads, int64_t stride_block, int64_t stride_head, const int32_t* block_tables,
+                           int64_t bt_stride, int64_t max_blocks, const int32_t* seq_lens, const float* sinks,
+                           int64_t window, float scale, int64_t batch, int64_t num_q_heads, void* out, int64_t out_stride_b,
+                           int64_t splits, void* workspace, int pdl, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
