@@ -28,6 +28,7 @@ struct ProjWorkspace {
 struct QkvArgs {
   const bf16* x;
   int64_t ldx;
+  const int* tokens;            // optional: row m of x is x + tokens[m] * ldx (embedding gather)
   const bf16* res;
   const bf16* nw;
   float eps;
@@ -155,13 +156,26 @@ qkv_kernel(const __grid_constant__ CUtensorMap mc, const __grid_constant__ CUten
   }
   pdl_wait();
   pdl_trigger();
-  add_rmsnorm_smem(args.x, args.ldx, args.res, args.nw, args.eps, args.M, args.H, sbuf, xnb,
+  const bf16* xin = args.x;
+  int64_t ldx = args.ldx;
+  if (args.tokens) {                 // gather the (<= 8) embedding rows into a contiguous staging area first
+    bf16* gxe = reinterpret_cast<bf16*>(xs);   // the f16 staging area is written only after the norm read it
+    for (int idx = threadIdx.x; idx < args.M * (args.H / 8); idx += kQkvWarps * 32) {
+      const int m = idx / (args.H / 8), k8 = idx - m * (args.H / 8);
+      reinterpret_cast<uint4*>(gxe + m * args.H)[k8] =
+          reinterpret_cast<const uint4*>(args.x + (int64_t)args.tokens[m] * args.ldx)[k8];
+    }
+    named_bar_sync(2, kQkvWarps * 32);
+    xin = gxe;
+    ldx = args.H;
+  }
+  add_rmsnorm_smem(xin, ldx, args.res, args.nw, args.eps, args.M, args.H, sbuf, xnb,
                    (head == 0 && rank == 0) ? args.res_out : nullptr, red, kQkvWarps * 32, 2);
   stage_rows_f16(xnb, args.H, args.M, args.H, xs, shift, red, kQkvWarps * 32, 2);
   engine_consume_cluster<kQkvWarps, kQkvStages, kQkvBox, kQkvCL>(plan, smem, dtile, pslot, &clbar, bars, args.status);
 }
 
-static size_t qkv_smem(int M, int H) {
+static size_t qkv_smem(int M, int H) {   // ring, dtile + partials, f16 x (or gathered rows), bf16 xn, fp32 scratch
   return 1024 + QkvL::ring_bytes + (size_t)kQkvCL * QkvL::ROWS * 8 * 4 + (size_t)M * xs_stride(H) * 2 + (size_t)M * H * 2 +
          (size_t)M * H * 4;
 }
@@ -243,7 +257,7 @@ using namespace flint;
 
 extern "C" int64_t flint_attn_proj_workspace_bytes(void) { return sizeof(ProjWorkspace); }
 
-extern "C" int flint_attn_qkv(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, const void* W,
+extern "C" int flint_attn_qkv(const void* x, int64_t ldx, const int32_t* tokens, const void* res, const void* norm_w, float eps, const void* W,
                               const void* S, const float* gs, int64_t M, int64_t H, int64_t N, int64_t num_q_heads,
                               int64_t num_kv_heads, int head_mode, const void* q_norm_w, const void* k_norm_w, float eps_head,
                               const int64_t* positions, const float* cos_sin, int64_t cos_sin_stride, void* k_cache,
@@ -251,6 +265,7 @@ extern "C" int flint_attn_qkv(const void* x, int64_t ldx, const void* res, const
                               int64_t block_size, const int64_t* slots, void* q_out, void* qkv_out, void* res_out,
                               void* workspace, int pdl, void* stream) {
   if (!x || !norm_w || !W || !S || !gs || !qkv_out || !workspace) return FLINT_ERR_ARGUMENT;
+  if (tokens && res) return FLINT_ERR_ARGUMENT;
   if (M < 1 || M > 8 || H % kSliceK != 0 || (H / kSliceK) % kQkvCL != 0 || H > 8192 || ldx < H || ldx % 8 != 0 ||
       N != (num_q_heads + 2 * num_kv_heads) * kHeadDim || num_q_heads < 1 || num_kv_heads < 1)
     return FLINT_ERR_SHAPE;
@@ -266,7 +281,7 @@ extern "C" int flint_attn_qkv(const void* x, int64_t ldx, const void* res, const
   rc = encode_u8_2d(&ms, S, H / 16, N, H / 16, 16, kQkvBox, false);
   if (rc) return rc;
   QkvArgs a;
-  a.x = (const bf16*)x; a.ldx = ldx; a.res = (const bf16*)res; a.nw = (const bf16*)norm_w; a.eps = eps; a.gs = gs;
+  a.x = (const bf16*)x; a.ldx = ldx; a.tokens = (const int*)tokens; a.res = (const bf16*)res; a.nw = (const bf16*)norm_w; a.eps = eps; a.gs = gs;
   a.M = (int)M; a.H = (int)H; a.N = (int)N; a.nq = (int)num_q_heads; a.nkv = (int)num_kv_heads; a.head_mode = head_mode;
   a.q_w = (const bf16*)q_norm_w; a.k_w = (const bf16*)k_norm_w; a.eps_head = eps_head; a.positions = positions;
   a.cos_sin = cos_sin; a.cs_stride = cos_sin_stride; a.k_cache = (bf16*)k_cache; a.v_cache = (bf16*)v_cache;

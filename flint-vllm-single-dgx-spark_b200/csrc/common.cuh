@@ -23,11 +23,13 @@ typedef __nv_bfloat16 bf16;
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-// read-once weight streams: non-coherent, no L1 allocation
+// read-once weight streams: non-coherent, no L1 allocation, L2 evict-first
 __device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
   uint4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p), "l"(pol));
   return r;
 }
 __device__ __forceinline__ uint32_t ldg_stream_u32(const void* p) {
@@ -233,6 +235,60 @@ __device__ __forceinline__ void add_rmsnorm_smem(const bf16* x, int64_t ldx, con
     }
     reinterpret_cast<uint4*>(xn + m * H)[k8] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
     if (res_out) reinterpret_cast<uint4*>(res_out + m * H)[k8] = make_uint4(rk[0], rk[1], rk[2], rk[3]);
+  }
+  sync();
+}
+
+// Two-pass variant without fp32 scratch (for kernels whose shared memory is taken by their weight ring):
+// pass 1 reduces sum(s^2) per row, pass 2 re-reads x (+ res) and writes xn = bf16(s * rsqrt(mean + eps) * w).
+__device__ __forceinline__ void add_rmsnorm_2pass(const bf16* x, int64_t ldx, const bf16* res, const bf16* __restrict__ w,
+                                                  float eps, int M, int H, bf16* xn, float* red, int nthreads, int bar) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = nthreads >> 5, H8 = H >> 3;
+  auto sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthreads) : "memory"); };
+  auto load = [&](int m, int k8, float* a) {
+    bf16x8_to_f32(reinterpret_cast<const uint4*>(x + m * ldx)[k8], a);
+    if (res) {
+      float b[8];
+      bf16x8_to_f32(reinterpret_cast<const uint4*>(res + m * ldx)[k8], b);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) a[j] += b[j];
+    }
+  };
+  float ss[8];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    ss[m] = 0.f;
+    if (m < M)
+      for (int k8 = tid; k8 < H8; k8 += nthreads) {
+        float a[8];
+        load(m, k8, a);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss[m] = fmaf(a[j], a[j], ss[m]);
+      }
+  }
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    float v = ss[m];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[warp * 8 + m] = v;
+  }
+  sync();
+  for (int idx = tid; idx < M * H8; idx += nthreads) {
+    const int m = idx / H8, k8 = idx - m * H8;
+    float tot = 0.f;
+    for (int ww = 0; ww < nw; ++ww) tot += red[ww * 8 + m];
+    const float rs = rsqrtf(tot / (float)H + eps);
+    float a[8], wf[8];
+    load(m, k8, a);
+    bf16x8_to_f32(reinterpret_cast<const uint4*>(w)[k8], wf);
+    uint32_t pk[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __nv_bfloat162 n2 = __floats2bfloat162_rn(a[2 * j] * rs * wf[2 * j], a[2 * j + 1] * rs * wf[2 * j + 1]);
+      pk[j] = *reinterpret_cast<uint32_t*>(&n2);
+    }
+    reinterpret_cast<uint4*>(xn + m * H)[k8] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
   }
   sync();
 }

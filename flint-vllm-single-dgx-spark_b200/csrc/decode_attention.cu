@@ -8,8 +8,8 @@
 // in the warp's private ring; pages not holding the current token are prefetched before the PDL wait.
 // Per page: S = K q (mma.sync, query heads padded 8 -> 16 rows), online softmax in fp32 as exp2(S*c - m*c) with
 // c = scale*log2(e), P rounded to bf16 for O += P V (the S accumulators are reused as P fragments), l sums the fp32 p.
-// Warps, then splits, merge their (m, l, O) in fixed order (deterministic); the last CTA of a (request, kv head) to
-// finish merges the splits and adds the sink term exp2(sink*log2e - m*c) to the denominator
+// The number of active splits follows the context (at least 8 pages each).  Warps, then splits, merge their (m, l, O)
+// in fixed order (deterministic); the last CTA of a (request, kv head) to finish merges the splits and adds the sink term exp2(sink*log2e - m*c) to the denominator
 // (numerics of patch:1444-1464).
 #include "common.cuh"
 #include "runtime.cuh"
@@ -23,6 +23,7 @@ constexpr int kAttnWarps = 4;
 constexpr int kAttnStages = 3;
 constexpr int kPageBytes = kPage * 2 * kAttnD * 2;       // 8 KB
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kMinPagesPerSplit = 8;
 
 struct AttnWorkspace {
   unsigned status;
@@ -81,7 +82,10 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kv, const AttnArgs a) {
   const int start = a.window > 0 ? max(0, seq - a.window) : 0;
   const int p_first = start / kPage, p_end = (seq + kPage - 1) / kPage;
   const int npages = max(0, p_end - p_first);
-  const int pps = (npages + a.splits - 1) / a.splits;
+  // active splits follow the context: at least kMinPagesPerSplit pages each (fewer partials to merge when short)
+  const int n_act = max(1, min(a.splits, npages / kMinPagesPerSplit));
+  if (split >= n_act) return;
+  const int pps = (npages + n_act - 1) / n_act;
   const int pb = p_first + split * pps, pe = min(p_end, pb + pps);
   const int last_page = p_end - 1;                          // holds the current token (written by the previous kernel)
   const int* bt = a.block_tables + (int64_t)b * a.bt_stride;
@@ -246,40 +250,41 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap kv, const AttnArgs a) {
     for (int i = 0; i < 4; ++i) pk[i] = pack_bf16(ov[2 * i] * inv, ov[2 * i + 1] * inv);
     *reinterpret_cast<uint4*>(a.out + (int64_t)b * a.out_stride_b + (int64_t)qh * kAttnD + d0) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
   };
-  if (a.splits == 1) {
+  if (n_act == 1) {
     finish(mc, lc, oc);
     return;
   }
-  const size_t pidx = (size_t)bh * a.splits + split;
-  float* po = part_o + (pidx * 8 + hh) * kAttnD + d0;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) __stcg(po + i, oc[i]);
-  if ((threadIdx.x & 15) == 0) {
-    __stcg(part_ml + (pidx * 8 + hh) * 2, mc);
-    __stcg(part_ml + (pidx * 8 + hh) * 2 + 1, lc);
-  }
+  // split partials, laid out [(request, kv head, head)][split] so the merging CTA reads each head's splits contiguously
+  const size_t row = (size_t)bh * 8 + hh;
+  float* po = part_o + (row * a.splits + split) * kAttnD + d0;
+  __stcg(reinterpret_cast<float4*>(po), make_float4(oc[0], oc[1], oc[2], oc[3]));
+  __stcg(reinterpret_cast<float4*>(po) + 1, make_float4(oc[4], oc[5], oc[6], oc[7]));
+  if ((threadIdx.x & 15) == 0) __stcg(reinterpret_cast<float2*>(part_ml) + row * a.splits + split, make_float2(mc, lc));
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
-    s_last = atomicAdd(&a.ws->counter[bh], 1u) == (unsigned)a.splits - 1;
+    s_last = atomicAdd(&a.ws->counter[bh], 1u) == (unsigned)n_act - 1;
     if (s_last) atomicExch(&a.ws->counter[bh], 0u);
   }
   __syncthreads();
   if (!s_last) return;
   __threadfence();
+  const float2* ml = reinterpret_cast<const float2*>(part_ml) + row * a.splits;
   float m = -INFINITY;
-  for (int sp = 0; sp < a.splits; ++sp) m = fmaxf(m, __ldcg(part_ml + (((size_t)bh * a.splits + sp) * 8 + hh) * 2));
+#pragma unroll 8
+  for (int sp = 0; sp < n_act; ++sp) m = fmaxf(m, __ldcg(ml + sp).x);
   float l = 0.f, ov[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) ov[i] = 0.f;
-  for (int sp = 0; sp < a.splits; ++sp) {
-    const size_t q = ((size_t)bh * a.splits + sp) * 8 + hh;
-    const float ms = __ldcg(part_ml + q * 2);
-    if (ms == -INFINITY) continue;
-    const float f = exp2f(ms * c - m * c);
-    l += __ldcg(part_ml + q * 2 + 1) * f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) ov[i] += __ldcg(part_o + q * kAttnD + d0 + i) * f;
+#pragma unroll 4
+  for (int sp = 0; sp < n_act; ++sp) {
+    const float2 v = __ldcg(ml + sp);
+    const float4* o4 = reinterpret_cast<const float4*>(part_o + (row * a.splits + sp) * kAttnD + d0);
+    const float4 u0 = __ldcg(o4), u1 = __ldcg(o4 + 1);
+    const float f = v.x == -INFINITY ? 0.f : exp2f(v.x * c - m * c);
+    l += v.y * f;
+    ov[0] += u0.x * f; ov[1] += u0.y * f; ov[2] += u0.z * f; ov[3] += u0.w * f;
+    ov[4] += u1.x * f; ov[5] += u1.y * f; ov[6] += u1.z * f; ov[7] += u1.w * f;
   }
   finish(m, l, ov);
 }

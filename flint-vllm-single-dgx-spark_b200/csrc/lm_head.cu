@@ -10,23 +10,26 @@ constexpr int kHeadStages = 4;
 constexpr int kHeadWarps = 16;
 constexpr int kHeadRows = kHeadWarps * 16;
 
-static size_t head_smem(int M, int K) {
-  return 1024 + (size_t)kHeadStages * StageGeom<kHeadRows>::bytes + (size_t)M * xs_stride(K) * 2;
+static size_t head_smem(int M, int K, bool norm) {
+  return 1024 + (size_t)kHeadStages * StageGeom<kHeadRows>::bytes + (size_t)M * xs_stride(K) * 2 +
+         (norm ? (size_t)M * K * 2 : 0);
 }
 
 }  // namespace flint
 
 extern "C" int64_t flint_lm_head_workspace_bytes(void) { return sizeof(flint::HeadWorkspace); }
 
-extern "C" int flint_lm_head_nv4(const void* x, int64_t ldx, int64_t M, const void* P, const void* S, float gs, int64_t V,
-                                 int64_t K, float* logits, int64_t ld_logits, int32_t* token_ids, void* workspace, int pdl,
-                                 void* stream) {
+extern "C" int flint_lm_head_nv4_fused(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, int64_t M,
+                                       const void* P, const void* S, float gs, int64_t V, int64_t K, float* logits,
+                                       int64_t ld_logits, int32_t* token_ids, void* workspace, int pdl, void* stream) {
   using namespace flint;
-  if (!x || !P || !S) return FLINT_ERR_ARGUMENT;
+  if (!x || !P || !S || (res && !norm_w)) return FLINT_ERR_ARGUMENT;
   if (M < 1 || M > 8 || V < 1 || V > (1ll << 30) || K < kSliceK || K % kSliceK != 0 || K > 8192 || ldx < K)
     return FLINT_ERR_SHAPE;
   if (logits && ld_logits < V) return FLINT_ERR_SHAPE;
-  if (!aligned(P, 16) || !aligned(S, 16) || !aligned(x, 2)) return FLINT_ERR_ALIGN;
+  if (!aligned(P, 16) || !aligned(S, 16) || !aligned(x, 16) || ldx % 8 != 0 || (res && !aligned(res, 16)) ||
+      (norm_w && !aligned(norm_w, 16)))
+    return FLINT_ERR_ALIGN;
   if (!workspace) return FLINT_ERR_WORKSPACE;
   if (!aligned(workspace, 8)) return FLINT_ERR_ALIGN;
   const int sms = num_sms();
@@ -37,11 +40,19 @@ extern "C" int flint_lm_head_nv4(const void* x, int64_t ldx, int64_t M, const vo
   rc = encode_u8_2d(&ms, S, K / 16, V, K / 16, 16, kHeadRows, false);
   if (rc) return rc;
   auto kern = lm_head_kernel<kHeadStages, kHeadWarps>;
-  const size_t smem = head_smem((int)M, (int)K);
+  const size_t smem = head_smem((int)M, (int)K, norm_w != nullptr);
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return FLINT_ERR_LAUNCH;
   const int ngroups = (int)((V + kHeadRows - 1) / kHeadRows);
   const int grid = ngroups < sms ? ngroups : sms;
-  return launch(kern, dim3(grid), dim3((kHeadWarps + 1) * 32), smem, stream, pdl, mc, ms, (const bf16*)x, ldx, (int)M, gs,
-                (int)V, (int)K, logits, ld_logits, (int*)token_ids, (HeadWorkspace*)workspace);
+  return launch(kern, dim3(grid), dim3((kHeadWarps + 1) * 32), smem, stream, pdl, mc, ms, (const bf16*)x, ldx,
+                (const bf16*)res, (const bf16*)norm_w, eps, (int)M, gs, (int)V, (int)K, logits, ld_logits, (int*)token_ids,
+                (HeadWorkspace*)workspace);
+}
+
+extern "C" int flint_lm_head_nv4(const void* x, int64_t ldx, int64_t M, const void* P, const void* S, float gs, int64_t V,
+                                 int64_t K, float* logits, int64_t ld_logits, int32_t* token_ids, void* workspace, int pdl,
+                                 void* stream) {
+  return flint_lm_head_nv4_fused(x, ldx, nullptr, nullptr, 0.f, M, P, S, gs, V, K, logits, ld_logits, token_ids, workspace,
+                                 pdl, stream);
 }

@@ -21,8 +21,9 @@ struct HeadWorkspace {
 template <int NS, int NW>
 __global__ void __launch_bounds__((NW + 1) * 32, 1)
 lm_head_kernel(const __grid_constant__ CUtensorMap map_codes, const __grid_constant__ CUtensorMap map_scales,
-               const bf16* __restrict__ x, int64_t ldx, int M, float gs, int V, int K, float* __restrict__ logits,
-               int64_t ldl, int* __restrict__ tokens, HeadWorkspace* ws) {
+               const bf16* __restrict__ x, int64_t ldx, const bf16* __restrict__ res, const bf16* __restrict__ norm_w,
+               float eps, int M, float gs, int V, int K, float* __restrict__ logits, int64_t ldl, int* __restrict__ tokens,
+               HeadWorkspace* ws) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   using G = StageGeom<NW * 16>;
@@ -31,7 +32,7 @@ lm_head_kernel(const __grid_constant__ CUtensorMap map_codes, const __grid_const
   uint8_t* ring_scales = smem + NS * G::code_bytes;
   __half* xs = reinterpret_cast<__half*>(smem + NS * G::bytes);
   __shared__ uint64_t bar_full[NS], bar_empty[NS];
-  __shared__ float red[(NW + 1) * 8];   // stage_rows_f16 scratch: warps x tokens
+  __shared__ float red[(NW + 1) * 8];   // norm / staging scratch: warps x tokens
   __shared__ int shift[8];
   __shared__ unsigned long long wbest[NW][8];
   __shared__ int s_last;
@@ -69,7 +70,13 @@ lm_head_kernel(const __grid_constant__ CUtensorMap map_codes, const __grid_const
     while (p_s < total && p_s < NS) produce_one();       // weights do not depend on the previous kernel
   }
   pdl_wait();
-  stage_x_f16(x, ldx, M, K, xs, shift, red);
+  if (norm_w) {                                          // fused final (residual add +) RMSNorm of the hidden state
+    bf16* xnb = reinterpret_cast<bf16*>(xs + M * xs_stride(K));
+    add_rmsnorm_2pass(x, ldx, res, norm_w, eps, M, K, xnb, red, blockDim.x, 0);
+    stage_x_f16(xnb, K, M, K, xs, shift, red);
+  } else {
+    stage_x_f16(x, ldx, M, K, xs, shift, red);
+  }
 
   if (warp == NW) {
     if (lane == 0) {

@@ -12,9 +12,21 @@ int num_sms(int* dev_out = nullptr);
 
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Every kernel runs with the maximum shared-memory carveout, so consecutive kernels of a decode step never make an
+// SM re-partition L1 / shared memory between them.
+template <typename... KArgs>
+inline void set_max_carveout(void (*kern)(KArgs...)) {
+  static int done_dev[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || done_dev[dev]) return;
+  cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+  done_dev[dev] = 1;
+}
+
 // Launch with optional programmatic dependent launch (PDL); returns FLINT_OK / FLINT_ERR_LAUNCH.
 template <typename... KArgs, typename... Args>
 int launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, void* stream, int pdl, Args... args) {
+  set_max_carveout(kern);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -33,6 +45,7 @@ int launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, void* str
 template <typename... KArgs, typename... Args>
 int launch_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, void* stream, int pdl, int cluster,
                    Args... args) {
+  set_max_carveout(kern);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;

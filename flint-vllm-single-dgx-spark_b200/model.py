@@ -1,0 +1,265 @@
+"""Flint-class synthetic decoder on the B200 kernels, for end-to-end decode runs.
+
+The layer structure follows the reference's fast decode path (fast/model.py: FlintDecoderLayer.forward 734-759,
+FlintAttention.forward_af 596-657, FlintSparseMoeBlock._forward_decode_rn 302-310, compute_logits 924-929):
+
+    layer l:  q, res = qkv_head(h, res)          add + RMSNorm + QKV + q/k norm + RoPE + KV write
+              a = o_gemv(decode_attention(q))
+              tw, ti, xn, res = route_norm(a, res)   add + RMSNorm + router + top-k
+              h = moe_down(moe_up(xn, ti), ti, tw)
+    head:     token = argmax(lm_head(final_norm(h + res)))
+
+with the BASELINE.json shapes (hidden 2048, 48 layers, 32/4 heads of 128, 128 experts top-8 softmax, I = 768,
+vocab 151552, RoPE theta 1e6) and seeded N(0, 0.02) NVFP4 weights.  One decode step of M <= 8 streams is a
+single CUDA graph (the embedding lookup is fused into the first QKV kernel, the final norm into the head,
+and the position / KV-slot bookkeeping runs on the device), so consecutive steps replay without the host.
+"""
+from __future__ import annotations
+
+import math
+import time
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import ops as _ops  # noqa: F401
+from .fp4moe_decode import DecodeWeights
+from .nvfp4 import random_nvfp4
+
+PAGE = 16
+
+
+@dataclass
+class FlintConfig:
+    hidden: int = 2048
+    layers: int = 48
+    num_heads: int = 32
+    num_kv_heads: int = 4
+    head_dim: int = 128
+    num_experts: int = 128
+    topk: int = 8
+    moe_inter: int = 768
+    vocab: int = 151552
+    rope_theta: float = 1e6
+    rms_eps: float = 1e-6
+    score: str = "softmax"
+    weight_std: float = 0.02
+
+    @property
+    def qkv_rows(self) -> int:
+        return (self.num_heads + 2 * self.num_kv_heads) * self.head_dim
+
+    def param_counts(self) -> tuple[int, int]:
+        """(total, active per token) parameters, embedding excluded."""
+        H, I, E, k = self.hidden, self.moe_inter, self.num_experts, self.topk
+        attn = self.qkv_rows * H + H * self.num_heads * self.head_dim
+        expert = 3 * H * I
+        per_layer_total = attn + E * expert + E * H
+        per_layer_active = attn + k * expert + E * H
+        return (self.layers * per_layer_total + self.vocab * H, self.layers * per_layer_active + self.vocab * H)
+
+    def weight_bytes_per_token(self) -> int:
+        """NVFP4 bytes streamed per decode token at batch 1 (0.5625 B/param; bf16 router and norms)."""
+        H, I, k = self.hidden, self.moe_inter, self.topk
+        nv = lambda n, kk: n * kk // 2 + n * kk // 16
+        attn = nv(self.qkv_rows, H) + nv(H, self.num_heads * self.head_dim)
+        moe = k * (nv(2 * I, H) + nv(H, I)) + self.num_experts * H * 2
+        return self.layers * (attn + moe) + nv(self.vocab, H)
+
+
+def rope_cos_sin(max_pos: int, dim: int, theta: float, device) -> torch.Tensor:
+    inv = 1.0 / (theta ** (torch.arange(0, dim, 2, dtype=torch.float64, device=device) / dim))
+    ang = torch.arange(max_pos, dtype=torch.float64, device=device)[:, None] * inv[None, :]
+    return torch.cat([torch.cos(ang), torch.sin(ang)], dim=1).to(torch.float32).contiguous()
+
+
+class FlintModel:
+    """Weights, KV cache and RoPE table of a synthetic Flint-class model on one GPU."""
+
+    def __init__(self, cfg: FlintConfig, device="cuda", seed: int = 0, max_ctx: int = 8192, max_batch: int = 1):
+        self.cfg, self.dev = cfg, torch.device(device)
+        self.max_ctx, self.max_batch = max_ctx, max_batch
+        c = cfg
+        g = torch.Generator(device=self.dev)
+        g.manual_seed(seed)
+        bf = lambda shape, std: (torch.randn(shape, generator=g, device=self.dev) * std).to(torch.bfloat16)
+        ones = lambda n: (1.0 + torch.randn((n,), generator=g, device=self.dev) * 0.05).to(torch.bfloat16)
+        self.embed = bf((c.vocab, c.hidden), 1.0)
+        self.layers = []
+        for _ in range(c.layers):
+            P, S, gs = random_nvfp4((), c.qkv_rows, c.hidden, c.weight_std, g, self.dev)
+            Po, So, gso = random_nvfp4((), c.hidden, c.num_heads * c.head_dim, c.weight_std, g, self.dev)
+            w13, s13, g13 = random_nvfp4((c.num_experts,), 2 * c.moe_inter, c.hidden, c.weight_std, g, self.dev)
+            w2, s2, g2 = random_nvfp4((c.num_experts,), c.hidden, c.moe_inter, c.weight_std, g, self.dev)
+            self.layers.append(dict(
+                ln1=ones(c.hidden), qkv=(P, S, gs.reshape(1)), q_norm=ones(c.head_dim), k_norm=ones(c.head_dim),
+                o=(Po, So, gso.reshape(1)), ln2=ones(c.hidden), gate=bf((c.num_experts, c.hidden), c.weight_std),
+                experts=DecodeWeights(w13, s13, g13, w2, s2, g2, topk=c.topk, score=c.score)))
+        self.final_norm = ones(c.hidden)
+        Ph, Sh, gsh = random_nvfp4((), c.vocab, c.hidden, c.weight_std, g, self.dev)
+        self.head = (Ph, Sh, float(gsh.item()))
+        self.cos_sin = rope_cos_sin(max_ctx, c.head_dim, c.rope_theta, self.dev)
+        # paged KV cache: FlashInfer HND [blocks, kv_heads, 16, 2*D] per layer; each stream owns a shuffled block set
+        self.blocks_per_stream = (max_ctx + PAGE - 1) // PAGE
+        nblk = self.blocks_per_stream * max_batch
+        self.kv = [torch.zeros((nblk, c.num_kv_heads, PAGE, 2 * c.head_dim), dtype=torch.bfloat16, device=self.dev)
+                   for _ in range(c.layers)]
+        perm = torch.randperm(nblk, generator=torch.Generator().manual_seed(seed + 1)).to(torch.int32)
+        self.block_tables = perm.reshape(max_batch, self.blocks_per_stream).to(self.dev).contiguous()
+
+    def kv_views(self, l):
+        kv = self.kv[l]
+        k, v = kv.transpose(1, 2).split(self.cfg.head_dim, dim=-1)
+        return kv, k, v
+
+
+class Decoder:
+    """Batch-M (M <= 8) decode of a FlintModel: teacher-forced prompt processing and greedy generation."""
+
+    def __init__(self, model: FlintModel, batch: int = 1):
+        self.m, self.c, self.M = model, model.cfg, batch
+        c, M, dev = model.cfg, batch, model.dev
+        assert 1 <= M <= min(8, model.max_batch)
+        e = lambda *s, dt=torch.bfloat16: torch.empty(s, dtype=dt, device=dev)
+        self.tokens = torch.zeros((M,), dtype=torch.int32, device=dev)
+        self.positions = torch.zeros((M,), dtype=torch.int64, device=dev)
+        self.seq_lens = torch.zeros((M,), dtype=torch.int32, device=dev)
+        self.slots = torch.zeros((M,), dtype=torch.int64, device=dev)
+        self.bt = model.block_tables[:M]
+        self.step_ctr = torch.zeros((1,), dtype=torch.int32, device=dev)
+        self.history = torch.zeros((M, 1), dtype=torch.int32, device=dev)
+        self.out_tok = torch.zeros((M,), dtype=torch.int32, device=dev)
+        self.q, self.qkv = e(M, c.num_heads * c.head_dim), e(M, c.qkv_rows)
+        self.res_a, self.res_b, self.h = e(M, c.hidden), e(M, c.hidden), e(M, c.hidden)
+        self.attn = e(M, c.num_heads, c.head_dim)
+        self.a, self.xn = e(M, c.hidden), e(M, c.hidden)
+        self.tw, self.ti = e(M, c.topk, dt=torch.float32), e(M, c.topk, dt=torch.int32)
+        self.lg = e(M, c.num_experts, dt=torch.float32)
+        self.act = e(M * c.topk, c.moe_inter)
+        self.dummy_f = e(1, 1, dt=torch.float32)
+        self.dummy_b = e(0)
+        self.splits = _ops.attention_splits(M, c.num_kv_heads)
+        self.scale = c.head_dim ** -0.5
+        self.graphs: dict[str, torch.cuda.CUDAGraph] = {}
+        self.launches_per_step = 6 * c.layers + 2      # 6 kernels per layer + head + advance
+
+    # ---- one decode step as torch ops on persistent buffers ----
+    def _layers(self):
+        c, m, ops = self.c, self.m, torch.ops.flint_b200
+        for l, L in enumerate(m.layers):
+            kv, kc, vc = m.kv_views(l)
+            P, S, gs = L["qkv"]
+            if l == 0:
+                ops.attn_qkv(m.embed, None, L["ln1"], c.rms_eps, P, S, gs, c.num_heads, c.num_kv_heads, True,
+                             L["q_norm"], L["k_norm"], c.rms_eps, self.positions, m.cos_sin, kc, vc, self.slots, self.q,
+                             self.qkv, self.res_a, True, self.tokens)
+            else:
+                ops.attn_qkv(self.h, self.res_b, L["ln1"], c.rms_eps, P, S, gs, c.num_heads, c.num_kv_heads, True,
+                             L["q_norm"], L["k_norm"], c.rms_eps, self.positions, m.cos_sin, kc, vc, self.slots, self.q,
+                             self.qkv, self.res_a, True, None)
+            ops.decode_attention(self.q.view(self.M, c.num_heads, c.head_dim), kv, self.bt, self.seq_lens, None, 0,
+                                 self.scale, self.attn, self.splits)
+            Po, So, gso = L["o"]
+            ops.attn_o(self.attn.view(self.M, -1), Po, So, gso, self.a)
+            ew = L["experts"]
+            ops.moe_route(self.a, self.res_a, L["ln2"], c.rms_eps, L["gate"], c.topk, ew.score_fn, self.lg, self.ti,
+                          self.tw, self.xn, self.res_b, True, True)
+            ops.moe_up(self.xn, self.ti, ew.w13, ew.s13, ew.g13, self.act)
+            ops.moe_down(self.act, self.ti, self.tw, ew.w2, ew.s2, ew.g2, self.h)
+
+    def _head_and_advance(self):
+        P, S, gs = self.m.head
+        ops = torch.ops.flint_b200
+        ops.lm_head_nv4(self.h, P, S, gs, self.dummy_f, self.out_tok, False, True, self.res_b, self.m.final_norm,
+                        self.c.rms_eps)
+        ops.decode_advance(self.out_tok, self.positions, self.seq_lens, self.slots, self.bt, PAGE, self.history,
+                           self.step_ctr, self.tokens)
+
+    def _step(self):
+        self._layers()
+        self._head_and_advance()
+
+    def capture(self):
+        """Capture the decode-step graph (greedy, with device bookkeeping) and the prompt graph (layers only)."""
+        # eager warm-up creates every workspace before capture
+        self._set_state(np.zeros(self.M, np.int64), np.zeros(self.M, np.int64))
+        self._layers()
+        self._head_and_advance()
+        torch.cuda.synchronize()
+        for name, fn in (("step", self._step), ("layers", self._layers)):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                fn()
+            self.graphs[name] = g
+        torch.cuda.synchronize()
+
+    # ---- host-side state (what vLLM's runner uploads each step) ----
+    def _slot(self, b, pos):
+        blk = self.m.block_tables[b].cpu().numpy() if not hasattr(self, "_bt_host") else self._bt_host[b]
+        return int(blk[pos // PAGE]) * PAGE + pos % PAGE
+
+    def _set_state(self, tokens, positions):
+        if not hasattr(self, "_bt_host"):
+            self._bt_host = self.bt.cpu().numpy()
+        pos = np.asarray(positions, np.int64)
+        slots = np.array([self._bt_host[b][p // PAGE] * PAGE + p % PAGE for b, p in enumerate(pos)], np.int64)
+        self.tokens.copy_(torch.from_numpy(np.asarray(tokens, np.int32)))
+        self.positions.copy_(torch.from_numpy(pos))
+        self.seq_lens.copy_(torch.from_numpy((pos + 1).astype(np.int32)))
+        self.slots.copy_(torch.from_numpy(slots))
+
+    def prefill(self, prompts: np.ndarray):
+        """Teacher-forced prompt processing through the decode kernels: writes K/V of positions 0..T-2 and leaves
+        the state at the last prompt token (position T-1), ready for the first generation step."""
+        if not self.graphs:
+            self.capture()
+        T = prompts.shape[1]
+        g = self.graphs["layers"]
+        for t in range(T - 1):
+            self._set_state(prompts[:, t], np.full(self.M, t))
+            g.replay()
+        self._set_state(prompts[:, T - 1], np.full(self.M, T - 1))
+        self.step_ctr.zero_()
+        torch.cuda.synchronize()
+
+    def decode(self, n: int):
+        """n greedy steps replayed back to back on the device; returns the tokens [M, n] (int32, on the device)."""
+        if self.history.shape[1] < n:
+            raise ValueError("call reserve_history(n) before capture")
+        g = self.graphs["step"]
+        for _ in range(n):
+            g.replay()
+        return self.history[:, :n]
+
+    def reserve_history(self, n: int):
+        self.history = torch.zeros((self.M, n), dtype=torch.int32, device=self.m.dev)
+        self.graphs.clear()
+
+    def generate_host_driven(self, n: int, pinned: dict):
+        """The serving loop of the public API: every step uploads its inputs from pinned host memory, replays the
+        step graph and reads the sampled token back (host <-> device copies inside the loop)."""
+        g = self.graphs["step"]
+        out = []
+        for _ in range(n):
+            self.tokens.copy_(pinned["tokens"], non_blocking=True)
+            self.positions.copy_(pinned["positions"], non_blocking=True)
+            self.seq_lens.copy_(pinned["seq_lens"], non_blocking=True)
+            self.slots.copy_(pinned["slots"], non_blocking=True)
+            g.replay()
+            pinned["out"].copy_(self.out_tok, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            tok = pinned["out"].numpy().copy()
+            out.append(tok)
+            pos = pinned["positions"].numpy() + 1
+            pinned["tokens"].numpy()[:] = tok
+            pinned["positions"].numpy()[:] = pos
+            pinned["seq_lens"].numpy()[:] = pos + 1
+            pinned["slots"].numpy()[:] = [self._bt_host[b][p // PAGE] * PAGE + p % PAGE for b, p in enumerate(pos)]
+        return np.stack(out, axis=1)
+
+    def pinned_state(self):
+        pos = self.positions.cpu()
+        return dict(tokens=self.tokens.cpu().pin_memory(), positions=pos.pin_memory(),
+                    seq_lens=self.seq_lens.cpu().pin_memory(), slots=self.slots.cpu().pin_memory(),
+                    out=torch.zeros((self.M,), dtype=torch.int32).pin_memory())

@@ -8,12 +8,17 @@ their workspaces exist (see ``_lib.workspace``).
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from . import _lib
 from ._lib import check, lib, ptr, stream_ptr
 
 NS = "flint_b200"
+# Programmatic dependent launch: each kernel starts (barrier setup, weight prefetch) while its predecessor in the
+# stream drains, and waits on it (griddepcontrol.wait) before touching its outputs.
+PDL = 1 if os.environ.get("FLINT_PDL", "1") == "1" else 0
 
 
 def _u8(t: torch.Tensor) -> torch.Tensor:
@@ -33,8 +38,10 @@ def _check_nvfp4(P: torch.Tensor, S: torch.Tensor, what: str) -> tuple[int, int]
 # ------------------------------------------------------------------------------------------------------------
 @torch.library.custom_op(f"{NS}::lm_head_nv4", mutates_args=("logits", "tokens"))
 def lm_head_nv4(x: torch.Tensor, P: torch.Tensor, S: torch.Tensor, gs: float, logits: torch.Tensor,
-                tokens: torch.Tensor, write_logits: bool, write_tokens: bool) -> None:
-    """logits[m] = gs * x[m] @ dequant(P, S)^T (fp32); tokens[m] = argmax (lowest index on ties)."""
+                tokens: torch.Tensor, write_logits: bool, write_tokens: bool, res: torch.Tensor | None = None,
+                norm_w: torch.Tensor | None = None, eps: float = 0.0) -> None:
+    """logits[m] = gs * x[m] @ dequant(P, S)^T (fp32); tokens[m] = argmax (lowest index on ties).  With norm_w the
+    final (residual add +) RMSNorm is applied to x first."""
     _lib.require_cuda(x, "lm_head_nv4")
     V, K = _check_nvfp4(P, S, "lm_head_nv4")
     if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != K or x.stride(1) != 1:
@@ -45,14 +52,15 @@ def lm_head_nv4(x: torch.Tensor, P: torch.Tensor, S: torch.Tensor, gs: float, lo
     if write_tokens and (tokens.dtype != torch.int32 or tokens.numel() < M):
         raise _lib.FlintError("lm_head_nv4: tokens must be int32 [M]")
     ws = _lib.workspace(x.device, "lm_head", lib().flint_lm_head_workspace_bytes())
-    rc = lib().flint_lm_head_nv4(ptr(x), x.stride(0), M, ptr(_u8(P)), ptr(_u8(S)), float(gs), V, K,
-                                 ptr(logits) if write_logits else None, logits.stride(0) if write_logits else 0,
-                                 ptr(tokens) if write_tokens else None, ptr(ws), 0, stream_ptr(x.device))
+    rc = lib().flint_lm_head_nv4_fused(ptr(x), x.stride(0), ptr(res), ptr(norm_w), float(eps), M, ptr(_u8(P)), ptr(_u8(S)),
+                                       float(gs), V, K, ptr(logits) if write_logits else None,
+                                       logits.stride(0) if write_logits else 0, ptr(tokens) if write_tokens else None,
+                                       ptr(ws), PDL, stream_ptr(x.device))
     check(rc, "flint_lm_head_nv4")
 
 
 @lm_head_nv4.register_fake
-def _(x, P, S, gs, logits, tokens, write_logits, write_tokens):
+def _(x, P, S, gs, logits, tokens, write_logits, write_tokens, res=None, norm_w=None, eps=0.0):
     return None
 
 
@@ -83,7 +91,7 @@ def moe_route(x: torch.Tensor, res: torch.Tensor | None, norm_w: torch.Tensor | 
         raise _lib.FlintError("moe_route: res must match x")
     rc = lib().flint_moe_route(ptr(x), x.stride(0), ptr(res), ptr(norm_w), float(eps), ptr(gate_w), M, H, E, topk,
                                score_fn, ptr(logits), ptr(topk_ids), ptr(topk_weights), ptr(xn) if write_xn else None,
-                               ptr(res_out) if write_res else None, ptr(_moe_ws(x.device, H)), 0, stream_ptr(x.device))
+                               ptr(res_out) if write_res else None, ptr(_moe_ws(x.device, H)), PDL, stream_ptr(x.device))
     check(rc, "flint_moe_route")
 
 
@@ -104,7 +112,7 @@ def moe_up(xn: torch.Tensor, topk_ids: torch.Tensor, w13: torch.Tensor, s13: tor
     if Hh * 2 != H or s13.shape != (E, I2, H // 16) or g13.numel() != E or act.shape != (M * topk, I2 // 2):
         raise _lib.FlintError("moe_up: weight / activation shapes mismatch")
     rc = lib().flint_moe_up(ptr(xn), xn.stride(0), M, ptr(topk_ids), topk, ptr(_u8(w13)), ptr(_u8(s13)), ptr(g13), E,
-                            I2 // 2, H, ptr(act), ptr(_moe_ws(xn.device, H)), 0, stream_ptr(xn.device))
+                            I2 // 2, H, ptr(act), ptr(_moe_ws(xn.device, H)), PDL, stream_ptr(xn.device))
     check(rc, "flint_moe_up")
 
 
@@ -123,7 +131,7 @@ def moe_down(act: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tens
     if act.shape != (M * topk, Ih * 2) or s2.shape != (E, H, Ih // 8) or g2.numel() != E or out.shape != (M, H):
         raise _lib.FlintError("moe_down: weight / activation shapes mismatch")
     rc = lib().flint_moe_down(ptr(act), M, ptr(topk_ids), ptr(topk_weights), topk, ptr(_u8(w2)), ptr(_u8(s2)), ptr(g2), E,
-                              Ih * 2, H, ptr(out), ptr(_moe_ws(act.device, H)), 0, stream_ptr(act.device))
+                              Ih * 2, H, ptr(out), ptr(_moe_ws(act.device, H)), PDL, stream_ptr(act.device))
     check(rc, "flint_moe_down")
 
 
@@ -163,12 +171,13 @@ def attn_qkv(x: torch.Tensor, res: torch.Tensor | None, norm_w: torch.Tensor, ep
              q_norm_w: torch.Tensor | None, k_norm_w: torch.Tensor | None, eps_head: float,
              positions: torch.Tensor | None, cos_sin: torch.Tensor | None, k_cache: torch.Tensor, v_cache: torch.Tensor,
              slots: torch.Tensor | None, q_out: torch.Tensor, qkv_out: torch.Tensor, res_out: torch.Tensor,
-             write_res: bool) -> None:
-    """Fused (add +) RMSNorm + NVFP4 QKV GEMV (+ q/k norm, RoPE and paged KV write when head_mode)."""
+             write_res: bool, tokens: torch.Tensor | None = None) -> None:
+    """Fused (add +) RMSNorm + NVFP4 QKV GEMV (+ q/k norm, RoPE and paged KV write when head_mode).  With tokens
+    (int32 [M]) x is an embedding table and row m of the input is x[tokens[m]]."""
     _lib.require_cuda(x, "attn_qkv")
     _bf16_2d(x, "attn_qkv x")
     N, K = _check_nvfp4(W, S, "attn_qkv")
-    M, H = x.shape
+    M, H = (x.shape[0], x.shape[1]) if tokens is None else (tokens.numel(), x.shape[1])
     if H != K or qkv_out.shape != (M, N) or (res is not None and res.stride() != x.stride()):
         raise _lib.FlintError("attn_qkv: shape mismatch")
     if head_mode and (k_cache.dim() != 4 or k_cache.stride(3) != 1 or v_cache.stride() != k_cache.stride()):
@@ -179,18 +188,18 @@ def attn_qkv(x: torch.Tensor, res: torch.Tensor | None, norm_w: torch.Tensor, ep
         raise _lib.FlintError("attn_qkv: slots must be int64")
     cs = cos_sin if (head_mode and cos_sin is not None) else None
     rc = lib().flint_attn_qkv(
-        ptr(x), x.stride(0), ptr(res), ptr(norm_w), float(eps), ptr(_u8(W)), ptr(_u8(S)), ptr(gs), M, H, N, num_q_heads,
+        ptr(x), x.stride(0), ptr(tokens), ptr(res), ptr(norm_w), float(eps), ptr(_u8(W)), ptr(_u8(S)), ptr(gs), M, H, N, num_q_heads,
         num_kv_heads, 1 if head_mode else 0, ptr(q_norm_w), ptr(k_norm_w), float(eps_head), ptr(positions), ptr(cs),
         cs.stride(0) if cs is not None else 0, ptr(k_cache) if head_mode else None, ptr(v_cache) if head_mode else None,
         k_cache.stride(0) if head_mode else 0, k_cache.stride(1) if head_mode else 0, k_cache.stride(2) if head_mode else 0,
         k_cache.shape[1] if head_mode else 1, ptr(slots), ptr(q_out) if head_mode else None, ptr(qkv_out),
-        ptr(res_out) if write_res else None, ptr(_proj_ws(x.device)), 0, stream_ptr(x.device))
+        ptr(res_out) if write_res else None, ptr(_proj_ws(x.device)), PDL, stream_ptr(x.device))
     check(rc, "flint_attn_qkv")
 
 
 @attn_qkv.register_fake
 def _(x, res, norm_w, eps, W, S, gs, num_q_heads, num_kv_heads, head_mode, q_norm_w, k_norm_w, eps_head, positions,
-      cos_sin, k_cache, v_cache, slots, q_out, qkv_out, res_out, write_res):
+      cos_sin, k_cache, v_cache, slots, q_out, qkv_out, res_out, write_res, tokens=None):
     return None
 
 
@@ -204,7 +213,7 @@ def attn_o(a: torch.Tensor, W: torch.Tensor, S: torch.Tensor, gs: torch.Tensor, 
     if a.shape[1] != K or y.shape != (M, N):
         raise _lib.FlintError("attn_o: shape mismatch")
     rc = lib().flint_attn_o(ptr(a), a.stride(0), M, ptr(_u8(W)), ptr(_u8(S)), ptr(gs), N, K, ptr(y),
-                            ptr(_proj_ws(a.device)), 0, stream_ptr(a.device))
+                            ptr(_proj_ws(a.device)), PDL, stream_ptr(a.device))
     check(rc, "flint_attn_o")
 
 
@@ -235,10 +244,34 @@ def decode_attention(q: torch.Tensor, kv_cache: torch.Tensor, block_tables: torc
     rc = lib().flint_decode_attention(ptr(q), q.stride(0), ptr(kv_cache), nblk, Hkv, kv_cache.stride(0),
                                       kv_cache.stride(1), ptr(block_tables), block_tables.stride(0),
                                       block_tables.shape[1], ptr(seq_lens), ptr(sinks), int(window), float(scale), B, Hq,
-                                      ptr(out), out.stride(0), splits, ptr(ws), 0, stream_ptr(q.device))
+                                      ptr(out), out.stride(0), splits, ptr(ws), PDL, stream_ptr(q.device))
     check(rc, "flint_decode_attention")
 
 
 @decode_attention.register_fake
 def _(q, kv_cache, block_tables, seq_lens, sinks, window, scale, out, splits):
+    return None
+
+
+# ------------------------------------------------------------------------------------------------------------
+# device-side decode bookkeeping
+# ------------------------------------------------------------------------------------------------------------
+@torch.library.custom_op(f"{NS}::decode_advance", mutates_args=("positions", "seq_lens", "slots", "history", "step",
+                                                                 "next_tokens"))
+def decode_advance(tokens: torch.Tensor, positions: torch.Tensor, seq_lens: torch.Tensor, slots: torch.Tensor,
+                   block_tables: torch.Tensor, block_size: int, history: torch.Tensor, step: torch.Tensor,
+                   next_tokens: torch.Tensor) -> None:
+    """Record tokens in history[:, step], advance positions / seq_lens, next KV slots from the block table."""
+    _lib.require_cuda(tokens, "decode_advance")
+    M = tokens.numel()
+    rc = lib().flint_decode_advance(ptr(tokens), M, ptr(positions), ptr(seq_lens), ptr(slots), ptr(block_tables),
+                                    block_tables.stride(0), block_tables.shape[1], block_size,
+                                    ptr(history) if history.numel() else None, history.stride(0) if history.dim() else 0,
+                                    ptr(step), history.shape[1] if history.dim() == 2 else 0,
+                                    ptr(next_tokens) if next_tokens.numel() else None, PDL, stream_ptr(tokens.device))
+    check(rc, "flint_decode_advance")
+
+
+@decode_advance.register_fake
+def _(tokens, positions, seq_lens, slots, block_tables, block_size, history, step, next_tokens):
     return None

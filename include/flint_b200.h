@@ -58,6 +58,12 @@ int64_t flint_lm_head_workspace_bytes(void);
 int flint_lm_head_nv4(const void* x, int64_t ldx, int64_t M, const void* P, const void* S, float gs, int64_t V,
                       int64_t K, float* logits, int64_t ld_logits, int32_t* token_ids, void* workspace, int pdl,
                       void* stream);
+/* Same, with the model's final (residual add +) RMSNorm fused in front: x <- bf16((x + res) *
+ * rsqrt(mean((x + res)^2) + eps) * norm_w) (res may be NULL; norm_w NULL = flint_lm_head_nv4).  The
+ * reference applies model.norm before compute_logits (fast/model.py:831,924-929). */
+int flint_lm_head_nv4_fused(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, int64_t M,
+                            const void* P, const void* S, float gs, int64_t V, int64_t K, float* logits,
+                            int64_t ld_logits, int32_t* token_ids, void* workspace, int pdl, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
  * (1) MoE decode, 1..8 tokens.  Replaces fast/fp4moe_mar.cu (route_kernel 243-303, route_norm_kernel
@@ -121,8 +127,10 @@ int64_t flint_attn_proj_workspace_bytes(void);
  * from cos_sin fp32 [max_pos, 128] (cos | sin; NULL = no RoPE) at positions[m] (int64), q heads to q_out bf16
  * [M, num_q_heads*128], k heads back into qkv_out and to k_cache, v heads (unnormalised) to v_cache, at
  * element offset (slot/block_size)*stride_block + (slot%block_size)*stride_slot + kv_head*stride_head of
- * slots[m] (int64; < 0 skips the write).  H % 512 == 0. */
-int flint_attn_qkv(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, const void* W, const void* S,
+ * slots[m] (int64; < 0 skips the write).  H % 512 == 0.
+ * tokens: NULL, or int32 [M] device token ids: row m of x is then x + tokens[m] * ldx (the embedding lookup of
+ * the first layer fused into the load; res must be NULL). */
+int flint_attn_qkv(const void* x, int64_t ldx, const int32_t* tokens, const void* res, const void* norm_w, float eps, const void* W, const void* S,
                    const float* gs, int64_t M, int64_t H, int64_t N, int64_t num_q_heads, int64_t num_kv_heads,
                    int head_mode, const void* q_norm_w, const void* k_norm_w, float eps_head, const int64_t* positions,
                    const float* cos_sin, int64_t cos_sin_stride, void* k_cache, void* v_cache, int64_t stride_block,
@@ -150,6 +158,17 @@ int flint_decode_attention(const void* q, int64_t q_stride_b, const void* kv_cac
                            int64_t bt_stride, int64_t max_blocks, const int32_t* seq_lens, const float* sinks,
                            int64_t window, float scale, int64_t batch, int64_t num_q_heads, void* out, int64_t out_stride_b,
                            int64_t splits, void* workspace, int pdl, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * Decode-step bookkeeping on the device (vLLM's GPUModelRunner prepares these on the host each step):
+ * history[m, *step] = tokens[m] (if history and *step < max_steps), next_tokens[m] = tokens[m] (optional),
+ * positions[m] += 1, seq_lens[m] = positions[m] + 1,
+ * slots[m] = block_tables[m, pos / block_size] * block_size + pos % block_size (-1 past max_blocks), *step += 1.
+ * ------------------------------------------------------------------------------------------------ */
+int flint_decode_advance(const int32_t* tokens, int64_t M, int64_t* positions, int32_t* seq_lens, int64_t* slots,
+                         const int32_t* block_tables, int64_t bt_stride, int64_t max_blocks, int64_t block_size,
+                         int32_t* history, int64_t hist_stride, int32_t* step, int64_t max_steps, int32_t* next_tokens,
+                         int pdl, void* stream);
 
 #ifdef __cplusplus
 }

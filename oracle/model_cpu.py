@@ -1,0 +1,118 @@
+"""CPU baseline: the reference's dequantise-to-fp32 torch path for a full decode token -- test infrastructure only.
+
+Used by bench.py (its cpu_baseline leg and ``--impl reference``) to time the reference algorithm on the host cores:
+every NVFP4 matrix is dequantised per call exactly as the reference's ``dequantize_nvfp4`` does (LUT decode in chunks
+of 8192 rows, patch:295-319) and multiplied in fp32 (the stock path feeding ``compute_logits``, fast/fast_head.py:
+360-381, and the GEMVs of fast/attn_gemv2.cu / fp4moe_mar.cu restated on the CPU); attention is a float32 GQA
+softmax over the paged context; routing is softmax top-k renormalised.
+
+Sample: ``n_tokens`` decode tokens at ``context`` tokens of KV.  To keep host memory bounded the expert tensors of
+one layer are shared by all layers (the per-token work -- which experts are dequantised and multiplied -- is the same
+as with distinct layers); all other weights and the KV cache are per layer.  Weights are random valid NVFP4 bytes.
+"""
+from __future__ import annotations
+
+import os
+import time
+
+import torch
+
+_E2M1 = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0)
+
+
+def dequantize_nvfp4(P: torch.Tensor, S: torch.Tensor, gs: float, chunk: int = 8192) -> torch.Tensor:
+    """Restates patch:295-319: [N, K/2] u8 codes (low nibble first) and E4M3 [N, K/16] -> fp32 [N, K] * gs."""
+    lut = torch.tensor(_E2M1, dtype=torch.float32)
+    N = P.shape[0]
+    out = torch.empty((N, P.shape[1] * 2), dtype=torch.float32)
+    for a in range(0, N, chunk):
+        w = P[a:a + chunk]
+        codes = torch.stack([w & 0x0F, w >> 4], dim=-1).int()
+        vals = lut[codes].reshape(w.shape[0], -1, 16)
+        vals = vals * S[a:a + chunk].view(torch.float8_e4m3fn).float().unsqueeze(-1)
+        out[a:a + chunk] = vals.flatten(-2) * gs
+    return out
+
+
+def _rand_nvfp4(gen, N, K):
+    P = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, generator=gen)
+    S = torch.randint(0x28, 0x47, (N, K // 16), dtype=torch.uint8, generator=gen)
+    return P, S, 0.02 / 3
+
+
+def _rmsnorm(x, w, eps):
+    return (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w).to(torch.bfloat16).float()
+
+
+class CpuFlint:
+    def __init__(self, cfg, context: int, seed: int = 0):
+        g = torch.Generator().manual_seed(seed)
+        c = self.c = cfg
+        self.context = context
+        self.layers = []
+        E, I, H = c.num_experts, c.moe_inter, c.hidden
+        self.experts = [(_rand_nvfp4(g, 2 * I, H), _rand_nvfp4(g, H, I)) for _ in range(E)]
+        for _ in range(c.layers):
+            self.layers.append(dict(
+                qkv=_rand_nvfp4(g, c.qkv_rows, H), o=_rand_nvfp4(g, H, c.num_heads * c.head_dim),
+                gate=(torch.randn((E, H), generator=g) * 0.02).to(torch.bfloat16).float(),
+                k=(torch.randn((context + 64, c.num_kv_heads, c.head_dim), generator=g)).to(torch.bfloat16).float(),
+                v=(torch.randn((context + 64, c.num_kv_heads, c.head_dim), generator=g)).to(torch.bfloat16).float()))
+        self.embed = (torch.randn((c.vocab, H), generator=g)).to(torch.bfloat16)
+        self.head = _rand_nvfp4(g, c.vocab, H)
+        self.ones = torch.ones(H)
+
+    @torch.no_grad()
+    def decode_token(self, token: int, pos: int) -> int:
+        c = self.c
+        H, D, nq, nkv = c.hidden, c.head_dim, c.num_heads, c.num_kv_heads
+        res = self.embed[token].float()[None]
+        h = torch.zeros_like(res)
+        for L in self.layers:
+            res = res + h
+            x = _rmsnorm(res, self.ones, c.rms_eps)
+            P, S, gs = L["qkv"]
+            y = (x @ dequantize_nvfp4(P, S, gs).t()).to(torch.bfloat16).float()
+            q = y[:, :nq * D].reshape(nq, D)
+            L["k"][pos] = y[0, nq * D:(nq + nkv) * D].reshape(nkv, D)
+            L["v"][pos] = y[0, (nq + nkv) * D:].reshape(nkv, D)
+            K, V = L["k"][:pos + 1], L["v"][:pos + 1]
+            G = nq // nkv
+            s = torch.einsum("hgd,thd->hgt", q.reshape(nkv, G, D), K) * D ** -0.5
+            p = torch.softmax(s, dim=-1)
+            attn = torch.einsum("hgt,thd->hgd", p, V).reshape(1, nq * D).to(torch.bfloat16).float()
+            P, S, gs = L["o"]
+            a = (attn @ dequantize_nvfp4(P, S, gs).t()).to(torch.bfloat16).float()
+            res = res + a
+            xn = _rmsnorm(res, self.ones, c.rms_eps)
+            logits = (xn @ L["gate"].t()).to(torch.bfloat16).float()
+            top = torch.topk(logits[0], c.topk)
+            tw = torch.softmax(top.values, dim=-1)
+            out = torch.zeros((1, H))
+            for w, e in zip(tw.tolist(), top.indices.tolist()):
+                (P13, S13, g13), (P2, S2, g2) = self.experts[e]
+                gu = xn @ dequantize_nvfp4(P13, S13, g13).t()
+                g_, u_ = gu[:, :c.moe_inter], gu[:, c.moe_inter:]
+                act = (torch.nn.functional.silu(g_) * u_).to(torch.bfloat16).float()
+                out += w * (act @ dequantize_nvfp4(P2, S2, g2).t()).to(torch.bfloat16).float()
+            h = out.to(torch.bfloat16).float()
+        x = _rmsnorm(res + h, self.ones, c.rms_eps)
+        P, S, gs = self.head
+        return int((x @ dequantize_nvfp4(P, S, gs).t()).argmax())
+
+
+def time_decode(cfg, n_tokens: int = 1, context: int = 6057, warmup: int = 0) -> dict:
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    m = CpuFlint(cfg, context)
+    tok = 1
+    for i in range(warmup):
+        tok = m.decode_token(tok, context + i)
+    t0 = time.perf_counter()
+    for i in range(n_tokens):
+        tok = m.decode_token(tok, context + warmup + i)
+    dt = time.perf_counter() - t0
+    return {"value": round(n_tokens / dt, 5), "unit": "tok/s", "cores": threads, "kind": "port",
+            "tokens": n_tokens, "seconds": round(dt, 2),
+            "sample": f"{n_tokens} full-model decode token(s) at {context} tokens of KV context; per-call NVFP4 "
+                      "dequantisation + fp32 matmuls (torch CPU), expert tensors shared across layers"}
