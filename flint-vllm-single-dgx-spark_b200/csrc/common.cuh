@@ -129,7 +129,7 @@ __device__ __forceinline__ int xs_perm(int k) {
 // One global pass: raw bf16 goes to its permuted place in xs while the row maxima accumulate (shared atomicMax on
 // the non-negative float bits), then each element is converted in place.  red: >= rows floats.
 __device__ __forceinline__ void stage_rows_f16(const bf16* __restrict__ src, int64_t ld, int rows, int K, __half* xs,
-                                               int* shift, float* red, int nthreads, int bar) {
+                                               int* shift, float* red, int nthreads, int bar, bool cg = false) {
   const int tid = threadIdx.x;
   const int K8 = K >> 3, n = rows * K8;
   auto sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthreads) : "memory"); };
@@ -138,7 +138,8 @@ __device__ __forceinline__ void stage_rows_f16(const bf16* __restrict__ src, int
   sync();
   for (int idx = tid; idx < n; idx += nthreads) {
     const int r = idx / K8, k8 = idx - r * K8;
-    const uint4 v = reinterpret_cast<const uint4*>(src + r * ld)[k8];
+    const uint4* vp = reinterpret_cast<const uint4*>(src + r * ld) + k8;
+    const uint4 v = cg ? __ldcg(vp) : *vp;          // cg: rows written by other CTAs of this kernel
     float f[8];
     bf16x8_to_f32(v, f);
     float mx = 0.f;

@@ -12,14 +12,10 @@
 //
 // Routes of the same expert are grouped (experts ascending, routes ascending inside an expert) so each expert's
 // weights stream once per step for all tokens routed to it (mma N dimension = up to 8 routes).
-#include "engine.cuh"
+#include "moe_common.cuh"
 #include "runtime.cuh"
 
 namespace flint {
-
-constexpr int kMaxTokens = 8;
-constexpr int kMaxRoutes = 64;      // tokens x top-k
-constexpr int kMaxExperts = 512;
 
 struct MoeWorkspace {
   unsigned route_counter;
@@ -34,14 +30,6 @@ static size_t moe_ws_bytes(int H) { return sizeof(MoeWorkspace) + (size_t)kMaxRo
 // Router
 // ------------------------------------------------------------------------------------------------------------
 constexpr int kRouteWarps = 8;
-
-// top-k key: order-preserving image of the bf16 logit in the high half, 0xFFFF - expert in the low half
-// (larger logit first, then the lower expert index)
-__device__ __forceinline__ uint32_t route_key(float bf16_logit, int e) {
-  const uint32_t b = __float_as_uint(bf16_logit) >> 16;
-  const uint32_t o = (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
-  return (o << 16) | (0xFFFFu - (uint32_t)e);
-}
 
 template <int NV>   // H / 256 (uint4 of weights per lane)
 __global__ void __launch_bounds__(kRouteWarps * 32)
@@ -152,87 +140,17 @@ route_kernel(const bf16* x, int64_t ldx, const bf16* res, const bf16* __restrict
   if (!s_last) return;
   __threadfence();
 
-  // ---- last CTA: top-k per token (one warp per token) on packed (logit, expert) keys ----
-  constexpr int PER = kMaxExperts / 32;
-  const int per = E / 32;
+  // ---- last CTA: top-k per token (one warp per token) ----
   for (int m = warp; m < M; m += kRouteWarps) {
-    uint32_t key[PER];
-#pragma unroll
-    for (int j = 0; j < PER; ++j) key[j] = j < per ? route_key(__ldcg(logits + m * E + lane + 32 * j), lane + 32 * j) : 0u;
-    float l_top = 0.f, sum = 0.f, my_p = 0.f;
-    int my_e = 0;
-    for (int t = 0; t < topk; ++t) {
-      uint32_t best = 0u;
-#pragma unroll
-      for (int j = 0; j < PER; ++j) best = max(best, key[j]);
-      best = __reduce_max_sync(0xffffffffu, best);
-#pragma unroll
-      for (int j = 0; j < PER; ++j)
-        if (key[j] == best) key[j] = 0u;
-      const int eb = (int)(0xFFFFu - (best & 0xFFFFu));
-      const uint32_t ob = best >> 16;
-      const float l = __uint_as_float(((ob & 0x8000u) ? (ob & 0x7FFFu) : (~ob & 0xFFFFu)) << 16);
-      if (t == 0) l_top = l;
-      const float p = score_fn == 1 ? 1.0f / (1.0f + expf(-l)) : expf(l - l_top);
-      sum += p;
-      if (lane == t) { my_p = p; my_e = eb; }
-    }
+    int my_e;
+    float my_w;
+    warp_topk(logits + m * E, E, topk, score_fn, lane, my_e, my_w);
     if (lane < topk) {
       ids[m * topk + lane] = my_e;
-      tw[m * topk + lane] = my_p / sum;
+      tw[m * topk + lane] = my_w;
     }
   }
   if (tid == 0) atomicExch(&ws->route_counter, 0u);
-}
-
-// ------------------------------------------------------------------------------------------------------------
-// Route grouping (both expert kernels): groups of routes sharing an expert, experts ascending.
-// ------------------------------------------------------------------------------------------------------------
-struct Groups {
-  int n;                         // number of groups (distinct experts)
-  int exp[kMaxRoutes];
-  int cnt[kMaxRoutes];
-  int route[kMaxRoutes][8];      // route index m*topk + slot
-  int tok[kMaxRoutes][8];
-};
-
-__device__ __forceinline__ void build_groups(const int* ids_g, int R, int topk, int E, Groups& G, int* sorted, int* ids,
-                                             unsigned* status) {
-  const int tid = threadIdx.x;
-  if (tid < R) {
-    const int e = ids_g[tid];
-    if ((e < 0 || e >= E) && status) atomicOr(status, 2u);
-    ids[tid] = min(max(e, 0), E - 1);
-  }
-  __syncthreads();
-  if (tid < R) {
-    const int e = ids[tid];
-    int rank = 0;
-    for (int r = 0; r < R; ++r) {
-      const int f = ids[r];
-      rank += (f < e) || (f == e && r < tid);
-    }
-    sorted[rank] = tid;
-  }
-  __syncthreads();
-  if (tid == 0) {
-    int n = -1, prev = -1;
-    for (int i = 0; i < R; ++i) {
-      const int r = sorted[i];
-      const int e = ids[r];
-      if (e != prev || G.cnt[n] == 8) {
-        ++n;
-        G.exp[n] = e;
-        G.cnt[n] = 0;
-        prev = e;
-      }
-      G.route[n][G.cnt[n]] = r;
-      G.tok[n][G.cnt[n]] = r / topk;
-      ++G.cnt[n];
-    }
-    G.n = n + 1;
-  }
-  __syncthreads();
 }
 
 // ------------------------------------------------------------------------------------------------------------
@@ -300,7 +218,7 @@ moe_up_kernel(const __grid_constant__ CUtensorMap mc, const __grid_constant__ CU
   __shared__ float red[kMaxTokens];
   engine_init_bars<kUpWarps, kUpStages>(bars);
   pdl_wait();
-  build_groups(ids, M * topk, topk, E, G, sorted, ids_s, &ws->status);
+  build_groups(ids, M * topk, topk, E, G, sorted, ids_s, &ws->status, blockDim.x, 0);
   const int tpg = I / kUpBox;
   const int total = G.n * tpg;
   UpPlan plan{&mc, &ms, &G, xs, shift, g13, act, I, H, tpg, 0, (int)blockIdx.x, (int)gridDim.x};
@@ -405,7 +323,7 @@ moe_down_kernel(const __grid_constant__ CUtensorMap mc, const __grid_constant__ 
   engine_init_bars<kDnWarps, kDnStages>(bars);
   pdl_wait();
   const int R = M * topk;
-  build_groups(ids, R, topk, E, G, sorted, ids_s, &ws->status);
+  build_groups(ids, R, topk, E, G, sorted, ids_s, &ws->status, blockDim.x, 0);
   const int tpg = H / kDnBox;
   const int total = G.n * tpg;
   bf16* ybuf = reinterpret_cast<bf16*>(ws + 1);

@@ -1,0 +1,103 @@
+// MoE device helpers shared by the per-op kernels (moe.cu) and the fused decode kernel (moe_fused.cu).
+#pragma once
+#include "engine.cuh"
+
+namespace flint {
+
+constexpr int kMaxTokens = 8;
+constexpr int kMaxRoutes = 64;      // tokens x top-k
+constexpr int kMaxExperts = 512;
+
+// top-k key: order-preserving image of the bf16 logit in the high half, 0xFFFF - expert in the low half
+// (larger logit first, then the lower expert index)
+__device__ __forceinline__ uint32_t route_key(float bf16_logit, int e) {
+  const uint32_t b = __float_as_uint(bf16_logit) >> 16;
+  const uint32_t o = (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
+  return (o << 16) | (0xFFFFu - (uint32_t)e);
+}
+
+// Top-k of one token's E logits by one warp: packed (bf16 logit, expert) keys, redux.sync max per round
+// (larger logit first, lower expert on ties).  Weights: softmax over the chosen logits (score_fn 0) or sigmoid
+// scores (1), renormalised.  Lane t < topk ends with (ids[t], weights[t]).
+__device__ __forceinline__ void warp_topk(const float* logits, int E, int topk, int score_fn, int lane, int& my_e,
+                                          float& my_w) {
+  constexpr int PER = kMaxExperts / 32;
+  const int per = E / 32;
+  uint32_t key[PER];
+#pragma unroll
+  for (int j = 0; j < PER; ++j) key[j] = j < per ? route_key(__ldcg(logits + lane + 32 * j), lane + 32 * j) : 0u;
+  float l_top = 0.f, sum = 0.f, my_p = 0.f;
+  my_e = 0;
+  for (int t = 0; t < topk; ++t) {
+    uint32_t best = 0u;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) best = max(best, key[j]);
+    best = __reduce_max_sync(0xffffffffu, best);
+#pragma unroll
+    for (int j = 0; j < PER; ++j)
+      if (key[j] == best) key[j] = 0u;
+    const int eb = (int)(0xFFFFu - (best & 0xFFFFu));
+    const uint32_t ob = best >> 16;
+    const float l = __uint_as_float(((ob & 0x8000u) ? (ob & 0x7FFFu) : (~ob & 0xFFFFu)) << 16);
+    if (t == 0) l_top = l;
+    const float p = score_fn == 1 ? 1.0f / (1.0f + expf(-l)) : expf(l - l_top);
+    sum += p;
+    if (lane == t) { my_p = p; my_e = eb; }
+  }
+  my_w = my_p / sum;
+}
+
+// ------------------------------------------------------------------------------------------------------------
+// Route grouping (both expert kernels): groups of routes sharing an expert, experts ascending.
+// ------------------------------------------------------------------------------------------------------------
+struct Groups {
+  int n;                         // number of groups (distinct experts)
+  int exp[kMaxRoutes];
+  int cnt[kMaxRoutes];
+  int route[kMaxRoutes][8];      // route index m*topk + slot
+  int tok[kMaxRoutes][8];
+};
+
+// Threads [0, nthreads) of the block call it and synchronise on named barrier `bar` (0 with nthreads == blockDim.x
+// is __syncthreads).
+__device__ __forceinline__ void build_groups(const int* ids_g, int R, int topk, int E, Groups& G, int* sorted, int* ids,
+                                             unsigned* status, int nthreads, int bar) {
+  const int tid = threadIdx.x;
+  auto sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthreads) : "memory"); };
+  if (tid < R) {
+    const int e = ids_g[tid];
+    if ((e < 0 || e >= E) && status) atomicOr(status, 2u);
+    ids[tid] = min(max(e, 0), E - 1);
+  }
+  sync();
+  if (tid < R) {
+    const int e = ids[tid];
+    int rank = 0;
+    for (int r = 0; r < R; ++r) {
+      const int f = ids[r];
+      rank += (f < e) || (f == e && r < tid);
+    }
+    sorted[rank] = tid;
+  }
+  sync();
+  if (tid == 0) {
+    int n = -1, prev = -1;
+    for (int i = 0; i < R; ++i) {
+      const int r = sorted[i];
+      const int e = ids[r];
+      if (e != prev || G.cnt[n] == 8) {
+        ++n;
+        G.exp[n] = e;
+        G.cnt[n] = 0;
+        prev = e;
+      }
+      G.route[n][G.cnt[n]] = r;
+      G.tok[n][G.cnt[n]] = r / topk;
+      ++G.cnt[n];
+    }
+    G.n = n + 1;
+  }
+  sync();
+}
+
+}  // namespace flint

@@ -1,0 +1,388 @@
+// (1) Fused MoE decode block: one persistent kernel per MoE layer for 1..8 tokens.
+// Replaces the reference's three-kernel chain route_norm_kernel -> up_mar -> down_mar (fast/fp4moe_mar.cu:311-417,
+// 67-152, 157-233; driven by fast/model.py:302-310) with one launch of one CTA per SM and three grid barriers:
+//
+//   R  every CTA: s = x + res, xn = bf16(RMSNorm(s)) (same fixed order everywhere); CTA 0 publishes res_out / xn;
+//      CTAs own router rows e = cta, cta + grid (weights prefetched into registers before the PDL wait) and write
+//      bf16 logits                                                                          -> grid barrier 0
+//   U  every CTA: top-k of each token from the logits (redundant, identical), routes grouped by expert;
+//      each CTA streams its share of (gate 64 rows + up 64 rows) x H tiles through the TMA ring and writes
+//      act = bf16(silu(g) * u); the producer warp keeps streaming the CTA's down tiles behind them
+//                                                                                           -> grid barrier 1
+//   D  stage all act rows, y = bf16(act . W2[e] * gs2[e]) for the CTA's 128-row down tiles -> grid barrier 2
+//   F  out[m, r] = bf16(sum_s tw[m, s] * y[m*k + s, r]) in slot order for the CTA's rows
+//
+// Numerics are those of the per-op kernels in moe.cu (same reduction orders), so routing is bit identical to them.
+// Up and down tiles are split over CTAs by a linear partition of their stage counts (balanced to within one tile).
+#include "gridsync.cuh"
+#include "moe_common.cuh"
+#include "runtime.cuh"
+
+namespace flint {
+
+constexpr int kFW = 8, kFBox = 64;
+
+struct MoeFusedWs {
+  GridSync sync;
+  unsigned status;
+  unsigned pad[31];
+  // followed by: logits fp32 [8][E], act bf16 [64][I], y bf16 [64][H]
+};
+
+struct MoeFusedArgs {
+  const bf16* x;
+  int64_t ldx;
+  const bf16* res;
+  const bf16* nw;
+  float eps;
+  const bf16* gate_w;
+  int E, topk, score_fn;
+  const float* g13;
+  const float* g2;
+  int M, H, I;
+  bf16* out;
+  bf16* res_out;
+  bf16* xn_out;
+  float* logits_out;
+  int* ids_out;
+  float* tw_out;
+  MoeFusedWs* ws;
+};
+
+__host__ __device__ inline size_t moe_fused_ws_bytes(int E, int H, int I) {
+  return sizeof(MoeFusedWs) + (size_t)kMaxTokens * E * 4 + (size_t)kMaxRoutes * I * 2 + (size_t)kMaxRoutes * H * 2;
+}
+
+// first tile whose stage prefix reaches `target` (prefix = nu * min(i, U) + nd * max(0, i - U), strictly increasing)
+__device__ __forceinline__ int tile_at(long target, int U, int nu, int nd) {
+  if (target <= (long)U * nu) return (int)((target + nu - 1) / nu);
+  return U + (int)((target - (long)U * nu + nd - 1) / nd);
+}
+
+template <int NS, int NV>
+__global__ void __launch_bounds__((kFW + 1) * 32, 1)
+moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant__ CUtensorMap up_s,
+                 const __grid_constant__ CUtensorMap dn_c, const __grid_constant__ CUtensorMap dn_s, const MoeFusedArgs a) {
+  using L = EngineSmem<kFW, NS, kFBox>;
+  constexpr int NT = kFW * 32;              // consumer threads
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* dtile = reinterpret_cast<float*>(smem + L::ring_bytes);
+  __half* xs = reinterpret_cast<__half*>(smem + L::ring_bytes + L::dtile_bytes);        // f16 [M][H+8]
+  uint8_t* region = reinterpret_cast<uint8_t*>(xs + a.M * xs_stride(a.H));              // phase R: bf16 xn; D: f16 act
+  bf16* xnb = reinterpret_cast<bf16*>(region);
+  __half* xa = reinterpret_cast<__half*>(region);
+  __shared__ uint64_t bars[2 * NS];
+  __shared__ uint64_t plan_bar;
+  __shared__ Groups G;
+  __shared__ int sorted[kMaxRoutes], ids_s[kMaxRoutes], ids_c[kMaxRoutes];
+  __shared__ float tw_s[kMaxRoutes];
+  __shared__ int shift_x[kMaxTokens], shift_a[kMaxRoutes];
+  __shared__ float red[kFW * kMaxRoutes];
+  __shared__ int s_ok;
+  __shared__ int tiles[4];                   // first / end tile of this CTA, U, total
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int M = a.M, H = a.H, I = a.I, E = a.E, topk = a.topk, R = M * topk;
+  const unsigned nb = gridDim.x;
+  MoeFusedWs* ws = a.ws;
+  unsigned* status = &ws->status;
+  float* lg = reinterpret_cast<float*>(ws + 1);
+  bf16* act_g = reinterpret_cast<bf16*>(lg + kMaxTokens * E);
+  bf16* y_g = act_g + (size_t)kMaxRoutes * I;
+  const int nks_up = H / kSliceK, nks_dn = I / kSliceK;
+  const int tpu = I / kFBox, tpd = H / (2 * kFBox);
+
+  if (tid == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&bars[i], 1);
+      mbar_init(&bars[NS + i], kFW);
+    }
+    mbar_init(&plan_bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  // router rows of this CTA: e = blockIdx.x (+ gridDim.x), one warp each, prefetched before the wait
+  const int my_row = blockIdx.x + warp * nb;
+  const bool has_row = warp < 2 && my_row < E;
+  uint4 wv[NV];
+  if (has_row) {
+    const uint4* wp = reinterpret_cast<const uint4*>(a.gate_w + (int64_t)my_row * H);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) wv[i] = ldg_stream_v4(wp + lane + 32 * i);
+  }
+  pdl_wait();
+
+  if (warp == kFW) {
+    // ---------------- producer: wait for the routing plan, then stream up tiles followed by down tiles ----------------
+    if (lane == 0) {
+      bool ok = false;
+      for (unsigned i = 0; i < FLINT_WAIT_LIMIT && !ok; ++i) ok = mbar_try_wait(&plan_bar, 0);
+      if (!ok) {
+        atomicOr(status, STATUS_WAIT_TIMEOUT);
+        return;
+      }
+      tma_prefetch_desc(&up_c);
+      tma_prefetch_desc(&dn_c);
+      const int t0 = tiles[0], t1 = tiles[1], U = tiles[2];
+      int slot = 0, s = 0;
+      unsigned phase = 0;
+      for (int t = t0; t < t1; ++t) {
+        const bool up = t < U;
+        const int nks = up ? nks_up : nks_dn;
+        int y0, y1;
+        if (up) {
+          const int u = t / tpu, j = t - u * tpu, e = G.exp[u];
+          y0 = e * 2 * I + j * kFBox;
+          y1 = y0 + I;
+        } else {
+          const int td = t - U, u = td / tpd, j = td - u * tpd;
+          y0 = G.exp[u] * H + j * 2 * kFBox;
+          y1 = y0 + kFBox;
+        }
+        const CUtensorMap* mc = up ? &up_c : &dn_c;
+        const CUtensorMap* ms = up ? &up_s : &dn_s;
+        for (int ks = 0; ks < nks; ++ks, ++s) {
+          if (s >= NS && !mbar_wait(&bars[NS + slot], phase ^ 1u, status)) return;
+          mbar_arrive_expect_tx(&bars[slot], L::code_bytes + L::scale_bytes);
+          uint8_t* cdst = smem + slot * L::code_bytes;
+          uint8_t* sdst = smem + NS * L::code_bytes + slot * L::scale_bytes;
+          tma_load_2d(cdst, mc, ks * 128, y0, &bars[slot]);
+          tma_load_2d(sdst, ms, ks * 16, y0, &bars[slot]);
+          tma_load_2d(cdst + kFBox * 128, mc, ks * 128, y1, &bars[slot]);
+          tma_load_2d(sdst + kFBox * 16, ms, ks * 16, y1, &bars[slot]);
+          if (++slot == NS) { slot = 0; phase ^= 1u; }
+        }
+      }
+    }
+    return;
+  }
+
+  // ---------------- phase R: norm, router rows ----------------
+  add_rmsnorm_2pass(a.x, a.ldx, a.res, a.nw, a.eps, M, H, xnb, red, NT, 2);
+  if (blockIdx.x == 0) {
+    for (int idx = tid; idx < M * (H / 8); idx += NT) {
+      const int m = idx / (H / 8), k8 = idx - m * (H / 8);
+      if (a.xn_out) reinterpret_cast<uint4*>(a.xn_out + (int64_t)m * H)[k8] = reinterpret_cast<const uint4*>(xnb + m * H)[k8];
+      if (a.res_out) {
+        float f[8], g[8];
+        bf16x8_to_f32(reinterpret_cast<const uint4*>(a.x + m * a.ldx)[k8], f);
+        if (a.res) {
+          bf16x8_to_f32(reinterpret_cast<const uint4*>(a.res + m * a.ldx)[k8], g);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) f[j] += g[j];
+        }
+        uint32_t rk[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          __nv_bfloat162 r2 = __floats2bfloat162_rn(f[2 * j], f[2 * j + 1]);
+          rk[j] = *reinterpret_cast<uint32_t*>(&r2);
+        }
+        reinterpret_cast<uint4*>(a.res_out + (int64_t)m * H)[k8] = make_uint4(rk[0], rk[1], rk[2], rk[3]);
+      }
+    }
+  }
+  if (has_row) {
+    for (int m = 0; m < M; ++m) {
+      const uint4* xp = reinterpret_cast<const uint4*>(xnb + m * H);
+      float acc = 0.f;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        float xf[8], wf[8];
+        bf16x8_to_f32(xp[lane + 32 * i], xf);
+        bf16x8_to_f32(wv[i], wf);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc = fmaf(wf[j], xf[j], acc);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0) __stcg(lg + m * E + my_row, bf16r(acc));
+    }
+  }
+  stage_rows_f16(xnb, H, M, H, xs, shift_x, red, NT, 2);
+  if (!grid_sync(&ws->sync, nb, 0, NT, 2, &s_ok, status)) return;
+
+  // ---------------- phase U: top-k, groups, plan, gate/up tiles ----------------
+  if (warp < M) {
+    int my_e;
+    float my_w;
+    warp_topk(lg + warp * E, E, topk, a.score_fn, lane, my_e, my_w);
+    if (lane < topk) {
+      ids_s[warp * topk + lane] = my_e;
+      tw_s[warp * topk + lane] = my_w;
+      if (blockIdx.x == 0) {
+        if (a.ids_out) a.ids_out[warp * topk + lane] = my_e;
+        if (a.tw_out) a.tw_out[warp * topk + lane] = my_w;
+      }
+    }
+  }
+  if (blockIdx.x == 0 && a.logits_out)
+    for (int i = tid; i < M * E; i += NT) a.logits_out[i] = __ldcg(lg + i);
+  named_bar_sync(2, NT);
+  build_groups(ids_s, R, topk, E, G, sorted, ids_c, status, NT, 2);
+  const int U = G.n * tpu, Dn = G.n * tpd;
+  const long total = (long)U * nks_up + (long)Dn * nks_dn;
+  const long tau = (total + nb - 1) / nb;
+  const int t0 = min(tile_at((long)blockIdx.x * tau, U, nks_up, nks_dn), U + Dn);
+  const int t1 = min(tile_at((long)(blockIdx.x + 1) * tau, U, nks_up, nks_dn), U + Dn);
+  if (tid == 0) {
+    tiles[0] = t0;
+    tiles[1] = t1;
+    tiles[2] = U;
+    mbar_arrive(&plan_bar);                  // release the producer
+  }
+
+  const int g = lane >> 2, t = lane & 3;
+  const int prow = 16 * warp + tile_phi(g);
+  int slot = 0;
+  unsigned phase = 0;
+  bool ok = true;
+  auto run_tile = [&](int nks, const __half* xrow, bool active, float (&d)[4]) {
+    float acc[4][4];
+    zero_acc(acc);
+    for (int ks = 0; ks < nks; ++ks) {
+      if (ok && !mbar_wait(&bars[slot], phase, status)) ok = false;
+      if (ok)
+        consume_stage(smem + slot * L::code_bytes, smem + NS * L::code_bytes + slot * L::scale_bytes, warp, g, t, ks, xrow,
+                      active, acc);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[NS + slot]);
+      if (++slot == NS) { slot = 0; phase ^= 1u; }
+    }
+    sum_acc(acc, d);
+  };
+  auto store_dtile = [&](const float (&d)[4]) {
+    dtile[prow * 8 + 2 * t] = d[0];
+    dtile[prow * 8 + 2 * t + 1] = d[1];
+    dtile[(prow + 8) * 8 + 2 * t] = d[2];
+    dtile[(prow + 8) * 8 + 2 * t + 1] = d[3];
+    named_bar_sync(1, NT);
+  };
+
+  for (int tt = t0; tt < min(t1, U); ++tt) {
+    const int u = tt / tpu, j = tt - u * tpu, cnt = G.cnt[u], e = G.exp[u];
+    const bool active = g < cnt;
+    float d[4];
+    run_tile(nks_up, xs + (active ? G.tok[u][g] : 0) * xs_stride(H), active, d);
+    store_dtile(d);
+    for (int idx = tid; idx < kFBox * 8; idx += NT) {
+      const int n = idx / kFBox, r = idx - n * kFBox;
+      if (n >= cnt) continue;
+      const float sc = ldexpf(a.g13[e], -shift_x[G.tok[u][n]]);
+      const float gv = dtile[r * 8 + n] * sc, uv = dtile[(kFBox + r) * 8 + n] * sc;
+      const float silu = gv / (1.0f + expf(-gv));
+      __stcg(reinterpret_cast<unsigned short*>(act_g + (int64_t)G.route[u][n] * I + j * kFBox + r),
+             __bfloat16_as_ushort(__float2bfloat16_rn(silu * uv)));
+    }
+    named_bar_sync(1, NT);
+  }
+  if (!grid_sync(&ws->sync, nb, 1, NT, 2, &s_ok, status)) return;
+
+  // ---------------- phase D: down tiles ----------------
+  if (t1 > U) stage_rows_f16(act_g, I, R, I, xa, shift_a, red, NT, 2, true);
+  for (int tt = max(t0, U); tt < t1; ++tt) {
+    const int td = tt - U, u = td / tpd, j = td - u * tpd, cnt = G.cnt[u], e = G.exp[u];
+    const bool active = g < cnt;
+    float d[4];
+    run_tile(nks_dn, xa + (active ? G.route[u][g] : 0) * xs_stride(I), active, d);
+    store_dtile(d);
+    for (int idx = tid; idx < 2 * kFBox * 8; idx += NT) {
+      const int n = idx / (2 * kFBox), r = idx - n * (2 * kFBox);
+      if (n >= cnt) continue;
+      const int route = G.route[u][n];
+      const float y = dtile[r * 8 + n] * ldexpf(a.g2[e], -shift_a[route]);
+      __stcg(reinterpret_cast<unsigned short*>(y_g + (int64_t)route * H + j * 2 * kFBox + r),
+             __bfloat16_as_ushort(__float2bfloat16_rn(y)));
+    }
+    named_bar_sync(1, NT);
+  }
+  pdl_trigger();
+  if (!grid_sync(&ws->sync, nb, 2, NT, 2, &s_ok, status)) return;
+
+  // ---------------- phase F: weighted sum in slot order ----------------
+  const int rows_per = (H + nb - 1) / nb;
+  const int r0 = blockIdx.x * rows_per, r1 = min(H, r0 + rows_per);
+  for (int idx = tid; idx < (r1 - r0) * M; idx += NT) {
+    const int m = idx / (r1 - r0), r = r0 + idx - m * (r1 - r0);
+    float acc = 0.f;
+    for (int s = 0; s < topk; ++s) {
+      const unsigned short b = __ldcg(reinterpret_cast<const unsigned short*>(y_g + (int64_t)(m * topk + s) * H + r));
+      acc = fmaf(tw_s[m * topk + s], bf16_bits_to_f32(b), acc);
+    }
+    a.out[(int64_t)m * H + r] = __float2bfloat16_rn(acc);
+  }
+  grid_sync_retire(&ws->sync, nb);
+}
+
+template <int NS, int NV>
+static int launch_fused(int sms, const CUtensorMap& uc, const CUtensorMap& us, const CUtensorMap& dc, const CUtensorMap& ds,
+                        const MoeFusedArgs& a, int pdl, void* stream) {
+  using L = EngineSmem<kFW, NS, kFBox>;
+  const size_t region = std::max((size_t)a.M * a.topk * xs_stride(a.I) * 2, (size_t)a.M * a.H * 2);
+  const size_t smem = 1024 + L::ring_bytes + L::dtile_bytes + (size_t)a.M * xs_stride(a.H) * 2 + region;
+  if (smem > 227 * 1024) return FLINT_ERR_SHAPE;
+  auto kern = moe_fused_kernel<NS, NV>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return FLINT_ERR_LAUNCH;
+  set_max_carveout(kern);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(sms);
+  cfg.blockDim = dim3((kFW + 1) * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeCooperative;
+  at[0].val.cooperative = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 2 : 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, uc, us, dc, ds, a);
+  return e == cudaSuccess ? FLINT_OK : FLINT_ERR_LAUNCH;
+}
+
+}  // namespace flint
+
+using namespace flint;
+
+extern "C" int64_t flint_moe_fused_workspace_bytes(int64_t E, int64_t H, int64_t I) {
+  return (int64_t)moe_fused_ws_bytes((int)E, (int)H, (int)I);
+}
+
+extern "C" int flint_moe_fused(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, const void* gate_w,
+                               int64_t M, int64_t H, int64_t E, int64_t topk, int score_fn, const void* w13, const void* s13,
+                               const float* g13, const void* w2, const void* s2, const float* g2, int64_t I, void* out,
+                               void* res_out, void* xn_out, float* logits_out, int32_t* topk_ids_out,
+                               float* topk_weights_out, void* workspace, int pdl, void* stream) {
+  if (!x || !norm_w || !gate_w || !w13 || !s13 || !g13 || !w2 || !s2 || !g2 || !out || !workspace) return FLINT_ERR_ARGUMENT;
+  const int sms = num_sms();
+  if (sms <= 0) return FLINT_ERR_DEVICE;
+  if (M < 1 || M > kMaxTokens || (H != 2048 && H != 4096) || E < 32 || E % 32 != 0 || E > 2 * sms || topk < 1 ||
+      topk > 32 || topk > E || M * topk > kMaxRoutes || I < kSliceK || I % kSliceK != 0 || I > 8192 || ldx < H ||
+      ldx % 8 != 0 || (score_fn != 0 && score_fn != 1))
+    return FLINT_ERR_SHAPE;
+  if (!aligned(x, 16) || (res && !aligned(res, 16)) || !aligned(norm_w, 16) || !aligned(gate_w, 16) || !aligned(w13, 16) ||
+      !aligned(s13, 16) || !aligned(w2, 16) || !aligned(s2, 16) || !aligned(out, 16) || (res_out && !aligned(res_out, 16)) ||
+      (xn_out && !aligned(xn_out, 16)) || !aligned(workspace, 16))
+    return FLINT_ERR_ALIGN;
+  if (res_out && !res) return FLINT_ERR_ARGUMENT;
+  CUtensorMap uc, us, dc, ds;
+  int rc = encode_u8_2d(&uc, w13, H / 2, E * 2 * I, H / 2, 128, kFBox, true);
+  if (!rc) rc = encode_u8_2d(&us, s13, H / 16, E * 2 * I, H / 16, 16, kFBox, false);
+  if (!rc) rc = encode_u8_2d(&dc, w2, I / 2, E * H, I / 2, 128, kFBox, true);
+  if (!rc) rc = encode_u8_2d(&ds, s2, I / 16, E * H, I / 16, 16, kFBox, false);
+  if (rc) return rc;
+  MoeFusedArgs a;
+  a.x = (const bf16*)x; a.ldx = ldx; a.res = (const bf16*)res; a.nw = (const bf16*)norm_w; a.eps = eps;
+  a.gate_w = (const bf16*)gate_w; a.E = (int)E; a.topk = (int)topk; a.score_fn = score_fn; a.g13 = g13; a.g2 = g2;
+  a.M = (int)M; a.H = (int)H; a.I = (int)I; a.out = (bf16*)out; a.res_out = (bf16*)res_out; a.xn_out = (bf16*)xn_out;
+  a.logits_out = logits_out; a.ids_out = (int*)topk_ids_out; a.tw_out = topk_weights_out;
+  a.ws = static_cast<MoeFusedWs*>(workspace);
+  if (H == 2048) {
+    if (M <= 2) return launch_fused<6, 8>(sms, uc, us, dc, ds, a, pdl, stream);
+    return launch_fused<4, 8>(sms, uc, us, dc, ds, a, pdl, stream);
+  }
+  if (M <= 2) return launch_fused<6, 16>(sms, uc, us, dc, ds, a, pdl, stream);
+  return launch_fused<4, 16>(sms, uc, us, dc, ds, a, pdl, stream);
+}

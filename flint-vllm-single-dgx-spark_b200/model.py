@@ -5,8 +5,7 @@ FlintAttention.forward_af 596-657, FlintSparseMoeBlock._forward_decode_rn 302-31
 
     layer l:  q, res = qkv_head(h, res)          add + RMSNorm + QKV + q/k norm + RoPE + KV write
               a = o_gemv(decode_attention(q))
-              tw, ti, xn, res = route_norm(a, res)   add + RMSNorm + router + top-k
-              h = moe_down(moe_up(xn, ti), ti, tw)
+              h, res = moe_fused(a, res)          add + RMSNorm + router + top-k + gate/up + SwiGLU + down + sum
     head:     token = argmax(lm_head(final_norm(h + res)))
 
 with the BASELINE.json shapes (hidden 2048, 48 layers, 32/4 heads of 128, 128 experts top-8 softmax, I = 768,
@@ -142,7 +141,7 @@ class Decoder:
         self.splits = _ops.attention_splits(M, c.num_kv_heads)
         self.scale = c.head_dim ** -0.5
         self.graphs: dict[str, torch.cuda.CUDAGraph] = {}
-        self.launches_per_step = 6 * c.layers + 2      # 6 kernels per layer + head + advance
+        self.launches_per_step = 4 * c.layers + 2      # qkv, attention, o, fused MoE per layer + head + advance
 
     # ---- one decode step as torch ops on persistent buffers ----
     def _layers(self):
@@ -163,10 +162,8 @@ class Decoder:
             Po, So, gso = L["o"]
             ops.attn_o(self.attn.view(self.M, -1), Po, So, gso, self.a)
             ew = L["experts"]
-            ops.moe_route(self.a, self.res_a, L["ln2"], c.rms_eps, L["gate"], c.topk, ew.score_fn, self.lg, self.ti,
-                          self.tw, self.xn, self.res_b, True, True)
-            ops.moe_up(self.xn, self.ti, ew.w13, ew.s13, ew.g13, self.act)
-            ops.moe_down(self.act, self.ti, self.tw, ew.w2, ew.s2, ew.g2, self.h)
+            ops.moe_fused(self.a, self.res_a, L["ln2"], c.rms_eps, L["gate"], c.topk, ew.score_fn, ew.w13, ew.s13, ew.g13,
+                          ew.w2, ew.s2, ew.g2, self.h, self.res_b, self.xn, self.lg, self.ti, self.tw, False)
 
     def _head_and_advance(self):
         P, S, gs = self.m.head

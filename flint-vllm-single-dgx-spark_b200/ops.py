@@ -140,6 +140,37 @@ def _(act, topk_ids, topk_weights, w2, s2, g2, out):
     return None
 
 
+@torch.library.custom_op(f"{NS}::moe_fused", mutates_args=("out", "res_out", "xn_out", "logits_out", "ids_out",
+                                                             "tw_out"))
+def moe_fused(x: torch.Tensor, res: torch.Tensor | None, norm_w: torch.Tensor, eps: float, gate_w: torch.Tensor, topk: int,
+              score_fn: int, w13: torch.Tensor, s13: torch.Tensor, g13: torch.Tensor, w2: torch.Tensor, s2: torch.Tensor,
+              g2: torch.Tensor, out: torch.Tensor, res_out: torch.Tensor, xn_out: torch.Tensor, logits_out: torch.Tensor,
+              ids_out: torch.Tensor, tw_out: torch.Tensor, write_extras: bool) -> None:
+    """The whole decode MoE block in one persistent launch: (add +) RMSNorm, router, top-k, gate/up + SwiGLU, down,
+    weighted sum.  res_out always written when res is given; xn / logits / ids / weights when write_extras."""
+    _lib.require_cuda(x, "moe_fused")
+    _bf16_2d(x, "moe_fused x")
+    M, H = x.shape
+    E, I2, Hh = w13.shape
+    if Hh * 2 != H or gate_w.shape != (E, H) or out.shape != (M, H):
+        raise _lib.FlintError("moe_fused: shape mismatch")
+    nbytes = lib().flint_moe_fused_workspace_bytes(E, H, I2 // 2)
+    ws = _lib.workspace(x.device, f"moe_fused_{E}_{H}_{I2 // 2}", nbytes)
+    ex = write_extras
+    rc = lib().flint_moe_fused(ptr(x), x.stride(0), ptr(res), ptr(norm_w), float(eps), ptr(gate_w), M, H, E, topk, score_fn,
+                               ptr(_u8(w13)), ptr(_u8(s13)), ptr(g13), ptr(_u8(w2)), ptr(_u8(s2)), ptr(g2), I2 // 2,
+                               ptr(out), ptr(res_out) if res is not None else None, ptr(xn_out) if ex else None,
+                               ptr(logits_out) if ex else None, ptr(ids_out) if ex else None, ptr(tw_out) if ex else None,
+                               ptr(ws), PDL, stream_ptr(x.device))
+    check(rc, "flint_moe_fused")
+
+
+@moe_fused.register_fake
+def _(x, res, norm_w, eps, gate_w, topk, score_fn, w13, s13, g13, w2, s2, g2, out, res_out, xn_out, logits_out, ids_out,
+      tw_out, write_extras):
+    return None
+
+
 @torch.library.custom_op(f"{NS}::moe_align", mutates_args=("sorted_ids", "expert_ids", "num_tokens_post_pad"))
 def moe_align(topk_ids: torch.Tensor, num_experts: int, block_size: int, sorted_ids: torch.Tensor,
               expert_ids: torch.Tensor, num_tokens_post_pad: torch.Tensor) -> None:

@@ -100,6 +100,19 @@ int flint_moe_down(const void* act, int64_t M, const int32_t* topk_ids, const fl
                    const void* w2, const void* s2, const float* g2, int64_t E, int64_t I, int64_t H, void* out,
                    void* workspace, int pdl, void* stream);
 
+/* The whole decode MoE block in ONE persistent launch (one CTA per SM, three grid barriers): router
+ * (+ residual add + RMSNorm) -> top-k -> gate/up GEMV + SwiGLU -> down GEMV -> weighted sum, the three-kernel
+ * chain route_norm / moe_up / moe_down (fast/fp4moe_decode.py:70-95, fast/model.py:302-310) fused, with the same
+ * numerics and routing as flint_moe_route / flint_moe_up / flint_moe_down above.  out bf16 [M, H]; res_out,
+ * xn_out, logits_out, topk_ids_out, topk_weights_out optional (NULL).  H in {2048, 4096}, E % 32 == 0,
+ * E <= 2 * SMs, I % 256 == 0, M <= 8.  workspace: flint_moe_fused_workspace_bytes(E, H, I), zeroed once. */
+int64_t flint_moe_fused_workspace_bytes(int64_t E, int64_t H, int64_t I);
+int flint_moe_fused(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, const void* gate_w,
+                    int64_t M, int64_t H, int64_t E, int64_t topk, int score_fn, const void* w13, const void* s13,
+                    const float* g13, const void* w2, const void* s2, const float* g2, int64_t I, void* out,
+                    void* res_out, void* xn_out, float* logits_out, int32_t* topk_ids_out, float* topk_weights_out,
+                    void* workspace, int pdl, void* stream);
+
 /* ------------------------------------------------------------------------------------------------
  * (2) Deterministic moe_align_block_size.  Replaces fast/patch_align.py:11-30 (_deterministic_align), the
  * vLLM call-site contract of moe_align_block_size (same buffers, same outputs): routes of each expert in

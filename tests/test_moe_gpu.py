@@ -122,3 +122,29 @@ def test_moe_layer_end_to_end_and_graph(fb, M):
         g.replay()
     torch.cuda.synchronize()
     np.testing.assert_array_equal(host(out_g), host(out))             # deterministic across replays
+
+
+@needs_cuda
+@pytest.mark.parametrize("cfg,M", [(BASE, 1), (BASE, 8), (FLINT, 1), (FLINT, 4)])
+def test_fused_moe_matches_three_kernel_chain(fb, cfg, M):
+    """The persistent fused MoE kernel gives bit-identical routing and outputs to route_norm -> up -> down."""
+    from flint_b200 import fp4moe_decode as fm
+    rng = np.random.default_rng(200 + M + cfg["E"])
+    H, E, topk = cfg["H"], cfg["E"], cfg["topk"]
+    L = make_layer(rng, **cfg)
+    w = dev_weights(L, topk, cfg["score"])
+    x, res = dev_bf16(bf16(rng, (M, H))), dev_bf16(bf16(rng, (M, H)))
+    nw, gate = dev_bf16(L["nw"]), dev_bf16(L["gate"])
+    ref_out, ref_res = fm.moe_decode(x, res, nw, 1e-6, gate, w, fused=False)
+    tw, ti, xn, _ = fm.route_norm(x, res, nw, 1e-6, gate, topk=topk, score=cfg["score"])
+    out, res_out, (xn_f, lg_f, ti_f, tw_f) = fm.moe_decode(x, res, nw, 1e-6, gate, w, fused=True, extras=True)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(host(ti_f), host(ti))
+    np.testing.assert_array_equal(host(tw_f), host(tw))
+    np.testing.assert_array_equal(host(xn_f), host(xn))
+    np.testing.assert_array_equal(host(res_out), host(ref_res))
+    np.testing.assert_array_equal(host(out), host(ref_out))
+    for _ in range(3):                                     # the grid barrier resets itself between launches
+        out2, _ = fm.moe_decode(x, res, nw, 1e-6, gate, w, fused=True)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(host(out2), host(ref_out))
