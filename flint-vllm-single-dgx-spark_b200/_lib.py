@@ -27,6 +27,7 @@ SIGNATURES: dict[str, tuple] = {
     "flint_error_string": (ctypes.c_char_p, [I32]),
     "flint_lm_head_workspace_bytes": (I64, []),
     "flint_lm_head_nv4": (I32, [P, I64, I64, P, P, F32, I64, I64, P, I64, P, P, I32, P]),
+    "flint_lm_head_nv4_noalloc": (I32, [P, I64, I64, P, P, F32, I64, I64, P, I64, P, I32, P]),
     "flint_lm_head_nv4_fused": (I32, [P, I64, P, P, F32, I64, P, P, F32, I64, I64, P, I64, P, P, I32, P]),
     "flint_moe_workspace_bytes": (I64, [I64]),
     "flint_moe_route": (I32, [P, I64, P, P, F32, P, I64, I64, I64, I64, I32, P, P, P, P, P, P, I32, P]),

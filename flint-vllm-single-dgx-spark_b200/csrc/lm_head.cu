@@ -56,3 +56,52 @@ extern "C" int flint_lm_head_nv4(const void* x, int64_t ldx, int64_t M, const vo
   return flint_lm_head_nv4_fused(x, ldx, nullptr, nullptr, 0.f, M, P, S, gs, V, K, logits, ld_logits, token_ids, workspace,
                                  pdl, stream);
 }
+
+// -------------------------------------------------------------------------------------------------------------------
+// Allocation-free variant of flint_lm_head_nv4.
+//
+// Some callers cannot allocate device memory when they call the head: an inference engine that has handed all free
+// HBM to its KV-cache pool up front, code running inside a CUDA-graph capture (where cudaMalloc is not allowed),
+// or a host runtime that reaches this library only through a C FFI and owns no CUDA allocator.  For them the
+// argmax scratch (the per-row best keys and the CTA arrival counter) lives in the file-scope array below, one copy
+// per device, held by every GPU that loads the library until the process exits.  The caller still provides x, the
+// weights and the outputs.
+//
+// Limits: at most kNoAllocMaxRows = 8 rows per call (the scratch holds 8 argmax slots; larger requests are refused
+// with FLINT_ERR_SCRATCH).  Every call uses the same scratch: it is cleared at the start of each call, and calls
+// that overlap on the GPU (different streams, or devices sharing nothing but this array's copy per device) race on
+// it, so issue them in one stream per device.  The first call on a device looks up the array's device address
+// (cudaGetSymbolAddress with that device current); make that first call before any stream capture.
+// -------------------------------------------------------------------------------------------------------------------
+namespace flint {
+
+constexpr int kNoAllocMaxRows = 8;
+static __device__ __align__(256) unsigned char g_head_noalloc_scratch[256];
+static_assert(sizeof(HeadWorkspace) <= sizeof(g_head_noalloc_scratch), "scratch too small for the argmax workspace");
+static void* g_head_noalloc_ptr[64] = {nullptr};
+
+static void* head_noalloc_scratch() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (g_head_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_head_noalloc_scratch) != cudaSuccess) return nullptr;
+    g_head_noalloc_ptr[dev] = p;
+  }
+  return g_head_noalloc_ptr[dev];
+}
+
+}  // namespace flint
+
+extern "C" int flint_lm_head_nv4_noalloc(const void* x, int64_t ldx, int64_t M, const void* P, const void* S, float gs,
+                                         int64_t V, int64_t K, float* logits, int64_t ld_logits, int32_t* token_ids,
+                                         int pdl, void* stream) {
+  using namespace flint;
+  if (M > kNoAllocMaxRows) return FLINT_ERR_SCRATCH;
+  if (num_sms() <= 0) return FLINT_ERR_DEVICE;
+  void* scratch = head_noalloc_scratch();
+  if (scratch == nullptr) return FLINT_ERR_DEVICE;
+  if (cudaMemsetAsync(scratch, 0, sizeof(HeadWorkspace), static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return FLINT_ERR_LAUNCH;
+  return flint_lm_head_nv4(x, ldx, M, P, S, gs, V, K, logits, ld_logits, token_ids, scratch, pdl, stream);
+}

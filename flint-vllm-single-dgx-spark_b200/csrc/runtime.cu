@@ -81,6 +81,7 @@ extern "C" const char* flint_error_string(int code) {
     case FLINT_ERR_LAUNCH: return "kernel launch failed";
     case FLINT_ERR_WORKSPACE: return "workspace missing or too small";
     case FLINT_ERR_ARGUMENT: return "invalid argument";
+    case FLINT_ERR_SCRATCH: return "request exceeds the fixed scratch of the allocation-free entry point";
     default: return "unknown error";
   }
 }

@@ -33,7 +33,8 @@ enum {
   FLINT_ERR_DEVICE = 3,       /* no CUDA device / not sm_100 */
   FLINT_ERR_LAUNCH = 4,       /* cudaLaunchKernelEx failed (the CUDA error is left for cudaGetLastError) */
   FLINT_ERR_WORKSPACE = 5,    /* workspace missing or too small */
-  FLINT_ERR_ARGUMENT = 6      /* null pointer or out-of-range scalar argument */
+  FLINT_ERR_ARGUMENT = 6,     /* null pointer or out-of-range scalar argument */
+  FLINT_ERR_SCRATCH = 7       /* request larger than the fixed scratch of an allocation-free entry point */
 };
 
 /* Library version (major*10000 + minor*100 + patch). */
@@ -61,6 +62,15 @@ int flint_lm_head_nv4(const void* x, int64_t ldx, int64_t M, const void* P, cons
 /* Same, with the model's final (residual add +) RMSNorm fused in front: x <- bf16((x + res) *
  * rsqrt(mean((x + res)^2) + eps) * norm_w) (res may be NULL; norm_w NULL = flint_lm_head_nv4).  The
  * reference applies model.norm before compute_logits (fast/model.py:831,924-929). */
+/* Allocation-free flint_lm_head_nv4 (no counterpart in the reference: the recipe always runs inside vLLM, which
+ * allocates).  For callers that cannot allocate device memory at call time -- an engine that has already given all
+ * free HBM to its KV-cache pool, a CUDA-graph capture region, a host runtime that only reaches the library through
+ * a C FFI -- the argmax scratch is a fixed 256-byte array inside the library, one per device, kept until the process
+ * exits; no workspace argument.  At most 8 rows (M <= 8); larger requests return FLINT_ERR_SCRATCH.  Each call
+ * clears the scratch first; calls that overlap on one GPU race on it (use one stream per device).  The first call
+ * on a device resolves the scratch address (cudaGetSymbolAddress), so make it before any stream capture. */
+int flint_lm_head_nv4_noalloc(const void* x, int64_t ldx, int64_t M, const void* P, const void* S, float gs, int64_t V,
+                              int64_t K, float* logits, int64_t ld_logits, int32_t* token_ids, int pdl, void* stream);
 int flint_lm_head_nv4_fused(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, int64_t M,
                             const void* P, const void* S, float gs, int64_t V, int64_t K, float* logits,
                             int64_t ld_logits, int32_t* token_ids, void* workspace, int pdl, void* stream);
