@@ -10,7 +10,8 @@ is one decode token.  Every step streams ~1.73 GB of weights (> L2), so no L2 fl
 value      device-resident decode: the step CUDA graph replayed K times back to back (tok/s, max over ranks)
 e2e        the public serving loop: per step the inputs are copied from pinned host memory, the graph replays and the
            token is read back (tok/s)
-roofline   the dominant kernel's algorithmic bytes / CUDA-event duration vs the measured HBM copy peak
+roofline   the kernel with the largest share of the step: algorithmic bytes / CUDA-event duration (timed alone over
+           its 48 per-layer launches) vs the measured HBM copy peak; roofline_kernels has every kernel
 cpu_baseline  the CPU oracle port of the reference's torch path on a bounded sample (rank 0, N = 1)
 
 With N > 1 (torchrun) every rank serves its own stream on its own GPU (replicas; weak scaling).
@@ -104,39 +105,46 @@ def dist_setup(n):
     return rank, world, dist
 
 
-def kernel_roofline(fb, model, dec, peak, peak_kind):
-    """Time the LM-head kernel alone (its whole 175 MB head is streamed per launch) with CUDA events over repeated
-    launches, and report achieved algorithmic GB/s against the measured copy peak."""
+# DRAM bytes per launch from ncu (dram__bytes_read.sum + dram__bytes_write.sum) of the kernels, profiles/*.txt;
+# None until captured.
+NCU_TRAFFIC: dict[str, float | None] = {}
+
+
+def kernel_rooflines(model, dec, peak, peak_kind, ctx, step_us):
+    """Each kernel of the decode step timed alone with CUDA events on its launch stream: a CUDA graph of its 48
+    per-layer launches (each on that layer's weights / KV cache, 0.2-0.7 GB in all, so nothing is served from L2)
+    or 20 head launches (175 MB each).  achieved = algorithmic bytes per launch / mean launch time."""
     import torch
-    c = model.cfg
-    P, S, gs = model.head
-    x = torch.randn((1, c.hidden), device=model.dev).to(torch.bfloat16)
-    tok = torch.empty((1,), dtype=torch.int32, device=model.dev)
-    dummy = torch.empty((1, 1), dtype=torch.float32, device=model.dev)
-    ops = torch.ops.flint_b200
-    for _ in range(3):
-        ops.lm_head_nv4(x, P, S, gs, dummy, tok, False, True)
-    torch.cuda.synchronize()
-    n = 20
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        for _ in range(n):
-            ops.lm_head_nv4(x, P, S, gs, dummy, tok, False, True)
-    g.replay()
-    torch.cuda.synchronize()
+    L = model.cfg.layers
     st = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(st)
-    g.replay()
-    e1.record(st)
-    torch.cuda.synchronize()
-    us = e0.elapsed_time(e1) * 1e3 / n
-    nbytes = c.vocab * c.hidden // 2 + c.vocab * c.hidden // 16
-    achieved = nbytes / us / 1e3
-    return {"kernel": "lm_head_kernel (NVFP4 head GEMV + argmax, 151552 x 2048)", "bound": "hbm",
-            "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-            "frac": round(achieved / peak, 4), "us_per_launch": round(us, 2), "bytes_per_launch": nbytes,
-            "traffic": None}
+    out = {}
+    for name in [n for n, _ in dec.layer_ops(0)] + ["head"]:
+        fns = [dec.head_op()] * 20 if name == "head" else [dict(dec.layer_ops(l))[name] for l in range(L)]
+        for fn in fns[:3]:
+            fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for fn in fns:
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(3):
+            g.replay()
+        e1.record(st)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (3 * len(fns))
+        nbytes = dec.algorithmic_bytes(name, ctx)
+        achieved = nbytes / us / 1e3
+        per_step = 1 if name == "head" else L
+        out[name] = {"kernel": name, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "us_per_launch": round(us, 2), "bytes_per_launch": nbytes, "launches_per_step": per_step,
+                     "share_of_step": round(us * per_step / step_us, 4), "traffic": NCU_TRAFFIC.get(name)}
+        del g
+    return out
 
 
 def run_ours(args):
@@ -147,15 +155,16 @@ def run_ours(args):
     from flint_b200.model import Decoder, FlintConfig, FlintModel
     dev = torch.device("cuda", torch.cuda.current_device())
     cfg = FlintConfig()
-    steps, warm = args.steps, args.warmup
-    max_ctx = PROMPT_LEN + warm + 2 * steps + 16
+    steps, warm, plen = args.steps, args.warmup, args.prompt
+    max_ctx = plen + warm + 2 * steps + 16
     model = FlintModel(cfg, dev, seed=1234 + rank, max_ctx=max_ctx, max_batch=1)
-    dec = Decoder(model, batch=1)
+    dec = Decoder(model, batch=1, moe=args.moe, attn=args.attn)
     dec.reserve_history(warm + steps)
     dec.capture()
-    prompt = np.random.default_rng(7 + rank).integers(0, cfg.vocab, size=(1, PROMPT_LEN))
+    prompt = np.random.default_rng(7 + rank).integers(0, cfg.vocab, size=(1, plen))
+    fill = dec.prefill if args.prefill == "teacher" else dec.fill_kv_random
     t0 = time.time()
-    dec.prefill(prompt)
+    fill(prompt)
     prefill_s = time.time() - t0
     dec.decode(warm)
     torch.cuda.synchronize()
@@ -183,7 +192,7 @@ def run_ours(args):
     e2e_steps = min(steps, 200)
     dec.reserve_history(1)
     dec.capture()
-    dec.prefill(prompt)
+    fill(prompt)
     pinned = dec.pinned_state()
     dec.generate_host_driven(3, pinned)
     torch.cuda.synchronize()
@@ -197,16 +206,17 @@ def run_ours(args):
         e2e_val = world * e2e_steps / float(t.item())
 
     peak, peak_kind = measured_peak()
-    roof = kernel_roofline(fb, model, dec, peak, peak_kind) if rank == 0 else None
+    mean_ctx = plen + warm + steps / 2
+    kernels = kernel_rooflines(model, dec, peak, peak_kind, int(mean_ctx), ms * 1e3 / steps) if rank == 0 else None
+    roof = max(kernels.values(), key=lambda r: r["share_of_step"]) if kernels else None
     value = world * steps / (ms / 1e3)
     wbytes = cfg.weight_bytes_per_token()
-    mean_ctx = PROMPT_LEN + warm + steps / 2
     kv_bytes = cfg.layers * int(mean_ctx) * cfg.num_kv_heads * 2 * cfg.head_dim * 2
     total, active = cfg.param_counts()
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            cpu = cpu_baseline_sample(cfg, args.cpu_sample_tokens)
+            cpu = cpu_baseline_sample(cfg, args.cpu_sample_tokens, plen)
         line = {
             "metric": "c1 decode tok/s, Flint-class NVFP4 MoE (greedy, 800 tokens after a 6057-token prompt)",
             "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warm,
@@ -214,17 +224,18 @@ def run_ours(args):
             "dtype": "nvfp4 weights (e2m1+e4m3), bf16 activations, fp32 accumulate", "data": "synthetic",
             "config": {"workload": "BASELINE configs[3]: full Flint-class synthetic model, 1 stream, greedy decode",
                        "layers": cfg.layers, "hidden": cfg.hidden, "experts": cfg.num_experts, "topk": cfg.topk,
-                       "moe_inter": cfg.moe_inter, "vocab": cfg.vocab, "prompt_tokens": PROMPT_LEN,
+                       "moe_inter": cfg.moe_inter, "vocab": cfg.vocab, "prompt_tokens": plen,
+                       "prefill": args.prefill, "moe_path": dec.moe, "attn_path": dec.attn_mode,
                        "params_total": total, "params_active": active, "weight_bytes_per_token": wbytes,
                        "kv_bytes_per_token_mean": kv_bytes, "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
                        "l2": "no flush: 1.73 GB of weights streamed per step (> 126 MB L2)",
-                       "prefill_s_teacher_forced": round(prefill_s, 2)},
+                       "prefill_s": round(prefill_s, 2)},
             "bound_tok_s": {"weights_only": round(peak * 1e9 / wbytes, 1),
                             "weights_plus_kv": round(peak * 1e9 / (wbytes + kv_bytes), 1), "peak_GBps": peak},
             "e2e": {"value": round(e2e_val, 2), "unit": "tok/s", "steps": e2e_steps, "h2d_bytes_per_step": 4 + 8 + 4 + 8,
                     "d2h_bytes_per_step": 4},
             "gpu_launches": dec.launches_per_step * steps,
-            "roofline": roof, "cpu_baseline": cpu, "clocks": clk.summary(),
+            "roofline": roof, "roofline_kernels": kernels, "cpu_baseline": cpu, "clocks": clk.summary(),
             "tokens_head": tokens[0, :8].tolist(),
         }
         print(json.dumps(line), flush=True)
@@ -232,12 +243,12 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-def cpu_baseline_sample(cfg, n_tokens):
+def cpu_baseline_sample(cfg, n_tokens, context):
     """The CPU oracle (the reference's dequantise-to-fp32 torch path) on a bounded sample: n decode tokens of the
     same model shape at the same context.  Returns the cpu_baseline object."""
     sys.path.insert(0, ROOT)
     from oracle import model_cpu
-    return model_cpu.time_decode(cfg, n_tokens=n_tokens, context=PROMPT_LEN)
+    return model_cpu.time_decode(cfg, n_tokens=n_tokens, context=context)
 
 
 def run_reference(args):
@@ -249,7 +260,7 @@ def run_reference(args):
     sys.path.insert(0, ROOT)
     from oracle import model_cpu
     cfg = FlintConfig()
-    res = model_cpu.time_decode(cfg, n_tokens=max(1, args.cpu_sample_tokens), context=PROMPT_LEN,
+    res = model_cpu.time_decode(cfg, n_tokens=max(1, args.cpu_sample_tokens), context=args.prompt,
                                 warmup=0)
     line = {
         "impl": "reference",
@@ -259,7 +270,7 @@ def run_reference(args):
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (weights dequantised from NVFP4 per call)",
         "data": "synthetic",
         "config": {"workload": "BASELINE configs[3] on the host CPU: the reference's dequantise-to-fp32 torch path",
-                   "prompt_tokens": PROMPT_LEN},
+                   "prompt_tokens": args.prompt},
         "cpu_baseline": res,
         "e2e": {"value": res["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -273,6 +284,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-sample-tokens", type=int, default=2)
+    ap.add_argument("--prompt", type=int, default=PROMPT_LEN, help="prompt tokens before the timed decode")
+    ap.add_argument("--attn", default="block", choices=["block", "chain"], help="attention block: one launch or three")
+    ap.add_argument("--moe", default="chain", choices=["chain", "fused"], help="MoE: three launches or one")
+    ap.add_argument("--prefill", default="teacher", choices=["teacher", "kv"],
+                    help="teacher: prompt run through the decode kernels; kv: KV cache filled with seeded N(0,1) "
+                         "(profiling runs)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

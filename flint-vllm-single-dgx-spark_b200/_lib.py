@@ -25,10 +25,14 @@ F32 = ctypes.c_float
 SIGNATURES: dict[str, tuple] = {
     "flint_version": (I32, []),
     "flint_error_string": (ctypes.c_char_p, [I32]),
+    "flint_last_cuda_error": (ctypes.c_char_p, []),
     "flint_lm_head_workspace_bytes": (I64, []),
     "flint_lm_head_nv4": (I32, [P, I64, I64, P, P, F32, I64, I64, P, I64, P, P, I32, P]),
     "flint_lm_head_nv4_noalloc": (I32, [P, I64, I64, P, P, F32, I64, I64, P, I64, P, I32, P]),
     "flint_lm_head_nv4_fused": (I32, [P, I64, P, P, F32, I64, P, P, F32, I64, I64, P, I64, P, P, I32, P]),
+    "flint_lm_head_sample_workspace_bytes": (I64, [I64, I64]),
+    "flint_lm_head_nv4_sample": (I32, [P, I64, P, P, F32, I64, P, P, F32, I64, I64, P, I64, F32, I64, F32, P, P, P, P, P, P,
+                                       P, I32, P]),
     "flint_moe_workspace_bytes": (I64, [I64]),
     "flint_moe_route": (I32, [P, I64, P, P, F32, P, I64, I64, I64, I64, I32, P, P, P, P, P, P, I32, P]),
     "flint_moe_up": (I32, [P, I64, I64, P, I64, P, P, P, I64, I64, I64, P, P, I32, P]),
@@ -41,6 +45,9 @@ SIGNATURES: dict[str, tuple] = {
     "flint_attn_qkv": (I32, [P, I64, P, P, P, F32, P, P, P, I64, I64, I64, I64, I64, I32, P, P, F32, P, P, I64, P, P, I64,
                              I64, I64, I64, P, P, P, P, P, I32, P]),
     "flint_attn_o": (I32, [P, I64, I64, P, P, P, I64, I64, P, P, I32, P]),
+    "flint_attn_block_workspace_bytes": (I64, [I64, I64]),
+    "flint_attn_block": (I32, [P, I64, P, P, I64, P, F32, I64, I64, P, P, P, I64, I64, P, P, F32, P, P, I64, P, I64, I64, I64,
+                               P, I64, I64, P, P, P, I64, F32, P, P, P, I64, P, P, P, P, P, I32, P]),
     "flint_decode_attention_splits": (I64, [I64, I64]),
     "flint_decode_attention_workspace_bytes": (I64, [I64, I64, I64]),
     "flint_decode_advance": (I32, [P, I64, P, P, P, P, I64, I64, I64, P, I64, P, I64, P, I32, P]),
@@ -75,7 +82,8 @@ def lib() -> ctypes.CDLL:
 def check(rc: int, what: str) -> None:
     if rc != 0:
         msg = lib().flint_error_string(rc).decode()
-        raise FlintError(f"{what} failed: {msg} (code {rc})")
+        detail = lib().flint_last_cuda_error().decode()
+        raise FlintError(f"{what} failed: {msg} (code {rc})" + (f" [{detail}]" if detail else ""))
 
 
 def ptr(t: torch.Tensor | None) -> int | None:

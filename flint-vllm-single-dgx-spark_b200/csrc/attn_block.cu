@@ -1,0 +1,818 @@
+// (3) Fused decode attention block: add + RMSNorm -> NVFP4 QKV GEMV -> q/k RMSNorm + RoPE + KV write -> paged
+// split-K GQA attention -> NVFP4 O projection, in ONE cooperative persistent launch (one CTA per SM).
+// Replaces the reference's qkv_head_kernel and o_gemv_kernel (fast/attn_gemv2.cu:170-289) together with the decode
+// attention between them (the Flint PR's CuTe _FlintDecodeAttention, patch:1741-2415); the numerics are those of
+// attn_proj.cu and decode_attention.cu (same rounding points), only the summation partition differs.
+//
+// Work of CTA c (grid G = #SMs, 8 consumer warps + 1 TMA producer warp):
+//  prologue  before the PDL wait the producer loads the CTA's QKV row groups (16 rows x K each) and O row groups into
+//            shared memory, where they stay for the whole launch; after the wait it streams the CTA's KV pages
+//            (8 KB: 16 tokens x [K | V] of one kv head) into a ring of np slots, so at short context every page is in
+//            flight while phase A runs.
+//  A  every CTA recomputes the add + RMSNorm (same bits everywhere; CTA 0 publishes res_out), stages it as f16 and
+//     computes y = bf16(acc * gs) for its QKV rows: the K slices are split over the 8 warps and the partial tiles
+//     summed in warp order.  y goes to the workspace.                                   -- grid barrier --
+//  B  the pages of all (request, kv head) segments, in linear order, are cut into G contiguous ranges.  For each
+//     segment piece of its range the CTA normalises + ropes the segment's q heads; the warp that holds the current
+//     token's page normalises + ropes the new k, writes k and v to the cache slot and patches its shared copy of the
+//     page; each warp runs the online softmax over its pages (S = K q, exp2, P rounded to bf16, O += P V); the CTA
+//     merges its warps (fixed order) and, unless it owns the whole segment (then it writes the output), writes one
+//     partial record.                                                                      -- grid barrier --
+//  B2 each (segment, q head) with several records is merged by one CTA: weights exp2(m_r c - m c) and l by one warp
+//     (fixed lane-strided order + butterfly), the records' O summed by 8 warps in record order mod 8 and the 8 warp
+//     partials in warp order (sinks in the denominator).                                  -- grid barrier --
+//  C  every CTA stages the attention output as f16 and computes its O rows from the resident weights.
+#include "common.cuh"
+#include "gridsync.cuh"
+#include "nvfp4_tile.cuh"
+#include "runtime.cuh"
+#include "tma.cuh"
+
+#include <algorithm>
+#include <stdio.h>
+
+namespace flint {
+
+constexpr int kBW = 8;                       // consumer warps
+constexpr int kBThreads = (kBW + 1) * 32;
+constexpr int kBCons = kBW * 32;
+constexpr int kBD = 128;                     // head dim
+constexpr int kBPage = 16;                   // tokens per KV page
+constexpr int kBPageBytes = kBPage * 2 * kBD * 2;
+constexpr int kBUnitBytes = 2048 + 256;      // one 16-row x 256-k unit of an NVFP4 matrix: codes + scales
+constexpr int kBMaxSeg = 64;                 // requests x kv heads
+constexpr int kBMaxSlots = 16;
+constexpr int kBGQ = 3;                      // max QKV row groups per CTA
+constexpr int kBGO = 2;                      // max O row groups per CTA
+constexpr float kBLog2e = 1.4426950408889634f;
+
+struct BlockWs {
+  GridSync gs;
+  unsigned status;
+  unsigned pad[31];
+  unsigned seg_cnt[kBMaxSeg];
+  // followed by: y bf16 [8][Nqkv], attention output bf16 [8][Ko], partial records
+};
+
+struct BlockArgs {
+  const bf16* x;
+  int64_t ldx;
+  const int* tokens;                 // optional embedding gather (row m of x = x[tokens[m]])
+  const bf16* res;
+  int64_t ldr;                       // row stride of res / res_out / out
+  const bf16* nw;
+  float eps;
+  int M, H, Nqkv, nq, nkv, Gq;
+  const float* gs_qkv;
+  const bf16* q_w;
+  const bf16* k_w;
+  float eps_head;
+  const int64_t* positions;
+  const float* cos_sin;              // [max_pos, 128] (cos | sin), or null: no RoPE
+  int64_t cs_stride;
+  bf16* kv;                          // HND [blocks, nkv, 16, 256]
+  int64_t st_block, st_head;         // elements
+  const int* bt;
+  int64_t bt_stride;
+  int max_blocks;
+  const int* seq_lens;
+  const int64_t* slots;
+  const float* sinks;
+  int window;
+  float c;                           // scale * log2(e)
+  int Ko, No;
+  const float* gs_o;
+  bf16* out;
+  bf16* res_out;
+  bf16* q_out;                       // optional
+  bf16* attn;                        // attention output [M][Ko] (caller's or workspace)
+  bf16* y;                           // workspace: raw QKV output [8][Nqkv]
+  float* rec;                        // workspace: partial records
+  int gq_total, go_total;            // row groups of 16
+  int nks_q, nks_o;                  // 256-k slices
+  int np;                            // page ring slots
+  uint32_t off_ring, off_wo, off_xs, off_red, wq_scale_off, wo_scale_off;
+  BlockWs* ws;
+};
+
+// record r: o [8][128] fp32, then (m, l) [8] float2
+constexpr int kBRecFloats = 8 * kBD + 16;
+
+__device__ __forceinline__ void cons_sync() { asm volatile("bar.sync 1, %0;" ::"r"(kBCons) : "memory"); }
+// consumer barrier that also ANDs a predicate over the 256 consumer threads (uniform decisions after bounded waits)
+__device__ __forceinline__ bool cons_sync_and(bool pred) {
+  int r;
+  asm volatile("{\n.reg .pred p, q;\nsetp.ne.s32 p, %1, 0;\nbar.red.and.pred q, 1, %2, p;\nselp.s32 %0, 1, 0, q;\n}"
+               : "=r"(r) : "r"((int)pred), "r"(kBCons) : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ void st_shared_u16(uint32_t addr, unsigned short v) {
+  asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(v) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+// shared address of the 16-byte unit (token row, dim unit) of a page held as four 128B-swizzled boxes K0 K1 V0 V1
+__device__ __forceinline__ uint32_t bpage_unit(uint32_t page, int box, int row, int unit) {
+  return page + box * 2048 + row * 128 + ((unit ^ (row & 7)) << 4);
+}
+
+// Resident NVFP4 GEMV: ng row groups x nks slices in shared memory (unit (gi, ks) codes at wc + (gi*nks+ks)*2048,
+// scales at wsc + (gi*nks+ks)*256); warp w takes slices w, w+8, ...; partial tiles to red[gi][w][16][8].
+template <int GMAX>
+__device__ __forceinline__ void gemv_resident(const uint8_t* wc, const uint8_t* wsc, int ng, int nks, const __half* xs, int K,
+                                              int M, float* red, int warp, int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  const bool active = g < M;
+  const __half* xrow = xs + (active ? g : 0) * xs_stride(K);
+  float acc[GMAX][4][4];
+#pragma unroll
+  for (int gi = 0; gi < GMAX; ++gi) zero_acc(acc[gi]);
+#pragma unroll
+  for (int gi = 0; gi < GMAX; ++gi) {
+    if (gi < ng)
+      for (int ks = warp; ks < nks; ks += kBW)
+        consume_stage(wc + (gi * nks + ks) * 2048, wsc + (gi * nks + ks) * 256, 0, g, t, ks, xrow, active, acc[gi]);
+  }
+  const int r0 = tile_phi(g), r1 = r0 + 8, n0 = 2 * t, n1 = 2 * t + 1;
+#pragma unroll
+  for (int gi = 0; gi < GMAX; ++gi) {
+    if (gi < ng) {
+      float d[4];
+      sum_acc(acc[gi], d);
+      float* rt = red + (gi * kBW + warp) * 128;
+      rt[r0 * 8 + n0] = d[0];
+      rt[r0 * 8 + n1] = d[1];
+      rt[r1 * 8 + n0] = d[2];
+      rt[r1 * 8 + n1] = d[3];
+    }
+  }
+}
+
+// out[m][row0 + 16 gi + r] = bf16(sum_w red[gi][w][r][m] * gs * 2^-shift[m]); consumer threads.
+__device__ __forceinline__ void gemv_finish(const float* red, int ng, int M, float gs, const int* shift, bf16* out,
+                                            int64_t ld, int row0) {
+  for (int idx = threadIdx.x; idx < ng * 16 * M; idx += kBCons) {
+    const int gi = idx / (16 * M), rem = idx - gi * 16 * M, r = rem / M, m = rem - r * M;
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < kBW; ++w) s += red[(gi * kBW + w) * 128 + r * 8 + m];
+    out[(int64_t)m * ld + row0 + gi * 16 + r] = __float2bfloat16_rn(s * ldexpf(gs, -shift[m]));
+  }
+}
+
+// q / k head finish (attn_proj.cu's epilogue): y (4 values per lane, dims lane + 32 i) -> bf16(rmsnorm(y) * w) -> RoPE.
+__device__ __forceinline__ void head_norm_rope(float (&v)[4], const bf16* w, float eps, const float* cs, int lane) {
+  float v2 = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v2 += __shfl_xor_sync(0xffffffffu, v2, off);
+  const float rs = rsqrtf(v2 / (float)kBD + eps);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = bf16r(v[i] * rs * __bfloat162float(w[lane + 32 * i]));
+  if (cs) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int r = lane + 32 * i;
+      const float c = cs[r], s = cs[64 + r];
+      const float n1 = v[i], n2 = v[i + 2];
+      v[i] = fmaf(n1, c, -(n2 * s));
+      v[i + 2] = fmaf(n2, c, n1 * s);
+    }
+  }
+}
+
+__device__ __forceinline__ float ldcg_bf16(const bf16* p) {
+  return bf16_bits_to_f32(__ldcg(reinterpret_cast<const unsigned short*>(p)));
+}
+
+__global__ void __launch_bounds__(kBThreads, 1)
+attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant__ CUtensorMap mqs,
+                  const __grid_constant__ CUtensorMap moc, const __grid_constant__ CUtensorMap mos,
+                  const __grid_constant__ CUtensorMap mkv, const BlockArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t full[kBMaxSlots], empty[kBMaxSlots], bar_wq, bar_wo;
+  __shared__ int shift[8];
+  __shared__ float red_n[kBW * 8 + 8];
+  __shared__ int s_pf[8], s_npg[8], s_seq[8], s_start[8], s_pre[9];
+  __shared__ __align__(16) bf16 q_tile[8][kBD];
+  __shared__ float s_stat[2];
+  __shared__ int s_ok;
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int G = gridDim.x, cta = blockIdx.x;
+  const int M = a.M;
+  unsigned* status = &a.ws->status;
+  uint8_t* ring = smem + a.off_ring;
+  uint8_t* wq = smem;                                  // QKV weights (phase A), then warp partials (phase B)
+  uint8_t* wo = smem + a.off_wo;
+  __half* xs = reinterpret_cast<__half*>(smem + a.off_xs);
+  float* red = reinterpret_cast<float*>(smem + a.off_red);
+  __half* xs_o = reinterpret_cast<__half*>(smem);       // phase C: over the QKV weights and the page ring
+
+  const int gq0 = (int)((int64_t)cta * a.gq_total / G), ngq = (int)((int64_t)(cta + 1) * a.gq_total / G) - gq0;
+  const int go0 = (int)((int64_t)cta * a.go_total / G), ngo = (int)((int64_t)(cta + 1) * a.go_total / G) - go0;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < a.np; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(&bar_wq, 1);
+    mbar_init(&bar_wo, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  // ---- prologue: resident weights (independent of the previous kernel) ----
+  if (warp == kBW && lane == 0) {
+    tma_prefetch_desc(&mqc);
+    tma_prefetch_desc(&mqs);
+    tma_prefetch_desc(&mkv);
+    // one 3-D box per 16-row group: all K slices at once, landing as [slice][16 rows][128 B] (codes, swizzled) and
+    // [slice][16 rows][16 B] (scales)
+    if (ngq > 0) {
+      mbar_arrive_expect_tx(&bar_wq, ngq * a.nks_q * kBUnitBytes);
+      for (int gi = 0; gi < ngq; ++gi) {
+        tma_load_3d(wq + gi * a.nks_q * 2048, &mqc, 0, (gq0 + gi) * 16, 0, &bar_wq);
+        tma_load_3d(wq + a.wq_scale_off + gi * a.nks_q * 256, &mqs, 0, (gq0 + gi) * 16, 0, &bar_wq);
+      }
+    }
+    if (ngo > 0) {
+      mbar_arrive_expect_tx(&bar_wo, ngo * a.nks_o * kBUnitBytes);
+      for (int gi = 0; gi < ngo; ++gi) {
+        tma_load_3d(wo + gi * a.nks_o * 2048, &moc, 0, (go0 + gi) * 16, 0, &bar_wo);
+        tma_load_3d(wo + a.wo_scale_off + gi * a.nks_o * 256, &mos, 0, (go0 + gi) * 16, 0, &bar_wo);
+      }
+    }
+  }
+  pdl_wait();
+  if (threadIdx.x == 0) {                              // page partition inputs
+    int pre = 0;
+    for (int b = 0; b < M; ++b) {
+      const int seq = a.seq_lens[b];
+      const int start = a.window > 0 ? max(0, seq - a.window) : 0;
+      const int pf = start / kBPage;
+      int pe = (seq + kBPage - 1) / kBPage;
+      if (pe > a.max_blocks) {
+        atomicOr(status, 4u);
+        pe = a.max_blocks;
+      }
+      s_seq[b] = seq;
+      s_start[b] = start;
+      s_pf[b] = pf;
+      s_npg[b] = max(0, pe - pf);
+      s_pre[b] = pre;
+      pre += s_npg[b];
+    }
+    s_pre[M] = pre;
+  }
+  __syncthreads();
+  const int S = M * a.nkv;
+  const int P = a.nkv * s_pre[M];
+  const int Geff = min(G, P);
+  const int lo = cta < Geff ? (int)((int64_t)cta * P / Geff) : P;
+  const int hi = cta < Geff ? (int)((int64_t)(cta + 1) * P / Geff) : P;
+  auto seg_start = [&](int s) { const int b = s / a.nkv; return a.nkv * s_pre[b] + (s - b * a.nkv) * s_npg[b]; };
+  auto owner = [&](int L) { return (int)(((int64_t)(L + 1) * Geff + P - 1) / P) - 1; };
+  // partial records: segment s owns n_parts(s) consecutive records from rec_base(s) (one per CTA touching it)
+  auto n_parts_of = [&](int s) {
+    const int n = s_npg[s / a.nkv];
+    if (n == 0) return 0;
+    const int A = seg_start(s);
+    return owner(A + n - 1) - owner(A) + 1;
+  };
+  auto rec_base = [&](int s) {
+    int r = 0;
+    for (int s2 = 0; s2 < s; ++s2) r += n_parts_of(s2);
+    return r;
+  };
+
+  if (warp == kBW) {
+    // ---- producer: this CTA's pages, in the order the consumers take them, once the resident weights have landed
+    // (they are needed first; the pages then stream in under the QKV GEMV and the barrier) ----
+    if (lane == 0) {
+      if (ngq > 0 && !mbar_wait(&bar_wq, 0, status)) return;
+      int j = 0;
+      for (int s = 0; s < S; ++s) {
+        const int b = s / a.nkv, kvh = s - b * a.nkv;
+        const int A = seg_start(s), from = max(A, lo), to = min(A + s_npg[b], hi);
+        const int* btb = a.bt + (int64_t)b * a.bt_stride;
+        for (int L = from; L < to; ++L, ++j) {
+          const int slot = j % a.np, round = j / a.np;
+          if (!mbar_wait(&empty[slot], (round & 1) ^ 1u, status)) return;
+          const int blk = btb[s_pf[b] + (L - A)];
+          mbar_arrive_expect_tx(&full[slot], kBPageBytes);
+          // the whole page in one 5-D box: [K0 K1 V0 V1][16 rows][64 dims], each quarter 128B-swizzled
+          tma_load_5d(ring + slot * kBPageBytes, &mkv, 0, 0, 0, kvh, blk, &full[slot]);
+        }
+      }
+    }
+    return;
+  }
+
+  // ================= consumers (256 threads) =================
+  // ---- A: add + RMSNorm, QKV rows ----
+  if (a.H / 8 <= kBCons)
+    norm_stage_f16_1(a.x, a.ldx, a.tokens, a.res, a.ldr, a.nw, a.eps, M, a.H, xs, shift, red_n,
+                     cta == 0 ? a.res_out : nullptr, kBCons, 1);
+  else
+    norm_stage_f16(a.x, a.ldx, a.tokens, a.res, a.ldr, a.nw, a.eps, M, a.H, xs, shift, red_n,
+                   cta == 0 ? a.res_out : nullptr, kBCons, 1);
+  if (ngq > 0 && cons_sync_and(mbar_wait(&bar_wq, 0, status))) {
+    gemv_resident<kBGQ>(wq, wq + a.wq_scale_off, ngq, a.nks_q, xs, a.H, M, red, warp, lane);
+    cons_sync();
+    gemv_finish(red, ngq, M, a.gs_qkv[0], shift, a.y, a.Nqkv, gq0 * 16);
+  }
+  grid_sync(&a.ws->gs, G, 0, kBCons, 1, &s_ok, status);
+
+  // ---- B: attention ----
+  const int tid = threadIdx.x, g = lane >> 2, t4 = lane & 3;
+  const float c = a.c;
+  float* wo_p = reinterpret_cast<float*>(wq);                     // [8 warps][8 heads][128]
+  float* wm = wo_p + kBW * 8 * kBD;                               // [8][16]
+  float* wl = wm + kBW * 16;
+  // empty segments (no pages): zero output, KV write of the slot (by CTA s % G)
+  for (int s = cta; s < S; s += G) {
+    const int b = s / a.nkv, kvh = s - b * a.nkv;
+    if (s_npg[b] != 0) continue;
+    if (tid < a.Gq * 16) {
+      const int hh = tid >> 4, d0 = (tid & 15) * 8;
+      *reinterpret_cast<uint4*>(a.attn + (int64_t)b * a.Ko + (kvh * a.Gq + hh) * kBD + d0) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    if (a.q_out && warp < a.Gq) {                                 // q of the empty request still goes out
+      const int qh = kvh * a.Gq + warp;
+      const bf16* yb = a.y + (int64_t)b * a.Nqkv;
+      float q[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) q[i] = ldcg_bf16(yb + qh * kBD + lane + 32 * i);
+      head_norm_rope(q, a.q_w, a.eps_head, a.cos_sin ? a.cos_sin + a.positions[b] * a.cs_stride : nullptr, lane);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a.q_out[(int64_t)b * a.nq * kBD + qh * kBD + lane + 32 * i] = __float2bfloat16_rn(q[i]);
+    }
+    if (warp == 0 && a.slots && a.slots[b] >= 0) {
+      const bf16* yb = a.y + (int64_t)b * a.Nqkv;
+      float k[4], v[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        k[i] = ldcg_bf16(yb + (a.nq + kvh) * kBD + lane + 32 * i);
+        v[i] = ldcg_bf16(yb + (a.nq + a.nkv + kvh) * kBD + lane + 32 * i);
+      }
+      head_norm_rope(k, a.k_w, a.eps_head, a.cos_sin ? a.cos_sin + a.positions[b] * a.cs_stride : nullptr, lane);
+      const int64_t slot = a.slots[b];
+      bf16* dst = a.kv + (slot / kBPage) * a.st_block + (int64_t)kvh * a.st_head + (slot % kBPage) * (2 * kBD);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        dst[lane + 32 * i] = __float2bfloat16_rn(k[i]);
+        dst[kBD + lane + 32 * i] = __float2bfloat16_rn(v[i]);
+      }
+    }
+  }
+
+  int j = 0;                                                       // CTA page sequence (matches the producer)
+  for (int s = 0; s < S; ++s) {
+    const int b = s / a.nkv, kvh = s - b * a.nkv;
+    const int A = seg_start(s), n = s_npg[b];
+    const int from = max(A, lo), to = min(A + n, hi);
+    if (from >= to) continue;
+    const int c_first = owner(A), n_parts = owner(A + n - 1) - c_first + 1;
+    const int seq = s_seq[b], start = s_start[b], last_page = (seq - 1) / kBPage;
+    const bf16* yb = a.y + (int64_t)b * a.Nqkv;
+    const float* cs = a.cos_sin ? a.cos_sin + a.positions[b] * a.cs_stride : nullptr;
+    // q heads of this segment: warp hh
+    {
+      float q[4] = {0.f, 0.f, 0.f, 0.f};
+      if (warp < a.Gq) {
+        const int qh = kvh * a.Gq + warp;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) q[i] = ldcg_bf16(yb + qh * kBD + lane + 32 * i);
+        head_norm_rope(q, a.q_w, a.eps_head, cs, lane);
+        if (a.q_out && cta == c_first) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) a.q_out[(int64_t)b * a.nq * kBD + qh * kBD + lane + 32 * i] = __float2bfloat16_rn(q[i]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) q_tile[warp][lane + 32 * i] = __float2bfloat16_rn(q[i]);
+    }
+    cons_sync();
+    uint32_t qa[8][2];
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      qa[kk][0] = *reinterpret_cast<const uint32_t*>(&q_tile[g][16 * kk + 2 * t4]);
+      qa[kk][1] = *reinterpret_cast<const uint32_t*>(&q_tile[g][16 * kk + 8 + 2 * t4]);
+    }
+    float o[16][4];
+#pragma unroll
+    for (int dt = 0; dt < 16; ++dt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[dt][e] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
+
+    for (int L = from; L < to; ++L, ++j) {
+      if (j % kBW != warp) continue;
+      const int slot = j % a.np;
+      if (!mbar_wait(&full[slot], (j / a.np) & 1, status)) break;
+      const uint32_t page = smem_u32(ring + slot * kBPageBytes);
+      const int p = s_pf[b] + (L - A);                             // page index within the request
+      if (p == last_page) {
+        // the current token: new k (normalised + roped) and v, to the cache slot and into this page's shared copy
+        float k[4], v[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          k[i] = ldcg_bf16(yb + (a.nq + kvh) * kBD + lane + 32 * i);
+          v[i] = ldcg_bf16(yb + (a.nq + a.nkv + kvh) * kBD + lane + 32 * i);
+        }
+        head_norm_rope(k, a.k_w, a.eps_head, cs, lane);
+        const int64_t slot_b = a.slots ? a.slots[b] : -1;
+        if (slot_b >= 0) {
+          bf16* dst = a.kv + (slot_b / kBPage) * a.st_block + (int64_t)kvh * a.st_head + (slot_b % kBPage) * (2 * kBD);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            dst[lane + 32 * i] = __float2bfloat16_rn(k[i]);
+            dst[kBD + lane + 32 * i] = __float2bfloat16_rn(v[i]);
+          }
+          const int row = (seq - 1) % kBPage;
+          const int64_t here = (int64_t)a.bt[(int64_t)b * a.bt_stride + p] * kBPage + row;
+          if (slot_b == here) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int d = lane + 32 * i;
+              const uint32_t off = (d & 7) * 2;
+              st_shared_u16(bpage_unit(page, d >> 6, row, (d & 63) >> 3) + off,
+                            __bfloat16_as_ushort(__float2bfloat16_rn(k[i])));
+              st_shared_u16(bpage_unit(page, 2 + (d >> 6), row, (d & 63) >> 3) + off,
+                            __bfloat16_as_ushort(__float2bfloat16_rn(v[i])));
+            }
+            fence_proxy_async();                                  // ordered before the slot's next TMA fill
+          }
+        }
+        __syncwarp();
+      }
+      // ---- S = K q ----
+      float sc[2][4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[nt][e] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const int mat = lane >> 3, r = lane & 7;
+        const int row = 8 * (mat >> 1) + r;
+        const int dim = 16 * kk + 8 * (mat & 1);
+        uint32_t k0, k1, k2, k3;
+        ldsm_x4(bpage_unit(page, dim >> 6, row, (dim & 63) >> 3), k0, k1, k2, k3);
+        const uint32_t aq[4] = {qa[kk][0], 0u, qa[kk][1], 0u};
+        mma_bf16(sc[0], aq, k0, k1);
+        mma_bf16(sc[1], aq, k2, k3);
+      }
+      // ---- mask + online softmax (row g = head g; lane holds tokens 8nt + 2t4 + {0,1}) ----
+      float sv[4] = {sc[0][0], sc[0][1], sc[1][0], sc[1][1]};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int tok = p * kBPage + 8 * (i >> 1) + 2 * t4 + (i & 1);
+        if (tok >= seq || tok < start) sv[i] = -INFINITY;
+      }
+      float mx = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float m_new = fmaxf(m_run, mx);
+      const float alpha = m_run == -INFINITY ? 0.f : exp2f(m_run * c - m_new * c);
+      float pv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) pv[i] = sv[i] == -INFINITY ? 0.f : exp2f(sv[i] * c - m_new * c);
+      l_run = l_run * alpha + ((pv[0] + pv[1]) + (pv[2] + pv[3]));
+      m_run = m_new;
+#pragma unroll
+      for (int dt = 0; dt < 16; ++dt) {
+        o[dt][0] *= alpha;
+        o[dt][1] *= alpha;
+      }
+      // ---- O += P V ----
+      const uint32_t pa[4] = {pack_bf16x2(pv[0], pv[1]), 0u, pack_bf16x2(pv[2], pv[3]), 0u};
+#pragma unroll
+      for (int dp = 0; dp < 8; ++dp) {
+        const int mat = lane >> 3, r = lane & 7;
+        const int row = 8 * (mat & 1) + r;
+        const int dim = 16 * dp + 8 * (mat >> 1);
+        uint32_t v0, v1, v2, v3;
+        ldsm_x4_t(bpage_unit(page, 2 + (dim >> 6), row, (dim & 63) >> 3), v0, v1, v2, v3);
+        mma_bf16(o[2 * dp], pa, v0, v1);
+        mma_bf16(o[2 * dp + 1], pa, v2, v3);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+
+    // ---- merge the warps (fixed order) ----
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+    if (t4 == 0) {
+      wm[warp * 16 + g] = m_run;
+      wl[warp * 16 + g] = l_run;
+    }
+#pragma unroll
+    for (int dt = 0; dt < 16; ++dt) {
+      wo_p[(warp * 8 + g) * kBD + 8 * dt + 2 * t4] = o[dt][0];
+      wo_p[(warp * 8 + g) * kBD + 8 * dt + 2 * t4 + 1] = o[dt][1];
+    }
+    cons_sync();
+    if (tid < 128) {
+      const int hh = tid >> 4, d0 = (tid & 15) * 8;
+      float mc = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kBW; ++w) mc = fmaxf(mc, wm[w * 16 + hh]);
+      float lc = 0.f, oc[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) oc[i] = 0.f;
+#pragma unroll
+      for (int w = 0; w < kBW; ++w) {
+        const float mw = wm[w * 16 + hh];
+        if (mw == -INFINITY) continue;
+        const float f = exp2f(mw * c - mc * c);
+        lc += wl[w * 16 + hh] * f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) oc[i] += wo_p[(w * 8 + hh) * kBD + d0 + i] * f;
+      }
+      if (n_parts == 1) {
+        if (hh < a.Gq) {
+          const int qh = kvh * a.Gq + hh;
+          float den = lc;
+          if (a.sinks && mc != -INFINITY) den += exp2f(a.sinks[qh] * kBLog2e - mc * c);
+          const float inv = den > 0.f ? 1.0f / den : 0.f;
+          uint32_t pk[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) pk[i] = pack_bf16x2(oc[2 * i] * inv, oc[2 * i + 1] * inv);
+          *reinterpret_cast<uint4*>(a.attn + (int64_t)b * a.Ko + qh * kBD + d0) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        }
+      } else {
+        float* rec = a.rec + (int64_t)(rec_base(s) + cta - c_first) * kBRecFloats;
+        __stcg(reinterpret_cast<float4*>(rec + hh * kBD + d0), make_float4(oc[0], oc[1], oc[2], oc[3]));
+        __stcg(reinterpret_cast<float4*>(rec + hh * kBD + d0) + 1, make_float4(oc[4], oc[5], oc[6], oc[7]));
+        if ((tid & 15) == 0) __stcg(reinterpret_cast<float2*>(rec + 8 * kBD) + hh, make_float2(mc, lc));
+      }
+    }
+    cons_sync();                                                   // warp partials are reused by the next piece
+  }
+  grid_sync(&a.ws->gs, G, 1, kBCons, 1, &s_ok, status);
+
+  // ---- B2: merge the partial records of split segments, one (segment, q head) per CTA at a time ----
+  {
+    float* fr = reinterpret_cast<float*>(wq);                     // [256] m_r then f_r, [256] l_r, [8][128] partials
+    float* part = fr + 512;
+    for (int u = cta; u < S * a.Gq; u += G) {
+      const int s = u / a.Gq, hh = u - s * a.Gq;
+      const int n = n_parts_of(s);
+      if (n <= 1) continue;                                        // written directly in phase B
+      const int b = s / a.nkv, kvh = s - b * a.nkv;
+      const float* r0 = a.rec + (int64_t)rec_base(s) * kBRecFloats;
+      if (warp == 0) {                                             // m, weights and l of every record, fixed order
+        float mloc = -INFINITY;
+        for (int r = lane; r < n; r += 32) {
+          const float2 ml = __ldcg(reinterpret_cast<const float2*>(r0 + (int64_t)r * kBRecFloats + 8 * kBD) + hh);
+          fr[r] = ml.x;
+          fr[256 + r] = ml.y;
+          mloc = fmaxf(mloc, ml.x);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
+        __syncwarp();
+        float lsum = 0.f;
+        for (int r = lane; r < n; r += 32) {
+          const float m = fr[r];
+          const float f = m == -INFINITY ? 0.f : exp2f(m * c - mloc * c);
+          fr[r] = f;
+          lsum += fr[256 + r] * f;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+        if (lane == 0) {
+          s_stat[0] = mloc;
+          s_stat[1] = lsum;
+        }
+      }
+      cons_sync();
+      {                                                            // warp w: records r = w (mod 8), 4 dims per lane
+        const int d0 = lane * 4;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+        for (int r = warp; r < n; r += kBW) {
+          const float f = fr[r];
+          const float4 v = __ldcg(reinterpret_cast<const float4*>(r0 + (int64_t)r * kBRecFloats + hh * kBD + d0));
+          acc[0] += v.x * f;
+          acc[1] += v.y * f;
+          acc[2] += v.z * f;
+          acc[3] += v.w * f;
+        }
+        *reinterpret_cast<float4*>(part + warp * kBD + d0) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      }
+      cons_sync();
+      if (tid < 32) {
+        const int d0 = tid * 4;
+        float ov[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int w = 0; w < kBW; ++w) {
+          const float4 v = *reinterpret_cast<const float4*>(part + w * kBD + d0);
+          ov[0] += v.x;
+          ov[1] += v.y;
+          ov[2] += v.z;
+          ov[3] += v.w;
+        }
+        const int qh = kvh * a.Gq + hh;
+        const float m = s_stat[0];
+        float den = s_stat[1];
+        if (a.sinks && m != -INFINITY) den += exp2f(a.sinks[qh] * kBLog2e - m * c);
+        const float inv = den > 0.f ? 1.0f / den : 0.f;
+        *reinterpret_cast<uint2*>(a.attn + (int64_t)b * a.Ko + qh * kBD + d0) =
+            make_uint2(pack_bf16x2(ov[0] * inv, ov[1] * inv), pack_bf16x2(ov[2] * inv, ov[3] * inv));
+      }
+      cons_sync();
+    }
+  }
+  grid_sync(&a.ws->gs, G, 2, kBCons, 1, &s_ok, status);
+  pdl_trigger();
+
+  // ---- C: O projection from the resident weights ----
+  if (ngo > 0) {
+    stage_rows_f16(a.attn, a.Ko, M, a.Ko, xs_o, shift, red_n, kBCons, 1, true);
+    if (cons_sync_and(mbar_wait(&bar_wo, 0, status))) {
+      gemv_resident<kBGO>(wo, wo + a.wo_scale_off, ngo, a.nks_o, xs_o, a.Ko, M, red, warp, lane);
+      cons_sync();
+      gemv_finish(red, ngo, M, a.gs_o[0], shift, a.out, a.ldr, go0 * 16);
+    }
+  }
+  grid_sync_retire(&a.ws->gs, G);
+}
+
+struct BlockLayout {
+  size_t wq_bytes, wo_bytes, xs_bytes, red_bytes, ring_off, wo_off, xs_off, red_off, total;
+  int np;
+};
+
+static BlockLayout block_layout(int M, int H, int Ko, int gq_per, int go_per, int nks_q, int nks_o, int sms) {
+  BlockLayout L{};
+  auto up = [](size_t v, size_t a) { return (v + a - 1) / a * a; };
+  const size_t wq = up((size_t)gq_per * nks_q * 2048, 1024) + up((size_t)gq_per * nks_q * 256, 1024);
+  // phase B over region A: warp partials [8][8][128] fp32, (m, l) [8][16] x 2, merge tables
+  const size_t partials = (size_t)kBW * 8 * kBD * 4 + (size_t)kBW * 16 * 8 + (size_t)sms * 64 + 64;
+  const size_t xs_o = (size_t)M * xs_stride(Ko) * 2;
+  L.wq_bytes = up(std::max(wq, partials), 1024);
+  L.wo_bytes = up((size_t)go_per * nks_o * 2048, 1024) + up((size_t)go_per * nks_o * 256, 1024);
+  L.xs_bytes = up((size_t)M * xs_stride(H) * 2, 1024);
+  L.red_bytes = up((size_t)std::max(kBGQ, kBGO) * kBW * 128 * 4, 1024);
+  const size_t budget = 227 * 1024 - 4096;           // dynamic shared memory left beside the static arrays
+  const size_t fixed = 1024 + L.wq_bytes + L.wo_bytes + L.xs_bytes + L.red_bytes;
+  L.np = 0;
+  if (fixed < budget) L.np = (int)std::min<size_t>(kBMaxSlots, (budget - fixed) / kBPageBytes);
+  if (L.np >= 2 && L.wq_bytes + (size_t)L.np * kBPageBytes < xs_o) {   // phase C staging must fit over A + ring
+    const size_t extra = up(xs_o - L.wq_bytes - (size_t)L.np * kBPageBytes, 1024);
+    L.wq_bytes += extra;
+    const size_t fixed2 = fixed + extra;
+    L.np = fixed2 < budget ? (int)std::min<size_t>(kBMaxSlots, (budget - fixed2) / kBPageBytes) : 0;
+  }
+  L.ring_off = L.wq_bytes;
+  L.wo_off = L.ring_off + (size_t)L.np * kBPageBytes;
+  L.xs_off = L.wo_off + L.wo_bytes;
+  L.red_off = L.xs_off + L.xs_bytes;
+  L.total = 1024 + L.red_off + L.red_bytes;
+  return L;
+}
+
+static size_t block_ws_bytes(int64_t Nqkv, int64_t Ko, int sms) {
+  return sizeof(BlockWs) + (size_t)8 * Nqkv * 2 + (size_t)8 * Ko * 2 + (size_t)(sms + kBMaxSeg) * kBRecFloats * 4 + 256;
+}
+
+}  // namespace flint
+
+using namespace flint;
+
+extern "C" int64_t flint_attn_block_workspace_bytes(int64_t n_qkv, int64_t k_o) {
+  const int sms = num_sms();
+  return (int64_t)block_ws_bytes(n_qkv, k_o, sms > 0 ? sms : 148);
+}
+
+extern "C" int flint_attn_block(const void* x, int64_t ldx, const int32_t* tokens, const void* res, int64_t ldr,
+                                const void* norm_w, float eps, int64_t M, int64_t H, const void* Wqkv, const void* Sqkv,
+                                const float* gs_qkv, int64_t num_q_heads, int64_t num_kv_heads, const void* q_norm_w,
+                                const void* k_norm_w, float eps_head, const int64_t* positions, const float* cos_sin,
+                                int64_t cs_stride, void* kv_cache, int64_t num_blocks, int64_t stride_block,
+                                int64_t stride_head, const int32_t* block_tables, int64_t bt_stride, int64_t max_blocks,
+                                const int32_t* seq_lens, const int64_t* slots, const float* sinks, int64_t window,
+                                float scale, const void* Wo, const void* So, const float* gs_o, int64_t n_o, void* out,
+                                void* res_out, void* q_out, void* attn_out, void* workspace, int pdl, void* stream) {
+  if (!x || !norm_w || !Wqkv || !Sqkv || !gs_qkv || !q_norm_w || !k_norm_w || !kv_cache || !block_tables || !seq_lens ||
+      !Wo || !So || !gs_o || !out || !res_out || !workspace || (cos_sin && !positions))
+    return FLINT_ERR_ARGUMENT;
+  const int sms = num_sms();
+  if (sms <= 0 || sms > 256) return FLINT_ERR_DEVICE;
+  if (M < 1 || M > 8 || H < kSliceK || H % kSliceK != 0 || H > 8192 || num_kv_heads < 1 || num_q_heads % num_kv_heads != 0 ||
+      num_q_heads / num_kv_heads > 8 || M * num_kv_heads > kBMaxSeg || ldx < H || ldr < H || n_o < 16 || n_o % 16 != 0 ||
+      num_blocks < 1 || max_blocks < 1 || window < 0 || stride_head < 2 * kBD || stride_block < num_kv_heads * stride_head)
+    return FLINT_ERR_SHAPE;
+  const int64_t Nqkv = (num_q_heads + 2 * num_kv_heads) * kBD, Ko = num_q_heads * kBD;
+  if (Ko % kSliceK != 0 || Ko > 8192) return FLINT_ERR_SHAPE;
+  if (!aligned(x, 16) || ldx % 8 != 0 || ldr % 8 != 0 || (res && !aligned(res, 16)) || !aligned(norm_w, 16) ||
+      !aligned(out, 16) || !aligned(res_out, 16) || !aligned(Wqkv, 16) || !aligned(Sqkv, 16) || !aligned(Wo, 16) ||
+      !aligned(So, 16) || !aligned(kv_cache, 16) || stride_block % 8 != 0 || stride_head % 8 != 0 ||
+      (attn_out && !aligned(attn_out, 16)) || !aligned(workspace, 256))
+    return FLINT_ERR_ALIGN;
+  const int gq_total = (int)(Nqkv / 16), go_total = (int)(n_o / 16);
+  const int gq_per = (gq_total + sms - 1) / sms, go_per = (go_total + sms - 1) / sms;
+  if (gq_per > kBGQ || go_per > kBGO) return FLINT_ERR_SHAPE;
+  const int nks_q = (int)(H / kSliceK), nks_o = (int)(Ko / kSliceK);
+  const BlockLayout L = block_layout((int)M, (int)H, (int)Ko, gq_per, go_per, nks_q, nks_o, sms);
+  if (L.np < 2 || L.total > 227 * 1024) return FLINT_ERR_SHAPE;
+
+  // weights as 3-D views [slice][row][bytes of the slice] so one box carries a 16-row group over all of K
+  CUtensorMap mqc, mqs, moc, mos, mkv;
+  auto enc3 = [](CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t row_bytes, uint64_t nks,
+                 bool swz) {
+    const uint64_t d[3] = {inner, rows, nks};
+    const uint64_t st[2] = {row_bytes, inner};
+    const uint32_t bx[3] = {(uint32_t)inner, 16u, (uint32_t)nks};
+    return encode_u8_3d(m, base, d, st, bx, swz);
+  };
+  int rc = enc3(&mqc, Wqkv, 128, Nqkv, H / 2, H / kSliceK, true);
+  if (!rc) rc = enc3(&mqs, Sqkv, 16, Nqkv, H / 16, H / kSliceK, false);
+  if (!rc) rc = enc3(&moc, Wo, 128, n_o, Ko / 2, Ko / kSliceK, true);
+  if (!rc) rc = enc3(&mos, So, 16, n_o, Ko / 16, Ko / kSliceK, false);
+  if (rc) return rc;
+  // KV pages as a 5-D view [block][head][quarter K0 K1 V0 V1][16 rows][64 dims]: one box per page
+  const uint64_t dims[5] = {64, kBPage, 4, (uint64_t)num_kv_heads, (uint64_t)num_blocks};
+  const uint64_t strides[4] = {2 * kBD * 2, 128, (uint64_t)stride_head * 2, (uint64_t)stride_block * 2};
+  const uint32_t box[5] = {64, kBPage, 4, 1, 1};
+  rc = encode_bf16_5d(&mkv, kv_cache, dims, strides, box);
+  if (rc) return rc;
+
+  uint8_t* wsb = static_cast<uint8_t*>(workspace);
+  BlockArgs a{};
+  a.x = (const bf16*)x; a.ldx = ldx; a.tokens = tokens; a.res = (const bf16*)res; a.ldr = ldr; a.nw = (const bf16*)norm_w;
+  a.eps = eps; a.M = (int)M; a.H = (int)H; a.Nqkv = (int)Nqkv; a.nq = (int)num_q_heads; a.nkv = (int)num_kv_heads;
+  a.Gq = (int)(num_q_heads / num_kv_heads); a.gs_qkv = gs_qkv; a.q_w = (const bf16*)q_norm_w; a.k_w = (const bf16*)k_norm_w;
+  a.eps_head = eps_head; a.positions = positions; a.cos_sin = cos_sin; a.cs_stride = cs_stride; a.kv = (bf16*)kv_cache;
+  a.st_block = stride_block; a.st_head = stride_head; a.bt = block_tables; a.bt_stride = bt_stride;
+  a.max_blocks = (int)max_blocks; a.seq_lens = seq_lens; a.slots = slots; a.sinks = sinks; a.window = (int)window;
+  a.c = scale * kBLog2e; a.Ko = (int)Ko; a.No = (int)n_o; a.gs_o = gs_o; a.out = (bf16*)out; a.res_out = (bf16*)res_out;
+  a.q_out = (bf16*)q_out;
+  a.y = reinterpret_cast<bf16*>(wsb + sizeof(BlockWs));
+  bf16* ws_attn = a.y + 8 * Nqkv;
+  a.attn = attn_out ? (bf16*)attn_out : ws_attn;
+  a.rec = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(ws_attn + 8 * Ko) + 255) & ~uintptr_t(255));
+  a.gq_total = gq_total; a.go_total = go_total; a.nks_q = nks_q; a.nks_o = nks_o; a.np = L.np;
+  a.off_ring = (uint32_t)L.ring_off; a.off_wo = (uint32_t)L.wo_off; a.off_xs = (uint32_t)L.xs_off;
+  a.off_red = (uint32_t)L.red_off;
+  a.wq_scale_off = (uint32_t)(((size_t)gq_per * nks_q * 2048 + 1023) / 1024 * 1024);
+  a.wo_scale_off = (uint32_t)(((size_t)go_per * nks_o * 2048 + 1023) / 1024 * 1024);
+  a.ws = reinterpret_cast<BlockWs*>(wsb);
+
+  // one CTA per SM must be resident (cooperative launch): give back ring slots until the occupancy query agrees
+  set_max_carveout(attn_block_kernel);
+  size_t smem = L.total;
+  int np = L.np;
+  for (;;) {
+    if (cudaFuncSetAttribute(attn_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return record_cuda(cudaGetLastError(), FLINT_ERR_LAUNCH);
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_block_kernel, kBThreads, smem) != cudaSuccess)
+      return record_cuda(cudaGetLastError(), FLINT_ERR_LAUNCH);
+    if (per_sm >= 1) break;
+    if (np <= 2) {
+      cudaFuncAttributes fa{};
+      cudaFuncGetAttributes(&fa, attn_block_kernel);
+      char msg[160];
+      snprintf(msg, sizeof(msg), "attn_block: no CTA fits an SM (regs %d, static smem %zu, dynamic smem %zu)", fa.numRegs,
+               fa.sharedSizeBytes, smem);
+      record_message(msg);
+      return FLINT_ERR_LAUNCH;
+    }
+    --np;
+    smem -= kBPageBytes;
+  }
+  a.np = np;
+  a.off_wo = (uint32_t)(L.ring_off + (size_t)np * kBPageBytes);
+  a.off_xs = a.off_wo + (uint32_t)L.wo_bytes;
+  a.off_red = a.off_xs + (uint32_t)L.xs_bytes;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(sms);
+  cfg.blockDim = dim3(kBThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeCooperative;
+  at[0].val.cooperative = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return record_cuda(cudaLaunchKernelEx(&cfg, attn_block_kernel, mqc, mqs, moc, mos, mkv, a), FLINT_ERR_LAUNCH);
+}

@@ -294,6 +294,194 @@ __device__ __forceinline__ void add_rmsnorm_2pass(const bf16* x, int64_t ldx, co
   sync();
 }
 
+// add_rmsnorm_2pass + stage_rows_f16 without the bf16 staging buffer: s = x (+ res) (row m of x at x + rows[m] * ldx
+// when rows is given: an embedding gather), res_out = bf16(s) (optional), xn = bf16(s * rsqrt(mean(s^2) + eps) * w)
+// written straight to its permuted place in xs and then rescaled to f16 by 2^shift[m] in place.  The same per-thread
+// fmaf chains and warp order as add_rmsnorm_2pass, so every CTA running it with the same thread count gets identical
+// bits.  res and res_out rows are ldr elements apart.  red: >= (nthreads/32) * 8 + 8 floats.
+__device__ __forceinline__ void norm_stage_f16(const bf16* x, int64_t ldx, const int* rows, const bf16* res, int64_t ldr,
+                                               const bf16* __restrict__ w, float eps, int M, int H, __half* xs, int* shift,
+                                               float* red, bf16* res_out, int nthreads, int bar) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = nthreads >> 5, H8 = H >> 3;
+  auto sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthreads) : "memory"); };
+  auto xrow = [&](int m) { return x + (rows ? (int64_t)rows[m] : (int64_t)m) * ldx; };
+  auto load = [&](int m, int k8, float* a) {
+    bf16x8_to_f32(reinterpret_cast<const uint4*>(xrow(m))[k8], a);
+    if (res) {
+      float b[8];
+      bf16x8_to_f32(reinterpret_cast<const uint4*>(res + m * ldr)[k8], b);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) a[j] += b[j];
+    }
+  };
+  int* rmax = reinterpret_cast<int*>(red + nw * 8);
+  float ss[8];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    ss[m] = 0.f;
+    if (m < M)
+      for (int k8 = tid; k8 < H8; k8 += nthreads) {
+        float a[8];
+        load(m, k8, a);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss[m] = fmaf(a[j], a[j], ss[m]);
+      }
+  }
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    float v = ss[m];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[warp * 8 + m] = v;
+  }
+  if (tid < 8) rmax[tid] = 0;
+  sync();
+  for (int idx = tid; idx < M * H8; idx += nthreads) {
+    const int m = idx / H8, k8 = idx - m * H8;
+    float tot = 0.f;
+    for (int ww = 0; ww < nw; ++ww) tot += red[ww * 8 + m];
+    const float rs = rsqrtf(tot / (float)H + eps);
+    float a[8], wf[8];
+    load(m, k8, a);
+    if (res_out) {
+      uint32_t pr[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __nv_bfloat162 r2 = __floats2bfloat162_rn(a[2 * j], a[2 * j + 1]);
+        pr[j] = *reinterpret_cast<uint32_t*>(&r2);
+      }
+      reinterpret_cast<uint4*>(res_out + m * ldr)[k8] = make_uint4(pr[0], pr[1], pr[2], pr[3]);
+    }
+    bf16x8_to_f32(reinterpret_cast<const uint4*>(w)[k8], wf);
+    uint32_t pk[4];
+    float mx = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __nv_bfloat162 n2 = __floats2bfloat162_rn(a[2 * j] * rs * wf[2 * j], a[2 * j + 1] * rs * wf[2 * j + 1]);
+      mx = fmaxf(mx, fmaxf(fabsf(__low2float(n2)), fabsf(__high2float(n2))));
+      pk[j] = *reinterpret_cast<uint32_t*>(&n2);
+    }
+    atomicMax(&rmax[m], __float_as_int(mx));
+    *reinterpret_cast<uint4*>(xs + m * xs_stride(H) + xs_perm(k8 * 8)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+  }
+  sync();
+  for (int r = tid; r < M; r += nthreads) {
+    const float mx = __int_as_float(rmax[r]);
+    int s = 0;
+    if (mx > 0.f && !(mx != mx) && mx <= 3.0e38f) s = 14 - ((int)((__float_as_uint(mx) >> 23) & 0xFF) - 127);
+    shift[r] = s;
+  }
+  sync();
+  for (int idx = tid; idx < M * H8; idx += nthreads) {
+    const int r = idx / H8, k8 = idx - r * H8;
+    uint4* p = reinterpret_cast<uint4*>(xs + r * xs_stride(H) + xs_perm(k8 * 8));
+    float f[8];
+    bf16x8_to_f32(*p, f);
+    const int s = shift[r];
+    uint32_t h[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __half2 v = __floats2half2_rn(ldexpf(f[2 * j], s), ldexpf(f[2 * j + 1], s));
+      h[j] = *reinterpret_cast<uint32_t*>(&v);
+    }
+    *p = make_uint4(h[0], h[1], h[2], h[3]);
+  }
+  sync();
+}
+
+// norm_stage_f16 with ONE global pass, for H / 8 <= nthreads: each thread owns one 8-wide chunk of every row and keeps
+// x (+ res) in registers between the sum of squares and the normalisation (same fmaf chains, same bits).
+// (norm_stage_f16_1w: the thread's 8 norm weights, w[8 tid .. 8 tid + 7], are passed in, loaded before the PDL wait.)
+__device__ __forceinline__ void norm_stage_f16_1w(const bf16* x, int64_t ldx, const int* rows, const bf16* res, int64_t ldr,
+                                                  uint4 wchunk, float eps, int M, int H, __half* xs, int* shift, float* red,
+                                                  bf16* res_out, int nthreads, int bar) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = nthreads >> 5, H8 = H >> 3;
+  auto sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthreads) : "memory"); };
+  const bool own = tid < H8;
+  int* rmax = reinterpret_cast<int*>(red + nw * 8);
+  float a[8][8], ss[8];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    ss[m] = 0.f;
+    if (m < M && own) {
+      bf16x8_to_f32(reinterpret_cast<const uint4*>(x + (rows ? (int64_t)rows[m] : (int64_t)m) * ldx)[tid], a[m]);
+      if (res) {
+        float b[8];
+        bf16x8_to_f32(reinterpret_cast<const uint4*>(res + m * ldr)[tid], b);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a[m][j] += b[j];
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss[m] = fmaf(a[m][j], a[m][j], ss[m]);
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    float v = ss[m];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[warp * 8 + m] = v;
+  }
+  if (tid < 8) rmax[tid] = 0;
+  sync();
+  float wf[8];
+  bf16x8_to_f32(wchunk, wf);
+  uint32_t pk[8][4];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    if (m < M && own) {
+      float tot = 0.f;
+      for (int ww = 0; ww < nw; ++ww) tot += red[ww * 8 + m];
+      const float rs = rsqrtf(tot / (float)H + eps);
+      if (res_out) {
+        uint32_t pr[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          __nv_bfloat162 r2 = __floats2bfloat162_rn(a[m][2 * j], a[m][2 * j + 1]);
+          pr[j] = *reinterpret_cast<uint32_t*>(&r2);
+        }
+        reinterpret_cast<uint4*>(res_out + m * ldr)[tid] = make_uint4(pr[0], pr[1], pr[2], pr[3]);
+      }
+      float mx = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __nv_bfloat162 n2 = __floats2bfloat162_rn(a[m][2 * j] * rs * wf[2 * j], a[m][2 * j + 1] * rs * wf[2 * j + 1]);
+        mx = fmaxf(mx, fmaxf(fabsf(__low2float(n2)), fabsf(__high2float(n2))));
+        pk[m][j] = *reinterpret_cast<uint32_t*>(&n2);
+      }
+      atomicMax(&rmax[m], __float_as_int(mx));
+    }
+  }
+  sync();
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    if (m < M) {
+      const float mx = __int_as_float(rmax[m]);
+      int s = 0;
+      if (mx > 0.f && !(mx != mx) && mx <= 3.0e38f) s = 14 - ((int)((__float_as_uint(mx) >> 23) & 0xFF) - 127);
+      if (tid == 0) shift[m] = s;
+      if (own) {
+        uint32_t h[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          __half2 v = __floats2half2_rn(ldexpf(bf16_bits_to_f32(pk[m][j] & 0xFFFFu), s),
+                                        ldexpf(bf16_bits_to_f32(pk[m][j] >> 16), s));
+          h[j] = *reinterpret_cast<uint32_t*>(&v);
+        }
+        *reinterpret_cast<uint4*>(xs + m * xs_stride(H) + xs_perm(tid * 8)) = make_uint4(h[0], h[1], h[2], h[3]);
+      }
+    }
+  }
+  sync();
+}
+
+__device__ __forceinline__ void norm_stage_f16_1(const bf16* x, int64_t ldx, const int* rows, const bf16* res, int64_t ldr,
+                                                 const bf16* __restrict__ w, float eps, int M, int H, __half* xs,
+                                                 int* shift, float* red, bf16* res_out, int nthreads, int bar) {
+  const uint4 wc = (int)threadIdx.x < (H >> 3) ? reinterpret_cast<const uint4*>(w)[threadIdx.x] : make_uint4(0u, 0u, 0u, 0u);
+  norm_stage_f16_1w(x, ldx, rows, res, ldr, wc, eps, M, H, xs, shift, red, res_out, nthreads, bar);
+}
+
 // Whole-block variant (the LM head): all threads, __syncthreads.
 __device__ __forceinline__ void stage_x_f16(const bf16* __restrict__ x, int64_t ldx, int M, int K, __half* xs,
                                             int* shift, float* red) {

@@ -1,8 +1,9 @@
 // Grid-wide barrier for persistent (cooperatively launched) kernels.
 //
 // A monotonic arrival counter: barrier k of a launch completes when the counter reaches (k + 1) * nblocks.  Each
-// CTA's thread 0 fences, adds 1 with a release reduction (no return value) and polls the counter with acquire loads;
-// the CTA's other participating threads wait on a named barrier.  Polls are bounded: after FLINT_WAIT_LIMIT polls the
+// CTA's thread 0 adds 1 with a release reduction (no return value) and polls the counter with acquire loads; the
+// CTA's other participating threads wait on a named barrier on both sides, which orders their memory operations
+// with thread 0's release / acquire (both are cumulative), so no separate fences are needed.  Polls are bounded: after FLINT_WAIT_LIMIT polls the
 // CTA records STATUS_WAIT_TIMEOUT and stops waiting.  At the end of a launch every CTA calls grid_sync_retire; the
 // last one to do so zeroes the counter for the next launch (all CTAs have finished polling by then).
 #pragma once
@@ -29,7 +30,6 @@ __device__ __forceinline__ bool grid_sync(GridSync* gs, unsigned nblocks, unsign
   asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthreads) : "memory");
   if (threadIdx.x == 0) {
     int ok = 1;
-    __threadfence();
     asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(&gs->count) : "memory");
     const unsigned target = (k + 1) * nblocks;
     unsigned i = 0;
@@ -40,7 +40,6 @@ __device__ __forceinline__ bool grid_sync(GridSync* gs, unsigned nblocks, unsign
         break;
       }
     }
-    __threadfence();
     *s_ok = ok;
   }
   asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthreads) : "memory");

@@ -1,6 +1,6 @@
-// (4) NVFP4 LM head: logits and the greedy argmax in one pass over the head.
-// Replaces the reference's Triton _nv4_fma / _nv4_head (fast/fast_head.py:68-121) and the greedy pick of vLLM's
-// sampler.  Kernel design: lm_head_kernel.cuh.
+// (4) NVFP4 LM head: logits and the greedy argmax, or the seeded top-k -> top-p draw, in one pass over the head.
+// Replaces the reference's Triton _nv4_fma / _nv4_head (fast/fast_head.py:68-121) and the pick of vLLM's sampler
+// that follows compute_logits (fast/fast_head.py:360-381).  Kernel design: lm_head_kernel.cuh, sampling.cuh.
 #include "lm_head_kernel.cuh"
 #include "runtime.cuh"
 
@@ -39,7 +39,7 @@ extern "C" int flint_lm_head_nv4_fused(const void* x, int64_t ldx, const void* r
   if (rc) return rc;
   rc = encode_u8_2d(&ms, S, K / 16, V, K / 16, 16, kHeadRows, false);
   if (rc) return rc;
-  auto kern = lm_head_kernel<kHeadStages, kHeadWarps>;
+  auto kern = lm_head_kernel<kHeadStages, kHeadWarps, false>;
   const size_t smem = head_smem((int)M, (int)K, norm_w != nullptr);
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return FLINT_ERR_LAUNCH;
@@ -47,7 +47,69 @@ extern "C" int flint_lm_head_nv4_fused(const void* x, int64_t ldx, const void* r
   const int grid = ngroups < sms ? ngroups : sms;
   return launch(kern, dim3(grid), dim3((kHeadWarps + 1) * 32), smem, stream, pdl, mc, ms, (const bf16*)x, ldx,
                 (const bf16*)res, (const bf16*)norm_w, eps, (int)M, gs, (int)V, (int)K, logits, ld_logits, (int*)token_ids,
-                (HeadWorkspace*)workspace);
+                (HeadWorkspace*)workspace, SampleParams{});
+}
+
+namespace flint {
+
+static size_t sample_cand_bytes() { return (size_t)8 * kSampleMaxCtas * kSampleMaxK * 8; }
+static size_t sample_logits_offset() { return (sizeof(HeadWorkspace) + sample_cand_bytes() + 255) & ~size_t(255); }
+
+}  // namespace flint
+
+extern "C" int64_t flint_lm_head_sample_workspace_bytes(int64_t M, int64_t V) {
+  using namespace flint;
+  if (M < 1 || M > 8 || V < 1) return -1;
+  return (int64_t)(sample_logits_offset() + (size_t)M * (size_t)V * 4);
+}
+
+extern "C" int flint_lm_head_nv4_sample(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps,
+                                        int64_t M, const void* P, const void* S, float gs, int64_t V, int64_t K,
+                                        float* logits, int64_t ld_logits, float temperature, int64_t top_k, float top_p,
+                                        const uint64_t* seeds, const int32_t* step, int32_t* token_ids, int32_t* cand_ids,
+                                        float* cand_logits, int32_t* kept, void* workspace, int pdl, void* stream) {
+  using namespace flint;
+  if (!x || !P || !S || (res && !norm_w) || !seeds || !token_ids) return FLINT_ERR_ARGUMENT;
+  if (!(temperature > 0.f) || !(temperature < INFINITY) || !(top_p > 0.f) || !(top_p <= 1.f)) return FLINT_ERR_ARGUMENT;
+  if (M < 1 || M > 8 || V < 1 || V > (1ll << 30) || K < kSliceK || K % kSliceK != 0 || K > 8192 || ldx < K)
+    return FLINT_ERR_SHAPE;
+  if (top_k < 1 || top_k > kSampleMaxK || top_k > V) return FLINT_ERR_ARGUMENT;
+  if (logits && ld_logits < V) return FLINT_ERR_SHAPE;
+  if (!aligned(P, 16) || !aligned(S, 16) || !aligned(x, 16) || ldx % 8 != 0 || (res && !aligned(res, 16)) ||
+      (norm_w && !aligned(norm_w, 16)) || (logits && !aligned(logits, 4)))
+    return FLINT_ERR_ALIGN;
+  if (!workspace) return FLINT_ERR_WORKSPACE;
+  if (!aligned(workspace, 256)) return FLINT_ERR_ALIGN;
+  const int sms = num_sms();
+  if (sms <= 0) return FLINT_ERR_DEVICE;
+  CUtensorMap mc, ms;
+  int rc = encode_u8_2d(&mc, P, K / 2, V, K / 2, 128, kHeadRows, true);
+  if (rc) return rc;
+  rc = encode_u8_2d(&ms, S, K / 16, V, K / 16, 16, kHeadRows, false);
+  if (rc) return rc;
+  auto kern = lm_head_kernel<kHeadStages, kHeadWarps, true>;
+  const size_t smem = head_smem((int)M, (int)K, norm_w != nullptr);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return FLINT_ERR_LAUNCH;
+  const int ngroups = (int)((V + kHeadRows - 1) / kHeadRows);
+  int grid = ngroups < sms ? ngroups : sms;
+  if (grid > kSampleMaxCtas) grid = kSampleMaxCtas;
+  uint8_t* wsb = static_cast<uint8_t*>(workspace);
+  SampleParams sp;
+  sp.temperature = temperature;
+  sp.top_p = top_p;
+  sp.top_k = (int)top_k;
+  sp.seeds = reinterpret_cast<const unsigned long long*>(seeds);
+  sp.step = step;
+  sp.cand = reinterpret_cast<unsigned long long*>(wsb + sizeof(HeadWorkspace));
+  sp.cand_ids = cand_ids;
+  sp.cand_logits = cand_logits;
+  sp.kept = kept;
+  float* lg = logits ? logits : reinterpret_cast<float*>(wsb + sample_logits_offset());
+  const int64_t ldl = logits ? ld_logits : V;
+  return launch(kern, dim3(grid), dim3((kHeadWarps + 1) * 32), smem, stream, pdl, mc, ms, (const bf16*)x, ldx,
+                (const bf16*)res, (const bf16*)norm_w, eps, (int)M, gs, (int)V, (int)K, lg, ldl, (int*)token_ids,
+                (HeadWorkspace*)workspace, sp);
 }
 
 extern "C" int flint_lm_head_nv4(const void* x, int64_t ldx, int64_t M, const void* P, const void* S, float gs, int64_t V,

@@ -5,9 +5,11 @@
 // NS stages of weights are in flight per SM without holding any of it in registers.  Products accumulate with
 // mma.sync (16 rows x up to 8 tokens per warp).  Epilogue: logits = D * 2^-shift[token] * gs (optionally stored),
 // then a (value, lowest index) argmax folded per warp, per CTA (shared memory) and across CTAs (64-bit atomicMax
-// in the workspace; the last CTA to arrive writes the token ids and zeroes the workspace).
+// in the workspace; the last CTA to arrive writes the token ids and zeroes the workspace).  The SAMPLE instantiation
+// replaces the argmax with the seeded top-k -> top-p -> draw of sampling.cuh over the logits the CTAs just wrote.
 #pragma once
 #include "nvfp4_tile.cuh"
+#include "sampling.cuh"
 
 namespace flint {
 
@@ -18,12 +20,136 @@ struct HeadWorkspace {
   unsigned pad[14];
 };
 
-template <int NS, int NW>
+// Sampling parameters and buffers of the SAMPLE instantiation (see sampling.cuh for the rule).
+struct SampleParams {
+  float temperature, top_p;
+  int top_k;
+  const unsigned long long* seeds;   // [M]
+  const int* step;                   // device step counter (the Philox counter's first word); null -> 0
+  unsigned long long* cand;          // workspace: per row, per CTA, its top_k keys sorted [M][grid][top_k]
+  int* cand_ids;                     // optional [M, top_k]: the candidates' token ids (-1 past the vocabulary)
+  float* cand_logits;                // optional [M, top_k]: their logits
+  int* kept;                         // optional [M]: candidates left after top-p
+};
+
+// Tail of the SAMPLE instantiation: per-CTA top_k of the rows it owns, then (last CTA) the global top_k, top-p and
+// the draw.  smem is the drained stage ring (at least 8 * kSampleSurvivors * 8 + 3 KB).
+template <int ROWS>
+__device__ __forceinline__ void head_sample_tail(uint8_t* smem, const float* logits, int64_t ldl, int M, int V, int g0,
+                                                 int g1, const SampleParams& sp, HeadWorkspace* ws, int* tokens,
+                                                 int* s_last) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int K = sp.top_k, G = gridDim.x;
+  unsigned long long* surv = reinterpret_cast<unsigned long long*>(smem);          // [8][kSampleSurvivors]
+  unsigned long long* tops = surv + 8 * kSampleSurvivors;                          // [8][kSampleMaxK]
+  float* wbuf = reinterpret_cast<float*>(tops + 8 * kSampleMaxK);                  // [8][kSampleMaxK]
+  unsigned long long* s_T = reinterpret_cast<unsigned long long*>(wbuf + 8 * kSampleMaxK);  // [8]
+  int* s_n = reinterpret_cast<int*>(s_T + 8);                                      // [8]
+
+  __syncthreads();                       // this CTA's logits are written and its stage ring is drained
+  if (warp < M) {
+    const int m = warp;
+    const float* lrow = logits + (int64_t)m * ldl;
+    const int r0 = min(g0 * ROWS, V), r1 = min(g1 * ROWS, V);
+    unsigned long long* buf = surv + m * kSampleSurvivors;
+    unsigned long long lm = 0ull;
+    for (int r = r0 + lane; r < r1; r += 32) lm = max(lm, argmax_key(lrow[r], r));
+    const unsigned long long T = warp_kth_largest(lm, K);
+    int n = 0;
+    for (int rb = r0; rb < r1; rb += 32) {
+      const int r = rb + lane;
+      n = warp_compact_ge(r < r1 ? argmax_key(lrow[r], r) : 0ull, T, buf, n, kSampleSurvivors, lane);
+    }
+    __syncwarp();
+    unsigned long long* out = sp.cand + ((int64_t)m * G + blockIdx.x) * K;
+    if (n <= kSampleSurvivors) {
+      warp_select_sorted(buf, n, K, out, lane);
+    } else {                             // heavy ties above the bound: K rounds straight over the logits
+      unsigned long long ceil = ~0ull;
+      for (int k = 0; k < K; ++k) {
+        unsigned long long best = 0ull;
+        for (int r = r0 + lane; r < r1; r += 32) {
+          const unsigned long long v = argmax_key(lrow[r], r);
+          if (v < ceil && v > best) best = v;
+        }
+        best = warp_max_u64(best);
+        if (lane == 0) out[k] = best;
+        ceil = best;
+      }
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) *s_last = (atomicAdd(&ws->counter, 1u) == (unsigned)G - 1u);
+  __syncthreads();
+  if (!*s_last) return;
+  __threadfence();
+
+  // last CTA: a lower bound on each row's global top_k-th key from the CTA maxima
+  if (warp < M) {
+    const int m = warp;
+    unsigned long long lm = 0ull;
+    for (int c = lane; c < G; c += 32) lm = max(lm, __ldcg(sp.cand + ((int64_t)m * G + c) * K));
+    const unsigned long long T = warp_kth_largest(lm, K);
+    if (lane == 0) {
+      s_T[m] = T;
+      s_n[m] = 0;
+    }
+  }
+  __syncthreads();
+  const int per_row = G * K;
+  for (int e = threadIdx.x; e < M * per_row; e += blockDim.x) {
+    const int m = e / per_row;
+    const unsigned long long key = __ldcg(sp.cand + e);
+    if (key != 0ull && key >= s_T[m]) {
+      const int pos = atomicAdd(&s_n[m], 1);
+      if (pos < kSampleSurvivors) surv[m * kSampleSurvivors + pos] = key;
+    }
+  }
+  __syncthreads();
+  if (warp < M) {
+    const int m = warp;
+    unsigned long long* top = tops + m * kSampleMaxK;
+    const int n = s_n[m];
+    if (n <= kSampleSurvivors) {
+      warp_select_sorted(surv + m * kSampleSurvivors, n, K, top, lane);
+    } else {                             // heavy ties: K rounds over the row's candidate lists
+      unsigned long long ceil = ~0ull;
+      for (int k = 0; k < K; ++k) {
+        unsigned long long best = 0ull;
+        for (int i = lane; i < per_row; i += 32) {
+          const unsigned long long v = __ldcg(sp.cand + (int64_t)m * per_row + i);
+          if (v < ceil && v > best) best = v;
+        }
+        best = warp_max_u64(best);
+        if (lane == 0) top[k] = best;
+        ceil = best;
+      }
+      __syncwarp();
+    }
+    const int step = sp.step ? *sp.step : 0;
+    const float u = sample_uniform(sp.seeds[m], (uint32_t)step, (uint32_t)m);
+    int kept = 1;
+    const int pick = sample_sorted(top, K, sp.temperature, sp.top_p, u, wbuf + m * kSampleMaxK, lane, &kept);
+    if (lane == 0) {
+      tokens[m] = (int)argmax_key_index(top[pick]);
+      if (sp.kept) sp.kept[m] = kept;
+    }
+    if (lane < K) {
+      const unsigned long long v = top[lane];
+      if (sp.cand_ids) sp.cand_ids[m * K + lane] = v ? (int)argmax_key_index(v) : -1;
+      if (sp.cand_logits) sp.cand_logits[m * K + lane] = v ? argmax_key_value(v) : -INFINITY;
+    }
+  }
+  if (threadIdx.x == 0) atomicExch(&ws->counter, 0u);
+}
+
+template <int NS, int NW, bool SAMPLE>
 __global__ void __launch_bounds__((NW + 1) * 32, 1)
 lm_head_kernel(const __grid_constant__ CUtensorMap map_codes, const __grid_constant__ CUtensorMap map_scales,
                const bf16* __restrict__ x, int64_t ldx, const bf16* __restrict__ res, const bf16* __restrict__ norm_w,
                float eps, int M, float gs, int V, int K, float* __restrict__ logits, int64_t ldl, int* __restrict__ tokens,
-               HeadWorkspace* ws) {
+               HeadWorkspace* ws, const SampleParams sp) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   using G = StageGeom<NW * 16>;
@@ -135,6 +261,11 @@ lm_head_kernel(const __grid_constant__ CUtensorMap map_codes, const __grid_const
       wbest[warp][n0] = kbest[0];
       wbest[warp][n1] = kbest[1];
     }
+  }
+  if constexpr (SAMPLE) {
+    static_assert(NS * G::bytes >= 8 * kSampleSurvivors * 8 + 8 * kSampleMaxK * 12 + 8 * 12, "stage ring too small");
+    head_sample_tail<ROWS>(smem, logits, ldl, M, V, g0, g1, sp, ws, tokens, &s_last);
+    return;
   }
   if (tokens == nullptr) return;
 

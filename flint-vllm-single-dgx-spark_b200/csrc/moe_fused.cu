@@ -338,8 +338,7 @@ static int launch_fused(int sms, const CUtensorMap& uc, const CUtensorMap& us, c
   at[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 2 : 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, uc, us, dc, ds, a);
-  return e == cudaSuccess ? FLINT_OK : FLINT_ERR_LAUNCH;
+  return record_cuda(cudaLaunchKernelEx(&cfg, kern, uc, us, dc, ds, a), FLINT_ERR_LAUNCH);
 }
 
 }  // namespace flint

@@ -1,5 +1,9 @@
 // Library-wide host helpers: version, error strings, per-device properties.
 #include "runtime.cuh"
+
+#include <stdio.h>
+
+#include <mutex>
 #include "tma.cuh"
 
 #include <cudaTypedefs.h>
@@ -51,6 +55,38 @@ int encode_u8_2d(CUtensorMap* map, const void* base, uint64_t cols_bytes, uint64
   return r == CUDA_SUCCESS ? FLINT_OK : FLINT_ERR_ALIGN;
 }
 
+int encode_u8_3d(CUtensorMap* map, const void* base, const uint64_t dims[3], const uint64_t strides_bytes[2],
+                 const uint32_t box[3], bool swizzle128) {
+  auto fn = get_encode_fn();
+  if (!fn) return FLINT_ERR_DEVICE;
+  if (!aligned(base, 16) || strides_bytes[0] % 16 != 0 || strides_bytes[1] % 16 != 0) return FLINT_ERR_ALIGN;
+  cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+  cuuint64_t st[2] = {strides_bytes[0], strides_bytes[1]};
+  cuuint32_t b[3] = {box[0], box[1], box[2]};
+  cuuint32_t e[3] = {1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), d, st, b, e,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? FLINT_OK : FLINT_ERR_ALIGN;
+}
+
+int encode_bf16_5d(CUtensorMap* map, const void* base, const uint64_t dims[5], const uint64_t strides_bytes[4],
+                   const uint32_t box[5]) {
+  auto fn = get_encode_fn();
+  if (!fn) return FLINT_ERR_DEVICE;
+  if (!aligned(base, 16)) return FLINT_ERR_ALIGN;
+  for (int i = 0; i < 4; ++i)
+    if (strides_bytes[i] % 16 != 0) return FLINT_ERR_ALIGN;
+  cuuint64_t d[5] = {dims[0], dims[1], dims[2], dims[3], dims[4]};
+  cuuint64_t st[4] = {strides_bytes[0], strides_bytes[1], strides_bytes[2], strides_bytes[3]};
+  cuuint32_t b[5] = {box[0], box[1], box[2], box[3], box[4]};
+  cuuint32_t e[5] = {1, 1, 1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(base), d, st, b, e,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? FLINT_OK : FLINT_ERR_ALIGN;
+}
+
 int encode_bf16_4d(CUtensorMap* map, const void* base, const uint64_t dims[4], const uint64_t strides_bytes[3],
                    const uint32_t box[4]) {
   auto fn = get_encode_fn();
@@ -69,6 +105,40 @@ int encode_bf16_4d(CUtensorMap* map, const void* base, const uint64_t dims[4], c
 }
 
 }  // namespace flint
+
+namespace flint {
+
+static thread_local char g_last_cuda_error[256] = "";
+
+int record_cuda(cudaError_t e, int code) {
+  if (e == cudaSuccess) return FLINT_OK;
+  snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "%s: %s", cudaGetErrorName(e), cudaGetErrorString(e));
+  return code;
+}
+
+bool carveout_pending(const void* kern) {
+  static std::mutex mu;
+  static const void* done_kern[256];
+  static int done_dev[256];
+  static int n_done = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < n_done; ++i)
+    if (done_kern[i] == kern && done_dev[i] == dev) return false;
+  if (n_done < 256) {
+    done_kern[n_done] = kern;
+    done_dev[n_done] = dev;
+    ++n_done;
+  }
+  return true;
+}
+
+void record_message(const char* msg) { snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "%s", msg); }
+
+}  // namespace flint
+
+extern "C" const char* flint_last_cuda_error(void) { return flint::g_last_cuda_error; }
 
 extern "C" int flint_version(void) { return 100; }
 

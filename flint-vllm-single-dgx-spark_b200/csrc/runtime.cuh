@@ -12,15 +12,20 @@ int num_sms(int* dev_out = nullptr);
 
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Records the CUDA error of a failed runtime call made by this library (per host thread; flint_last_cuda_error) and
+// returns the library status for it: FLINT_OK for cudaSuccess, else `code`.
+int record_cuda(cudaError_t e, int code);
+// Records a library diagnostic in the same slot (flint_last_cuda_error).
+void record_message(const char* msg);
+
 // Every kernel runs with the maximum shared-memory carveout, so consecutive kernels of a decode step never make an
-// SM re-partition L1 / shared memory between them.
+// SM re-partition L1 / shared memory between them.  Set once per (kernel, device).
+bool carveout_pending(const void* kern);
+
 template <typename... KArgs>
 inline void set_max_carveout(void (*kern)(KArgs...)) {
-  static int done_dev[64] = {0};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || done_dev[dev]) return;
+  if (!carveout_pending(reinterpret_cast<const void*>(kern))) return;
   cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
-  done_dev[dev] = 1;
 }
 
 // Launch with optional programmatic dependent launch (PDL); returns FLINT_OK / FLINT_ERR_LAUNCH.
@@ -37,8 +42,7 @@ int launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, void* str
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 1 : 0;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
-  return e == cudaSuccess ? FLINT_OK : FLINT_ERR_LAUNCH;
+  return record_cuda(cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...), FLINT_ERR_LAUNCH);
 }
 
 // Launch with a thread-block cluster of `cluster` CTAs along x (grid.x must be a multiple), optional PDL.
@@ -60,8 +64,7 @@ int launch_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, v
   at[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 2 : 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
-  return e == cudaSuccess ? FLINT_OK : FLINT_ERR_LAUNCH;
+  return record_cuda(cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...), FLINT_ERR_LAUNCH);
 }
 
 }  // namespace flint

@@ -80,6 +80,25 @@ __device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* m
         "l"(l2_evict_first())
       : "memory");
 }
+// 3-D tensor tile load (x, y, z), streaming L2 policy.
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;"
+      ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)),
+        "l"(l2_evict_first())
+      : "memory");
+}
+// 5-D tensor tile load, streaming L2 policy.
+__device__ __forceinline__ void tma_load_5d(void* smem_dst, const CUtensorMap* map, int x, int y, int z, int w, int v,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7], %8;"
+      ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(v),
+        "r"(smem_u32(bar)), "l"(l2_evict_first())
+      : "memory");
+}
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -90,5 +109,11 @@ int encode_u8_2d(CUtensorMap* map, const void* base, uint64_t cols_bytes, uint64
 // bf16 4-D map (dims innermost first, strides in bytes for dims 1..3), 128-byte swizzle.
 int encode_bf16_4d(CUtensorMap* map, const void* base, const uint64_t dims[4], const uint64_t strides_bytes[3],
                    const uint32_t box[4]);
+// u8 3-D map (dims innermost first, strides in bytes for dims 1..2), optional 128-byte swizzle.
+int encode_u8_3d(CUtensorMap* map, const void* base, const uint64_t dims[3], const uint64_t strides_bytes[2],
+                 const uint32_t box[3], bool swizzle128);
+// bf16 5-D map (dims innermost first, strides in bytes for dims 1..4), 128-byte swizzle.
+int encode_bf16_5d(CUtensorMap* map, const void* base, const uint64_t dims[5], const uint64_t strides_bytes[4],
+                   const uint32_t box[5]);
 
 }  // namespace flint

@@ -89,6 +89,27 @@ class FastHead:
         torch.ops.flint_b200.lm_head_nv4(x, self.P, self.S, self.scale, out, tok, want_logits, True)
         return tok, (out if want_logits else None)
 
+    def sample(self, x, seeds, step=None, temperature: float = 1.0, top_k: int = 20, top_p: float = 0.95,
+               want_logits: bool = False, want_candidates: bool = False):
+        """Seeded temperature -> top-k -> top-p draw in the same pass over the head (the reference's defaults,
+        README.md:67: T 1.0, top-k 20, top-p 0.95).  seeds: int64 [M] on the device (one Philox key per stream);
+        step: int32 [1] device counter (None = 0).  Returns (token ids int32 [M], dict with ``logits`` and/or
+        ``cand_ids`` / ``cand_logits`` / ``kept`` when asked)."""
+        x = x.contiguous()
+        m, dev = x.shape[0], x.device
+        tok = torch.empty((m,), dtype=torch.int32, device=dev)
+        extra = {}
+        if want_logits:
+            extra["logits"] = torch.empty((m, self.V), dtype=torch.float32, device=dev)
+        if want_candidates:
+            extra["cand_ids"] = torch.empty((m, top_k), dtype=torch.int32, device=dev)
+            extra["cand_logits"] = torch.empty((m, top_k), dtype=torch.float32, device=dev)
+            extra["kept"] = torch.empty((m,), dtype=torch.int32, device=dev)
+        torch.ops.flint_b200.lm_head_sample(x, self.P, self.S, self.scale, float(temperature), int(top_k), float(top_p),
+                                            seeds, step, tok, extra.get("logits"), extra.get("cand_ids"),
+                                            extra.get("cand_logits"), extra.get("kept"))
+        return tok, extra
+
 
 # ---------------------------------------------------------------------------------------------------------
 # integration hook (reference: fast/fast_head.py:285-312,360-381)

@@ -1,0 +1,95 @@
+"""Per-kernel microbenchmark of the decode step (CUDA events on the launch stream, no profiler).
+
+    python flint-vllm-single-dgx-spark_b200/kernel_bench.py --kernel attention [--ctx 6057] [--layers 4] [--reps 5]
+        [--batch 1] [--moe chain|fused]
+
+A synthetic Flint-class model with --layers layers (a few GB on the device) is built, its KV cache filled with seeded
+N(0, 1) to --ctx tokens, and the chosen kernel is launched once per layer (each launch on that layer's weights / KV,
+so consecutive launches do not hit in L2 when the layers together exceed it) inside one CUDA graph replayed --reps
+times.  Prints one JSON line: microseconds per launch, algorithmic bytes per launch and GB/s.  Kernel names are
+those of Decoder.layer_ops (attn_block, or qkv / attention / o with --attn chain; route, up, down, or moe_fused with --moe fused)
+plus head and head_sample.  This is
+also the small case used for full ncu captures of one kernel.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _package():
+    if "flint_b200" in sys.modules:
+        return sys.modules["flint_b200"]
+    spec = importlib.util.spec_from_file_location("flint_b200", os.path.join(HERE, "__init__.py"),
+                                                  submodule_search_locations=[HERE])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["flint_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--kernel", required=True)
+    ap.add_argument("--ctx", type=int, default=6057)
+    ap.add_argument("--layers", type=int, default=4)
+    ap.add_argument("--reps", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--moe", default="chain", choices=["chain", "fused"])
+    ap.add_argument("--attn", default="block", choices=["block", "chain"])
+    args = ap.parse_args(argv)
+    _package()
+    from flint_b200.model import Decoder, FlintConfig, FlintModel
+
+    cfg = FlintConfig(layers=args.layers)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    model = FlintModel(cfg, dev, seed=5, max_ctx=args.ctx + 16, max_batch=args.batch)
+    dec = Decoder(model, batch=args.batch, moe=args.moe, attn=args.attn)
+    prompt = np.random.default_rng(3).integers(0, cfg.vocab, size=(args.batch, args.ctx))
+    dec.fill_kv_random(prompt)
+    dec.decode(1)                      # one real step so routing, q and activations hold live values
+    name = args.kernel
+    if name == "head":
+        fns = [dec.head_op()] * max(args.layers, 4)
+    elif name == "head_sample":
+        P, S, gs = model.head
+        seeds = torch.arange(1, args.batch + 1, dtype=torch.int64, device=dev)
+        ops = torch.ops.flint_b200
+        fns = [lambda: ops.lm_head_sample(dec.h, P, S, gs, 1.0, 20, 0.95, seeds, dec.step_ctr, dec.out_tok,
+                                          None, None, None, None, dec.res_b, model.final_norm, cfg.rms_eps)]
+        fns = fns * max(args.layers, 4)
+    else:
+        fns = [dict(dec.layer_ops(l))[name] for l in range(cfg.layers)]
+    for fn in fns:
+        fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for fn in fns:
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(args.reps):
+        g.replay()
+    e1.record(st)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (args.reps * len(fns))
+    nbytes = dec.algorithmic_bytes("head" if name.startswith("head") else name, args.ctx)
+    print(json.dumps({"kernel": name, "batch": args.batch, "ctx": args.ctx, "launches": args.reps * len(fns),
+                      "us_per_launch": round(us, 2), "bytes_per_launch": nbytes,
+                      "GBps": round(nbytes / us / 1e3, 1)}), flush=True)
+
+
+if __name__ == "__main__":
+    main()

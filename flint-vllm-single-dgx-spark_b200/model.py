@@ -3,9 +3,12 @@
 The layer structure follows the reference's fast decode path (fast/model.py: FlintDecoderLayer.forward 734-759,
 FlintAttention.forward_af 596-657, FlintSparseMoeBlock._forward_decode_rn 302-310, compute_logits 924-929):
 
-    layer l:  q, res = qkv_head(h, res)          add + RMSNorm + QKV + q/k norm + RoPE + KV write
-              a = o_gemv(decode_attention(q))
-              h, res = moe_fused(a, res)          add + RMSNorm + router + top-k + gate/up + SwiGLU + down + sum
+    layer l:  a, res = attn_block(h, res)        add + RMSNorm + QKV + q/k norm + RoPE + KV write + paged
+                                                  attention + O projection, one launch (or attn="chain":
+                                                  qkv_head, decode_attention, o_gemv)
+              xn, res, ids, w = moe_route(a, res)  add + RMSNorm + router + top-k (renormalised weights)
+              h = moe_down(moe_up(xn, ids), ids, w) gate/up + SwiGLU, then down + weighted expert sum
+              (or the single persistent moe_fused launch, moe="fused")
     head:     token = argmax(lm_head(final_norm(h + res)))
 
 with the BASELINE.json shapes (hidden 2048, 48 layers, 32/4 heads of 128, 128 experts top-8 softmax, I = 768,
@@ -116,8 +119,14 @@ class FlintModel:
 class Decoder:
     """Batch-M (M <= 8) decode of a FlintModel: teacher-forced prompt processing and greedy generation."""
 
-    def __init__(self, model: FlintModel, batch: int = 1):
-        self.m, self.c, self.M = model, model.cfg, batch
+    def __init__(self, model: FlintModel, batch: int = 1, moe: str = "chain", attn: str = "block"):
+        """moe: "chain" (route, up, down: three launches, the faster at batch 1) or "fused" (one persistent launch);
+        attn: "block" (QKV + attention + O in one persistent launch) or "chain" (three launches)."""
+        if moe not in ("chain", "fused"):
+            raise ValueError(f"moe must be 'chain' or 'fused', got {moe!r}")
+        if attn not in ("block", "chain"):
+            raise ValueError(f"attn must be 'block' or 'chain', got {attn!r}")
+        self.m, self.c, self.M, self.moe, self.attn_mode = model, model.cfg, batch, moe, attn
         c, M, dev = model.cfg, batch, model.dev
         assert 1 <= M <= min(8, model.max_batch)
         e = lambda *s, dt=torch.bfloat16: torch.empty(s, dtype=dt, device=dev)
@@ -141,35 +150,92 @@ class Decoder:
         self.splits = _ops.attention_splits(M, c.num_kv_heads)
         self.scale = c.head_dim ** -0.5
         self.graphs: dict[str, torch.cuda.CUDAGraph] = {}
-        self.launches_per_step = 4 * c.layers + 2      # qkv, attention, o, fused MoE per layer + head + advance
+        # (qkv, attention, o | attention block) + (route, up, down | fused MoE) per layer, then head + advance
+        self.launches_per_step = ((3 if attn == "chain" else 1) + (3 if moe == "chain" else 1)) * c.layers + 2
 
     # ---- one decode step as torch ops on persistent buffers ----
+    def layer_ops(self, l: int) -> list[tuple[str, callable]]:
+        """The launches of layer l in order, as (kernel name, zero-argument call) on the persistent buffers."""
+        c, m, ops, L = self.c, self.m, torch.ops.flint_b200, self.m.layers[l]
+        kv, kc, vc = m.kv_views(l)
+        P, S, gs = L["qkv"]
+        Po, So, gso = L["o"]
+        ew = L["experts"]
+        if l == 0:      # the embedding gather is fused into the first QKV kernel
+            qkv = lambda: ops.attn_qkv(m.embed, None, L["ln1"], c.rms_eps, P, S, gs, c.num_heads, c.num_kv_heads, True,
+                                       L["q_norm"], L["k_norm"], c.rms_eps, self.positions, m.cos_sin, kc, vc,
+                                       self.slots, self.q, self.qkv, self.res_a, True, self.tokens)
+        else:
+            qkv = lambda: ops.attn_qkv(self.h, self.res_b, L["ln1"], c.rms_eps, P, S, gs, c.num_heads, c.num_kv_heads,
+                                       True, L["q_norm"], L["k_norm"], c.rms_eps, self.positions, m.cos_sin, kc, vc,
+                                       self.slots, self.q, self.qkv, self.res_a, True, None)
+        if self.attn_mode == "block":
+            x_in, res_in, tok = (m.embed, None, self.tokens) if l == 0 else (self.h, self.res_b, None)
+            seq = [("attn_block", lambda: ops.attn_block(x_in, res_in, L["ln1"], c.rms_eps, P, S, gs, c.num_heads,
+                                                         c.num_kv_heads, L["q_norm"], L["k_norm"], c.rms_eps,
+                                                         self.positions, m.cos_sin, kv, self.bt, self.seq_lens,
+                                                         self.slots, None, 0, self.scale, Po, So, gso, self.a,
+                                                         self.res_a, None, None, tok))]
+        else:
+            seq = [("qkv", qkv),
+                   ("attention", lambda: ops.decode_attention(self.q.view(self.M, c.num_heads, c.head_dim), kv, self.bt,
+                                                              self.seq_lens, None, 0, self.scale, self.attn,
+                                                              self.splits)),
+                   ("o", lambda: ops.attn_o(self.attn.view(self.M, -1), Po, So, gso, self.a))]
+        if self.moe == "fused":
+            seq.append(("moe_fused", lambda: ops.moe_fused(self.a, self.res_a, L["ln2"], c.rms_eps, L["gate"], c.topk,
+                                                           ew.score_fn, ew.w13, ew.s13, ew.g13, ew.w2, ew.s2, ew.g2,
+                                                           self.h, self.res_b, self.xn, self.lg, self.ti, self.tw,
+                                                           False)))
+        else:
+            seq += [("route", lambda: ops.moe_route(self.a, self.res_a, L["ln2"], c.rms_eps, L["gate"], c.topk,
+                                                    ew.score_fn, self.lg, self.ti, self.tw, self.xn, self.res_b, True,
+                                                    True)),
+                    ("up", lambda: ops.moe_up(self.xn, self.ti, ew.w13, ew.s13, ew.g13, self.act)),
+                    ("down", lambda: ops.moe_down(self.act, self.ti, self.tw, ew.w2, ew.s2, ew.g2, self.h))]
+        return seq
+
     def _layers(self):
-        c, m, ops = self.c, self.m, torch.ops.flint_b200
-        for l, L in enumerate(m.layers):
-            kv, kc, vc = m.kv_views(l)
-            P, S, gs = L["qkv"]
-            if l == 0:
-                ops.attn_qkv(m.embed, None, L["ln1"], c.rms_eps, P, S, gs, c.num_heads, c.num_kv_heads, True,
-                             L["q_norm"], L["k_norm"], c.rms_eps, self.positions, m.cos_sin, kc, vc, self.slots, self.q,
-                             self.qkv, self.res_a, True, self.tokens)
-            else:
-                ops.attn_qkv(self.h, self.res_b, L["ln1"], c.rms_eps, P, S, gs, c.num_heads, c.num_kv_heads, True,
-                             L["q_norm"], L["k_norm"], c.rms_eps, self.positions, m.cos_sin, kc, vc, self.slots, self.q,
-                             self.qkv, self.res_a, True, None)
-            ops.decode_attention(self.q.view(self.M, c.num_heads, c.head_dim), kv, self.bt, self.seq_lens, None, 0,
-                                 self.scale, self.attn, self.splits)
-            Po, So, gso = L["o"]
-            ops.attn_o(self.attn.view(self.M, -1), Po, So, gso, self.a)
-            ew = L["experts"]
-            ops.moe_fused(self.a, self.res_a, L["ln2"], c.rms_eps, L["gate"], c.topk, ew.score_fn, ew.w13, ew.s13, ew.g13,
-                          ew.w2, ew.s2, ew.g2, self.h, self.res_b, self.xn, self.lg, self.ti, self.tw, False)
+        for l in range(self.c.layers):
+            for _, fn in self.layer_ops(l):
+                fn()
+
+    def head_op(self):
+        P, S, gs = self.m.head
+        return lambda: torch.ops.flint_b200.lm_head_nv4(self.h, P, S, gs, self.dummy_f, self.out_tok, False, True,
+                                                        self.res_b, self.m.final_norm, self.c.rms_eps)
+
+    def algorithmic_bytes(self, name: str, ctx: int) -> int:
+        """Bytes one launch of kernel `name` must move at batch M and context ctx (weights / KV read once,
+        activations in and out): the roofline numerator."""
+        c, M = self.c, self.M
+        nv = lambda n, k: n * k // 2 + n * k // 16
+        H, D = c.hidden, c.head_dim
+        if name == "qkv":
+            return nv(c.qkv_rows, H) + M * (3 * H * 2 + c.qkv_rows * 2 + c.num_heads * D * 2 + 2 * c.num_kv_heads * D * 2)
+        if name == "attention":
+            return M * (ctx * c.num_kv_heads * 2 * D * 2 + 2 * c.num_heads * D * 2)
+        if name == "o":
+            return nv(H, c.num_heads * D) + M * (c.num_heads * D * 2 + H * 2)
+        if name == "route":
+            return c.num_experts * H * 2 + M * (4 * H * 2 + c.num_experts * 4 + c.topk * 8)
+        if name == "up":
+            return M * c.topk * (nv(2 * c.moe_inter, H) + c.moe_inter * 2) + M * H * 2
+        if name == "down":
+            return M * c.topk * (nv(H, c.moe_inter) + c.moe_inter * 2) + M * H * 2
+        if name == "attn_block":
+            return (self.algorithmic_bytes("qkv", ctx) + self.algorithmic_bytes("attention", ctx)
+                    + self.algorithmic_bytes("o", ctx))
+        if name == "moe_fused":
+            return (self.algorithmic_bytes("route", ctx) + self.algorithmic_bytes("up", ctx)
+                    + self.algorithmic_bytes("down", ctx))
+        if name == "head":
+            return nv(c.vocab, H) + M * 2 * H * 2
+        raise KeyError(name)
 
     def _head_and_advance(self):
-        P, S, gs = self.m.head
         ops = torch.ops.flint_b200
-        ops.lm_head_nv4(self.h, P, S, gs, self.dummy_f, self.out_tok, False, True, self.res_b, self.m.final_norm,
-                        self.c.rms_eps)
+        self.head_op()()
         ops.decode_advance(self.out_tok, self.positions, self.seq_lens, self.slots, self.bt, PAGE, self.history,
                            self.step_ctr, self.tokens)
 
@@ -216,6 +282,20 @@ class Decoder:
         for t in range(T - 1):
             self._set_state(prompts[:, t], np.full(self.M, t))
             g.replay()
+        self._set_state(prompts[:, T - 1], np.full(self.M, T - 1))
+        self.step_ctr.zero_()
+        torch.cuda.synchronize()
+
+    def fill_kv_random(self, prompts: np.ndarray, seed: int = 0):
+        """Stand-in for prefill when only the decode steps matter (profiling runs): every layer's KV cache is filled
+        with seeded N(0, 1) bf16 and the state is left at the last prompt token, as after prefill()."""
+        if not self.graphs:
+            self.capture()
+        g = torch.Generator(device=self.m.dev)
+        g.manual_seed(seed)
+        for kv in self.m.kv:
+            kv.copy_(torch.randn(kv.shape, generator=g, device=self.m.dev).to(torch.bfloat16))
+        T = prompts.shape[1]
         self._set_state(prompts[:, T - 1], np.full(self.M, T - 1))
         self.step_ctr.zero_()
         torch.cuda.synchronize()

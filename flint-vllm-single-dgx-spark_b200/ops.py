@@ -64,6 +64,50 @@ def _(x, P, S, gs, logits, tokens, write_logits, write_tokens, res=None, norm_w=
     return None
 
 
+@torch.library.custom_op(f"{NS}::lm_head_sample", mutates_args=("tokens", "logits", "cand_ids", "cand_logits", "kept"))
+def lm_head_sample(x: torch.Tensor, P: torch.Tensor, S: torch.Tensor, gs: float, temperature: float, top_k: int,
+                   top_p: float, seeds: torch.Tensor, step: torch.Tensor | None, tokens: torch.Tensor,
+                   logits: torch.Tensor | None, cand_ids: torch.Tensor | None, cand_logits: torch.Tensor | None,
+                   kept: torch.Tensor | None, res: torch.Tensor | None = None, norm_w: torch.Tensor | None = None,
+                   eps: float = 0.0) -> None:
+    """Seeded temperature -> top-k -> top-p draw fused into the NVFP4 head (rule: include/flint_b200.h,
+    flint_lm_head_nv4_sample).  seeds: int64 [M] (the bits are the Philox key); step: int32 [1] device counter.
+    The optional outputs (logits, cand_ids, cand_logits, kept) are positional without defaults: torch drops trailing
+    arguments equal to their defaults when it boxes a call, which would hide a mutated argument."""
+    _lib.require_cuda(x, "lm_head_sample")
+    V, K = _check_nvfp4(P, S, "lm_head_sample")
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != K or x.stride(1) != 1:
+        raise _lib.FlintError(f"lm_head_sample: x must be bf16 [M, {K}] with unit inner stride")
+    M = x.shape[0]
+    if seeds.dtype != torch.int64 or seeds.numel() < M or not seeds.is_contiguous():
+        raise _lib.FlintError("lm_head_sample: seeds must be contiguous int64 [M]")
+    if step is not None and step.dtype != torch.int32:
+        raise _lib.FlintError("lm_head_sample: step must be an int32 device counter")
+    if tokens.dtype != torch.int32 or tokens.numel() < M:
+        raise _lib.FlintError("lm_head_sample: tokens must be int32 [M]")
+    if logits is not None and (logits.dtype != torch.float32 or logits.shape[0] < M or logits.shape[1] < V
+                               or logits.stride(1) != 1):
+        raise _lib.FlintError("lm_head_sample: logits must be fp32 [M, V]")
+    for t, dt, what in ((cand_ids, torch.int32, "cand_ids"), (cand_logits, torch.float32, "cand_logits")):
+        if t is not None and (t.dtype != dt or t.numel() < M * top_k or not t.is_contiguous()):
+            raise _lib.FlintError(f"lm_head_sample: {what} must be contiguous {dt} [M, top_k]")
+    if kept is not None and (kept.dtype != torch.int32 or kept.numel() < M):
+        raise _lib.FlintError("lm_head_sample: kept must be int32 [M]")
+    nbytes = lib().flint_lm_head_sample_workspace_bytes(M, V)
+    ws = _lib.workspace(x.device, f"lm_head_sample_{M}_{V}", nbytes)
+    rc = lib().flint_lm_head_nv4_sample(
+        ptr(x), x.stride(0), ptr(res), ptr(norm_w), float(eps), M, ptr(_u8(P)), ptr(_u8(S)), float(gs), V, K, ptr(logits),
+        logits.stride(0) if logits is not None else 0, float(temperature), int(top_k), float(top_p), ptr(seeds), ptr(step),
+        ptr(tokens), ptr(cand_ids), ptr(cand_logits), ptr(kept), ptr(ws), PDL, stream_ptr(x.device))
+    check(rc, "flint_lm_head_nv4_sample")
+
+
+@lm_head_sample.register_fake
+def _(x, P, S, gs, temperature, top_k, top_p, seeds, step, tokens, logits, cand_ids, cand_logits, kept, res=None,
+      norm_w=None, eps=0.0):
+    return None
+
+
 # ------------------------------------------------------------------------------------------------------------
 # (1) MoE decode and (2) deterministic align
 # ------------------------------------------------------------------------------------------------------------
@@ -250,6 +294,54 @@ def attn_o(a: torch.Tensor, W: torch.Tensor, S: torch.Tensor, gs: torch.Tensor, 
 
 @attn_o.register_fake
 def _(a, W, S, gs, y):
+    return None
+
+
+@torch.library.custom_op(f"{NS}::attn_block", mutates_args=("kv_cache", "out", "res_out", "q_out", "attn_out"))
+def attn_block(x: torch.Tensor, res: torch.Tensor | None, norm_w: torch.Tensor, eps: float, W: torch.Tensor,
+               S: torch.Tensor, gs: torch.Tensor, num_q_heads: int, num_kv_heads: int, q_norm_w: torch.Tensor,
+               k_norm_w: torch.Tensor, eps_head: float, positions: torch.Tensor, cos_sin: torch.Tensor | None,
+               kv_cache: torch.Tensor, block_tables: torch.Tensor, seq_lens: torch.Tensor, slots: torch.Tensor,
+               sinks: torch.Tensor | None, window: int, scale: float, Wo: torch.Tensor, So: torch.Tensor,
+               gs_o: torch.Tensor, out: torch.Tensor, res_out: torch.Tensor, q_out: torch.Tensor | None,
+               attn_out: torch.Tensor | None, tokens: torch.Tensor | None = None) -> None:
+    """The fused decode attention block (one launch): add + RMSNorm, QKV, q/k norm + RoPE + KV write, paged attention,
+    O projection.  With tokens (int32 [M]) x is the embedding table.  q_out / attn_out: optional outputs (positional,
+    no defaults, so that torch never drops them when it boxes the call)."""
+    _lib.require_cuda(x, "attn_block")
+    _bf16_2d(x, "attn_block x")
+    N, K = _check_nvfp4(W, S, "attn_block qkv")
+    No, Ko = _check_nvfp4(Wo, So, "attn_block o")
+    M = x.shape[0] if tokens is None else tokens.numel()
+    H = x.shape[1]
+    if H != K or Ko != num_q_heads * 128 or N != (num_q_heads + 2 * num_kv_heads) * 128:
+        raise _lib.FlintError("attn_block: weight shapes do not match the head layout")
+    if out.shape != (M, No) or res_out.shape != (M, H) or out.stride() != res_out.stride():
+        raise _lib.FlintError("attn_block: out / res_out must be [M, N_o] / [M, H] with equal strides")
+    if res is not None and (res.shape != (M, H) or res.stride() != out.stride()):
+        raise _lib.FlintError("attn_block: res must be [M, H] with the stride of out")
+    nblk, hkv, page, d2 = kv_cache.shape
+    if hkv != num_kv_heads or page != 16 or d2 != 256 or kv_cache.stride(3) != 1 or kv_cache.stride(2) != 256:
+        raise _lib.FlintError("attn_block: kv_cache must be HND bf16 [blocks, kv_heads, 16, 256]")
+    if block_tables.dtype != torch.int32 or seq_lens.dtype != torch.int32 or positions.dtype != torch.int64 \
+            or slots.dtype != torch.int64:
+        raise _lib.FlintError("attn_block: block_tables / seq_lens int32, positions / slots int64")
+    nbytes = lib().flint_attn_block_workspace_bytes(N, Ko)
+    ws = _lib.workspace(x.device, f"attn_block_{N}_{Ko}", nbytes)
+    rc = lib().flint_attn_block(
+        ptr(x), x.stride(0), ptr(tokens), ptr(res), out.stride(0), ptr(norm_w), float(eps), M, H, ptr(_u8(W)), ptr(_u8(S)),
+        ptr(gs), num_q_heads, num_kv_heads, ptr(q_norm_w), ptr(k_norm_w), float(eps_head), ptr(positions), ptr(cos_sin),
+        cos_sin.stride(0) if cos_sin is not None else 0, ptr(kv_cache), nblk, kv_cache.stride(0), kv_cache.stride(1),
+        ptr(block_tables), block_tables.stride(0), block_tables.shape[1], ptr(seq_lens), ptr(slots), ptr(sinks),
+        int(window), float(scale), ptr(_u8(Wo)), ptr(_u8(So)), ptr(gs_o), No, ptr(out), ptr(res_out), ptr(q_out),
+        ptr(attn_out), ptr(ws), PDL, stream_ptr(x.device))
+    check(rc, "flint_attn_block")
+
+
+@attn_block.register_fake
+def _(x, res, norm_w, eps, W, S, gs, num_q_heads, num_kv_heads, q_norm_w, k_norm_w, eps_head, positions, cos_sin,
+      kv_cache, block_tables, seq_lens, slots, sinks, window, scale, Wo, So, gs_o, out, res_out, q_out, attn_out,
+      tokens=None):
     return None
 
 

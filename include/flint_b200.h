@@ -41,6 +41,9 @@ enum {
 int flint_version(void);
 /* Human-readable name of an error code. */
 const char* flint_error_string(int code);
+/* "cudaErrorName: description" of the last CUDA runtime call of this library that failed on the calling host thread
+ * (the detail behind FLINT_ERR_LAUNCH / FLINT_ERR_DEVICE), or "" if none has. */
+const char* flint_last_cuda_error(void);
 
 /* ------------------------------------------------------------------------------------------------
  * (4) NVFP4 LM head.
@@ -62,6 +65,28 @@ int flint_lm_head_nv4(const void* x, int64_t ldx, int64_t M, const void* P, cons
 /* Same, with the model's final (residual add +) RMSNorm fused in front: x <- bf16((x + res) *
  * rsqrt(mean((x + res)^2) + eps) * norm_w) (res may be NULL; norm_w NULL = flint_lm_head_nv4).  The
  * reference applies model.norm before compute_logits (fast/model.py:831,924-929). */
+int flint_lm_head_nv4_fused(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, int64_t M,
+                            const void* P, const void* S, float gs, int64_t V, int64_t K, float* logits,
+                            int64_t ld_logits, int32_t* token_ids, void* workspace, int pdl, void* stream);
+/* Sampled decoding in the same pass (replaces vLLM's temperature -> top-k -> top-p -> draw that follows the
+ * reference's compute_logits, fast/fast_head.py:360-381; the reference's draw is not reproducible, so the rule is
+ * this library's own and seeded):
+ *   candidates c_0 >= ... >= c_{k-1}: the top_k logits (ties -> lowest id), 1 <= top_k <= 32;
+ *   w_i = expf((c_i - c_0) / temperature);  S_j = w_{k-1} + ... + w_j;  candidate j >= 1 survives top-p iff
+ *   S_j > (1 - top_p) * S_0 (vLLM's rule: drop while the ascending cumulative probability is <= 1 - top_p);
+ *   u = Philox4x32-10(counter {*step, m, 0, 0}, key seeds[m]).x >> 8, times 2^-24;
+ *   token_ids[m] = id of the first kept i with w_0 + ... + w_i > u * (sum of the kept w).
+ * temperature > 0 (greedy callers use flint_lm_head_nv4_fused); 0 < top_p <= 1.  seeds: uint64 [M] (device);
+ * step: int32 device counter read at launch (NULL = 0), so a captured graph draws afresh after the counter moves.
+ * logits: fp32 [M, V] output or NULL (then kept in the workspace).  cand_ids / cand_logits: optional [M, top_k]
+ * outputs of the sorted candidates; kept: optional [M] count after top-p.
+ * workspace: flint_lm_head_sample_workspace_bytes(M, V), 256-byte aligned, zeroed once. */
+int64_t flint_lm_head_sample_workspace_bytes(int64_t M, int64_t V);
+int flint_lm_head_nv4_sample(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, int64_t M,
+                             const void* P, const void* S, float gs, int64_t V, int64_t K, float* logits,
+                             int64_t ld_logits, float temperature, int64_t top_k, float top_p, const uint64_t* seeds,
+                             const int32_t* step, int32_t* token_ids, int32_t* cand_ids, float* cand_logits,
+                             int32_t* kept, void* workspace, int pdl, void* stream);
 /* Allocation-free flint_lm_head_nv4 (no counterpart in the reference: the recipe always runs inside vLLM, which
  * allocates).  For callers that cannot allocate device memory at call time -- an engine that has already given all
  * free HBM to its KV-cache pool, a CUDA-graph capture region, a host runtime that only reaches the library through
@@ -71,9 +96,6 @@ int flint_lm_head_nv4(const void* x, int64_t ldx, int64_t M, const void* P, cons
  * on a device resolves the scratch address (cudaGetSymbolAddress), so make it before any stream capture. */
 int flint_lm_head_nv4_noalloc(const void* x, int64_t ldx, int64_t M, const void* P, const void* S, float gs, int64_t V,
                               int64_t K, float* logits, int64_t ld_logits, int32_t* token_ids, int pdl, void* stream);
-int flint_lm_head_nv4_fused(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, int64_t M,
-                            const void* P, const void* S, float gs, int64_t V, int64_t K, float* logits,
-                            int64_t ld_logits, int32_t* token_ids, void* workspace, int pdl, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
  * (1) MoE decode, 1..8 tokens.  Replaces fast/fp4moe_mar.cu (route_kernel 243-303, route_norm_kernel
@@ -164,6 +186,29 @@ int flint_attn_qkv(const void* x, int64_t ldx, const int32_t* tokens, const void
  * K % 1024 == 0, N % 64 == 0. */
 int flint_attn_o(const void* a, int64_t lda, int64_t M, const void* W, const void* S, const float* gs, int64_t N, int64_t K,
                  void* y, void* workspace, int pdl, void* stream);
+
+/* The whole decode attention block in ONE cooperative launch (fuses flint_attn_qkv in head mode, the paged decode
+ * attention and flint_attn_o; replaces fast/attn_gemv2.cu qkv_head_kernel 170-265 + o_gemv_kernel 268-289 and the PR
+ * decode attention patch:1741-2415 with the same rounding points):
+ *   s = x + res (res NULL: s = x; tokens non-NULL: row m of x is x[tokens[m]], an embedding gather), res_out = bf16(s),
+ *   y = bf16(gs_qkv * rmsnorm(s) . Wqkv^T), q / k heads RMSNorm'd (q_norm_w / k_norm_w, eps_head) and NeoX-roped
+ *   (cos_sin [max_pos, 128] at positions; NULL: no RoPE), the new k / v written to kv_cache at slots[m] (< 0: skip),
+ *   paged GQA attention over seq_lens[m] tokens (block_tables, sinks, sliding window, scale), then
+ *   out = bf16(gs_o * attn . Wo^T).
+ * kv_cache: HND bf16 [num_blocks, num_kv_heads, 16, 256] (K | V), strides in elements; head dim 128; the page of the
+ * current token is patched in shared memory, so attention sees the new k / v exactly as if read back from the cache.
+ * res / res_out / out rows are ldr elements apart.  q_out bf16 [M, nq*128] and attn_out bf16 [M, nq*128] are optional
+ * outputs.  M <= 8, num_q_heads / num_kv_heads <= 8, H % 256 == 0, n_o % 16 == 0.  workspace:
+ * flint_attn_block_workspace_bytes(n_qkv, nq*128), zero-filled once, 256-byte aligned (self-resetting). */
+int64_t flint_attn_block_workspace_bytes(int64_t n_qkv, int64_t k_o);
+int flint_attn_block(const void* x, int64_t ldx, const int32_t* tokens, const void* res, int64_t ldr, const void* norm_w,
+                     float eps, int64_t M, int64_t H, const void* Wqkv, const void* Sqkv, const float* gs_qkv,
+                     int64_t num_q_heads, int64_t num_kv_heads, const void* q_norm_w, const void* k_norm_w, float eps_head,
+                     const int64_t* positions, const float* cos_sin, int64_t cs_stride, void* kv_cache, int64_t num_blocks,
+                     int64_t stride_block, int64_t stride_head, const int32_t* block_tables, int64_t bt_stride,
+                     int64_t max_blocks, const int32_t* seq_lens, const int64_t* slots, const float* sinks, int64_t window,
+                     float scale, const void* Wo, const void* So, const float* gs_o, int64_t n_o, void* out, void* res_out,
+                     void* q_out, void* attn_out, void* workspace, int pdl, void* stream);
 
 /* Paged decode attention with optional sinks and sliding window, one query token per request:
  * q bf16 [batch, num_q_heads, 128] (request stride q_stride_b elements); kv_cache bf16 HND

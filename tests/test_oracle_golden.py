@@ -62,3 +62,34 @@ def test_e4m3_table_roundtrip():
     # +0 / -0 both map to a zero code
     ok = (back == bits) | ((vals == 0) & ((back & 0x7F) == 0))
     assert ok.all()
+
+
+def test_philox_known_answers():
+    """Philox4x32-10 against the published Random123 known-answer vectors (kat_vectors, philox4x32 10)."""
+    from oracle import sampling as osamp
+    M = 0xFFFFFFFF
+    cases = [([0, 0, 0, 0], [0, 0], [0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8]),
+             ([M, M, M, M], [M, M], [0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD]),
+             ([0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344], [0xA4093822, 0x299F31D0],
+              [0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1])]
+    for ctr, key, want in cases:
+        assert osamp.philox4x32_10(ctr, key) == want
+
+
+def test_sampling_rule_host():
+    """Top-p keeps vLLM's prefix; k = 1 and tiny top-p are greedy; ties keep the lowest ids."""
+    from oracle import sampling as osamp
+    logits = np.array([0.0, 2.0, 1.0, 2.0, -1.0, 1.5], np.float32)
+    np.testing.assert_array_equal(osamp.topk_ids(logits, 4), [1, 3, 5, 2])
+    for step in range(20):
+        assert osamp.sample_row(logits, 1, 1.0, 0.95, 5, step, 0)["token"] == 1
+        assert osamp.sample_row(logits, 6, 1.0, 1e-6, 5, step, 0)["token"] == 1
+    r = osamp.sample_row(logits, 6, 1.0, 1.0, 5, 0, 0)
+    assert r["kept"] == 6
+    # vLLM: sort ascending, drop while the cumulative probability <= 1 - p (p = 0.5 keeps the two tied best)
+    r = osamp.sample_row(logits, 6, 1.0, 0.5, 5, 0, 0)
+    w = np.exp(np.sort(logits)[::-1] - 2.0)
+    asc = np.cumsum(np.sort(w / w.sum()))
+    assert r["kept"] == int((asc > 0.5).sum())
+    us = [float(osamp.uniform(99, s, 3)) for s in range(2000)]
+    assert 0.0 <= min(us) and max(us) < 1.0 and abs(np.mean(us) - 0.5) < 0.03
