@@ -286,7 +286,8 @@ def main():
     ap.add_argument("--cpu-sample-tokens", type=int, default=2)
     ap.add_argument("--prompt", type=int, default=PROMPT_LEN, help="prompt tokens before the timed decode")
     ap.add_argument("--attn", default="block", choices=["block", "chain"], help="attention block: one launch or three")
-    ap.add_argument("--moe", default="chain", choices=["chain", "fused"], help="MoE: three launches or one")
+    ap.add_argument("--moe", default=None, choices=["block", "chain", "fused"],
+                    help="MoE: one launch for one token, three launches, or one launch for 1..8 tokens")
     ap.add_argument("--prefill", default="teacher", choices=["teacher", "kv"],
                     help="teacher: prompt run through the decode kernels; kv: KV cache filled with seeded N(0,1) "
                          "(profiling runs)")

@@ -482,6 +482,64 @@ __device__ __forceinline__ void norm_stage_f16_1(const bf16* x, int64_t ldx, con
   norm_stage_f16_1w(x, ldx, rows, res, ldr, wc, eps, M, H, xs, shift, red, res_out, nthreads, bar);
 }
 
+// add_rmsnorm_2pass with ONE global pass, for H / 8 <= nthreads (one 8-wide chunk per thread and row, kept in
+// registers): the same per-thread chains, butterfly and warp order, so xn has the same bits.  xn: bf16 [M][H] in
+// shared memory; res_out / xn_out: optional global copies (rows H apart).  red: >= (nthreads/32) * 8 floats.
+__device__ __forceinline__ void add_rmsnorm_1pass(const bf16* x, int64_t ldx, const bf16* res, const bf16* __restrict__ w,
+                                                  float eps, int M, int H, bf16* xn, bf16* res_out, bf16* xn_out,
+                                                  float* red, int nthreads, int bar) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = nthreads >> 5, H8 = H >> 3;
+  auto sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthreads) : "memory"); };
+  const bool own = tid < H8;
+  float a[8][8], ss[8];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    ss[m] = 0.f;
+    if (m < M && own) {
+      bf16x8_to_f32(reinterpret_cast<const uint4*>(x + m * ldx)[tid], a[m]);
+      if (res) {
+        float b[8];
+        bf16x8_to_f32(reinterpret_cast<const uint4*>(res + m * ldx)[tid], b);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a[m][j] += b[j];
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss[m] = fmaf(a[m][j], a[m][j], ss[m]);
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    float v = ss[m];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[warp * 8 + m] = v;
+  }
+  sync();
+  float wf[8];
+  if (own) bf16x8_to_f32(reinterpret_cast<const uint4*>(w)[tid], wf);
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    if (m < M && own) {
+      float tot = 0.f;
+      for (int ww = 0; ww < nw; ++ww) tot += red[ww * 8 + m];
+      const float rs = rsqrtf(tot / (float)H + eps);
+      uint32_t pk[4], pr[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __nv_bfloat162 n2 = __floats2bfloat162_rn(a[m][2 * j] * rs * wf[2 * j], a[m][2 * j + 1] * rs * wf[2 * j + 1]);
+        pk[j] = *reinterpret_cast<uint32_t*>(&n2);
+        __nv_bfloat162 r2 = __floats2bfloat162_rn(a[m][2 * j], a[m][2 * j + 1]);
+        pr[j] = *reinterpret_cast<uint32_t*>(&r2);
+      }
+      const uint4 nv = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      reinterpret_cast<uint4*>(xn + m * H)[tid] = nv;
+      if (xn_out) reinterpret_cast<uint4*>(xn_out + (int64_t)m * H)[tid] = nv;
+      if (res_out) reinterpret_cast<uint4*>(res_out + (int64_t)m * H)[tid] = make_uint4(pr[0], pr[1], pr[2], pr[3]);
+    }
+  }
+  sync();
+}
+
 // Whole-block variant (the LM head): all threads, __syncthreads.
 __device__ __forceinline__ void stage_x_f16(const bf16* __restrict__ x, int64_t ldx, int M, int K, __half* xs,
                                             int* shift, float* red) {

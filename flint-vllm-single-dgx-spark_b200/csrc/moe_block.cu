@@ -1,0 +1,346 @@
+// (1) MoE decode block for one token: router + top-k, NVFP4 gate/up GEMV + SwiGLU, NVFP4 down GEMV and the
+// weighted expert sum in ONE cooperative launch (one CTA per SM, two grid barriers).  Replaces the reference's
+// route_norm_kernel -> up_mar -> down_mar chain (fast/fp4moe_mar.cu:311-417, 67-152, 157-233; driven by
+// fast/model.py:302-310) at batch 1, where every routed expert is distinct (topk <= 8).
+//
+//  R  every CTA: s = x + res, xn = bf16(RMSNorm(s)) in one register pass (CTA 0 publishes res_out / xn); CTAs own
+//     router rows e = cta, cta + grid (prefetched into registers before the PDL wait) and write bf16 logits.
+//                                                                                            -- grid barrier --
+//  U  every CTA: top-k from the logits (redundant, identical everywhere).  The TMA producer then loads, in one go,
+//     the CTA's share of the up work (units of 16 gate + 16 up rows x H, balanced over the CTAs) and its down block
+//     (16 output rows of every routed expert) into shared memory; the down weights land while the up units run.
+//     Per unit the 8 warps split K, the partial tiles are summed in warp order and act = bf16(silu(g) * u) is
+//     written to the workspace.                                                               -- grid barrier --
+//  D  CTA c < H/16: warp s computes y_s = bf16(act_s . W2[e_s] * gs2[e_s]) for the block's 16 rows (one 16-row
+//     tile over all of I, the accumulation order of moe_down), then out = bf16(sum_s tw_s * y_s) in slot order.
+//
+// Routing, xn, res_out and the down step have the bits of flint_moe_route / flint_moe_down; the gate/up sums split
+// K across warps, so act (and hence out) agrees with the chain to fp32 rounding, not bit for bit.
+#include "gridsync.cuh"
+#include "moe_common.cuh"
+#include "runtime.cuh"
+
+#include <algorithm>
+
+namespace flint {
+
+constexpr int kXW = 8;                  // consumer warps
+constexpr int kXT = kXW * 32;
+constexpr int kXMaxUnits = 3;           // up units (16 gate + 16 up rows) per CTA
+constexpr int kXMaxSlots = 8;           // routed experts
+
+struct MoeBlockWs {
+  GridSync sync;
+  unsigned status;
+  unsigned pad[31];
+  // followed by: logits fp32 [E], act bf16 [8][I]
+};
+
+struct MoeBlockArgs {
+  const bf16* x;
+  int64_t ldx;
+  const bf16* res;
+  const bf16* nw;
+  float eps;
+  const bf16* gate_w;
+  int E, topk, score_fn, H, I;
+  const float* g13;
+  const float* g2;
+  bf16* out;
+  bf16* res_out;
+  bf16* xn_out;
+  float* logits_out;
+  int* ids_out;
+  float* tw_out;
+  uint32_t unit_bytes, dslot_bytes, off_dn, off_xn, off_xs, off_xa, off_red;
+  MoeBlockWs* ws;
+};
+
+static size_t moe_block_ws_bytes(int E, int I) {
+  return sizeof(MoeBlockWs) + (size_t)E * 4 + (size_t)kXMaxSlots * I * 2 + 256;
+}
+
+__device__ __forceinline__ void xsync() { asm volatile("bar.sync 1, %0;" ::"r"(kXT) : "memory"); }
+__device__ __forceinline__ bool xsync_and(bool pred) {
+  int r;
+  asm volatile("{\n.reg .pred p, q;\nsetp.ne.s32 p, %1, 0;\nbar.red.and.pred q, 1, %2, p;\nselp.s32 %0, 1, 0, q;\n}"
+               : "=r"(r) : "r"((int)pred), "r"(kXT) : "memory");
+  return r != 0;
+}
+
+template <int NV>   // H / 256
+__global__ void __launch_bounds__((kXW + 1) * 32, 1)
+moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant__ CUtensorMap up_s,
+                 const __grid_constant__ CUtensorMap dn_c, const __grid_constant__ CUtensorMap dn_s, const MoeBlockArgs a) {
+  constexpr int H = NV * 256;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t bar_up[kXMaxUnits], bar_dn, bar_plan;
+  __shared__ int s_ids[kXMaxSlots];
+  __shared__ float s_tw[kXMaxSlots];
+  __shared__ int shift_x[kMaxTokens], shift_a[kXMaxSlots];
+  __shared__ float red_n[kXW * 8 + 8];
+  __shared__ float ybuf[kXMaxSlots][16];
+  __shared__ int s_ok;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nb = gridDim.x, cta = blockIdx.x;
+  const int E = a.E, I = a.I, topk = a.topk;
+  const int nks_u = H / kSliceK, nks_d = I / kSliceK, jpe = I / 16;
+  const int U = topk * jpe;
+  const int u0 = (int)((int64_t)cta * U / nb), nu = (int)((int64_t)(cta + 1) * U / nb) - u0;
+  const bool has_dn = cta < H / 16;
+  MoeBlockWs* ws = a.ws;
+  unsigned* status = &ws->status;
+  float* lg = reinterpret_cast<float*>(ws + 1);
+  bf16* act_g = reinterpret_cast<bf16*>(lg + E);
+  uint8_t* up_base = smem;                              // [unit][gate codes | up codes | gate scales | up scales]
+  uint8_t* dn_base = smem + a.off_dn;                   // [slot][codes | scales]
+  bf16* xnb = reinterpret_cast<bf16*>(smem + a.off_xn);
+  __half* xs = reinterpret_cast<__half*>(smem + a.off_xs);
+  __half* xa = reinterpret_cast<__half*>(smem + a.off_xa);
+  float* red = reinterpret_cast<float*>(smem + a.off_red);   // [2][8 warps][16 rows][8 cols]
+
+  if (tid == 0) {
+    for (int i = 0; i < kXMaxUnits; ++i) mbar_init(&bar_up[i], 1);
+    mbar_init(&bar_dn, 1);
+    mbar_init(&bar_plan, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  // router rows of this CTA: e = cta (+ nb), one warp each, prefetched before the wait
+  const int my_row = cta + warp * nb;
+  const bool has_row = warp < 2 && my_row < E;
+  uint4 wv[NV];
+  if (has_row) {
+    const uint4* wp = reinterpret_cast<const uint4*>(a.gate_w + (int64_t)my_row * H);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) wv[i] = ldg_stream_v4(wp + lane + 32 * i);
+  }
+  pdl_wait();
+
+  if (warp == kXW) {
+    // ---- producer: once the routing is known, this CTA's up units and down block ----
+    if (lane == 0) {
+      tma_prefetch_desc(&up_c);
+      tma_prefetch_desc(&up_s);
+      tma_prefetch_desc(&dn_c);
+      tma_prefetch_desc(&dn_s);
+      if (!mbar_wait(&bar_plan, 0, status)) return;
+      for (int u = 0; u < nu; ++u) {
+        const int unit = u0 + u, s = unit / jpe, j = unit - s * jpe;
+        const int rows_g = s_ids[s] * 2 * I + j * 16, rows_u = rows_g + I;
+        uint8_t* b = up_base + u * a.unit_bytes;
+        mbar_arrive_expect_tx(&bar_up[u], 2 * nks_u * (2048 + 256));
+        tma_load_3d(b, &up_c, 0, rows_g, 0, &bar_up[u]);
+        tma_load_3d(b + nks_u * 2048, &up_c, 0, rows_u, 0, &bar_up[u]);
+        tma_load_3d(b + 2 * nks_u * 2048, &up_s, 0, rows_g, 0, &bar_up[u]);
+        tma_load_3d(b + 2 * nks_u * 2048 + nks_u * 256, &up_s, 0, rows_u, 0, &bar_up[u]);
+      }
+      if (has_dn) {
+        mbar_arrive_expect_tx(&bar_dn, topk * nks_d * (2048 + 256));
+        for (int s = 0; s < topk; ++s) {
+          const int rows = s_ids[s] * H + cta * 16;
+          uint8_t* b = dn_base + s * a.dslot_bytes;
+          tma_load_3d(b, &dn_c, 0, rows, 0, &bar_dn);
+          tma_load_3d(b + nks_d * 2048, &dn_s, 0, rows, 0, &bar_dn);
+        }
+      }
+    }
+    return;
+  }
+
+  // ================= consumers =================
+  // ---- R: norm, router rows ----
+  add_rmsnorm_1pass(a.x, a.ldx, a.res, a.nw, a.eps, 1, H, xnb, cta == 0 ? a.res_out : nullptr,
+                    cta == 0 ? a.xn_out : nullptr, red_n, kXT, 1);
+  if (has_row) {
+    const uint4* xp = reinterpret_cast<const uint4*>(xnb);
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      float xf[8], wf[8];
+      bf16x8_to_f32(xp[lane + 32 * i], xf);
+      bf16x8_to_f32(wv[i], wf);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc = fmaf(wf[j], xf[j], acc);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) __stcg(lg + my_row, bf16r(acc));
+  }
+  stage_rows_f16(xnb, H, 1, H, xs, shift_x, red_n, kXT, 1);
+  grid_sync(&ws->sync, nb, 0, kXT, 1, &s_ok, status);
+
+  // ---- U: top-k, then the up units ----
+  if (warp == 0) {
+    int my_e;
+    float my_w;
+    warp_topk(lg, E, topk, a.score_fn, lane, my_e, my_w);
+    if (lane < topk) {
+      s_ids[lane] = my_e;
+      s_tw[lane] = my_w;
+      if (cta == 0) {
+        if (a.ids_out) a.ids_out[lane] = my_e;
+        if (a.tw_out) a.tw_out[lane] = my_w;
+      }
+    }
+  }
+  if (cta == 0 && a.logits_out)
+    for (int i = tid; i < E; i += kXT) a.logits_out[i] = __ldcg(lg + i);
+  xsync();
+  if (tid == 0) mbar_arrive(&bar_plan);                 // release the producer
+
+  const int g = lane >> 2, t = lane & 3;
+  const __half* xrow = xs;                              // token 0 (lanes g > 0 feed zero columns)
+  const bool active = g == 0;
+  for (int u = 0; u < nu; ++u) {
+    if (!xsync_and(mbar_wait(&bar_up[u], 0, status))) break;
+    const int unit = u0 + u, s = unit / jpe, j = unit - s * jpe, e = s_ids[s];
+    const uint8_t* b = up_base + u * a.unit_bytes;
+    float acc_g[4][4], acc_u[4][4];
+    zero_acc(acc_g);
+    zero_acc(acc_u);
+    for (int ks = warp; ks < nks_u; ks += kXW) {
+      consume_stage(b + ks * 2048, b + 2 * nks_u * 2048 + ks * 256, 0, g, t, ks, xrow, active, acc_g);
+      consume_stage(b + (nks_u + ks) * 2048, b + 2 * nks_u * 2048 + (nks_u + ks) * 256, 0, g, t, ks, xrow, active, acc_u);
+    }
+    float dg[4], du[4];
+    sum_acc(acc_g, dg);
+    sum_acc(acc_u, du);
+    if (t == 0) {                                       // column 0 = the token
+      const int r0 = tile_phi(g);
+      red[(0 * kXW + warp) * 16 + r0] = dg[0];
+      red[(0 * kXW + warp) * 16 + r0 + 8] = dg[2];
+      red[(1 * kXW + warp) * 16 + r0] = du[0];
+      red[(1 * kXW + warp) * 16 + r0 + 8] = du[2];
+    }
+    xsync();
+    if (tid < 16) {
+      float gs = 0.f, us = 0.f;
+#pragma unroll
+      for (int w = 0; w < kXW; ++w) {
+        gs += red[(0 * kXW + w) * 16 + tid];
+        us += red[(1 * kXW + w) * 16 + tid];
+      }
+      const float sc = ldexpf(a.g13[e], -shift_x[0]);
+      const float gv = gs * sc, uv = us * sc;
+      const float silu = gv / (1.0f + expf(-gv));
+      __stcg(reinterpret_cast<unsigned short*>(act_g + (int64_t)s * I + j * 16 + tid),
+             __bfloat16_as_ushort(__float2bfloat16_rn(silu * uv)));
+    }
+    xsync();
+  }
+  grid_sync(&ws->sync, nb, 1, kXT, 1, &s_ok, status);
+  pdl_trigger();
+
+  // ---- D: this CTA's 16 output rows over every routed expert, then the slot-order sum ----
+  if (has_dn) {
+    stage_rows_f16(act_g, I, topk, I, xa, shift_a, red_n, kXT, 1, true);
+    if (xsync_and(mbar_wait(&bar_dn, 0, status))) {
+      if (warp < topk) {
+        const int s = warp, e = s_ids[s];
+        const uint8_t* b = dn_base + s * a.dslot_bytes;
+        const bool act_col = g == 0;
+        const __half* arow = xa + s * xs_stride(I);
+        float acc[4][4];
+        zero_acc(acc);
+        for (int ks = 0; ks < nks_d; ++ks) consume_stage(b + ks * 2048, b + nks_d * 2048 + ks * 256, 0, g, t, ks, arow, act_col, acc);
+        float d[4];
+        sum_acc(acc, d);
+        if (t == 0) {
+          const int r0 = tile_phi(g);
+          const float sc = ldexpf(a.g2[e], -shift_a[s]);
+          ybuf[s][r0] = bf16r(d[0] * sc);
+          ybuf[s][r0 + 8] = bf16r(d[2] * sc);
+        }
+      }
+      xsync();
+      if (tid < 16) {
+        float acc = 0.f;
+        for (int s = 0; s < topk; ++s) acc = fmaf(s_tw[s], ybuf[s][tid], acc);
+        a.out[cta * 16 + tid] = __float2bfloat16_rn(acc);
+      }
+    }
+  }
+  grid_sync_retire(&ws->sync, nb);
+}
+
+}  // namespace flint
+
+using namespace flint;
+
+extern "C" int64_t flint_moe_block_workspace_bytes(int64_t E, int64_t I) { return (int64_t)moe_block_ws_bytes((int)E, (int)I); }
+
+extern "C" int flint_moe_block(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, const void* gate_w,
+                               int64_t H, int64_t E, int64_t topk, int score_fn, const void* w13, const void* s13,
+                               const float* g13, const void* w2, const void* s2, const float* g2, int64_t I, void* out,
+                               void* res_out, void* xn_out, float* logits_out, int32_t* topk_ids_out,
+                               float* topk_weights_out, void* workspace, int pdl, void* stream) {
+  if (!x || !norm_w || !gate_w || !w13 || !s13 || !g13 || !w2 || !s2 || !g2 || !out || !workspace) return FLINT_ERR_ARGUMENT;
+  const int sms = num_sms();
+  if (sms <= 0) return FLINT_ERR_DEVICE;
+  if (H != 2048 || E < 32 || E % 32 != 0 || E > kMaxExperts || E > 2 * sms || topk < 1 ||
+      topk > kXMaxSlots || topk > E || I < kSliceK || I % kSliceK != 0 || ldx < H || score_fn < 0 || score_fn > 1 ||
+      H / 16 > sms)
+    return FLINT_ERR_SHAPE;
+  const int U = (int)(topk * (I / 16));
+  if ((U + sms - 1) / sms > kXMaxUnits) return FLINT_ERR_SHAPE;
+  if (!aligned(x, 16) || ldx % 8 != 0 || (res && !aligned(res, 16)) || !aligned(norm_w, 16) || !aligned(gate_w, 16) ||
+      !aligned(w13, 16) || !aligned(s13, 16) || !aligned(w2, 16) || !aligned(s2, 16) || !aligned(out, 16) ||
+      (res_out && !aligned(res_out, 16)) || (xn_out && !aligned(xn_out, 16)) || !aligned(workspace, 256))
+    return FLINT_ERR_ALIGN;
+  auto up = [](size_t v, size_t al) { return (v + al - 1) / al * al; };
+  const int nks_u = (int)(H / kSliceK), nks_d = (int)(I / kSliceK);
+  MoeBlockArgs a{};
+  a.unit_bytes = (uint32_t)up((size_t)2 * nks_u * (2048 + 256), 1024);
+  a.dslot_bytes = (uint32_t)up((size_t)nks_d * (2048 + 256), 1024);
+  a.off_dn = kXMaxUnits * a.unit_bytes;
+  a.off_xn = a.off_dn + kXMaxSlots * a.dslot_bytes;
+  a.off_xs = a.off_xn + (uint32_t)up((size_t)H * 2, 1024);
+  a.off_xa = a.off_xs + (uint32_t)up((size_t)xs_stride((int)H) * 2, 1024);
+  a.off_red = a.off_xa + (uint32_t)up((size_t)kXMaxSlots * xs_stride((int)I) * 2, 1024);
+  const size_t smem = 1024 + a.off_red + 2 * kXW * 16 * 4;
+  if (smem > 227 * 1024 - 2048) return FLINT_ERR_SHAPE;
+
+  // weights as 3-D views [slice][row][bytes of the slice]: one box per 16-row block over all of K
+  auto enc3 = [](CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t row_bytes, uint64_t nks,
+                 bool swz) {
+    const uint64_t d[3] = {inner, rows, nks};
+    const uint64_t st[2] = {row_bytes, inner};
+    const uint32_t bx[3] = {(uint32_t)inner, 16u, (uint32_t)nks};
+    return encode_u8_3d(m, base, d, st, bx, swz);
+  };
+  CUtensorMap uc, us, dc, ds;
+  int rc = enc3(&uc, w13, 128, (uint64_t)E * 2 * I, H / 2, nks_u, true);
+  if (!rc) rc = enc3(&us, s13, 16, (uint64_t)E * 2 * I, H / 16, nks_u, false);
+  if (!rc) rc = enc3(&dc, w2, 128, (uint64_t)E * H, I / 2, nks_d, true);
+  if (!rc) rc = enc3(&ds, s2, 16, (uint64_t)E * H, I / 16, nks_d, false);
+  if (rc) return rc;
+
+  a.x = (const bf16*)x; a.ldx = ldx; a.res = (const bf16*)res; a.nw = (const bf16*)norm_w; a.eps = eps;
+  a.gate_w = (const bf16*)gate_w; a.E = (int)E; a.topk = (int)topk; a.score_fn = score_fn; a.H = (int)H; a.I = (int)I;
+  a.g13 = g13; a.g2 = g2; a.out = (bf16*)out; a.res_out = (bf16*)res_out; a.xn_out = (bf16*)xn_out;
+  a.logits_out = logits_out; a.ids_out = topk_ids_out; a.tw_out = topk_weights_out;
+  a.ws = static_cast<MoeBlockWs*>(workspace);
+
+  // H = 2048: the single-pass norm keeps one 8-wide chunk per consumer thread
+  void (*kern)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, MoeBlockArgs) = moe_block_kernel<8>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return record_cuda(cudaGetLastError(), FLINT_ERR_LAUNCH);
+  set_max_carveout(kern);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(sms);
+  cfg.blockDim = dim3((kXW + 1) * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeCooperative;
+  at[0].val.cooperative = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return record_cuda(cudaLaunchKernelEx(&cfg, kern, uc, us, dc, ds, a), FLINT_ERR_LAUNCH);
+}

@@ -100,11 +100,25 @@ def moe_down(act, sact, ti, tw, w: DecodeWeights, trigger=0):
     return out
 
 
-def moe_decode(x, res, nw, eps, gate_w, w: DecodeWeights, fused: bool = True, extras: bool = False):
-    """The whole decode MoE block: (mlp(norm(x + res)), x + res).  fused=True: one persistent launch
-    (flint_moe_fused); fused=False: the three launches route_norm -> moe_up -> moe_down.
-    extras=True (fused only) also returns (xn, logits, topk_ids, topk_weights)."""
-    if not fused:
+def moe_decode(x, res, nw, eps, gate_w, w: DecodeWeights, fused: bool = True, extras: bool = False,
+               impl: str | None = None):
+    """The whole decode MoE block: (mlp(norm(x + res)), x + res).  impl "chain" (fused=False): the three launches
+    route_norm -> moe_up -> moe_down; "fused" (fused=True): one persistent launch for 1..8 tokens (flint_moe_fused);
+    "block": one launch for one token with the down weights prefetched under the gate/up work (flint_moe_block).
+    extras=True (fused / block) also returns (xn, logits, topk_ids, topk_weights)."""
+    impl = impl or ("fused" if fused else "chain")
+    if impl == "block":
+        M, H = x.shape
+        dev = x.device
+        out = torch.empty((M, H), dtype=torch.bfloat16, device=dev)
+        res_out = torch.empty((M, H), dtype=torch.bfloat16, device=dev) if res is not None else None
+        ex = (torch.empty((M, H), dtype=torch.bfloat16, device=dev), torch.empty((M, w.E), dtype=torch.float32, device=dev),
+              torch.empty((M, w.topk), dtype=torch.int32, device=dev), torch.empty((M, w.topk), dtype=torch.float32, device=dev))
+        xn, lg, ti, tw = ex if extras else (None, None, None, None)
+        torch.ops.flint_b200.moe_block(x, res, nw, float(eps), gate_w, w.topk, w.score_fn, w.w13, w.s13, w.g13, w.w2, w.s2,
+                                       w.g2, out, res_out, xn, lg, ti, tw)
+        return (out, res_out, ex) if extras else (out, res_out)
+    if impl == "chain":
         tw, ti, xn, res_out = route_norm(x, res, nw, eps, gate_w, topk=w.topk,
                                          score=("softmax", "sigmoid")[w.score_fn])
         act, sact = moe_up(xn, ti, w)

@@ -43,7 +43,7 @@ def main(argv=None):
     ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--reps", type=int, default=5)
     ap.add_argument("--batch", type=int, default=1)
-    ap.add_argument("--moe", default="chain", choices=["chain", "fused"])
+    ap.add_argument("--moe", default=None, choices=["block", "chain", "fused"])
     ap.add_argument("--attn", default="block", choices=["block", "chain"])
     args = ap.parse_args(argv)
     _package()

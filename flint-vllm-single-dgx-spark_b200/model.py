@@ -119,11 +119,15 @@ class FlintModel:
 class Decoder:
     """Batch-M (M <= 8) decode of a FlintModel: teacher-forced prompt processing and greedy generation."""
 
-    def __init__(self, model: FlintModel, batch: int = 1, moe: str = "chain", attn: str = "block"):
-        """moe: "chain" (route, up, down: three launches, the faster at batch 1) or "fused" (one persistent launch);
-        attn: "block" (QKV + attention + O in one persistent launch) or "chain" (three launches)."""
-        if moe not in ("chain", "fused"):
-            raise ValueError(f"moe must be 'chain' or 'fused', got {moe!r}")
+    def __init__(self, model: FlintModel, batch: int = 1, moe: str | None = None, attn: str = "block"):
+        """moe: "block" (one launch, one token; the default at batch 1), "chain" (route, up, down: three launches;
+        the default for 2..8 tokens) or "fused" (one persistent launch for 1..8 tokens); attn: "block" (QKV +
+        attention + O in one persistent launch) or "chain" (three launches)."""
+        moe = moe or ("block" if batch == 1 else "chain")
+        if moe not in ("block", "chain", "fused"):
+            raise ValueError(f"moe must be 'block', 'chain' or 'fused', got {moe!r}")
+        if moe == "block" and batch != 1:
+            raise ValueError("moe='block' decodes one token; use 'chain' or 'fused' for batches")
         if attn not in ("block", "chain"):
             raise ValueError(f"attn must be 'block' or 'chain', got {attn!r}")
         self.m, self.c, self.M, self.moe, self.attn_mode = model, model.cfg, batch, moe, attn
@@ -182,7 +186,11 @@ class Decoder:
                                                               self.seq_lens, None, 0, self.scale, self.attn,
                                                               self.splits)),
                    ("o", lambda: ops.attn_o(self.attn.view(self.M, -1), Po, So, gso, self.a))]
-        if self.moe == "fused":
+        if self.moe == "block":
+            seq.append(("moe_block", lambda: ops.moe_block(self.a, self.res_a, L["ln2"], c.rms_eps, L["gate"], c.topk,
+                                                           ew.score_fn, ew.w13, ew.s13, ew.g13, ew.w2, ew.s2, ew.g2, self.h,
+                                                           self.res_b, None, None, None, None)))
+        elif self.moe == "fused":
             seq.append(("moe_fused", lambda: ops.moe_fused(self.a, self.res_a, L["ln2"], c.rms_eps, L["gate"], c.topk,
                                                            ew.score_fn, ew.w13, ew.s13, ew.g13, ew.w2, ew.s2, ew.g2,
                                                            self.h, self.res_b, self.xn, self.lg, self.ti, self.tw,
@@ -226,7 +234,7 @@ class Decoder:
         if name == "attn_block":
             return (self.algorithmic_bytes("qkv", ctx) + self.algorithmic_bytes("attention", ctx)
                     + self.algorithmic_bytes("o", ctx))
-        if name == "moe_fused":
+        if name in ("moe_fused", "moe_block"):
             return (self.algorithmic_bytes("route", ctx) + self.algorithmic_bytes("up", ctx)
                     + self.algorithmic_bytes("down", ctx))
         if name == "head":

@@ -215,6 +215,35 @@ def _(x, res, norm_w, eps, gate_w, topk, score_fn, w13, s13, g13, w2, s2, g2, ou
     return None
 
 
+@torch.library.custom_op(f"{NS}::moe_block", mutates_args=("out", "res_out", "xn_out", "logits_out", "ids_out",
+                                                             "tw_out"))
+def moe_block(x: torch.Tensor, res: torch.Tensor | None, norm_w: torch.Tensor, eps: float, gate_w: torch.Tensor, topk: int,
+              score_fn: int, w13: torch.Tensor, s13: torch.Tensor, g13: torch.Tensor, w2: torch.Tensor, s2: torch.Tensor,
+              g2: torch.Tensor, out: torch.Tensor, res_out: torch.Tensor | None, xn_out: torch.Tensor | None,
+              logits_out: torch.Tensor | None, ids_out: torch.Tensor | None, tw_out: torch.Tensor | None) -> None:
+    """The decode MoE block of ONE token in one launch (flint_moe_block).  The optional outputs are positional
+    without defaults (torch drops trailing default-valued arguments when it boxes a call)."""
+    _lib.require_cuda(x, "moe_block")
+    _bf16_2d(x, "moe_block x")
+    M, H = x.shape
+    E, I2, Hh = w13.shape
+    if M != 1 or Hh * 2 != H or gate_w.shape != (E, H) or out.shape != (1, H):
+        raise _lib.FlintError("moe_block: one token, shapes must match the expert weights")
+    nbytes = lib().flint_moe_block_workspace_bytes(E, I2 // 2)
+    ws = _lib.workspace(x.device, f"moe_block_{E}_{I2 // 2}", nbytes)
+    rc = lib().flint_moe_block(ptr(x), x.stride(0), ptr(res), ptr(norm_w), float(eps), ptr(gate_w), H, E, topk, score_fn,
+                               ptr(_u8(w13)), ptr(_u8(s13)), ptr(g13), ptr(_u8(w2)), ptr(_u8(s2)), ptr(g2), I2 // 2,
+                               ptr(out), ptr(res_out), ptr(xn_out), ptr(logits_out), ptr(ids_out), ptr(tw_out), ptr(ws),
+                               PDL, stream_ptr(x.device))
+    check(rc, "flint_moe_block")
+
+
+@moe_block.register_fake
+def _(x, res, norm_w, eps, gate_w, topk, score_fn, w13, s13, g13, w2, s2, g2, out, res_out, xn_out, logits_out, ids_out,
+      tw_out):
+    return None
+
+
 @torch.library.custom_op(f"{NS}::moe_align", mutates_args=("sorted_ids", "expert_ids", "num_tokens_post_pad"))
 def moe_align(topk_ids: torch.Tensor, num_experts: int, block_size: int, sorted_ids: torch.Tensor,
               expert_ids: torch.Tensor, num_tokens_post_pad: torch.Tensor) -> None:

@@ -145,6 +145,20 @@ int flint_moe_fused(const void* x, int64_t ldx, const void* res, const void* nor
                     void* res_out, void* xn_out, float* logits_out, int32_t* topk_ids_out, float* topk_weights_out,
                     void* workspace, int pdl, void* stream);
 
+/* The decode MoE block for ONE token in one cooperative launch (router + top-k -> gate/up + SwiGLU -> down ->
+ * weighted sum, two grid barriers): each CTA loads its share of the gate/up rows and its 16 output rows of every
+ * routed expert's down matrix as soon as the routing is known, so the down weights stream in under the gate/up
+ * work and the weighted sum needs no cross-CTA reduction.  Same arguments and outputs as flint_moe_fused at M = 1;
+ * routing, xn, res_out and the down step have the bits of flint_moe_route / flint_moe_down, act matches
+ * flint_moe_up to fp32 rounding.  H = 2048, E % 32 == 0, E <= 2 * SMs, topk <= 8, I % 256 == 0,
+ * topk * I / 16 <= 3 * SMs.  workspace: flint_moe_block_workspace_bytes(E, I), zero-filled once, 256-byte aligned. */
+int64_t flint_moe_block_workspace_bytes(int64_t E, int64_t I);
+int flint_moe_block(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, const void* gate_w,
+                    int64_t H, int64_t E, int64_t topk, int score_fn, const void* w13, const void* s13, const float* g13,
+                    const void* w2, const void* s2, const float* g2, int64_t I, void* out, void* res_out, void* xn_out,
+                    float* logits_out, int32_t* topk_ids_out, float* topk_weights_out, void* workspace, int pdl,
+                    void* stream);
+
 /* ------------------------------------------------------------------------------------------------
  * (2) Deterministic moe_align_block_size.  Replaces fast/patch_align.py:11-30 (_deterministic_align), the
  * vLLM call-site contract of moe_align_block_size (same buffers, same outputs): routes of each expert in

@@ -148,3 +148,55 @@ def test_fused_moe_matches_three_kernel_chain(fb, cfg, M):
         out2, _ = fm.moe_decode(x, res, nw, 1e-6, gate, w, fused=True)
     torch.cuda.synchronize()
     np.testing.assert_array_equal(host(out2), host(ref_out))
+
+
+@needs_cuda
+@pytest.mark.parametrize("cfg", [BASE, FLINT])
+def test_moe_block_vs_oracle_and_chain(fb, cfg):
+    """The one-token MoE block: routing, xn and res_out bit-identical to the chain (and the routing to the oracle
+    mirror), the output within the activation tolerance of the oracle and of the chain."""
+    from flint_b200 import fp4moe_decode as fm
+    rng = np.random.default_rng(300 + cfg["E"])
+    H, E, topk = cfg["H"], cfg["E"], cfg["topk"]
+    L = make_layer(rng, **cfg)
+    w = dev_weights(L, topk, cfg["score"])
+    x, res = bf16(rng, (1, H)), bf16(rng, (1, H))
+    xd, rd, nw, gate = dev_bf16(x), dev_bf16(res), dev_bf16(L["nw"]), dev_bf16(L["gate"])
+    out, res_out, (xn, lg, ti, tw) = fm.moe_decode(xd, rd, nw, 1e-6, gate, w, extras=True, impl="block")
+    out_c, res_c, (xn_c, lg_c, ti_c, tw_c) = fm.moe_decode(xd, rd, nw, 1e-6, gate, w, extras=True, impl="fused")
+    torch.cuda.synchronize()
+    sf = 0 if cfg["score"] == "softmax" else 1
+    np.testing.assert_array_equal(host(res_out), host(res_c))
+    np.testing.assert_array_equal(host(xn), host(xn_c))
+    np.testing.assert_array_equal(host(lg), host(lg_c))
+    np.testing.assert_array_equal(host(ti), host(ti_c))
+    np.testing.assert_array_equal(host(tw), host(tw_c))
+    lg_ref = omoe.router_logits_mirror(host(xn), L["gate"])
+    np.testing.assert_array_equal(host(lg), lg_ref)
+    ids_ref, tw_ref = omoe.topk_route(lg_ref, topk, sf)
+    np.testing.assert_array_equal(host(ti), ids_ref)
+    act_ref = omoe.experts_up(host(xn), ids_ref, L["w13"], L["s13"], L["g13"])
+    out_ref = omoe.experts_down(act_ref, ids_ref, tw_ref, L["w2"], L["s2"], L["g2"])
+    assert_bf16_close(host(out), out_ref, rel=2 ** -6, abs_frac=4e-3, what="moe block vs oracle")
+    assert_bf16_close(host(out), host(out_c), rel=2 ** -6, abs_frac=4e-3, what="moe block vs chain")
+
+
+@needs_cuda
+def test_moe_block_graph_replay_deterministic(fb):
+    from flint_b200 import fp4moe_decode as fm
+    cfg = BASE
+    rng = np.random.default_rng(77)
+    L = make_layer(rng, **cfg)
+    w = dev_weights(L, cfg["topk"], "softmax")
+    xd, rd = dev_bf16(bf16(rng, (1, cfg["H"]))), dev_bf16(bf16(rng, (1, cfg["H"])))
+    nw, gate = dev_bf16(L["nw"]), dev_bf16(L["gate"])
+    out, _ = fm.moe_decode(xd, rd, nw, 1e-6, gate, w, impl="block")
+    torch.cuda.synchronize()
+    ref = host(out).copy()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out_g, _ = fm.moe_decode(xd, rd, nw, 1e-6, gate, w, impl="block")
+    for _ in range(5):
+        g.replay()
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(host(out_g), ref)
