@@ -42,6 +42,11 @@ SIGNATURES: dict[str, tuple] = {
                               P]),
     "flint_moe_block_workspace_bytes": (I64, [I64, I64]),
     "flint_moe_block": (I32, [P, I64, P, P, F32, P, I64, I64, I64, I32, P, P, P, P, P, P, I64, P, P, P, P, P, P, P, I32, P]),
+    "flint_moe_block_ep": (I32, [P, I64, P, P, F32, P, I64, I64, I64, I32, P, P, P, P, P, P, I64, I64, I64, P, P, P, P, I32,
+                                 P]),
+    "flint_moe_combine": (I32, [P, P, I64, I64, P, I32, P]),
+    "flint_lm_head_nv4_shard": (I32, [P, I64, P, P, F32, I64, P, P, F32, I64, I64, I64, P, P, I32, P]),
+    "flint_argmax_keys_to_tokens": (I32, [P, I64, P, I32, P]),
     "flint_moe_align": (I32, [P, I64, I64, I64, P, I64, P, I64, P, P, I32, P]),
     "flint_attn_proj_workspace_bytes": (I64, []),
     "flint_attn_qkv": (I32, [P, I64, P, P, P, F32, P, P, P, I64, I64, I64, I64, I64, I32, P, P, F32, P, P, I64, P, P, I64,

@@ -43,3 +43,21 @@ extern "C" int flint_decode_advance(const int32_t* tokens, int64_t M, int64_t* p
                 positions, (int*)seq_lens, slots, (const int*)block_tables, bt_stride, (int)max_blocks, (int)block_size,
                 (int*)history, hist_stride, (int*)step, (int)max_steps, (int*)next_tokens);
 }
+
+namespace flint {
+
+__global__ void keys_to_tokens_kernel(const unsigned long long* __restrict__ keys, int M, int* __restrict__ tokens) {
+  pdl_wait();
+  if ((int)threadIdx.x < M) tokens[threadIdx.x] = (int)argmax_key_index(keys[threadIdx.x]);
+  pdl_trigger();
+}
+
+}  // namespace flint
+
+extern "C" int flint_argmax_keys_to_tokens(const uint64_t* keys, int64_t M, int32_t* tokens, int pdl, void* stream) {
+  using namespace flint;
+  if (!keys || !tokens) return FLINT_ERR_ARGUMENT;
+  if (M < 1 || M > 1024) return FLINT_ERR_SHAPE;
+  return launch(keys_to_tokens_kernel, dim3(1), dim3((unsigned)((M + 31) / 32 * 32)), 0, stream, pdl,
+                reinterpret_cast<const unsigned long long*>(keys), (int)M, (int*)tokens);
+}

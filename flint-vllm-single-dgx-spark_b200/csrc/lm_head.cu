@@ -47,7 +47,42 @@ extern "C" int flint_lm_head_nv4_fused(const void* x, int64_t ldx, const void* r
   const int grid = ngroups < sms ? ngroups : sms;
   return launch(kern, dim3(grid), dim3((kHeadWarps + 1) * 32), smem, stream, pdl, mc, ms, (const bf16*)x, ldx,
                 (const bf16*)res, (const bf16*)norm_w, eps, (int)M, gs, (int)V, (int)K, logits, ld_logits, (int*)token_ids,
-                (HeadWorkspace*)workspace, SampleParams{});
+                (HeadWorkspace*)workspace, SampleParams{}, 0u, (unsigned long long*)nullptr);
+}
+
+// Vocabulary shard of the head (rows index_base .. index_base + V - 1 of the full vocabulary): the per-row argmax
+// key (order-preserving value, then the lowest global id) of this shard goes to keys_out; the maximum of the keys
+// over all shards (an integer MAX all-reduce) is the full-vocabulary argmax key (flint_argmax_keys_to_tokens).
+extern "C" int flint_lm_head_nv4_shard(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps,
+                                       int64_t M, const void* P, const void* S, float gs, int64_t V, int64_t K,
+                                       int64_t index_base, uint64_t* keys_out, void* workspace, int pdl, void* stream) {
+  using namespace flint;
+  if (!x || !P || !S || (res && !norm_w) || !keys_out) return FLINT_ERR_ARGUMENT;
+  if (M < 1 || M > 8 || V < 1 || V > (1ll << 30) || K < kSliceK || K % kSliceK != 0 || K > 8192 || ldx < K ||
+      index_base < 0 || index_base + V > (1ll << 31))
+    return FLINT_ERR_SHAPE;
+  if (!aligned(P, 16) || !aligned(S, 16) || !aligned(x, 16) || ldx % 8 != 0 || (res && !aligned(res, 16)) ||
+      (norm_w && !aligned(norm_w, 16)))
+    return FLINT_ERR_ALIGN;
+  if (!workspace) return FLINT_ERR_WORKSPACE;
+  if (!aligned(workspace, 8)) return FLINT_ERR_ALIGN;
+  const int sms = num_sms();
+  if (sms <= 0) return FLINT_ERR_DEVICE;
+  CUtensorMap mc, ms;
+  int rc = encode_u8_2d(&mc, P, K / 2, V, K / 2, 128, kHeadRows, true);
+  if (rc) return rc;
+  rc = encode_u8_2d(&ms, S, K / 16, V, K / 16, 16, kHeadRows, false);
+  if (rc) return rc;
+  auto kern = lm_head_kernel<kHeadStages, kHeadWarps, false>;
+  const size_t smem = head_smem((int)M, (int)K, norm_w != nullptr);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return FLINT_ERR_LAUNCH;
+  const int ngroups = (int)((V + kHeadRows - 1) / kHeadRows);
+  const int grid = ngroups < sms ? ngroups : sms;
+  return launch(kern, dim3(grid), dim3((kHeadWarps + 1) * 32), smem, stream, pdl, mc, ms, (const bf16*)x, ldx,
+                (const bf16*)res, (const bf16*)norm_w, eps, (int)M, gs, (int)V, (int)K, (float*)nullptr, (int64_t)0,
+                (int*)nullptr, (HeadWorkspace*)workspace, SampleParams{}, (uint32_t)index_base,
+                reinterpret_cast<unsigned long long*>(keys_out));
 }
 
 namespace flint {
@@ -109,7 +144,7 @@ extern "C" int flint_lm_head_nv4_sample(const void* x, int64_t ldx, const void* 
   const int64_t ldl = logits ? ld_logits : V;
   return launch(kern, dim3(grid), dim3((kHeadWarps + 1) * 32), smem, stream, pdl, mc, ms, (const bf16*)x, ldx,
                 (const bf16*)res, (const bf16*)norm_w, eps, (int)M, gs, (int)V, (int)K, lg, ldl, (int*)token_ids,
-                (HeadWorkspace*)workspace, sp);
+                (HeadWorkspace*)workspace, sp, 0u, (unsigned long long*)nullptr);
 }
 
 extern "C" int flint_lm_head_nv4(const void* x, int64_t ldx, int64_t M, const void* P, const void* S, float gs, int64_t V,

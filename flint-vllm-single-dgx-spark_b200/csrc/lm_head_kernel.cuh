@@ -149,7 +149,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
 lm_head_kernel(const __grid_constant__ CUtensorMap map_codes, const __grid_constant__ CUtensorMap map_scales,
                const bf16* __restrict__ x, int64_t ldx, const bf16* __restrict__ res, const bf16* __restrict__ norm_w,
                float eps, int M, float gs, int V, int K, float* __restrict__ logits, int64_t ldl, int* __restrict__ tokens,
-               HeadWorkspace* ws, const SampleParams sp) {
+               HeadWorkspace* ws, const SampleParams sp, uint32_t index_base, unsigned long long* keys_out) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   using G = StageGeom<NW * 16>;
@@ -238,13 +238,14 @@ lm_head_kernel(const __grid_constant__ CUtensorMap map_codes, const __grid_const
         zero_acc(acc);
         const float v00 = (d[0] * inv0) * gs, v01 = (d[1] * inv1) * gs;
         const float v10 = (d[2] * inv0) * gs, v11 = (d[3] * inv1) * gs;
+        const uint32_t k0 = index_base + (uint32_t)r0, k1 = index_base + (uint32_t)r1;   // global row ids
         if (r0 < V) {
-          if (n0 < M) { if (logits) logits[n0 * ldl + r0] = v00; kbest[0] = max(kbest[0], argmax_key(v00, r0)); }
-          if (n1 < M) { if (logits) logits[n1 * ldl + r0] = v01; kbest[1] = max(kbest[1], argmax_key(v01, r0)); }
+          if (n0 < M) { if (logits) logits[n0 * ldl + r0] = v00; kbest[0] = max(kbest[0], argmax_key(v00, k0)); }
+          if (n1 < M) { if (logits) logits[n1 * ldl + r0] = v01; kbest[1] = max(kbest[1], argmax_key(v01, k0)); }
         }
         if (r1 < V) {
-          if (n0 < M) { if (logits) logits[n0 * ldl + r1] = v10; kbest[0] = max(kbest[0], argmax_key(v10, r1)); }
-          if (n1 < M) { if (logits) logits[n1 * ldl + r1] = v11; kbest[1] = max(kbest[1], argmax_key(v11, r1)); }
+          if (n0 < M) { if (logits) logits[n0 * ldl + r1] = v10; kbest[0] = max(kbest[0], argmax_key(v10, k1)); }
+          if (n1 < M) { if (logits) logits[n1 * ldl + r1] = v11; kbest[1] = max(kbest[1], argmax_key(v11, k1)); }
         }
         ks = 0;
         ++grp;
@@ -267,7 +268,7 @@ lm_head_kernel(const __grid_constant__ CUtensorMap map_codes, const __grid_const
     head_sample_tail<ROWS>(smem, logits, ldl, M, V, g0, g1, sp, ws, tokens, &s_last);
     return;
   }
-  if (tokens == nullptr) return;
+  if (tokens == nullptr && keys_out == nullptr) return;
 
   // ---- argmax across warps, then across CTAs ----
   __syncthreads();
@@ -285,7 +286,10 @@ lm_head_kernel(const __grid_constant__ CUtensorMap map_codes, const __grid_const
   __threadfence();
   if (threadIdx.x < M) {
     const unsigned long long k = atomicExch(&ws->best[threadIdx.x], 0ull);
-    tokens[threadIdx.x] = (int)argmax_key_index(k);
+    // vocabulary shard: the (value, lowest id) key with its top bit flipped, so that a signed int64 MAX over the
+    // shards orders keys as the unsigned comparison does (the id in the low half is unchanged)
+    if (keys_out) keys_out[threadIdx.x] = k ^ 0x8000000000000000ull;
+    else tokens[threadIdx.x] = (int)argmax_key_index(k);
   }
   if (threadIdx.x == 0) atomicExch(&ws->counter, 0u);
 }

@@ -16,6 +16,12 @@
 //
 // Routing, xn, res_out and the down step have the bits of flint_moe_route / flint_moe_down; the gate/up sums split
 // K across warps, so act (and hence out) agrees with the chain to fp32 rounding, not bit for bit.
+//
+// Expert-parallel mode (y_out given): this rank holds experts [e_lo, e_hi) only; the router and top-k run in full
+// (identical on every rank), only routed slots whose expert is local get up units and down rows, and instead of
+// the weighted sum the kernel writes y[slot][H] (bf16 y_s for local slots, zero rows otherwise) and the routing
+// weights; a sum over ranks (exact: one non-zero term per element) followed by flint_moe_combine gives the
+// single-GPU output bit for bit.
 #include "gridsync.cuh"
 #include "moe_common.cuh"
 #include "runtime.cuh"
@@ -53,6 +59,8 @@ struct MoeBlockArgs {
   int* ids_out;
   float* tw_out;
   uint32_t unit_bytes, dslot_bytes, off_dn, off_xn, off_xs, off_xa, off_red;
+  int e_lo, e_hi;                    // local experts (weights hold rows of experts e_lo .. e_hi-1 only)
+  bf16* y_out;                       // expert-parallel mode: per-slot outputs [topk][H] (NULL: weighted sum to out)
   MoeBlockWs* ws;
 };
 
@@ -81,15 +89,20 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   __shared__ int shift_x[kMaxTokens], shift_a[kXMaxSlots];
   __shared__ float red_n[kXW * 8 + 8];
   __shared__ float ybuf[kXMaxSlots][16];
+  __shared__ int s_local[kXMaxSlots], s_nlocal;
   __shared__ int s_ok;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nb = gridDim.x, cta = blockIdx.x;
   const int E = a.E, I = a.I, topk = a.topk;
   const int nks_u = H / kSliceK, nks_d = I / kSliceK, jpe = I / 16;
-  const int U = topk * jpe;
-  const int u0 = (int)((int64_t)cta * U / nb), nu = (int)((int64_t)(cta + 1) * U / nb) - u0;
   const bool has_dn = cta < H / 16;
+  // up units follow the local routed slots (known after top-k): unit u -> slot s_local[u / jpe], rows 16 (u % jpe)
+  auto unit_range = [&](int& u0, int& nu) {
+    const int U = s_nlocal * jpe;
+    u0 = (int)((int64_t)cta * U / nb);
+    nu = (int)((int64_t)(cta + 1) * U / nb) - u0;
+  };
   MoeBlockWs* ws = a.ws;
   unsigned* status = &ws->status;
   float* lg = reinterpret_cast<float*>(ws + 1);
@@ -128,9 +141,11 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
       tma_prefetch_desc(&dn_c);
       tma_prefetch_desc(&dn_s);
       if (!mbar_wait(&bar_plan, 0, status)) return;
+      int u0, nu;
+      unit_range(u0, nu);
       for (int u = 0; u < nu; ++u) {
-        const int unit = u0 + u, s = unit / jpe, j = unit - s * jpe;
-        const int rows_g = s_ids[s] * 2 * I + j * 16, rows_u = rows_g + I;
+        const int unit = u0 + u, s = s_local[unit / jpe], j = unit - (unit / jpe) * jpe;
+        const int rows_g = (s_ids[s] - a.e_lo) * 2 * I + j * 16, rows_u = rows_g + I;
         uint8_t* b = up_base + u * a.unit_bytes;
         mbar_arrive_expect_tx(&bar_up[u], 2 * nks_u * (2048 + 256));
         tma_load_3d(b, &up_c, 0, rows_g, 0, &bar_up[u]);
@@ -138,10 +153,11 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
         tma_load_3d(b + 2 * nks_u * 2048, &up_s, 0, rows_g, 0, &bar_up[u]);
         tma_load_3d(b + 2 * nks_u * 2048 + nks_u * 256, &up_s, 0, rows_u, 0, &bar_up[u]);
       }
-      if (has_dn) {
-        mbar_arrive_expect_tx(&bar_dn, topk * nks_d * (2048 + 256));
+      if (has_dn && s_nlocal > 0) {
+        mbar_arrive_expect_tx(&bar_dn, s_nlocal * nks_d * (2048 + 256));
         for (int s = 0; s < topk; ++s) {
-          const int rows = s_ids[s] * H + cta * 16;
+          if (s_ids[s] < a.e_lo || s_ids[s] >= a.e_hi) continue;
+          const int rows = (s_ids[s] - a.e_lo) * H + cta * 16;
           uint8_t* b = dn_base + s * a.dslot_bytes;
           tma_load_3d(b, &dn_c, 0, rows, 0, &bar_dn);
           tma_load_3d(b + nks_d * 2048, &dn_s, 0, rows, 0, &bar_dn);
@@ -186,6 +202,10 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
         if (a.tw_out) a.tw_out[lane] = my_w;
       }
     }
+    const bool loc = lane < topk && my_e >= a.e_lo && my_e < a.e_hi;
+    const unsigned lm = __ballot_sync(0xffffffffu, loc);
+    if (loc) s_local[__popc(lm & ((1u << lane) - 1u))] = lane;
+    if (lane == 0) s_nlocal = __popc(lm);
   }
   if (cta == 0 && a.logits_out)
     for (int i = tid; i < E; i += kXT) a.logits_out[i] = __ldcg(lg + i);
@@ -195,9 +215,11 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   const int g = lane >> 2, t = lane & 3;
   const __half* xrow = xs;                              // token 0 (lanes g > 0 feed zero columns)
   const bool active = g == 0;
+  int u0, nu;
+  unit_range(u0, nu);
   for (int u = 0; u < nu; ++u) {
     if (!xsync_and(mbar_wait(&bar_up[u], 0, status))) break;
-    const int unit = u0 + u, s = unit / jpe, j = unit - s * jpe, e = s_ids[s];
+    const int unit = u0 + u, s = s_local[unit / jpe], j = unit - (unit / jpe) * jpe, e = s_ids[s] - a.e_lo;
     const uint8_t* b = up_base + u * a.unit_bytes;
     float acc_g[4][4], acc_u[4][4];
     zero_acc(acc_g);
@@ -238,9 +260,11 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   // ---- D: this CTA's 16 output rows over every routed expert, then the slot-order sum ----
   if (has_dn) {
     stage_rows_f16(act_g, I, topk, I, xa, shift_a, red_n, kXT, 1, true);
-    if (xsync_and(mbar_wait(&bar_dn, 0, status))) {
-      if (warp < topk) {
-        const int s = warp, e = s_ids[s];
+    if (s_nlocal == 0 || xsync_and(mbar_wait(&bar_dn, 0, status))) {
+      if (warp < topk && (s_ids[warp] < a.e_lo || s_ids[warp] >= a.e_hi)) {
+        if (lane < 16) ybuf[warp][lane] = 0.f;           // expert of another rank
+      } else if (warp < topk) {
+        const int s = warp, e = s_ids[s] - a.e_lo;
         const uint8_t* b = dn_base + s * a.dslot_bytes;
         const bool act_col = g == 0;
         const __half* arow = xa + s * xs_stride(I);
@@ -257,7 +281,10 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
         }
       }
       xsync();
-      if (tid < 16) {
+      if (a.y_out) {
+        for (int i = tid; i < topk * 16; i += kXT)
+          a.y_out[(int64_t)(i >> 4) * H + cta * 16 + (i & 15)] = __float2bfloat16_rn(ybuf[i >> 4][i & 15]);
+      } else if (tid < 16) {
         float acc = 0.f;
         for (int s = 0; s < topk; ++s) acc = fmaf(s_tw[s], ybuf[s][tid], acc);
         a.out[cta * 16 + tid] = __float2bfloat16_rn(acc);
@@ -267,18 +294,35 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   grid_sync_retire(&ws->sync, nb);
 }
 
+// out[r] = bf16(sum_s tw[s] * y[s][r]) in slot order (the weighted sum of flint_moe_block after an expert-parallel
+// sum of the per-slot rows over ranks).
+__global__ void moe_combine_kernel(const bf16* __restrict__ y, const float* __restrict__ tw, int topk, int H,
+                                   bf16* __restrict__ out) {
+  pdl_wait();
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r < H) {
+    float acc = 0.f;
+    for (int s = 0; s < topk; ++s) acc = fmaf(tw[s], __bfloat162float(y[(int64_t)s * H + r]), acc);
+    out[r] = __float2bfloat16_rn(acc);
+  }
+  pdl_trigger();
+}
+
 }  // namespace flint
 
 using namespace flint;
 
 extern "C" int64_t flint_moe_block_workspace_bytes(int64_t E, int64_t I) { return (int64_t)moe_block_ws_bytes((int)E, (int)I); }
 
-extern "C" int flint_moe_block(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, const void* gate_w,
-                               int64_t H, int64_t E, int64_t topk, int score_fn, const void* w13, const void* s13,
-                               const float* g13, const void* w2, const void* s2, const float* g2, int64_t I, void* out,
-                               void* res_out, void* xn_out, float* logits_out, int32_t* topk_ids_out,
-                               float* topk_weights_out, void* workspace, int pdl, void* stream) {
-  if (!x || !norm_w || !gate_w || !w13 || !s13 || !g13 || !w2 || !s2 || !g2 || !out || !workspace) return FLINT_ERR_ARGUMENT;
+static int moe_block_launch(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps,
+                            const void* gate_w, int64_t H, int64_t E, int64_t topk, int score_fn, const void* w13,
+                            const void* s13, const float* g13, const void* w2, const void* s2, const float* g2, int64_t I,
+                            int64_t e_lo, int64_t n_local, void* out, void* y_out, void* res_out, void* xn_out,
+                            float* logits_out, int32_t* topk_ids_out, float* topk_weights_out, void* workspace, int pdl,
+                            void* stream) {
+  if (!x || !norm_w || !gate_w || !w13 || !s13 || !g13 || !w2 || !s2 || !g2 || (!out && !y_out) || !workspace)
+    return FLINT_ERR_ARGUMENT;
+  if (e_lo < 0 || n_local < 1 || e_lo + n_local > E || (y_out && !topk_weights_out)) return FLINT_ERR_ARGUMENT;
   const int sms = num_sms();
   if (sms <= 0) return FLINT_ERR_DEVICE;
   if (H != 2048 || E < 32 || E % 32 != 0 || E > kMaxExperts || E > 2 * sms || topk < 1 ||
@@ -288,7 +332,8 @@ extern "C" int flint_moe_block(const void* x, int64_t ldx, const void* res, cons
   const int U = (int)(topk * (I / 16));
   if ((U + sms - 1) / sms > kXMaxUnits) return FLINT_ERR_SHAPE;
   if (!aligned(x, 16) || ldx % 8 != 0 || (res && !aligned(res, 16)) || !aligned(norm_w, 16) || !aligned(gate_w, 16) ||
-      !aligned(w13, 16) || !aligned(s13, 16) || !aligned(w2, 16) || !aligned(s2, 16) || !aligned(out, 16) ||
+      !aligned(w13, 16) || !aligned(s13, 16) || !aligned(w2, 16) || !aligned(s2, 16) || (out && !aligned(out, 16)) ||
+      (y_out && !aligned(y_out, 16)) ||
       (res_out && !aligned(res_out, 16)) || (xn_out && !aligned(xn_out, 16)) || !aligned(workspace, 256))
     return FLINT_ERR_ALIGN;
   auto up = [](size_t v, size_t al) { return (v + al - 1) / al * al; };
@@ -313,16 +358,17 @@ extern "C" int flint_moe_block(const void* x, int64_t ldx, const void* res, cons
     return encode_u8_3d(m, base, d, st, bx, swz);
   };
   CUtensorMap uc, us, dc, ds;
-  int rc = enc3(&uc, w13, 128, (uint64_t)E * 2 * I, H / 2, nks_u, true);
-  if (!rc) rc = enc3(&us, s13, 16, (uint64_t)E * 2 * I, H / 16, nks_u, false);
-  if (!rc) rc = enc3(&dc, w2, 128, (uint64_t)E * H, I / 2, nks_d, true);
-  if (!rc) rc = enc3(&ds, s2, 16, (uint64_t)E * H, I / 16, nks_d, false);
+  int rc = enc3(&uc, w13, 128, (uint64_t)n_local * 2 * I, H / 2, nks_u, true);
+  if (!rc) rc = enc3(&us, s13, 16, (uint64_t)n_local * 2 * I, H / 16, nks_u, false);
+  if (!rc) rc = enc3(&dc, w2, 128, (uint64_t)n_local * H, I / 2, nks_d, true);
+  if (!rc) rc = enc3(&ds, s2, 16, (uint64_t)n_local * H, I / 16, nks_d, false);
   if (rc) return rc;
 
   a.x = (const bf16*)x; a.ldx = ldx; a.res = (const bf16*)res; a.nw = (const bf16*)norm_w; a.eps = eps;
   a.gate_w = (const bf16*)gate_w; a.E = (int)E; a.topk = (int)topk; a.score_fn = score_fn; a.H = (int)H; a.I = (int)I;
   a.g13 = g13; a.g2 = g2; a.out = (bf16*)out; a.res_out = (bf16*)res_out; a.xn_out = (bf16*)xn_out;
   a.logits_out = logits_out; a.ids_out = topk_ids_out; a.tw_out = topk_weights_out;
+  a.e_lo = (int)e_lo; a.e_hi = (int)(e_lo + n_local); a.y_out = (bf16*)y_out;
   a.ws = static_cast<MoeBlockWs*>(workspace);
 
   // H = 2048: the single-pass norm keeps one 8-wide chunk per consumer thread
@@ -343,4 +389,31 @@ extern "C" int flint_moe_block(const void* x, int64_t ldx, const void* res, cons
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 2 : 1;
   return record_cuda(cudaLaunchKernelEx(&cfg, kern, uc, us, dc, ds, a), FLINT_ERR_LAUNCH);
+}
+
+extern "C" int flint_moe_block(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, const void* gate_w,
+                               int64_t H, int64_t E, int64_t topk, int score_fn, const void* w13, const void* s13,
+                               const float* g13, const void* w2, const void* s2, const float* g2, int64_t I, void* out,
+                               void* res_out, void* xn_out, float* logits_out, int32_t* topk_ids_out,
+                               float* topk_weights_out, void* workspace, int pdl, void* stream) {
+  return moe_block_launch(x, ldx, res, norm_w, eps, gate_w, H, E, topk, score_fn, w13, s13, g13, w2, s2, g2, I, 0, E, out,
+                          nullptr, res_out, xn_out, logits_out, topk_ids_out, topk_weights_out, workspace, pdl, stream);
+}
+
+extern "C" int flint_moe_block_ep(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps,
+                                  const void* gate_w, int64_t H, int64_t E, int64_t topk, int score_fn, const void* w13,
+                                  const void* s13, const float* g13, const void* w2, const void* s2, const float* g2,
+                                  int64_t I, int64_t expert_lo, int64_t n_local, void* y_out, float* topk_weights_out,
+                                  void* res_out, void* workspace, int pdl, void* stream) {
+  return moe_block_launch(x, ldx, res, norm_w, eps, gate_w, H, E, topk, score_fn, w13, s13, g13, w2, s2, g2, I, expert_lo,
+                          n_local, nullptr, y_out, res_out, nullptr, nullptr, nullptr, topk_weights_out, workspace, pdl,
+                          stream);
+}
+
+extern "C" int flint_moe_combine(const void* y, const float* topk_weights, int64_t topk, int64_t H, void* out, int pdl,
+                                 void* stream) {
+  if (!y || !topk_weights || !out) return FLINT_ERR_ARGUMENT;
+  if (topk < 1 || topk > kXMaxSlots || H < 1 || H > (1 << 20)) return FLINT_ERR_SHAPE;
+  return launch(moe_combine_kernel, dim3((unsigned)((H + 255) / 256)), dim3(256), 0, stream, pdl, (const bf16*)y,
+                topk_weights, (int)topk, (int)H, (bf16*)out);
 }

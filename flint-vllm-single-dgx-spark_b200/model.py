@@ -77,11 +77,24 @@ def rope_cos_sin(max_pos: int, dim: int, theta: float, device) -> torch.Tensor:
 
 
 class FlintModel:
-    """Weights, KV cache and RoPE table of a synthetic Flint-class model on one GPU."""
+    """Weights, KV cache and RoPE table of a synthetic Flint-class model on one GPU.
 
-    def __init__(self, cfg: FlintConfig, device="cuda", seed: int = 0, max_ctx: int = 8192, max_batch: int = 1):
+    shard = (rank, world): this GPU's part of a model split over `world` GPUs by expert parallelism (experts
+    rank*E/world .. (rank+1)*E/world - 1 of every MoE layer) and vocabulary sharding (rows rank*V/world ..
+    (rank+1)*V/world - 1 of the LM head); attention, router, norms and embedding are replicated.  Every rank draws
+    the whole model from the same seeded sequence and keeps its slices, so the shards are exactly the single-GPU
+    model's tensors."""
+
+    def __init__(self, cfg: FlintConfig, device="cuda", seed: int = 0, max_ctx: int = 8192, max_batch: int = 1,
+                 shard: tuple[int, int] = (0, 1)):
         self.cfg, self.dev = cfg, torch.device(device)
         self.max_ctx, self.max_batch = max_ctx, max_batch
+        self.rank, self.world = shard
+        if cfg.num_experts % self.world or cfg.vocab % (256 * self.world):
+            raise ValueError("experts and vocab / 256 must divide by the number of shards")
+        self.e_lo, self.n_local = self.rank * cfg.num_experts // self.world, cfg.num_experts // self.world
+        self.v_lo, self.v_local = self.rank * cfg.vocab // self.world, cfg.vocab // self.world
+        sl = lambda t: t[self.e_lo:self.e_lo + self.n_local].contiguous() if self.world > 1 else t
         c = cfg
         g = torch.Generator(device=self.dev)
         g.manual_seed(seed)
@@ -92,14 +105,18 @@ class FlintModel:
         for _ in range(c.layers):
             P, S, gs = random_nvfp4((), c.qkv_rows, c.hidden, c.weight_std, g, self.dev)
             Po, So, gso = random_nvfp4((), c.hidden, c.num_heads * c.head_dim, c.weight_std, g, self.dev)
-            w13, s13, g13 = random_nvfp4((c.num_experts,), 2 * c.moe_inter, c.hidden, c.weight_std, g, self.dev)
-            w2, s2, g2 = random_nvfp4((c.num_experts,), c.hidden, c.moe_inter, c.weight_std, g, self.dev)
+            w13, s13, g13 = (sl(t) for t in random_nvfp4((c.num_experts,), 2 * c.moe_inter, c.hidden, c.weight_std, g,
+                                                          self.dev))
+            w2, s2, g2 = (sl(t) for t in random_nvfp4((c.num_experts,), c.hidden, c.moe_inter, c.weight_std, g, self.dev))
             self.layers.append(dict(
                 ln1=ones(c.hidden), qkv=(P, S, gs.reshape(1)), q_norm=ones(c.head_dim), k_norm=ones(c.head_dim),
                 o=(Po, So, gso.reshape(1)), ln2=ones(c.hidden), gate=bf((c.num_experts, c.hidden), c.weight_std),
                 experts=DecodeWeights(w13, s13, g13, w2, s2, g2, topk=c.topk, score=c.score)))
         self.final_norm = ones(c.hidden)
         Ph, Sh, gsh = random_nvfp4((), c.vocab, c.hidden, c.weight_std, g, self.dev)
+        if self.world > 1:
+            Ph = Ph[self.v_lo:self.v_lo + self.v_local].contiguous()
+            Sh = Sh[self.v_lo:self.v_lo + self.v_local].contiguous()
         self.head = (Ph, Sh, float(gsh.item()))
         self.cos_sin = rope_cos_sin(max_ctx, c.head_dim, c.rope_theta, self.dev)
         # paged KV cache: FlashInfer HND [blocks, kv_heads, 16, 2*D] per layer; each stream owns a shuffled block set
@@ -119,7 +136,7 @@ class FlintModel:
 class Decoder:
     """Batch-M (M <= 8) decode of a FlintModel: teacher-forced prompt processing and greedy generation."""
 
-    def __init__(self, model: FlintModel, batch: int = 1, moe: str | None = None, attn: str = "block"):
+    def __init__(self, model: FlintModel, batch: int = 1, moe: str | None = None, attn: str = "block", group=None):
         """moe: "block" (one launch, one token; the default at batch 1), "chain" (route, up, down: three launches;
         the default for 2..8 tokens) or "fused" (one persistent launch for 1..8 tokens); attn: "block" (QKV +
         attention + O in one persistent launch) or "chain" (three launches)."""
@@ -128,6 +145,9 @@ class Decoder:
             raise ValueError(f"moe must be 'block', 'chain' or 'fused', got {moe!r}")
         if moe == "block" and batch != 1:
             raise ValueError("moe='block' decodes one token; use 'chain' or 'fused' for batches")
+        if model.world > 1 and (moe != "block" or group is None):
+            raise ValueError("a sharded model decodes one token with moe='block' and needs its process group")
+        self.group = group
         if attn not in ("block", "chain"):
             raise ValueError(f"attn must be 'block' or 'chain', got {attn!r}")
         self.m, self.c, self.M, self.moe, self.attn_mode = model, model.cfg, batch, moe, attn
@@ -148,14 +168,19 @@ class Decoder:
         self.a, self.xn = e(M, c.hidden), e(M, c.hidden)
         self.tw, self.ti = e(M, c.topk, dt=torch.float32), e(M, c.topk, dt=torch.int32)
         self.lg = e(M, c.num_experts, dt=torch.float32)
+        self.y_slots = torch.zeros((c.topk, c.hidden), dtype=torch.bfloat16, device=dev)   # expert-parallel exchange
+        self.keys = torch.zeros((M,), dtype=torch.int64, device=dev)                        # vocab-shard argmax
         self.act = e(M * c.topk, c.moe_inter)
         self.dummy_f = e(1, 1, dt=torch.float32)
         self.dummy_b = e(0)
         self.splits = _ops.attention_splits(M, c.num_kv_heads)
         self.scale = c.head_dim ** -0.5
         self.graphs: dict[str, torch.cuda.CUDAGraph] = {}
-        # (qkv, attention, o | attention block) + (route, up, down | fused MoE) per layer, then head + advance
-        self.launches_per_step = ((3 if attn == "chain" else 1) + (3 if moe == "chain" else 1)) * c.layers + 2
+        # (qkv, attention, o | attention block) + (route, up, down | fused MoE | EP block + combine) per layer, then
+        # head (+ key conversion when sharded) + advance; NCCL's own kernels are not counted
+        ep = model.world > 1
+        self.launches_per_step = ((3 if attn == "chain" else 1) + (3 if moe == "chain" else 2 if ep else 1)) * c.layers \
+            + 2 + (1 if ep else 0)
 
     # ---- one decode step as torch ops on persistent buffers ----
     def layer_ops(self, l: int) -> list[tuple[str, callable]]:
@@ -186,7 +211,16 @@ class Decoder:
                                                               self.seq_lens, None, 0, self.scale, self.attn,
                                                               self.splits)),
                    ("o", lambda: ops.attn_o(self.attn.view(self.M, -1), Po, So, gso, self.a))]
-        if self.moe == "block":
+        if self.moe == "block" and m.world > 1:
+            import torch.distributed as dist
+
+            def moe_ep():
+                ops.moe_block_ep(self.a, self.res_a, L["ln2"], c.rms_eps, L["gate"], c.topk, ew.score_fn, ew.w13, ew.s13,
+                                 ew.g13, ew.w2, ew.s2, ew.g2, m.e_lo, self.y_slots, self.tw, self.res_b)
+                dist.all_reduce(self.y_slots, group=self.group)
+                ops.moe_combine(self.y_slots, self.tw, self.h)
+            seq.append(("moe_block_ep", moe_ep))
+        elif self.moe == "block":
             seq.append(("moe_block", lambda: ops.moe_block(self.a, self.res_a, L["ln2"], c.rms_eps, L["gate"], c.topk,
                                                            ew.score_fn, ew.w13, ew.s13, ew.g13, ew.w2, ew.s2, ew.g2, self.h,
                                                            self.res_b, None, None, None, None)))
@@ -210,8 +244,17 @@ class Decoder:
 
     def head_op(self):
         P, S, gs = self.m.head
-        return lambda: torch.ops.flint_b200.lm_head_nv4(self.h, P, S, gs, self.dummy_f, self.out_tok, False, True,
-                                                        self.res_b, self.m.final_norm, self.c.rms_eps)
+        ops = torch.ops.flint_b200
+        if self.m.world > 1:
+            import torch.distributed as dist
+
+            def head_shard():
+                ops.lm_head_shard(self.h, P, S, gs, self.m.v_lo, self.keys, self.res_b, self.m.final_norm, self.c.rms_eps)
+                dist.all_reduce(self.keys, op=dist.ReduceOp.MAX, group=self.group)
+                ops.keys_to_tokens(self.keys, self.out_tok)
+            return head_shard
+        return lambda: ops.lm_head_nv4(self.h, P, S, gs, self.dummy_f, self.out_tok, False, True, self.res_b,
+                                       self.m.final_norm, self.c.rms_eps)
 
     def algorithmic_bytes(self, name: str, ctx: int) -> int:
         """Bytes one launch of kernel `name` must move at batch M and context ctx (weights / KV read once,
@@ -234,7 +277,7 @@ class Decoder:
         if name == "attn_block":
             return (self.algorithmic_bytes("qkv", ctx) + self.algorithmic_bytes("attention", ctx)
                     + self.algorithmic_bytes("o", ctx))
-        if name in ("moe_fused", "moe_block"):
+        if name in ("moe_fused", "moe_block", "moe_block_ep"):
             return (self.algorithmic_bytes("route", ctx) + self.algorithmic_bytes("up", ctx)
                     + self.algorithmic_bytes("down", ctx))
         if name == "head":

@@ -64,6 +64,38 @@ def _(x, P, S, gs, logits, tokens, write_logits, write_tokens, res=None, norm_w=
     return None
 
 
+@torch.library.custom_op(f"{NS}::lm_head_shard", mutates_args=("keys_out",))
+def lm_head_shard(x: torch.Tensor, P: torch.Tensor, S: torch.Tensor, gs: float, index_base: int, keys_out: torch.Tensor,
+                  res: torch.Tensor | None, norm_w: torch.Tensor | None, eps: float) -> None:
+    """One vocabulary shard of the NVFP4 head: per-row argmax keys (int64 [M], global ids from index_base)."""
+    _lib.require_cuda(x, "lm_head_shard")
+    V, K = _check_nvfp4(P, S, "lm_head_shard")
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != K or keys_out.dtype != torch.int64:
+        raise _lib.FlintError("lm_head_shard: x bf16 [M, K], keys_out int64 [M]")
+    ws = _lib.workspace(x.device, "lm_head", lib().flint_lm_head_workspace_bytes())
+    rc = lib().flint_lm_head_nv4_shard(ptr(x), x.stride(0), ptr(res), ptr(norm_w), float(eps), x.shape[0], ptr(_u8(P)),
+                                       ptr(_u8(S)), float(gs), V, K, int(index_base), ptr(keys_out), ptr(ws), PDL,
+                                       stream_ptr(x.device))
+    check(rc, "flint_lm_head_nv4_shard")
+
+
+@lm_head_shard.register_fake
+def _(x, P, S, gs, index_base, keys_out, res, norm_w, eps):
+    return None
+
+
+@torch.library.custom_op(f"{NS}::keys_to_tokens", mutates_args=("tokens",))
+def keys_to_tokens(keys: torch.Tensor, tokens: torch.Tensor) -> None:
+    _lib.require_cuda(keys, "keys_to_tokens")
+    rc = lib().flint_argmax_keys_to_tokens(ptr(keys), keys.numel(), ptr(tokens), PDL, stream_ptr(keys.device))
+    check(rc, "flint_argmax_keys_to_tokens")
+
+
+@keys_to_tokens.register_fake
+def _(keys, tokens):
+    return None
+
+
 @torch.library.custom_op(f"{NS}::lm_head_sample", mutates_args=("tokens", "logits", "cand_ids", "cand_logits", "kept"))
 def lm_head_sample(x: torch.Tensor, P: torch.Tensor, S: torch.Tensor, gs: float, temperature: float, top_k: int,
                    top_p: float, seeds: torch.Tensor, step: torch.Tensor | None, tokens: torch.Tensor,
@@ -241,6 +273,48 @@ def moe_block(x: torch.Tensor, res: torch.Tensor | None, norm_w: torch.Tensor, e
 @moe_block.register_fake
 def _(x, res, norm_w, eps, gate_w, topk, score_fn, w13, s13, g13, w2, s2, g2, out, res_out, xn_out, logits_out, ids_out,
       tw_out):
+    return None
+
+
+@torch.library.custom_op(f"{NS}::moe_block_ep", mutates_args=("y_out", "tw_out", "res_out"))
+def moe_block_ep(x: torch.Tensor, res: torch.Tensor | None, norm_w: torch.Tensor, eps: float, gate_w: torch.Tensor,
+                 topk: int, score_fn: int, w13: torch.Tensor, s13: torch.Tensor, g13: torch.Tensor, w2: torch.Tensor,
+                 s2: torch.Tensor, g2: torch.Tensor, expert_lo: int, y_out: torch.Tensor, tw_out: torch.Tensor,
+                 res_out: torch.Tensor | None) -> None:
+    """Expert-parallel one-token MoE block (flint_moe_block_ep): the local experts' rows of y_out [topk, H], zeros for
+    the other ranks' slots, and the routing weights."""
+    _lib.require_cuda(x, "moe_block_ep")
+    _bf16_2d(x, "moe_block_ep x")
+    M, H = x.shape
+    n_local, I2, Hh = w13.shape
+    E = gate_w.shape[0]
+    if M != 1 or Hh * 2 != H or gate_w.shape[1] != H or y_out.shape != (topk, H) or tw_out.numel() < topk:
+        raise _lib.FlintError("moe_block_ep: shapes do not match")
+    nbytes = lib().flint_moe_block_workspace_bytes(E, I2 // 2)
+    ws = _lib.workspace(x.device, f"moe_block_{E}_{I2 // 2}", nbytes)
+    rc = lib().flint_moe_block_ep(ptr(x), x.stride(0), ptr(res), ptr(norm_w), float(eps), ptr(gate_w), H, E, topk,
+                                  score_fn, ptr(_u8(w13)), ptr(_u8(s13)), ptr(g13), ptr(_u8(w2)), ptr(_u8(s2)), ptr(g2),
+                                  I2 // 2, int(expert_lo), n_local, ptr(y_out), ptr(tw_out), ptr(res_out), ptr(ws), PDL,
+                                  stream_ptr(x.device))
+    check(rc, "flint_moe_block_ep")
+
+
+@moe_block_ep.register_fake
+def _(x, res, norm_w, eps, gate_w, topk, score_fn, w13, s13, g13, w2, s2, g2, expert_lo, y_out, tw_out, res_out):
+    return None
+
+
+@torch.library.custom_op(f"{NS}::moe_combine", mutates_args=("out",))
+def moe_combine(y: torch.Tensor, tw: torch.Tensor, out: torch.Tensor) -> None:
+    """out [1, H] = bf16(sum_s tw[s] * y[s]) in slot order."""
+    _lib.require_cuda(y, "moe_combine")
+    topk, H = y.shape
+    rc = lib().flint_moe_combine(ptr(y), ptr(tw), topk, H, ptr(out), PDL, stream_ptr(y.device))
+    check(rc, "flint_moe_combine")
+
+
+@moe_combine.register_fake
+def _(y, tw, out):
     return None
 
 

@@ -87,6 +87,16 @@ int flint_lm_head_nv4_sample(const void* x, int64_t ldx, const void* res, const 
                              int64_t ld_logits, float temperature, int64_t top_k, float top_p, const uint64_t* seeds,
                              const int32_t* step, int32_t* token_ids, int32_t* cand_ids, float* cand_logits,
                              int32_t* kept, void* workspace, int pdl, void* stream);
+/* One vocabulary shard of the head, for a head split over ranks: P / S hold rows index_base .. index_base + V - 1
+ * of the full vocabulary; keys_out int64 [M] receives each row's best (value, lowest global id) argmax key
+ * ((order-preserving fp32 image << 32 | (0xFFFFFFFF - id)) with the top bit flipped, so signed comparison orders it).
+ * The maximum over all shards (a signed int64 MAX all-reduce) is the full-vocabulary key; flint_argmax_keys_to_tokens turns keys into token ids.  Optional fused final norm as
+ * flint_lm_head_nv4_fused.  workspace: flint_lm_head_workspace_bytes(). */
+int flint_lm_head_nv4_shard(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, int64_t M,
+                            const void* P, const void* S, float gs, int64_t V, int64_t K, int64_t index_base,
+                            uint64_t* keys_out, void* workspace, int pdl, void* stream);
+/* tokens[m] = the id carried by argmax key keys[m] (M <= 1024). */
+int flint_argmax_keys_to_tokens(const uint64_t* keys, int64_t M, int32_t* tokens, int pdl, void* stream);
 /* Allocation-free flint_lm_head_nv4 (no counterpart in the reference: the recipe always runs inside vLLM, which
  * allocates).  For callers that cannot allocate device memory at call time -- an engine that has already given all
  * free HBM to its KV-cache pool, a CUDA-graph capture region, a host runtime that only reaches the library through
@@ -158,6 +168,20 @@ int flint_moe_block(const void* x, int64_t ldx, const void* res, const void* nor
                     const void* w2, const void* s2, const float* g2, int64_t I, void* out, void* res_out, void* xn_out,
                     float* logits_out, int32_t* topk_ids_out, float* topk_weights_out, void* workspace, int pdl,
                     void* stream);
+
+/* Expert-parallel form of flint_moe_block (the MoE of a model whose experts are split over ranks): this rank's
+ * weights hold experts expert_lo .. expert_lo + n_local - 1 (w13 / s13 / g13 / w2 / s2 / g2 indexed by local
+ * expert); the router and top-k run in full.  Writes y_out bf16 [topk, H] (row s = y of routed slot s when its
+ * expert is local, zeros otherwise) and topk_weights_out fp32 [topk]; res_out as flint_moe_block.  Summing y_out over
+ * all ranks (each element has one non-zero term, so the sum is exact) and calling flint_moe_combine gives the
+ * single-GPU output of flint_moe_block bit for bit. */
+int flint_moe_block_ep(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, const void* gate_w,
+                       int64_t H, int64_t E, int64_t topk, int score_fn, const void* w13, const void* s13, const float* g13,
+                       const void* w2, const void* s2, const float* g2, int64_t I, int64_t expert_lo, int64_t n_local,
+                       void* y_out, float* topk_weights_out, void* res_out, void* workspace, int pdl, void* stream);
+/* out bf16 [H] = bf16(sum_s topk_weights[s] * y[s, :]) in slot order (fp32 FMA): the weighted expert sum of the
+ * expert-parallel MoE. */
+int flint_moe_combine(const void* y, const float* topk_weights, int64_t topk, int64_t H, void* out, int pdl, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
  * (2) Deterministic moe_align_block_size.  Replaces fast/patch_align.py:11-30 (_deterministic_align), the

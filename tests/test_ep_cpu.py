@@ -1,0 +1,66 @@
+"""Multi-GPU exchange logic on CPU: world_size-2 gloo ranks run the sharded MoE sum + combine and the
+vocabulary-sharded argmax with the same arithmetic as the GPU path, against the single-process result."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    from oracle import sharding as sh
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        rng = np.random.default_rng(0)                      # identical on every rank
+        E, topk, H, V = 16, 8, 256, 4096
+        res = {}
+        for trial in range(4):
+            ids = rng.permutation(E)[:topk].astype(np.int64)
+            tw = rng.dirichlet(np.ones(topk)).astype(np.float32)
+            y = torch.from_numpy(rng.standard_normal((topk, H)).astype(np.float32)).to(torch.bfloat16).float().numpy()
+            lo, hi = sh.expert_range(rank, world, E)
+            mine = torch.from_numpy(sh.local_slot_rows(y, ids, lo, hi))
+            dist.all_reduce(mine)                           # exact: one non-zero term per element
+            res[f"moe{trial}"] = bool(np.array_equal(sh.combine(mine.numpy(), tw), sh.combine(y, tw)))
+            logits = rng.standard_normal(V).astype(np.float32)
+            if trial == 1:                                  # tie across the shard boundary: the lower id must win
+                logits[V // 2 + 7] = logits[V // 2 - 3] = np.float32(9.0)
+            if trial == 2:                                  # all negative logits
+                logits = -np.abs(logits) - 1.0
+            v0, v1 = sh.vocab_range(rank, world, V)
+            key = torch.tensor([sh.shard_key(logits[v0:v1], v0)], dtype=torch.int64)
+            dist.all_reduce(key, op=dist.ReduceOp.MAX)
+            want = int(np.flatnonzero(logits == logits.max())[0])
+            res[f"head{trial}"] = sh.key_token(int(key.item())) == want
+        q.put((rank, res))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_exchange_gloo_world2():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, res in out:
+        assert all(res.values()), (rank, res)
