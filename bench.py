@@ -162,7 +162,8 @@ def run_ours(args):
     steps, warm, plen = args.steps, args.warmup, args.prompt
     max_ctx = plen + warm + 2 * steps + 16
     model = FlintModel(cfg, dev, seed=1234, max_ctx=max_ctx, max_batch=1, shard=(rank, world))
-    dec = Decoder(model, batch=1, moe=args.moe, attn=args.attn, group=dist.group.WORLD if dist else None)
+    dec = Decoder(model, batch=1, moe=args.moe, attn=args.attn, group=dist.group.WORLD if dist else None,
+                  exchange=args.exchange)
     dec.reserve_history(warm + steps)
     dec.capture()
     prompt = np.random.default_rng(7).integers(0, cfg.vocab, size=(1, plen))
@@ -234,6 +235,8 @@ def run_ours(args):
                        "params_total": total, "params_active": active, "weight_bytes_per_token": wbytes,
                        "kv_bytes_per_token_mean": kv_bytes,
                        "parallelism": f"ep{world} + vocab{world} (attention replicated)" if world > 1 else "1 GPU",
+                       "exchange": (("in-kernel NVLink peer stores" if args.exchange == "peer" else "NCCL all-reduce")
+                                    if world > 1 else None),
                        "l2": "no flush: 1.73 GB of weights streamed per step (> 126 MB L2)",
                        "prefill_s": round(prefill_s, 2)},
             "bound_tok_s": {"weights_only": round(peak * 1e9 / wbytes, 1),
@@ -247,10 +250,9 @@ def run_ours(args):
         print(json.dumps(line), flush=True)
     if dist:
         # graphs holding NCCL calls must be released before the process group, or the exit waits for good
-        dec.graphs.clear()
+        dec.close()
         del dec
         gc.collect()
-        torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
 
@@ -303,6 +305,8 @@ def main():
     ap.add_argument("--prefill", default="teacher", choices=["teacher", "kv"],
                     help="teacher: prompt run through the decode kernels; kv: KV cache filled with seeded N(0,1) "
                          "(profiling runs)")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="N > 1: MoE / head exchange fused into the kernels over NVLink peer memory, or NCCL calls")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

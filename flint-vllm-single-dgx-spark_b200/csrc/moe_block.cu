@@ -22,8 +22,16 @@
 // the weighted sum the kernel writes y[slot][H] (bf16 y_s for local slots, zero rows otherwise) and the routing
 // weights; a sum over ranks (exact: one non-zero term per element) followed by flint_moe_combine gives the
 // single-GPU output bit for bit.
+//
+// Peer mode (peers given): expert parallel with the exchange fused in.  After phase D, block c stores the 16 rows of
+// each local slot straight into every rank's exchange buffer over NVLink (its own included), raises its flag (c, rank)
+// on every rank, waits until all ranks' flags for block c show this launch, and computes out rows 16c..16c+15 =
+// bf16(sum_s tw_s * y_s) in slot order from the received rows (exactly one rank owns each slot).  No collective
+// library call, no zero rows, no extra launch; the output equals the single-GPU block bit for bit (peer.cuh has the
+// protocol).
 #include "gridsync.cuh"
 #include "moe_common.cuh"
+#include "peer.cuh"
 #include "runtime.cuh"
 
 #include <algorithm>
@@ -62,6 +70,8 @@ struct MoeBlockArgs {
   int e_lo, e_hi;                    // local experts (weights hold rows of experts e_lo .. e_hi-1 only)
   bf16* y_out;                       // expert-parallel mode: per-slot outputs [topk][H] (NULL: weighted sum to out)
   MoeBlockWs* ws;
+  int peer_mode;                     // expert parallel with the fused peer exchange
+  PeerSet peers;
 };
 
 static size_t moe_block_ws_bytes(int E, int I) {
@@ -284,6 +294,37 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
       if (a.y_out) {
         for (int i = tid; i < topk * 16; i += kXT)
           a.y_out[(int64_t)(i >> 4) * H + cta * 16 + (i & 15)] = __float2bfloat16_rn(ybuf[i >> 4][i & 15]);
+      } else if (a.peer_mode) {
+        if (warp == 0) {
+          // push the local slots' rows of this block to every rank, flag, wait for every rank, combine
+          uint8_t* const mine = a.peers.base[a.peers.rank];
+          PeerHeader* own = peer_header(mine);
+          const unsigned ep = ld_relaxed_sys_u32(&own->moe_epoch) + 1u, par = ep & 1u;
+          const int W = a.peers.world, nl = s_nlocal;
+          for (int i = lane; i < nl * W * 2; i += 32) {
+            const int j = i / (2 * W), p = (i >> 1) - j * W, half = i & 1, s = s_local[j];
+            const float* yv = &ybuf[s][half * 8];
+            uint4 v;
+            v.x = peer_pack_bf16x2(yv[0], yv[1]);
+            v.y = peer_pack_bf16x2(yv[2], yv[3]);
+            v.z = peer_pack_bf16x2(yv[4], yv[5]);
+            v.w = peer_pack_bf16x2(yv[6], yv[7]);
+            *reinterpret_cast<uint4*>(peer_moe_rows(a.peers.base[p], par, H) + (int64_t)s * H + cta * 16 + half * 8) = v;
+          }
+          __threadfence_system();
+          __syncwarp();
+          if (lane < W) st_release_sys_u32(peer_moe_flags(a.peers.base[lane]) + cta * kPeerMax + a.peers.rank, ep);
+          bool ok = true;
+          if (lane < W) ok = peer_wait(peer_moe_flags(mine) + cta * kPeerMax + lane, ep, own);
+          ok = __all_sync(0xffffffffu, ok);
+          __syncwarp();   // orders every lane's reads after the acquiring lanes' loads
+          if (ok && lane < 16) {
+            const bf16* rows = peer_moe_rows(mine, par, H) + cta * 16 + lane;
+            float acc = 0.f;
+            for (int s = 0; s < topk; ++s) acc = fmaf(s_tw[s], peer_ldcg_bf16(rows + (int64_t)s * H), acc);
+            a.out[cta * 16 + lane] = __float2bfloat16_rn(acc);
+          }
+        }
       } else if (tid < 16) {
         float acc = 0.f;
         for (int s = 0; s < topk; ++s) acc = fmaf(s_tw[s], ybuf[s][tid], acc);
@@ -291,7 +332,7 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
       }
     }
   }
-  grid_sync_retire(&ws->sync, nb);
+  grid_sync_retire(&ws->sync, nb, a.peer_mode ? &peer_header(a.peers.base[a.peers.rank])->moe_epoch : nullptr);
 }
 
 // out[r] = bf16(sum_s tw[s] * y[s][r]) in slot order (the weighted sum of flint_moe_block after an expert-parallel
@@ -319,9 +360,11 @@ static int moe_block_launch(const void* x, int64_t ldx, const void* res, const v
                             const void* s13, const float* g13, const void* w2, const void* s2, const float* g2, int64_t I,
                             int64_t e_lo, int64_t n_local, void* out, void* y_out, void* res_out, void* xn_out,
                             float* logits_out, int32_t* topk_ids_out, float* topk_weights_out, void* workspace, int pdl,
-                            void* stream) {
+                            void* stream, const PeerSet* peers = nullptr) {
   if (!x || !norm_w || !gate_w || !w13 || !s13 || !g13 || !w2 || !s2 || !g2 || (!out && !y_out) || !workspace)
     return FLINT_ERR_ARGUMENT;
+  if (peers && (!out || y_out)) return FLINT_ERR_ARGUMENT;
+  if (peers && (H / 16 != kPeerMoeBlocks || topk > kPeerSlots)) return FLINT_ERR_SHAPE;
   if (e_lo < 0 || n_local < 1 || e_lo + n_local > E || (y_out && !topk_weights_out)) return FLINT_ERR_ARGUMENT;
   const int sms = num_sms();
   if (sms <= 0) return FLINT_ERR_DEVICE;
@@ -370,6 +413,10 @@ static int moe_block_launch(const void* x, int64_t ldx, const void* res, const v
   a.logits_out = logits_out; a.ids_out = topk_ids_out; a.tw_out = topk_weights_out;
   a.e_lo = (int)e_lo; a.e_hi = (int)(e_lo + n_local); a.y_out = (bf16*)y_out;
   a.ws = static_cast<MoeBlockWs*>(workspace);
+  if (peers) {
+    a.peer_mode = 1;
+    a.peers = *peers;
+  }
 
   // H = 2048: the single-pass norm keeps one 8-wide chunk per consumer thread
   void (*kern)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, MoeBlockArgs) = moe_block_kernel<8>;
@@ -416,4 +463,16 @@ extern "C" int flint_moe_combine(const void* y, const float* topk_weights, int64
   if (topk < 1 || topk > kXMaxSlots || H < 1 || H > (1 << 20)) return FLINT_ERR_SHAPE;
   return launch(moe_combine_kernel, dim3((unsigned)((H + 255) / 256)), dim3(256), 0, stream, pdl, (const bf16*)y,
                 topk_weights, (int)topk, (int)H, (bf16*)out);
+}
+
+extern "C" int flint_moe_block_peer(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps,
+                                    const void* gate_w, int64_t H, int64_t E, int64_t topk, int score_fn, const void* w13,
+                                    const void* s13, const float* g13, const void* w2, const void* s2, const float* g2,
+                                    int64_t I, int64_t expert_lo, int64_t n_local, const void* const* peers, int rank,
+                                    int world, void* out, void* res_out, void* workspace, int pdl, void* stream) {
+  PeerSet ps;
+  const int rc = peer_set(peers, rank, world, &ps);
+  if (rc) return rc;
+  return moe_block_launch(x, ldx, res, norm_w, eps, gate_w, H, E, topk, score_fn, w13, s13, g13, w2, s2, g2, I, expert_lo,
+                          n_local, out, nullptr, res_out, nullptr, nullptr, nullptr, nullptr, workspace, pdl, stream, &ps);
 }

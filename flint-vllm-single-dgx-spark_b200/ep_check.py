@@ -3,8 +3,9 @@
     torchrun --nproc-per-node N --master-addr 127.0.0.1 flint-vllm-single-dgx-spark_b200/ep_check.py [--layers 4]
 
 Every rank builds the same small synthetic Flint-class model and keeps its shard (experts and head rows), then the
-ranks decode a prompt together (MoE: local experts' slot rows + a sum over ranks + the slot-order combine; head:
-per-shard argmax keys + a MAX over ranks).  Rank 0 also decodes the unsharded model on its GPU; the sharded token
+ranks decode a prompt together, once per exchange: "peer" (the MoE block pushes its local slots' rows to every rank
+over NVLink and combines in-kernel; the head's shard keys go through the peer argmax exchange) and "nccl" (local
+slot rows + an NCCL sum + the slot-order combine; head keys + an NCCL MAX).  Rank 0 also decodes the unsharded model on its GPU; the sharded token
 stream and final hidden state must equal it bit for bit.  Prints one JSON line (rank 0) and exits non-zero on a
 mismatch.
 """
@@ -36,19 +37,20 @@ def _package():
     return mod
 
 
-def decode(model, prompt, n, group=None):
+def decode(model, prompt, n, group=None, exchange="peer"):
     from flint_b200.model import Decoder
-    dec = Decoder(model, batch=1, group=group)
+    dec = Decoder(model, batch=1, group=group, exchange=exchange)
     dec.reserve_history(n)
     dec.capture()
     dec.prefill(prompt)
     toks = dec.decode(n).cpu().numpy().copy()
     torch.cuda.synchronize()
     h = dec.h.float().cpu().numpy().copy()
-    dec.graphs.clear()          # graphs holding NCCL calls are released before the process group goes away
+    status = dec.peers.status() if dec.peers is not None else 0
+    dec.close()                 # graphs holding NCCL calls / peer buffers go before the process group
     del dec
     gc.collect()
-    return toks, h
+    return toks, h, status
 
 
 def main():
@@ -56,6 +58,7 @@ def main():
     ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--prompt", type=int, default=40)
     ap.add_argument("--tokens", type=int, default=24)
+    ap.add_argument("--exchange", default="peer,nccl", help="exchanges to check, comma separated: peer, nccl")
     args = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
@@ -67,16 +70,23 @@ def main():
     prompt = np.random.default_rng(5).integers(0, cfg.vocab, size=(1, args.prompt))
     ctx = args.prompt + args.tokens + 16
     model = FlintModel(cfg, dev, seed=11, max_ctx=ctx, max_batch=1, shard=(rank, world))
-    toks, h = decode(model, prompt, args.tokens, group=dist.group.WORLD)
-    dist.barrier()
+    runs = {}
+    for exchange in args.exchange.split(","):
+        toks, h, status = decode(model, prompt, args.tokens, group=dist.group.WORLD, exchange=exchange)
+        runs[exchange] = (toks, h, status)
+        dist.barrier()
     ok = True
     if rank == 0:
         del model
         torch.cuda.empty_cache()
-        ref_toks, ref_h = decode(FlintModel(cfg, dev, seed=11, max_ctx=ctx, max_batch=1), prompt, args.tokens)
-        ok = bool((toks == ref_toks).all() and np.array_equal(h, ref_h))
-        print(json.dumps({"world": world, "layers": cfg.layers, "tokens": int(toks.size), "match": ok,
-                          "sharded": toks[0, :12].tolist(), "single": ref_toks[0, :12].tolist()}), flush=True)
+        ref_toks, ref_h, _ = decode(FlintModel(cfg, dev, seed=11, max_ctx=ctx, max_batch=1), prompt, args.tokens)
+        rep = {"world": world, "layers": cfg.layers, "tokens": int(ref_toks.size), "single": ref_toks[0, :12].tolist()}
+        for exchange, (toks, h, status) in runs.items():
+            match = bool((toks == ref_toks).all() and np.array_equal(h, ref_h)) and status == 0
+            rep[exchange] = {"match": match, "status": status, "tokens": toks[0, :12].tolist()}
+            ok = ok and match
+        rep["match"] = ok
+        print(json.dumps(rep), flush=True)
     flag = torch.tensor([1 if ok else 0], device=dev)
     dist.broadcast(flag, 0)
     dist.barrier()

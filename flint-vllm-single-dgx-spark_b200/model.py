@@ -136,7 +136,8 @@ class FlintModel:
 class Decoder:
     """Batch-M (M <= 8) decode of a FlintModel: teacher-forced prompt processing and greedy generation."""
 
-    def __init__(self, model: FlintModel, batch: int = 1, moe: str | None = None, attn: str = "block", group=None):
+    def __init__(self, model: FlintModel, batch: int = 1, moe: str | None = None, attn: str = "block", group=None,
+                 exchange: str = "peer"):
         """moe: "block" (one launch, one token; the default at batch 1), "chain" (route, up, down: three launches;
         the default for 2..8 tokens) or "fused" (one persistent launch for 1..8 tokens); attn: "block" (QKV +
         attention + O in one persistent launch) or "chain" (three launches)."""
@@ -147,7 +148,13 @@ class Decoder:
             raise ValueError("moe='block' decodes one token; use 'chain' or 'fused' for batches")
         if model.world > 1 and (moe != "block" or group is None):
             raise ValueError("a sharded model decodes one token with moe='block' and needs its process group")
-        self.group = group
+        if exchange not in ("peer", "nccl"):
+            raise ValueError(f"exchange must be 'peer' or 'nccl', got {exchange!r}")
+        self.group, self.exchange = group, exchange
+        self.peers = None
+        if model.world > 1 and exchange == "peer":
+            from .peer import PeerBuffers
+            self.peers = PeerBuffers(group, model.cfg.hidden)
         if attn not in ("block", "chain"):
             raise ValueError(f"attn must be 'block' or 'chain', got {attn!r}")
         self.m, self.c, self.M, self.moe, self.attn_mode = model, model.cfg, batch, moe, attn
@@ -178,9 +185,10 @@ class Decoder:
         self.graphs: dict[str, torch.cuda.CUDAGraph] = {}
         # (qkv, attention, o | attention block) + (route, up, down | fused MoE | EP block + combine) per layer, then
         # head (+ key conversion when sharded) + advance; NCCL's own kernels are not counted
+        # (peer exchange: the MoE block exchanges in-kernel; the head adds one exchange kernel)
         ep = model.world > 1
-        self.launches_per_step = ((3 if attn == "chain" else 1) + (3 if moe == "chain" else 2 if ep else 1)) * c.layers \
-            + 2 + (1 if ep else 0)
+        moe_launches = 3 if moe == "chain" else 2 if (ep and exchange == "nccl") else 1
+        self.launches_per_step = ((3 if attn == "chain" else 1) + moe_launches) * c.layers + 2 + (1 if ep else 0)
 
     # ---- one decode step as torch ops on persistent buffers ----
     def layer_ops(self, l: int) -> list[tuple[str, callable]]:
@@ -211,7 +219,12 @@ class Decoder:
                                                               self.seq_lens, None, 0, self.scale, self.attn,
                                                               self.splits)),
                    ("o", lambda: ops.attn_o(self.attn.view(self.M, -1), Po, So, gso, self.a))]
-        if self.moe == "block" and m.world > 1:
+        if self.moe == "block" and m.world > 1 and self.peers is not None:
+            pp = self.peers
+            seq.append(("moe_block_peer", lambda: ops.moe_block_peer(
+                self.a, self.res_a, L["ln2"], c.rms_eps, L["gate"], c.topk, ew.score_fn, ew.w13, ew.s13, ew.g13, ew.w2,
+                ew.s2, ew.g2, m.e_lo, pp.ptrs, pp.rank, self.h, self.res_b)))
+        elif self.moe == "block" and m.world > 1:
             import torch.distributed as dist
 
             def moe_ep():
@@ -245,6 +258,13 @@ class Decoder:
     def head_op(self):
         P, S, gs = self.m.head
         ops = torch.ops.flint_b200
+        if self.m.world > 1 and self.peers is not None:
+            pp = self.peers
+
+            def head_peer():
+                ops.lm_head_shard(self.h, P, S, gs, self.m.v_lo, self.keys, self.res_b, self.m.final_norm, self.c.rms_eps)
+                ops.keys_allmax_peer(self.keys, pp.ptrs, pp.rank, self.out_tok)
+            return head_peer
         if self.m.world > 1:
             import torch.distributed as dist
 
@@ -277,12 +297,26 @@ class Decoder:
         if name == "attn_block":
             return (self.algorithmic_bytes("qkv", ctx) + self.algorithmic_bytes("attention", ctx)
                     + self.algorithmic_bytes("o", ctx))
-        if name in ("moe_fused", "moe_block", "moe_block_ep"):
+        if name in ("moe_fused", "moe_block"):
             return (self.algorithmic_bytes("route", ctx) + self.algorithmic_bytes("up", ctx)
                     + self.algorithmic_bytes("down", ctx))
-        if name == "head":
-            return nv(c.vocab, H) + M * 2 * H * 2
+        if name in ("moe_block_ep", "moe_block_peer"):   # local experts only: topk / world routed slots on average
+            return self.algorithmic_bytes("route", ctx) + (self.algorithmic_bytes("up", ctx)
+                                                           + self.algorithmic_bytes("down", ctx)) // self.m.world
+        if name == "head":                                 # this rank's vocabulary rows
+            return nv(self.m.v_local, H) + M * 2 * H * 2
         raise KeyError(name)
+
+    def close(self):
+        """Release the captured graphs and, for a sharded model, the peer exchange buffers (collective: every rank
+        calls it, after its last decode step and before the process group is destroyed)."""
+        import gc
+        self.graphs.clear()
+        gc.collect()
+        torch.cuda.synchronize()
+        if self.peers is not None:
+            self.peers.close()
+            self.peers = None
 
     def _head_and_advance(self):
         ops = torch.ops.flint_b200

@@ -8,6 +8,7 @@ their workspaces exist (see ``_lib.workspace``).
 """
 from __future__ import annotations
 
+import ctypes
 import os
 
 import torch
@@ -315,6 +316,52 @@ def moe_combine(y: torch.Tensor, tw: torch.Tensor, out: torch.Tensor) -> None:
 
 @moe_combine.register_fake
 def _(y, tw, out):
+    return None
+
+
+def _peer_array(peers: list[int]):
+    return (ctypes.c_void_p * len(peers))(*peers)
+
+
+@torch.library.custom_op(f"{NS}::moe_block_peer", mutates_args=("out", "res_out"))
+def moe_block_peer(x: torch.Tensor, res: torch.Tensor | None, norm_w: torch.Tensor, eps: float, gate_w: torch.Tensor,
+                   topk: int, score_fn: int, w13: torch.Tensor, s13: torch.Tensor, g13: torch.Tensor, w2: torch.Tensor,
+                   s2: torch.Tensor, g2: torch.Tensor, expert_lo: int, peers: list[int], rank: int, out: torch.Tensor,
+                   res_out: torch.Tensor | None) -> None:
+    """Expert-parallel one-token MoE block with the exchange fused in (flint_moe_block_peer): every rank gets the
+    full weighted expert sum in out [1, H].  peers: every rank's exchange buffer as mapped here (PeerBuffers.ptrs)."""
+    _lib.require_cuda(x, "moe_block_peer")
+    _bf16_2d(x, "moe_block_peer x")
+    M, H = x.shape
+    n_local, I2, Hh = w13.shape
+    E = gate_w.shape[0]
+    if M != 1 or Hh * 2 != H or gate_w.shape[1] != H or out.shape[-1] != H:
+        raise _lib.FlintError("moe_block_peer: shapes do not match")
+    nbytes = lib().flint_moe_block_workspace_bytes(E, I2 // 2)
+    ws = _lib.workspace(x.device, f"moe_block_{E}_{I2 // 2}", nbytes)
+    rc = lib().flint_moe_block_peer(ptr(x), x.stride(0), ptr(res), ptr(norm_w), float(eps), ptr(gate_w), H, E, topk,
+                                    score_fn, ptr(_u8(w13)), ptr(_u8(s13)), ptr(g13), ptr(_u8(w2)), ptr(_u8(s2)), ptr(g2),
+                                    I2 // 2, int(expert_lo), n_local, _peer_array(peers), int(rank), len(peers), ptr(out),
+                                    ptr(res_out), ptr(ws), PDL, stream_ptr(x.device))
+    check(rc, "flint_moe_block_peer")
+
+
+@moe_block_peer.register_fake
+def _(x, res, norm_w, eps, gate_w, topk, score_fn, w13, s13, g13, w2, s2, g2, expert_lo, peers, rank, out, res_out):
+    return None
+
+
+@torch.library.custom_op(f"{NS}::keys_allmax_peer", mutates_args=("tokens",))
+def keys_allmax_peer(keys: torch.Tensor, peers: list[int], rank: int, tokens: torch.Tensor) -> None:
+    """Argmax over the vocabulary shards of all ranks (flint_argmax_keys_allmax_peer)."""
+    _lib.require_cuda(keys, "keys_allmax_peer")
+    rc = lib().flint_argmax_keys_allmax_peer(ptr(keys), keys.numel(), _peer_array(peers), int(rank), len(peers),
+                                             ptr(tokens), PDL, stream_ptr(keys.device))
+    check(rc, "flint_argmax_keys_allmax_peer")
+
+
+@keys_allmax_peer.register_fake
+def _(keys, peers, rank, tokens):
     return None
 
 

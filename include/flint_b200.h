@@ -184,6 +184,37 @@ int flint_moe_block_ep(const void* x, int64_t ldx, const void* res, const void* 
 int flint_moe_combine(const void* y, const float* topk_weights, int64_t topk, int64_t H, void* out, int pdl, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
+ * Peer exchange of the multi-GPU decode (one process per GPU; new in this build: the reference decodes on one GPU
+ * and has no collective on this path).  Each rank allocates one exchange buffer (flint_peer_alloc: cudaMalloc +
+ * zero fill + CUDA IPC handle, 64 bytes), shares the handle with the other ranks (any host channel) and maps theirs
+ * (flint_peer_open).  `peers` is then a host array of world pointers, peers[r] = rank r's buffer as mapped in this
+ * process (peers[rank] = its own).  Kernels store into peers' buffers over NVLink and raise per-source flags there;
+ * every wait is bounded (10 s), after which the kernel records status bit 4 in this rank's buffer
+ * (flint_peer_status) and later launches on this rank stop waiting.  All ranks must issue the same sequence of
+ * exchange launches.  Kernels that wait on one another must run on different GPUs (one rank per GPU).
+ * ------------------------------------------------------------------------------------------------ */
+int64_t flint_peer_buffer_bytes(int64_t H);
+int flint_peer_alloc(int64_t bytes, void** ptr, void* ipc_handle);
+int flint_peer_open(const void* ipc_handle, void** ptr);
+int flint_peer_close(void* ptr);                       /* a mapping made by flint_peer_open */
+int flint_peer_free(void* ptr);                        /* this rank's own buffer */
+int flint_peer_status(const void* own, uint32_t* status);
+
+/* Expert-parallel flint_moe_block with the exchange fused in: weights as flint_moe_block_ep; each down block pushes
+ * its rows of the local slots to every rank, waits for every rank's rows of the same block and writes
+ * out bf16 [H] = bf16(sum_s tw_s * y_s) in slot order -- the single-GPU flint_moe_block output bit for bit, on every
+ * rank.  H = 2048, topk <= 8, 2 <= world <= 8. */
+int flint_moe_block_peer(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, const void* gate_w,
+                         int64_t H, int64_t E, int64_t topk, int score_fn, const void* w13, const void* s13,
+                         const float* g13, const void* w2, const void* s2, const float* g2, int64_t I, int64_t expert_lo,
+                         int64_t n_local, const void* const* peers, int rank, int world, void* out, void* res_out,
+                         void* workspace, int pdl, void* stream);
+/* Vocabulary-shard argmax exchange: keys = this rank's M (<= 8) keys from flint_lm_head_nv4_shard; tokens int32 [M]
+ * = the argmax over all ranks' shards (lowest id among the largest logits), -1 if a peer wait timed out. */
+int flint_argmax_keys_allmax_peer(const uint64_t* keys, int64_t M, const void* const* peers, int rank, int world,
+                                  int32_t* tokens, int pdl, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
  * (2) Deterministic moe_align_block_size.  Replaces fast/patch_align.py:11-30 (_deterministic_align), the
  * vLLM call-site contract of moe_align_block_size (same buffers, same outputs): routes of each expert in
  * ascending route order, each expert padded to block_size, unused slots = numel, expert_ids[blk] = expert
