@@ -41,9 +41,10 @@ SIGNATURES: dict[str, tuple] = {
     "flint_moe_fused": (I32, [P, I64, P, P, F32, P, I64, I64, I64, I64, I32, P, P, P, P, P, P, I64, P, P, P, P, P, P, P, I32,
                               P]),
     "flint_moe_block_workspace_bytes": (I64, [I64, I64]),
-    "flint_moe_block": (I32, [P, I64, P, P, F32, P, I64, I64, I64, I32, P, P, P, P, P, P, I64, P, P, P, P, P, P, P, I32, P]),
-    "flint_moe_block_ep": (I32, [P, I64, P, P, F32, P, I64, I64, I64, I32, P, P, P, P, P, P, I64, I64, I64, P, P, P, P, I32,
-                                 P]),
+    "flint_moe_block": (I32, [P, I64, P, P, F32, P, I64, I64, I64, I32, P, P, P, P, P, P, I64, P, P, P, P, P, P, P, P, I32,
+                              P]),
+    "flint_moe_block_ep": (I32, [P, I64, P, P, F32, P, I64, I64, I64, I32, P, P, P, P, P, P, I64, I64, I64, P, P, P, P, P,
+                                 I32, P]),
     "flint_moe_combine": (I32, [P, P, I64, I64, P, I32, P]),
     "flint_peer_buffer_bytes": (I64, [I64]),
     "flint_peer_alloc": (I32, [I64, P, P]),
@@ -52,7 +53,7 @@ SIGNATURES: dict[str, tuple] = {
     "flint_peer_free": (I32, [P]),
     "flint_peer_status": (I32, [P, P]),
     "flint_moe_block_peer": (I32, [P, I64, P, P, F32, P, I64, I64, I64, I32, P, P, P, P, P, P, I64, I64, I64, P, I32, I32,
-                                   P, P, P, I32, P]),
+                                   P, P, P, P, I32, P]),
     "flint_argmax_keys_allmax_peer": (I32, [P, I64, P, I32, I32, P, I32, P]),
     "flint_lm_head_nv4_shard": (I32, [P, I64, P, P, F32, I64, P, P, F32, I64, I64, I64, P, P, I32, P]),
     "flint_argmax_keys_to_tokens": (I32, [P, I64, P, I32, P]),

@@ -195,6 +195,9 @@ __device__ __forceinline__ float ldcg_bf16(const bf16* p) {
   return bf16_bits_to_f32(__ldcg(reinterpret_cast<const unsigned short*>(p)));
 }
 
+// MC > 0: the batch size fixed at compile time (MC = 1 is the single-stream decode: every per-token loop collapses,
+// which shrinks the code each launch has to fetch into the instruction caches); MC = 0: M = a.M at run time.
+template <int MC>
 __global__ void __launch_bounds__(kBThreads, 1)
 attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant__ CUtensorMap mqs,
                   const __grid_constant__ CUtensorMap moc, const __grid_constant__ CUtensorMap mos,
@@ -211,7 +214,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int G = gridDim.x, cta = blockIdx.x;
-  const int M = a.M;
+  const int M = MC > 0 ? MC : a.M;
   unsigned* status = &a.ws->status;
   uint8_t* ring = smem + a.off_ring;
   uint8_t* wq = smem;                                  // QKV weights (phase A), then warp partials (phase B)
@@ -257,10 +260,23 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
     }
   }
   pdl_wait();
+  // ---- A (first half): add + RMSNorm.  It runs before the page partition and before any page is requested, so its
+  // loads of x / res are not queued behind the KV stream; the sequence lengths load alongside. ----
+  const int my_seq = (int)threadIdx.x < M ? a.seq_lens[threadIdx.x] : 0;
+  if (warp < kBW) {
+    if (a.H / 8 <= kBCons)
+      norm_stage_f16_1(a.x, a.ldx, a.tokens, a.res, a.ldr, a.nw, a.eps, M, a.H, xs, shift, red_n,
+                       cta == 0 ? a.res_out : nullptr, kBCons, 1);
+    else
+      norm_stage_f16(a.x, a.ldx, a.tokens, a.res, a.ldr, a.nw, a.eps, M, a.H, xs, shift, red_n,
+                     cta == 0 ? a.res_out : nullptr, kBCons, 1);
+    if ((int)threadIdx.x < M) s_seq[threadIdx.x] = my_seq;
+  }
+  __syncthreads();
   if (threadIdx.x == 0) {                              // page partition inputs
     int pre = 0;
     for (int b = 0; b < M; ++b) {
-      const int seq = a.seq_lens[b];
+      const int seq = s_seq[b];
       const int start = a.window > 0 ? max(0, seq - a.window) : 0;
       const int pf = start / kBPage;
       int pe = (seq + kBPage - 1) / kBPage;
@@ -322,13 +338,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
   }
 
   // ================= consumers (256 threads) =================
-  // ---- A: add + RMSNorm, QKV rows ----
-  if (a.H / 8 <= kBCons)
-    norm_stage_f16_1(a.x, a.ldx, a.tokens, a.res, a.ldr, a.nw, a.eps, M, a.H, xs, shift, red_n,
-                     cta == 0 ? a.res_out : nullptr, kBCons, 1);
-  else
-    norm_stage_f16(a.x, a.ldx, a.tokens, a.res, a.ldr, a.nw, a.eps, M, a.H, xs, shift, red_n,
-                   cta == 0 ? a.res_out : nullptr, kBCons, 1);
+  // ---- A (second half): QKV rows ----
   if (ngq > 0 && cons_sync_and(mbar_wait(&bar_wq, 0, status))) {
     gemv_resident<kBGQ>(wq, wq + a.wq_scale_off, ngq, a.nks_q, xs, a.H, M, red, warp, lane);
     cons_sync();
@@ -776,19 +786,21 @@ extern "C" int flint_attn_block(const void* x, int64_t ldx, const int32_t* token
   a.ws = reinterpret_cast<BlockWs*>(wsb);
 
   // one CTA per SM must be resident (cooperative launch): give back ring slots until the occupancy query agrees
-  set_max_carveout(attn_block_kernel);
+  void (*kern)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, BlockArgs) =
+      M == 1 ? attn_block_kernel<1> : attn_block_kernel<0>;
+  set_max_carveout(kern);
   size_t smem = L.total;
   int np = L.np;
   for (;;) {
-    if (cudaFuncSetAttribute(attn_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return record_cuda(cudaGetLastError(), FLINT_ERR_LAUNCH);
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_block_kernel, kBThreads, smem) != cudaSuccess)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kBThreads, smem) != cudaSuccess)
       return record_cuda(cudaGetLastError(), FLINT_ERR_LAUNCH);
     if (per_sm >= 1) break;
     if (np <= 2) {
       cudaFuncAttributes fa{};
-      cudaFuncGetAttributes(&fa, attn_block_kernel);
+      cudaFuncGetAttributes(&fa, kern);
       char msg[160];
       snprintf(msg, sizeof(msg), "attn_block: no CTA fits an SM (regs %d, static smem %zu, dynamic smem %zu)", fa.numRegs,
                fa.sharedSizeBytes, smem);
@@ -814,5 +826,5 @@ extern "C" int flint_attn_block(const void* x, int64_t ldx, const int32_t* token
   at[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 2 : 1;
-  return record_cuda(cudaLaunchKernelEx(&cfg, attn_block_kernel, mqc, mqs, moc, mos, mkv, a), FLINT_ERR_LAUNCH);
+  return record_cuda(cudaLaunchKernelEx(&cfg, kern, mqc, mqs, moc, mos, mkv, a), FLINT_ERR_LAUNCH);
 }

@@ -123,6 +123,15 @@ __device__ __forceinline__ int xs_perm(int k) {
   return (k & ~31) + ((q ^ ((t >> 1) << 1)) << 3) + (k & 7);
 }
 
+// x * 2^s for |s| <= 252 as two exact power-of-two products.  Equal to ldexpf(x, s) whenever the product is a
+// normal float; below that (|x * 2^s| < 2^-126) it may round differently, which no f16 conversion of the result can
+// see (f16 flushes everything below 2^-25 to zero).  A short multiply instead of the library routine keeps the
+// staging loops small.
+__device__ __forceinline__ float scale_pow2(float x, int s) {
+  const int a = s >> 1, b = s - a;
+  return (x * __int_as_float((127 + a) << 23)) * __int_as_float((127 + b) << 23);
+}
+
 // Stage `rows` activation rows (src + r*ld, bf16, K columns, 16-byte aligned rows) as f16 into xs (row stride
 // xs_stride(K)) with a per-row power-of-two rescale shift[r].  Called by threads [0, nthreads) of the block (a multiple
 // of 32), which synchronise on named barrier `bar` (0 = __syncthreads when nthreads == blockDim.x).
@@ -136,17 +145,35 @@ __device__ __forceinline__ void stage_rows_f16(const bf16* __restrict__ src, int
   int* redi = reinterpret_cast<int*>(red);
   for (int r = tid; r < rows; r += nthreads) redi[r] = 0;
   sync();
-  for (int idx = tid; idx < n; idx += nthreads) {
-    const int r = idx / K8, k8 = idx - r * K8;
-    const uint4* vp = reinterpret_cast<const uint4*>(src + r * ld) + k8;
-    const uint4 v = cg ? __ldcg(vp) : *vp;          // cg: rows written by other CTAs of this kernel
-    float f[8];
-    bf16x8_to_f32(v, f);
-    float mx = 0.f;
+  // up to kB 16-byte loads per thread are issued back to back (one memory round trip per kB * nthreads units)
+  constexpr int kB = 4;
+  for (int base = 0; base < n; base += kB * nthreads) {
+    uint4 v[kB];
+    int rr[kB], kk[kB];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(f[j]));
-    atomicMax(&redi[r], __float_as_int(mx));
-    *reinterpret_cast<uint4*>(xs + r * xs_stride(K) + xs_perm(k8 * 8)) = v;   // 8 consecutive k: one 16-byte unit
+    for (int i = 0; i < kB; ++i) {
+      const int idx = base + i * nthreads + tid;
+      rr[i] = idx / K8;
+      kk[i] = idx - rr[i] * K8;
+      if (idx < n) {
+        const uint4* vp = reinterpret_cast<const uint4*>(src + rr[i] * ld) + kk[i];
+        v[i] = cg ? __ldcg(vp) : *vp;                 // cg: rows written by other CTAs of this kernel
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kB; ++i) {
+      const int idx = base + i * nthreads + tid;
+      if (idx < n) {
+        const int r = rr[i], k8 = kk[i];
+        float f[8];
+        bf16x8_to_f32(v[i], f);
+        float mx = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(f[j]));
+        atomicMax(&redi[r], __float_as_int(mx));
+        *reinterpret_cast<uint4*>(xs + r * xs_stride(K) + xs_perm(k8 * 8)) = v[i];   // 8 consecutive k: one 16-byte unit
+      }
+    }
   }
   sync();
   for (int r = tid; r < rows; r += nthreads) {
@@ -165,7 +192,7 @@ __device__ __forceinline__ void stage_rows_f16(const bf16* __restrict__ src, int
     uint32_t h[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      __half2 v = __floats2half2_rn(ldexpf(f[2 * j], s), ldexpf(f[2 * j + 1], s));
+      __half2 v = __floats2half2_rn(scale_pow2(f[2 * j], s), scale_pow2(f[2 * j + 1], s));
       h[j] = *reinterpret_cast<uint32_t*>(&v);
     }
     *p = make_uint4(h[0], h[1], h[2], h[3]);
@@ -381,7 +408,7 @@ __device__ __forceinline__ void norm_stage_f16(const bf16* x, int64_t ldx, const
     uint32_t h[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      __half2 v = __floats2half2_rn(ldexpf(f[2 * j], s), ldexpf(f[2 * j + 1], s));
+      __half2 v = __floats2half2_rn(scale_pow2(f[2 * j], s), scale_pow2(f[2 * j + 1], s));
       h[j] = *reinterpret_cast<uint32_t*>(&v);
     }
     *p = make_uint4(h[0], h[1], h[2], h[3]);
@@ -464,8 +491,8 @@ __device__ __forceinline__ void norm_stage_f16_1w(const bf16* x, int64_t ldx, co
         uint32_t h[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          __half2 v = __floats2half2_rn(ldexpf(bf16_bits_to_f32(pk[m][j] & 0xFFFFu), s),
-                                        ldexpf(bf16_bits_to_f32(pk[m][j] >> 16), s));
+          __half2 v = __floats2half2_rn(scale_pow2(bf16_bits_to_f32(pk[m][j] & 0xFFFFu), s),
+                                        scale_pow2(bf16_bits_to_f32(pk[m][j] >> 16), s));
           h[j] = *reinterpret_cast<uint32_t*>(&v);
         }
         *reinterpret_cast<uint4*>(xs + m * xs_stride(H) + xs_perm(tid * 8)) = make_uint4(h[0], h[1], h[2], h[3]);

@@ -72,6 +72,7 @@ struct MoeBlockArgs {
   MoeBlockWs* ws;
   int peer_mode;                     // expert parallel with the fused peer exchange
   PeerSet peers;
+  L2Prefetch pf;                     // the next op's bytes, pulled into L2 during phase D
 };
 
 static size_t moe_block_ws_bytes(int E, int I) {
@@ -227,6 +228,7 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   const bool active = g == 0;
   int u0, nu;
   unit_range(u0, nu);
+  #pragma unroll 1
   for (int u = 0; u < nu; ++u) {
     if (!xsync_and(mbar_wait(&bar_up[u], 0, status))) break;
     const int unit = u0 + u, s = s_local[unit / jpe], j = unit - (unit / jpe) * jpe, e = s_ids[s] - a.e_lo;
@@ -234,6 +236,7 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
     float acc_g[4][4], acc_u[4][4];
     zero_acc(acc_g);
     zero_acc(acc_u);
+    #pragma unroll 1
     for (int ks = warp; ks < nks_u; ks += kXW) {
       consume_stage(b + ks * 2048, b + 2 * nks_u * 2048 + ks * 256, 0, g, t, ks, xrow, active, acc_g);
       consume_stage(b + (nks_u + ks) * 2048, b + 2 * nks_u * 2048 + (nks_u + ks) * 256, 0, g, t, ks, xrow, active, acc_u);
@@ -266,6 +269,8 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   }
   grid_sync(&ws->sync, nb, 1, kXT, 1, &s_ok, status);
   pdl_trigger();
+  // the next op's bytes into L2: HBM is idle from here on (the down weights were requested with the up units)
+  if (tid == 32) l2_prefetch_share(a.pf, cta, nb);
 
   // ---- D: this CTA's 16 output rows over every routed expert, then the slot-order sum ----
   if (has_dn) {
@@ -280,6 +285,7 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
         const __half* arow = xa + s * xs_stride(I);
         float acc[4][4];
         zero_acc(acc);
+        #pragma unroll 1
         for (int ks = 0; ks < nks_d; ++ks) consume_stage(b + ks * 2048, b + nks_d * 2048 + ks * 256, 0, g, t, ks, arow, act_col, acc);
         float d[4];
         sum_acc(acc, d);
@@ -359,8 +365,8 @@ static int moe_block_launch(const void* x, int64_t ldx, const void* res, const v
                             const void* gate_w, int64_t H, int64_t E, int64_t topk, int score_fn, const void* w13,
                             const void* s13, const float* g13, const void* w2, const void* s2, const float* g2, int64_t I,
                             int64_t e_lo, int64_t n_local, void* out, void* y_out, void* res_out, void* xn_out,
-                            float* logits_out, int32_t* topk_ids_out, float* topk_weights_out, void* workspace, int pdl,
-                            void* stream, const PeerSet* peers = nullptr) {
+                            float* logits_out, int32_t* topk_ids_out, float* topk_weights_out, void* workspace,
+                            const flint_l2_prefetch* next, int pdl, void* stream, const PeerSet* peers = nullptr) {
   if (!x || !norm_w || !gate_w || !w13 || !s13 || !g13 || !w2 || !s2 || !g2 || (!out && !y_out) || !workspace)
     return FLINT_ERR_ARGUMENT;
   if (peers && (!out || y_out)) return FLINT_ERR_ARGUMENT;
@@ -417,6 +423,7 @@ static int moe_block_launch(const void* x, int64_t ldx, const void* res, const v
     a.peer_mode = 1;
     a.peers = *peers;
   }
+  if (!l2_prefetch_pack(next, &a.pf)) return FLINT_ERR_ARGUMENT;
 
   // H = 2048: the single-pass norm keeps one 8-wide chunk per consumer thread
   void (*kern)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, MoeBlockArgs) = moe_block_kernel<8>;
@@ -442,19 +449,22 @@ extern "C" int flint_moe_block(const void* x, int64_t ldx, const void* res, cons
                                int64_t H, int64_t E, int64_t topk, int score_fn, const void* w13, const void* s13,
                                const float* g13, const void* w2, const void* s2, const float* g2, int64_t I, void* out,
                                void* res_out, void* xn_out, float* logits_out, int32_t* topk_ids_out,
-                               float* topk_weights_out, void* workspace, int pdl, void* stream) {
+                               float* topk_weights_out, void* workspace, const flint_l2_prefetch* next, int pdl,
+                               void* stream) {
   return moe_block_launch(x, ldx, res, norm_w, eps, gate_w, H, E, topk, score_fn, w13, s13, g13, w2, s2, g2, I, 0, E, out,
-                          nullptr, res_out, xn_out, logits_out, topk_ids_out, topk_weights_out, workspace, pdl, stream);
+                          nullptr, res_out, xn_out, logits_out, topk_ids_out, topk_weights_out, workspace, next, pdl,
+                          stream);
 }
 
 extern "C" int flint_moe_block_ep(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps,
                                   const void* gate_w, int64_t H, int64_t E, int64_t topk, int score_fn, const void* w13,
                                   const void* s13, const float* g13, const void* w2, const void* s2, const float* g2,
                                   int64_t I, int64_t expert_lo, int64_t n_local, void* y_out, float* topk_weights_out,
-                                  void* res_out, void* workspace, int pdl, void* stream) {
+                                  void* res_out, void* workspace, const flint_l2_prefetch* next, int pdl,
+                                  void* stream) {
   return moe_block_launch(x, ldx, res, norm_w, eps, gate_w, H, E, topk, score_fn, w13, s13, g13, w2, s2, g2, I, expert_lo,
-                          n_local, nullptr, y_out, res_out, nullptr, nullptr, nullptr, topk_weights_out, workspace, pdl,
-                          stream);
+                          n_local, nullptr, y_out, res_out, nullptr, nullptr, nullptr, topk_weights_out, workspace, next,
+                          pdl, stream);
 }
 
 extern "C" int flint_moe_combine(const void* y, const float* topk_weights, int64_t topk, int64_t H, void* out, int pdl,
@@ -469,10 +479,12 @@ extern "C" int flint_moe_block_peer(const void* x, int64_t ldx, const void* res,
                                     const void* gate_w, int64_t H, int64_t E, int64_t topk, int score_fn, const void* w13,
                                     const void* s13, const float* g13, const void* w2, const void* s2, const float* g2,
                                     int64_t I, int64_t expert_lo, int64_t n_local, const void* const* peers, int rank,
-                                    int world, void* out, void* res_out, void* workspace, int pdl, void* stream) {
+                                    int world, void* out, void* res_out, void* workspace, const flint_l2_prefetch* next,
+                                    int pdl, void* stream) {
   PeerSet ps;
   const int rc = peer_set(peers, rank, world, &ps);
   if (rc) return rc;
   return moe_block_launch(x, ldx, res, norm_w, eps, gate_w, H, E, topk, score_fn, w13, s13, g13, w2, s2, g2, I, expert_lo,
-                          n_local, out, nullptr, res_out, nullptr, nullptr, nullptr, nullptr, workspace, pdl, stream, &ps);
+                          n_local, out, nullptr, res_out, nullptr, nullptr, nullptr, nullptr, workspace, next, pdl, stream,
+                          &ps);
 }

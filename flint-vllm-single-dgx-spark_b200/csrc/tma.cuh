@@ -103,6 +103,39 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// ---- L2 prefetch of the next op's bytes (flint_l2_prefetch) ----
+struct L2Prefetch {
+  const uint8_t* ptr[8];
+  unsigned long long n16[8];           // 16-byte units of each range
+  int n;
+};
+
+// Host: validates and converts the ABI struct (NULL or n = 0: nothing); false on a bad range.
+inline bool l2_prefetch_pack(const flint_l2_prefetch* in, L2Prefetch* out) {
+  *out = L2Prefetch{};
+  if (!in || in->n == 0) return true;
+  if (in->n < 0 || in->n > 8) return false;
+  for (int r = 0; r < in->n; ++r) {
+    if (!in->ptr[r] || in->bytes[r] < 0 || (reinterpret_cast<uintptr_t>(in->ptr[r]) & 15)) return false;
+    out->ptr[r] = static_cast<const uint8_t*>(in->ptr[r]);
+    out->n16[r] = (unsigned long long)in->bytes[r] >> 4;
+  }
+  out->n = in->n;
+  return true;
+}
+
+// One thread: this CTA's 1/nb share of every range, as bulk L2 prefetches of at most 32 KB.
+__device__ __forceinline__ void l2_prefetch_share(const L2Prefetch& pf, int cta, int nb) {
+  for (int r = 0; r < pf.n; ++r) {
+    const unsigned long long lo = pf.n16[r] * cta / nb, hi = pf.n16[r] * (cta + 1) / nb;
+    for (unsigned long long u = lo; u < hi; u += 2048) {
+      const unsigned long long k = hi - u < 2048 ? hi - u : 2048;
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(pf.ptr[r] + u * 16), "r"((uint32_t)(k * 16))
+                   : "memory");
+    }
+  }
+}
+
 // ---- host: tensor-map encoding through the driver entry point (no libcuda link needed) ----
 int encode_u8_2d(CUtensorMap* map, const void* base, uint64_t cols_bytes, uint64_t rows, uint64_t row_stride_bytes,
                  uint32_t box_cols, uint32_t box_rows, bool swizzle128);

@@ -25,7 +25,7 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
-from . import ops as _ops  # noqa: F401
+from . import ops as _ops
 from .fp4moe_decode import DecodeWeights
 from .nvfp4 import random_nvfp4
 
@@ -137,7 +137,7 @@ class Decoder:
     """Batch-M (M <= 8) decode of a FlintModel: teacher-forced prompt processing and greedy generation."""
 
     def __init__(self, model: FlintModel, batch: int = 1, moe: str | None = None, attn: str = "block", group=None,
-                 exchange: str = "peer"):
+                 exchange: str = "peer", prefetch: bool = False):
         """moe: "block" (one launch, one token; the default at batch 1), "chain" (route, up, down: three launches;
         the default for 2..8 tokens) or "fused" (one persistent launch for 1..8 tokens); attn: "block" (QKV +
         attention + O in one persistent launch) or "chain" (three launches)."""
@@ -150,7 +150,7 @@ class Decoder:
             raise ValueError("a sharded model decodes one token with moe='block' and needs its process group")
         if exchange not in ("peer", "nccl"):
             raise ValueError(f"exchange must be 'peer' or 'nccl', got {exchange!r}")
-        self.group, self.exchange = group, exchange
+        self.group, self.exchange, self.prefetch = group, exchange, prefetch
         self.peers = None
         if model.world > 1 and exchange == "peer":
             from .peer import PeerBuffers
@@ -219,24 +219,31 @@ class Decoder:
                                                               self.seq_lens, None, 0, self.scale, self.attn,
                                                               self.splits)),
                    ("o", lambda: ops.attn_o(self.attn.view(self.M, -1), Po, So, gso, self.a))]
+        # prefetch=True: the MoE block pulls the next layer's attention weights into L2 while HBM would otherwise
+        # idle.  Off by default: measured in place it does not shorten the attention block (its critical path starts
+        # with the norm, not the weights) and it adds ~1 us to the MoE block.
+        pf = None
+        if self.prefetch and l + 1 < c.layers:
+            Ln = m.layers[l + 1]
+            pf = _ops.prefetch_ranges(Ln["qkv"][0], Ln["qkv"][1], Ln["o"][0], Ln["o"][1])
         if self.moe == "block" and m.world > 1 and self.peers is not None:
             pp = self.peers
             seq.append(("moe_block_peer", lambda: ops.moe_block_peer(
                 self.a, self.res_a, L["ln2"], c.rms_eps, L["gate"], c.topk, ew.score_fn, ew.w13, ew.s13, ew.g13, ew.w2,
-                ew.s2, ew.g2, m.e_lo, pp.ptrs, pp.rank, self.h, self.res_b)))
+                ew.s2, ew.g2, m.e_lo, pp.ptrs, pp.rank, self.h, self.res_b, pf)))
         elif self.moe == "block" and m.world > 1:
             import torch.distributed as dist
 
             def moe_ep():
                 ops.moe_block_ep(self.a, self.res_a, L["ln2"], c.rms_eps, L["gate"], c.topk, ew.score_fn, ew.w13, ew.s13,
-                                 ew.g13, ew.w2, ew.s2, ew.g2, m.e_lo, self.y_slots, self.tw, self.res_b)
+                                 ew.g13, ew.w2, ew.s2, ew.g2, m.e_lo, self.y_slots, self.tw, self.res_b, pf)
                 dist.all_reduce(self.y_slots, group=self.group)
                 ops.moe_combine(self.y_slots, self.tw, self.h)
             seq.append(("moe_block_ep", moe_ep))
         elif self.moe == "block":
             seq.append(("moe_block", lambda: ops.moe_block(self.a, self.res_a, L["ln2"], c.rms_eps, L["gate"], c.topk,
                                                            ew.score_fn, ew.w13, ew.s13, ew.g13, ew.w2, ew.s2, ew.g2, self.h,
-                                                           self.res_b, None, None, None, None)))
+                                                           self.res_b, None, None, None, None, pf)))
         elif self.moe == "fused":
             seq.append(("moe_fused", lambda: ops.moe_fused(self.a, self.res_a, L["ln2"], c.rms_eps, L["gate"], c.topk,
                                                            ew.score_fn, ew.w13, ew.s13, ew.g13, ew.w2, ew.s2, ew.g2,

@@ -253,9 +253,11 @@ def _(x, res, norm_w, eps, gate_w, topk, score_fn, w13, s13, g13, w2, s2, g2, ou
 def moe_block(x: torch.Tensor, res: torch.Tensor | None, norm_w: torch.Tensor, eps: float, gate_w: torch.Tensor, topk: int,
               score_fn: int, w13: torch.Tensor, s13: torch.Tensor, g13: torch.Tensor, w2: torch.Tensor, s2: torch.Tensor,
               g2: torch.Tensor, out: torch.Tensor, res_out: torch.Tensor | None, xn_out: torch.Tensor | None,
-              logits_out: torch.Tensor | None, ids_out: torch.Tensor | None, tw_out: torch.Tensor | None) -> None:
+              logits_out: torch.Tensor | None, ids_out: torch.Tensor | None, tw_out: torch.Tensor | None,
+              prefetch: list[int] | None = None) -> None:
     """The decode MoE block of ONE token in one launch (flint_moe_block).  The optional outputs are positional
-    without defaults (torch drops trailing default-valued arguments when it boxes a call)."""
+    without defaults (torch drops trailing default-valued arguments when it boxes a call).  prefetch: optional
+    (pointer, bytes) pairs the kernel pulls into L2 for the op that follows (prefetch_ranges)."""
     _lib.require_cuda(x, "moe_block")
     _bf16_2d(x, "moe_block x")
     M, H = x.shape
@@ -264,16 +266,17 @@ def moe_block(x: torch.Tensor, res: torch.Tensor | None, norm_w: torch.Tensor, e
         raise _lib.FlintError("moe_block: one token, shapes must match the expert weights")
     nbytes = lib().flint_moe_block_workspace_bytes(E, I2 // 2)
     ws = _lib.workspace(x.device, f"moe_block_{E}_{I2 // 2}", nbytes)
+    pf, pf_arg = _prefetch_arg(prefetch)
     rc = lib().flint_moe_block(ptr(x), x.stride(0), ptr(res), ptr(norm_w), float(eps), ptr(gate_w), H, E, topk, score_fn,
                                ptr(_u8(w13)), ptr(_u8(s13)), ptr(g13), ptr(_u8(w2)), ptr(_u8(s2)), ptr(g2), I2 // 2,
                                ptr(out), ptr(res_out), ptr(xn_out), ptr(logits_out), ptr(ids_out), ptr(tw_out), ptr(ws),
-                               PDL, stream_ptr(x.device))
+                               pf_arg, PDL, stream_ptr(x.device))
     check(rc, "flint_moe_block")
 
 
 @moe_block.register_fake
 def _(x, res, norm_w, eps, gate_w, topk, score_fn, w13, s13, g13, w2, s2, g2, out, res_out, xn_out, logits_out, ids_out,
-      tw_out):
+      tw_out, prefetch=None):
     return None
 
 
@@ -281,7 +284,7 @@ def _(x, res, norm_w, eps, gate_w, topk, score_fn, w13, s13, g13, w2, s2, g2, ou
 def moe_block_ep(x: torch.Tensor, res: torch.Tensor | None, norm_w: torch.Tensor, eps: float, gate_w: torch.Tensor,
                  topk: int, score_fn: int, w13: torch.Tensor, s13: torch.Tensor, g13: torch.Tensor, w2: torch.Tensor,
                  s2: torch.Tensor, g2: torch.Tensor, expert_lo: int, y_out: torch.Tensor, tw_out: torch.Tensor,
-                 res_out: torch.Tensor | None) -> None:
+                 res_out: torch.Tensor | None, prefetch: list[int] | None = None) -> None:
     """Expert-parallel one-token MoE block (flint_moe_block_ep): the local experts' rows of y_out [topk, H], zeros for
     the other ranks' slots, and the routing weights."""
     _lib.require_cuda(x, "moe_block_ep")
@@ -293,15 +296,17 @@ def moe_block_ep(x: torch.Tensor, res: torch.Tensor | None, norm_w: torch.Tensor
         raise _lib.FlintError("moe_block_ep: shapes do not match")
     nbytes = lib().flint_moe_block_workspace_bytes(E, I2 // 2)
     ws = _lib.workspace(x.device, f"moe_block_{E}_{I2 // 2}", nbytes)
+    pf, pf_arg = _prefetch_arg(prefetch)
     rc = lib().flint_moe_block_ep(ptr(x), x.stride(0), ptr(res), ptr(norm_w), float(eps), ptr(gate_w), H, E, topk,
                                   score_fn, ptr(_u8(w13)), ptr(_u8(s13)), ptr(g13), ptr(_u8(w2)), ptr(_u8(s2)), ptr(g2),
-                                  I2 // 2, int(expert_lo), n_local, ptr(y_out), ptr(tw_out), ptr(res_out), ptr(ws), PDL,
-                                  stream_ptr(x.device))
+                                  I2 // 2, int(expert_lo), n_local, ptr(y_out), ptr(tw_out), ptr(res_out), ptr(ws), pf_arg,
+                                  PDL, stream_ptr(x.device))
     check(rc, "flint_moe_block_ep")
 
 
 @moe_block_ep.register_fake
-def _(x, res, norm_w, eps, gate_w, topk, score_fn, w13, s13, g13, w2, s2, g2, expert_lo, y_out, tw_out, res_out):
+def _(x, res, norm_w, eps, gate_w, topk, score_fn, w13, s13, g13, w2, s2, g2, expert_lo, y_out, tw_out, res_out,
+      prefetch=None):
     return None
 
 
@@ -319,6 +324,32 @@ def _(y, tw, out):
     return None
 
 
+class _L2Prefetch(ctypes.Structure):
+    """flint_l2_prefetch (include/flint_b200.h)."""
+    _fields_ = [("ptr", ctypes.c_void_p * 8), ("bytes", ctypes.c_int64 * 8), ("n", ctypes.c_int32)]
+
+
+def _prefetch_arg(spec: list[int] | None):
+    """[ptr0, bytes0, ptr1, bytes1, ...] -> (struct kept alive by the caller, pointer argument) or (None, None)."""
+    if not spec:
+        return None, None
+    if len(spec) % 2 or len(spec) > 16:
+        raise _lib.FlintError("prefetch: up to 8 (pointer, bytes) pairs")
+    pf = _L2Prefetch()
+    pf.n = len(spec) // 2
+    for i in range(pf.n):
+        pf.ptr[i], pf.bytes[i] = spec[2 * i], spec[2 * i + 1]
+    return pf, ctypes.cast(ctypes.pointer(pf), ctypes.c_void_p)
+
+
+def prefetch_ranges(*tensors: torch.Tensor) -> list[int]:
+    """The flattened (pointer, bytes) list of whole tensors, for the ops' `prefetch` argument."""
+    out: list[int] = []
+    for t in tensors:
+        out += [t.data_ptr(), t.numel() * t.element_size()]
+    return out
+
+
 def _peer_array(peers: list[int]):
     return (ctypes.c_void_p * len(peers))(*peers)
 
@@ -327,7 +358,7 @@ def _peer_array(peers: list[int]):
 def moe_block_peer(x: torch.Tensor, res: torch.Tensor | None, norm_w: torch.Tensor, eps: float, gate_w: torch.Tensor,
                    topk: int, score_fn: int, w13: torch.Tensor, s13: torch.Tensor, g13: torch.Tensor, w2: torch.Tensor,
                    s2: torch.Tensor, g2: torch.Tensor, expert_lo: int, peers: list[int], rank: int, out: torch.Tensor,
-                   res_out: torch.Tensor | None) -> None:
+                   res_out: torch.Tensor | None, prefetch: list[int] | None = None) -> None:
     """Expert-parallel one-token MoE block with the exchange fused in (flint_moe_block_peer): every rank gets the
     full weighted expert sum in out [1, H].  peers: every rank's exchange buffer as mapped here (PeerBuffers.ptrs)."""
     _lib.require_cuda(x, "moe_block_peer")
@@ -339,15 +370,17 @@ def moe_block_peer(x: torch.Tensor, res: torch.Tensor | None, norm_w: torch.Tens
         raise _lib.FlintError("moe_block_peer: shapes do not match")
     nbytes = lib().flint_moe_block_workspace_bytes(E, I2 // 2)
     ws = _lib.workspace(x.device, f"moe_block_{E}_{I2 // 2}", nbytes)
+    pf, pf_arg = _prefetch_arg(prefetch)
     rc = lib().flint_moe_block_peer(ptr(x), x.stride(0), ptr(res), ptr(norm_w), float(eps), ptr(gate_w), H, E, topk,
                                     score_fn, ptr(_u8(w13)), ptr(_u8(s13)), ptr(g13), ptr(_u8(w2)), ptr(_u8(s2)), ptr(g2),
                                     I2 // 2, int(expert_lo), n_local, _peer_array(peers), int(rank), len(peers), ptr(out),
-                                    ptr(res_out), ptr(ws), PDL, stream_ptr(x.device))
+                                    ptr(res_out), ptr(ws), pf_arg, PDL, stream_ptr(x.device))
     check(rc, "flint_moe_block_peer")
 
 
 @moe_block_peer.register_fake
-def _(x, res, norm_w, eps, gate_w, topk, score_fn, w13, s13, g13, w2, s2, g2, expert_lo, peers, rank, out, res_out):
+def _(x, res, norm_w, eps, gate_w, topk, score_fn, w13, s13, g13, w2, s2, g2, expert_lo, peers, rank, out, res_out,
+      prefetch=None):
     return None
 
 

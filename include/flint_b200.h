@@ -37,6 +37,15 @@ enum {
   FLINT_ERR_SCRATCH = 7       /* request larger than the fixed scratch of an allocation-free entry point */
 };
 
+/* L2 prefetch hint: up to 8 device byte ranges (16-byte aligned; a tail below 16 bytes is skipped) that a kernel
+ * taking one prefetches into L2 for the op that follows it -- in a decode step, the next layer's weights, whose
+ * loads otherwise start only when the next kernel's blocks become resident.  Pure hint: no effect on results. */
+typedef struct flint_l2_prefetch {
+  const void* ptr[8];
+  int64_t bytes[8];
+  int32_t n;
+} flint_l2_prefetch;
+
 /* Library version (major*10000 + minor*100 + patch). */
 int flint_version(void);
 /* Human-readable name of an error code. */
@@ -161,13 +170,14 @@ int flint_moe_fused(const void* x, int64_t ldx, const void* res, const void* nor
  * work and the weighted sum needs no cross-CTA reduction.  Same arguments and outputs as flint_moe_fused at M = 1;
  * routing, xn, res_out and the down step have the bits of flint_moe_route / flint_moe_down, act matches
  * flint_moe_up to fp32 rounding.  H = 2048, E % 32 == 0, E <= 2 * SMs, topk <= 8, I % 256 == 0,
- * topk * I / 16 <= 3 * SMs.  workspace: flint_moe_block_workspace_bytes(E, I), zero-filled once, 256-byte aligned. */
+ * topk * I / 16 <= 3 * SMs.  workspace: flint_moe_block_workspace_bytes(E, I), zero-filled once, 256-byte aligned.
+ * next: optional L2 prefetch (NULL: none), issued once the expert weights are requested (HBM is idle after that). */
 int64_t flint_moe_block_workspace_bytes(int64_t E, int64_t I);
 int flint_moe_block(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, const void* gate_w,
                     int64_t H, int64_t E, int64_t topk, int score_fn, const void* w13, const void* s13, const float* g13,
                     const void* w2, const void* s2, const float* g2, int64_t I, void* out, void* res_out, void* xn_out,
-                    float* logits_out, int32_t* topk_ids_out, float* topk_weights_out, void* workspace, int pdl,
-                    void* stream);
+                    float* logits_out, int32_t* topk_ids_out, float* topk_weights_out, void* workspace,
+                    const flint_l2_prefetch* next, int pdl, void* stream);
 
 /* Expert-parallel form of flint_moe_block (the MoE of a model whose experts are split over ranks): this rank's
  * weights hold experts expert_lo .. expert_lo + n_local - 1 (w13 / s13 / g13 / w2 / s2 / g2 indexed by local
@@ -178,7 +188,8 @@ int flint_moe_block(const void* x, int64_t ldx, const void* res, const void* nor
 int flint_moe_block_ep(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, const void* gate_w,
                        int64_t H, int64_t E, int64_t topk, int score_fn, const void* w13, const void* s13, const float* g13,
                        const void* w2, const void* s2, const float* g2, int64_t I, int64_t expert_lo, int64_t n_local,
-                       void* y_out, float* topk_weights_out, void* res_out, void* workspace, int pdl, void* stream);
+                       void* y_out, float* topk_weights_out, void* res_out, void* workspace,
+                       const flint_l2_prefetch* next, int pdl, void* stream);
 /* out bf16 [H] = bf16(sum_s topk_weights[s] * y[s, :]) in slot order (fp32 FMA): the weighted expert sum of the
  * expert-parallel MoE. */
 int flint_moe_combine(const void* y, const float* topk_weights, int64_t topk, int64_t H, void* out, int pdl, void* stream);
@@ -208,7 +219,7 @@ int flint_moe_block_peer(const void* x, int64_t ldx, const void* res, const void
                          int64_t H, int64_t E, int64_t topk, int score_fn, const void* w13, const void* s13,
                          const float* g13, const void* w2, const void* s2, const float* g2, int64_t I, int64_t expert_lo,
                          int64_t n_local, const void* const* peers, int rank, int world, void* out, void* res_out,
-                         void* workspace, int pdl, void* stream);
+                         void* workspace, const flint_l2_prefetch* next, int pdl, void* stream);
 /* Vocabulary-shard argmax exchange: keys = this rank's M (<= 8) keys from flint_lm_head_nv4_shard; tokens int32 [M]
  * = the argmax over all ranks' shards (lowest id among the largest logits), -1 if a peer wait timed out. */
 int flint_argmax_keys_allmax_peer(const uint64_t* keys, int64_t M, const void* const* peers, int rank, int world,
