@@ -129,33 +129,29 @@ __device__ __forceinline__ uint32_t bpage_unit(uint32_t page, int box, int row, 
 
 // Resident NVFP4 GEMV: ng row groups x nks slices in shared memory (unit (gi, ks) codes at wc + (gi*nks+ks)*2048,
 // scales at wsc + (gi*nks+ks)*256); warp w takes slices w, w+8, ...; partial tiles to red[gi][w][16][8].
-template <int GMAX>
-__device__ __forceinline__ void gemv_resident(const uint8_t* wc, const uint8_t* wsc, int ng, int nks, const __half* xs, int K,
-                                              int M, float* red, int warp, int lane) {
+// One out-of-line copy serves both projections (QKV in phase A, O in phase C), so the O projection finds its code
+// already in the instruction caches.
+__device__ __noinline__ void gemv_resident(const uint8_t* wc, const uint8_t* wsc, int ng, int nks, const __half* xs, int K,
+                                           int M, float* red, int warp, int lane) {
   const int g = lane >> 2, t = lane & 3;
   const bool active = g < M;
   const __half* xrow = xs + (active ? g : 0) * xs_stride(K);
-  float acc[GMAX][4][4];
-#pragma unroll
-  for (int gi = 0; gi < GMAX; ++gi) zero_acc(acc[gi]);
-#pragma unroll
-  for (int gi = 0; gi < GMAX; ++gi) {
-    if (gi < ng)
-      for (int ks = warp; ks < nks; ks += kBW)
-        consume_stage(wc + (gi * nks + ks) * 2048, wsc + (gi * nks + ks) * 256, 0, g, t, ks, xrow, active, acc[gi]);
-  }
   const int r0 = tile_phi(g), r1 = r0 + 8, n0 = 2 * t, n1 = 2 * t + 1;
-#pragma unroll
-  for (int gi = 0; gi < GMAX; ++gi) {
-    if (gi < ng) {
-      float d[4];
-      sum_acc(acc[gi], d);
-      float* rt = red + (gi * kBW + warp) * 128;
-      rt[r0 * 8 + n0] = d[0];
-      rt[r0 * 8 + n1] = d[1];
-      rt[r1 * 8 + n0] = d[2];
-      rt[r1 * 8 + n1] = d[3];
-    }
+  // one row group at a time, slice loop rolled: the tile code appears once; the per-group sums are unchanged
+#pragma unroll 1
+  for (int gi = 0; gi < ng; ++gi) {
+    float acc[4][4];
+    zero_acc(acc);
+#pragma unroll 1
+    for (int ks = warp; ks < nks; ks += kBW)
+      consume_stage(wc + (gi * nks + ks) * 2048, wsc + (gi * nks + ks) * 256, 0, g, t, ks, xrow, active, acc);
+    float d[4];
+    sum_acc(acc, d);
+    float* rt = red + (gi * kBW + warp) * 128;
+    rt[r0 * 8 + n0] = d[0];
+    rt[r0 * 8 + n1] = d[1];
+    rt[r1 * 8 + n0] = d[2];
+    rt[r1 * 8 + n1] = d[3];
   }
 }
 
@@ -208,8 +204,10 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
   __shared__ int shift[8];
   __shared__ float red_n[kBW * 8 + 8];
   __shared__ int s_pf[8], s_npg[8], s_seq[8], s_start[8], s_pre[9];
+  // per segment (request x kv head): first page slot A in the flattened page list, first owning CTA, number of
+  // owning CTAs (partial records) and first record; plus the flattened page count P
+  __shared__ int s_segA[kBMaxSeg], s_first[kBMaxSeg], s_nparts[kBMaxSeg], s_recb[kBMaxSeg], s_P;
   __shared__ __align__(16) bf16 q_tile[8][kBD];
-  __shared__ float s_stat[2];
   __shared__ int s_ok;
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -292,27 +290,28 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
       pre += s_npg[b];
     }
     s_pre[M] = pre;
+    // CTA c owns flattened pages [c P / Geff, (c + 1) P / Geff); page L belongs to CTA ceil((L + 1) Geff / P) - 1.
+    // 32-bit arithmetic: the host keeps M * nkv * max_blocks * grid below 2^32.
+    const unsigned Pu = (unsigned)(a.nkv * pre), Gu = (unsigned)min(G, (int)Pu);
+    auto owner = [&](unsigned L) { return (int)(((L + 1u) * Gu + Pu - 1u) / Pu) - 1; };
+    int rb = 0;
+    for (int sg = 0; sg < M * a.nkv; ++sg) {
+      const int b = sg / a.nkv, n = s_npg[b];
+      const int A = a.nkv * s_pre[b] + (sg - b * a.nkv) * n;
+      s_segA[sg] = A;
+      s_first[sg] = n > 0 ? owner((unsigned)A) : 0;
+      s_nparts[sg] = n > 0 ? owner((unsigned)(A + n - 1)) - s_first[sg] + 1 : 0;
+      s_recb[sg] = rb;
+      rb += s_nparts[sg];
+    }
+    s_P = (int)Pu;
   }
   __syncthreads();
   const int S = M * a.nkv;
-  const int P = a.nkv * s_pre[M];
+  const int P = s_P;
   const int Geff = min(G, P);
-  const int lo = cta < Geff ? (int)((int64_t)cta * P / Geff) : P;
-  const int hi = cta < Geff ? (int)((int64_t)(cta + 1) * P / Geff) : P;
-  auto seg_start = [&](int s) { const int b = s / a.nkv; return a.nkv * s_pre[b] + (s - b * a.nkv) * s_npg[b]; };
-  auto owner = [&](int L) { return (int)(((int64_t)(L + 1) * Geff + P - 1) / P) - 1; };
-  // partial records: segment s owns n_parts(s) consecutive records from rec_base(s) (one per CTA touching it)
-  auto n_parts_of = [&](int s) {
-    const int n = s_npg[s / a.nkv];
-    if (n == 0) return 0;
-    const int A = seg_start(s);
-    return owner(A + n - 1) - owner(A) + 1;
-  };
-  auto rec_base = [&](int s) {
-    int r = 0;
-    for (int s2 = 0; s2 < s; ++s2) r += n_parts_of(s2);
-    return r;
-  };
+  const int lo = cta < Geff ? (int)((unsigned)cta * (unsigned)P / (unsigned)Geff) : P;
+  const int hi = cta < Geff ? (int)((unsigned)(cta + 1) * (unsigned)P / (unsigned)Geff) : P;
 
   if (warp == kBW) {
     // ---- producer: this CTA's pages, in the order the consumers take them, once the resident weights have landed
@@ -322,7 +321,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
       int j = 0;
       for (int s = 0; s < S; ++s) {
         const int b = s / a.nkv, kvh = s - b * a.nkv;
-        const int A = seg_start(s), from = max(A, lo), to = min(A + s_npg[b], hi);
+        const int A = s_segA[s], from = max(A, lo), to = min(A + s_npg[b], hi);
         const int* btb = a.bt + (int64_t)b * a.bt_stride;
         for (int L = from; L < to; ++L, ++j) {
           const int slot = j % a.np, round = j / a.np;
@@ -340,7 +339,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
   // ================= consumers (256 threads) =================
   // ---- A (second half): QKV rows ----
   if (ngq > 0 && cons_sync_and(mbar_wait(&bar_wq, 0, status))) {
-    gemv_resident<kBGQ>(wq, wq + a.wq_scale_off, ngq, a.nks_q, xs, a.H, M, red, warp, lane);
+    gemv_resident(wq, wq + a.wq_scale_off, ngq, a.nks_q, xs, a.H, M, red, warp, lane);
     cons_sync();
     gemv_finish(red, ngq, M, a.gs_qkv[0], shift, a.y, a.Nqkv, gq0 * 16);
   }
@@ -392,10 +391,10 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
   int j = 0;                                                       // CTA page sequence (matches the producer)
   for (int s = 0; s < S; ++s) {
     const int b = s / a.nkv, kvh = s - b * a.nkv;
-    const int A = seg_start(s), n = s_npg[b];
+    const int A = s_segA[s], n = s_npg[b];
     const int from = max(A, lo), to = min(A + n, hi);
     if (from >= to) continue;
-    const int c_first = owner(A), n_parts = owner(A + n - 1) - c_first + 1;
+    const int c_first = s_first[s], n_parts = s_nparts[s];
     const int seq = s_seq[b], start = s_start[b], last_page = (seq - 1) / kBPage;
     const bf16* yb = a.y + (int64_t)b * a.Nqkv;
     const float* cs = a.cos_sin ? a.cos_sin + a.positions[b] * a.cs_stride : nullptr;
@@ -566,7 +565,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
           *reinterpret_cast<uint4*>(a.attn + (int64_t)b * a.Ko + qh * kBD + d0) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
       } else {
-        float* rec = a.rec + (int64_t)(rec_base(s) + cta - c_first) * kBRecFloats;
+        float* rec = a.rec + (int64_t)(s_recb[s] + cta - c_first) * kBRecFloats;
         __stcg(reinterpret_cast<float4*>(rec + hh * kBD + d0), make_float4(oc[0], oc[1], oc[2], oc[3]));
         __stcg(reinterpret_cast<float4*>(rec + hh * kBD + d0) + 1, make_float4(oc[4], oc[5], oc[6], oc[7]));
         if ((tid & 15) == 0) __stcg(reinterpret_cast<float2*>(rec + 8 * kBD) + hh, make_float2(mc, lc));
@@ -576,71 +575,82 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
   }
   grid_sync(&a.ws->gs, G, 1, kBCons, 1, &s_ok, status);
 
-  // ---- B2: merge the partial records of split segments, one (segment, q head) per CTA at a time ----
+  // ---- B2: merge the partial records of split segments, one (segment, q head) per CTA at a time.  Warp w folds
+  // records r = w, w + 8, ... (loaded together: one memory round trip per 64 records) with the online softmax rule;
+  // the 8 warp results are then folded in warp order.  Fixed order throughout, so the result is deterministic. ----
   {
-    float* fr = reinterpret_cast<float*>(wq);                     // [256] m_r then f_r, [256] l_r, [8][128] partials
-    float* part = fr + 512;
+    constexpr int kMR = 8;                                         // records per warp per round
+    float* part = reinterpret_cast<float*>(wq);                    // [8 warps][128]
+    float* wml = part + kBW * kBD;                                 // [8 warps][2]: m, l
     for (int u = cta; u < S * a.Gq; u += G) {
       const int s = u / a.Gq, hh = u - s * a.Gq;
-      const int n = n_parts_of(s);
+      const int n = s_nparts[s];
       if (n <= 1) continue;                                        // written directly in phase B
       const int b = s / a.nkv, kvh = s - b * a.nkv;
-      const float* r0 = a.rec + (int64_t)rec_base(s) * kBRecFloats;
-      if (warp == 0) {                                             // m, weights and l of every record, fixed order
-        float mloc = -INFINITY;
-        for (int r = lane; r < n; r += 32) {
-          const float2 ml = __ldcg(reinterpret_cast<const float2*>(r0 + (int64_t)r * kBRecFloats + 8 * kBD) + hh);
-          fr[r] = ml.x;
-          fr[256 + r] = ml.y;
-          mloc = fmaxf(mloc, ml.x);
-        }
+      const float* r0 = a.rec + (int64_t)s_recb[s] * kBRecFloats;
+      const int d0 = lane * 4;
+      float m_w = -INFINITY, l_w = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+      for (int base = 0; base < n; base += kBW * kMR) {
+        float4 v[kMR];
+        float2 ml[kMR];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
-        __syncwarp();
-        float lsum = 0.f;
-        for (int r = lane; r < n; r += 32) {
-          const float m = fr[r];
-          const float f = m == -INFINITY ? 0.f : exp2f(m * c - mloc * c);
-          fr[r] = f;
-          lsum += fr[256 + r] * f;
+        for (int i = 0; i < kMR; ++i) {
+          const int r = base + warp + kBW * i;
+          if (r < n) {
+            const float* rec = r0 + (int64_t)r * kBRecFloats;
+            v[i] = __ldcg(reinterpret_cast<const float4*>(rec + hh * kBD + d0));
+            ml[i] = __ldcg(reinterpret_cast<const float2*>(rec + 8 * kBD) + hh);
+          } else {
+            v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            ml[i] = make_float2(-INFINITY, 0.f);
+          }
         }
+        float m_new = m_w;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
-        if (lane == 0) {
-          s_stat[0] = mloc;
-          s_stat[1] = lsum;
+        for (int i = 0; i < kMR; ++i) m_new = fmaxf(m_new, ml[i].x);
+        if (m_new != -INFINITY) {
+          const float sc = m_w == -INFINITY ? 0.f : exp2f(m_w * c - m_new * c);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[e] *= sc;
+          l_w *= sc;
+#pragma unroll
+          for (int i = 0; i < kMR; ++i) {
+            const float f = ml[i].x == -INFINITY ? 0.f : exp2f(ml[i].x * c - m_new * c);
+            acc[0] = fmaf(v[i].x, f, acc[0]);
+            acc[1] = fmaf(v[i].y, f, acc[1]);
+            acc[2] = fmaf(v[i].z, f, acc[2]);
+            acc[3] = fmaf(v[i].w, f, acc[3]);
+            l_w = fmaf(ml[i].y, f, l_w);
+          }
+          m_w = m_new;
         }
       }
-      cons_sync();
-      {                                                            // warp w: records r = w (mod 8), 4 dims per lane
-        const int d0 = lane * 4;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-        for (int r = warp; r < n; r += kBW) {
-          const float f = fr[r];
-          const float4 v = __ldcg(reinterpret_cast<const float4*>(r0 + (int64_t)r * kBRecFloats + hh * kBD + d0));
-          acc[0] += v.x * f;
-          acc[1] += v.y * f;
-          acc[2] += v.z * f;
-          acc[3] += v.w * f;
-        }
-        *reinterpret_cast<float4*>(part + warp * kBD + d0) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      *reinterpret_cast<float4*>(part + warp * kBD + d0) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      if (lane == 0) {
+        wml[2 * warp] = m_w;
+        wml[2 * warp + 1] = l_w;
       }
       cons_sync();
       if (tid < 32) {
-        const int d0 = tid * 4;
-        float ov[4] = {0.f, 0.f, 0.f, 0.f};
+        float m = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < kBW; ++w) {
-          const float4 v = *reinterpret_cast<const float4*>(part + w * kBD + d0);
-          ov[0] += v.x;
-          ov[1] += v.y;
-          ov[2] += v.z;
-          ov[3] += v.w;
+        for (int w = 0; w < kBW; ++w) m = fmaxf(m, wml[2 * w]);
+        float ov[4] = {0.f, 0.f, 0.f, 0.f}, den = 0.f;
+        if (m != -INFINITY) {
+#pragma unroll
+          for (int w = 0; w < kBW; ++w) {
+            const float mw = wml[2 * w];
+            const float f = mw == -INFINITY ? 0.f : exp2f(mw * c - m * c);
+            const float4 pv = *reinterpret_cast<const float4*>(part + w * kBD + d0);
+            ov[0] = fmaf(pv.x, f, ov[0]);
+            ov[1] = fmaf(pv.y, f, ov[1]);
+            ov[2] = fmaf(pv.z, f, ov[2]);
+            ov[3] = fmaf(pv.w, f, ov[3]);
+            den = fmaf(wml[2 * w + 1], f, den);
+          }
         }
         const int qh = kvh * a.Gq + hh;
-        const float m = s_stat[0];
-        float den = s_stat[1];
         if (a.sinks && m != -INFINITY) den += exp2f(a.sinks[qh] * kBLog2e - m * c);
         const float inv = den > 0.f ? 1.0f / den : 0.f;
         *reinterpret_cast<uint2*>(a.attn + (int64_t)b * a.Ko + qh * kBD + d0) =
@@ -656,7 +666,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
   if (ngo > 0) {
     stage_rows_f16(a.attn, a.Ko, M, a.Ko, xs_o, shift, red_n, kBCons, 1, true);
     if (cons_sync_and(mbar_wait(&bar_wo, 0, status))) {
-      gemv_resident<kBGO>(wo, wo + a.wo_scale_off, ngo, a.nks_o, xs_o, a.Ko, M, red, warp, lane);
+      gemv_resident(wo, wo + a.wo_scale_off, ngo, a.nks_o, xs_o, a.Ko, M, red, warp, lane);
       cons_sync();
       gemv_finish(red, ngo, M, a.gs_o[0], shift, a.out, a.ldr, go0 * 16);
     }
@@ -731,6 +741,9 @@ extern "C" int flint_attn_block(const void* x, int64_t ldx, const int32_t* token
     return FLINT_ERR_SHAPE;
   const int64_t Nqkv = (num_q_heads + 2 * num_kv_heads) * kBD, Ko = num_q_heads * kBD;
   if (Ko % kSliceK != 0 || Ko > 8192) return FLINT_ERR_SHAPE;
+  // the kernel's page partition runs in 32-bit arithmetic: pages x (grid + 1) must stay below 2^32
+  if ((uint64_t)M * (uint64_t)num_kv_heads * (uint64_t)max_blocks * (uint64_t)(sms + 1) >= (1ull << 32))
+    return FLINT_ERR_SHAPE;
   if (!aligned(x, 16) || ldx % 8 != 0 || ldr % 8 != 0 || (res && !aligned(res, 16)) || !aligned(norm_w, 16) ||
       !aligned(out, 16) || !aligned(res_out, 16) || !aligned(Wqkv, 16) || !aligned(Sqkv, 16) || !aligned(Wo, 16) ||
       !aligned(So, 16) || !aligned(kv_cache, 16) || stride_block % 8 != 0 || stride_head % 8 != 0 ||

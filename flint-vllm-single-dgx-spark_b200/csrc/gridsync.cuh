@@ -33,6 +33,7 @@ __device__ __forceinline__ bool grid_sync(GridSync* gs, unsigned nblocks, unsign
     asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(&gs->count) : "memory");
     const unsigned target = (k + 1) * nblocks;
     unsigned i = 0;
+#pragma unroll 1
     while ((int)(ld_acquire_u32(&gs->count) - target) < 0) {
       if (++i > FLINT_WAIT_LIMIT) {
         atomicOr(status, STATUS_WAIT_TIMEOUT);

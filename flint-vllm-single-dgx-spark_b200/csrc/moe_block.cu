@@ -109,10 +109,10 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   const int nks_u = H / kSliceK, nks_d = I / kSliceK, jpe = I / 16;
   const bool has_dn = cta < H / 16;
   // up units follow the local routed slots (known after top-k): unit u -> slot s_local[u / jpe], rows 16 (u % jpe)
-  auto unit_range = [&](int& u0, int& nu) {
-    const int U = s_nlocal * jpe;
-    u0 = (int)((int64_t)cta * U / nb);
-    nu = (int)((int64_t)(cta + 1) * U / nb) - u0;
+  auto unit_range = [&](int& u0, int& nu) {        // 32-bit: U <= 8 slots x I / 16 units, cta < 2^16
+    const unsigned U = (unsigned)(s_nlocal * jpe);
+    u0 = (int)((unsigned)cta * U / (unsigned)nb);
+    nu = (int)((unsigned)(cta + 1) * U / (unsigned)nb) - u0;
   };
   MoeBlockWs* ws = a.ws;
   unsigned* status = &ws->status;

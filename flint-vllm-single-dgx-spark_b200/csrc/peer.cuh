@@ -97,6 +97,7 @@ __device__ __forceinline__ bool peer_wait(const unsigned* flag, unsigned epoch, 
   if (ld_relaxed_sys_u32(&own->status) & STATUS_PEER_TIMEOUT) return false;
   const unsigned long long t0 = global_ns();
   unsigned i = 0;
+#pragma unroll 1
   while ((int)(ld_acquire_sys_u32(flag) - epoch) < 0) {
     if ((++i & 255u) == 0 && (global_ns() - t0 > kPeerWaitNs || i > (1u << 30))) {
       atomicOr(&own->status, STATUS_PEER_TIMEOUT);

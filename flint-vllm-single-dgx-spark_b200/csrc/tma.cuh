@@ -48,6 +48,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
 }
 // Bounded wait for the phase of the given parity; returns false (and sets *status) on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, unsigned* status) {
+#pragma unroll 1
   for (unsigned i = 0; i < FLINT_WAIT_LIMIT; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   if (status) atomicOr(status, STATUS_WAIT_TIMEOUT);
