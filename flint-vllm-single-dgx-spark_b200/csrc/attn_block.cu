@@ -24,6 +24,7 @@
 //  C  every CTA stages the attention output as f16 and computes its O rows from the resident weights.
 #include "common.cuh"
 #include "gridsync.cuh"
+#include "tagged.cuh"
 #include "nvfp4_tile.cuh"
 #include "runtime.cuh"
 #include "tma.cuh"
@@ -49,9 +50,10 @@ constexpr float kBLog2e = 1.4426950408889634f;
 struct BlockWs {
   GridSync gs;
   unsigned status;
-  unsigned pad[31];
+  unsigned epoch;                    // launches so far: this launch tags its published words with epoch + 1
+  unsigned pad[30];
   unsigned seg_cnt[kBMaxSeg];
-  // followed by: y bf16 [8][Nqkv], attention output bf16 [8][Ko], partial records
+  // followed by: y bf16 [8][Nqkv], attention output as tagged words [8][Ko / 2], partial records
 };
 
 struct BlockArgs {
@@ -85,7 +87,8 @@ struct BlockArgs {
   bf16* out;
   bf16* res_out;
   bf16* q_out;                       // optional
-  bf16* attn;                        // attention output [M][Ko] (caller's or workspace)
+  bf16* attn;                        // optional plain copy of the attention output [M][Ko] (the caller's)
+  unsigned long long* attn_tag;      // workspace: attention output as tagged words [8][Ko / 2] (tagged.cuh)
   bf16* y;                           // workspace: raw QKV output [8][Nqkv]
   float* rec;                        // workspace: partial records
   int gq_total, go_total;            // row groups of 16
@@ -187,6 +190,14 @@ __device__ __forceinline__ void head_norm_rope(float (&v)[4], const bf16* w, flo
   }
 }
 
+// attention output of request b, columns col .. col + 2 n - 1 (n bf16 pairs, col even): tagged words for the O
+// projection of this launch, plus the caller's plain copy when one was asked for
+__device__ __forceinline__ void publish_attn(const BlockArgs& a, unsigned ep, int b, int col, const uint32_t* pk, int n) {
+  for (int i = 0; i < n; ++i) st_tagged(a.attn_tag + (int64_t)b * (a.Ko / 2) + col / 2 + i, ep, pk[i]);
+  if (a.attn)
+    for (int i = 0; i < n; ++i) reinterpret_cast<uint32_t*>(a.attn + (int64_t)b * a.Ko + col)[i] = pk[i];
+}
+
 __device__ __forceinline__ float ldcg_bf16(const bf16* p) {
   return bf16_bits_to_f32(__ldcg(reinterpret_cast<const unsigned short*>(p)));
 }
@@ -200,7 +211,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
                   const __grid_constant__ CUtensorMap mkv, const BlockArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t full[kBMaxSlots], empty[kBMaxSlots], bar_wq, bar_wo;
+  __shared__ uint64_t full[kBMaxSlots], empty[kBMaxSlots], bar_wq, bar_wo, bar_tab;
   __shared__ int shift[8];
   __shared__ float red_n[kBW * 8 + 8];
   __shared__ int s_pf[8], s_npg[8], s_seq[8], s_start[8], s_pre[9];
@@ -231,6 +242,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
     }
     mbar_init(&bar_wq, 1);
     mbar_init(&bar_wo, 1);
+    mbar_init(&bar_tab, 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -258,6 +270,9 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
     }
   }
   pdl_wait();
+  unsigned ep;                                         // this launch's tag (the last CTA to retire advances it)
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(ep) : "l"(&a.ws->epoch) : "memory");
+  ep += 1u;
   // ---- A (first half): add + RMSNorm.  It runs before the page partition and before any page is requested, so its
   // loads of x / res are not queued behind the KV stream; the sequence lengths load alongside. ----
   const int my_seq = (int)threadIdx.x < M ? a.seq_lens[threadIdx.x] : 0;
@@ -290,21 +305,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
       pre += s_npg[b];
     }
     s_pre[M] = pre;
-    // CTA c owns flattened pages [c P / Geff, (c + 1) P / Geff); page L belongs to CTA ceil((L + 1) Geff / P) - 1.
-    // 32-bit arithmetic: the host keeps M * nkv * max_blocks * grid below 2^32.
-    const unsigned Pu = (unsigned)(a.nkv * pre), Gu = (unsigned)min(G, (int)Pu);
-    auto owner = [&](unsigned L) { return (int)(((L + 1u) * Gu + Pu - 1u) / Pu) - 1; };
-    int rb = 0;
-    for (int sg = 0; sg < M * a.nkv; ++sg) {
-      const int b = sg / a.nkv, n = s_npg[b];
-      const int A = a.nkv * s_pre[b] + (sg - b * a.nkv) * n;
-      s_segA[sg] = A;
-      s_first[sg] = n > 0 ? owner((unsigned)A) : 0;
-      s_nparts[sg] = n > 0 ? owner((unsigned)(A + n - 1)) - s_first[sg] + 1 : 0;
-      s_recb[sg] = rb;
-      rb += s_nparts[sg];
-    }
-    s_P = (int)Pu;
+    s_P = a.nkv * pre;
   }
   __syncthreads();
   const int S = M * a.nkv;
@@ -314,6 +315,42 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
   const int hi = cta < Geff ? (int)((unsigned)(cta + 1) * (unsigned)P / (unsigned)Geff) : P;
 
   if (warp == kBW) {
+    // ---- producer, first: the segment tables (lane sg and sg + 32), off the consumers' critical path; they are
+    // released to the consumers through bar_tab.  CTA c owns flattened pages [c P / Geff, (c + 1) P / Geff); page L
+    // belongs to CTA ceil((L + 1) Geff / P) - 1 (32-bit: the host keeps M * nkv * max_blocks * grid below 2^32). ----
+    {
+      const unsigned Pu = (unsigned)P, Gu = (unsigned)Geff;
+      auto owner = [&](unsigned L) { return (int)(((L + 1u) * Gu + Pu - 1u) / Pu) - 1; };
+      int np[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int sg = lane + 32 * h;
+        np[h] = 0;
+        if (sg < S) {
+          const int b = sg / a.nkv, n = s_npg[b];
+          const int A = a.nkv * s_pre[b] + (sg - b * a.nkv) * n;
+          const int first = n > 0 ? owner((unsigned)A) : 0;
+          np[h] = n > 0 ? owner((unsigned)(A + n - 1)) - first + 1 : 0;
+          s_segA[sg] = A;
+          s_first[sg] = first;
+          s_nparts[sg] = np[h];
+        }
+      }
+      int inc0 = np[0], inc1 = np[1];                              // record bases: exclusive scan in segment order
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v0 = __shfl_up_sync(0xffffffffu, inc0, o), v1 = __shfl_up_sync(0xffffffffu, inc1, o);
+        if (lane >= o) {
+          inc0 += v0;
+          inc1 += v1;
+        }
+      }
+      const int tot0 = __shfl_sync(0xffffffffu, inc0, 31);
+      if (lane < S) s_recb[lane] = inc0 - np[0];
+      if (lane + 32 < S) s_recb[lane + 32] = tot0 + inc1 - np[1];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_tab);
+    }
     // ---- producer: this CTA's pages, in the order the consumers take them, once the resident weights have landed
     // (they are needed first; the pages then stream in under the QKV GEMV and the barrier) ----
     if (lane == 0) {
@@ -344,6 +381,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
     gemv_finish(red, ngq, M, a.gs_qkv[0], shift, a.y, a.Nqkv, gq0 * 16);
   }
   grid_sync(&a.ws->gs, G, 0, kBCons, 1, &s_ok, status);
+  const bool have_tab = cons_sync_and(mbar_wait(&bar_tab, 0, status));   // segment tables from the producer warp
 
   // ---- B: attention ----
   const int tid = threadIdx.x, g = lane >> 2, t4 = lane & 3;
@@ -357,7 +395,8 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
     if (s_npg[b] != 0) continue;
     if (tid < a.Gq * 16) {
       const int hh = tid >> 4, d0 = (tid & 15) * 8;
-      *reinterpret_cast<uint4*>(a.attn + (int64_t)b * a.Ko + (kvh * a.Gq + hh) * kBD + d0) = make_uint4(0u, 0u, 0u, 0u);
+      const uint32_t zero[4] = {0u, 0u, 0u, 0u};
+      publish_attn(a, ep, b, (kvh * a.Gq + hh) * kBD + d0, zero, 4);
     }
     if (a.q_out && warp < a.Gq) {                                 // q of the empty request still goes out
       const int qh = kvh * a.Gq + warp;
@@ -389,7 +428,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
   }
 
   int j = 0;                                                       // CTA page sequence (matches the producer)
-  for (int s = 0; s < S; ++s) {
+  for (int s = 0; have_tab && s < S; ++s) {
     const int b = s / a.nkv, kvh = s - b * a.nkv;
     const int A = s_segA[s], n = s_npg[b];
     const int from = max(A, lo), to = min(A + n, hi);
@@ -562,7 +601,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
           uint32_t pk[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) pk[i] = pack_bf16x2(oc[2 * i] * inv, oc[2 * i + 1] * inv);
-          *reinterpret_cast<uint4*>(a.attn + (int64_t)b * a.Ko + qh * kBD + d0) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          publish_attn(a, ep, b, qh * kBD + d0, pk, 4);
         }
       } else {
         float* rec = a.rec + (int64_t)(s_recb[s] + cta - c_first) * kBRecFloats;
@@ -582,7 +621,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
     constexpr int kMR = 8;                                         // records per warp per round
     float* part = reinterpret_cast<float*>(wq);                    // [8 warps][128]
     float* wml = part + kBW * kBD;                                 // [8 warps][2]: m, l
-    for (int u = cta; u < S * a.Gq; u += G) {
+    for (int u = cta; have_tab && u < S * a.Gq; u += G) {
       const int s = u / a.Gq, hh = u - s * a.Gq;
       const int n = s_nparts[s];
       if (n <= 1) continue;                                        // written directly in phase B
@@ -653,25 +692,25 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
         const int qh = kvh * a.Gq + hh;
         if (a.sinks && m != -INFINITY) den += exp2f(a.sinks[qh] * kBLog2e - m * c);
         const float inv = den > 0.f ? 1.0f / den : 0.f;
-        *reinterpret_cast<uint2*>(a.attn + (int64_t)b * a.Ko + qh * kBD + d0) =
-            make_uint2(pack_bf16x2(ov[0] * inv, ov[1] * inv), pack_bf16x2(ov[2] * inv, ov[3] * inv));
+        const uint32_t pk[2] = {pack_bf16x2(ov[0] * inv, ov[1] * inv), pack_bf16x2(ov[2] * inv, ov[3] * inv)};
+        publish_attn(a, ep, b, qh * kBD + d0, pk, 2);
       }
       cons_sync();
     }
   }
-  grid_sync(&a.ws->gs, G, 2, kBCons, 1, &s_ok, status);
   pdl_trigger();
 
   // ---- C: O projection from the resident weights ----
   if (ngo > 0) {
-    stage_rows_f16(a.attn, a.Ko, M, a.Ko, xs_o, shift, red_n, kBCons, 1, true);
+    // the attention output of every head, once all its words carry this launch's tag (no grid barrier)
+    stage_rows_f16_tagged(a.attn_tag, M, a.Ko, ep, xs_o, shift, red_n, kBCons, 1, status);
     if (cons_sync_and(mbar_wait(&bar_wo, 0, status))) {
       gemv_resident(wo, wo + a.wo_scale_off, ngo, a.nks_o, xs_o, a.Ko, M, red, warp, lane);
       cons_sync();
       gemv_finish(red, ngo, M, a.gs_o[0], shift, a.out, a.ldr, go0 * 16);
     }
   }
-  grid_sync_retire(&a.ws->gs, G);
+  grid_sync_retire(&a.ws->gs, G, &a.ws->epoch);
 }
 
 struct BlockLayout {
@@ -709,7 +748,8 @@ static BlockLayout block_layout(int M, int H, int Ko, int gq_per, int go_per, in
 }
 
 static size_t block_ws_bytes(int64_t Nqkv, int64_t Ko, int sms) {
-  return sizeof(BlockWs) + (size_t)8 * Nqkv * 2 + (size_t)8 * Ko * 2 + (size_t)(sms + kBMaxSeg) * kBRecFloats * 4 + 256;
+  return sizeof(BlockWs) + (size_t)8 * Nqkv * 2 + (size_t)8 * (Ko / 2) * 8 + (size_t)(sms + kBMaxSeg) * kBRecFloats * 4 +
+         512;
 }
 
 }  // namespace flint
@@ -788,9 +828,9 @@ extern "C" int flint_attn_block(const void* x, int64_t ldx, const int32_t* token
   a.c = scale * kBLog2e; a.Ko = (int)Ko; a.No = (int)n_o; a.gs_o = gs_o; a.out = (bf16*)out; a.res_out = (bf16*)res_out;
   a.q_out = (bf16*)q_out;
   a.y = reinterpret_cast<bf16*>(wsb + sizeof(BlockWs));
-  bf16* ws_attn = a.y + 8 * Nqkv;
-  a.attn = attn_out ? (bf16*)attn_out : ws_attn;
-  a.rec = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(ws_attn + 8 * Ko) + 255) & ~uintptr_t(255));
+  a.attn_tag = reinterpret_cast<unsigned long long*>((reinterpret_cast<uintptr_t>(a.y + 8 * Nqkv) + 255) & ~uintptr_t(255));
+  a.attn = (bf16*)attn_out;
+  a.rec = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(a.attn_tag + 8 * (Ko / 2)) + 255) & ~uintptr_t(255));
   a.gq_total = gq_total; a.go_total = go_total; a.nks_q = nks_q; a.nks_o = nks_o; a.np = L.np;
   a.off_ring = (uint32_t)L.ring_off; a.off_wo = (uint32_t)L.wo_off; a.off_xs = (uint32_t)L.xs_off;
   a.off_red = (uint32_t)L.red_off;

@@ -47,14 +47,16 @@ __device__ __forceinline__ bool grid_sync(GridSync* gs, unsigned nblocks, unsign
   return *s_ok != 0;
 }
 
-// Thread 0 of every CTA, after its last grid_sync of the launch.  `bump` (optional): a launch counter the last CTA
-// increments (every CTA has read it by then).
-__device__ __forceinline__ void grid_sync_retire(GridSync* gs, unsigned nblocks, unsigned* bump = nullptr) {
+// Thread 0 of every CTA, after its last grid_sync of the launch.  `bump`, `bump2` (optional): launch counters the
+// last CTA increments (every CTA has read them by then).
+__device__ __forceinline__ void grid_sync_retire(GridSync* gs, unsigned nblocks, unsigned* bump = nullptr,
+                                                 unsigned* bump2 = nullptr) {
   if (threadIdx.x != 0) return;
   if (atomicAdd(&gs->retired, 1u) == nblocks - 1) {
     atomicExch(&gs->count, 0u);
     atomicExch(&gs->retired, 0u);
     if (bump) atomicAdd(bump, 1u);
+    if (bump2) atomicAdd(bump2, 1u);
   }
 }
 

@@ -1,17 +1,17 @@
 // (1) MoE decode block for one token: router + top-k, NVFP4 gate/up GEMV + SwiGLU, NVFP4 down GEMV and the
-// weighted expert sum in ONE cooperative launch (one CTA per SM, two grid barriers).  Replaces the reference's
+// weighted expert sum in ONE cooperative launch (one CTA per SM, no grid barrier: the router logits and the
+// activations cross between CTAs as epoch-tagged words, tagged.cuh).  Replaces the reference's
 // route_norm_kernel -> up_mar -> down_mar chain (fast/fp4moe_mar.cu:311-417, 67-152, 157-233; driven by
 // fast/model.py:302-310) at batch 1, where every routed expert is distinct (topk <= 8).
 //
 //  R  every CTA: s = x + res, xn = bf16(RMSNorm(s)) in one register pass (CTA 0 publishes res_out / xn); CTAs own
-//     router rows e = cta, cta + grid (prefetched into registers before the PDL wait) and write bf16 logits.
-//                                                                                            -- grid barrier --
-//  U  every CTA: top-k from the logits (redundant, identical everywhere).  The TMA producer then loads, in one go,
+//     router rows e = cta, cta + grid (prefetched into registers before the PDL wait) and publish bf16 logits.
+//  U  every CTA: top-k from the logits once all carry this launch's tag (redundant, identical everywhere).  The TMA producer then loads, in one go,
 //     the CTA's share of the up work (units of 16 gate + 16 up rows x H, balanced over the CTAs) and its down block
 //     (16 output rows of every routed expert) into shared memory; the down weights land while the up units run.
 //     Per unit the 8 warps split K, the partial tiles are summed in warp order and act = bf16(silu(g) * u) is
-//     written to the workspace.                                                               -- grid barrier --
-//  D  CTA c < H/16: warp s computes y_s = bf16(act_s . W2[e_s] * gs2[e_s]) for the block's 16 rows (one 16-row
+//     published to the workspace.
+//  D  CTA c < H/16, once the act rows of the routed slots carry this launch's tag: warp s computes y_s = bf16(act_s . W2[e_s] * gs2[e_s]) for the block's 16 rows (one 16-row
 //     tile over all of I, the accumulation order of moe_down), then out = bf16(sum_s tw_s * y_s) in slot order.
 //
 // Routing, xn, res_out and the down step have the bits of flint_moe_route / flint_moe_down; the gate/up sums split
@@ -32,6 +32,7 @@
 #include "gridsync.cuh"
 #include "moe_common.cuh"
 #include "peer.cuh"
+#include "tagged.cuh"
 #include "runtime.cuh"
 
 #include <algorithm>
@@ -46,8 +47,9 @@ constexpr int kXMaxSlots = 8;           // routed experts
 struct MoeBlockWs {
   GridSync sync;
   unsigned status;
-  unsigned pad[31];
-  // followed by: logits fp32 [E], act bf16 [8][I]
+  unsigned epoch;                       // launches so far: the tag of this launch's published words is epoch + 1
+  unsigned pad[30];
+  // followed by: logits as tagged words [E] (data = fp32 bits), act as tagged words [8][I / 2] (data = bf16 pair)
 };
 
 struct MoeBlockArgs {
@@ -76,7 +78,7 @@ struct MoeBlockArgs {
 };
 
 static size_t moe_block_ws_bytes(int E, int I) {
-  return sizeof(MoeBlockWs) + (size_t)E * 4 + (size_t)kXMaxSlots * I * 2 + 256;
+  return sizeof(MoeBlockWs) + (size_t)E * 8 + (size_t)kXMaxSlots * (I / 2) * 8 + 256;
 }
 
 __device__ __forceinline__ void xsync() { asm volatile("bar.sync 1, %0;" ::"r"(kXT) : "memory"); }
@@ -101,7 +103,6 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   __shared__ float red_n[kXW * 8 + 8];
   __shared__ float ybuf[kXMaxSlots][16];
   __shared__ int s_local[kXMaxSlots], s_nlocal;
-  __shared__ int s_ok;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nb = gridDim.x, cta = blockIdx.x;
@@ -116,8 +117,8 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   };
   MoeBlockWs* ws = a.ws;
   unsigned* status = &ws->status;
-  float* lg = reinterpret_cast<float*>(ws + 1);
-  bf16* act_g = reinterpret_cast<bf16*>(lg + E);
+  unsigned long long* lg = reinterpret_cast<unsigned long long*>(ws + 1);    // tagged logits
+  unsigned long long* act_g = lg + E;                                         // tagged act pairs
   uint8_t* up_base = smem;                              // [unit][gate codes | up codes | gate scales | up scales]
   uint8_t* dn_base = smem + a.off_dn;                   // [slot][codes | scales]
   bf16* xnb = reinterpret_cast<bf16*>(smem + a.off_xn);
@@ -179,6 +180,10 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   }
 
   // ================= consumers =================
+  // this launch's tag for the words it publishes (the last CTA to retire advances ws->epoch)
+  unsigned ep;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(ep) : "l"(&ws->epoch) : "memory");
+  ep += 1u;
   // ---- R: norm, router rows ----
   add_rmsnorm_1pass(a.x, a.ldx, a.res, a.nw, a.eps, 1, H, xnb, cta == 0 ? a.res_out : nullptr,
                     cta == 0 ? a.xn_out : nullptr, red_n, kXT, 1);
@@ -195,16 +200,40 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) __stcg(lg + my_row, bf16r(acc));
+    if (lane == 0) st_tagged(lg + my_row, ep, __float_as_uint(bf16r(acc)));
   }
   stage_rows_f16(xnb, H, 1, H, xs, shift_x, red_n, kXT, 1);
-  grid_sync(&ws->sync, nb, 0, kXT, 1, &s_ok, status);
 
-  // ---- U: top-k, then the up units ----
+  // ---- U: top-k once every CTA's router rows carry this launch's tag (no grid barrier), then the up units ----
   if (warp == 0) {
+    constexpr int PER = 8;                              // E <= 256
+    const int per = E / 32;
+    float lv[PER];
+    unsigned need = 0, got = 0;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      lv[j] = 0.f;
+      if (j < per) need |= 1u << j;
+    }
+#pragma unroll 1
+    for (unsigned it = 0; __any_sync(0xffffffffu, got != need); ++it) {
+      if (it == FLINT_WAIT_LIMIT) {
+        atomicOr(status, STATUS_WAIT_TIMEOUT);
+        break;
+      }
+#pragma unroll
+      for (int j = 0; j < PER; ++j)
+        if ((need & ~got) & (1u << j)) {
+          const unsigned long long w = ld_tagged(lg + lane + 32 * j);
+          if (tag_is(w, ep)) {
+            lv[j] = __uint_as_float((uint32_t)w);
+            got |= 1u << j;
+          }
+        }
+    }
     int my_e;
     float my_w;
-    warp_topk(lg, E, topk, a.score_fn, lane, my_e, my_w);
+    warp_topk_regs<PER>(lv, per, topk, a.score_fn, lane, my_e, my_w);
     if (lane < topk) {
       s_ids[lane] = my_e;
       s_tw[lane] = my_w;
@@ -218,9 +247,9 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
     if (loc) s_local[__popc(lm & ((1u << lane) - 1u))] = lane;
     if (lane == 0) s_nlocal = __popc(lm);
   }
-  if (cta == 0 && a.logits_out)
-    for (int i = tid; i < E; i += kXT) a.logits_out[i] = __ldcg(lg + i);
   xsync();
+  if (cta == 0 && a.logits_out)                         // every tag was seen by warp 0 before the xsync
+    for (int i = tid; i < E; i += kXT) a.logits_out[i] = __uint_as_float((uint32_t)ld_tagged(lg + i));
   if (tid == 0) mbar_arrive(&bar_plan);                 // release the producer
 
   const int g = lane >> 2, t = lane & 3;
@@ -262,19 +291,20 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
       const float sc = ldexpf(a.g13[e], -shift_x[0]);
       const float gv = gs * sc, uv = us * sc;
       const float silu = gv / (1.0f + expf(-gv));
-      __stcg(reinterpret_cast<unsigned short*>(act_g + (int64_t)s * I + j * 16 + tid),
-             __bfloat16_as_ushort(__float2bfloat16_rn(silu * uv)));
+      const unsigned vb = __bfloat16_as_ushort(__float2bfloat16_rn(silu * uv));
+      const unsigned hi = __shfl_down_sync(0x0000ffffu, vb, 1);   // act pair (2i, 2i+1) -> one tagged word
+      if ((tid & 1) == 0) st_tagged(act_g + (int64_t)s * (I / 2) + (j * 16 + tid) / 2, ep, vb | (hi << 16));
     }
     xsync();
   }
-  grid_sync(&ws->sync, nb, 1, kXT, 1, &s_ok, status);
   pdl_trigger();
   // the next op's bytes into L2: HBM is idle from here on (the down weights were requested with the up units)
   if (tid == 32) l2_prefetch_share(a.pf, cta, nb);
 
   // ---- D: this CTA's 16 output rows over every routed expert, then the slot-order sum ----
   if (has_dn) {
-    stage_rows_f16(act_g, I, topk, I, xa, shift_a, red_n, kXT, 1, true);
+    // the act rows of the local slots, once their words carry this launch's tag (no grid barrier)
+    stage_rows_f16_tagged(act_g, s_nlocal, I, ep, xa, shift_a, red_n, kXT, 1, status, s_local);
     if (s_nlocal == 0 || xsync_and(mbar_wait(&bar_dn, 0, status))) {
       if (warp < topk && (s_ids[warp] < a.e_lo || s_ids[warp] >= a.e_hi)) {
         if (lane < 16) ybuf[warp][lane] = 0.f;           // expert of another rank
@@ -338,7 +368,7 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
       }
     }
   }
-  grid_sync_retire(&ws->sync, nb, a.peer_mode ? &peer_header(a.peers.base[a.peers.rank])->moe_epoch : nullptr);
+  grid_sync_retire(&ws->sync, nb, &ws->epoch, a.peer_mode ? &peer_header(a.peers.base[a.peers.rank])->moe_epoch : nullptr);
 }
 
 // out[r] = bf16(sum_s tw[s] * y[s][r]) in slot order (the weighted sum of flint_moe_block after an expert-parallel
@@ -374,7 +404,7 @@ static int moe_block_launch(const void* x, int64_t ldx, const void* res, const v
   if (e_lo < 0 || n_local < 1 || e_lo + n_local > E || (y_out && !topk_weights_out)) return FLINT_ERR_ARGUMENT;
   const int sms = num_sms();
   if (sms <= 0) return FLINT_ERR_DEVICE;
-  if (H != 2048 || E < 32 || E % 32 != 0 || E > kMaxExperts || E > 2 * sms || topk < 1 ||
+  if (H != 2048 || E < 32 || E % 32 != 0 || E > 256 || E > 2 * sms || topk < 1 || topk * (I / 8) > 4 * kXT ||
       topk > kXMaxSlots || topk > E || I < kSliceK || I % kSliceK != 0 || ldx < H || score_fn < 0 || score_fn > 1 ||
       H / 16 > sms)
     return FLINT_ERR_SHAPE;

@@ -47,6 +47,48 @@ __device__ __forceinline__ void warp_topk(const float* logits, int E, int topk, 
   my_w = my_p / sum;
 }
 
+// warp_topk for logits already in registers (lane holds lv[j] = logit of expert lane + 32 j, j < per <= PER), with
+// the same keys, order, weights and bits: each lane sorts its keys once, then every round is one redux.sync max over
+// the lane heads and a pop on the winning lane; the scores are evaluated afterwards in parallel and summed in round
+// order (the sequential sum of warp_topk).
+template <int PER>
+__device__ __forceinline__ void warp_topk_regs(const float (&lv)[PER], int per, int topk, int score_fn, int lane,
+                                               int& my_e, float& my_w) {
+  uint32_t key[PER];
+#pragma unroll
+  for (int j = 0; j < PER; ++j) key[j] = j < per ? route_key(lv[j], lane + 32 * j) : 0u;
+#pragma unroll
+  for (int i = 1; i < PER; ++i)                       // insertion network, descending
+#pragma unroll
+    for (int j = i; j > 0; --j) {
+      const uint32_t hi = max(key[j - 1], key[j]), lo = min(key[j - 1], key[j]);
+      key[j - 1] = hi;
+      key[j] = lo;
+    }
+  float my_l = 0.f;
+  my_e = 0;
+#pragma unroll 1
+  for (int t = 0; t < topk; ++t) {
+    const uint32_t best = __reduce_max_sync(0xffffffffu, key[0]);
+    if (key[0] == best) {                             // keys are unique (the expert id is part of the key)
+#pragma unroll
+      for (int j = 0; j + 1 < PER; ++j) key[j] = key[j + 1];
+      key[PER - 1] = 0u;
+    }
+    if (lane == t) {
+      my_e = (int)(0xFFFFu - (best & 0xFFFFu));
+      const uint32_t ob = best >> 16;
+      my_l = __uint_as_float(((ob & 0x8000u) ? (ob & 0x7FFFu) : (~ob & 0xFFFFu)) << 16);
+    }
+  }
+  const float l_top = __shfl_sync(0xffffffffu, my_l, 0);
+  const float my_p = lane < topk ? (score_fn == 1 ? 1.0f / (1.0f + expf(-my_l)) : expf(my_l - l_top)) : 0.f;
+  float sum = 0.f;
+#pragma unroll 1
+  for (int t = 0; t < topk; ++t) sum += __shfl_sync(0xffffffffu, my_p, t);
+  my_w = my_p / sum;
+}
+
 // ------------------------------------------------------------------------------------------------------------
 // Route grouping (both expert kernels): groups of routes sharing an expert, experts ascending.
 // ------------------------------------------------------------------------------------------------------------
