@@ -52,7 +52,8 @@ struct BlockWs {
   unsigned status;
   unsigned epoch;                    // launches so far: this launch tags its published words with epoch + 1
   unsigned pad[30];
-  unsigned seg_cnt[kBMaxSeg];
+  unsigned seg_cnt[kBMaxSeg];         // per split segment: pieces whose record is written (tickets taken)
+  unsigned seg_done[kBMaxSeg];        // per split segment: merges finished (the last one resets both counters)
   // followed by: y bf16 [8][Nqkv], attention output as tagged words [8][Ko / 2], partial records
 };
 
@@ -218,6 +219,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
   // per segment (request x kv head): first page slot A in the flattened page list, first owning CTA, number of
   // owning CTAs (partial records) and first record; plus the flattened page count P
   __shared__ int s_segA[kBMaxSeg], s_first[kBMaxSeg], s_nparts[kBMaxSeg], s_recb[kBMaxSeg], s_P;
+  __shared__ int s_tk_seg[kBMaxSeg], s_tk[kBMaxSeg], s_ntk, s_go;   // this CTA's merge tickets
   __shared__ __align__(16) bf16 q_tile[8][kBD];
   __shared__ int s_ok;
 
@@ -306,6 +308,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
     }
     s_pre[M] = pre;
     s_P = a.nkv * pre;
+    s_ntk = 0;
   }
   __syncthreads();
   const int S = M * a.nkv;
@@ -608,94 +611,126 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
         __stcg(reinterpret_cast<float4*>(rec + hh * kBD + d0), make_float4(oc[0], oc[1], oc[2], oc[3]));
         __stcg(reinterpret_cast<float4*>(rec + hh * kBD + d0) + 1, make_float4(oc[4], oc[5], oc[6], oc[7]));
         if ((tid & 15) == 0) __stcg(reinterpret_cast<float2*>(rec + 8 * kBD) + hh, make_float2(mc, lc));
+        __threadfence();                                           // this thread's record before the ticket
       }
     }
     cons_sync();                                                   // warp partials are reused by the next piece
+    if (n_parts > 1 && tid == 0) {                                 // ticket: order of arrival among the pieces
+      s_tk_seg[s_ntk] = s;
+      s_tk[s_ntk] = (int)atomicAdd(&a.ws->seg_cnt[s], 1u);
+      ++s_ntk;
+    }
   }
-  grid_sync(&a.ws->gs, G, 1, kBCons, 1, &s_ok, status);
+  cons_sync();
 
-  // ---- B2: merge the partial records of split segments, one (segment, q head) per CTA at a time.  Warp w folds
-  // records r = w, w + 8, ... (loaded together: one memory round trip per 64 records) with the online softmax rule;
-  // the 8 warp results are then folded in warp order.  Fixed order throughout, so the result is deterministic. ----
+  // ---- B2: merge the partial records of each split segment without a grid barrier.  The CTAs holding the last
+  // nm = min(n, Gq) of the segment's n tickets merge it, merger j taking q heads j, j + nm, ...; each waits until all
+  // n pieces have taken their tickets (records written), then warp w folds records r = w, w + 8, ... (loaded
+  // together) with the online softmax rule and the 8 warp results are folded in warp order.  Fixed order throughout,
+  // so the result does not depend on which CTA merges.  The last merger to finish resets the segment's counters. ----
   {
     constexpr int kMR = 8;                                         // records per warp per round
     float* part = reinterpret_cast<float*>(wq);                    // [8 warps][128]
     float* wml = part + kBW * kBD;                                 // [8 warps][2]: m, l
-    for (int u = cta; have_tab && u < S * a.Gq; u += G) {
-      const int s = u / a.Gq, hh = u - s * a.Gq;
-      const int n = s_nparts[s];
-      if (n <= 1) continue;                                        // written directly in phase B
-      const int b = s / a.nkv, kvh = s - b * a.nkv;
-      const float* r0 = a.rec + (int64_t)s_recb[s] * kBRecFloats;
-      const int d0 = lane * 4;
-      float m_w = -INFINITY, l_w = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+    const int ntk = s_ntk;
+    for (int k = 0; k < ntk; ++k) {
+      const int s = s_tk_seg[k], n = s_nparts[s], nm = min(n, a.Gq), jm = s_tk[k] - (n - nm);
+      if (jm < 0) continue;                                          // not one of the last nm tickets
+      if (tid == 0) {                                                // every piece's record is written
+        int ok = 1;
+        unsigned it = 0;
 #pragma unroll 1
-      for (int base = 0; base < n; base += kBW * kMR) {
-        float4 v[kMR];
-        float2 ml[kMR];
-#pragma unroll
-        for (int i = 0; i < kMR; ++i) {
-          const int r = base + warp + kBW * i;
-          if (r < n) {
-            const float* rec = r0 + (int64_t)r * kBRecFloats;
-            v[i] = __ldcg(reinterpret_cast<const float4*>(rec + hh * kBD + d0));
-            ml[i] = __ldcg(reinterpret_cast<const float2*>(rec + 8 * kBD) + hh);
-          } else {
-            v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-            ml[i] = make_float2(-INFINITY, 0.f);
+        while ((int)ld_acquire_u32(&a.ws->seg_cnt[s]) < n) {
+          if (++it > FLINT_WAIT_LIMIT) {
+            atomicOr(status, STATUS_WAIT_TIMEOUT);
+            ok = 0;
+            break;
           }
         }
-        float m_new = m_w;
-#pragma unroll
-        for (int i = 0; i < kMR; ++i) m_new = fmaxf(m_new, ml[i].x);
-        if (m_new != -INFINITY) {
-          const float sc = m_w == -INFINITY ? 0.f : exp2f(m_w * c - m_new * c);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) acc[e] *= sc;
-          l_w *= sc;
+        __threadfence();
+        s_go = ok;
+      }
+      cons_sync();
+      const bool go = s_go != 0;
+      for (int hh = jm; go && hh < a.Gq; hh += nm) {
+        const int b = s / a.nkv, kvh = s - b * a.nkv;
+        const float* r0 = a.rec + (int64_t)s_recb[s] * kBRecFloats;
+        const int d0 = lane * 4;
+        float m_w = -INFINITY, l_w = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+        for (int base = 0; base < n; base += kBW * kMR) {
+          float4 v[kMR];
+          float2 ml[kMR];
 #pragma unroll
           for (int i = 0; i < kMR; ++i) {
-            const float f = ml[i].x == -INFINITY ? 0.f : exp2f(ml[i].x * c - m_new * c);
-            acc[0] = fmaf(v[i].x, f, acc[0]);
-            acc[1] = fmaf(v[i].y, f, acc[1]);
-            acc[2] = fmaf(v[i].z, f, acc[2]);
-            acc[3] = fmaf(v[i].w, f, acc[3]);
-            l_w = fmaf(ml[i].y, f, l_w);
+            const int r = base + warp + kBW * i;
+            if (r < n) {
+              const float* rec = r0 + (int64_t)r * kBRecFloats;
+              v[i] = __ldcg(reinterpret_cast<const float4*>(rec + hh * kBD + d0));
+              ml[i] = __ldcg(reinterpret_cast<const float2*>(rec + 8 * kBD) + hh);
+            } else {
+              v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+              ml[i] = make_float2(-INFINITY, 0.f);
+            }
           }
-          m_w = m_new;
-        }
-      }
-      *reinterpret_cast<float4*>(part + warp * kBD + d0) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-      if (lane == 0) {
-        wml[2 * warp] = m_w;
-        wml[2 * warp + 1] = l_w;
-      }
-      cons_sync();
-      if (tid < 32) {
-        float m = -INFINITY;
+          float m_new = m_w;
 #pragma unroll
-        for (int w = 0; w < kBW; ++w) m = fmaxf(m, wml[2 * w]);
-        float ov[4] = {0.f, 0.f, 0.f, 0.f}, den = 0.f;
-        if (m != -INFINITY) {
+          for (int i = 0; i < kMR; ++i) m_new = fmaxf(m_new, ml[i].x);
+          if (m_new != -INFINITY) {
+            const float sc = m_w == -INFINITY ? 0.f : exp2f(m_w * c - m_new * c);
 #pragma unroll
-          for (int w = 0; w < kBW; ++w) {
-            const float mw = wml[2 * w];
-            const float f = mw == -INFINITY ? 0.f : exp2f(mw * c - m * c);
-            const float4 pv = *reinterpret_cast<const float4*>(part + w * kBD + d0);
-            ov[0] = fmaf(pv.x, f, ov[0]);
-            ov[1] = fmaf(pv.y, f, ov[1]);
-            ov[2] = fmaf(pv.z, f, ov[2]);
-            ov[3] = fmaf(pv.w, f, ov[3]);
-            den = fmaf(wml[2 * w + 1], f, den);
+            for (int e = 0; e < 4; ++e) acc[e] *= sc;
+            l_w *= sc;
+#pragma unroll
+            for (int i = 0; i < kMR; ++i) {
+              const float f = ml[i].x == -INFINITY ? 0.f : exp2f(ml[i].x * c - m_new * c);
+              acc[0] = fmaf(v[i].x, f, acc[0]);
+              acc[1] = fmaf(v[i].y, f, acc[1]);
+              acc[2] = fmaf(v[i].z, f, acc[2]);
+              acc[3] = fmaf(v[i].w, f, acc[3]);
+              l_w = fmaf(ml[i].y, f, l_w);
+            }
+            m_w = m_new;
           }
         }
-        const int qh = kvh * a.Gq + hh;
-        if (a.sinks && m != -INFINITY) den += exp2f(a.sinks[qh] * kBLog2e - m * c);
-        const float inv = den > 0.f ? 1.0f / den : 0.f;
-        const uint32_t pk[2] = {pack_bf16x2(ov[0] * inv, ov[1] * inv), pack_bf16x2(ov[2] * inv, ov[3] * inv)};
-        publish_attn(a, ep, b, qh * kBD + d0, pk, 2);
+        *reinterpret_cast<float4*>(part + warp * kBD + d0) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        if (lane == 0) {
+          wml[2 * warp] = m_w;
+          wml[2 * warp + 1] = l_w;
+        }
+        cons_sync();
+        if (tid < 32) {
+          float m = -INFINITY;
+#pragma unroll
+          for (int w = 0; w < kBW; ++w) m = fmaxf(m, wml[2 * w]);
+          float ov[4] = {0.f, 0.f, 0.f, 0.f}, den = 0.f;
+          if (m != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < kBW; ++w) {
+              const float mw = wml[2 * w];
+              const float f = mw == -INFINITY ? 0.f : exp2f(mw * c - m * c);
+              const float4 pv = *reinterpret_cast<const float4*>(part + w * kBD + d0);
+              ov[0] = fmaf(pv.x, f, ov[0]);
+              ov[1] = fmaf(pv.y, f, ov[1]);
+              ov[2] = fmaf(pv.z, f, ov[2]);
+              ov[3] = fmaf(pv.w, f, ov[3]);
+              den = fmaf(wml[2 * w + 1], f, den);
+            }
+          }
+          const int qh = kvh * a.Gq + hh;
+          if (a.sinks && m != -INFINITY) den += exp2f(a.sinks[qh] * kBLog2e - m * c);
+          const float inv = den > 0.f ? 1.0f / den : 0.f;
+          const uint32_t pk[2] = {pack_bf16x2(ov[0] * inv, ov[1] * inv), pack_bf16x2(ov[2] * inv, ov[3] * inv)};
+          publish_attn(a, ep, b, qh * kBD + d0, pk, 2);
+        }
+        cons_sync();
       }
-      cons_sync();
+      // the last merger to finish resets the counters for the next launch
+      if (tid == 0 && atomicAdd(&a.ws->seg_done[s], 1u) == (unsigned)(nm - 1)) {
+        atomicExch(&a.ws->seg_cnt[s], 0u);
+        atomicExch(&a.ws->seg_done[s], 0u);
+      }
+      cons_sync();                                                   // s_go is rewritten for the next ticket
     }
   }
   pdl_trigger();
