@@ -11,17 +11,18 @@
 //            flight while phase A runs.
 //  A  every CTA recomputes the add + RMSNorm (same bits everywhere; CTA 0 publishes res_out), stages it as f16 and
 //     computes y = bf16(acc * gs) for its QKV rows: the K slices are split over the 8 warps and the partial tiles
-//     summed in warp order.  y goes to the workspace.                                   -- grid barrier --
+//     summed in warp order.  y is published as epoch-tagged words (tagged.cuh); no grid barrier follows.
 //  B  the pages of all (request, kv head) segments, in linear order, are cut into G contiguous ranges.  For each
-//     segment piece of its range the CTA normalises + ropes the segment's q heads; the warp that holds the current
-//     token's page normalises + ropes the new k, writes k and v to the cache slot and patches its shared copy of the
-//     page; each warp runs the online softmax over its pages (S = K q, exp2, P rounded to bf16, O += P V); the CTA
-//     merges its warps (fixed order) and, unless it owns the whole segment (then it writes the output), writes one
-//     partial record.                                                                      -- grid barrier --
-//  B2 each (segment, q head) with several records is merged by one CTA: weights exp2(m_r c - m c) and l by one warp
-//     (fixed lane-strided order + butterfly), the records' O summed by 8 warps in record order mod 8 and the 8 warp
-//     partials in warp order (sinks in the denominator).                                  -- grid barrier --
-//  C  every CTA stages the attention output as f16 and computes its O rows from the resident weights.
+//     segment piece of its range the CTA polls its q heads' words, normalises + ropes them; the warp that holds the
+//     current token's page normalises + ropes the new k, writes k and v to the cache slot and patches its shared copy
+//     of the page; each warp runs the online softmax over its pages (S = K q, exp2, P rounded to bf16, O += P V); the
+//     CTA merges its warps (fixed order) and, unless it owns the whole segment (then it publishes the output),
+//     writes one partial record and takes an arrival ticket for the segment.
+//  B2 the CTAs with the last min(n, Gq) tickets of a segment merge its records once all n have arrived: per q head,
+//     record weights exp2(m_r c - m c), the records' O folded by 8 warps in record order mod 8 and the 8 warp
+//     results in warp order (sinks in the denominator); the output is published as tagged words.
+//  C  every CTA stages the attention output (polling its tagged words) as f16 and computes its O rows from the
+//     resident weights.  The kernel has no grid barrier.
 #include "common.cuh"
 #include "gridsync.cuh"
 #include "tagged.cuh"
@@ -54,7 +55,7 @@ struct BlockWs {
   unsigned pad[30];
   unsigned seg_cnt[kBMaxSeg];         // per split segment: pieces whose record is written (tickets taken)
   unsigned seg_done[kBMaxSeg];        // per split segment: merges finished (the last one resets both counters)
-  // followed by: y bf16 [8][Nqkv], attention output as tagged words [8][Ko / 2], partial records
+  // followed by: QKV output as tagged words [8][Nqkv / 2], attention output as tagged words [8][Ko / 2], records
 };
 
 struct BlockArgs {
@@ -90,7 +91,7 @@ struct BlockArgs {
   bf16* q_out;                       // optional
   bf16* attn;                        // optional plain copy of the attention output [M][Ko] (the caller's)
   unsigned long long* attn_tag;      // workspace: attention output as tagged words [8][Ko / 2] (tagged.cuh)
-  bf16* y;                           // workspace: raw QKV output [8][Nqkv]
+  unsigned long long* y_tag;         // workspace: raw QKV output as tagged words of row pairs [8][Nqkv / 2]
   float* rec;                        // workspace: partial records
   int gq_total, go_total;            // row groups of 16
   int nks_q, nks_o;                  // 256-k slices
@@ -171,18 +172,62 @@ __device__ __forceinline__ void gemv_finish(const float* red, int ng, int M, flo
   }
 }
 
-// q / k head finish (attn_proj.cu's epilogue): y (4 values per lane, dims lane + 32 i) -> bf16(rmsnorm(y) * w) -> RoPE.
+// out[m][row0 + 16 gi + r] for the QKV rows, as tagged words of row pairs (same per-row sums and rounding as
+// gemv_finish): word (row0 + 16 gi + r) / 2 of row m carries rows r, r + 1 (r even).
+__device__ __forceinline__ void gemv_finish_tagged(const float* red, int ng, int M, float gs, const int* shift,
+                                                   unsigned long long* out, int64_t ld_words, int row0, unsigned ep) {
+  for (int idx = threadIdx.x; idx < ng * 8 * M; idx += kBCons) {
+    const int gi = idx / (8 * M), rem = idx - gi * 8 * M, r = 2 * (rem / M), m = rem - (r / 2) * M;
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int w = 0; w < kBW; ++w) {
+      s0 += red[(gi * kBW + w) * 128 + r * 8 + m];
+      s1 += red[(gi * kBW + w) * 128 + (r + 1) * 8 + m];
+    }
+    const float sc = ldexpf(gs, -shift[m]);
+    st_tagged(out + (int64_t)m * ld_words + (row0 + gi * 16 + r) / 2, ep, pack_bf16x2(s0 * sc, s1 * sc));
+  }
+}
+
+// A lane's 4 dims of a 128-dim head in the pair layout of the tagged QKV words: 2 lane, 2 lane + 1, 64 + 2 lane,
+// 65 + 2 lane (so RoPE partners d and d + 64 sit in one lane, as i and i + 2).
+__device__ __forceinline__ int pdim(int lane, int i) { return (i & 2) * 32 + 2 * lane + (i & 1); }
+
+// The lane's 4 values of head `head` of a tagged QKV row, once they carry this launch's tag (bounded poll).
+__device__ __forceinline__ void fetch_head(const unsigned long long* yrow, int head, unsigned ep, float (&v)[4], int lane,
+                                           unsigned* status) {
+  const unsigned long long* p = yrow + head * (kBD / 2) + lane;
+  unsigned long long w0 = 0, w1 = 0;
+  unsigned it = 0;
+#pragma unroll 1
+  for (;; ++it) {
+    w0 = ld_tagged(p);
+    w1 = ld_tagged(p + 32);
+    if (tag_is(w0, ep) && tag_is(w1, ep)) break;
+    if (it == FLINT_WAIT_LIMIT) {
+      atomicOr(status, STATUS_WAIT_TIMEOUT);
+      break;
+    }
+  }
+  v[0] = bf16_bits_to_f32((uint32_t)w0 & 0xFFFFu);
+  v[1] = bf16_bits_to_f32(((uint32_t)w0) >> 16);
+  v[2] = bf16_bits_to_f32((uint32_t)w1 & 0xFFFFu);
+  v[3] = bf16_bits_to_f32(((uint32_t)w1) >> 16);
+}
+
+// q / k head finish (attn_proj.cu's epilogue): y (4 values per lane, dims pdim(lane, i)) -> bf16(rmsnorm(y) * w) ->
+// RoPE (rotate-half: d with d + 64).
 __device__ __forceinline__ void head_norm_rope(float (&v)[4], const bf16* w, float eps, const float* cs, int lane) {
   float v2 = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) v2 += __shfl_xor_sync(0xffffffffu, v2, off);
   const float rs = rsqrtf(v2 / (float)kBD + eps);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) v[i] = bf16r(v[i] * rs * __bfloat162float(w[lane + 32 * i]));
+  for (int i = 0; i < 4; ++i) v[i] = bf16r(v[i] * rs * __bfloat162float(w[pdim(lane, i)]));
   if (cs) {
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-      const int r = lane + 32 * i;
+      const int r = 2 * lane + i;
       const float c = cs[r], s = cs[64 + r];
       const float n1 = v[i], n2 = v[i + 2];
       v[i] = fmaf(n1, c, -(n2 * s));
@@ -197,10 +242,6 @@ __device__ __forceinline__ void publish_attn(const BlockArgs& a, unsigned ep, in
   for (int i = 0; i < n; ++i) st_tagged(a.attn_tag + (int64_t)b * (a.Ko / 2) + col / 2 + i, ep, pk[i]);
   if (a.attn)
     for (int i = 0; i < n; ++i) reinterpret_cast<uint32_t*>(a.attn + (int64_t)b * a.Ko + col)[i] = pk[i];
-}
-
-__device__ __forceinline__ float ldcg_bf16(const bf16* p) {
-  return bf16_bits_to_f32(__ldcg(reinterpret_cast<const unsigned short*>(p)));
 }
 
 // MC > 0: the batch size fixed at compile time (MC = 1 is the single-stream decode: every per-token loop collapses,
@@ -221,7 +262,6 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
   __shared__ int s_segA[kBMaxSeg], s_first[kBMaxSeg], s_nparts[kBMaxSeg], s_recb[kBMaxSeg], s_P;
   __shared__ int s_tk_seg[kBMaxSeg], s_tk[kBMaxSeg], s_ntk, s_go;   // this CTA's merge tickets
   __shared__ __align__(16) bf16 q_tile[8][kBD];
-  __shared__ int s_ok;
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int G = gridDim.x, cta = blockIdx.x;
@@ -381,9 +421,8 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
   if (ngq > 0 && cons_sync_and(mbar_wait(&bar_wq, 0, status))) {
     gemv_resident(wq, wq + a.wq_scale_off, ngq, a.nks_q, xs, a.H, M, red, warp, lane);
     cons_sync();
-    gemv_finish(red, ngq, M, a.gs_qkv[0], shift, a.y, a.Nqkv, gq0 * 16);
+    gemv_finish_tagged(red, ngq, M, a.gs_qkv[0], shift, a.y_tag, a.Nqkv / 2, gq0 * 16, ep);
   }
-  grid_sync(&a.ws->gs, G, 0, kBCons, 1, &s_ok, status);
   const bool have_tab = cons_sync_and(mbar_wait(&bar_tab, 0, status));   // segment tables from the producer warp
 
   // ---- B: attention ----
@@ -403,29 +442,24 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
     }
     if (a.q_out && warp < a.Gq) {                                 // q of the empty request still goes out
       const int qh = kvh * a.Gq + warp;
-      const bf16* yb = a.y + (int64_t)b * a.Nqkv;
       float q[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) q[i] = ldcg_bf16(yb + qh * kBD + lane + 32 * i);
+      fetch_head(a.y_tag + (int64_t)b * (a.Nqkv / 2), qh, ep, q, lane, status);
       head_norm_rope(q, a.q_w, a.eps_head, a.cos_sin ? a.cos_sin + a.positions[b] * a.cs_stride : nullptr, lane);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) a.q_out[(int64_t)b * a.nq * kBD + qh * kBD + lane + 32 * i] = __float2bfloat16_rn(q[i]);
+      for (int i = 0; i < 4; ++i) a.q_out[(int64_t)b * a.nq * kBD + qh * kBD + pdim(lane, i)] = __float2bfloat16_rn(q[i]);
     }
     if (warp == 0 && a.slots && a.slots[b] >= 0) {
-      const bf16* yb = a.y + (int64_t)b * a.Nqkv;
+      const unsigned long long* yrow = a.y_tag + (int64_t)b * (a.Nqkv / 2);
       float k[4], v[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        k[i] = ldcg_bf16(yb + (a.nq + kvh) * kBD + lane + 32 * i);
-        v[i] = ldcg_bf16(yb + (a.nq + a.nkv + kvh) * kBD + lane + 32 * i);
-      }
+      fetch_head(yrow, a.nq + kvh, ep, k, lane, status);
+      fetch_head(yrow, a.nq + a.nkv + kvh, ep, v, lane, status);
       head_norm_rope(k, a.k_w, a.eps_head, a.cos_sin ? a.cos_sin + a.positions[b] * a.cs_stride : nullptr, lane);
       const int64_t slot = a.slots[b];
       bf16* dst = a.kv + (slot / kBPage) * a.st_block + (int64_t)kvh * a.st_head + (slot % kBPage) * (2 * kBD);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        dst[lane + 32 * i] = __float2bfloat16_rn(k[i]);
-        dst[kBD + lane + 32 * i] = __float2bfloat16_rn(v[i]);
+        dst[pdim(lane, i)] = __float2bfloat16_rn(k[i]);
+        dst[kBD + pdim(lane, i)] = __float2bfloat16_rn(v[i]);
       }
     }
   }
@@ -438,23 +472,22 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
     if (from >= to) continue;
     const int c_first = s_first[s], n_parts = s_nparts[s];
     const int seq = s_seq[b], start = s_start[b], last_page = (seq - 1) / kBPage;
-    const bf16* yb = a.y + (int64_t)b * a.Nqkv;
+    const unsigned long long* yrow = a.y_tag + (int64_t)b * (a.Nqkv / 2);
     const float* cs = a.cos_sin ? a.cos_sin + a.positions[b] * a.cs_stride : nullptr;
-    // q heads of this segment: warp hh
+    // q heads of this segment: warp hh, once the QKV rows carry this launch's tag (no grid barrier)
     {
       float q[4] = {0.f, 0.f, 0.f, 0.f};
       if (warp < a.Gq) {
         const int qh = kvh * a.Gq + warp;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) q[i] = ldcg_bf16(yb + qh * kBD + lane + 32 * i);
+        fetch_head(yrow, qh, ep, q, lane, status);
         head_norm_rope(q, a.q_w, a.eps_head, cs, lane);
         if (a.q_out && cta == c_first) {
 #pragma unroll
-          for (int i = 0; i < 4; ++i) a.q_out[(int64_t)b * a.nq * kBD + qh * kBD + lane + 32 * i] = __float2bfloat16_rn(q[i]);
+          for (int i = 0; i < 4; ++i) a.q_out[(int64_t)b * a.nq * kBD + qh * kBD + pdim(lane, i)] = __float2bfloat16_rn(q[i]);
         }
       }
 #pragma unroll
-      for (int i = 0; i < 4; ++i) q_tile[warp][lane + 32 * i] = __float2bfloat16_rn(q[i]);
+      for (int i = 0; i < 4; ++i) q_tile[warp][pdim(lane, i)] = __float2bfloat16_rn(q[i]);
     }
     cons_sync();
     uint32_t qa[8][2];
@@ -479,26 +512,23 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
       if (p == last_page) {
         // the current token: new k (normalised + roped) and v, to the cache slot and into this page's shared copy
         float k[4], v[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          k[i] = ldcg_bf16(yb + (a.nq + kvh) * kBD + lane + 32 * i);
-          v[i] = ldcg_bf16(yb + (a.nq + a.nkv + kvh) * kBD + lane + 32 * i);
-        }
+        fetch_head(yrow, a.nq + kvh, ep, k, lane, status);
+        fetch_head(yrow, a.nq + a.nkv + kvh, ep, v, lane, status);
         head_norm_rope(k, a.k_w, a.eps_head, cs, lane);
         const int64_t slot_b = a.slots ? a.slots[b] : -1;
         if (slot_b >= 0) {
           bf16* dst = a.kv + (slot_b / kBPage) * a.st_block + (int64_t)kvh * a.st_head + (slot_b % kBPage) * (2 * kBD);
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            dst[lane + 32 * i] = __float2bfloat16_rn(k[i]);
-            dst[kBD + lane + 32 * i] = __float2bfloat16_rn(v[i]);
+            dst[pdim(lane, i)] = __float2bfloat16_rn(k[i]);
+            dst[kBD + pdim(lane, i)] = __float2bfloat16_rn(v[i]);
           }
           const int row = (seq - 1) % kBPage;
           const int64_t here = (int64_t)a.bt[(int64_t)b * a.bt_stride + p] * kBPage + row;
           if (slot_b == here) {
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              const int d = lane + 32 * i;
+              const int d = pdim(lane, i);
               const uint32_t off = (d & 7) * 2;
               st_shared_u16(bpage_unit(page, d >> 6, row, (d & 63) >> 3) + off,
                             __bfloat16_as_ushort(__float2bfloat16_rn(k[i])));
@@ -783,8 +813,8 @@ static BlockLayout block_layout(int M, int H, int Ko, int gq_per, int go_per, in
 }
 
 static size_t block_ws_bytes(int64_t Nqkv, int64_t Ko, int sms) {
-  return sizeof(BlockWs) + (size_t)8 * Nqkv * 2 + (size_t)8 * (Ko / 2) * 8 + (size_t)(sms + kBMaxSeg) * kBRecFloats * 4 +
-         512;
+  return sizeof(BlockWs) + (size_t)8 * (Nqkv / 2) * 8 + (size_t)8 * (Ko / 2) * 8 +
+         (size_t)(sms + kBMaxSeg) * kBRecFloats * 4 + 512;
 }
 
 }  // namespace flint
@@ -862,8 +892,9 @@ extern "C" int flint_attn_block(const void* x, int64_t ldx, const int32_t* token
   a.max_blocks = (int)max_blocks; a.seq_lens = seq_lens; a.slots = slots; a.sinks = sinks; a.window = (int)window;
   a.c = scale * kBLog2e; a.Ko = (int)Ko; a.No = (int)n_o; a.gs_o = gs_o; a.out = (bf16*)out; a.res_out = (bf16*)res_out;
   a.q_out = (bf16*)q_out;
-  a.y = reinterpret_cast<bf16*>(wsb + sizeof(BlockWs));
-  a.attn_tag = reinterpret_cast<unsigned long long*>((reinterpret_cast<uintptr_t>(a.y + 8 * Nqkv) + 255) & ~uintptr_t(255));
+  a.y_tag = reinterpret_cast<unsigned long long*>(wsb + sizeof(BlockWs));
+  a.attn_tag = reinterpret_cast<unsigned long long*>(
+      (reinterpret_cast<uintptr_t>(a.y_tag + 8 * (Nqkv / 2)) + 255) & ~uintptr_t(255));
   a.attn = (bf16*)attn_out;
   a.rec = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(a.attn_tag + 8 * (Ko / 2)) + 255) & ~uintptr_t(255));
   a.gq_total = gq_total; a.go_total = go_total; a.nks_q = nks_q; a.nks_o = nks_o; a.np = L.np;
