@@ -161,12 +161,15 @@ def run_ours(args):
     cfg = FlintConfig()
     steps, warm, plen = args.steps, args.warmup, args.prompt
     max_ctx = plen + warm + 2 * steps + 16
-    model = FlintModel(cfg, dev, seed=1234, max_ctx=max_ctx, max_batch=1, shard=(rank, world))
-    dec = Decoder(model, batch=1, moe=args.moe, attn=args.attn, group=dist.group.WORLD if dist else None,
-                  exchange=args.exchange)
+    M = args.streams
+    model = FlintModel(cfg, dev, seed=1234, max_ctx=max_ctx, max_batch=M, shard=(rank, world))
+    sampling = (dict(temperature=1.0, top_k=20, top_p=0.95, seeds=[1000 + i for i in range(M)]) if args.sample
+                else None)
+    dec = Decoder(model, batch=M, moe=args.moe, attn=args.attn, group=dist.group.WORLD if dist else None,
+                  exchange=args.exchange, sampling=sampling)
     dec.reserve_history(warm + steps)
     dec.capture()
-    prompt = np.random.default_rng(7).integers(0, cfg.vocab, size=(1, plen))
+    prompt = np.random.default_rng(7).integers(0, cfg.vocab, size=(M, plen))
     fill = dec.prefill if args.prefill == "teacher" else dec.fill_kv_random
     t0 = time.time()
     fill(prompt)
@@ -204,31 +207,42 @@ def run_ours(args):
     t0 = time.perf_counter()
     dec.generate_host_driven(e2e_steps, pinned)
     e2e_s = time.perf_counter() - t0
-    e2e_val = e2e_steps / e2e_s
+    e2e_val = M * e2e_steps / e2e_s
     if dist:
         t = torch.tensor([e2e_s], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_val = e2e_steps / float(t.item())
+        e2e_val = M * e2e_steps / float(t.item())
 
     peak, peak_kind = measured_peak()
     mean_ctx = plen + warm + steps / 2
     # every rank times the kernels in lockstep (the sharded MoE and head contain collectives); rank 0 reports
     kernels = kernel_rooflines(model, dec, peak, peak_kind, int(mean_ctx), ms * 1e3 / steps)
     roof = max(kernels.values(), key=lambda r: r["share_of_step"]) if kernels else None
-    value = steps / (ms / 1e3)          # one stream decoded by all the GPUs together
+    value = M * steps / (ms / 1e3)      # tokens of all streams, decoded by all the GPUs together
     wbytes = cfg.weight_bytes_per_token()
     kv_bytes = cfg.layers * int(mean_ctx) * cfg.num_kv_heads * 2 * cfg.head_dim * 2
     total, active = cfg.param_counts()
+    if M > 1 or args.sample:           # several streams and/or sampled decoding
+        for r in kernels.values():
+            r["traffic"] = None           # the committed ncu traffic figures are for one greedy stream
+        metric = (f"decode tok/s summed over {M} stream(s), Flint-class NVFP4 MoE "
+                  f"({'sampled T1.0 / top-p 0.95 / top-k 20' if args.sample else 'greedy'}, after a {plen}-token prompt)")
+        workload = (f"BASELINE configs[4]: full Flint-class synthetic model, {M} concurrent stream(s), "
+                    f"{'seeded sampled' if args.sample else 'greedy'} decode")
+    else:
+        metric = "c1 decode tok/s, Flint-class NVFP4 MoE (greedy, 800 tokens after a 6057-token prompt)"
+        workload = "BASELINE configs[3]: full Flint-class synthetic model, 1 stream, greedy decode"
     if rank == 0:
         cpu = None
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and M == 1 and not args.sample and not args.no_cpu_baseline:
             cpu = cpu_baseline_sample(cfg, args.cpu_sample_tokens, plen)
         line = {
-            "metric": "c1 decode tok/s, Flint-class NVFP4 MoE (greedy, 800 tokens after a 6057-token prompt)",
+            "metric": metric,
             "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warm,
             "ms_per_step": round(ms / steps, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "nvfp4 weights (e2m1+e4m3), bf16 activations, fp32 accumulate", "data": "synthetic",
-            "config": {"workload": "BASELINE configs[3]: full Flint-class synthetic model, 1 stream, greedy decode",
+            "config": {"workload": workload, "streams": M, "sampling": sampling and {k: v for k, v in sampling.items()
+                                                                                      if k != "seeds"},
                        "layers": cfg.layers, "hidden": cfg.hidden, "experts": cfg.num_experts, "topk": cfg.topk,
                        "moe_inter": cfg.moe_inter, "vocab": cfg.vocab, "prompt_tokens": plen,
                        "prefill": args.prefill, "moe_path": dec.moe, "attn_path": dec.attn_mode,
@@ -241,8 +255,8 @@ def run_ours(args):
                        "prefill_s": round(prefill_s, 2)},
             "bound_tok_s": {"weights_only": round(peak * 1e9 / wbytes, 1),
                             "weights_plus_kv": round(peak * 1e9 / (wbytes + kv_bytes), 1), "peak_GBps": peak},
-            "e2e": {"value": round(e2e_val, 2), "unit": "tok/s", "steps": e2e_steps, "h2d_bytes_per_step": 4 + 8 + 4 + 8,
-                    "d2h_bytes_per_step": 4},
+            "e2e": {"value": round(e2e_val, 2), "unit": "tok/s", "steps": e2e_steps,
+                    "h2d_bytes_per_step": M * (4 + 8 + 4 + 8), "d2h_bytes_per_step": M * 4},
             "gpu_launches": dec.launches_per_step * steps,
             "roofline": roof, "roofline_kernels": kernels, "cpu_baseline": cpu, "clocks": clk.summary(),
             "tokens_head": tokens[0, :8].tolist(),
@@ -307,6 +321,8 @@ def main():
                          "(profiling runs)")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="N > 1: MoE / head exchange fused into the kernels over NVLink peer memory, or NCCL calls")
+    ap.add_argument("--streams", type=int, default=1, help="concurrent streams (1..8; BASELINE configs[4])")
+    ap.add_argument("--sample", action="store_true", help="seeded T 1.0 / top-k 20 / top-p 0.95 sampling")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -137,10 +137,12 @@ class Decoder:
     """Batch-M (M <= 8) decode of a FlintModel: teacher-forced prompt processing and greedy generation."""
 
     def __init__(self, model: FlintModel, batch: int = 1, moe: str | None = None, attn: str = "block", group=None,
-                 exchange: str = "peer", prefetch: bool = False):
+                 exchange: str = "peer", prefetch: bool = False, sampling: dict | None = None):
         """moe: "block" (one launch, one token; the default at batch 1), "chain" (route, up, down: three launches;
         the default for 2..8 tokens) or "fused" (one persistent launch for 1..8 tokens); attn: "block" (QKV +
-        attention + O in one persistent launch) or "chain" (three launches)."""
+        attention + O in one persistent launch) or "chain" (three launches).  sampling: None for greedy decode, or
+        {"temperature", "top_k", "top_p", "seeds"} (one int64 seed per stream) for the seeded top-k -> top-p draw of
+        flint_lm_head_nv4_sample; the draw of step t uses the Philox counter (t, stream)."""
         moe = moe or ("block" if batch == 1 else "chain")
         if moe not in ("block", "chain", "fused"):
             raise ValueError(f"moe must be 'block', 'chain' or 'fused', got {moe!r}")
@@ -148,6 +150,8 @@ class Decoder:
             raise ValueError("moe='block' decodes one token; use 'chain' or 'fused' for batches")
         if model.world > 1 and (moe != "block" or group is None):
             raise ValueError("a sharded model decodes one token with moe='block' and needs its process group")
+        if model.world > 1 and sampling is not None:
+            raise ValueError("sampled decoding of a sharded model is not supported; use greedy")
         if exchange not in ("peer", "nccl"):
             raise ValueError(f"exchange must be 'peer' or 'nccl', got {exchange!r}")
         self.group, self.exchange, self.prefetch = group, exchange, prefetch
@@ -169,6 +173,14 @@ class Decoder:
         self.step_ctr = torch.zeros((1,), dtype=torch.int32, device=dev)
         self.history = torch.zeros((M, 1), dtype=torch.int32, device=dev)
         self.out_tok = torch.zeros((M,), dtype=torch.int32, device=dev)
+        self.sampling = None
+        if sampling is not None:
+            seeds = torch.as_tensor(np.asarray(sampling["seeds"], dtype=np.int64).reshape(-1)[:M])
+            if seeds.numel() != M:
+                raise ValueError("sampling needs one seed per stream")
+            self.sampling = dict(temperature=float(sampling.get("temperature", 1.0)),
+                                 top_k=int(sampling.get("top_k", 20)), top_p=float(sampling.get("top_p", 1.0)))
+            self.seeds = seeds.to(dev)
         self.q, self.qkv = e(M, c.num_heads * c.head_dim), e(M, c.qkv_rows)
         self.res_a, self.res_b, self.h = e(M, c.hidden), e(M, c.hidden), e(M, c.hidden)
         self.attn = e(M, c.num_heads, c.head_dim)
@@ -280,6 +292,11 @@ class Decoder:
                 dist.all_reduce(self.keys, op=dist.ReduceOp.MAX, group=self.group)
                 ops.keys_to_tokens(self.keys, self.out_tok)
             return head_shard
+        if self.sampling is not None:
+            sp = self.sampling
+            return lambda: ops.lm_head_sample(self.h, P, S, gs, sp["temperature"], sp["top_k"], sp["top_p"], self.seeds,
+                                              self.step_ctr, self.out_tok, None, None, None, None, self.res_b,
+                                              self.m.final_norm, self.c.rms_eps)
         return lambda: ops.lm_head_nv4(self.h, P, S, gs, self.dummy_f, self.out_tok, False, True, self.res_b,
                                        self.m.final_norm, self.c.rms_eps)
 
