@@ -188,6 +188,7 @@ def run_ours(args):
             g.replay()
         e1.record(st)
         torch.cuda.synchronize()
+    del g                               # no stray reference may keep a graph (with NCCL calls) past the group
     ms = e0.elapsed_time(e1)
     if dist:
         t = torch.tensor([ms], device=dev)

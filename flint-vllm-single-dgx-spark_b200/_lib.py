@@ -45,7 +45,9 @@ SIGNATURES: dict[str, tuple] = {
                               P]),
     "flint_moe_block_ep": (I32, [P, I64, P, P, F32, P, I64, I64, I64, I32, P, P, P, P, P, P, I64, I64, I64, P, P, P, P, P,
                                  I32, P]),
-    "flint_moe_combine": (I32, [P, P, I64, I64, P, I32, P]),
+    "flint_moe_combine": (I32, [P, P, I64, I64, I64, P, I32, P]),
+    "flint_moe_up_ep": (I32, [P, I64, I64, P, I64, P, P, P, I64, I64, I64, I64, I64, P, P, I32, P]),
+    "flint_moe_down_ep": (I32, [P, I64, P, I64, P, P, P, I64, I64, I64, I64, I64, P, P, I32, P]),
     "flint_peer_buffer_bytes": (I64, [I64]),
     "flint_peer_alloc": (I32, [I64, P, P]),
     "flint_peer_open": (I32, [P, P]),
@@ -57,6 +59,8 @@ SIGNATURES: dict[str, tuple] = {
     "flint_argmax_keys_allmax_peer": (I32, [P, I64, P, I32, I32, P, I32, P]),
     "flint_lm_head_nv4_shard": (I32, [P, I64, P, P, F32, I64, P, P, F32, I64, I64, I64, P, P, I32, P]),
     "flint_argmax_keys_to_tokens": (I32, [P, I64, P, I32, P]),
+    "flint_lm_head_nv4_sample_shard": (I32, [P, I64, P, P, F32, I64, P, P, F32, I64, I64, I64, I64, P, P, P, P, I32, P]),
+    "flint_sample_merge": (I32, [P, P, I64, I64, I64, F32, F32, P, P, P, P, I32, P]),
     "flint_moe_align": (I32, [P, I64, I64, I64, P, I64, P, I64, P, P, I32, P]),
     "flint_attn_proj_workspace_bytes": (I64, []),
     "flint_attn_qkv": (I32, [P, I64, P, P, P, F32, P, P, P, I64, I64, I64, I64, I64, I32, P, P, F32, P, P, I64, P, P, I64,

@@ -98,17 +98,18 @@ extern "C" int64_t flint_lm_head_sample_workspace_bytes(int64_t M, int64_t V) {
   return (int64_t)(sample_logits_offset() + (size_t)M * (size_t)V * 4);
 }
 
-extern "C" int flint_lm_head_nv4_sample(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps,
-                                        int64_t M, const void* P, const void* S, float gs, int64_t V, int64_t K,
-                                        float* logits, int64_t ld_logits, float temperature, int64_t top_k, float top_p,
-                                        const uint64_t* seeds, const int32_t* step, int32_t* token_ids, int32_t* cand_ids,
-                                        float* cand_logits, int32_t* kept, void* workspace, int pdl, void* stream) {
+static int lm_head_sample_launch(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, int64_t M,
+                                 const void* P, const void* S, float gs, int64_t V, int64_t K, float* logits,
+                                 int64_t ld_logits, float temperature, int64_t top_k, float top_p, const uint64_t* seeds,
+                                 const int32_t* step, int32_t* token_ids, int32_t* cand_ids, float* cand_logits,
+                                 int32_t* kept, void* workspace, int pdl, void* stream, int64_t id_base) {
   using namespace flint;
-  if (!x || !P || !S || (res && !norm_w) || !seeds || !token_ids) return FLINT_ERR_ARGUMENT;
+  if (!x || !P || !S || (res && !norm_w) || !token_ids) return FLINT_ERR_ARGUMENT;
   if (!(temperature > 0.f) || !(temperature < INFINITY) || !(top_p > 0.f) || !(top_p <= 1.f)) return FLINT_ERR_ARGUMENT;
   if (M < 1 || M > 8 || V < 1 || V > (1ll << 30) || K < kSliceK || K % kSliceK != 0 || K > 8192 || ldx < K)
     return FLINT_ERR_SHAPE;
   if (top_k < 1 || top_k > kSampleMaxK || top_k > V) return FLINT_ERR_ARGUMENT;
+  if (id_base < 0 || id_base + V > (1ll << 31)) return FLINT_ERR_ARGUMENT;
   if (logits && ld_logits < V) return FLINT_ERR_SHAPE;
   if (!aligned(P, 16) || !aligned(S, 16) || !aligned(x, 16) || ldx % 8 != 0 || (res && !aligned(res, 16)) ||
       (norm_w && !aligned(norm_w, 16)) || (logits && !aligned(logits, 4)))
@@ -140,11 +141,82 @@ extern "C" int flint_lm_head_nv4_sample(const void* x, int64_t ldx, const void* 
   sp.cand_ids = cand_ids;
   sp.cand_logits = cand_logits;
   sp.kept = kept;
+  sp.id_base = (unsigned)id_base;
   float* lg = logits ? logits : reinterpret_cast<float*>(wsb + sample_logits_offset());
   const int64_t ldl = logits ? ld_logits : V;
   return launch(kern, dim3(grid), dim3((kHeadWarps + 1) * 32), smem, stream, pdl, mc, ms, (const bf16*)x, ldx,
                 (const bf16*)res, (const bf16*)norm_w, eps, (int)M, gs, (int)V, (int)K, lg, ldl, (int*)token_ids,
                 (HeadWorkspace*)workspace, sp, 0u, (unsigned long long*)nullptr);
+}
+
+namespace flint {
+
+// Sampled decoding over vocabulary shards: cand_ids / cand_logits [R][M][K] hold each shard's sorted top K (global
+// ids, -1 padding).  One warp per row re-selects the top K of their union by (logit desc, id asc) -- the global top
+// K, since every entry of the global top K is in its shard's top K -- and applies the sampling rule of
+// flint_lm_head_nv4_sample with the same uniform, so the token is the one-GPU token.
+__global__ void sample_merge_kernel(const int* __restrict__ cand_ids, const float* __restrict__ cand_logits, int R, int M,
+                                    int K, float temperature, float top_p, const unsigned long long* __restrict__ seeds,
+                                    const int* step, int* tokens, int* kept_out) {
+  __shared__ unsigned long long buf[8][8 * kSampleMaxK];
+  __shared__ unsigned long long top[8][kSampleMaxK];
+  __shared__ float w[8][kSampleMaxK];
+  pdl_wait();
+  const int lane = threadIdx.x & 31, m = threadIdx.x >> 5;
+  if (m < M) {
+    const int n = R * K;
+    for (int i = lane; i < n; i += 32) {
+      const int r = i / K, k = i - r * K;
+      const int64_t at = ((int64_t)r * M + m) * K + k;
+      const int id = cand_ids[at];
+      buf[m][i] = id >= 0 ? argmax_key(cand_logits[at], (uint32_t)id) : 0ull;
+    }
+    __syncwarp();
+    warp_select_sorted(buf[m], n, K, top[m], lane);
+    const int st = step ? *step : 0;
+    const float u = sample_uniform(seeds[m], (uint32_t)st, (uint32_t)m);
+    int kept = 1;
+    const int pick = sample_sorted(top[m], K, temperature, top_p, u, w[m], lane, &kept);
+    if (lane == 0) {
+      tokens[m] = (int)argmax_key_index(top[m][pick]);
+      if (kept_out) kept_out[m] = kept;
+    }
+  }
+  pdl_trigger();
+}
+
+}  // namespace flint
+
+extern "C" int flint_sample_merge(const int32_t* cand_ids, const float* cand_logits, int64_t R, int64_t M, int64_t top_k,
+                                  float temperature, float top_p, const uint64_t* seeds, const int32_t* step,
+                                  int32_t* token_ids, int32_t* kept, int pdl, void* stream) {
+  using namespace flint;
+  if (!cand_ids || !cand_logits || !seeds || !token_ids) return FLINT_ERR_ARGUMENT;
+  if (!(temperature > 0.f) || !(temperature < INFINITY) || !(top_p > 0.f) || !(top_p <= 1.f)) return FLINT_ERR_ARGUMENT;
+  if (R < 1 || R > 8 || M < 1 || M > 8 || top_k < 1 || top_k > kSampleMaxK) return FLINT_ERR_SHAPE;
+  return launch(sample_merge_kernel, dim3(1), dim3((unsigned)(32 * M)), 0, stream, pdl, cand_ids, cand_logits, (int)R,
+                (int)M, (int)top_k, temperature, top_p, reinterpret_cast<const unsigned long long*>(seeds), step,
+                (int*)token_ids, (int*)kept);
+}
+
+extern "C" int flint_lm_head_nv4_sample(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps,
+                                        int64_t M, const void* P, const void* S, float gs, int64_t V, int64_t K,
+                                        float* logits, int64_t ld_logits, float temperature, int64_t top_k, float top_p,
+                                        const uint64_t* seeds, const int32_t* step, int32_t* token_ids, int32_t* cand_ids,
+                                        float* cand_logits, int32_t* kept, void* workspace, int pdl, void* stream) {
+  if (!seeds) return FLINT_ERR_ARGUMENT;
+  return lm_head_sample_launch(x, ldx, res, norm_w, eps, M, P, S, gs, V, K, logits, ld_logits, temperature, top_k, top_p,
+                               seeds, step, token_ids, cand_ids, cand_logits, kept, workspace, pdl, stream, 0);
+}
+
+extern "C" int flint_lm_head_nv4_sample_shard(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps,
+                                              int64_t M, const void* P, const void* S, float gs, int64_t V, int64_t K,
+                                              int64_t index_base, int64_t top_k, int32_t* cand_ids, float* cand_logits,
+                                              int32_t* scratch_tokens, void* workspace, int pdl, void* stream) {
+  if (!cand_ids || !cand_logits || !scratch_tokens) return FLINT_ERR_ARGUMENT;
+  // the shard's own draw (seed 0, step 0) is discarded; its sorted candidates are the output
+  return lm_head_sample_launch(x, ldx, res, norm_w, eps, M, P, S, gs, V, K, nullptr, 0, 1.0f, top_k, 1.0f, nullptr,
+                               nullptr, scratch_tokens, cand_ids, cand_logits, nullptr, workspace, pdl, stream, index_base);
 }
 
 extern "C" int flint_lm_head_nv4(const void* x, int64_t ldx, int64_t M, const void* P, const void* S, float gs, int64_t V,

@@ -24,12 +24,13 @@ struct HeadWorkspace {
 struct SampleParams {
   float temperature, top_p;
   int top_k;
-  const unsigned long long* seeds;   // [M]
+  const unsigned long long* seeds;   // [M] (null: seed 0)
   const int* step;                   // device step counter (the Philox counter's first word); null -> 0
   unsigned long long* cand;          // workspace: per row, per CTA, its top_k keys sorted [M][grid][top_k]
   int* cand_ids;                     // optional [M, top_k]: the candidates' token ids (-1 past the vocabulary)
   float* cand_logits;                // optional [M, top_k]: their logits
   int* kept;                         // optional [M]: candidates left after top-p
+  unsigned id_base;                  // global id of row 0 (a vocabulary shard's first row; 0 for the whole head)
 };
 
 // Tail of the SAMPLE instantiation: per-CTA top_k of the rows it owns, then (last CTA) the global top_k, top-p and
@@ -53,12 +54,12 @@ __device__ __forceinline__ void head_sample_tail(uint8_t* smem, const float* log
     const int r0 = min(g0 * ROWS, V), r1 = min(g1 * ROWS, V);
     unsigned long long* buf = surv + m * kSampleSurvivors;
     unsigned long long lm = 0ull;
-    for (int r = r0 + lane; r < r1; r += 32) lm = max(lm, argmax_key(lrow[r], r));
+    for (int r = r0 + lane; r < r1; r += 32) lm = max(lm, argmax_key(lrow[r], sp.id_base + r));
     const unsigned long long T = warp_kth_largest(lm, K);
     int n = 0;
     for (int rb = r0; rb < r1; rb += 32) {
       const int r = rb + lane;
-      n = warp_compact_ge(r < r1 ? argmax_key(lrow[r], r) : 0ull, T, buf, n, kSampleSurvivors, lane);
+      n = warp_compact_ge(r < r1 ? argmax_key(lrow[r], sp.id_base + r) : 0ull, T, buf, n, kSampleSurvivors, lane);
     }
     __syncwarp();
     unsigned long long* out = sp.cand + ((int64_t)m * G + blockIdx.x) * K;
@@ -69,7 +70,7 @@ __device__ __forceinline__ void head_sample_tail(uint8_t* smem, const float* log
       for (int k = 0; k < K; ++k) {
         unsigned long long best = 0ull;
         for (int r = r0 + lane; r < r1; r += 32) {
-          const unsigned long long v = argmax_key(lrow[r], r);
+          const unsigned long long v = argmax_key(lrow[r], sp.id_base + r);
           if (v < ceil && v > best) best = v;
         }
         best = warp_max_u64(best);
@@ -128,7 +129,7 @@ __device__ __forceinline__ void head_sample_tail(uint8_t* smem, const float* log
       __syncwarp();
     }
     const int step = sp.step ? *sp.step : 0;
-    const float u = sample_uniform(sp.seeds[m], (uint32_t)step, (uint32_t)m);
+    const float u = sample_uniform(sp.seeds ? sp.seeds[m] : 0ull, (uint32_t)step, (uint32_t)m);
     int kept = 1;
     const int pick = sample_sorted(top, K, sp.temperature, sp.top_p, u, wbuf + m * kSampleMaxK, lane, &kept);
     if (lane == 0) {

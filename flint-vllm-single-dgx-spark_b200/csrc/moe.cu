@@ -206,7 +206,8 @@ struct UpPlan {
 
 __global__ void __launch_bounds__((kUpWarps + 1) * 32)
 moe_up_kernel(const __grid_constant__ CUtensorMap mc, const __grid_constant__ CUtensorMap ms, const bf16* x, int64_t ldx,
-              const int* ids, int M, int topk, int E, int I, int H, const float* __restrict__ g13, bf16* act, MoeWorkspace* ws) {
+              const int* ids, int M, int topk, int E, int I, int H, const float* __restrict__ g13, bf16* act, MoeWorkspace* ws,
+              int e_lo, int e_hi) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* dtile = reinterpret_cast<float*>(smem + UpL::ring_bytes);
@@ -218,7 +219,7 @@ moe_up_kernel(const __grid_constant__ CUtensorMap mc, const __grid_constant__ CU
   __shared__ float red[kMaxTokens];
   engine_init_bars<kUpWarps, kUpStages>(bars);
   pdl_wait();
-  build_groups(ids, M * topk, topk, E, G, sorted, ids_s, &ws->status, blockDim.x, 0);
+  build_groups(ids, M * topk, topk, E, G, sorted, ids_s, &ws->status, blockDim.x, 0, e_lo, e_hi);
   const int tpg = I / kUpBox;
   const int total = G.n * tpg;
   UpPlan plan{&mc, &ms, &G, xs, shift, g13, act, I, H, tpg, 0, (int)blockIdx.x, (int)gridDim.x};
@@ -248,7 +249,7 @@ struct DownPlan {
   const float* g2;
   const float* tw;
   bf16* ybuf;
-  bf16* out;
+  bf16* out;                         // null in expert-parallel mode (the per-route rows in ybuf are the output)
   unsigned* counters;
   int* s_last;
   int M, topk, I, H, tpg, n_local, first, stride;
@@ -284,6 +285,7 @@ struct DownPlan {
       const float y = dt[r * 8 + n] * ldexpf(g2[e], -shift[route]);
       ybuf[(int64_t)route * H + j * kDnBox + r] = __float2bfloat16_rn(y);
     }
+    if (!out) return;                                 // expert parallel: the rows are summed over ranks elsewhere
     __threadfence();
     named_bar_sync(1, nthreads);
     if (tid == 0) {
@@ -309,7 +311,7 @@ struct DownPlan {
 __global__ void __launch_bounds__((kDnWarps + 1) * 32)
 moe_down_kernel(const __grid_constant__ CUtensorMap mc, const __grid_constant__ CUtensorMap ms, const bf16* act,
                 const int* ids, const float* tw, int M, int topk, int E, int I, int H, const float* __restrict__ g2, bf16* out,
-                MoeWorkspace* ws) {
+                MoeWorkspace* ws, int e_lo, int e_hi, bf16* y_out) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* dtile = reinterpret_cast<float*>(smem + DnL::ring_bytes);
@@ -323,11 +325,18 @@ moe_down_kernel(const __grid_constant__ CUtensorMap mc, const __grid_constant__ 
   engine_init_bars<kDnWarps, kDnStages>(bars);
   pdl_wait();
   const int R = M * topk;
-  build_groups(ids, R, topk, E, G, sorted, ids_s, &ws->status, blockDim.x, 0);
+  build_groups(ids, R, topk, E, G, sorted, ids_s, &ws->status, blockDim.x, 0, e_lo, e_hi);
   const int tpg = H / kDnBox;
   const int total = G.n * tpg;
-  bf16* ybuf = reinterpret_cast<bf16*>(ws + 1);
-  DownPlan plan{&mc, &ms, &G, xs, shift, g2, tw, ybuf, out, ws->down_counter, &s_last, M, topk, I, H, tpg, 0,
+  bf16* ybuf = y_out ? y_out : reinterpret_cast<bf16*>(ws + 1);
+  if (y_out) {                                        // expert parallel: the other ranks' routes get zero rows
+    const int H8 = H / 8;
+    for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < R * H8; idx += gridDim.x * blockDim.x) {
+      const int r = idx / H8;
+      if (ids_s[r] == kNotLocal) reinterpret_cast<uint4*>(y_out)[idx] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  DownPlan plan{&mc, &ms, &G, xs, shift, g2, tw, ybuf, y_out ? nullptr : out, ws->down_counter, &s_last, M, topk, I, H, tpg, 0,
                 (int)blockIdx.x, (int)gridDim.x};
   plan.n_local = blockIdx.x < total ? (total - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
   if (threadIdx.x >= kDnWarps * 32) {
@@ -458,18 +467,19 @@ static bool moe_shapes_ok(int64_t M, int64_t topk, int64_t E, int64_t I, int64_t
          I % kSliceK == 0 && I <= 8192 && H >= kSliceK && H % kSliceK == 0 && H <= 16384 && H / 64 <= 256;
 }
 
-extern "C" int flint_moe_up(const void* xn, int64_t ldx, int64_t M, const int32_t* topk_ids, int64_t topk, const void* w13,
-                            const void* s13, const float* g13, int64_t E, int64_t I, int64_t H, void* act, void* workspace,
-                            int pdl, void* stream) {
+static int moe_up_launch(const void* xn, int64_t ldx, int64_t M, const int32_t* topk_ids, int64_t topk, const void* w13,
+                         const void* s13, const float* g13, int64_t E, int64_t I, int64_t H, int64_t e_lo, int64_t n_local,
+                         void* act, void* workspace, int pdl, void* stream) {
   if (!xn || !topk_ids || !w13 || !s13 || !g13 || !act || !workspace) return FLINT_ERR_ARGUMENT;
   if (!moe_shapes_ok(M, topk, E, I, H) || ldx < H || ldx % 8 != 0) return FLINT_ERR_SHAPE;
+  if (e_lo < 0 || n_local < 1 || e_lo + n_local > E) return FLINT_ERR_ARGUMENT;
   if (!aligned(xn, 16) || !aligned(w13, 16) || !aligned(s13, 16)) return FLINT_ERR_ALIGN;
   const int sms = num_sms();
   if (sms <= 0) return FLINT_ERR_DEVICE;
   CUtensorMap mc, ms;
-  int rc = encode_u8_2d(&mc, w13, H / 2, E * 2 * I, H / 2, 128, kUpBox, true);
+  int rc = encode_u8_2d(&mc, w13, H / 2, n_local * 2 * I, H / 2, 128, kUpBox, true);
   if (rc) return rc;
-  rc = encode_u8_2d(&ms, s13, H / 16, E * 2 * I, H / 16, 16, kUpBox, false);
+  rc = encode_u8_2d(&ms, s13, H / 16, n_local * 2 * I, H / 16, 16, kUpBox, false);
   if (rc) return rc;
   const size_t smem = 1024 + UpL::ring_bytes + UpL::dtile_bytes + (size_t)M * xs_stride((int)H) * 2;
   if (cudaFuncSetAttribute(moe_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
@@ -478,21 +488,37 @@ extern "C" int flint_moe_up(const void* xn, int64_t ldx, int64_t M, const int32_
   const int grid = tiles < 2 * sms ? tiles : 2 * sms;
   return launch(moe_up_kernel, dim3(grid), dim3((kUpWarps + 1) * 32), smem, stream, pdl, mc, ms, (const bf16*)xn, ldx,
                 (const int*)topk_ids, (int)M, (int)topk, (int)E, (int)I, (int)H, g13, (bf16*)act,
-                static_cast<MoeWorkspace*>(workspace));
+                static_cast<MoeWorkspace*>(workspace), (int)e_lo, (int)(e_lo + n_local));
 }
 
-extern "C" int flint_moe_down(const void* act, int64_t M, const int32_t* topk_ids, const float* topk_weights, int64_t topk,
-                              const void* w2, const void* s2, const float* g2, int64_t E, int64_t I, int64_t H, void* out,
-                              void* workspace, int pdl, void* stream) {
-  if (!act || !topk_ids || !topk_weights || !w2 || !s2 || !g2 || !out || !workspace) return FLINT_ERR_ARGUMENT;
+extern "C" int flint_moe_up(const void* xn, int64_t ldx, int64_t M, const int32_t* topk_ids, int64_t topk, const void* w13,
+                            const void* s13, const float* g13, int64_t E, int64_t I, int64_t H, void* act, void* workspace,
+                            int pdl, void* stream) {
+  return moe_up_launch(xn, ldx, M, topk_ids, topk, w13, s13, g13, E, I, H, 0, E, act, workspace, pdl, stream);
+}
+
+extern "C" int flint_moe_up_ep(const void* xn, int64_t ldx, int64_t M, const int32_t* topk_ids, int64_t topk,
+                               const void* w13, const void* s13, const float* g13, int64_t E, int64_t I, int64_t H,
+                               int64_t expert_lo, int64_t n_local, void* act, void* workspace, int pdl, void* stream) {
+  return moe_up_launch(xn, ldx, M, topk_ids, topk, w13, s13, g13, E, I, H, expert_lo, n_local, act, workspace, pdl,
+                       stream);
+}
+
+static int moe_down_launch(const void* act, int64_t M, const int32_t* topk_ids, const float* topk_weights, int64_t topk,
+                           const void* w2, const void* s2, const float* g2, int64_t E, int64_t I, int64_t H, int64_t e_lo,
+                           int64_t n_local, void* out, void* y_out, void* workspace, int pdl, void* stream) {
+  if (!act || !topk_ids || !w2 || !s2 || !g2 || (!out && !y_out) || !workspace || (out && !topk_weights))
+    return FLINT_ERR_ARGUMENT;
   if (!moe_shapes_ok(M, topk, E, I, H)) return FLINT_ERR_SHAPE;
+  if (e_lo < 0 || n_local < 1 || e_lo + n_local > E) return FLINT_ERR_ARGUMENT;
+  if (y_out && !aligned(y_out, 16)) return FLINT_ERR_ALIGN;
   if (!aligned(act, 16) || !aligned(w2, 16) || !aligned(s2, 16)) return FLINT_ERR_ALIGN;
   const int sms = num_sms();
   if (sms <= 0) return FLINT_ERR_DEVICE;
   CUtensorMap mc, ms;
-  int rc = encode_u8_2d(&mc, w2, I / 2, E * H, I / 2, 128, kDnBox, true);
+  int rc = encode_u8_2d(&mc, w2, I / 2, n_local * H, I / 2, 128, kDnBox, true);
   if (rc) return rc;
-  rc = encode_u8_2d(&ms, s2, I / 16, E * H, I / 16, 16, kDnBox, false);
+  rc = encode_u8_2d(&ms, s2, I / 16, n_local * H, I / 16, 16, kDnBox, false);
   if (rc) return rc;
   const size_t smem = 1024 + DnL::ring_bytes + DnL::dtile_bytes + (size_t)M * topk * xs_stride((int)I) * 2;
   if (smem > 227 * 1024) return FLINT_ERR_SHAPE;
@@ -503,7 +529,21 @@ extern "C" int flint_moe_down(const void* act, int64_t M, const int32_t* topk_id
   const int grid = tiles < per_sm * sms ? tiles : per_sm * sms;
   return launch(moe_down_kernel, dim3(grid), dim3((kDnWarps + 1) * 32), smem, stream, pdl, mc, ms, (const bf16*)act,
                 (const int*)topk_ids, topk_weights, (int)M, (int)topk, (int)E, (int)I, (int)H, g2, (bf16*)out,
-                static_cast<MoeWorkspace*>(workspace));
+                static_cast<MoeWorkspace*>(workspace), (int)e_lo, (int)(e_lo + n_local), (bf16*)y_out);
+}
+
+extern "C" int flint_moe_down(const void* act, int64_t M, const int32_t* topk_ids, const float* topk_weights, int64_t topk,
+                              const void* w2, const void* s2, const float* g2, int64_t E, int64_t I, int64_t H, void* out,
+                              void* workspace, int pdl, void* stream) {
+  return moe_down_launch(act, M, topk_ids, topk_weights, topk, w2, s2, g2, E, I, H, 0, E, out, nullptr, workspace, pdl,
+                         stream);
+}
+
+extern "C" int flint_moe_down_ep(const void* act, int64_t M, const int32_t* topk_ids, int64_t topk, const void* w2,
+                                 const void* s2, const float* g2, int64_t E, int64_t I, int64_t H, int64_t expert_lo,
+                                 int64_t n_local, void* y_out, void* workspace, int pdl, void* stream) {
+  return moe_down_launch(act, M, topk_ids, nullptr, topk, w2, s2, g2, E, I, H, expert_lo, n_local, nullptr, y_out,
+                         workspace, pdl, stream);
 }
 
 extern "C" int flint_moe_align(const int32_t* topk_ids, int64_t numel, int64_t num_experts, int64_t block_size,

@@ -371,16 +371,17 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   grid_sync_retire(&ws->sync, nb, &ws->epoch, a.peer_mode ? &peer_header(a.peers.base[a.peers.rank])->moe_epoch : nullptr);
 }
 
-// out[r] = bf16(sum_s tw[s] * y[s][r]) in slot order (the weighted sum of flint_moe_block after an expert-parallel
-// sum of the per-slot rows over ranks).
+// out[m][r] = bf16(sum_s tw[m][s] * y[m topk + s][r]) in slot order (the weighted sum of flint_moe_block /
+// flint_moe_down after an expert-parallel sum of the per-route rows over ranks).
 __global__ void moe_combine_kernel(const bf16* __restrict__ y, const float* __restrict__ tw, int topk, int H,
                                    bf16* __restrict__ out) {
   pdl_wait();
-  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  const int r = blockIdx.x * blockDim.x + threadIdx.x, m = blockIdx.y;
   if (r < H) {
     float acc = 0.f;
-    for (int s = 0; s < topk; ++s) acc = fmaf(tw[s], __bfloat162float(y[(int64_t)s * H + r]), acc);
-    out[r] = __float2bfloat16_rn(acc);
+    for (int s = 0; s < topk; ++s)
+      acc = fmaf(tw[m * topk + s], __bfloat162float(y[(int64_t)(m * topk + s) * H + r]), acc);
+    out[(int64_t)m * H + r] = __float2bfloat16_rn(acc);
   }
   pdl_trigger();
 }
@@ -497,12 +498,12 @@ extern "C" int flint_moe_block_ep(const void* x, int64_t ldx, const void* res, c
                           pdl, stream);
 }
 
-extern "C" int flint_moe_combine(const void* y, const float* topk_weights, int64_t topk, int64_t H, void* out, int pdl,
-                                 void* stream) {
+extern "C" int flint_moe_combine(const void* y, const float* topk_weights, int64_t M, int64_t topk, int64_t H, void* out,
+                                 int pdl, void* stream) {
   if (!y || !topk_weights || !out) return FLINT_ERR_ARGUMENT;
-  if (topk < 1 || topk > kXMaxSlots || H < 1 || H > (1 << 20)) return FLINT_ERR_SHAPE;
-  return launch(moe_combine_kernel, dim3((unsigned)((H + 255) / 256)), dim3(256), 0, stream, pdl, (const bf16*)y,
-                topk_weights, (int)topk, (int)H, (bf16*)out);
+  if (M < 1 || M > 8 || topk < 1 || topk > kXMaxSlots || H < 1 || H > (1 << 20)) return FLINT_ERR_SHAPE;
+  return launch(moe_combine_kernel, dim3((unsigned)((H + 255) / 256), (unsigned)M), dim3(256), 0, stream, pdl,
+                (const bf16*)y, topk_weights, (int)topk, (int)H, (bf16*)out);
 }
 
 extern "C" int flint_moe_block_peer(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps,

@@ -101,15 +101,19 @@ struct Groups {
 };
 
 // Threads [0, nthreads) of the block call it and synchronise on named barrier `bar` (0 with nthreads == blockDim.x
-// is __syncthreads).
+// is __syncthreads).  Expert parallel: only routes whose expert is in [e_lo, e_hi) are grouped, G.exp holds the
+// local expert index e - e_lo, and the other routes end with ids[r] = kNotLocal.
+constexpr int kNotLocal = 0x7fffffff;
 __device__ __forceinline__ void build_groups(const int* ids_g, int R, int topk, int E, Groups& G, int* sorted, int* ids,
-                                             unsigned* status, int nthreads, int bar) {
+                                             unsigned* status, int nthreads, int bar, int e_lo = 0,
+                                             int e_hi = kNotLocal) {
   const int tid = threadIdx.x;
   auto sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthreads) : "memory"); };
   if (tid < R) {
     const int e = ids_g[tid];
     if ((e < 0 || e >= E) && status) atomicOr(status, 2u);
-    ids[tid] = min(max(e, 0), E - 1);
+    const int ec = min(max(e, 0), E - 1);
+    ids[tid] = ec >= e_lo && ec < e_hi ? ec : kNotLocal;
   }
   sync();
   if (tid < R) {
@@ -127,9 +131,10 @@ __device__ __forceinline__ void build_groups(const int* ids_g, int R, int topk, 
     for (int i = 0; i < R; ++i) {
       const int r = sorted[i];
       const int e = ids[r];
+      if (e == kNotLocal) break;                      // the non-local routes sort last
       if (e != prev || G.cnt[n] == 8) {
         ++n;
-        G.exp[n] = e;
+        G.exp[n] = e - e_lo;
         G.cnt[n] = 0;
         prev = e;
       }

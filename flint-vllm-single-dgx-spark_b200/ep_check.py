@@ -3,9 +3,11 @@
     torchrun --nproc-per-node N --master-addr 127.0.0.1 flint-vllm-single-dgx-spark_b200/ep_check.py [--layers 4]
 
 Every rank builds the same small synthetic Flint-class model and keeps its shard (experts and head rows), then the
-ranks decode a prompt together, once per exchange: "peer" (the MoE block pushes its local slots' rows to every rank
-over NVLink and combines in-kernel; the head's shard keys go through the peer argmax exchange) and "nccl" (local
-slot rows + an NCCL sum + the slot-order combine; head keys + an NCCL MAX).  Rank 0 also decodes the unsharded model on its GPU; the sharded token
+ranks decode prompts together in several modes: one stream through the one-launch MoE block with the in-kernel
+peer exchange ("peer": local slots' rows pushed to every rank over NVLink, combined in-kernel; head keys through the
+peer argmax exchange) or with NCCL (local slot rows + an NCCL sum + the slot-order combine; head keys + an NCCL
+MAX); three streams through the MoE chain (local routes' rows + an NCCL sum + the combine); and seeded sampled
+decoding (each shard's top-k candidates gathered, then the one-GPU draw over their union).  Rank 0 also decodes the unsharded model on its GPU; the sharded token
 stream and final hidden state must equal it bit for bit.  Prints one JSON line (rank 0) and exits non-zero on a
 mismatch.
 """
@@ -37,12 +39,21 @@ def _package():
     return mod
 
 
-def decode(model, prompt, n, group=None, exchange="peer"):
+SAMPLING = dict(temperature=1.0, top_k=20, top_p=0.95)
+
+# (name, batch, moe path, exchange, sampled)
+CASES = [("b1_block_peer", 1, "block", "peer", False), ("b1_block_nccl", 1, "block", "nccl", False),
+         ("b3_chain", 3, "chain", "peer", False), ("b3_chain_sampled", 3, "chain", "peer", True),
+         ("b1_block_sampled", 1, "block", "peer", True)]
+
+
+def decode(model, prompt, n, batch, moe, group=None, exchange="peer", sampled=False):
     from flint_b200.model import Decoder
-    dec = Decoder(model, batch=1, group=group, exchange=exchange)
+    sampling = dict(SAMPLING, seeds=[100 + i for i in range(batch)]) if sampled else None
+    dec = Decoder(model, batch=batch, moe=moe, group=group, exchange=exchange, sampling=sampling)
     dec.reserve_history(n)
     dec.capture()
-    dec.prefill(prompt)
+    dec.prefill(prompt[:batch])
     toks = dec.decode(n).cpu().numpy().copy()
     torch.cuda.synchronize()
     h = dec.h.float().cpu().numpy().copy()
@@ -58,7 +69,7 @@ def main():
     ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--prompt", type=int, default=40)
     ap.add_argument("--tokens", type=int, default=24)
-    ap.add_argument("--exchange", default="peer,nccl", help="exchanges to check, comma separated: peer, nccl")
+    ap.add_argument("--cases", default=",".join(c[0] for c in CASES), help="comma-separated case names")
     args = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
@@ -67,23 +78,27 @@ def main():
     from flint_b200.model import FlintConfig, FlintModel
     cfg = FlintConfig(layers=args.layers, vocab=256 * 8 * 16)
     dev = torch.device("cuda", torch.cuda.current_device())
-    prompt = np.random.default_rng(5).integers(0, cfg.vocab, size=(1, args.prompt))
+    prompt = np.random.default_rng(5).integers(0, cfg.vocab, size=(3, args.prompt))
     ctx = args.prompt + args.tokens + 16
-    model = FlintModel(cfg, dev, seed=11, max_ctx=ctx, max_batch=1, shard=(rank, world))
+    cases = [c for c in CASES if c[0] in args.cases.split(",")]
+    model = FlintModel(cfg, dev, seed=11, max_ctx=ctx, max_batch=3, shard=(rank, world))
     runs = {}
-    for exchange in args.exchange.split(","):
-        toks, h, status = decode(model, prompt, args.tokens, group=dist.group.WORLD, exchange=exchange)
-        runs[exchange] = (toks, h, status)
+    for name, batch, moe, exchange, sampled in cases:
+        runs[name] = decode(model, prompt, args.tokens, batch, moe, group=dist.group.WORLD, exchange=exchange,
+                            sampled=sampled)
         dist.barrier()
     ok = True
     if rank == 0:
         del model
         torch.cuda.empty_cache()
-        ref_toks, ref_h, _ = decode(FlintModel(cfg, dev, seed=11, max_ctx=ctx, max_batch=1), prompt, args.tokens)
-        rep = {"world": world, "layers": cfg.layers, "tokens": int(ref_toks.size), "single": ref_toks[0, :12].tolist()}
-        for exchange, (toks, h, status) in runs.items():
+        single = FlintModel(cfg, dev, seed=11, max_ctx=ctx, max_batch=3)
+        rep = {"world": world, "layers": cfg.layers}
+        for name, batch, moe, exchange, sampled in cases:
+            ref_toks, ref_h, _ = decode(single, prompt, args.tokens, batch, moe, sampled=sampled)
+            toks, h, status = runs[name]
             match = bool((toks == ref_toks).all() and np.array_equal(h, ref_h)) and status == 0
-            rep[exchange] = {"match": match, "status": status, "tokens": toks[0, :12].tolist()}
+            rep[name] = {"match": match, "status": status, "tokens": toks[0, :8].tolist(),
+                         "single": ref_toks[0, :8].tolist()}
             ok = ok and match
         rep["match"] = ok
         print(json.dumps(rep), flush=True)

@@ -148,10 +148,8 @@ class Decoder:
             raise ValueError(f"moe must be 'block', 'chain' or 'fused', got {moe!r}")
         if moe == "block" and batch != 1:
             raise ValueError("moe='block' decodes one token; use 'chain' or 'fused' for batches")
-        if model.world > 1 and (moe != "block" or group is None):
-            raise ValueError("a sharded model decodes one token with moe='block' and needs its process group")
-        if model.world > 1 and sampling is not None:
-            raise ValueError("sampled decoding of a sharded model is not supported; use greedy")
+        if model.world > 1 and (moe == "fused" or group is None):
+            raise ValueError("a sharded model decodes with moe='block' (one token) or 'chain' and needs its process group")
         if exchange not in ("peer", "nccl"):
             raise ValueError(f"exchange must be 'peer' or 'nccl', got {exchange!r}")
         self.group, self.exchange, self.prefetch = group, exchange, prefetch
@@ -188,6 +186,7 @@ class Decoder:
         self.tw, self.ti = e(M, c.topk, dt=torch.float32), e(M, c.topk, dt=torch.int32)
         self.lg = e(M, c.num_experts, dt=torch.float32)
         self.y_slots = torch.zeros((c.topk, c.hidden), dtype=torch.bfloat16, device=dev)   # expert-parallel exchange
+        self.y_rows = torch.zeros((M * c.topk, c.hidden), dtype=torch.bfloat16, device=dev)  # ... of the chain
         self.keys = torch.zeros((M,), dtype=torch.int64, device=dev)                        # vocab-shard argmax
         self.act = e(M * c.topk, c.moe_inter)
         self.dummy_f = e(1, 1, dt=torch.float32)
@@ -199,7 +198,7 @@ class Decoder:
         # head (+ key conversion when sharded) + advance; NCCL's own kernels are not counted
         # (peer exchange: the MoE block exchanges in-kernel; the head adds one exchange kernel)
         ep = model.world > 1
-        moe_launches = 3 if moe == "chain" else 2 if (ep and exchange == "nccl") else 1
+        moe_launches = (4 if ep else 3) if moe == "chain" else 2 if (ep and exchange == "nccl") else 1
         self.launches_per_step = ((3 if attn == "chain" else 1) + moe_launches) * c.layers + 2 + (1 if ep else 0)
 
     # ---- one decode step as torch ops on persistent buffers ----
@@ -262,11 +261,23 @@ class Decoder:
                                                            self.h, self.res_b, self.xn, self.lg, self.ti, self.tw,
                                                            False)))
         else:
-            seq += [("route", lambda: ops.moe_route(self.a, self.res_a, L["ln2"], c.rms_eps, L["gate"], c.topk,
-                                                    ew.score_fn, self.lg, self.ti, self.tw, self.xn, self.res_b, True,
-                                                    True)),
-                    ("up", lambda: ops.moe_up(self.xn, self.ti, ew.w13, ew.s13, ew.g13, self.act)),
-                    ("down", lambda: ops.moe_down(self.act, self.ti, self.tw, ew.w2, ew.s2, ew.g2, self.h))]
+            seq.append(("route", lambda: ops.moe_route(self.a, self.res_a, L["ln2"], c.rms_eps, L["gate"], c.topk,
+                                                       ew.score_fn, self.lg, self.ti, self.tw, self.xn, self.res_b, True,
+                                                       True)))
+            if m.world > 1:
+                # expert parallel: routing replicated; local routes' rows, an exact sum over ranks, slot-order combine
+                import torch.distributed as dist
+
+                def down_ep():
+                    ops.moe_down_ep(self.act, self.ti, ew.w2, ew.s2, ew.g2, c.num_experts, m.e_lo, self.y_rows)
+                    dist.all_reduce(self.y_rows, group=self.group)
+                    ops.moe_combine(self.y_rows, self.tw, self.h)
+                seq += [("up_ep", lambda: ops.moe_up_ep(self.xn, self.ti, ew.w13, ew.s13, ew.g13, c.num_experts, m.e_lo,
+                                                        self.act)),
+                        ("down_ep", down_ep)]
+            else:
+                seq += [("up", lambda: ops.moe_up(self.xn, self.ti, ew.w13, ew.s13, ew.g13, self.act)),
+                        ("down", lambda: ops.moe_down(self.act, self.ti, self.tw, ew.w2, ew.s2, ew.g2, self.h))]
         return seq
 
     def _layers(self):
@@ -277,6 +288,26 @@ class Decoder:
     def head_op(self):
         P, S, gs = self.m.head
         ops = torch.ops.flint_b200
+        if self.m.world > 1 and self.sampling is not None:
+            import torch.distributed as dist
+            sp, k, R = self.sampling, self.sampling["top_k"], self.m.world
+            if not hasattr(self, "cand_ids"):
+                dev = self.h.device
+                self.cand_ids = torch.zeros((self.M, k), dtype=torch.int32, device=dev)
+                self.cand_logits = torch.zeros((self.M, k), dtype=torch.float32, device=dev)
+                self.cand_scratch = torch.zeros((self.M,), dtype=torch.int32, device=dev)
+                self.all_ids = torch.zeros((R, self.M, k), dtype=torch.int32, device=dev)
+                self.all_logits = torch.zeros((R, self.M, k), dtype=torch.float32, device=dev)
+
+            def head_sample_shard():
+                # this shard's sorted top-k, every rank's candidates, then the one-GPU draw over their union
+                ops.lm_head_sample_shard(self.h, P, S, gs, self.m.v_lo, k, self.cand_ids, self.cand_logits,
+                                         self.cand_scratch, self.res_b, self.m.final_norm, self.c.rms_eps)
+                dist.all_gather_into_tensor(self.all_ids, self.cand_ids, group=self.group)
+                dist.all_gather_into_tensor(self.all_logits, self.cand_logits, group=self.group)
+                ops.sample_merge(self.all_ids, self.all_logits, sp["temperature"], sp["top_p"], self.seeds,
+                                 self.step_ctr, self.out_tok)
+            return head_sample_shard
         if self.m.world > 1 and self.peers is not None:
             pp = self.peers
 
@@ -324,6 +355,8 @@ class Decoder:
         if name in ("moe_fused", "moe_block"):
             return (self.algorithmic_bytes("route", ctx) + self.algorithmic_bytes("up", ctx)
                     + self.algorithmic_bytes("down", ctx))
+        if name in ("up_ep", "down_ep"):                  # local experts only: topk / world routes on average
+            return self.algorithmic_bytes(name[:-3], ctx) // self.m.world
         if name in ("moe_block_ep", "moe_block_peer"):   # local experts only: topk / world routed slots on average
             return self.algorithmic_bytes("route", ctx) + (self.algorithmic_bytes("up", ctx)
                                                            + self.algorithmic_bytes("down", ctx)) // self.m.world

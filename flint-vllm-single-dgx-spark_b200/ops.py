@@ -97,6 +97,44 @@ def _(keys, tokens):
     return None
 
 
+@torch.library.custom_op(f"{NS}::lm_head_sample_shard", mutates_args=("cand_ids", "cand_logits", "scratch"))
+def lm_head_sample_shard(x: torch.Tensor, P: torch.Tensor, S: torch.Tensor, gs: float, index_base: int, top_k: int,
+                         cand_ids: torch.Tensor, cand_logits: torch.Tensor, scratch: torch.Tensor, res: torch.Tensor | None,
+                         norm_w: torch.Tensor | None, eps: float) -> None:
+    """One vocabulary shard's sorted top-k sampling candidates (global ids) per row (flint_lm_head_nv4_sample_shard)."""
+    _lib.require_cuda(x, "lm_head_sample_shard")
+    V, K = _check_nvfp4(P, S, "lm_head_sample_shard")
+    M = x.shape[0]
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != K or cand_ids.numel() < M * top_k:
+        raise _lib.FlintError("lm_head_sample_shard: x bf16 [M, K], candidates [M, top_k]")
+    ws = _lib.workspace(x.device, f"lm_head_sample_{M}_{V}", lib().flint_lm_head_sample_workspace_bytes(M, V))
+    rc = lib().flint_lm_head_nv4_sample_shard(ptr(x), x.stride(0), ptr(res), ptr(norm_w), float(eps), M, ptr(_u8(P)),
+                                              ptr(_u8(S)), float(gs), V, K, int(index_base), int(top_k), ptr(cand_ids),
+                                              ptr(cand_logits), ptr(scratch), ptr(ws), PDL, stream_ptr(x.device))
+    check(rc, "flint_lm_head_nv4_sample_shard")
+
+
+@lm_head_sample_shard.register_fake
+def _(x, P, S, gs, index_base, top_k, cand_ids, cand_logits, scratch, res, norm_w, eps):
+    return None
+
+
+@torch.library.custom_op(f"{NS}::sample_merge", mutates_args=("tokens",))
+def sample_merge(cand_ids: torch.Tensor, cand_logits: torch.Tensor, temperature: float, top_p: float,
+                 seeds: torch.Tensor, step: torch.Tensor | None, tokens: torch.Tensor) -> None:
+    """Draw from the gathered shard candidates [R, M, top_k] (flint_sample_merge)."""
+    _lib.require_cuda(cand_ids, "sample_merge")
+    R, M, k = cand_ids.shape
+    rc = lib().flint_sample_merge(ptr(cand_ids), ptr(cand_logits), R, M, k, float(temperature), float(top_p), ptr(seeds),
+                                  ptr(step), ptr(tokens), None, PDL, stream_ptr(cand_ids.device))
+    check(rc, "flint_sample_merge")
+
+
+@sample_merge.register_fake
+def _(cand_ids, cand_logits, temperature, top_p, seeds, step, tokens):
+    return None
+
+
 @torch.library.custom_op(f"{NS}::lm_head_sample", mutates_args=("tokens", "logits", "cand_ids", "cand_logits", "kept"))
 def lm_head_sample(x: torch.Tensor, P: torch.Tensor, S: torch.Tensor, gs: float, temperature: float, top_k: int,
                    top_p: float, seeds: torch.Tensor, step: torch.Tensor | None, tokens: torch.Tensor,
@@ -217,6 +255,50 @@ def _(act, topk_ids, topk_weights, w2, s2, g2, out):
     return None
 
 
+@torch.library.custom_op(f"{NS}::moe_up_ep", mutates_args=("act",))
+def moe_up_ep(xn: torch.Tensor, topk_ids: torch.Tensor, w13: torch.Tensor, s13: torch.Tensor, g13: torch.Tensor,
+              num_experts: int, expert_lo: int, act: torch.Tensor) -> None:
+    """Expert-parallel moe_up (flint_moe_up_ep): act rows of the routes whose expert is local (w13 holds experts
+    expert_lo .. expert_lo + n_local - 1 of num_experts)."""
+    _lib.require_cuda(xn, "moe_up_ep")
+    _bf16_2d(xn, "moe_up_ep xn")
+    M, H = xn.shape
+    n_local, I2, Hh = w13.shape
+    topk = topk_ids.shape[-1]
+    if Hh * 2 != H or act.shape != (M * topk, I2 // 2):
+        raise _lib.FlintError("moe_up_ep: weight / activation shapes mismatch")
+    rc = lib().flint_moe_up_ep(ptr(xn), xn.stride(0), M, ptr(topk_ids), topk, ptr(_u8(w13)), ptr(_u8(s13)), ptr(g13),
+                               int(num_experts), I2 // 2, H, int(expert_lo), n_local, ptr(act), ptr(_moe_ws(xn.device, H)),
+                               PDL, stream_ptr(xn.device))
+    check(rc, "flint_moe_up_ep")
+
+
+@moe_up_ep.register_fake
+def _(xn, topk_ids, w13, s13, g13, num_experts, expert_lo, act):
+    return None
+
+
+@torch.library.custom_op(f"{NS}::moe_down_ep", mutates_args=("y_out",))
+def moe_down_ep(act: torch.Tensor, topk_ids: torch.Tensor, w2: torch.Tensor, s2: torch.Tensor, g2: torch.Tensor,
+                num_experts: int, expert_lo: int, y_out: torch.Tensor) -> None:
+    """Expert-parallel moe_down (flint_moe_down_ep): y_out [M * topk, H] = y of each local route, zero rows for the
+    others (sum over ranks, then moe_combine)."""
+    _lib.require_cuda(act, "moe_down_ep")
+    n_local, H, Ih = w2.shape
+    M, topk = topk_ids.shape
+    if act.shape != (M * topk, Ih * 2) or y_out.shape != (M * topk, H):
+        raise _lib.FlintError("moe_down_ep: weight / activation shapes mismatch")
+    rc = lib().flint_moe_down_ep(ptr(act), M, ptr(topk_ids), topk, ptr(_u8(w2)), ptr(_u8(s2)), ptr(g2), int(num_experts),
+                                 Ih * 2, H, int(expert_lo), n_local, ptr(y_out), ptr(_moe_ws(act.device, H)), PDL,
+                                 stream_ptr(act.device))
+    check(rc, "flint_moe_down_ep")
+
+
+@moe_down_ep.register_fake
+def _(act, topk_ids, w2, s2, g2, num_experts, expert_lo, y_out):
+    return None
+
+
 @torch.library.custom_op(f"{NS}::moe_fused", mutates_args=("out", "res_out", "xn_out", "logits_out", "ids_out",
                                                              "tw_out"))
 def moe_fused(x: torch.Tensor, res: torch.Tensor | None, norm_w: torch.Tensor, eps: float, gate_w: torch.Tensor, topk: int,
@@ -312,10 +394,13 @@ def _(x, res, norm_w, eps, gate_w, topk, score_fn, w13, s13, g13, w2, s2, g2, ex
 
 @torch.library.custom_op(f"{NS}::moe_combine", mutates_args=("out",))
 def moe_combine(y: torch.Tensor, tw: torch.Tensor, out: torch.Tensor) -> None:
-    """out [1, H] = bf16(sum_s tw[s] * y[s]) in slot order."""
+    """out [M, H] = bf16(sum_s tw[m, s] * y[m * topk + s]) in slot order; y [M * topk, H], tw [M, topk]."""
     _lib.require_cuda(y, "moe_combine")
-    topk, H = y.shape
-    rc = lib().flint_moe_combine(ptr(y), ptr(tw), topk, H, ptr(out), PDL, stream_ptr(y.device))
+    M = out.shape[0] if out.dim() == 2 else 1
+    R, H = y.shape
+    if R % M or tw.numel() != R:
+        raise _lib.FlintError("moe_combine: y [M * topk, H], tw [M, topk], out [M, H]")
+    rc = lib().flint_moe_combine(ptr(y), ptr(tw), M, R // M, H, ptr(out), PDL, stream_ptr(y.device))
     check(rc, "flint_moe_combine")
 
 

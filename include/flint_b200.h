@@ -106,6 +106,19 @@ int flint_lm_head_nv4_shard(const void* x, int64_t ldx, const void* res, const v
                             uint64_t* keys_out, void* workspace, int pdl, void* stream);
 /* tokens[m] = the id carried by argmax key keys[m] (M <= 1024). */
 int flint_argmax_keys_to_tokens(const uint64_t* keys, int64_t M, int32_t* tokens, int pdl, void* stream);
+/* Sampled decoding over a head split over R ranks (vocabulary shards).  Each rank:
+ * flint_lm_head_nv4_sample_shard -> its shard's top_k candidates, sorted by (logit desc, id asc), global ids
+ * (index_base + row) in cand_ids int32 [M, top_k] and logits in cand_logits fp32 [M, top_k]; scratch_tokens int32 [M]
+ * receives a discarded draw; workspace as flint_lm_head_sample_workspace_bytes(M, V).  After gathering every rank's
+ * candidates into [R][M][top_k], flint_sample_merge re-selects the top_k of their union and draws with the rule and
+ * uniform of flint_lm_head_nv4_sample: the same token as one GPU over the whole vocabulary.  R <= 8, M <= 8. */
+int flint_lm_head_nv4_sample_shard(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, int64_t M,
+                                   const void* P, const void* S, float gs, int64_t V, int64_t K, int64_t index_base,
+                                   int64_t top_k, int32_t* cand_ids, float* cand_logits, int32_t* scratch_tokens,
+                                   void* workspace, int pdl, void* stream);
+int flint_sample_merge(const int32_t* cand_ids, const float* cand_logits, int64_t R, int64_t M, int64_t top_k,
+                       float temperature, float top_p, const uint64_t* seeds, const int32_t* step, int32_t* token_ids,
+                       int32_t* kept, int pdl, void* stream);
 /* Allocation-free flint_lm_head_nv4 (no counterpart in the reference: the recipe always runs inside vLLM, which
  * allocates).  For callers that cannot allocate device memory at call time -- an engine that has already given all
  * free HBM to its KV-cache pool, a CUDA-graph capture region, a host runtime that only reaches the library through
@@ -190,9 +203,22 @@ int flint_moe_block_ep(const void* x, int64_t ldx, const void* res, const void* 
                        const void* w2, const void* s2, const float* g2, int64_t I, int64_t expert_lo, int64_t n_local,
                        void* y_out, float* topk_weights_out, void* res_out, void* workspace,
                        const flint_l2_prefetch* next, int pdl, void* stream);
-/* out bf16 [H] = bf16(sum_s topk_weights[s] * y[s, :]) in slot order (fp32 FMA): the weighted expert sum of the
- * expert-parallel MoE. */
-int flint_moe_combine(const void* y, const float* topk_weights, int64_t topk, int64_t H, void* out, int pdl, void* stream);
+/* out bf16 [M, H] = bf16(sum_s topk_weights[m, s] * y[m * topk + s, :]) in slot order (fp32 FMA): the weighted
+ * expert sum of the expert-parallel MoE (y summed over ranks first), M <= 8. */
+int flint_moe_combine(const void* y, const float* topk_weights, int64_t M, int64_t topk, int64_t H, void* out, int pdl,
+                      void* stream);
+
+/* Expert-parallel forms of flint_moe_up / flint_moe_down for 1..8 tokens: the routing (topk_ids over all E experts)
+ * is the full one, the weights hold experts expert_lo .. expert_lo + n_local - 1 only.  Up computes the act rows of
+ * the routes whose expert is local; down writes y_out bf16 [M * topk, H]: row r = y of route r (m * topk + slot)
+ * when its expert is local, zeros otherwise.  Summing y_out over ranks (one non-zero term per element, exact) and
+ * flint_moe_combine give flint_moe_down's output bit for bit.  Same workspace as flint_moe_up / flint_moe_down. */
+int flint_moe_up_ep(const void* xn, int64_t ldx, int64_t M, const int32_t* topk_ids, int64_t topk, const void* w13,
+                    const void* s13, const float* g13, int64_t E, int64_t I, int64_t H, int64_t expert_lo, int64_t n_local,
+                    void* act, void* workspace, int pdl, void* stream);
+int flint_moe_down_ep(const void* act, int64_t M, const int32_t* topk_ids, int64_t topk, const void* w2, const void* s2,
+                      const float* g2, int64_t E, int64_t I, int64_t H, int64_t expert_lo, int64_t n_local, void* y_out,
+                      void* workspace, int pdl, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
  * Peer exchange of the multi-GPU decode (one process per GPU; new in this build: the reference decodes on one GPU

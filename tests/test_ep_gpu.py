@@ -1,6 +1,6 @@
 """Sharded decode on 2 GPUs (skipped with fewer): ep_check.py under torchrun decodes a 4-layer model with the experts
-and head rows split over two ranks, once with the in-kernel peer exchange and once with NCCL, and compares both token
-streams and final hidden states with the unsharded model on one GPU (bit-exact)."""
+and head rows split over two ranks in every mode (one-token block with the peer or the NCCL exchange, three-stream
+chain, seeded sampling) and compares token streams and final hidden states with the unsharded model (bit-exact)."""
 import json
 import os
 import subprocess
@@ -24,4 +24,4 @@ def test_sharded_decode_matches_single_gpu():
     lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
     assert r.returncode == 0 and lines, r.stdout[-2000:] + r.stderr[-4000:]
     rep = json.loads(lines[-1])
-    assert rep["match"] and rep["peer"]["match"] and rep["nccl"]["match"], rep
+    assert rep["match"] and all(v["match"] for k, v in rep.items() if isinstance(v, dict)), rep
