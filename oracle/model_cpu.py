@@ -6,6 +6,10 @@ of 8192 rows, patch:295-319) and multiplied in fp32 (the stock path feeding ``co
 360-381, and the GEMVs of fast/attn_gemv2.cu / fp4moe_mar.cu restated on the CPU); attention is a float32 GQA
 softmax over the paged context; routing is softmax top-k renormalised.
 
+Two variants, as the reference can run either way: ``predequantized=False`` dequantises every matrix at every call
+(the literal path); ``predequantized=True`` dequantises all weights to fp32 once at construction (not timed) and
+only multiplies per token (the steady state).
+
 Sample: ``n_tokens`` decode tokens at ``context`` tokens of KV.  To keep host memory bounded the expert tensors of
 one layer are shared by all layers (the per-token work -- which experts are dequantised and multiplied -- is the same
 as with distinct layers); all other weights and the KV cache are per layer.  Weights are random valid NVFP4 bytes.
@@ -45,7 +49,7 @@ def _rmsnorm(x, w, eps):
 
 
 class CpuFlint:
-    def __init__(self, cfg, context: int, seed: int = 0):
+    def __init__(self, cfg, context: int, seed: int = 0, predequantized: bool = False):
         g = torch.Generator().manual_seed(seed)
         c = self.c = cfg
         self.context = context
@@ -61,6 +65,20 @@ class CpuFlint:
         self.embed = (torch.randn((c.vocab, H), generator=g)).to(torch.bfloat16)
         self.head = _rand_nvfp4(g, c.vocab, H)
         self.ones = torch.ones(H)
+        self.fp32 = {}
+        if predequantized:                           # steady state: every matrix dequantised once, up front
+            for i, L in enumerate(self.layers):
+                self.fp32[("qkv", i)] = dequantize_nvfp4(*L["qkv"])
+                self.fp32[("o", i)] = dequantize_nvfp4(*L["o"])
+            for e, (w13, w2) in enumerate(self.experts):
+                self.fp32[("w13", e)] = dequantize_nvfp4(*w13)
+                self.fp32[("w2", e)] = dequantize_nvfp4(*w2)
+            self.fp32[("head", 0)] = dequantize_nvfp4(*self.head)
+
+    def _w(self, key, idx, nv):
+        """fp32 weight: the pre-dequantised copy, or the reference's per-call dequantisation."""
+        w = self.fp32.get((key, idx))
+        return w if w is not None else dequantize_nvfp4(*nv)
 
     @torch.no_grad()
     def decode_token(self, token: int, pos: int) -> int:
@@ -68,11 +86,10 @@ class CpuFlint:
         H, D, nq, nkv = c.hidden, c.head_dim, c.num_heads, c.num_kv_heads
         res = self.embed[token].float()[None]
         h = torch.zeros_like(res)
-        for L in self.layers:
+        for li, L in enumerate(self.layers):
             res = res + h
             x = _rmsnorm(res, self.ones, c.rms_eps)
-            P, S, gs = L["qkv"]
-            y = (x @ dequantize_nvfp4(P, S, gs).t()).to(torch.bfloat16).float()
+            y = (x @ self._w("qkv", li, L["qkv"]).t()).to(torch.bfloat16).float()
             q = y[:, :nq * D].reshape(nq, D)
             L["k"][pos] = y[0, nq * D:(nq + nkv) * D].reshape(nkv, D)
             L["v"][pos] = y[0, (nq + nkv) * D:].reshape(nkv, D)
@@ -81,8 +98,7 @@ class CpuFlint:
             s = torch.einsum("hgd,thd->hgt", q.reshape(nkv, G, D), K) * D ** -0.5
             p = torch.softmax(s, dim=-1)
             attn = torch.einsum("hgt,thd->hgd", p, V).reshape(1, nq * D).to(torch.bfloat16).float()
-            P, S, gs = L["o"]
-            a = (attn @ dequantize_nvfp4(P, S, gs).t()).to(torch.bfloat16).float()
+            a = (attn @ self._w("o", li, L["o"]).t()).to(torch.bfloat16).float()
             res = res + a
             xn = _rmsnorm(res, self.ones, c.rms_eps)
             logits = (xn @ L["gate"].t()).to(torch.bfloat16).float()
@@ -90,21 +106,20 @@ class CpuFlint:
             tw = torch.softmax(top.values, dim=-1)
             out = torch.zeros((1, H))
             for w, e in zip(tw.tolist(), top.indices.tolist()):
-                (P13, S13, g13), (P2, S2, g2) = self.experts[e]
-                gu = xn @ dequantize_nvfp4(P13, S13, g13).t()
+                w13, w2 = self.experts[e]
+                gu = xn @ self._w("w13", e, w13).t()
                 g_, u_ = gu[:, :c.moe_inter], gu[:, c.moe_inter:]
                 act = (torch.nn.functional.silu(g_) * u_).to(torch.bfloat16).float()
-                out += w * (act @ dequantize_nvfp4(P2, S2, g2).t()).to(torch.bfloat16).float()
+                out += w * (act @ self._w("w2", e, w2).t()).to(torch.bfloat16).float()
             h = out.to(torch.bfloat16).float()
         x = _rmsnorm(res + h, self.ones, c.rms_eps)
-        P, S, gs = self.head
-        return int((x @ dequantize_nvfp4(P, S, gs).t()).argmax())
+        return int((x @ self._w("head", 0, self.head).t()).argmax())
 
 
-def time_decode(cfg, n_tokens: int = 1, context: int = 6057, warmup: int = 0) -> dict:
+def time_decode(cfg, n_tokens: int = 1, context: int = 6057, warmup: int = 0, predequantized: bool = False) -> dict:
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    m = CpuFlint(cfg, context)
+    m = CpuFlint(cfg, context, predequantized=predequantized)
     tok = 1
     for i in range(warmup):
         tok = m.decode_token(tok, context + i)
@@ -114,5 +129,7 @@ def time_decode(cfg, n_tokens: int = 1, context: int = 6057, warmup: int = 0) ->
     dt = time.perf_counter() - t0
     return {"value": round(n_tokens / dt, 5), "unit": "tok/s", "cores": threads, "kind": "port",
             "tokens": n_tokens, "seconds": round(dt, 2),
-            "sample": f"{n_tokens} full-model decode token(s) at {context} tokens of KV context; per-call NVFP4 "
-                      "dequantisation + fp32 matmuls (torch CPU), expert tensors shared across layers"}
+            "sample": f"{n_tokens} full-model decode token(s) at {context} tokens of KV context; "
+                      + ("weights dequantised to fp32 once (steady state)" if predequantized else
+                         "per-call NVFP4 dequantisation") + " + fp32 matmuls (torch CPU), expert tensors shared across "
+                      "layers"}
