@@ -261,6 +261,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
   // owning CTAs (partial records) and first record; plus the flattened page count P
   __shared__ int s_segA[kBMaxSeg], s_first[kBMaxSeg], s_nparts[kBMaxSeg], s_recb[kBMaxSeg], s_P;
   __shared__ int s_tk_seg[kBMaxSeg], s_tk[kBMaxSeg], s_ntk, s_go;   // this CTA's merge tickets
+  __shared__ int s_lo, s_hi;                                          // this CTA's flattened page range
   __shared__ __align__(16) bf16 q_tile[8][kBD];
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -353,33 +354,76 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
   __syncthreads();
   const int S = M * a.nkv;
   const int P = s_P;
-  const int Geff = min(G, P);
-  const int lo = cta < Geff ? (int)((unsigned)cta * (unsigned)P / (unsigned)Geff) : P;
-  const int hi = cta < Geff ? (int)((unsigned)(cta + 1) * (unsigned)P / (unsigned)Geff) : P;
 
   if (warp == kBW) {
-    // ---- producer, first: the segment tables (lane sg and sg + 32), off the consumers' critical path; they are
-    // released to the consumers through bar_tab.  CTA c owns flattened pages [c P / Geff, (c + 1) P / Geff); page L
-    // belongs to CTA ceil((L + 1) Geff / P) - 1 (32-bit: the host keeps M * nkv * max_blocks * grid below 2^32). ----
+    // ---- producer, first: the partition, off the consumers' critical path (released to them through bar_tab).
+    // Each CTA works on ONE segment: segment s gets k_s CTAs in proportion to its n_s pages (floor of n_s G / P, at
+    // least 1, at most n_s; spare CTAs to the largest remainders, ties to the lower segment), which split its pages
+    // evenly in CTA order; CTA c0_s + i owns pages [A_s + i n_s / k_s, A_s + (i + 1) n_s / k_s) and writes record
+    // c0_s + i when k_s > 1.  Lane sg (and sg + 32) handles segment sg.  32-bit: the host keeps M * nkv * max_blocks *
+    // grid below 2^32. ----
     {
-      const unsigned Pu = (unsigned)P, Gu = (unsigned)Geff;
-      auto owner = [&](unsigned L) { return (int)(((L + 1u) * Gu + Pu - 1u) / Pu) - 1; };
-      int np[2];
+      const unsigned Pu = (unsigned)P, Gu = (unsigned)G;
+      int n[2], k[2], rm[2], A[2];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int sg = lane + 32 * h;
-        np[h] = 0;
+        n[h] = k[h] = A[h] = 0;
+        rm[h] = -1;
         if (sg < S) {
-          const int b = sg / a.nkv, n = s_npg[b];
-          const int A = a.nkv * s_pre[b] + (sg - b * a.nkv) * n;
-          const int first = n > 0 ? owner((unsigned)A) : 0;
-          np[h] = n > 0 ? owner((unsigned)(A + n - 1)) - first + 1 : 0;
-          s_segA[sg] = A;
-          s_first[sg] = first;
-          s_nparts[sg] = np[h];
+          const int b = sg / a.nkv;
+          n[h] = s_npg[b];
+          A[h] = a.nkv * s_pre[b] + (sg - b * a.nkv) * n[h];
+          if (n[h] > 0) {
+            const unsigned q = (unsigned)n[h] * Gu;
+            k[h] = (int)(q / Pu);
+            rm[h] = (int)(q - (unsigned)k[h] * Pu);
+            if (k[h] == 0) {
+              k[h] = 1;
+              rm[h] = -1;
+            }
+            if (k[h] >= n[h]) {
+              k[h] = n[h];
+              rm[h] = -1;
+            }
+          }
         }
       }
-      int inc0 = np[0], inc1 = np[1];                              // record bases: exclusive scan in segment order
+      auto warp_total = [&]() {
+        int t = k[0] + k[1];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+        return t;
+      };
+      int tot = warp_total();
+      if (tot < G) {                                               // spare CTAs: largest remainders first
+        int rank[2] = {0, 0};
+#pragma unroll 1
+        for (int jj = 0; jj < 64; ++jj) {
+          const int rj = __shfl_sync(0xffffffffu, jj < 32 ? rm[0] : rm[1], jj & 31);
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+            if (rj > rm[h] || (rj == rm[h] && jj < lane + 32 * h)) ++rank[h];
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          if (rm[h] >= 0 && rank[h] < G - tot) ++k[h];
+        tot = warp_total();
+      }
+#pragma unroll 1
+      for (int guard = 0; tot > G && guard < 64; ++guard) {        // segments bumped to one CTA: give back the largest
+        unsigned best = 0u;
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          if (k[h] > 1) best = max(best, ((unsigned)k[h] << 8) | (unsigned)(lane + 32 * h));
+        best = __reduce_max_sync(0xffffffffu, best);
+        if (best == 0u) break;
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          if (k[h] > 1 && (((unsigned)k[h] << 8) | (unsigned)(lane + 32 * h)) == best) --k[h];
+        --tot;
+      }
+      int inc0 = k[0], inc1 = k[1];                                // first CTA of each segment: exclusive scan
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int v0 = __shfl_up_sync(0xffffffffu, inc0, o), v1 = __shfl_up_sync(0xffffffffu, inc1, o);
@@ -389,11 +433,28 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
         }
       }
       const int tot0 = __shfl_sync(0xffffffffu, inc0, 31);
-      if (lane < S) s_recb[lane] = inc0 - np[0];
-      if (lane + 32 < S) s_recb[lane + 32] = tot0 + inc1 - np[1];
+      const int c0[2] = {inc0 - k[0], tot0 + inc1 - k[1]};
+      if (lane == 0) s_lo = s_hi = 0;                              // a CTA without a segment has no pages
+      __syncwarp();
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int sg = lane + 32 * h;
+        if (sg < S) {
+          s_segA[sg] = A[h];
+          s_first[sg] = c0[h];
+          s_nparts[sg] = k[h];
+          s_recb[sg] = c0[h];
+          if (k[h] > 0 && cta >= c0[h] && cta < c0[h] + k[h]) {
+            const int i = cta - c0[h];
+            s_lo = A[h] + i * n[h] / k[h];
+            s_hi = A[h] + (i + 1) * n[h] / k[h];
+          }
+        }
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar_tab);
     }
+    const int lo = s_lo, hi = s_hi;
     // ---- producer: this CTA's pages, in the order the consumers take them, once the resident weights have landed
     // (they are needed first; the pages then stream in under the QKV GEMV and the barrier) ----
     if (lane == 0) {
@@ -424,6 +485,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
     gemv_finish_tagged(red, ngq, M, a.gs_qkv[0], shift, a.y_tag, a.Nqkv / 2, gq0 * 16, ep);
   }
   const bool have_tab = cons_sync_and(mbar_wait(&bar_tab, 0, status));   // segment tables from the producer warp
+  const int lo = s_lo, hi = s_hi;
 
   // ---- B: attention ----
   const int tid = threadIdx.x, g = lane >> 2, t4 = lane & 3;
@@ -846,6 +908,8 @@ extern "C" int flint_attn_block(const void* x, int64_t ldx, const int32_t* token
     return FLINT_ERR_SHAPE;
   const int64_t Nqkv = (num_q_heads + 2 * num_kv_heads) * kBD, Ko = num_q_heads * kBD;
   if (Ko % kSliceK != 0 || Ko > 8192) return FLINT_ERR_SHAPE;
+  // every (request, kv head) segment gets a CTA of its own
+  if (M * num_kv_heads > sms) return FLINT_ERR_SHAPE;
   // the kernel's page partition runs in 32-bit arithmetic: pages x (grid + 1) must stay below 2^32
   if ((uint64_t)M * (uint64_t)num_kv_heads * (uint64_t)max_blocks * (uint64_t)(sms + 1) >= (1ull << 32))
     return FLINT_ERR_SHAPE;
