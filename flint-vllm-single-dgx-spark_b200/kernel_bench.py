@@ -38,7 +38,8 @@ def _package():
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", required=True)
+    ap.add_argument("--kernel", required=True, help="a layer op name (attn_block, moe_block, route, ...), head, "
+                    "head_sample, or all")
     ap.add_argument("--ctx", type=int, default=6057)
     ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--reps", type=int, default=5)
@@ -56,7 +57,13 @@ def main(argv=None):
     prompt = np.random.default_rng(3).integers(0, cfg.vocab, size=(args.batch, args.ctx))
     dec.fill_kv_random(prompt)
     dec.decode(1)                      # one real step so routing, q and activations hold live values
-    name = args.kernel
+    names = [n for n, _ in dec.layer_ops(0)] + ["head"] if args.kernel == "all" else [args.kernel]
+    for name in names:
+        time_kernel(name, args, dec, model, cfg, dev)
+
+
+def time_kernel(name, args, dec, model, cfg, dev):
+    """One kernel type alone: a CUDA graph of its per-layer launches (or repeated head launches), CUDA events."""
     if name == "head":
         fns = [dec.head_op()] * max(args.layers, 4)
     elif name == "head_sample":
@@ -86,9 +93,10 @@ def main(argv=None):
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / (args.reps * len(fns))
     nbytes = dec.algorithmic_bytes("head" if name.startswith("head") else name, args.ctx)
-    print(json.dumps({"kernel": name, "batch": args.batch, "ctx": args.ctx, "launches": args.reps * len(fns),
-                      "us_per_launch": round(us, 2), "bytes_per_launch": nbytes,
+    print(json.dumps({"kernel": name, "batch": args.batch, "moe": dec.moe, "ctx": args.ctx,
+                      "launches": args.reps * len(fns), "us_per_launch": round(us, 2), "bytes_per_launch": nbytes,
                       "GBps": round(nbytes / us / 1e3, 1)}), flush=True)
+    del g
 
 
 if __name__ == "__main__":

@@ -143,7 +143,9 @@ class Decoder:
         attention + O in one persistent launch) or "chain" (three launches).  sampling: None for greedy decode, or
         {"temperature", "top_k", "top_p", "seeds"} (one int64 seed per stream) for the seeded top-k -> top-p draw of
         flint_lm_head_nv4_sample; the draw of step t uses the Philox counter (t, stream)."""
-        moe = moe or ("block" if batch == 1 else "chain")
+        # measured per layer at 6K context: one stream, the block; 2..5 streams, the chain (67.7 us at 4 against the
+        # fused launch's 70.9); 6..8, the fused launch (118 us at 8 against the chain's 135).  Sharded: block or chain.
+        moe = moe or ("block" if batch == 1 else "chain" if batch <= 5 or model.world > 1 else "fused")
         if moe not in ("block", "chain", "fused"):
             raise ValueError(f"moe must be 'block', 'chain' or 'fused', got {moe!r}")
         if moe == "block" and batch != 1:
