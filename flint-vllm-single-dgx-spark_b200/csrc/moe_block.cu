@@ -303,20 +303,23 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
 
   // ---- D: this CTA's 16 output rows over every routed expert, then the slot-order sum ----
   if (has_dn) {
-    // the act rows of the local slots, once their words carry this launch's tag (no grid barrier)
-    stage_rows_f16_tagged(act_g, s_nlocal, I, ep, xa, shift_a, red_n, kXT, 1, status, s_local);
-    if (s_nlocal == 0 || xsync_and(mbar_wait(&bar_dn, 0, status))) {
+    {
       if (warp < topk && (s_ids[warp] < a.e_lo || s_ids[warp] >= a.e_hi)) {
         if (lane < 16) ybuf[warp][lane] = 0.f;           // expert of another rank
       } else if (warp < topk) {
+        // warp s: slot s's act row once its words carry this launch's tag (each warp on its own row, no block-wide
+        // staging), then the 16 down rows of this block for that slot
         const int s = warp, e = s_ids[s] - a.e_lo;
+        __half* arow = xa + s * xs_stride(I);
+        stage_row_f16_tagged_warp(act_g + (int64_t)s * (I / 2), I, ep, arow, &shift_a[s], lane, status);
         const uint8_t* b = dn_base + s * a.dslot_bytes;
         const bool act_col = g == 0;
-        const __half* arow = xa + s * xs_stride(I);
         float acc[4][4];
         zero_acc(acc);
-        #pragma unroll 1
-        for (int ks = 0; ks < nks_d; ++ks) consume_stage(b + ks * 2048, b + nks_d * 2048 + ks * 256, 0, g, t, ks, arow, act_col, acc);
+        if (__all_sync(0xffffffffu, mbar_wait(&bar_dn, 0, status))) {
+          #pragma unroll 1
+          for (int ks = 0; ks < nks_d; ++ks) consume_stage(b + ks * 2048, b + nks_d * 2048 + ks * 256, 0, g, t, ks, arow, act_col, acc);
+        }
         float d[4];
         sum_acc(acc, d);
         if (t == 0) {
@@ -405,7 +408,7 @@ static int moe_block_launch(const void* x, int64_t ldx, const void* res, const v
   if (e_lo < 0 || n_local < 1 || e_lo + n_local > E || (y_out && !topk_weights_out)) return FLINT_ERR_ARGUMENT;
   const int sms = num_sms();
   if (sms <= 0) return FLINT_ERR_DEVICE;
-  if (H != 2048 || E < 32 || E % 32 != 0 || E > 256 || E > 2 * sms || topk < 1 || topk * (I / 8) > 4 * kXT ||
+  if (H != 2048 || E < 32 || E % 32 != 0 || E > 256 || E > 2 * sms || topk < 1 || I > 1024 ||
       topk > kXMaxSlots || topk > E || I < kSliceK || I % kSliceK != 0 || ldx < H || score_fn < 0 || score_fn > 1 ||
       H / 16 > sms)
     return FLINT_ERR_SHAPE;

@@ -111,4 +111,69 @@ __device__ __forceinline__ void stage_rows_f16_tagged(const unsigned long long* 
   sync();
 }
 
+// One warp stages one row published as tagged words (the pair layout of stage_rows_f16_tagged): polls its 16-byte
+// units until they carry `epoch`, takes the row's max |value| (unsigned max over the float bits, as the block-wide
+// form's atomicMax does), derives the same power-of-two shift and writes the f16 row.  K <= 1024.
+__device__ __forceinline__ void stage_row_f16_tagged_warp(const unsigned long long* __restrict__ src, int K,
+                                                          unsigned epoch, __half* xs_row, int* shift_out, int lane,
+                                                          unsigned* status) {
+  const int K8 = K >> 3;
+  constexpr int kU = 4;
+  uint32_t w[kU][4];
+  unsigned need = 0, got = 0;
+#pragma unroll
+  for (int i = 0; i < kU; ++i) {
+    w[i][0] = w[i][1] = w[i][2] = w[i][3] = 0u;
+    if (lane + 32 * i < K8) need |= 1u << i;
+  }
+#pragma unroll 1
+  for (unsigned it = 0; got != need; ++it) {
+    if (it == FLINT_WAIT_LIMIT) {
+      atomicOr(status, STATUS_WAIT_TIMEOUT);
+      break;
+    }
+#pragma unroll
+    for (int i = 0; i < kU; ++i) {
+      if ((need & ~got) & (1u << i)) {
+        const unsigned long long* p = src + (int64_t)(lane + 32 * i) * 4;
+        const ulonglong2 a = ld_tagged2(p), b = ld_tagged2(p + 2);
+        if (tag_is(a.x, epoch) && tag_is(a.y, epoch) && tag_is(b.x, epoch) && tag_is(b.y, epoch)) {
+          w[i][0] = (uint32_t)a.x;
+          w[i][1] = (uint32_t)a.y;
+          w[i][2] = (uint32_t)b.x;
+          w[i][3] = (uint32_t)b.y;
+          got |= 1u << i;
+        }
+      }
+    }
+  }
+  unsigned mxb = 0u;
+#pragma unroll
+  for (int i = 0; i < kU; ++i) {
+    float f[8];
+    bf16x8_to_f32(make_uint4(w[i][0], w[i][1], w[i][2], w[i][3]), f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) mxb = max(mxb, __float_as_uint(fabsf(f[j])));
+  }
+  mxb = __reduce_max_sync(0xffffffffu, mxb);
+  const float mx = __uint_as_float(mxb);
+  int s = 0;
+  if (mx > 0.f && !(mx != mx) && mx <= 3.0e38f) s = 14 - ((int)((mxb >> 23) & 0xFF) - 127);
+  if (lane == 0) *shift_out = s;
+#pragma unroll
+  for (int i = 0; i < kU; ++i) {
+    if (!((need >> i) & 1u)) continue;
+    float f[8];
+    bf16x8_to_f32(make_uint4(w[i][0], w[i][1], w[i][2], w[i][3]), f);
+    uint32_t h[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __half2 v = __floats2half2_rn(scale_pow2(f[2 * j], s), scale_pow2(f[2 * j + 1], s));
+      h[j] = *reinterpret_cast<uint32_t*>(&v);
+    }
+    *reinterpret_cast<uint4*>(xs_row + xs_perm((lane + 32 * i) * 8)) = make_uint4(h[0], h[1], h[2], h[3]);
+  }
+  __syncwarp();
+}
+
 }  // namespace flint
