@@ -160,6 +160,87 @@ __device__ __noinline__ void gemv_resident(const uint8_t* wc, const uint8_t* wsc
   }
 }
 
+// O projection streamed over the attention output (tagged words, src[m * src_words + k / 2]): warp w takes K slices
+// w, w + 8, ... (256 k = two heads each) and stages each one as soon as its words carry `ep` -- per token with the
+// slice's own power-of-two shift (the rule of stage_rows_f16 over the slice) -- so a warp starts while other heads are
+// still being merged.  Each slice's partial tile is rescaled by 2^-shift before it joins the warp's sum; partial
+// tiles go to red[gi][w][16][8] with the scales applied (finish with zero shifts).
+__device__ __noinline__ void gemv_stream_o(const uint8_t* wc, const uint8_t* wsc, int ng, int nks,
+                                           const unsigned long long* src, int64_t src_words, unsigned ep, __half* xs,
+                                           int K, int M, float* red, int warp, int lane, unsigned* status) {
+  const int g = lane >> 2, t = lane & 3;
+  const bool active = g < M;
+  const __half* xrow = xs + (active ? g : 0) * xs_stride(K);
+  float tot[kBGO][4];
+#pragma unroll
+  for (int gi = 0; gi < kBGO; ++gi) tot[gi][0] = tot[gi][1] = tot[gi][2] = tot[gi][3] = 0.f;
+#pragma unroll 1
+  for (int ks = warp; ks < nks; ks += kBW) {
+    int my_sh = 0;                                     // lane m < M: the shift of token m for this slice
+#pragma unroll 1
+    for (int m = 0; m < M; ++m) {
+      const unsigned long long* p = src + (int64_t)m * src_words + ks * 128 + lane * 4;
+      ulonglong2 w0, w1;
+      unsigned it = 0;
+#pragma unroll 1
+      for (;; ++it) {
+        w0 = ld_tagged2(p);
+        w1 = ld_tagged2(p + 2);
+        if (tag_is(w0.x, ep) && tag_is(w0.y, ep) && tag_is(w1.x, ep) && tag_is(w1.y, ep)) break;
+        if (it == FLINT_WAIT_LIMIT) {
+          atomicOr(status, STATUS_WAIT_TIMEOUT);
+          break;
+        }
+      }
+      const uint4 v = make_uint4((uint32_t)w0.x, (uint32_t)w0.y, (uint32_t)w1.x, (uint32_t)w1.y);
+      float f[8];
+      bf16x8_to_f32(v, f);
+      unsigned mxb = 0u;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mxb = max(mxb, __float_as_uint(fabsf(f[j])));
+      mxb = __reduce_max_sync(0xffffffffu, mxb);
+      const float mx = __uint_as_float(mxb);
+      int sh = 0;
+      if (mx > 0.f && !(mx != mx) && mx <= 3.0e38f) sh = 14 - ((int)((mxb >> 23) & 0xFF) - 127);
+      if (lane == m) my_sh = sh;
+      uint32_t h[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __half2 hv = __floats2half2_rn(scale_pow2(f[2 * j], sh), scale_pow2(f[2 * j + 1], sh));
+        h[j] = *reinterpret_cast<uint32_t*>(&hv);
+      }
+      *reinterpret_cast<uint4*>(xs + m * xs_stride(K) + xs_perm(ks * 256 + lane * 8)) = make_uint4(h[0], h[1], h[2], h[3]);
+    }
+    __syncwarp();
+    const int c0 = 2 * t, c1 = 2 * t + 1;              // this lane's tile columns (tokens)
+    const int sh0 = __shfl_sync(0xffffffffu, my_sh, c0 & 31), sh1 = __shfl_sync(0xffffffffu, my_sh, c1 & 31);
+#pragma unroll
+    for (int gi = 0; gi < kBGO; ++gi) {
+      if (gi >= ng) break;
+      float acc[4][4];
+      zero_acc(acc);
+      consume_stage(wc + (gi * nks + ks) * 2048, wsc + (gi * nks + ks) * 256, 0, g, t, ks, xrow, active, acc);
+      float d[4];
+      sum_acc(acc, d);
+      tot[gi][0] += scale_pow2(d[0], -sh0);
+      tot[gi][1] += scale_pow2(d[1], -sh1);
+      tot[gi][2] += scale_pow2(d[2], -sh0);
+      tot[gi][3] += scale_pow2(d[3], -sh1);
+    }
+    __syncwarp();
+  }
+  const int r0 = tile_phi(g), r1 = r0 + 8, n0 = 2 * t, n1 = 2 * t + 1;
+#pragma unroll
+  for (int gi = 0; gi < kBGO; ++gi) {
+    if (gi >= ng) break;
+    float* rt = red + (gi * kBW + warp) * 128;
+    rt[r0 * 8 + n0] = tot[gi][0];
+    rt[r0 * 8 + n1] = tot[gi][1];
+    rt[r1 * 8 + n0] = tot[gi][2];
+    rt[r1 * 8 + n1] = tot[gi][3];
+  }
+}
+
 // out[m][row0 + 16 gi + r] = bf16(sum_w red[gi][w][r][m] * gs * 2^-shift[m]); consumer threads.
 __device__ __forceinline__ void gemv_finish(const float* red, int ng, int M, float gs, const int* shift, bf16* out,
                                             int64_t ld, int row0) {
@@ -827,12 +908,13 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
   }
   pdl_trigger();
 
-  // ---- C: O projection from the resident weights ----
+  // ---- C: O projection from the resident weights, each warp's K slices staged as their heads arrive ----
   if (ngo > 0) {
-    // the attention output of every head, once all its words carry this launch's tag (no grid barrier)
-    stage_rows_f16_tagged(a.attn_tag, M, a.Ko, ep, xs_o, shift, red_n, kBCons, 1, status);
+    cons_sync();                                                   // xs_o overlays the merge scratch of B2
+    if (tid < 8) shift[tid] = 0;                                   // the slices' scales are applied in the sums
     if (cons_sync_and(mbar_wait(&bar_wo, 0, status))) {
-      gemv_resident(wo, wo + a.wo_scale_off, ngo, a.nks_o, xs_o, a.Ko, M, red, warp, lane);
+      gemv_stream_o(wo, wo + a.wo_scale_off, ngo, a.nks_o, a.attn_tag, a.Ko / 2, ep, xs_o, a.Ko, M, red, warp, lane,
+                    status);
       cons_sync();
       gemv_finish(red, ngo, M, a.gs_o[0], shift, a.out, a.ldr, go0 * 16);
     }
