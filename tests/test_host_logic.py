@@ -37,3 +37,56 @@ def test_c_abi_rejects_bad_moe_shapes(fb):
     # align buffers shorter than vLLM's allocation are refused
     assert lib.flint_moe_align(16, 64, 128, 16, 16, 100, 16, 10, 16, 16, 0, None) == 1
     assert lib.flint_moe_workspace_bytes(2048) >= 64 * 2048 * 2
+
+
+def _attention_partition(pages_per_request, nkv, G):
+    """Python statement of the attention block's page partition (csrc/attn_block.cu, producer warp): segment s (request
+    b, kv head) gets k_s = floor(n_s G / P) CTAs, at least 1 and at most n_s, spare CTAs to the largest remainders
+    (ties to the lower segment); CTA c0_s + i owns pages [A_s + i n_s / k_s, A_s + (i + 1) n_s / k_s)."""
+    S = len(pages_per_request) * nkv
+    pre = np.concatenate([[0], np.cumsum(pages_per_request)]).astype(int)
+    P = nkv * int(pre[-1])
+    n = [int(pages_per_request[s // nkv]) for s in range(S)]
+    A = [nkv * int(pre[s // nkv]) + (s % nkv) * n[s] for s in range(S)]
+    k, rm = [0] * S, [-1] * S
+    for s in range(S):
+        if n[s]:
+            q = n[s] * G
+            k[s], rm[s] = q // P, q % P
+            if k[s] == 0:
+                k[s], rm[s] = 1, -1
+            if k[s] >= n[s]:
+                k[s], rm[s] = n[s], -1
+    left = G - sum(k)
+    if left > 0:
+        order = sorted(range(S), key=lambda s: (-rm[s], s))
+        for s in order[:left]:
+            if rm[s] >= 0:
+                k[s] += 1
+    while sum(k) > G:
+        s = max((v, i) for i, v in enumerate(k) if v > 1)[1]
+        k[s] -= 1
+    c0 = np.concatenate([[0], np.cumsum(k)]).astype(int)
+    owner = {}
+    for s in range(S):
+        for i in range(k[s]):
+            lo, hi = A[s] + i * n[s] // k[s], A[s] + (i + 1) * n[s] // k[s]
+            for L in range(lo, hi):
+                owner[L] = (int(c0[s]) + i, s)
+    return k, owner, P
+
+
+@pytest.mark.parametrize("pages,nkv,G", [([379], 4, 148), ([379, 2, 0, 16384], 4, 148), ([1], 8, 148),
+                                         ([17] * 8, 8, 148), ([1000, 3, 3, 3, 3, 3, 3, 3], 4, 132)])
+def test_attention_partition_invariants(pages, nkv, G):
+    k, owner, P = _attention_partition(pages, nkv, G)
+    assert sum(k) <= G
+    assert len(owner) == P                                  # every page has exactly one owner
+    seg_of_cta = {}
+    for cta, s in owner.values():
+        assert seg_of_cta.setdefault(cta, s) == s           # no CTA spans two segments
+    per_seg = [sum(1 for v in owner.values() if v[1] == s) for s in range(len(pages) * nkv)]
+    for s, (ks, ns) in enumerate(zip(k, per_seg)):
+        assert (ks == 0) == (ns == 0)
+    if pages == [379] and nkv == 4:
+        assert k == [37, 37, 37, 37]                        # the single-stream 6K case: 148 CTAs, 37 per kv head
