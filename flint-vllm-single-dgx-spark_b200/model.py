@@ -18,8 +18,6 @@ and the position / KV-slot bookkeeping runs on the device), so consecutive steps
 """
 from __future__ import annotations
 
-import math
-import time
 from dataclasses import dataclass
 
 import numpy as np

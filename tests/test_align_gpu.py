@@ -3,7 +3,7 @@ import numpy as np
 import pytest
 import torch
 
-from oracle.align import align_sizes, deterministic_align
+from oracle.align import deterministic_align
 
 pytestmark = pytest.mark.gpu
 needs_cuda = pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device")
