@@ -56,3 +56,20 @@ def shard_key(logits: np.ndarray, base: int) -> int:
 
 def key_token(k: int) -> int:
     return 0xFFFFFFFF - ((k + (1 << 64)) % (1 << 64) & 0xFFFFFFFF)
+
+
+def shard_candidates(logits: np.ndarray, base: int, k: int) -> tuple[np.ndarray, np.ndarray]:
+    """The k best (global id, fp32 logit) pairs of one vocabulary shard, value descending, lowest id first on ties:
+    what lm_head_sample_shard writes for one row."""
+    v = np.asarray(logits, np.float32)
+    order = np.lexsort((np.arange(v.size), -v.astype(np.float64)))[:k]
+    return (order + base).astype(np.int64), v[order]
+
+
+def merge_candidates(ids: np.ndarray, vals: np.ndarray, k: int) -> tuple[np.ndarray, np.ndarray]:
+    """The k best of the gathered candidates of all shards ([R, k] each) under the same order (value descending,
+    lowest global id first): what sample_merge selects before its draw.  Every member of the global top-k is in its
+    own shard's top-k, so the result equals the top-k of the whole vocabulary."""
+    ids, vals = np.asarray(ids).reshape(-1), np.asarray(vals, np.float32).reshape(-1)
+    order = np.lexsort((ids, -vals.astype(np.float64)))[:k]
+    return ids[order], vals[order]
