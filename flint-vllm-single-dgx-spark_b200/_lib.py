@@ -72,6 +72,8 @@ SIGNATURES: dict[str, tuple] = {
     "flint_decode_attention_splits": (I64, [I64, I64]),
     "flint_decode_attention_workspace_bytes": (I64, [I64, I64, I64]),
     "flint_decode_advance": (I32, [P, I64, P, P, P, P, I64, I64, I64, P, I64, P, I64, P, I32, P]),
+    "flint_gguf_nvfp4_repack": (I32, [P, I64, I64, P, P, P, I32, P]),
+    "flint_nvfp4_dequant": (I32, [P, P, I64, I64, P, I32, P, I32, P]),
     "flint_decode_attention": (I32, [P, I64, P, I64, I64, I64, I64, P, I64, I64, P, P, I64, F32, I64, I64, P, I64, I64, P,
                                      I32, P]),
 }

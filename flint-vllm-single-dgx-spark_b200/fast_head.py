@@ -121,11 +121,46 @@ def _log(msg):
     print(f"[flint-fast-head] {msg}", file=sys.stderr, flush=True)
 
 
+def _nv4_from_gguf(model, W):
+    """The head's native NVFP4 tensors straight from the checkpoint (``model.gguf_path``, tensor ``output.weight``),
+    repacked on the GPU and checked bit-exact against the bf16 weight the stock loader produced (``e2m1 * e4m3``,
+    the dequantised head); None on a mismatch (reference: fast/fast_head.py:271-282)."""
+    import gguf
+    from .gguf_nvfp4 import _as_tensor, _repack_nvfp4, dequantize_nvfp4
+    reader = gguf.GGUFReader(model.gguf_path)
+    t = {x.name: x for x in reader.tensors}["output.weight"]
+    P, S = _repack_nvfp4(_as_tensor(t.data).to(W.device), int(t.shape[0]))
+    ok = tuple(P.shape) == (W.shape[0], W.shape[1] // 2)
+    for a in range(0, W.shape[0] if ok else 0, 8192):
+        ok &= bool(torch.equal(dequantize_nvfp4(P[a:a + 8192], S[a:a + 8192], out_dtype=torch.bfloat16),
+                               W[a:a + 8192]))
+    return (P.contiguous(), S.contiguous()) if ok else None
+
+
 def _build(model):
-    """The model exposes its NVFP4 head as ``model.lm_head.{weight (u8), weight_scale (E4M3), weight_scale_2}``
-    and an optional ``model.logits_processor.scale`` (fp32, multiplies the logits)."""
+    """Two ways in.  (1) The model exposes its NVFP4 head as ``model.lm_head.{weight (u8), weight_scale (E4M3),
+    weight_scale_2}``.  (2) The reference's: ``model.lm_head.weight`` is the bf16 dequantised head (``e2m1 * e4m3``)
+    with its global scale in ``model.logits_processor.scale``, and ``model.gguf_path`` names the checkpoint the
+    NVFP4 tensors are repacked from (checked bit-exact against the bf16 weight).  An optional
+    ``model.logits_processor.scale`` (fp32) multiplies the logits."""
     lm = model.lm_head
     P = getattr(lm, "weight", None)
+    lp = getattr(model, "logits_processor", None)
+    if (P is not None and P.dtype == torch.bfloat16 and P.dim() == 2 and getattr(lm, "tp_size", 1) == 1
+            and getattr(model, "gguf_path", None)):
+        nv4 = None
+        try:
+            nv4 = _nv4_from_gguf(model, P.data)
+        except Exception as e:
+            _log(f"nv4 repack failed: {type(e).__name__}: {e}")
+        if nv4 is None:
+            _log("nv4 head unavailable (repack mismatch/failure) -> fast head disabled")
+            _state["failed"] = True
+            return
+        scale = float(getattr(lp, "scale", 1.0) if lp is not None else 1.0)
+        _state["head"] = FastHead(P.data, scale, "nv4", nv4)
+        _state["org_vocab"] = int(getattr(lp, "org_vocab_size", P.shape[0]) if lp is not None else P.shape[0])
+        return
     S = getattr(lm, "weight_scale", None)
     gs = getattr(lm, "weight_scale_2", None)
     ok = (P is not None and S is not None and gs is not None and P.dtype == torch.uint8 and P.dim() == 2
@@ -134,7 +169,6 @@ def _build(model):
         _log("fast head disabled: unsupported lm_head")
         _state["failed"] = True
         return
-    lp = getattr(model, "logits_processor", None)
     scale = _scale_value(gs) * float(getattr(lp, "scale", 1.0) if lp is not None else 1.0)
     _state["head"] = FastHead(None, scale, "nv4", (P, S))
     _state["org_vocab"] = int(getattr(lp, "org_vocab_size", P.shape[0]) if lp is not None else P.shape[0])

@@ -10,6 +10,12 @@ times.  Prints one JSON line: microseconds per launch, algorithmic bytes per lau
 those of Decoder.layer_ops (attn_block, or qkv / attention / o with --attn chain; route, up, down, or moe_fused with --moe fused)
 plus head and head_sample.  This is
 also the small case used for full ncu captures of one kernel.
+
+    python flint-vllm-single-dgx-spark_b200/kernel_bench.py --kernel gguf_repack|nvfp4_dequant [--rows 151552]
+        [--cols 2048] [--reps 20]
+
+times the checkpoint-format kernels on one tensor of --rows x --cols values (default: the LM head, 174.6 MB of GGUF
+bytes, larger than L2) and the CPU oracle beside them on a bounded slice of the same tensor.
 """
 from __future__ import annotations
 
@@ -46,8 +52,12 @@ def main(argv=None):
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--moe", default=None, choices=["block", "chain", "fused"])
     ap.add_argument("--attn", default="block", choices=["block", "chain"])
+    ap.add_argument("--rows", type=int, default=151552)
+    ap.add_argument("--cols", type=int, default=2048)
     args = ap.parse_args(argv)
     _package()
+    if args.kernel in ("gguf_repack", "nvfp4_dequant"):
+        return time_format_kernel(args)
     from flint_b200.model import Decoder, FlintConfig, FlintModel
 
     cfg = FlintConfig(layers=args.layers)
@@ -97,6 +107,69 @@ def time_kernel(name, args, dec, model, cfg, dev):
                       "launches": args.reps * len(fns), "us_per_launch": round(us, 2), "bytes_per_launch": nbytes,
                       "GBps": round(nbytes / us / 1e3, 1)}), flush=True)
     del g
+
+
+def time_format_kernel(args):
+    """GGUF -> ModelOpt repack (36 B read + 36 B written per 64 values) or the bf16 dequant (9 B read + 32 B written
+    per 16 values) of one --rows x --cols tensor: CUDA events around one replay of a graph of --reps launches, after
+    3 warm-ups (the tensor is larger than L2, so back-to-back launches do not hit in it); the CPU oracle
+    on 4096 rows of the same tensor, scaled per byte."""
+    import time
+    sys.path.insert(0, os.path.dirname(HERE))
+    from oracle import nvfp4 as onv
+    dev = torch.device("cuda", torch.cuda.current_device())
+    ops = torch.ops.flint_b200
+    R, C = args.rows, args.cols
+    g = torch.Generator(device=dev).manual_seed(17)
+    blocks = torch.randint(0, 256, (R, C // 64, 36), dtype=torch.uint8, device=dev, generator=g)
+    blocks[..., :4] &= 0x7E                              # finite scales only
+    blocks = blocks.reshape(R, C // 64 * 36)
+    packed = torch.empty((R, C // 2), dtype=torch.uint8, device=dev)
+    scales = torch.empty((R, C // 16), dtype=torch.uint8, device=dev)
+    bad = torch.zeros(1, dtype=torch.int32, device=dev)
+    if args.kernel == "gguf_repack":
+        fn = lambda: ops.gguf_nvfp4_repack(blocks, C, packed, scales, bad)
+        nbytes = 2 * blocks.numel()
+    else:
+        ops.gguf_nvfp4_repack(blocks, C, packed, scales, bad)
+        out = torch.empty((R, C), dtype=torch.bfloat16, device=dev)
+        fn = lambda: ops.nvfp4_dequant(packed, scales, None, out)
+        nbytes = packed.numel() + scales.numel() + 2 * out.numel()
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()                      # --reps launches back to back, no host gaps between them
+    with torch.cuda.graph(graph):
+        for _ in range(args.reps):
+            fn()
+    graph.replay()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    graph.replay()
+    e1.record(st)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / args.reps
+    del graph
+    assert int(bad.item()) == 0
+    rows = min(R, 4096)
+    hb = blocks[:rows].cpu().numpy()
+    t0 = time.perf_counter()
+    Po, So = onv.repack_gguf_nvfp4(hb, C)
+    if args.kernel == "nvfp4_dequant":
+        onv.bf16_bits(onv.dequantize_nvfp4(Po, So))
+    cpu_s = (time.perf_counter() - t0) * R / rows
+    peak = None
+    peaks = os.path.join(os.path.dirname(HERE), "MEASURED_PEAKS.json")
+    if os.path.exists(peaks):
+        peak = json.load(open(peaks)).get("hbm_gbs")
+    gbps = nbytes / us / 1e3
+    print(json.dumps({"kernel": args.kernel, "rows": R, "cols": C, "launches": args.reps,
+                      "us_per_launch": round(us, 2), "bytes_per_launch": nbytes, "GBps": round(gbps, 1),
+                      "frac_of_measured_hbm": round(gbps / peak, 3) if peak else None,
+                      "cpu_oracle_ms_per_tensor": round(cpu_s * 1e3, 1), "cpu_sample_rows": rows,
+                      "cpu_cores": 1}), flush=True)
 
 
 if __name__ == "__main__":

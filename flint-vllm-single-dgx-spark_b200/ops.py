@@ -666,3 +666,59 @@ def decode_advance(tokens: torch.Tensor, positions: torch.Tensor, seq_lens: torc
 @decode_advance.register_fake
 def _(tokens, positions, seq_lens, slots, block_tables, block_size, history, step, next_tokens):
     return None
+
+
+# ------------------------------------------------------------------------------------------------------------
+# checkpoint format: GGUF NVFP4 -> ModelOpt NVFP4, and the exact dequant
+# ------------------------------------------------------------------------------------------------------------
+@torch.library.custom_op(f"{NS}::gguf_nvfp4_repack", mutates_args=("packed", "scales", "bad_blocks"))
+def gguf_nvfp4_repack(blocks: torch.Tensor, n_cols: int, packed: torch.Tensor, scales: torch.Tensor,
+                      bad_blocks: torch.Tensor) -> None:
+    """GGUF NVFP4 super-blocks u8 [..., n_cols/64*36] -> packed u8 [..., n_cols/2] and E4M3 bits u8
+    [..., n_cols/16]; bad_blocks (int32 [1], zeroed by the caller) counts warps that met the scale byte 0xFF."""
+    _lib.require_cuda(blocks, "gguf_nvfp4_repack")
+    if n_cols % 64 or blocks.shape[-1] != n_cols // 64 * 36:
+        raise _lib.FlintError(f"gguf_nvfp4_repack: last dim {blocks.shape[-1]} is not {n_cols}/64*36")
+    rows = blocks.numel() // blocks.shape[-1] if blocks.shape[-1] else 0
+    if packed.numel() != rows * n_cols // 2 or scales.numel() != rows * n_cols // 16:
+        raise _lib.FlintError("gguf_nvfp4_repack: output sizes do not match the input")
+    if not (blocks.is_contiguous() and packed.is_contiguous() and scales.is_contiguous()):
+        raise _lib.FlintError("gguf_nvfp4_repack: tensors must be contiguous")
+    if rows == 0:
+        return
+    rc = lib().flint_gguf_nvfp4_repack(ptr(blocks), rows, n_cols, ptr(packed), ptr(scales), ptr(bad_blocks), 0,
+                                       stream_ptr(blocks.device))
+    check(rc, "flint_gguf_nvfp4_repack")
+
+
+@gguf_nvfp4_repack.register_fake
+def _(blocks, n_cols, packed, scales, bad_blocks):
+    return None
+
+
+@torch.library.custom_op(f"{NS}::nvfp4_dequant", mutates_args=("out",))
+def nvfp4_dequant(P: torch.Tensor, S: torch.Tensor, global_scale: torch.Tensor | None, out: torch.Tensor) -> None:
+    """out [..., K] (fp32 or bf16) = e2m1(P) * e4m3(S) (* global_scale, one fp32 scalar on the device)."""
+    _lib.require_cuda(P, "nvfp4_dequant")
+    K = P.shape[-1] * 2
+    rows = P.numel() // P.shape[-1] if P.shape[-1] else 0
+    if S.numel() != rows * K // 16 or out.numel() != rows * K or out.dtype not in (torch.float32, torch.bfloat16):
+        raise _lib.FlintError(f"nvfp4_dequant: weight {tuple(P.shape)}, scales {tuple(S.shape)}, "
+                              f"out {tuple(out.shape)} {out.dtype}")
+    if not (P.is_contiguous() and S.is_contiguous() and out.is_contiguous()):
+        raise _lib.FlintError("nvfp4_dequant: tensors must be contiguous")
+    gs = None
+    if global_scale is not None:
+        if global_scale.numel() != 1 or global_scale.dtype != torch.float32 or global_scale.device != P.device:
+            raise _lib.FlintError("nvfp4_dequant: global_scale must be one fp32 value on the weight's device")
+        gs = ptr(global_scale)
+    if rows == 0:
+        return
+    rc = lib().flint_nvfp4_dequant(ptr(_u8(P)), ptr(_u8(S)), rows, K, gs, 1 if out.dtype == torch.float32 else 0,
+                                   ptr(out), 0, stream_ptr(P.device))
+    check(rc, "flint_nvfp4_dequant")
+
+
+@nvfp4_dequant.register_fake
+def _(P, S, global_scale, out):
+    return None

@@ -344,6 +344,26 @@ int flint_decode_advance(const int32_t* tokens, int64_t M, int64_t* positions, i
                          int32_t* history, int64_t hist_stride, int32_t* step, int64_t max_steps, int32_t* next_tokens,
                          int pdl, void* stream);
 
+/* ------------------------------------------------------------------------------------------------
+ * Checkpoint format: GGUF NVFP4 (ggml type 40) -> the ModelOpt NVFP4 layout of every kernel above.
+ * ------------------------------------------------------------------------------------------------ */
+
+/* Replaces gguf_nvfp4._repack_nvfp4 (patch:269-288).  blocks: rows x (n_cols/64) GGUF super-blocks of 36 bytes
+ * (4 UE4M3 scale bytes, then 4 x 8 code bytes: low nibbles = values 0..7 of the sub-block, high nibbles = 8..15),
+ * 16-byte aligned.  Writes packed u8 [rows, n_cols/2] (16-byte aligned; even value in the low nibble) and scales
+ * E4M3 bits u8 [rows, n_cols/16] (4-byte aligned): 0x7F -> 0, other bytes with the sign bit cleared.  A scale byte
+ * 0xFF is not representable: every warp that met one adds 1 to *bad_blocks (device int32, zeroed by the caller);
+ * its outputs are then meaningless (the reference raises ValueError).  n_cols % 64 == 0. */
+int flint_gguf_nvfp4_repack(const void* blocks, int64_t rows, int64_t n_cols, void* packed, void* scales,
+                            int32_t* bad_blocks, int pdl, void* stream);
+
+/* Replaces gguf_nvfp4.dequantize_nvfp4 (patch:295-319).  out[r, k] = e2m1(P) * e4m3(S) (exact), times
+ * *global_scale (device fp32, optional; one fp32 multiply, round to nearest), stored as fp32 (out_f32 = 1) or
+ * rounded once to bf16.  P u8 [rows, n_cols/2] (8-byte aligned), S u8 [rows, n_cols/16], out 16-byte aligned.
+ * n_cols % 16 == 0. */
+int flint_nvfp4_dequant(const void* P, const void* S, int64_t rows, int64_t n_cols, const float* global_scale,
+                        int out_f32, void* out, int pdl, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
