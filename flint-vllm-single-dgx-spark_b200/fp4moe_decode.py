@@ -9,9 +9,15 @@ Same entry points, argument order and outputs as the reference (fast/fp4moe_deco
 
 Differences, by design: the kernels read the ModelOpt NVFP4 tensors in place (``DecodeWeights``) instead of the
 Marlin repack the GB10 kernels need, run 1..8 tokens instead of 1, and take the expert count / top-k / score
-function from the weights instead of hard-coding Flint's 256 / 6 / sigmoid.  ``sact`` (the shared-expert
-activation of Flint) is ``None``: the BASELINE model has no shared expert.  ``trigger`` is accepted for
+function from the weights instead of hard-coding Flint's 256 / 6 / sigmoid.  ``trigger`` is accepted for
 signature compatibility (every launch is stream ordered).
+
+Flint's ungated shared expert (``DecodeWeights(..., shared=...)``): ``moe_up`` also returns its activation ``sact``
+[M, SI] and ``moe_down`` adds its output, ``out = bf16(routed + shared)`` with ``routed = bf16(sum tw * y_e)`` and
+``shared = bf16(sact . W2s * gs)`` -- the PR's combine rule (patch:3391-3397); the GB10 kernels fold the same sum
+(fast/fp4moe_mar.cu:224-231).  The shared expert runs on the routed kernels as a one-expert stack that every token
+routes to with weight 1; the final add is one bf16 elementwise add.  ``sact`` is ``None`` without a shared expert
+(the BASELINE model).  ``dense_mlp`` is Flint's dense SwiGLU layer (``mlp_only_layers``) on the same kernels.
 """
 from __future__ import annotations
 
@@ -42,7 +48,9 @@ class DecodeWeights:
     the first column is used, as fast/fp4moe_decode.py:41 does); w2 u8 [E, H, I/2], s2 E4M3 [E, H, I/16], g2 fp32 [E].
     topk / score select the router (softmax with renormalised top-k, or sigmoid)."""
 
-    def __init__(self, w13, s13, g13, w2, s2, g2, topk: int = TOPK, score: str = SCORE):
+    def __init__(self, w13, s13, g13, w2, s2, g2, topk: int = TOPK, score: str = SCORE, shared=None):
+        """shared: None, or the shared expert's (w13, s13, g13, w2, s2, g2) -- u8 [2SI, H/2], E4M3 [2SI, H/16],
+        fp32 scalar, u8 [H, SI/2], E4M3 [H, SI/16], fp32 scalar (a leading dimension of 1 is accepted)."""
         E, I2, Hh = w13.shape
         assert w13.dtype == torch.uint8 and w2.dtype == torch.uint8, (w13.dtype, w2.dtype)
         assert tuple(s13.shape) == (E, I2, Hh // 8) and tuple(w2.shape) == (E, Hh * 2, I2 // 4), (s13.shape, w2.shape)
@@ -56,6 +64,13 @@ class DecodeWeights:
         self.g2 = g2.float().reshape(E, -1)[:, 0].contiguous()
         self.topk = int(topk)
         self.score_fn = _SCORE_FN[score]
+        self.shared = None
+        if shared is not None:
+            sw13, ss13, sg13, sw2, ss2, sg2 = shared
+            one = lambda t: t.reshape(1, *t.shape[-2:])
+            self.shared = DecodeWeights(one(sw13), one(ss13), sg13.reshape(1), one(sw2), one(ss2), sg2.reshape(1),
+                                        topk=1, score="softmax")
+            assert self.shared.H == self.H, "shared expert hidden size"
 
 
 def _route_impl(x, res, nw, eps, gate_w, topk, score_fn, want_norm):
@@ -86,27 +101,85 @@ def route_norm(x, res, nw, eps, gate_w, trigger=0, topk: int = TOPK, score: str 
     return tw, ti, xn, (res_out if res is not None else None)
 
 
+_ONE_ROUTE: dict = {}
+
+
+def _one_route(M: int, device):
+    """(ids int32 [M, 1] = 0, weights fp32 [M, 1] = 1): every token to expert 0 of a one-expert stack, weight 1."""
+    key = (M, device)
+    r = _ONE_ROUTE.get(key)
+    if r is None:
+        r = _ONE_ROUTE[key] = (torch.zeros((M, 1), dtype=torch.int32, device=device),
+                               torch.ones((M, 1), dtype=torch.float32, device=device))
+    return r
+
+
 def moe_up(x, ti, w: DecodeWeights):
+    """-> (act bf16 [M*k, I], sact bf16 [M, SI] of the shared expert or None)."""
     act = torch.empty((x.shape[0] * ti.shape[-1], w.I), dtype=torch.bfloat16, device=x.device)
     torch.ops.flint_b200.moe_up(x, ti, w.w13, w.s13, w.g13, act)
-    return act, None
+    sact = None
+    if w.shared is not None:
+        sw = w.shared
+        ids0, _ = _one_route(x.shape[0], x.device)
+        sact = torch.empty((x.shape[0], sw.I), dtype=torch.bfloat16, device=x.device)
+        torch.ops.flint_b200.moe_up(x, ids0, sw.w13, sw.s13, sw.g13, sact)
+    return act, sact
 
 
 def moe_down(act, sact, ti, tw, w: DecodeWeights, trigger=0):
-    """-> sum_j tw_j * expert_{ti_j}(x) (bf16)."""
+    """-> bf16(sum_j tw_j * expert_{ti_j}(x)) (+ the shared expert's output, then rounded once more when sact is
+    given)."""
     M = ti.shape[0]
     out = torch.empty((M, w.H), dtype=torch.bfloat16, device=act.device)
     torch.ops.flint_b200.moe_down(act, ti, tw, w.w2, w.s2, w.g2, out)
+    if sact is not None:
+        out = out + shared_down(sact, w)
     return out
 
 
+def shared_down(sact, w: DecodeWeights):
+    """The shared expert's output bf16(sact . W2s^T * gs) [M, H] (weight 1 on its one route)."""
+    sw = w.shared
+    ids0, one = _one_route(sact.shape[0], sact.device)
+    ys = torch.empty((sact.shape[0], sw.H), dtype=torch.bfloat16, device=sact.device)
+    torch.ops.flint_b200.moe_down(sact, ids0, one, sw.w2, sw.s2, sw.g2, ys)
+    return ys
+
+
+_ZERO_ROUTER: dict = {}
+
+
+def dense_mlp(x, res, nw, eps, w: DecodeWeights):
+    """Flint's dense SwiGLU layer (the PR's FlintMLP on ``mlp_only_layers``): (bf16(down(silu(g) * u)) of
+    rmsnorm(x + res), x + res).  w: a one-expert DecodeWeights (w13 [1, 2I, H/2], w2 [1, H, I/2]).  Runs on the
+    MoE chain: the route kernel's add + RMSNorm with an all-zero 32-way router (every token's top-1 is expert 0,
+    weight exactly 1), then the up and down kernels."""
+    if w.E != 1:
+        raise ValueError("dense_mlp takes a one-expert DecodeWeights")
+    key = (x.device, w.H)
+    zr = _ZERO_ROUTER.get(key)
+    if zr is None:
+        zr = _ZERO_ROUTER[key] = torch.zeros((32, w.H), dtype=torch.bfloat16, device=x.device)
+    tw, ti, xn, res_out, _ = _route_impl(x, res, nw, eps, zr, 1, 0, True)
+    act, _ = moe_up(xn, ti, w)
+    return moe_down(act, None, ti, tw, w), (res_out if res is not None else None)
+
+
 def moe_decode(x, res, nw, eps, gate_w, w: DecodeWeights, fused: bool = True, extras: bool = False,
-               impl: str | None = None):
+               impl: str | None = None, _routed_only: bool = False):
     """The whole decode MoE block: (mlp(norm(x + res)), x + res).  impl "chain" (fused=False): the three launches
     route_norm -> moe_up -> moe_down; "fused" (fused=True): one persistent launch for 1..8 tokens (flint_moe_fused);
     "block": one launch for one token with the down weights prefetched under the gate/up work (flint_moe_block).
     extras=True (fused / block) also returns (xn, logits, topk_ids, topk_weights)."""
     impl = impl or ("fused" if fused else "chain")
+    if w.shared is not None and impl != "chain" and not _routed_only:
+        out, res_out, ex = moe_decode(x, res, nw, eps, gate_w, w, impl=impl, extras=True, _routed_only=True)
+        sact = torch.empty((x.shape[0], w.shared.I), dtype=torch.bfloat16, device=x.device)
+        ids0, _ = _one_route(x.shape[0], x.device)
+        torch.ops.flint_b200.moe_up(ex[0], ids0, w.shared.w13, w.shared.s13, w.shared.g13, sact)
+        out = out + shared_down(sact, w)
+        return (out, res_out, ex) if extras else (out, res_out)
     if impl == "block":
         M, H = x.shape
         dev = x.device

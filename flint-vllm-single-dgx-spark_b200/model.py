@@ -45,6 +45,45 @@ class FlintConfig:
     rms_eps: float = 1e-6
     score: str = "softmax"
     weight_std: float = 0.02
+    # Flint's own layer structure (the PR's FlintConfig, patch:105-173); the defaults give the BASELINE model.
+    shared_inter: int = 0                  # ungated shared expert of every MoE layer (0: none)
+    mlp_only_layers: tuple = ()            # layers with a dense SwiGLU MLP instead of the MoE
+    dense_inter: int = 6144                # its intermediate size
+    layer_types: tuple = ()                # "sliding_attention" / "full_attention" per layer; () = all full
+    sliding_window: int = 0                # window of the sliding layers
+    no_rope_layers: tuple = ()             # layers without positional encoding
+    attn_sinks: bool = False               # learned per-head softmax sinks in every layer
+
+    def __post_init__(self):
+        if self.layer_types and len(self.layer_types) != self.layers:
+            raise ValueError(f"layer_types has {len(self.layer_types)} entries but layers is {self.layers}")
+        bad = [t for t in self.layer_types if t not in ("sliding_attention", "full_attention")]
+        if bad:
+            raise ValueError(f"unknown layer type {bad[0]!r}")
+        if any(t == "sliding_attention" for t in self.layer_types) and self.sliding_window < 1:
+            raise ValueError("sliding layers need sliding_window >= 1")
+        for name in ("mlp_only_layers", "no_rope_layers"):
+            if any(not 0 <= l < self.layers for l in getattr(self, name)):
+                raise ValueError(f"{name} holds a layer index outside 0..{self.layers - 1}")
+
+    @classmethod
+    def flint(cls, layers: int = 49, **overrides) -> "FlintConfig":
+        """Flint's own shapes (patch:105-136): 256 experts, sigmoid top-6, I = 512, an ungated shared expert of
+        1024, vocab 150144, RoPE theta 1e4, sliding window 513 and attention sinks.  Which layers slide, skip RoPE
+        or are dense comes from the checkpoint's config: pass layer_types / no_rope_layers / mlp_only_layers."""
+        base = dict(layers=layers, num_experts=256, topk=6, moe_inter=512, vocab=150144, rope_theta=1e4,
+                    score="sigmoid", shared_inter=1024, sliding_window=513, attn_sinks=True)
+        base.update(overrides)
+        return cls(**base)
+
+    def is_dense(self, l: int) -> bool:
+        return l in self.mlp_only_layers
+
+    def window(self, l: int) -> int:
+        return self.sliding_window if self.layer_types and self.layer_types[l] == "sliding_attention" else 0
+
+    def uses_rope(self, l: int) -> bool:
+        return l not in self.no_rope_layers
 
     @property
     def qkv_rows(self) -> int:
@@ -54,18 +93,23 @@ class FlintConfig:
         """(total, active per token) parameters, embedding excluded."""
         H, I, E, k = self.hidden, self.moe_inter, self.num_experts, self.topk
         attn = self.qkv_rows * H + H * self.num_heads * self.head_dim
-        expert = 3 * H * I
-        per_layer_total = attn + E * expert + E * H
-        per_layer_active = attn + k * expert + E * H
-        return (self.layers * per_layer_total + self.vocab * H, self.layers * per_layer_active + self.vocab * H)
+        expert, shared, dense = 3 * H * I, 3 * H * self.shared_inter, 3 * H * self.dense_inter
+        nd = len(self.mlp_only_layers)
+        total = self.layers * attn + (self.layers - nd) * (E * expert + E * H + shared) + nd * dense
+        active = self.layers * attn + (self.layers - nd) * (k * expert + E * H + shared) + nd * dense
+        return total + self.vocab * H, active + self.vocab * H
 
     def weight_bytes_per_token(self) -> int:
         """NVFP4 bytes streamed per decode token at batch 1 (0.5625 B/param; bf16 router and norms)."""
-        H, I, k = self.hidden, self.moe_inter, self.topk
+        H, I, k, SI, DI = self.hidden, self.moe_inter, self.topk, self.shared_inter, self.dense_inter
         nv = lambda n, kk: n * kk // 2 + n * kk // 16
         attn = nv(self.qkv_rows, H) + nv(H, self.num_heads * self.head_dim)
         moe = k * (nv(2 * I, H) + nv(H, I)) + self.num_experts * H * 2
-        return self.layers * (attn + moe) + nv(self.vocab, H)
+        if SI:
+            moe += nv(2 * SI, H) + nv(H, SI)
+        nd = len(self.mlp_only_layers)
+        dense = nv(2 * DI, H) + nv(H, DI) + 32 * H * 2
+        return self.layers * attn + (self.layers - nd) * moe + nd * dense + nv(self.vocab, H)
 
 
 def rope_cos_sin(max_pos: int, dim: int, theta: float, device) -> torch.Tensor:
@@ -88,8 +132,10 @@ class FlintModel:
         self.cfg, self.dev = cfg, torch.device(device)
         self.max_ctx, self.max_batch = max_ctx, max_batch
         self.rank, self.world = shard
-        if cfg.num_experts % self.world or cfg.vocab % (256 * self.world):
+        if self.world > 1 and (cfg.num_experts % self.world or cfg.vocab % (256 * self.world)):
             raise ValueError("experts and vocab / 256 must divide by the number of shards")
+        if self.world > 1 and (cfg.shared_inter or cfg.mlp_only_layers):
+            raise ValueError("shared experts and dense layers run on one GPU only")
         self.e_lo, self.n_local = self.rank * cfg.num_experts // self.world, cfg.num_experts // self.world
         self.v_lo, self.v_local = self.rank * cfg.vocab // self.world, cfg.vocab // self.world
         sl = lambda t: t[self.e_lo:self.e_lo + self.n_local].contiguous() if self.world > 1 else t
@@ -100,16 +146,30 @@ class FlintModel:
         ones = lambda n: (1.0 + torch.randn((n,), generator=g, device=self.dev) * 0.05).to(torch.bfloat16)
         self.embed = bf((c.vocab, c.hidden), 1.0)
         self.layers = []
-        for _ in range(c.layers):
+        for l in range(c.layers):
             P, S, gs = random_nvfp4((), c.qkv_rows, c.hidden, c.weight_std, g, self.dev)
             Po, So, gso = random_nvfp4((), c.hidden, c.num_heads * c.head_dim, c.weight_std, g, self.dev)
-            w13, s13, g13 = (sl(t) for t in random_nvfp4((c.num_experts,), 2 * c.moe_inter, c.hidden, c.weight_std, g,
+            if c.is_dense(l):       # dense SwiGLU: one expert that every token takes with weight 1
+                w13, s13, g13 = random_nvfp4((1,), 2 * c.dense_inter, c.hidden, c.weight_std, g, self.dev)
+                w2, s2, g2 = random_nvfp4((1,), c.hidden, c.dense_inter, c.weight_std, g, self.dev)
+                L = dict(ln1=ones(c.hidden), qkv=(P, S, gs.reshape(1)), q_norm=ones(c.head_dim), k_norm=ones(c.head_dim),
+                         o=(Po, So, gso.reshape(1)), ln2=ones(c.hidden), gate=None,
+                         experts=DecodeWeights(w13, s13, g13, w2, s2, g2, topk=1, score="softmax"))
+            else:
+                w13, s13, g13 = (sl(t) for t in random_nvfp4((c.num_experts,), 2 * c.moe_inter, c.hidden, c.weight_std,
+                                                              g, self.dev))
+                w2, s2, g2 = (sl(t) for t in random_nvfp4((c.num_experts,), c.hidden, c.moe_inter, c.weight_std, g,
                                                           self.dev))
-            w2, s2, g2 = (sl(t) for t in random_nvfp4((c.num_experts,), c.hidden, c.moe_inter, c.weight_std, g, self.dev))
-            self.layers.append(dict(
-                ln1=ones(c.hidden), qkv=(P, S, gs.reshape(1)), q_norm=ones(c.head_dim), k_norm=ones(c.head_dim),
-                o=(Po, So, gso.reshape(1)), ln2=ones(c.hidden), gate=bf((c.num_experts, c.hidden), c.weight_std),
-                experts=DecodeWeights(w13, s13, g13, w2, s2, g2, topk=c.topk, score=c.score)))
+                L = dict(ln1=ones(c.hidden), qkv=(P, S, gs.reshape(1)), q_norm=ones(c.head_dim), k_norm=ones(c.head_dim),
+                         o=(Po, So, gso.reshape(1)), ln2=ones(c.hidden), gate=bf((c.num_experts, c.hidden), c.weight_std))
+                shared = None
+                if c.shared_inter:
+                    shared = (random_nvfp4((1,), 2 * c.shared_inter, c.hidden, c.weight_std, g, self.dev)
+                              + random_nvfp4((1,), c.hidden, c.shared_inter, c.weight_std, g, self.dev))
+                L["experts"] = DecodeWeights(w13, s13, g13, w2, s2, g2, topk=c.topk, score=c.score, shared=shared)
+            L["sinks"] = (torch.randn((c.num_heads,), generator=g, device=self.dev).float()
+                          if c.attn_sinks else None)
+            self.layers.append(L)
         self.final_norm = ones(c.hidden)
         Ph, Sh, gsh = random_nvfp4((), c.vocab, c.hidden, c.weight_std, g, self.dev)
         if self.world > 1:
@@ -189,6 +249,16 @@ class Decoder:
         self.y_rows = torch.zeros((M * c.topk, c.hidden), dtype=torch.bfloat16, device=dev)  # ... of the chain
         self.keys = torch.zeros((M,), dtype=torch.int64, device=dev)                        # vocab-shard argmax
         self.act = e(M * c.topk, c.moe_inter)
+        # Flint's dense layers and shared expert: one-expert chains (every token to expert 0, weight 1)
+        self.ti0 = torch.zeros((M, 1), dtype=torch.int32, device=dev)
+        self.tw1 = torch.ones((M, 1), dtype=torch.float32, device=dev)
+        if c.mlp_only_layers:
+            self.zero_router = torch.zeros((32, c.hidden), dtype=torch.bfloat16, device=dev)
+            self.lg32 = e(M, 32, dt=torch.float32)
+            self.ti_d, self.tw_d = e(M, 1, dt=torch.int32), e(M, 1, dt=torch.float32)
+            self.dact = e(M, c.dense_inter)
+        if c.shared_inter:
+            self.sact, self.ys = e(M, c.shared_inter), e(M, c.hidden)
         self.dummy_f = e(1, 1, dt=torch.float32)
         self.dummy_b = e(0)
         self.splits = _ops.attention_splits(M, c.num_kv_heads)
@@ -197,9 +267,12 @@ class Decoder:
         # (qkv, attention, o | attention block) + (route, up, down | fused MoE | EP block + combine) per layer, then
         # head (+ key conversion when sharded) + advance; NCCL's own kernels are not counted
         # (peer exchange: the MoE block exchanges in-kernel; the head adds one exchange kernel)
+        # dense layers: route + up + down; the shared expert: up + down (its bf16 add is a torch elementwise op)
         ep = model.world > 1
         moe_launches = (4 if ep else 3) if moe == "chain" else 2 if (ep and exchange == "nccl") else 1
-        self.launches_per_step = ((3 if attn == "chain" else 1) + moe_launches) * c.layers + 2 + (1 if ep else 0)
+        n_dense = len(c.mlp_only_layers)
+        mlp_launches = n_dense * 3 + (c.layers - n_dense) * (moe_launches + (2 if c.shared_inter else 0))
+        self.launches_per_step = (3 if attn == "chain" else 1) * c.layers + mlp_launches + 2 + (1 if ep else 0)
 
     # ---- one decode step as torch ops on persistent buffers ----
     def layer_ops(self, l: int) -> list[tuple[str, callable]]:
@@ -209,27 +282,38 @@ class Decoder:
         P, S, gs = L["qkv"]
         Po, So, gso = L["o"]
         ew = L["experts"]
+        cs = m.cos_sin if c.uses_rope(l) else None           # full-attention layers of Flint use no RoPE
+        sinks, window = L["sinks"], c.window(l)
         if l == 0:      # the embedding gather is fused into the first QKV kernel
             qkv = lambda: ops.attn_qkv(m.embed, None, L["ln1"], c.rms_eps, P, S, gs, c.num_heads, c.num_kv_heads, True,
-                                       L["q_norm"], L["k_norm"], c.rms_eps, self.positions, m.cos_sin, kc, vc,
+                                       L["q_norm"], L["k_norm"], c.rms_eps, self.positions, cs, kc, vc,
                                        self.slots, self.q, self.qkv, self.res_a, True, self.tokens)
         else:
             qkv = lambda: ops.attn_qkv(self.h, self.res_b, L["ln1"], c.rms_eps, P, S, gs, c.num_heads, c.num_kv_heads,
-                                       True, L["q_norm"], L["k_norm"], c.rms_eps, self.positions, m.cos_sin, kc, vc,
+                                       True, L["q_norm"], L["k_norm"], c.rms_eps, self.positions, cs, kc, vc,
                                        self.slots, self.q, self.qkv, self.res_a, True, None)
         if self.attn_mode == "block":
             x_in, res_in, tok = (m.embed, None, self.tokens) if l == 0 else (self.h, self.res_b, None)
             seq = [("attn_block", lambda: ops.attn_block(x_in, res_in, L["ln1"], c.rms_eps, P, S, gs, c.num_heads,
                                                          c.num_kv_heads, L["q_norm"], L["k_norm"], c.rms_eps,
-                                                         self.positions, m.cos_sin, kv, self.bt, self.seq_lens,
-                                                         self.slots, None, 0, self.scale, Po, So, gso, self.a,
+                                                         self.positions, cs, kv, self.bt, self.seq_lens,
+                                                         self.slots, sinks, window, self.scale, Po, So, gso, self.a,
                                                          self.res_a, None, None, tok))]
         else:
             seq = [("qkv", qkv),
                    ("attention", lambda: ops.decode_attention(self.q.view(self.M, c.num_heads, c.head_dim), kv, self.bt,
-                                                              self.seq_lens, None, 0, self.scale, self.attn,
+                                                              self.seq_lens, sinks, window, self.scale, self.attn,
                                                               self.splits)),
                    ("o", lambda: ops.attn_o(self.attn.view(self.M, -1), Po, So, gso, self.a))]
+        if c.is_dense(l):
+            # dense SwiGLU: the route kernel's add + RMSNorm (an all-zero 32-way router sends every token to expert
+            # 0 with weight 1), then the one-expert up and down
+            seq += [("dense_route", lambda: ops.moe_route(self.a, self.res_a, L["ln2"], c.rms_eps, self.zero_router, 1,
+                                                          0, self.lg32, self.ti_d, self.tw_d, self.xn, self.res_b, True,
+                                                          True)),
+                    ("dense_up", lambda: ops.moe_up(self.xn, self.ti_d, ew.w13, ew.s13, ew.g13, self.dact)),
+                    ("dense_down", lambda: ops.moe_down(self.dact, self.ti_d, self.tw_d, ew.w2, ew.s2, ew.g2, self.h))]
+            return seq
         # prefetch=True: the MoE block pulls the next layer's attention weights into L2 while HBM would otherwise
         # idle.  Off by default: measured in place it does not shorten the attention block (its critical path starts
         # with the norm, not the weights) and it adds ~1 us to the MoE block.
@@ -252,14 +336,15 @@ class Decoder:
                 ops.moe_combine(self.y_slots, self.tw, self.h)
             seq.append(("moe_block_ep", moe_ep))
         elif self.moe == "block":
+            xn_out = self.xn if ew.shared is not None else None      # the shared expert reads the normalised input
             seq.append(("moe_block", lambda: ops.moe_block(self.a, self.res_a, L["ln2"], c.rms_eps, L["gate"], c.topk,
                                                            ew.score_fn, ew.w13, ew.s13, ew.g13, ew.w2, ew.s2, ew.g2, self.h,
-                                                           self.res_b, None, None, None, None, pf)))
+                                                           self.res_b, xn_out, None, None, None, pf)))
         elif self.moe == "fused":
             seq.append(("moe_fused", lambda: ops.moe_fused(self.a, self.res_a, L["ln2"], c.rms_eps, L["gate"], c.topk,
                                                            ew.score_fn, ew.w13, ew.s13, ew.g13, ew.w2, ew.s2, ew.g2,
                                                            self.h, self.res_b, self.xn, self.lg, self.ti, self.tw,
-                                                           False)))
+                                                           ew.shared is not None)))
         else:
             seq.append(("route", lambda: ops.moe_route(self.a, self.res_a, L["ln2"], c.rms_eps, L["gate"], c.topk,
                                                        ew.score_fn, self.lg, self.ti, self.tw, self.xn, self.res_b, True,
@@ -278,6 +363,15 @@ class Decoder:
             else:
                 seq += [("up", lambda: ops.moe_up(self.xn, self.ti, ew.w13, ew.s13, ew.g13, self.act)),
                         ("down", lambda: ops.moe_down(self.act, self.ti, self.tw, ew.w2, ew.s2, ew.g2, self.h))]
+        if ew.shared is not None:
+            # Flint's ungated shared expert: h = bf16(routed + shared) (the PR's combine rule, patch:3391-3397)
+            sw = ew.shared
+
+            def shared_down():
+                ops.moe_down(self.sact, self.ti0, self.tw1, sw.w2, sw.s2, sw.g2, self.ys)
+                self.h.add_(self.ys)
+            seq += [("shared_up", lambda: ops.moe_up(self.xn, self.ti0, sw.w13, sw.s13, sw.g13, self.sact)),
+                    ("shared_down", shared_down)]
         return seq
 
     def _layers(self):
@@ -360,6 +454,14 @@ class Decoder:
         if name in ("moe_block_ep", "moe_block_peer"):   # local experts only: topk / world routed slots on average
             return self.algorithmic_bytes("route", ctx) + (self.algorithmic_bytes("up", ctx)
                                                            + self.algorithmic_bytes("down", ctx)) // self.m.world
+        if name == "dense_route":
+            return 32 * H * 2 + M * (4 * H * 2 + 32 * 4 + 8)
+        if name in ("dense_up", "shared_up"):             # one expert, read once for all M tokens
+            inter = c.dense_inter if name == "dense_up" else c.shared_inter
+            return nv(2 * inter, H) + M * (inter * 2 + H * 2)
+        if name in ("dense_down", "shared_down"):
+            inter = c.dense_inter if name == "dense_down" else c.shared_inter
+            return nv(H, inter) + M * (inter * 2 + H * 2 * (1 if name == "dense_down" else 3))
         if name == "head":                                 # this rank's vocabulary rows
             return nv(self.m.v_local, H) + M * 2 * H * 2
         raise KeyError(name)
