@@ -12,7 +12,10 @@ FlintAttention.forward_af 596-657, FlintSparseMoeBlock._forward_decode_rn 302-31
     head:     token = argmax(lm_head(final_norm(h + res)))
 
 with the BASELINE.json shapes (hidden 2048, 48 layers, 32/4 heads of 128, 128 experts top-8 softmax, I = 768,
-vocab 151552, RoPE theta 1e6) and seeded N(0, 0.02) NVFP4 weights.  One decode step of M <= 8 streams is a
+vocab 151552, RoPE theta 1e6) and seeded N(0, 0.02) NVFP4 weights.  ``FlintConfig.flint`` gives Flint's own
+structure (the PR's FlintConfig, patch:105-173): 256 experts sigmoid top-6 with an ungated shared expert, dense
+SwiGLU layers (``mlp_only_layers``), sliding-window layers with attention sinks and full-attention layers without
+RoPE, each run on the same kernels.  One decode step of M <= 8 streams is a
 single CUDA graph (the embedding lookup is fused into the first QKV kernel, the final norm into the head,
 and the position / KV-slot bookkeeping runs on the device), so consecutive steps replay without the host.
 """
