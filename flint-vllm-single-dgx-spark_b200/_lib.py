@@ -73,6 +73,8 @@ SIGNATURES: dict[str, tuple] = {
     "flint_decode_attention_workspace_bytes": (I64, [I64, I64, I64]),
     "flint_decode_advance": (I32, [P, I64, P, P, P, P, I64, I64, I64, P, I64, P, I64, P, I32, P]),
     "flint_gguf_nvfp4_repack": (I32, [P, I64, I64, P, P, P, I32, P]),
+    "flint_workspace_status_offset": (I64, [I32]),
+    "flint_workspace_status": (I32, [P, I32, P, I32]),
     "flint_nvfp4_dequant": (I32, [P, P, I64, I64, P, I32, P, I32, P]),
     "flint_decode_attention": (I32, [P, I64, P, I64, I64, I64, I64, P, I64, I64, P, P, I64, F32, I64, I64, P, I64, I64, P,
                                      I32, P]),
@@ -142,3 +144,69 @@ def workspace(device: torch.device, kind: str, nbytes: int) -> torch.Tensor:
         ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
         _workspaces[key] = ws
     return ws
+
+
+# ---------------------------------------------------------------------------------------------------------
+# Device-side health: the sticky status word of every workspace (bounded waits never trap; they record here).
+# ---------------------------------------------------------------------------------------------------------
+STATUS_BITS = {1: "a bounded wait timed out (that launch's outputs are invalid)", 2: "a routed expert id was out "
+               "of range (clamped)", 4: "a sequence was longer than its block table (clamped)"}
+_ALIGN_BITS = {1: "an expert id was out of range or sorted_ids was too small"}
+
+
+def _status_kind(name: str) -> int | None:
+    """FLINT_WS_* kind of a workspace registered under `name` by the ops (None: no status word)."""
+    if name == "lm_head" or name.startswith("lm_head_sample_"):
+        return 0
+    if name == "moe":
+        return 1
+    for prefix, kind in (("moe_fused_", 2), ("moe_block_", 3), ("attn_block_", 5)):
+        if name.startswith(prefix):
+            return kind
+    return {"attn_proj": 4, "decode_attention": 6}.get(name)
+
+
+def _status_offset(name: str) -> int | None:
+    if name == "align_status":                        # the whole 4-byte buffer is moe_align's status word
+        return 0
+    kind = _status_kind(name)
+    return None if kind is None else int(lib().flint_workspace_status_offset(kind))
+
+
+def describe_status(name: str, bits: int) -> str:
+    table = _ALIGN_BITS if name == "align_status" else STATUS_BITS
+    parts = [text for bit, text in table.items() if bits & bit]
+    rest = bits & ~sum(table)
+    return ", ".join(parts + ([f"bits {rest:#x}"] if rest else []))
+
+
+def device_status(device: torch.device | None = None, clear: bool = False) -> dict[tuple[int, str], int]:
+    """{(device index, workspace name): status bits} of every workspace of this process whose status word is not
+    zero (all devices, or only `device`).  One small synchronous read per workspace; clear=True zeroes the words
+    it reports.  Workspaces outgrown by a larger one (kept alive for captured graphs) are not read."""
+    want = None
+    if device is not None:
+        device = torch.device(device)
+        want = device.index if device.index is not None else torch.cuda.current_device()
+    out = {}
+    for (idx, name), ws in list(_workspaces.items()):
+        if want is not None and idx != want:
+            continue
+        off = _status_offset(name)
+        if off is None or off + 4 > ws.numel():
+            continue
+        word = ws[off:off + 4].view(torch.int32)
+        bits = int(word.item()) & 0xFFFFFFFF
+        if bits:
+            out[(idx, name)] = bits
+            if clear:
+                word.zero_()
+    return out
+
+
+def check_device_status(device: torch.device | None = None, clear: bool = True) -> None:
+    """Raise FlintError naming every workspace whose kernels reported a problem (and clear those words)."""
+    bad = device_status(device, clear)
+    if bad:
+        raise FlintError("device status: " + "; ".join(f"{name} on cuda:{idx}: {describe_status(name, bits)}"
+                                                       for (idx, name), bits in sorted(bad.items())))

@@ -965,6 +965,8 @@ static size_t block_ws_bytes(int64_t Nqkv, int64_t Ko, int sms) {
 
 using namespace flint;
 
+int64_t flint::status_offset_attn_block() { return (int64_t)offsetof(BlockWs, status); }
+
 extern "C" int64_t flint_attn_block_workspace_bytes(int64_t n_qkv, int64_t k_o) {
   const int sms = num_sms();
   return (int64_t)block_ws_bytes(n_qkv, k_o, sms > 0 ? sms : 148);

@@ -256,6 +256,7 @@ static size_t o_smem(int M, int K) { return 1024 + OL::ring_bytes + (size_t)kOCL
 using namespace flint;
 
 extern "C" int64_t flint_attn_proj_workspace_bytes(void) { return sizeof(ProjWorkspace); }
+int64_t flint::status_offset_attn_proj() { return (int64_t)offsetof(ProjWorkspace, status); }
 
 extern "C" int flint_attn_qkv(const void* x, int64_t ldx, const int32_t* tokens, const void* res, const void* norm_w, float eps, const void* W,
                               const void* S, const float* gs, int64_t M, int64_t H, int64_t N, int64_t num_q_heads,

@@ -303,6 +303,8 @@ extern "C" int64_t flint_decode_attention_splits(int64_t batch, int64_t num_kv_h
   return n < 1 ? 1 : (n > 256 ? 256 : n);
 }
 
+int64_t flint::status_offset_decode_attention() { return (int64_t)offsetof(AttnWorkspace, status); }
+
 extern "C" int64_t flint_decode_attention_workspace_bytes(int64_t batch, int64_t num_kv_heads, int64_t splits) {
   return (int64_t)attn_ws_bytes((int)batch, (int)num_kv_heads, (int)splits);
 }

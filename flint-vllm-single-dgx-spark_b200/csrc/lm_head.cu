@@ -18,6 +18,7 @@ static size_t head_smem(int M, int K, bool norm) {
 }  // namespace flint
 
 extern "C" int64_t flint_lm_head_workspace_bytes(void) { return sizeof(flint::HeadWorkspace); }
+int64_t flint::status_offset_lm_head() { return (int64_t)offsetof(flint::HeadWorkspace, status); }
 
 extern "C" int flint_lm_head_nv4_fused(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, int64_t M,
                                        const void* P, const void* S, float gs, int64_t V, int64_t K, float* logits,

@@ -433,6 +433,7 @@ moe_align_kernel(const int* __restrict__ topk_ids, int n, int E, int B, int* __r
 using namespace flint;
 
 extern "C" int64_t flint_moe_workspace_bytes(int64_t H) { return (int64_t)moe_ws_bytes((int)H); }
+int64_t flint::status_offset_moe() { return (int64_t)offsetof(MoeWorkspace, status); }
 
 extern "C" int flint_moe_route(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, const void* gate_w,
                                int64_t M, int64_t H, int64_t E, int64_t topk, int score_fn, float* logits, int32_t* topk_ids,

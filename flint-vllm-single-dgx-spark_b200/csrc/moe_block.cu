@@ -393,6 +393,8 @@ __global__ void moe_combine_kernel(const bf16* __restrict__ y, const float* __re
 
 using namespace flint;
 
+int64_t flint::status_offset_moe_block() { return (int64_t)offsetof(MoeBlockWs, status); }
+
 extern "C" int64_t flint_moe_block_workspace_bytes(int64_t E, int64_t I) { return (int64_t)moe_block_ws_bytes((int)E, (int)I); }
 
 static int moe_block_launch(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps,

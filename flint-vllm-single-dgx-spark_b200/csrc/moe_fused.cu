@@ -345,6 +345,8 @@ static int launch_fused(int sms, const CUtensorMap& uc, const CUtensorMap& us, c
 
 using namespace flint;
 
+int64_t flint::status_offset_moe_fused() { return (int64_t)offsetof(MoeFusedWs, status); }
+
 extern "C" int64_t flint_moe_fused_workspace_bytes(int64_t E, int64_t H, int64_t I) {
   return (int64_t)moe_fused_ws_bytes((int)E, (int)H, (int)I);
 }

@@ -142,6 +142,30 @@ extern "C" const char* flint_last_cuda_error(void) { return flint::g_last_cuda_e
 
 extern "C" int flint_version(void) { return 100; }
 
+extern "C" int64_t flint_workspace_status_offset(int kind) {
+  using namespace flint;
+  switch (kind) {
+    case FLINT_WS_LM_HEAD: return status_offset_lm_head();
+    case FLINT_WS_MOE: return status_offset_moe();
+    case FLINT_WS_MOE_FUSED: return status_offset_moe_fused();
+    case FLINT_WS_MOE_BLOCK: return status_offset_moe_block();
+    case FLINT_WS_ATTN_PROJ: return status_offset_attn_proj();
+    case FLINT_WS_ATTN_BLOCK: return status_offset_attn_block();
+    case FLINT_WS_DECODE_ATTENTION: return status_offset_decode_attention();
+    default: return -1;
+  }
+}
+
+extern "C" int flint_workspace_status(const void* workspace, int kind, uint32_t* status, int clear) {
+  const int64_t off = flint_workspace_status_offset(kind);
+  if (!workspace || !status) return FLINT_ERR_ARGUMENT;
+  if (off < 0) return FLINT_ERR_ARGUMENT;
+  uint8_t* word = (uint8_t*)workspace + off;
+  int rc = flint::record_cuda(cudaMemcpy(status, word, 4, cudaMemcpyDeviceToHost), FLINT_ERR_DEVICE);
+  if (rc == FLINT_OK && clear && *status) rc = flint::record_cuda(cudaMemset(word, 0, 4), FLINT_ERR_DEVICE);
+  return rc;
+}
+
 extern "C" const char* flint_error_string(int code) {
   switch (code) {
     case FLINT_OK: return "ok";

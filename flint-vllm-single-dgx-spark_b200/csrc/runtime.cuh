@@ -1,6 +1,7 @@
 // Host-side launch helpers shared by the entry points.
 #pragma once
 #include <cuda_runtime.h>
+#include <stddef.h>
 #include <stdint.h>
 
 #include "../../include/flint_b200.h"
@@ -17,6 +18,16 @@ inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintp
 int record_cuda(cudaError_t e, int code);
 // Records a library diagnostic in the same slot (flint_last_cuda_error).
 void record_message(const char* msg);
+
+// Byte offset of the sticky status word inside each kernel family's workspace (flint_workspace_status_offset);
+// each is defined beside its workspace struct.
+int64_t status_offset_lm_head();
+int64_t status_offset_moe();
+int64_t status_offset_moe_fused();
+int64_t status_offset_moe_block();
+int64_t status_offset_attn_proj();
+int64_t status_offset_attn_block();
+int64_t status_offset_decode_attention();
 
 // Every kernel runs with the maximum shared-memory carveout, so consecutive kernels of a decode step never make an
 // SM re-partition L1 / shared memory between them.  Set once per (kernel, device).

@@ -26,6 +26,7 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
+from . import _lib
 from . import ops as _ops
 from .fp4moe_decode import DecodeWeights
 from .nvfp4 import random_nvfp4
@@ -468,6 +469,13 @@ class Decoder:
         if name == "head":                                 # this rank's vocabulary rows
             return nv(self.m.v_local, H) + M * 2 * H * 2
         raise KeyError(name)
+
+    def check_status(self, clear: bool = True):
+        """Raise FlintError if a kernel of this device reported a problem since the last check (a bounded wait
+        that timed out, an expert id or a sequence out of range) or a peer wait of this rank timed out."""
+        _lib.check_device_status(self.m.dev, clear)
+        if self.peers is not None and self.peers.status():
+            raise _lib.FlintError(f"peer exchange status {self.peers.status():#x}: a wait for another rank timed out")
 
     def close(self):
         """Release the captured graphs and, for a sharded model, the peer exchange buffers (collective: every rank

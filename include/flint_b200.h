@@ -54,6 +54,29 @@ const char* flint_error_string(int code);
  * (the detail behind FLINT_ERR_LAUNCH / FLINT_ERR_DEVICE), or "" if none has. */
 const char* flint_last_cuda_error(void);
 
+/* Device-side health.  Every kernel that waits (on an mbarrier, a grid barrier, another CTA's published words) waits
+ * for a bounded time and never traps; what went wrong is OR-ed into a sticky status word in its workspace, and the
+ * launch returns.  The host reads it between steps.  Workspace kinds (the workspace passed to the entry points of
+ * that family) and status bits: */
+enum {
+  FLINT_WS_LM_HEAD = 0,           /* flint_lm_head_* (plain and sampling workspaces) */
+  FLINT_WS_MOE = 1,               /* flint_moe_route / up / down (+ _ep) */
+  FLINT_WS_MOE_FUSED = 2,         /* flint_moe_fused */
+  FLINT_WS_MOE_BLOCK = 3,         /* flint_moe_block (+ _ep, _peer) */
+  FLINT_WS_ATTN_PROJ = 4,         /* flint_attn_qkv, flint_attn_o */
+  FLINT_WS_ATTN_BLOCK = 5,        /* flint_attn_block */
+  FLINT_WS_DECODE_ATTENTION = 6   /* flint_decode_attention */
+};
+enum {
+  FLINT_STATUS_WAIT_TIMEOUT = 1,  /* a bounded wait gave up: that launch's outputs are invalid */
+  FLINT_STATUS_BAD_EXPERT = 2,    /* a routed expert id outside 0..E-1 (clamped) */
+  FLINT_STATUS_BAD_SEQUENCE = 4   /* a sequence longer than its block table (clamped to the table) */
+};
+/* Byte offset of the status word inside a workspace of `kind`, or -1 for an unknown kind (no GPU needed). */
+int64_t flint_workspace_status_offset(int kind);
+/* Reads the status word of `workspace` (synchronous device-to-host copy); clear != 0 also zeroes a non-zero word. */
+int flint_workspace_status(const void* workspace, int kind, uint32_t* status, int clear);
+
 /* ------------------------------------------------------------------------------------------------
  * (4) NVFP4 LM head.
  * Replaces fast/fast_head.py: FastHead.__call__ (lines 200-207) -> nv4_logits_fma (118-121) /

@@ -90,3 +90,38 @@ def test_attention_partition_invariants(pages, nkv, G):
         assert (ks == 0) == (ns == 0)
     if pages == [379] and nkv == 4:
         assert k == [37, 37, 37, 37]                        # the single-stream 6K case: 148 CTAs, 37 per kv head
+
+
+def test_workspace_status_words(fb, monkeypatch):
+    """The sticky status word of every workspace kind: offsets from the library (no GPU), the C argument checks,
+    and the host reader / raiser on stand-in workspaces in host memory."""
+    import ctypes
+    import torch
+    L = fb._lib
+    lib = L.lib()
+    want = {0: 68, 1: 4, 2: 128, 3: 128, 4: 0, 5: 128, 6: 0}
+    assert {k: lib.flint_workspace_status_offset(k) for k in want} == want
+    assert lib.flint_workspace_status_offset(7) == -1 and lib.flint_workspace_status_offset(-1) == -1
+    st = ctypes.c_uint32()
+    assert lib.flint_workspace_status(None, 0, ctypes.byref(st), 0) == 6
+    assert lib.flint_workspace_status(ctypes.c_void_p(256), 9, ctypes.byref(st), 0) == 6
+    fake = {(0, "lm_head"): torch.zeros(256, dtype=torch.uint8), (0, "moe"): torch.zeros(1088, dtype=torch.uint8),
+            (0, "attn_block_5120_4096"): torch.zeros(4096, dtype=torch.uint8),
+            (1, "moe_block_128_768"): torch.zeros(4096, dtype=torch.uint8),
+            (0, "align_status"): torch.zeros(4, dtype=torch.uint8), (0, "other"): torch.full((8,), 255, dtype=torch.uint8)}
+    monkeypatch.setattr(L, "_workspaces", fake)
+    assert L.device_status() == {}
+    fake[(0, "lm_head")][68:72].view(torch.int32)[0] = 1
+    fake[(0, "attn_block_5120_4096")][128:132].view(torch.int32)[0] = 4
+    fake[(1, "moe_block_128_768")][128:132].view(torch.int32)[0] = 3
+    fake[(0, "moe")][0:4].view(torch.int32)[0] = 7            # the route counter, not the status word
+    assert L.device_status() == {(0, "lm_head"): 1, (0, "attn_block_5120_4096"): 4, (1, "moe_block_128_768"): 3}
+    assert L.device_status(torch.device("cuda", 1)) == {(1, "moe_block_128_768"): 3}
+    with pytest.raises(L.FlintError, match="bounded wait timed out.*expert id"):
+        L.check_device_status(torch.device("cuda", 1))
+    assert L.device_status(torch.device("cuda", 1)) == {}      # cleared by the check
+    fake[(0, "align_status")].view(torch.int32)[0] = 1
+    with pytest.raises(L.FlintError, match="align_status.*sorted_ids"):
+        L.check_device_status(torch.device("cuda", 0))
+    assert L.device_status() == {}
+    assert fake[(0, "moe")][0:4].view(torch.int32)[0] == 7      # only status words are cleared
