@@ -1,9 +1,11 @@
 /*
  * flint_b200.h -- C ABI of the B200 (sm_100a) NVFP4 batch-1 decode kernels.
  *
- * Every entry point takes plain device pointers, sizes and a cudaStream_t passed as void*, launches
- * asynchronously on that stream and returns FLINT_OK or one of the FLINT_ERR_* codes below.  Nothing
- * here aborts, allocates device memory or synchronises the stream.
+ * Every compute entry point takes plain device pointers, sizes and a cudaStream_t passed as void*, launches
+ * asynchronously on that stream and returns FLINT_OK or one of the FLINT_ERR_* codes below; none of them
+ * aborts, allocates device memory or synchronises the stream.  The exceptions are marked where declared:
+ * the peer-buffer management (flint_peer_alloc / open / close / free / status) and flint_workspace_status.
+ * The header is plain C99.
  *
  * NVFP4 tensors use the ModelOpt layout the reference loads (patches/flint-vllm-pr62938.patch,
  * gguf_nvfp4.py, patch:269-319): codes uint8 [N, K/2] with the even k in the low nibble, block scales

@@ -52,3 +52,35 @@ def test_ops_refuse_cpu_tensors(fb):
     with pytest.raises(fb._lib.FlintError):
         fast_head.nv4_logits(torch.zeros((1, 128), dtype=torch.bfloat16), P, S, 1.0,
                              torch.empty((1, 16), dtype=torch.float32))
+
+
+def test_header_is_plain_c_and_links(fb, tmp_path):
+    """A C99 program (what a cgo / FFI host compiles) includes the header with -pedantic -Werror, takes the address
+    of every declared entry point (so linking proves each is exported) and runs the host-only calls."""
+    import shutil
+    import subprocess
+    if shutil.which("gcc") is None:
+        pytest.skip("no C compiler")
+    syms = _declared_symbols()
+    pkg = os.path.dirname(fb._lib.LIB_PATH)
+    src = tmp_path / "abi.c"
+    src.write_text(
+        '#include "flint_b200.h"\n#include <stdio.h>\n#include <string.h>\n'
+        "typedef void (*fn_t)(void);\n"
+        "static const fn_t all[] = {" + ", ".join(f"(fn_t){s}" for s in syms) + "};\n"
+        "int main(void) {\n"
+        "  int bad = 0;\n"
+        "  bad |= flint_version() < 100;\n"
+        '  bad |= strcmp(flint_error_string(FLINT_OK), "ok") != 0;\n'
+        "  bad |= flint_lm_head_workspace_bytes() < 72;\n"
+        "  bad |= flint_workspace_status_offset(FLINT_WS_MOE_BLOCK) < 0 || flint_workspace_status_offset(99) != -1;\n"
+        "  bad |= flint_gguf_nvfp4_repack(NULL, 1, 64, NULL, NULL, NULL, 0, NULL) != FLINT_ERR_ARGUMENT;\n"
+        '  printf("%d %d\\n", (int)(sizeof(all) / sizeof(all[0])), bad);\n'
+        "  return bad;\n}\n")
+    exe = tmp_path / "abi"
+    cc = subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror",
+                         "-I", os.path.join(ROOT, "include"), str(src), "-L", pkg, "-lflint_b200",
+                         f"-Wl,-rpath,{pkg}", "-o", str(exe)], capture_output=True, text=True)
+    assert cc.returncode == 0, cc.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0 and run.stdout.split() == [str(len(syms)), "0"], (run.stdout, run.stderr)
