@@ -72,6 +72,17 @@ class DecodeWeights:
                                         topk=1, score="softmax")
             assert self.shared.H == self.H, "shared expert hidden size"
 
+    @classmethod
+    def from_layer(cls, w13, s13, g13, w2, s2, g2, sh_gu=None, sh_dn=None, topk: int = TOPK, score: str = SCORE):
+        """The reference's argument grouping (MarlinDecodeWeights, fast/fp4moe_decode.py:27-44): the routed experts'
+        six tensors, then the shared expert's gate_up and down projections as (weight, weight_scale, global scale)
+        tuples -- here the layer's ModelOpt NVFP4 tensors (gate rows before up rows), not the Marlin repack."""
+        if (sh_gu is None) != (sh_dn is None):
+            raise ValueError("the shared expert needs both its gate_up and its down projection")
+        shared = None if sh_gu is None else (sh_gu[0], sh_gu[1], sh_gu[2].float().reshape(-1)[:1], sh_dn[0], sh_dn[1],
+                                             sh_dn[2].float().reshape(-1)[:1])
+        return cls(w13, s13, g13, w2, s2, g2, topk=topk, score=score, shared=shared)
+
 
 def _route_impl(x, res, nw, eps, gate_w, topk, score_fn, want_norm):
     M, H = x.shape

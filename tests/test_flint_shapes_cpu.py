@@ -160,3 +160,19 @@ def test_config_validation_and_bytes(fb):
     battn = nv(b.qkv_rows, H) + nv(H, 4096)
     bmoe = 8 * (nv(2 * 768, H) + nv(H, 768)) + 128 * H * 2
     assert b.weight_bytes_per_token() == 48 * (battn + bmoe) + nv(151552, H) == 1_728_577_536
+
+
+def test_from_layer_takes_the_reference_grouping(fb):
+    from flint_b200 import fp4moe_decode as fm
+    from flint_b200.nvfp4 import random_nvfp4
+    g = torch.Generator().manual_seed(2)
+    E, H, I, SI = 32, 256, 64, 128
+    routed = random_nvfp4((E,), 2 * I, H, 0.02, g, "cpu") + random_nvfp4((E,), H, I, 0.02, g, "cpu")
+    gu, dn = random_nvfp4((), 2 * SI, H, 0.02, g, "cpu"), random_nvfp4((), H, SI, 0.02, g, "cpu")
+    w = fm.DecodeWeights.from_layer(*routed, (gu[0], gu[1], gu[2].reshape(1, 1)), dn, topk=4, score="sigmoid")
+    assert (w.E, w.I, w.topk, w.score_fn) == (E, I, 4, 1)
+    assert (w.shared.I, w.shared.H) == (SI, H) and w.shared.g13.shape == (1,)
+    assert torch.equal(w.shared.w13[0], gu[0]) and torch.equal(w.shared.w2[0], dn[0])
+    assert fm.DecodeWeights.from_layer(*routed).shared is None
+    with pytest.raises(ValueError):
+        fm.DecodeWeights.from_layer(*routed, gu, None)
