@@ -127,9 +127,10 @@ class FlintModel:
 
     shard = (rank, world): this GPU's part of a model split over `world` GPUs by expert parallelism (experts
     rank*E/world .. (rank+1)*E/world - 1 of every MoE layer) and vocabulary sharding (rows rank*V/world ..
-    (rank+1)*V/world - 1 of the LM head); attention, router, norms and embedding are replicated.  Every rank draws
-    the whole model from the same seeded sequence and keeps its slices, so the shards are exactly the single-GPU
-    model's tensors."""
+    (rank+1)*V/world - 1 of the LM head); attention, router, norms, embedding, the shared expert and the dense
+    layers are replicated (every rank computes them in full after the expert exchange, so all ranks hold the same
+    hidden state).  Every rank draws the whole model from the same seeded sequence and keeps its slices, so the
+    shards are exactly the single-GPU model's tensors."""
 
     def __init__(self, cfg: FlintConfig, device="cuda", seed: int = 0, max_ctx: int = 8192, max_batch: int = 1,
                  shard: tuple[int, int] = (0, 1)):
@@ -138,8 +139,6 @@ class FlintModel:
         self.rank, self.world = shard
         if self.world > 1 and (cfg.num_experts % self.world or cfg.vocab % (256 * self.world)):
             raise ValueError("experts and vocab / 256 must divide by the number of shards")
-        if self.world > 1 and (cfg.shared_inter or cfg.mlp_only_layers):
-            raise ValueError("shared experts and dense layers run on one GPU only")
         self.e_lo, self.n_local = self.rank * cfg.num_experts // self.world, cfg.num_experts // self.world
         self.v_lo, self.v_local = self.rank * cfg.vocab // self.world, cfg.vocab // self.world
         sl = lambda t: t[self.e_lo:self.e_lo + self.n_local].contiguous() if self.world > 1 else t
@@ -207,7 +206,12 @@ class Decoder:
         flint_lm_head_nv4_sample; the draw of step t uses the Philox counter (t, stream)."""
         # measured per layer at 6K context: one stream, the block; 2..5 streams, the chain (67.7 us at 4 against the
         # fused launch's 70.9); 6..8, the fused launch (118 us at 8 against the chain's 135).  Sharded: block or chain.
-        moe = moe or ("block" if batch == 1 else "chain" if batch <= 5 or model.world > 1 else "fused")
+        sharded_shared = model.world > 1 and model.cfg.shared_inter > 0
+        moe = moe or ("block" if batch == 1 and not sharded_shared else
+                      "chain" if batch <= 5 or model.world > 1 else "fused")
+        if sharded_shared and moe != "chain":
+            # the shared expert reads the normalised input, which the sharded block launches do not write out
+            raise ValueError("a sharded model with a shared expert decodes with moe='chain'")
         if moe not in ("block", "chain", "fused"):
             raise ValueError(f"moe must be 'block', 'chain' or 'fused', got {moe!r}")
         if moe == "block" and batch != 1:

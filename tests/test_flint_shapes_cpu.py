@@ -176,3 +176,36 @@ def test_from_layer_takes_the_reference_grouping(fb):
     assert fm.DecodeWeights.from_layer(*routed).shared is None
     with pytest.raises(ValueError):
         fm.DecodeWeights.from_layer(*routed, gu, None)
+
+
+def test_sharded_flint_layers_dispatch(rec, tmp_path):
+    """Expert-parallel decode of a Flint-shaped model: routed experts sliced per rank, the shared expert and the
+    dense layer replicated and run after the exchange (a one-rank gloo group stands in for the NCCL group)."""
+    import socket
+    import torch.distributed as dist
+    from flint_b200.model import Decoder, FlintModel
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1)
+    try:
+        cfg = _small(layers=2, mlp_only_layers=(0,), shared_inter=128, dense_inter=192, score="sigmoid")
+        m0 = FlintModel(cfg, device="cpu", seed=3, max_ctx=64, max_batch=2, shard=(0, 2))
+        m1 = FlintModel(cfg, device="cpu", seed=3, max_ctx=64, max_batch=2, shard=(1, 2))
+        e0, e1 = m0.layers[1]["experts"], m1.layers[1]["experts"]
+        assert e0.E == e1.E == 16 and not torch.equal(e0.w13, e1.w13)                  # routed: this rank's half
+        assert torch.equal(e0.shared.w13, e1.shared.w13)                                  # shared: replicated
+        assert torch.equal(m0.layers[0]["experts"].w2, m1.layers[0]["experts"].w2)        # dense: replicated
+        with pytest.raises(ValueError, match="moe='chain'"):
+            Decoder(m0, batch=1, moe="block", group=dist.group.WORLD, exchange="nccl")
+        dec = Decoder(m0, batch=1, group=dist.group.WORLD, exchange="nccl")
+        assert dec.moe == "chain"
+        calls = _step_calls(rec, dec)
+        assert [n for n, _ in calls[0]] == ["attn_block", "moe_route", "moe_up", "moe_down"]
+        assert [n for n, _ in calls[1]] == ["attn_block", "moe_route", "moe_up_ep", "moe_down_ep", "moe_combine",
+                                            "moe_up", "moe_down"]
+        assert calls[1][-2][1][0] is dec.xn and calls[1][-1][1][6] is dec.ys
+        assert dec.launches_per_step == 2 + 3 + (4 + 2) + 2 + 1
+    finally:
+        dist.destroy_process_group()
