@@ -84,6 +84,23 @@ class DecodeWeights:
         return cls(w13, s13, g13, w2, s2, g2, topk=topk, score=score, shared=shared)
 
 
+class MarlinDecodeWeights(DecodeWeights):
+    """The reference's constructor and argument order (fast/fp4moe_decode.py:27-44, called at fast/model.py:277-282):
+    the routed experts' six tensors, then the shared expert's gate_up and down as (weight, weight_scale, global
+    scale) tuples, with Flint's routing (top-6 sigmoid, or FLINT_MOE_TOPK / FLINT_MOE_SCORE).  These kernels read
+    the ModelOpt NVFP4 layout in place, so the tensors must be the ModelOpt ones (uint8 codes); the Marlin repack the
+    GB10 kernels read (int32 tiles) is refused with a ValueError."""
+
+    def __init__(self, w13, s13, g13, w2, s2, g2, sh_gu, sh_dn):
+        if w13.dtype != torch.uint8 or w2.dtype != torch.uint8:
+            raise ValueError("MarlinDecodeWeights: these kernels read the ModelOpt NVFP4 layout (uint8 codes "
+                             f"[E, 2I, H/2]), got {w13.dtype} / {w2.dtype}: pass the layer's ModelOpt w13_weight / "
+                             "w2_weight (and scales), not the Marlin repack")
+        shared = (sh_gu[0], sh_gu[1], sh_gu[2].float().reshape(-1)[:1], sh_dn[0], sh_dn[1],
+                  sh_dn[2].float().reshape(-1)[:1])
+        super().__init__(w13, s13, g13, w2, s2, g2, topk=TOPK, score=SCORE, shared=shared)
+
+
 def _route_impl(x, res, nw, eps, gate_w, topk, score_fn, want_norm):
     M, H = x.shape
     E = gate_w.shape[0]

@@ -209,3 +209,20 @@ def test_sharded_flint_layers_dispatch(rec, tmp_path):
         assert dec.launches_per_step == 2 + 3 + (4 + 2) + 2 + 1
     finally:
         dist.destroy_process_group()
+
+
+def test_marlin_decode_weights_name_takes_modelopt_tensors(fb):
+    """The reference's MarlinDecodeWeights(w13, s13, g13, w2, s2, g2, sh_gu, sh_dn) call works unchanged with the
+    ModelOpt tensors (Flint's top-6 sigmoid routing + the shared expert) and refuses Marlin's int32 tiles."""
+    from flint_b200 import fp4moe_decode as fm
+    from flint_b200.nvfp4 import random_nvfp4
+    g = torch.Generator().manual_seed(4)
+    E, H, I, SI = 32, 256, 64, 128
+    routed = random_nvfp4((E,), 2 * I, H, 0.02, g, "cpu") + random_nvfp4((E,), H, I, 0.02, g, "cpu")
+    gu, dn = random_nvfp4((), 2 * SI, H, 0.02, g, "cpu"), random_nvfp4((), H, SI, 0.02, g, "cpu")
+    w = fm.MarlinDecodeWeights(*routed, gu, dn)
+    assert isinstance(w, fm.DecodeWeights) and (w.topk, w.score_fn) == (fm.TOPK, fm._SCORE_FN[fm.SCORE])
+    assert w.shared is not None and w.shared.I == SI
+    marlin = (torch.zeros((E, 8, 16), dtype=torch.int32),) + routed[1:]
+    with pytest.raises(ValueError, match="ModelOpt"):
+        fm.MarlinDecodeWeights(*marlin, gu, dn)
