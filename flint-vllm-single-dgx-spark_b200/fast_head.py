@@ -7,6 +7,10 @@ Same entry points and argument meaning as the reference:
 * ``FastHead(weight, scale, mode, nv4)`` (fast/fast_head.py:182-215) with ``__call__(x) -> logits``.
 * ``compute_logits(model, hidden_states)`` (fast/fast_head.py:360-381): logits or ``None`` for the caller's
   stock path, env-gated by ``FLINT_FAST_HEAD`` / ``FLINT_FAST_HEAD_MAX_M``.
+* The reference's run-time aids, same switches: ``install_guards()`` keeps vLLM's prompt-logprob calls on the stock
+  path (fast/fast_head.py:235-268); ``FLINT_FAST_HEAD_VERIFY=1`` also runs the stock path on every call and logs the
+  argmax / top-20 / value / log-sum-exp agreement every 400 calls (:337-357); ``FLINT_HEAD_CAPTURE_DIR`` collects the
+  hidden states the head sees and writes them out when a ``FLUSH`` file appears there (:313-334).
 
 Additions for the fused path: ``FastHead.greedy(x)`` (logits + argmax in the same pass) and
 ``FastHead.sample(...)`` (top-k -> top-p -> seeded draw without materialising the logits).
@@ -22,6 +26,8 @@ import torch
 from . import ops as _ops
 
 ENABLED = os.environ.get("FLINT_FAST_HEAD", "0") == "1"
+VERIFY = os.environ.get("FLINT_FAST_HEAD_VERIFY", "0") == "1"
+CAPTURE_DIR = os.environ.get("FLINT_HEAD_CAPTURE_DIR", "")
 MAX_M = int(os.environ.get("FLINT_FAST_HEAD_MAX_M", "8"))
 MODE = os.environ.get("FLINT_FAST_HEAD_MODE", "nv4")
 GROUP = 16
@@ -115,10 +121,110 @@ class FastHead:
 # integration hook (reference: fast/fast_head.py:285-312,360-381)
 # ---------------------------------------------------------------------------------------------------------
 _state = {"head": None, "failed": False, "bypass": 0}
+_cap = {"buf": [], "n": 0, "part": 0}
+_ver = {"n": 0, "rows": 0, "argmax_mis": None, "top20_miss": None, "val_mis": None, "val_cnt": None,
+        "maxdiff": None, "lse_maxdiff": None}
 
 
 def _log(msg):
     print(f"[flint-fast-head] {msg}", file=sys.stderr, flush=True)
+
+
+def _capturing() -> bool:
+    """A CUDA graph capture is in progress on the current stream (never on a host without a usable GPU)."""
+    return torch.cuda.is_available() and torch.cuda.is_current_stream_capturing()
+
+
+def _wrap_bypass(cls, name):
+    """Make cls.name run with the fast head bypassed (compute_logits returns None inside it); idempotent."""
+    orig = getattr(cls, name, None)
+    if orig is None or getattr(orig, "_flint_bypass", False):
+        return
+
+    def bypassed(*args, **kwargs):
+        _state["bypass"] += 1
+        try:
+            return orig(*args, **kwargs)
+        finally:
+            _state["bypass"] -= 1
+    bypassed._flint_bypass = True
+    bypassed.__wrapped__ = orig
+    setattr(cls, name, bypassed)
+
+
+def install_guards() -> int:
+    """Prompt logprobs are computed from compute_logits on prompt rows: keep those calls on the stock path.  Wraps
+    the prompt-logprob methods of vLLM's model runners that exist in the installed vLLM; returns how many."""
+    n = 0
+    targets = (("vllm.v1.worker.gpu.sample.prompt_logprob", "PromptLogprobsWorker",
+                ("compute_prompt_logprobs", "compute_prompt_token_id_logprobs")),
+               ("vllm.v1.worker.gpu_model_runner", "GPUModelRunner", ("_get_prompt_logprobs_dict",)))
+    for module, cls_name, methods in targets:
+        try:
+            import importlib
+            cls = getattr(importlib.import_module(module), cls_name)
+        except Exception as e:                         # this vLLM has no such runner: nothing to guard
+            _log(f"{module}.{cls_name} guard not installed: {type(e).__name__}: {e}")
+            continue
+        for m in methods:
+            if getattr(cls, m, None) is not None:
+                _wrap_bypass(cls, m)
+                n += 1
+    _log(f"prompt-logprob guards installed: {n}")
+    return n
+
+
+def _flush_capture(model, label):
+    """Write the collected hidden rows (and once, the head they go through) under CAPTURE_DIR."""
+    if not _cap["buf"]:
+        return
+    h = torch.cat(_cap["buf"], 0).cpu()
+    path = os.path.join(CAPTURE_DIR, f"part{_cap['part']:03d}_{label}.pt")
+    torch.save({"hidden": h, "label": label}, path)
+    head_path = os.path.join(CAPTURE_DIR, "head.pt")
+    if not os.path.exists(head_path):
+        lm, lp = model.lm_head, getattr(model, "logits_processor", None)
+        head = {k: getattr(lm, k).data.cpu() for k in ("weight", "weight_scale", "weight_scale_2")
+                if isinstance(getattr(lm, k, None), torch.Tensor)}
+        head["scale"] = float(getattr(lp, "scale", 1.0) if lp is not None else 1.0)
+        torch.save(head, head_path)
+    _log(f"captured {h.shape[0]} hidden rows -> {path}")
+    _cap.update(buf=[], n=0, part=_cap["part"] + 1)
+
+
+def _capture(model, x):
+    """Keep a copy of the hidden rows; a FLUSH file in CAPTURE_DIR (its text = the label) writes the earlier ones."""
+    flag = os.path.join(CAPTURE_DIR, "FLUSH")
+    if os.path.exists(flag):
+        with open(flag) as f:
+            label = f.read().strip() or "x"
+        os.remove(flag)
+        _flush_capture(model, label)
+    _cap["buf"].append(x.detach().clone())
+    _cap["n"] += x.shape[0]
+
+
+def _verify(model, x, fast_out):
+    """Accumulate the agreement of the fast logits with the stock path's on the same rows; log every 400 calls."""
+    stock = model.logits_processor(model.lm_head, x).float()
+    fast = fast_out[:, :stock.shape[1]].float()
+    finite = fast > float("-inf")
+    diff = (fast - stock).abs().masked_fill(~finite, 0.0)
+    stats = dict(argmax_mis=(stock.argmax(-1) != fast.argmax(-1)).sum(),
+                 top20_miss=(fast.gather(1, stock.topk(min(20, stock.shape[1]), dim=-1).indices)
+                             == float("-inf")).sum(),
+                 val_mis=((diff != 0) & finite).sum(), val_cnt=finite.sum(), maxdiff=diff.max(),
+                 lse_maxdiff=(torch.logsumexp(stock, -1) - torch.logsumexp(fast, -1)).abs().max())
+    for k, v in stats.items():
+        prev = _ver[k]
+        _ver[k] = v if prev is None else (torch.maximum(prev, v) if k in ("maxdiff", "lse_maxdiff") else prev + v)
+    _ver["rows"] += x.shape[0]
+    _ver["n"] += 1
+    if _ver["n"] % 400 == 0:
+        _log("VERIFY rows=%d argmax_mismatch=%d top20_missing=%d value_mismatches=%d/%d max|fast-stock|=%.4g "
+             "max|lse_stock-lse_fast|=%.4g" % (_ver["rows"], int(_ver["argmax_mis"]), int(_ver["top20_miss"]),
+                                                int(_ver["val_mis"]), int(_ver["val_cnt"]), float(_ver["maxdiff"]),
+                                                float(_ver["lse_maxdiff"])))
 
 
 def _nv4_from_gguf(model, W):
@@ -181,13 +287,21 @@ def compute_logits(model, hidden_states):
     m = hidden_states.shape[0]
     if m < 1 or m > MAX_M:
         return None
+    if CAPTURE_DIR and not _capturing():
+        _capture(model, hidden_states)
     if not ENABLED or _state["failed"]:
         return None
     if _state["head"] is None:
-        if torch.cuda.is_current_stream_capturing():
+        if _capturing():
             return None
         _build(model)
         if _state["head"] is None:
             return None
-    out = _state["head"](hidden_states)
-    return out[:, :_state["org_vocab"]]
+    out = _state["head"](hidden_states)[:, :_state["org_vocab"]]
+    if VERIFY and not _capturing():
+        _verify(model, hidden_states, out)
+    return out
+
+
+if ENABLED or CAPTURE_DIR:
+    install_guards()
