@@ -274,12 +274,13 @@ def run_ours(args):
 
 def cpu_baseline_sample(cfg, n_tokens, context):
     """The CPU oracle (the reference's dequantise-to-fp32 torch path) on a bounded sample: n decode tokens of the
-    same model shape at the same context.  Returns the cpu_baseline object."""
+    same model shape at the same context, after one untimed warm-up token.  Returns the cpu_baseline object."""
     sys.path.insert(0, ROOT)
     from oracle import model_cpu
-    res = model_cpu.time_decode(cfg, n_tokens=n_tokens, context=context)
+    res = model_cpu.time_decode(cfg, n_tokens=n_tokens, context=context, warmup=1)   # after one untimed token
     try:                                # the steady-state variant needs ~7.5 GB of host memory for fp32 weights
-        res["steady_state"] = model_cpu.time_decode(cfg, n_tokens=n_tokens, context=context, predequantized=True)
+        res["steady_state"] = model_cpu.time_decode(cfg, n_tokens=n_tokens, context=context, warmup=1,
+                                                    predequantized=True)
     except (RuntimeError, MemoryError) as e:
         res["steady_state"] = {"unavailable": str(e)[:200]}
     return res
@@ -294,12 +295,15 @@ def run_reference(args):
     sys.path.insert(0, ROOT)
     from oracle import model_cpu
     cfg = FlintConfig()
+    # a bounded sample: --cpu-sample-tokens timed tokens after one untimed warm-up token (thread pool, allocator),
+    # so the whole run stays within minutes whatever --steps asks for
+    warm = min(max(args.warmup, 0), 1)
     res = model_cpu.time_decode(cfg, n_tokens=max(1, args.cpu_sample_tokens), context=args.prompt,
-                                warmup=0)
+                                warmup=warm)
     line = {
         "impl": "reference",
         "metric": "c1 decode tok/s, Flint-class NVFP4 MoE (greedy, 800 tokens after a 6057-token prompt)",
-        "value": res["value"], "unit": "tok/s", "n_gpus": 0, "steps": res["tokens"], "warmup": 0,
+        "value": res["value"], "unit": "tok/s", "n_gpus": args.gpus, "steps": res["tokens"], "warmup": warm,
         "ms_per_step": round(1e3 / res["value"], 2) if res["value"] else None, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp32 (weights dequantised from NVFP4 per call)",
         "data": "synthetic",

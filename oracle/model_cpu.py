@@ -129,7 +129,7 @@ def time_decode(cfg, n_tokens: int = 1, context: int = 6057, warmup: int = 0, pr
     dt = time.perf_counter() - t0
     return {"value": round(n_tokens / dt, 5), "unit": "tok/s", "cores": threads, "kind": "port",
             "tokens": n_tokens, "seconds": round(dt, 2),
-            "sample": f"{n_tokens} full-model decode token(s) at {context} tokens of KV context; "
+            "sample": f"{n_tokens} full-model decode token(s) at {context} tokens of KV context after {warmup} untimed; "
                       + ("weights dequantised to fp32 once (steady state)" if predequantized else
                          "per-call NVFP4 dequantisation") + " + fp32 matmuls (torch CPU), expert tensors shared across "
                       "layers"}
