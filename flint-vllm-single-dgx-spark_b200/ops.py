@@ -722,3 +722,91 @@ def nvfp4_dequant(P: torch.Tensor, S: torch.Tensor, global_scale: torch.Tensor |
 @nvfp4_dequant.register_fake
 def _(P, S, global_scale, out):
     return None
+
+
+# ------------------------------------------------------------------------------------------------------------
+# functional fused forms (allocate their outputs): the whole MoE block, the whole attention block, the whole head
+# ------------------------------------------------------------------------------------------------------------
+@torch.library.custom_op(f"{NS}::moe_decode", mutates_args=())
+def moe_decode(x: torch.Tensor, res: torch.Tensor | None, norm_w: torch.Tensor, eps: float, gate_w: torch.Tensor,
+               w13: torch.Tensor, s13: torch.Tensor, g13: torch.Tensor, w2: torch.Tensor, s2: torch.Tensor,
+               g2: torch.Tensor, topk: int, score_fn: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """(mlp(rmsnorm(x + res)), x + res) of the decode MoE block in one launch: flint_moe_block for one token when
+    its shape limits allow (H 2048, E <= 256, I <= 1024), else flint_moe_fused (1..8 tokens)."""
+    M, H = x.shape
+    E, I2, _ = w13.shape
+    out = torch.empty((M, H), dtype=torch.bfloat16, device=x.device)
+    res_out = torch.empty((M, H), dtype=torch.bfloat16, device=x.device)
+    if res is None:
+        res_out.copy_(x)
+    if M == 1 and H == 2048 and E <= 256 and I2 // 2 <= 1024:
+        moe_block(x, res, norm_w, eps, gate_w, topk, score_fn, w13, s13, g13, w2, s2, g2, out,
+                  res_out if res is not None else None, None, None, None, None)
+    else:
+        dev = x.device
+        moe_fused(x, res, norm_w, eps, gate_w, topk, score_fn, w13, s13, g13, w2, s2, g2, out, res_out,
+                  torch.empty((M, H), dtype=torch.bfloat16, device=dev),
+                  torch.empty((M, E), dtype=torch.float32, device=dev),
+                  torch.empty((M, topk), dtype=torch.int32, device=dev),
+                  torch.empty((M, topk), dtype=torch.float32, device=dev), False)
+    return out, res_out
+
+
+@moe_decode.register_fake
+def _(x, res, norm_w, eps, gate_w, w13, s13, g13, w2, s2, g2, topk, score_fn):
+    return torch.empty_like(x), torch.empty_like(x)
+
+
+@torch.library.custom_op(f"{NS}::attn_decode", mutates_args=("kv_cache",))
+def attn_decode(x: torch.Tensor, res: torch.Tensor | None, norm_w: torch.Tensor, eps: float, W: torch.Tensor,
+                S: torch.Tensor, gs: torch.Tensor, num_q_heads: int, num_kv_heads: int, q_norm_w: torch.Tensor,
+                k_norm_w: torch.Tensor, eps_head: float, positions: torch.Tensor, cos_sin: torch.Tensor | None,
+                kv_cache: torch.Tensor, block_tables: torch.Tensor, seq_lens: torch.Tensor, slots: torch.Tensor,
+                sinks: torch.Tensor | None, window: int, scale: float, Wo: torch.Tensor, So: torch.Tensor,
+                gs_o: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """(o_proj(attention(qkv(rmsnorm(x + res)))), x + res) of the decode attention block in one launch
+    (flint_attn_block): add + RMSNorm, QKV, q/k norm, RoPE (cos_sin None: none), the KV write at slots, paged GQA
+    attention (sinks, window) and the O projection."""
+    M = x.shape[0]
+    out = torch.empty((M, Wo.shape[0]), dtype=torch.bfloat16, device=x.device)
+    res_out = torch.empty((M, x.shape[1]), dtype=torch.bfloat16, device=x.device)
+    attn_block(x, res, norm_w, eps, W, S, gs, num_q_heads, num_kv_heads, q_norm_w, k_norm_w, eps_head, positions,
+               cos_sin, kv_cache, block_tables, seq_lens, slots, sinks, window, scale, Wo, So, gs_o, out, res_out, None,
+               None)
+    return out, res_out
+
+
+@attn_decode.register_fake
+def _(x, res, norm_w, eps, W, S, gs, num_q_heads, num_kv_heads, q_norm_w, k_norm_w, eps_head, positions, cos_sin,
+      kv_cache, block_tables, seq_lens, slots, sinks, window, scale, Wo, So, gs_o):
+    M = x.shape[0]
+    return x.new_empty((M, Wo.shape[0])), x.new_empty((M, x.shape[1]))
+
+
+@torch.library.custom_op(f"{NS}::lm_head", mutates_args=())
+def lm_head(x: torch.Tensor, P: torch.Tensor, S: torch.Tensor, gs: float, mode: str, temperature: float, top_k: int,
+            top_p: float, seeds: torch.Tensor | None, step: torch.Tensor | None,
+            want_logits: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    """(tokens int32 [M], logits fp32 [M, V] or an empty tensor) of the NVFP4 head in one pass: mode "greedy" (argmax,
+    lowest id on ties) or "sample" (seeded temperature -> top-k -> top-p draw; seeds int64 [M], step int32 [1])."""
+    if mode not in ("greedy", "sample"):
+        raise _lib.FlintError(f"lm_head: mode must be 'greedy' or 'sample', got {mode!r}")
+    M, dev = x.shape[0], x.device
+    tokens = torch.empty((M,), dtype=torch.int32, device=dev)
+    logits = torch.empty((M, P.shape[0]) if want_logits else (0,), dtype=torch.float32, device=dev)
+    if mode == "greedy":
+        lm_head_nv4(x, P, S, gs, logits if want_logits else torch.empty((1, 1), dtype=torch.float32, device=dev),
+                    tokens, want_logits, True)
+    else:
+        if seeds is None:
+            raise _lib.FlintError("lm_head: mode 'sample' needs one int64 seed per row")
+        lm_head_sample(x, P, S, gs, temperature, top_k, top_p, seeds, step, tokens, logits if want_logits else None,
+                       None, None, None)
+    return tokens, logits
+
+
+@lm_head.register_fake
+def _(x, P, S, gs, mode, temperature, top_k, top_p, seeds, step, want_logits):
+    M = x.shape[0]
+    return (x.new_empty((M,), dtype=torch.int32),
+            x.new_empty((M, P.shape[0]) if want_logits else (0,), dtype=torch.float32))
