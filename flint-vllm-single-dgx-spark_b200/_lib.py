@@ -130,10 +130,24 @@ def require_cuda(t: torch.Tensor, what: str) -> None:
 # ---------------------------------------------------------------------------------------------------------
 _workspaces: dict[tuple[int, str], torch.Tensor] = {}
 _retired: list[torch.Tensor] = []     # grown-out workspaces stay alive: captured graphs may still point at them
+_last_stream: dict[tuple[int, str], object] = {}
+
+
+def _order_after_last(key, stream, capturing: bool) -> None:
+    """Launches that share a workspace must not overlap: a launch from another stream than the previous user of
+    `key` first waits for that stream (as the PR's decode attention does, patch:2468-2481).  Not while a graph is
+    being captured: the captured order is the graph's own."""
+    if capturing:
+        return
+    last = _last_stream.get(key)
+    if last is not None and last != stream:
+        stream.wait_stream(last)
+    _last_stream[key] = stream
 
 
 def workspace(device: torch.device, kind: str, nbytes: int) -> torch.Tensor:
     key = (device.index if device.index is not None else torch.cuda.current_device(), kind)
+    _order_after_last(key, torch.cuda.current_stream(key[0]), torch.cuda.is_current_stream_capturing())
     ws = _workspaces.get(key)
     if ws is None or ws.numel() < nbytes:
         if torch.cuda.is_current_stream_capturing():

@@ -125,3 +125,29 @@ def test_workspace_status_words(fb, monkeypatch):
         L.check_device_status(torch.device("cuda", 0))
     assert L.device_status() == {}
     assert fake[(0, "moe")][0:4].view(torch.int32)[0] == 7      # only status words are cleared
+
+
+def test_workspace_users_on_other_streams_wait(fb, monkeypatch):
+    """A workspace used from a second stream makes that stream wait for the first one (never during capture)."""
+    L = fb._lib
+    monkeypatch.setattr(L, "_last_stream", {})
+
+    class Stream:
+        def __init__(self, name):
+            self.name, self.waited = name, []
+
+        def wait_stream(self, other):
+            self.waited.append(other.name)
+
+    a, b = Stream("a"), Stream("b")
+    L._order_after_last((0, "moe"), a, False)
+    L._order_after_last((0, "moe"), a, False)
+    assert a.waited == []
+    L._order_after_last((0, "moe"), b, False)
+    assert b.waited == ["a"]
+    L._order_after_last((0, "lm_head"), b, False)          # another workspace: its own history
+    assert b.waited == ["a"]
+    L._order_after_last((0, "moe"), a, True)               # capturing: no cross-stream wait, history unchanged
+    assert a.waited == [] and L._last_stream[(0, "moe")] is b
+    L._order_after_last((0, "moe"), a, False)
+    assert a.waited == ["b"]
