@@ -23,7 +23,7 @@ import sys
 
 import torch
 
-from . import ops as _ops
+from . import ops as _ops  # noqa: F401  (registers torch.ops.flint_b200.*)
 
 ENABLED = os.environ.get("FLINT_FAST_HEAD", "0") == "1"
 VERIFY = os.environ.get("FLINT_FAST_HEAD_VERIFY", "0") == "1"
