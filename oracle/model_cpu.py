@@ -13,6 +13,8 @@ only multiplies per token (the steady state).
 Sample: ``n_tokens`` decode tokens at ``context`` tokens of KV.  To keep host memory bounded the expert tensors of
 one layer are shared by all layers (the per-token work -- which experts are dequantised and multiplied -- is the same
 as with distinct layers); all other weights and the KV cache are per layer.  Weights are random valid NVFP4 bytes.
+Per layer: add + RMSNorm, QKV, q/k RMSNorm and NeoX RoPE (fast/attn_gemv2.cu:170-265), GQA attention over the
+context, O, add + RMSNorm, router top-k, the routed experts and their weighted sum; then the final norm and head.
 """
 from __future__ import annotations
 
@@ -46,6 +48,13 @@ def _rand_nvfp4(gen, N, K):
 
 def _rmsnorm(x, w, eps):
     return (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w).to(torch.bfloat16).float()
+
+
+def _rope(t, cos, sin):
+    """NeoX rotation of the last dimension (halves rotated against each other)."""
+    h = t.shape[-1] // 2
+    a, b = t[..., :h], t[..., h:]
+    return torch.cat([a * cos - b * sin, b * cos + a * sin], dim=-1)
 
 
 class CpuFlint:
@@ -86,12 +95,17 @@ class CpuFlint:
         H, D, nq, nkv = c.hidden, c.head_dim, c.num_heads, c.num_kv_heads
         res = self.embed[token].float()[None]
         h = torch.zeros_like(res)
+        ang = pos * (1.0 / (c.rope_theta ** (torch.arange(0, D, 2, dtype=torch.float64) / D)))
+        cos, sin = torch.cos(ang).float(), torch.sin(ang).float()
+        head_ones = torch.ones(D)
         for li, L in enumerate(self.layers):
             res = res + h
             x = _rmsnorm(res, self.ones, c.rms_eps)
             y = (x @ self._w("qkv", li, L["qkv"]).t()).to(torch.bfloat16).float()
-            q = y[:, :nq * D].reshape(nq, D)
-            L["k"][pos] = y[0, nq * D:(nq + nkv) * D].reshape(nkv, D)
+            q = _rope(_rmsnorm(y[:, :nq * D].reshape(nq, D), head_ones, c.rms_eps), cos, sin)
+            q = q.to(torch.bfloat16).float()
+            k_new = _rope(_rmsnorm(y[0, nq * D:(nq + nkv) * D].reshape(nkv, D), head_ones, c.rms_eps), cos, sin)
+            L["k"][pos] = k_new.to(torch.bfloat16).float()
             L["v"][pos] = y[0, (nq + nkv) * D:].reshape(nkv, D)
             K, V = L["k"][:pos + 1], L["v"][:pos + 1]
             G = nq // nkv

@@ -93,3 +93,26 @@ def test_sampling_rule_host():
     assert r["kept"] == int((asc > 0.5).sum())
     us = [float(osamp.uniform(99, s, 3)) for s in range(2000)]
     assert 0.0 <= min(us) and max(us) < 1.0 and abs(np.mean(us) - 0.5) < 0.03
+
+
+def test_cpu_baseline_pieces_match_the_pinned_oracle():
+    """The CPU baseline (oracle/model_cpu.py, timed by bench.py) computes with the same pieces as the pinned oracle:
+    its per-call dequantisation equals the oracle's bit for bit (itself pinned to the reference above) and its
+    NeoX rotation equals the oracle's RoPE table applied to the same vectors."""
+    import torch
+    from oracle import attention as oatt
+    from oracle import model_cpu
+    rng = np.random.default_rng(3)
+    P = rng.integers(0, 256, (40, 64), dtype=np.uint8)
+    S = rng.integers(0, 0x7F, (40, 8), dtype=np.uint8)
+    gs = np.float32(0.0371)
+    got = model_cpu.dequantize_nvfp4(torch.from_numpy(P), torch.from_numpy(S), float(gs), chunk=16).numpy()
+    np.testing.assert_array_equal(got, onv.dequantize_nvfp4(P, S, gs))
+    D, pos, theta = 128, 4321, 1e6
+    t = rng.standard_normal((5, D)).astype(np.float32)
+    ang = pos * (1.0 / (theta ** (torch.arange(0, D, 2, dtype=torch.float64) / D)))
+    mine = model_cpu._rope(torch.from_numpy(t), torch.cos(ang).float(), torch.sin(ang).float()).numpy()
+    cs = oatt.rope_cos_sin(pos + 1, D, theta)[pos]
+    c, s = cs[:D // 2], cs[D // 2:]
+    ref = np.concatenate([t[:, :D // 2] * c - t[:, D // 2:] * s, t[:, D // 2:] * c + t[:, :D // 2] * s], axis=1)
+    np.testing.assert_allclose(mine, ref, rtol=1e-6, atol=1e-6)
