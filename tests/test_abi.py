@@ -84,3 +84,31 @@ def test_header_is_plain_c_and_links(fb, tmp_path):
     assert cc.returncode == 0, cc.stderr
     run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert run.returncode == 0 and run.stdout.split() == [str(len(syms)), "0"], (run.stdout, run.stderr)
+
+
+_NULL_CALLS = r"""
+import ctypes, sys
+sys.path.insert(0, sys.argv[1])
+from conftest import load_package
+fb = load_package()
+lib = fb._lib.lib()
+for name, (res, args) in fb._lib.SIGNATURES.items():
+    if res is not ctypes.c_int or not args:
+        continue
+    print(name, end=" ", flush=True)
+    vals = [None if a is ctypes.c_void_p else (0.0 if a is ctypes.c_float else 0) for a in args]
+    print(getattr(lib, name)(*vals), flush=True)
+"""
+
+
+def test_every_entry_point_rejects_null_arguments(fb):
+    """Null pointers and zero sizes give an error code from every status-returning entry point -- no crash, no
+    launch (run in a child process, so a crash would name the entry point)."""
+    import subprocess
+    import sys
+    run = subprocess.run([sys.executable, "-c", _NULL_CALLS, os.path.join(ROOT, "tests")], capture_output=True,
+                         text=True, timeout=300, cwd=ROOT)
+    assert run.returncode == 0, (run.stdout[-500:], run.stderr[-1500:])
+    results = dict(line.split() for line in run.stdout.strip().splitlines())
+    assert len(results) >= 30
+    assert all(int(rc) != 0 for rc in results.values()), {k: v for k, v in results.items() if int(v) == 0}
