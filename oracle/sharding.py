@@ -9,6 +9,9 @@ TEST INFRASTRUCTURE ONLY: used by tests/ (gloo ranks on CPU) to check the exchan
 * Head: rank r holds rows [r*V/N, (r+1)*V/N); its best argmax key is (order-preserving fp32 image << 32 |
   (0xFFFFFFFF - global id)) with the top bit flipped so that a signed int64 MAX over ranks orders keys as the
   unsigned comparison does; the maximum key carries the lowest id among the largest logits (vLLM's greedy pick).
+* Sampled head: rank r's shard contributes its own top-k (global ids, fp32 logits, value descending, lowest id first
+  on ties); the top-k of the gathered candidates under the same order is the full vocabulary's top-k, since every
+  member of the global top-k is in its own shard's top-k, so the draw over them equals the one-GPU draw.
 """
 from __future__ import annotations
 
