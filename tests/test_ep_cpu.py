@@ -1,10 +1,11 @@
-"""Multi-GPU exchange logic on CPU: world_size-2 gloo ranks run the sharded MoE sum + combine, the
+"""Multi-GPU exchange logic on CPU: world_size-2 and -4 gloo ranks run the sharded MoE sum + combine, the
 vocabulary-sharded argmax and the vocabulary-sharded sampled head (per-shard top-k candidates, all_gather, merge,
 draw) with the same arithmetic as the GPU path, against the single-process result."""
 import os
 import socket
 
 import numpy as np
+import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
@@ -68,11 +69,12 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_sharded_exchange_gloo_world2():
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_exchange_gloo(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     out = [q.get(timeout=120) for _ in procs]
