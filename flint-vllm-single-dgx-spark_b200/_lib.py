@@ -29,6 +29,7 @@ SIGNATURES: dict[str, tuple] = {
     "flint_lm_head_workspace_bytes": (I64, []),
     "flint_lm_head_nv4": (I32, [P, I64, I64, P, P, F32, I64, I64, P, I64, P, P, I32, P]),
     "flint_lm_head_nv4_noalloc": (I32, [P, I64, I64, P, P, F32, I64, I64, P, I64, P, I32, P]),
+    "flint_lm_head_noalloc_status": (I32, [P, I32]),
     "flint_lm_head_nv4_fused": (I32, [P, I64, P, P, F32, I64, P, P, F32, I64, I64, P, I64, P, P, I32, P]),
     "flint_lm_head_sample_workspace_bytes": (I64, [I64, I64]),
     "flint_lm_head_nv4_sample": (I32, [P, I64, P, P, F32, I64, P, P, F32, I64, I64, P, I64, F32, I64, F32, P, P, P, P, P, P,

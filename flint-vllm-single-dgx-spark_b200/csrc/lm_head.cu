@@ -1,6 +1,9 @@
 // (4) NVFP4 LM head: logits and the greedy argmax, or the seeded top-k -> top-p draw, in one pass over the head.
 // Replaces the reference's Triton _nv4_fma / _nv4_head (fast/fast_head.py:68-121) and the pick of vLLM's sampler
 // that follows compute_logits (fast/fast_head.py:360-381).  Kernel design: lm_head_kernel.cuh, sampling.cuh.
+#include <atomic>
+#include <cstddef>
+
 #include "lm_head_kernel.cuh"
 #include "runtime.cuh"
 
@@ -20,10 +23,12 @@ static size_t head_smem(int M, int K, bool norm) {
 extern "C" int64_t flint_lm_head_workspace_bytes(void) { return sizeof(flint::HeadWorkspace); }
 int64_t flint::status_offset_lm_head() { return (int64_t)offsetof(flint::HeadWorkspace, status); }
 
-extern "C" int flint_lm_head_nv4_fused(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, int64_t M,
-                                       const void* P, const void* S, float gs, int64_t V, int64_t K, float* logits,
-                                       int64_t ld_logits, int32_t* token_ids, void* workspace, int pdl, void* stream) {
-  using namespace flint;
+namespace flint {
+
+// Argument, shape and alignment checks of the greedy head (everything but the workspace), shared by the entry
+// points that take a workspace and the allocation-free one, which must refuse a call before it touches its scratch.
+static int head_check_args(const void* x, int64_t ldx, const void* res, const void* norm_w, int64_t M, const void* P,
+                           const void* S, int64_t V, int64_t K, const float* logits, int64_t ld_logits) {
   if (!x || !P || !S || (res && !norm_w)) return FLINT_ERR_ARGUMENT;
   if (M < 1 || M > 8 || V < 1 || V > (1ll << 30) || K < kSliceK || K % kSliceK != 0 || K > 8192 || ldx < K)
     return FLINT_ERR_SHAPE;
@@ -31,6 +36,17 @@ extern "C" int flint_lm_head_nv4_fused(const void* x, int64_t ldx, const void* r
   if (!aligned(P, 16) || !aligned(S, 16) || !aligned(x, 16) || ldx % 8 != 0 || (res && !aligned(res, 16)) ||
       (norm_w && !aligned(norm_w, 16)))
     return FLINT_ERR_ALIGN;
+  return FLINT_OK;
+}
+
+}  // namespace flint
+
+extern "C" int flint_lm_head_nv4_fused(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, int64_t M,
+                                       const void* P, const void* S, float gs, int64_t V, int64_t K, float* logits,
+                                       int64_t ld_logits, int32_t* token_ids, void* workspace, int pdl, void* stream) {
+  using namespace flint;
+  const int arg_rc = head_check_args(x, ldx, res, norm_w, M, P, S, V, K, logits, ld_logits);
+  if (arg_rc != FLINT_OK) return arg_rc;
   if (!workspace) return FLINT_ERR_WORKSPACE;
   if (!aligned(workspace, 8)) return FLINT_ERR_ALIGN;
   const int sms = num_sms();
@@ -231,34 +247,39 @@ extern "C" int flint_lm_head_nv4(const void* x, int64_t ldx, int64_t M, const vo
 // Allocation-free variant of flint_lm_head_nv4.
 //
 // Some callers cannot allocate device memory when they call the head: an inference engine that has handed all free
-// HBM to its KV-cache pool up front, code running inside a CUDA-graph capture (where cudaMalloc is not allowed),
-// or a host runtime that reaches this library only through a C FFI and owns no CUDA allocator.  For them the
-// argmax scratch (the per-row best keys and the CTA arrival counter) lives in the file-scope array below, one copy
-// per device, held by every GPU that loads the library until the process exits.  The caller still provides x, the
-// weights and the outputs.
+// HBM to its KV-cache pool up front (a cudaMalloc then fails or evicts cache pages), or a host runtime that reaches
+// this library only through a C FFI and owns no CUDA allocator of its own.  For them the argmax scratch (the per-row
+// best keys, the CTA arrival counter and the status word) lives in the file-scope array below, one copy per device,
+// held by every GPU that loads the library until the process exits.  The caller still provides x, the weights and
+// the outputs.
 //
 // Limits: at most kNoAllocMaxRows = 8 rows per call (the scratch holds 8 argmax slots; larger requests are refused
-// with FLINT_ERR_SCRATCH).  Every call uses the same scratch: it is cleared at the start of each call, and calls
-// that overlap on the GPU (different streams, or devices sharing nothing but this array's copy per device) race on
-// it, so issue them in one stream per device.  The first call on a device looks up the array's device address
-// (cudaGetSymbolAddress with that device current); make that first call before any stream capture.
+// with FLINT_ERR_SCRATCH).  Every call uses the same scratch and it keeps the last call's contents: each call clears
+// the argmax slots and the counter before its kernel, but not the status word, which stays set until
+// flint_lm_head_noalloc_status clears it.  Calls that overlap on the GPU (different streams on one device) race on
+// the scratch, so issue them in one stream per device.  A call the argument checks refuse enqueues nothing.  The
+// first call on a device looks up the array's device address (cudaGetSymbolAddress with that device current); make
+// that first call before any stream capture.
 // -------------------------------------------------------------------------------------------------------------------
 namespace flint {
 
 constexpr int kNoAllocMaxRows = 8;
+constexpr int kNoAllocMaxDevices = 64;
 static __device__ __align__(256) unsigned char g_head_noalloc_scratch[256];
 static_assert(sizeof(HeadWorkspace) <= sizeof(g_head_noalloc_scratch), "scratch too small for the argmax workspace");
-static void* g_head_noalloc_ptr[64] = {nullptr};
+static std::atomic<void*> g_head_noalloc_ptr[kNoAllocMaxDevices];
 
+// Device address of this device's copy of the scratch array (host code cannot use the symbol itself: on the host it
+// names a stand-in, not device memory).  Racing first calls from several host threads store the same value.
 static void* head_noalloc_scratch() {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (g_head_noalloc_ptr[dev] == nullptr) {
-    void* p = nullptr;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return nullptr;
+  void* p = g_head_noalloc_ptr[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
     if (cudaGetSymbolAddress(&p, g_head_noalloc_scratch) != cudaSuccess) return nullptr;
-    g_head_noalloc_ptr[dev] = p;
+    g_head_noalloc_ptr[dev].store(p, std::memory_order_release);
   }
-  return g_head_noalloc_ptr[dev];
+  return p;
 }
 
 }  // namespace flint
@@ -268,10 +289,25 @@ extern "C" int flint_lm_head_nv4_noalloc(const void* x, int64_t ldx, int64_t M, 
                                          int pdl, void* stream) {
   using namespace flint;
   if (M > kNoAllocMaxRows) return FLINT_ERR_SCRATCH;
+  const int arg_rc = head_check_args(x, ldx, nullptr, nullptr, M, P, S, V, K, logits, ld_logits);
+  if (arg_rc != FLINT_OK) return arg_rc;                 // refused before anything is enqueued
   if (num_sms() <= 0) return FLINT_ERR_DEVICE;
   void* scratch = head_noalloc_scratch();
   if (scratch == nullptr) return FLINT_ERR_DEVICE;
-  if (cudaMemsetAsync(scratch, 0, sizeof(HeadWorkspace), static_cast<cudaStream_t>(stream)) != cudaSuccess)
+  // clear the argmax slots and the arrival counter; the status word (after them) keeps any earlier time-out
+  if (cudaMemsetAsync(scratch, 0, offsetof(HeadWorkspace, status), static_cast<cudaStream_t>(stream)) != cudaSuccess)
     return FLINT_ERR_LAUNCH;
   return flint_lm_head_nv4(x, ldx, M, P, S, gs, V, K, logits, ld_logits, token_ids, scratch, pdl, stream);
+}
+
+extern "C" int flint_lm_head_noalloc_status(uint32_t* status, int clear) {
+  using namespace flint;
+  if (!status) return FLINT_ERR_ARGUMENT;
+  void* scratch = head_noalloc_scratch();
+  if (scratch == nullptr) return FLINT_ERR_DEVICE;
+  uint8_t* word = static_cast<uint8_t*>(scratch) + offsetof(HeadWorkspace, status);
+  // a blocking copy: it waits for the head launches already issued on this device
+  if (cudaMemcpy(status, word, sizeof(uint32_t), cudaMemcpyDeviceToHost) != cudaSuccess) return FLINT_ERR_LAUNCH;
+  if (clear && cudaMemset(word, 0, sizeof(uint32_t)) != cudaSuccess) return FLINT_ERR_LAUNCH;
+  return FLINT_OK;
 }

@@ -146,13 +146,18 @@ int flint_sample_merge(const int32_t* cand_ids, const float* cand_logits, int64_
                        int32_t* kept, int pdl, void* stream);
 /* Allocation-free flint_lm_head_nv4 (no counterpart in the reference: the recipe always runs inside vLLM, which
  * allocates).  For callers that cannot allocate device memory at call time -- an engine that has already given all
- * free HBM to its KV-cache pool, a CUDA-graph capture region, a host runtime that only reaches the library through
- * a C FFI -- the argmax scratch is a fixed 256-byte array inside the library, one per device, kept until the process
- * exits; no workspace argument.  At most 8 rows (M <= 8); larger requests return FLINT_ERR_SCRATCH.  Each call
- * clears the scratch first; calls that overlap on one GPU race on it (use one stream per device).  The first call
- * on a device resolves the scratch address (cudaGetSymbolAddress), so make it before any stream capture. */
+ * free HBM to its KV-cache pool, a host runtime that only reaches the library through a C FFI and has no CUDA
+ * allocator -- the argmax scratch is a fixed 256-byte array inside the library, one per device, kept until the
+ * process exits; no workspace argument.  At most 8 rows (M <= 8); larger requests return FLINT_ERR_SCRATCH, and
+ * every other refused call returns its error code before anything is enqueued.  Each call clears the argmax slots
+ * first but keeps the scratch's status word, read (and cleared) by flint_lm_head_noalloc_status; calls that overlap
+ * on one GPU race on the scratch (use one stream per device).  The first call on a device resolves the scratch
+ * address (cudaGetSymbolAddress), so make it before any stream capture. */
 int flint_lm_head_nv4_noalloc(const void* x, int64_t ldx, int64_t M, const void* P, const void* S, float gs, int64_t V,
                               int64_t K, float* logits, int64_t ld_logits, int32_t* token_ids, int pdl, void* stream);
+/* Status word of the current device's allocation-free head scratch (FLINT_STATUS_* bits, e.g. a bounded wait that
+ * gave up), after the launches already issued on that device (a blocking read); clear != 0 resets it. */
+int flint_lm_head_noalloc_status(uint32_t* status, int clear);
 
 /* ------------------------------------------------------------------------------------------------
  * (1) MoE decode, 1..8 tokens.  Replaces fast/fp4moe_mar.cu (route_kernel 243-303, route_norm_kernel

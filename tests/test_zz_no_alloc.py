@@ -1,8 +1,8 @@
 """The allocation-free LM head (flint_lm_head_nv4_noalloc) against the regular entry point.
 
 Callers that cannot allocate device memory when they call the head -- an engine whose KV-cache pool already owns
-all free HBM, a CUDA-graph capture region, a host runtime reaching the library only through the C ABI -- use this
-entry point: its argmax scratch is a fixed array inside the library instead of a caller-provided workspace.  This
+all free HBM, a host runtime reaching the library only through the C ABI with no CUDA allocator of its own -- use
+this entry point: its argmax scratch is a fixed array inside the library instead of a caller-provided workspace.  This
 file is collected last so that a run stopping at the first failure has run every other test first; it also passes
 on its own in a fresh process.
 """
@@ -48,6 +48,9 @@ def test_noalloc_head_matches_regular_entry_point_twice(fb):
         assert (logits - ref_logits).abs().max().item() <= LOGIT_RTOL * scale
         np.testing.assert_array_equal(tok.cpu().numpy(), ref_tok.cpu().numpy())
         np.testing.assert_array_equal(tok.cpu().numpy(), ref_logits.argmax(dim=1).to(torch.int32).cpu().numpy())
+    status = ctypes.c_uint32(0xFFFFFFFF)
+    assert lib.flint_lm_head_noalloc_status(ctypes.byref(status), 1) == 0
+    assert status.value == 0                                # no bounded wait gave up
 
 
 @needs_cuda
@@ -60,3 +63,28 @@ def test_noalloc_head_refuses_more_rows_than_its_scratch(fb):
     tok = torch.empty((9,), dtype=torch.int32, device="cuda")
     assert _call(lib, lib.flint_lm_head_nv4_noalloc, x, P, S, 1.0, logits, tok) == 7
     assert b"scratch" in lib.flint_error_string(7)
+
+
+@needs_cuda
+def test_noalloc_head_refuses_bad_arguments_before_enqueuing(fb):
+    """Rows < 1, a null input or a misaligned row stride return their error code and leave the scratch alone: a
+    valid call issued before them on the same stream still produces the regular head's tokens."""
+    lib = fb._lib.lib()
+    g = torch.Generator(device="cuda").manual_seed(5)
+    V, K, M = 4096, 2048, 2
+    P = torch.randint(0, 256, (V, K // 2), dtype=torch.uint8, device="cuda", generator=g)
+    S = torch.randint(0x28, 0x47, (V, K // 16), dtype=torch.uint8, device="cuda", generator=g)
+    x = torch.randn((M, K), device="cuda", generator=g).to(torch.bfloat16)
+    logits = torch.empty((M, V), dtype=torch.float32, device="cuda")
+    tok = torch.empty((M,), dtype=torch.int32, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    assert _call(lib, lib.flint_lm_head_nv4_noalloc, x, P, S, 0.004, logits, tok) == 0
+    # M = 0, a null x, an odd row stride: refused (shape, argument, alignment) with nothing enqueued
+    assert lib.flint_lm_head_nv4_noalloc(x.data_ptr(), K, 0, P.data_ptr(), S.data_ptr(), ctypes.c_float(0.004), V, K,
+                                         logits.data_ptr(), V, tok.data_ptr(), 0, st) == 1
+    assert lib.flint_lm_head_nv4_noalloc(None, K, M, P.data_ptr(), S.data_ptr(), ctypes.c_float(0.004), V, K,
+                                         logits.data_ptr(), V, tok.data_ptr(), 0, st) == 6
+    assert lib.flint_lm_head_nv4_noalloc(x.data_ptr(), K + 1, 1, P.data_ptr(), S.data_ptr(), ctypes.c_float(0.004), V,
+                                         K, logits.data_ptr(), V, tok.data_ptr(), 0, st) == 2
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(tok.cpu().numpy(), logits.argmax(dim=1).to(torch.int32).cpu().numpy())
