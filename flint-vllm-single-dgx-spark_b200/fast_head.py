@@ -18,6 +18,8 @@ The reference's inexact ``int2`` mode (coarse INT2 logits + top-C refine) is not
 """
 from __future__ import annotations
 
+import contextlib
+import functools
 import os
 import sys
 
@@ -118,14 +120,9 @@ class FastHead:
 
 
 # ---------------------------------------------------------------------------------------------------------
-# integration hook (reference: fast/fast_head.py:285-312,360-381)
+# vLLM integration: the compute_logits hook (contract of fast/fast_head.py:360-381 and fast/model.py:924-929:
+# fp32 logits [M, org_vocab], or None for the caller's stock path) and its run-time aids.
 # ---------------------------------------------------------------------------------------------------------
-_state = {"head": None, "failed": False, "bypass": 0}
-_cap = {"buf": [], "n": 0, "part": 0}
-_ver = {"n": 0, "rows": 0, "argmax_mis": None, "top20_miss": None, "val_mis": None, "val_cnt": None,
-        "maxdiff": None, "lse_maxdiff": None}
-
-
 def _log(msg):
     print(f"[flint-fast-head] {msg}", file=sys.stderr, flush=True)
 
@@ -135,171 +132,236 @@ def _capturing() -> bool:
     return torch.cuda.is_available() and torch.cuda.is_current_stream_capturing()
 
 
-def _wrap_bypass(cls, name):
-    """Make cls.name run with the fast head bypassed (compute_logits returns None inside it); idempotent."""
-    orig = getattr(cls, name, None)
-    if orig is None or getattr(orig, "_flint_bypass", False):
-        return
+class _Hook:
+    """What the hook knows about the model's head: the built FastHead, the vocabulary width it returns, whether
+    building failed for good, and how many stock-path regions are open (compute_logits declines inside them)."""
 
-    def bypassed(*args, **kwargs):
-        _state["bypass"] += 1
+    def __init__(self):
+        self.head: FastHead | None = None
+        self.org_vocab = 0
+        self.failed = False
+        self.stock_depth = 0
+
+    @contextlib.contextmanager
+    def stock_path(self):
+        """Inside this block compute_logits returns None, so the caller computes its own (stock) logits."""
+        self.stock_depth += 1
         try:
-            return orig(*args, **kwargs)
+            yield
         finally:
-            _state["bypass"] -= 1
-    bypassed._flint_bypass = True
-    bypassed.__wrapped__ = orig
-    setattr(cls, name, bypassed)
+            self.stock_depth -= 1
+
+
+_hook = _Hook()
+
+# vLLM methods that compute prompt logprobs through compute_logits (module, class, methods): their logits must be
+# the stock ones (fast/fast_head.py:235-268 names the same three)
+_PROMPT_LOGPROB_METHODS = (
+    ("vllm.v1.worker.gpu.sample.prompt_logprob", "PromptLogprobsWorker",
+     ("compute_prompt_logprobs", "compute_prompt_token_id_logprobs")),
+    ("vllm.v1.worker.gpu_model_runner", "GPUModelRunner", ("_get_prompt_logprobs_dict",)),
+)
+
+
+def _on_stock_path(fn):
+    """fn, run inside _hook.stock_path(); marks the wrapper so wrapping twice is a no-op."""
+    if getattr(fn, "_flint_stock_path", False):
+        return fn
+
+    @functools.wraps(fn)
+    def run(*args, **kwargs):
+        with _hook.stock_path():
+            return fn(*args, **kwargs)
+    run._flint_stock_path = True
+    return run
 
 
 def install_guards() -> int:
-    """Prompt logprobs are computed from compute_logits on prompt rows: keep those calls on the stock path.  Wraps
-    the prompt-logprob methods of vLLM's model runners that exist in the installed vLLM; returns how many."""
-    n = 0
-    targets = (("vllm.v1.worker.gpu.sample.prompt_logprob", "PromptLogprobsWorker",
-                ("compute_prompt_logprobs", "compute_prompt_token_id_logprobs")),
-               ("vllm.v1.worker.gpu_model_runner", "GPUModelRunner", ("_get_prompt_logprobs_dict",)))
-    for module, cls_name, methods in targets:
+    """Route vLLM's prompt-logprob computations to the stock head (they must see the stock logits).  Methods of
+    runners absent from the installed vLLM are skipped.  Returns the number of guarded methods."""
+    import importlib
+    guarded = 0
+    for module, cls_name, methods in _PROMPT_LOGPROB_METHODS:
         try:
-            import importlib
             cls = getattr(importlib.import_module(module), cls_name)
         except Exception as e:                         # this vLLM has no such runner: nothing to guard
             _log(f"{module}.{cls_name} guard not installed: {type(e).__name__}: {e}")
             continue
-        for m in methods:
-            if getattr(cls, m, None) is not None:
-                _wrap_bypass(cls, m)
-                n += 1
-    _log(f"prompt-logprob guards installed: {n}")
-    return n
+        for name in methods:
+            fn = getattr(cls, name, None)
+            if fn is not None:
+                setattr(cls, name, _on_stock_path(fn))
+                guarded += 1
+    _log(f"prompt-logprob guards installed: {guarded}")
+    return guarded
 
 
-def _flush_capture(model, label):
-    """Write the collected hidden rows (and once, the head they go through) under CAPTURE_DIR."""
-    if not _cap["buf"]:
-        return
-    h = torch.cat(_cap["buf"], 0).cpu()
-    path = os.path.join(CAPTURE_DIR, f"part{_cap['part']:03d}_{label}.pt")
-    torch.save({"hidden": h, "label": label}, path)
-    head_path = os.path.join(CAPTURE_DIR, "head.pt")
-    if not os.path.exists(head_path):
-        lm, lp = model.lm_head, getattr(model, "logits_processor", None)
-        head = {k: getattr(lm, k).data.cpu() for k in ("weight", "weight_scale", "weight_scale_2")
-                if isinstance(getattr(lm, k, None), torch.Tensor)}
-        head["scale"] = float(getattr(lp, "scale", 1.0) if lp is not None else 1.0)
-        torch.save(head, head_path)
-    _log(f"captured {h.shape[0]} hidden rows -> {path}")
-    _cap.update(buf=[], n=0, part=_cap["part"] + 1)
+class VerifyStats:
+    """FLINT_FAST_HEAD_VERIFY: agreement of the fast logits with the stock path's on the same rows, accumulated over
+    calls and logged every `every` calls.  Fields: rows, argmax mismatches, stock top-20 ids that the fast head left
+    at -inf, differing finite values / finite values, max |fast - stock|, max |logsumexp difference|."""
+
+    SUMS = ("argmax_mis", "top20_miss", "val_mis", "val_cnt")
+    MAXES = ("maxdiff", "lse_maxdiff")
+
+    def __init__(self, every: int = 400):
+        self.every, self.calls, self.rows = every, 0, 0
+        self.acc: dict[str, torch.Tensor] = {}
+
+    def update(self, stock: torch.Tensor, fast: torch.Tensor):
+        stock = stock.float()
+        fast = fast[:, :stock.shape[1]].float()           # the fast head may return padded vocabulary columns
+        finite = ~torch.isneginf(fast)                   # entries the fast head did not mask out
+        diff = torch.where(finite, (fast - stock).abs(), torch.zeros_like(fast))
+        top = stock.topk(min(20, stock.shape[1]), dim=-1).indices
+        now = {"argmax_mis": (stock.argmax(-1) != fast.argmax(-1)).sum(),
+               "top20_miss": torch.isneginf(fast.gather(1, top)).sum(),
+               "val_mis": ((diff != 0) & finite).sum(), "val_cnt": finite.sum(),
+               "maxdiff": diff.max(),
+               "lse_maxdiff": (torch.logsumexp(stock, -1) - torch.logsumexp(fast, -1)).abs().max()}
+        for k, v in now.items():                          # device tensors: no sync per call
+            old = self.acc.get(k)
+            self.acc[k] = v if old is None else (old + v if k in self.SUMS else torch.maximum(old, v))
+        self.calls += 1
+        self.rows += stock.shape[0]
+        if self.calls % self.every == 0:
+            _log(self.line())
+
+    def line(self) -> str:
+        a = {k: (float(v) if k in self.MAXES else int(v)) for k, v in self.acc.items()}
+        return ("VERIFY rows=%d argmax_mismatch=%d top20_missing=%d value_mismatches=%d/%d max|fast-stock|=%.4g "
+                "max|lse_stock-lse_fast|=%.4g" % (self.rows, a["argmax_mis"], a["top20_miss"], a["val_mis"],
+                                                  a["val_cnt"], a["maxdiff"], a["lse_maxdiff"]))
 
 
-def _capture(model, x):
-    """Keep a copy of the hidden rows; a FLUSH file in CAPTURE_DIR (its text = the label) writes the earlier ones."""
-    flag = os.path.join(CAPTURE_DIR, "FLUSH")
-    if os.path.exists(flag):
-        with open(flag) as f:
-            label = f.read().strip() or "x"
-        os.remove(flag)
-        _flush_capture(model, label)
-    _cap["buf"].append(x.detach().clone())
-    _cap["n"] += x.shape[0]
+class HiddenCapture:
+    """FLINT_HEAD_CAPTURE_DIR: keeps a copy of every hidden row the head sees; when a file named FLUSH appears in the
+    directory, the rows kept so far are written as part<NNN>_<label>.pt (label = the file's text) and, the first
+    time, the head's own tensors as head.pt (the offline replay of fast/fast_head.py:313-334)."""
+
+    def __init__(self, directory: str):
+        self.dir, self.rows, self.parts = directory, [], 0
+
+    @property
+    def pending(self) -> int:
+        return sum(r.shape[0] for r in self.rows)
+
+    def add(self, model, x: torch.Tensor):
+        flag = os.path.join(self.dir, "FLUSH")
+        if os.path.exists(flag):
+            with open(flag) as f:
+                label = f.read().strip() or "x"
+            os.remove(flag)
+            self.write(model, label)
+        self.rows.append(x.detach().clone())
+
+    def write(self, model, label: str):
+        if not self.rows:
+            return
+        hidden = torch.cat(self.rows, 0).cpu()
+        path = os.path.join(self.dir, f"part{self.parts:03d}_{label}.pt")
+        torch.save({"hidden": hidden, "label": label}, path)
+        head_path = os.path.join(self.dir, "head.pt")
+        if not os.path.exists(head_path):
+            torch.save(_head_tensors(model), head_path)
+        _log(f"captured {hidden.shape[0]} hidden rows -> {path}")
+        self.rows, self.parts = [], self.parts + 1
 
 
-def _verify(model, x, fast_out):
-    """Accumulate the agreement of the fast logits with the stock path's on the same rows; log every 400 calls."""
-    stock = model.logits_processor(model.lm_head, x).float()
-    fast = fast_out[:, :stock.shape[1]].float()
-    finite = fast > float("-inf")
-    diff = (fast - stock).abs().masked_fill(~finite, 0.0)
-    stats = dict(argmax_mis=(stock.argmax(-1) != fast.argmax(-1)).sum(),
-                 top20_miss=(fast.gather(1, stock.topk(min(20, stock.shape[1]), dim=-1).indices)
-                             == float("-inf")).sum(),
-                 val_mis=((diff != 0) & finite).sum(), val_cnt=finite.sum(), maxdiff=diff.max(),
-                 lse_maxdiff=(torch.logsumexp(stock, -1) - torch.logsumexp(fast, -1)).abs().max())
-    for k, v in stats.items():
-        prev = _ver[k]
-        _ver[k] = v if prev is None else (torch.maximum(prev, v) if k in ("maxdiff", "lse_maxdiff") else prev + v)
-    _ver["rows"] += x.shape[0]
-    _ver["n"] += 1
-    if _ver["n"] % 400 == 0:
-        _log("VERIFY rows=%d argmax_mismatch=%d top20_missing=%d value_mismatches=%d/%d max|fast-stock|=%.4g "
-             "max|lse_stock-lse_fast|=%.4g" % (_ver["rows"], int(_ver["argmax_mis"]), int(_ver["top20_miss"]),
-                                                int(_ver["val_mis"]), int(_ver["val_cnt"]), float(_ver["maxdiff"]),
-                                                float(_ver["lse_maxdiff"])))
+def _logits_scale(model) -> float:
+    lp = getattr(model, "logits_processor", None)
+    return float(getattr(lp, "scale", 1.0)) if lp is not None else 1.0
+
+
+def _head_tensors(model) -> dict:
+    lm = model.lm_head
+    out = {k: getattr(lm, k).data.cpu() for k in ("weight", "weight_scale", "weight_scale_2")
+           if isinstance(getattr(lm, k, None), torch.Tensor)}
+    out["scale"] = _logits_scale(model)
+    return out
+
+
+_verify_stats = VerifyStats()
+_capture = HiddenCapture(CAPTURE_DIR) if CAPTURE_DIR else None
 
 
 def _nv4_from_gguf(model, W):
-    """The head's native NVFP4 tensors straight from the checkpoint (``model.gguf_path``, tensor ``output.weight``),
-    repacked on the GPU and checked bit-exact against the bf16 weight the stock loader produced (``e2m1 * e4m3``,
-    the dequantised head); None on a mismatch (reference: fast/fast_head.py:271-282)."""
+    """The head's NVFP4 codes and scales from the checkpoint (``model.gguf_path``, tensor ``output.weight``),
+    repacked on the GPU; accepted only if they dequantise bit for bit to W, the bf16 head the stock loader made
+    (reference: fast/fast_head.py:271-282).  -> (P, S) or None."""
     import gguf
-    from .gguf_nvfp4 import _as_tensor, _repack_nvfp4, dequantize_nvfp4
-    reader = gguf.GGUFReader(model.gguf_path)
-    t = {x.name: x for x in reader.tensors}["output.weight"]
-    P, S = _repack_nvfp4(_as_tensor(t.data).to(W.device), int(t.shape[0]))
-    ok = tuple(P.shape) == (W.shape[0], W.shape[1] // 2)
-    for a in range(0, W.shape[0] if ok else 0, 8192):
-        ok &= bool(torch.equal(dequantize_nvfp4(P[a:a + 8192], S[a:a + 8192], out_dtype=torch.bfloat16),
-                               W[a:a + 8192]))
-    return (P.contiguous(), S.contiguous()) if ok else None
+    from .gguf_nvfp4 import _host_tensor, _repack_nvfp4, dequantize_nvfp4
+    found = [t for t in gguf.GGUFReader(model.gguf_path).tensors if t.name == "output.weight"]
+    if not found:
+        return None
+    P, S = _repack_nvfp4(_host_tensor(found[0].data).to(W.device), int(found[0].shape[0]))
+    if tuple(P.shape) != (W.shape[0], W.shape[1] // 2):
+        return None
+    rows = 8192                                         # bounded temporary: one bf16 slab at a time
+    same = all(torch.equal(dequantize_nvfp4(P[a:a + rows], S[a:a + rows], out_dtype=torch.bfloat16), W[a:a + rows])
+               for a in range(0, W.shape[0], rows))
+    return (P.contiguous(), S.contiguous()) if same else None
+
+
+def _head_source(model):
+    """-> (FastHead, org_vocab) or None.  Two heads are understood: (1) ModelOpt tensors on ``model.lm_head``
+    (``weight`` u8 codes, ``weight_scale`` E4M3, ``weight_scale_2`` fp32); (2) the reference's layout, a bf16
+    ``lm_head.weight`` equal to the dequantised head with ``model.gguf_path`` naming the GGUF to take the NVFP4
+    tensors from.  ``model.logits_processor.scale`` (default 1) multiplies the logits; its ``org_vocab_size`` (default
+    the head's rows) is the width returned."""
+    lm = model.lm_head
+    W = getattr(lm, "weight", None)
+    if W is None or W.dim() != 2 or getattr(lm, "tp_size", 1) != 1:
+        return None
+    lp = getattr(model, "logits_processor", None)
+    org_vocab = int(getattr(lp, "org_vocab_size", W.shape[0]) if lp is not None else W.shape[0])
+    scale = _logits_scale(model)
+    if W.dtype == torch.uint8:
+        S, gs = getattr(lm, "weight_scale", None), getattr(lm, "weight_scale_2", None)
+        if S is None or gs is None or S.shape[0] != W.shape[0]:
+            return None
+        return FastHead(None, _scale_value(gs) * scale, "nv4", (W, S)), org_vocab
+    if W.dtype == torch.bfloat16 and getattr(model, "gguf_path", None):
+        try:
+            nv4 = _nv4_from_gguf(model, W.data)
+        except Exception as e:
+            _log(f"nv4 repack failed: {type(e).__name__}: {e}")
+            nv4 = None
+        if nv4 is None:
+            _log("nv4 head unavailable (repack mismatch or failure)")
+            return None
+        return FastHead(W.data, scale, "nv4", nv4), org_vocab
+    return None
 
 
 def _build(model):
-    """Two ways in.  (1) The model exposes its NVFP4 head as ``model.lm_head.{weight (u8), weight_scale (E4M3),
-    weight_scale_2}``.  (2) The reference's: ``model.lm_head.weight`` is the bf16 dequantised head (``e2m1 * e4m3``)
-    with its global scale in ``model.logits_processor.scale``, and ``model.gguf_path`` names the checkpoint the
-    NVFP4 tensors are repacked from (checked bit-exact against the bf16 weight).  An optional
-    ``model.logits_processor.scale`` (fp32) multiplies the logits."""
-    lm = model.lm_head
-    P = getattr(lm, "weight", None)
-    lp = getattr(model, "logits_processor", None)
-    if (P is not None and P.dtype == torch.bfloat16 and P.dim() == 2 and getattr(lm, "tp_size", 1) == 1
-            and getattr(model, "gguf_path", None)):
-        nv4 = None
-        try:
-            nv4 = _nv4_from_gguf(model, P.data)
-        except Exception as e:
-            _log(f"nv4 repack failed: {type(e).__name__}: {e}")
-        if nv4 is None:
-            _log("nv4 head unavailable (repack mismatch/failure) -> fast head disabled")
-            _state["failed"] = True
-            return
-        scale = float(getattr(lp, "scale", 1.0) if lp is not None else 1.0)
-        _state["head"] = FastHead(P.data, scale, "nv4", nv4)
-        _state["org_vocab"] = int(getattr(lp, "org_vocab_size", P.shape[0]) if lp is not None else P.shape[0])
-        return
-    S = getattr(lm, "weight_scale", None)
-    gs = getattr(lm, "weight_scale_2", None)
-    ok = (P is not None and S is not None and gs is not None and P.dtype == torch.uint8 and P.dim() == 2
-          and S.shape[0] == P.shape[0] and getattr(lm, "tp_size", 1) == 1)
-    if not ok:
+    built = _head_source(model)
+    if built is None:
         _log("fast head disabled: unsupported lm_head")
-        _state["failed"] = True
+        _hook.failed = True
         return
-    scale = _scale_value(gs) * float(getattr(lp, "scale", 1.0) if lp is not None else 1.0)
-    _state["head"] = FastHead(None, scale, "nv4", (P, S))
-    _state["org_vocab"] = int(getattr(lp, "org_vocab_size", P.shape[0]) if lp is not None else P.shape[0])
+    _hook.head, _hook.org_vocab = built
 
 
 def compute_logits(model, hidden_states):
-    """Returns logits (fp32, [M, org_vocab]) or None to let the caller use the stock path."""
-    if _state["bypass"] > 0:
+    """The fast head's fp32 logits [M, org_vocab] for the hidden rows, or None when the caller should compute them
+    on its stock path (disabled, too many rows, inside a prompt-logprob call, head not usable, or the first call
+    falls inside a graph capture, where the head is not built)."""
+    if _hook.stock_depth > 0 or not 1 <= hidden_states.shape[0] <= MAX_M:
         return None
-    m = hidden_states.shape[0]
-    if m < 1 or m > MAX_M:
+    if _capture is not None and not _capturing():
+        _capture.add(model, hidden_states)
+    if not ENABLED or _hook.failed:
         return None
-    if CAPTURE_DIR and not _capturing():
-        _capture(model, hidden_states)
-    if not ENABLED or _state["failed"]:
-        return None
-    if _state["head"] is None:
+    if _hook.head is None:
         if _capturing():
             return None
         _build(model)
-        if _state["head"] is None:
+        if _hook.head is None:
             return None
-    out = _state["head"](hidden_states)[:, :_state["org_vocab"]]
+    out = _hook.head(hidden_states)[:, :_hook.org_vocab]
     if VERIFY and not _capturing():
-        _verify(model, hidden_states, out)
+        _verify_stats.update(model.logits_processor(model.lm_head, hidden_states), out)
     return out
 
 

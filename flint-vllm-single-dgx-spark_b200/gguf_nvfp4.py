@@ -22,7 +22,6 @@ from __future__ import annotations
 
 import glob
 import os
-import re
 import warnings
 from collections.abc import Iterator
 
@@ -62,7 +61,6 @@ _GLOBAL_NAMES = {
     "output_norm.weight": "model.norm.weight",
     "output": "lm_head",
 }
-_LAYER_RE = re.compile(r"blk\.(\d+)\.(.+)")
 
 _E2M1_POS = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0)
 _E2M1 = _E2M1_POS + tuple(-v for v in _E2M1_POS)
@@ -127,27 +125,63 @@ def dequantize_nvfp4(weight: torch.Tensor, weight_scale: torch.Tensor, global_sc
     return out if direct else out.to(out_dtype)
 
 
-def _as_tensor(data: np.ndarray) -> torch.Tensor:
-    # the reader memory-maps the file read-only; the tensors are only read
+def _host_tensor(array) -> torch.Tensor:
+    """Zero-copy torch view of a tensor's bytes inside the memory-mapped GGUF file.  The mapping is read-only; the
+    loader only reads through the view (NVFP4 bytes are copied to the device, other tensors are handed out as they
+    are), so torch's warning about a non-writable array is filtered here."""
+    arr = np.asarray(array)
     with warnings.catch_warnings():
-        warnings.simplefilter("ignore", UserWarning)
-        return torch.from_numpy(np.asarray(data))
+        warnings.filterwarnings("ignore", message=".*not writable.*", category=UserWarning)
+        return torch.from_numpy(arr)
+
+
+_as_tensor = _host_tensor       # the PR module's name for it (fast/fast_head.py imports it under that name)
 
 
 def _map_name(name: str) -> tuple[str, bool]:
-    """GGUF tensor base name -> (HF base name, is_stacked_experts); ``ValueError`` for a name Flint does not have."""
+    """GGUF tensor base name -> (HF base name, is_stacked_experts); ``ValueError`` for a name Flint does not have.
+    Stacked expert names come back with a ``{}`` placeholder for the expert index."""
     if name in _GLOBAL_NAMES:
         return _GLOBAL_NAMES[name], False
-    m = _LAYER_RE.fullmatch(name)
-    if m is None:
-        raise ValueError(f"Unexpected tensor in Flint GGUF: {name}")
-    prefix = f"model.layers.{m.group(1)}."
-    rest = m.group(2)
-    if rest in _EXPERT_NAMES:
-        return prefix + "mlp.experts.{}." + _EXPERT_NAMES[rest], True
-    if rest not in _LAYER_NAMES:
-        raise ValueError(f"Unexpected tensor in Flint GGUF: {name}")
-    return prefix + _LAYER_NAMES[rest], False
+    blk, layer, key = (name.split(".", 2) + ["", ""])[:3]
+    if blk == "blk" and layer.isdigit():
+        prefix = f"model.layers.{layer}."
+        if key in _EXPERT_NAMES:
+            return f"{prefix}mlp.experts.{{}}.{_EXPERT_NAMES[key]}", True
+        if key in _LAYER_NAMES:
+            return prefix + _LAYER_NAMES[key], False
+    raise ValueError(f"Unexpected tensor in Flint GGUF: {name}")
+
+
+def _reader(path: str):
+    try:
+        import gguf
+    except ImportError as err:
+        raise ImportError("Loading Flint NVFP4 GGUF checkpoints requires the `gguf` package (>= 0.19.0).") from err
+    reader = gguf.GGUFReader(path)
+    a4 = reader.fields.get("general.tensor_extra.prec_a4")
+    if a4 is not None and any(a4.contents()):
+        raise ValueError("GGUF marks tensors with FP4 activations (prec_a4); only weight-only NVFP4 (W4A16) is "
+                         "supported.")
+    return gguf, reader
+
+
+def _nvfp4_entries(t, scale_tensor, device, dequantize) -> list[tuple[str, torch.Tensor]]:
+    """The HF entries of one NVFP4 GGUF tensor: its codes repacked on the device, then either the three ModelOpt
+    tensors (per expert for stacked expert tensors) or, for names in ``dequantize``, a bf16 weight + global scale."""
+    base = t.name.removesuffix(".weight")
+    hf, stacked = _map_name(base)
+    codes, scales = _repack_nvfp4(_host_tensor(t.data).to(device), int(t.shape[0]))   # shape[0]: innermost dim
+    gscale = _host_tensor(scale_tensor.data)
+    if hf in dequantize:
+        return [(hf + ".weight", dequantize_nvfp4(codes, scales, out_dtype=torch.bfloat16)),
+                (hf + ".weight_scale_2", gscale.reshape(()))]
+    if stacked:
+        parts = [(hf.format(e), codes[e], scales[e], gscale[e]) for e in range(codes.shape[0])]
+    else:
+        parts = [(hf, codes, scales, gscale.reshape(()))]
+    return [(name + suffix, value) for name, c, s, g in parts
+            for suffix, value in ((".weight", c), (".weight_scale", s), (".weight_scale_2", g))]
 
 
 def gguf_nvfp4_weights_iterator(path: str, device: torch.device | str = "cuda",
@@ -157,46 +191,18 @@ def gguf_nvfp4_weights_iterator(path: str, device: torch.device | str = "cuda",
     BF16 ``.weight`` holding ``e2m1 * e4m3`` plus the F32 ``.weight_scale_2`` the caller applies to the fp32 output.
     F32 / BF16 tensors pass through unchanged (host memory-mapped).  Raises ``ValueError`` for FP4-activation
     checkpoints (prec_a4), unknown tensor names and other tensor types."""
-    try:
-        import gguf
-    except ImportError as err:
-        raise ImportError("Loading Flint NVFP4 GGUF checkpoints requires the `gguf` package (>= 0.19.0).") from err
-
-    reader = gguf.GGUFReader(path)
-    prec_a4 = reader.fields.get("general.tensor_extra.prec_a4")
-    if prec_a4 is not None and any(prec_a4.contents()):
-        raise ValueError("GGUF marks tensors with FP4 activations (prec_a4); only weight-only NVFP4 (W4A16) is "
-                         "supported.")
-    tensors = {t.name: t for t in reader.tensors}
-    for name, t in tensors.items():
-        if name.endswith(".scale"):
-            continue                                   # consumed with its NVFP4 tensor
-        data = _as_tensor(t.data)
-        if t.tensor_type != _GGUF_NVFP4:
-            hf_name, _ = _map_name(name)
-            if t.tensor_type == gguf.GGMLQuantizationType.BF16:
-                data = data.view(torch.bfloat16)
-            elif t.tensor_type != gguf.GGMLQuantizationType.F32:
-                raise ValueError(f"Unsupported GGUF tensor type for {name}: {t.tensor_type}")
-            yield hf_name, data
+    gguf, reader = _reader(path)
+    qt = gguf.GGMLQuantizationType
+    as_plain = {qt.F32: lambda v: v, qt.BF16: lambda v: v.view(torch.bfloat16)}
+    by_name = {t.name: t for t in reader.tensors}
+    for t in reader.tensors:
+        if t.name.endswith(".scale"):
+            continue                                   # an NVFP4 tensor's global scale: emitted with that tensor
+        if t.tensor_type == _GGUF_NVFP4:
+            yield from _nvfp4_entries(t, by_name[t.name.removesuffix(".weight") + ".scale"], device, dequantize)
             continue
-
-        base = name.removesuffix(".weight")
-        hf_base, stacked = _map_name(base)
-        n_cols = int(t.shape[0])                       # GGUF lists the innermost dimension first
-        weight, weight_scale = _repack_nvfp4(data.to(device), n_cols)
-        global_scale = _as_tensor(tensors[base + ".scale"].data)
-        if hf_base in dequantize:
-            yield hf_base + ".weight", dequantize_nvfp4(weight, weight_scale, out_dtype=torch.bfloat16)
-            yield hf_base + ".weight_scale_2", global_scale.reshape(())
-            continue
-        if not stacked:
-            yield hf_base + ".weight", weight
-            yield hf_base + ".weight_scale", weight_scale
-            yield hf_base + ".weight_scale_2", global_scale.reshape(())
-            continue
-        for e in range(weight.shape[0]):
-            expert = hf_base.format(e)
-            yield expert + ".weight", weight[e]
-            yield expert + ".weight_scale", weight_scale[e]
-            yield expert + ".weight_scale_2", global_scale[e]
+        hf, _ = _map_name(t.name)
+        convert = as_plain.get(t.tensor_type)
+        if convert is None:
+            raise ValueError(f"Unsupported GGUF tensor type for {t.name}: {t.tensor_type}")
+        yield hf, convert(_host_tensor(t.data))

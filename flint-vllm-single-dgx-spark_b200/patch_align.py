@@ -28,8 +28,11 @@ def align_sizes(numel: int, num_experts: int, block_size: int, pad_sorted_ids: b
 
 
 def _deterministic_align(topk_ids, num_experts, block_size, sorted_ids, expert_ids, num_tokens_post_pad):
-    """Same outputs as the CUDA moe_align_block_size except the order of routes inside an expert is ascending
-    (route index) instead of atomicAdd-arrival order.  Writes the three output buffers in place; sync-free."""
+    """Fills sorted_ids, expert_ids and num_tokens_post_pad in place with one kernel launch (no host sync).
+
+    The buffers follow vLLM's moe_align_block_size contract; the one difference is the placement of an expert's
+    routes inside its padded span, which is by increasing flat route index here rather than by the order in which
+    atomics happened to land, so every run produces identical buffers (fast/patch_align.py:11-30)."""
     torch.ops.flint_b200.moe_align(topk_ids, int(num_experts), int(block_size), sorted_ids, expert_ids,
                                    num_tokens_post_pad)
 

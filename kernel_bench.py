@@ -1,6 +1,6 @@
 """Per-kernel microbenchmark of the decode step (CUDA events on the launch stream, no profiler).
 
-    python flint-vllm-single-dgx-spark_b200/kernel_bench.py --kernel attention [--ctx 6057] [--layers 4] [--reps 5]
+    python kernel_bench.py --kernel attention [--ctx 6057] [--layers 4] [--reps 5]
         [--batch 1] [--moe chain|fused]
 
 A synthetic Flint-class model with --layers layers (a few GB on the device) is built, its KV cache filled with seeded
@@ -11,7 +11,7 @@ those of Decoder.layer_ops (attn_block, or qkv / attention / o with --attn chain
 plus head and head_sample.  This is
 also the small case used for full ncu captures of one kernel.
 
-    python flint-vllm-single-dgx-spark_b200/kernel_bench.py --kernel gguf_repack|nvfp4_dequant [--rows 151552]
+    python kernel_bench.py --kernel gguf_repack|nvfp4_dequant [--rows 151552]
         [--cols 2048] [--reps 20]
 
 times the checkpoint-format kernels on one tensor of --rows x --cols values (default: the LM head, 174.6 MB of GGUF
@@ -28,14 +28,15 @@ import sys
 import numpy as np
 import torch
 
-HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(ROOT, "flint-vllm-single-dgx-spark_b200")
 
 
 def _package():
     if "flint_b200" in sys.modules:
         return sys.modules["flint_b200"]
-    spec = importlib.util.spec_from_file_location("flint_b200", os.path.join(HERE, "__init__.py"),
-                                                  submodule_search_locations=[HERE])
+    spec = importlib.util.spec_from_file_location("flint_b200", os.path.join(PKG_DIR, "__init__.py"),
+                                                  submodule_search_locations=[PKG_DIR])
     mod = importlib.util.module_from_spec(spec)
     sys.modules["flint_b200"] = mod
     spec.loader.exec_module(mod)
@@ -115,7 +116,7 @@ def time_format_kernel(args):
     3 warm-ups (the tensor is larger than L2, so back-to-back launches do not hit in it); the CPU oracle
     on 4096 rows of the same tensor, scaled per byte."""
     import time
-    sys.path.insert(0, os.path.dirname(HERE))
+    sys.path.insert(0, ROOT)
     from oracle import nvfp4 as onv
     dev = torch.device("cuda", torch.cuda.current_device())
     ops = torch.ops.flint_b200
@@ -161,7 +162,7 @@ def time_format_kernel(args):
         onv.bf16_bits(onv.dequantize_nvfp4(Po, So))
     cpu_s = (time.perf_counter() - t0) * R / rows
     peak = None
-    peaks = os.path.join(os.path.dirname(HERE), "MEASURED_PEAKS.json")
+    peaks = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(peaks):
         peak = json.load(open(peaks)).get("hbm_gbs")
     gbps = nbytes / us / 1e3

@@ -21,7 +21,7 @@ def deterministic_align(topk_ids: np.ndarray, num_experts: int, block_size: int,
                         n_sorted: int | None = None, n_blocks: int | None = None):
     """-> (sorted_ids i32 [n_sorted], expert_ids i32 [n_blocks], num_tokens_post_pad i32 [1]).
 
-    fast/patch_align.py:179-193 step by step: counts = bincount(ids);
+    fast/patch_align.py:11-30 step by step: counts = bincount(ids);
     padded = ceil(count/B)*B; pad_end = cumsum; routes of each expert placed
     in ascending route index at pad_start[e] + rank; unused slots = numel;
     expert_ids[blk] = searchsorted(pad_end, blk*B, right) or -1 past the last

@@ -4,7 +4,9 @@ Restates, with the rounding points of the reference's dequantise-to-fp32 path (p
 patch:4937-4952, GB10 kernels fast/fp4moe_mar.cu:267,341-366):
   s = x + res (fp32); res_out = bf16(s); xn = bf16(s * rsqrt(mean(s^2) + eps) * w)
   logit[e] = bf16(xn . Wr[e])                                    (fp32 dot)
-  top-k on the bf16 logits, ties -> lowest expert index; weights softmax or sigmoid, renormalised
+  top-k on the bf16 logits, ties -> lowest expert index; weights softmax or sigmoid, renormalised and kept in fp32
+  (tw = val / sum, the GB10 kernel's rule, fast/fp4moe_mar.cu:297-301; the PR's SM100 decode instead rounds tw to
+  bf16, patch:3049-3050 -- this library and this oracle keep the fp32 weights)
   g, u = xn . W13[e] * gs13[e]; act = bf16(silu(g) * u)           (fp32)
   y_e = bf16(act . W2[e] * gs2[e]); out = bf16(sum_slot tw * y_e)  (fp32, slot order)
 ``router_logits_mirror`` reproduces the GPU router's exact fp32 summation order (lane-strided chains over
@@ -51,7 +53,7 @@ def topk_route(logits: np.ndarray, topk: int, score_fn: int):
     """-> (ids int32 [M, k], weights fp32 [M, k]); score_fn 0 = softmax (select on logits), 1 = sigmoid."""
     lg = logits.astype(np.float32)
     # selection on the bf16 logits for both score functions (sigmoid is monotone), ties -> lowest expert
-    # (the SM100 rule, patch:3015-3050)
+    # (patch:3015-3048 and fast/fp4moe_mar.cu:286-290); weights stay fp32 (fast/fp4moe_mar.cu:301)
     order = np.lexsort((np.broadcast_to(np.arange(lg.shape[-1]), lg.shape), -lg), axis=-1)
     ids = order[:, :topk].astype(np.int32)
     if score_fn == 1:

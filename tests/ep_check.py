@@ -1,6 +1,6 @@
 """Expert-parallel + vocabulary-sharded decode check, one process per GPU:
 
-    torchrun --nproc-per-node N --master-addr 127.0.0.1 flint-vllm-single-dgx-spark_b200/ep_check.py [--layers 4]
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 tests/ep_check.py [--layers 4]
 
 Every rank builds the same small synthetic Flint-class model and keeps its shard (experts and head rows), then the
 ranks decode prompts together in several modes: one stream through the one-launch MoE block with the in-kernel
@@ -25,14 +25,15 @@ import numpy as np
 import torch
 import torch.distributed as dist
 
-HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PKG_DIR = os.path.join(ROOT, "flint-vllm-single-dgx-spark_b200")
 
 
 def _package():
     if "flint_b200" in sys.modules:
         return sys.modules["flint_b200"]
-    spec = importlib.util.spec_from_file_location("flint_b200", os.path.join(HERE, "__init__.py"),
-                                                  submodule_search_locations=[HERE])
+    spec = importlib.util.spec_from_file_location("flint_b200", os.path.join(PKG_DIR, "__init__.py"),
+                                                  submodule_search_locations=[PKG_DIR])
     mod = importlib.util.module_from_spec(spec)
     sys.modules["flint_b200"] = mod
     spec.loader.exec_module(mod)

@@ -18,7 +18,7 @@ def test_sharded_decode_matches_single_gpu():
         pytest.skip("needs 2 GPUs")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2", "--master-addr",
-           "127.0.0.1", "--master-port", "29533", os.path.join(ROOT, "flint-vllm-single-dgx-spark_b200", "ep_check.py"),
+           "127.0.0.1", "--master-port", "29533", os.path.join(ROOT, "tests", "ep_check.py"),
            "--layers", "4", "--tokens", "16"]
     r = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env, cwd=ROOT)
     lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
