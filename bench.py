@@ -231,7 +231,7 @@ def run_ours(args):
         workload = (f"BASELINE configs[4]: full Flint-class synthetic model, {M} concurrent stream(s), "
                     f"{'seeded sampled' if args.sample else 'greedy'} decode")
     else:
-        metric = "c1 decode tok/s, Flint-class NVFP4 MoE (greedy, 800 tokens after a 6057-token prompt)"
+        metric = f"c1 decode tok/s, Flint-class NVFP4 MoE (greedy, {steps} timed tokens after a {plen}-token prompt)"
         workload = "BASELINE configs[3]: full Flint-class synthetic model, 1 stream, greedy decode"
     if rank == 0:
         cpu = None
@@ -302,7 +302,8 @@ def run_reference(args):
                                 warmup=warm)
     line = {
         "impl": "reference",
-        "metric": "c1 decode tok/s, Flint-class NVFP4 MoE (greedy, 800 tokens after a 6057-token prompt)",
+        "metric": f"c1 decode tok/s, Flint-class NVFP4 MoE (greedy, {args.steps} timed tokens after a {args.prompt}-token "
+                  "prompt)",
         "value": res["value"], "unit": "tok/s", "n_gpus": args.gpus, "steps": res["tokens"], "warmup": warm,
         "ms_per_step": round(1e3 / res["value"], 2) if res["value"] else None, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp32 (weights dequantised from NVFP4 per call)",

@@ -29,7 +29,8 @@ import torch
 from . import _lib
 from . import ops as _ops
 from .fp4moe_decode import DecodeWeights
-from .nvfp4 import random_nvfp4
+from .nvfp4 import random_codes_nvfp4
+from .nvfp4 import random_nvfp4 as _random_nvfp4
 
 PAGE = 16
 
@@ -133,7 +134,12 @@ class FlintModel:
     shards are exactly the single-GPU model's tensors."""
 
     def __init__(self, cfg: FlintConfig, device="cuda", seed: int = 0, max_ctx: int = 8192, max_batch: int = 1,
-                 shard: tuple[int, int] = (0, 1)):
+                 shard: tuple[int, int] = (0, 1), weights: str = "quantized"):
+        """weights: "quantized" (seeded N(0, weight_std) quantised to NVFP4) or "codes" (uniformly random NVFP4
+        bytes, a few launches per tensor: for small models that only need valid weights)."""
+        if weights not in ("quantized", "codes"):
+            raise ValueError(f"weights must be 'quantized' or 'codes', got {weights!r}")
+        random_nvfp4 = _random_nvfp4 if weights == "quantized" else random_codes_nvfp4
         self.cfg, self.dev = cfg, torch.device(device)
         self.max_ctx, self.max_batch = max_ctx, max_batch
         self.rank, self.world = shard

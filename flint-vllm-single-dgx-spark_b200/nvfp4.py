@@ -62,3 +62,16 @@ def random_nvfp4(shape_lead, N: int, K: int, std: float, gen: torch.Generator, d
         P[i:i + n], S[i:i + n], gs[i:i + n] = p, s, g
         del w
     return P.reshape(*lead, N, K // 2), S.reshape(*lead, N, K // 16), gs.reshape(lead)
+
+
+@torch.no_grad()
+def random_codes_nvfp4(shape_lead, N: int, K: int, std: float, gen: torch.Generator, device):
+    """Uniformly random NVFP4 bytes: every code byte in 0..255 and every E4M3 scale byte in [0x28, 0x47) (0.25 to
+    3.5), with the global scale set so the dequantised weights have a standard deviation of about ``std`` (the
+    E2M1 codes have an rms of 2.93, the scales about 1.7).  Three launches per tensor instead of the quantiser's
+    dozens; for small models whose numbers only need to be valid NVFP4 (the smoke run, launch-list captures)."""
+    lead = tuple(shape_lead)
+    P = torch.randint(0, 256, (*lead, N, K // 2), generator=gen, device=device, dtype=torch.uint8)
+    S = torch.randint(0x28, 0x47, (*lead, N, K // 16), generator=gen, device=device, dtype=torch.uint8)
+    gs = torch.full(lead, std / 5.0, dtype=torch.float32, device=device)
+    return P, S, gs
