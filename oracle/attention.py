@@ -19,10 +19,13 @@ from .nvfp4 import bf16_round, dequantize_nvfp4
 LOG2E = 1.4426950408889634
 
 
-def gemv_nvfp4(x: np.ndarray, P, S, gs) -> np.ndarray:
-    """bf16(gs * x . dequant(P, S)^T): x [M, K] -> [M, N] (bf16 values as fp32)."""
-    W = dequantize_nvfp4(P, S).astype(np.float64)
-    acc = (np.asarray(x, np.float64) @ W.T).astype(np.float32)
+def gemv_nvfp4(x: np.ndarray, P, S, gs, W: np.ndarray | None = None) -> np.ndarray:
+    """bf16(gs * x . dequant(P, S)^T): x [M, K] -> [M, N] (bf16 values as fp32).  The dot is float64 unless W, the
+    already dequantised weight, is given: then it runs in W's precision (fp32 W = the reference's dequantise-to-fp32
+    matmul, fast/fast_head.py:95-115 and patch:295-319)."""
+    if W is None:
+        W = dequantize_nvfp4(P, S).astype(np.float64)
+    acc = (np.asarray(x, W.dtype) @ W.T).astype(np.float32)
     return bf16_round(acc * np.float32(gs))
 
 
@@ -33,10 +36,11 @@ def rope_cos_sin(max_pos: int, dim: int = 128, theta: float = 1e6) -> np.ndarray
     return np.concatenate([np.cos(ang), np.sin(ang)], axis=1).astype(np.float32)
 
 
-def qkv_head(x, res, nw, eps, P, S, gs, q_w, k_w, positions, cos_sin, nq, nkv, D=128):
-    """-> (q [M, nq*D], y [M, N] (raw q and v heads, normalised+rotated k heads), res_out, k_new, v_new [M, nkv, D])."""
+def qkv_head(x, res, nw, eps, P, S, gs, q_w, k_w, positions, cos_sin, nq, nkv, D=128, W=None):
+    """-> (q [M, nq*D], y [M, N] (raw q and v heads, normalised+rotated k heads), res_out, k_new, v_new [M, nkv, D]).
+    W: optional dequantised QKV weight (see gemv_nvfp4)."""
     xn, res_out = rmsnorm(x, res, nw, eps)
-    y = gemv_nvfp4(xn, P, S, gs)
+    y = gemv_nvfp4(xn, P, S, gs, W)
     M = y.shape[0]
     heads = y.reshape(M, nq + 2 * nkv, D).copy()
     out = heads.copy()

@@ -12,8 +12,12 @@ import numpy as np
 from .nvfp4 import dequantize_nvfp4
 
 
-def lm_head_logits(x: np.ndarray, P: np.ndarray, S: np.ndarray, gs: float, chunk: int = 8192) -> np.ndarray:
-    """x fp32 (bf16 values) [M, K] -> fp32 logits [M, V]."""
+def lm_head_logits(x: np.ndarray, P: np.ndarray, S: np.ndarray, gs: float, chunk: int = 8192,
+                   W: np.ndarray | None = None) -> np.ndarray:
+    """x fp32 (bf16 values) [M, K] -> fp32 logits [M, V].  W: optional already dequantised head; the dots then
+    run in W's precision (fp32: the reference's dequantise-to-fp32 matmul), else in float64."""
+    if W is not None:
+        return ((np.asarray(x, W.dtype) @ W.T).astype(np.float32) * np.float32(gs)).astype(np.float32)
     x64 = np.asarray(x, dtype=np.float64)
     V = P.shape[0]
     out = np.empty((x64.shape[0], V), dtype=np.float32)

@@ -49,6 +49,14 @@ def router_logits_mirror(xn: np.ndarray, wr: np.ndarray) -> np.ndarray:
     return bf16_round(acc[..., 0])
 
 
+def route_weights(logits: np.ndarray, ids: np.ndarray, score_fn: int) -> np.ndarray:
+    """Renormalised routing weights of the chosen experts ids [M, k] (fp32): softmax over the chosen logits
+    (score_fn 0) or sigmoid of each, divided by their sum (score_fn 1)."""
+    sel = np.take_along_axis(logits.astype(np.float32), ids, -1).astype(np.float64)
+    v = 1.0 / (1.0 + np.exp(-sel)) if score_fn == 1 else np.exp(sel - sel.max(-1, keepdims=True))
+    return (v / v.sum(-1, keepdims=True)).astype(np.float32)
+
+
 def topk_route(logits: np.ndarray, topk: int, score_fn: int):
     """-> (ids int32 [M, k], weights fp32 [M, k]); score_fn 0 = softmax (select on logits), 1 = sigmoid."""
     lg = logits.astype(np.float32)
@@ -56,16 +64,12 @@ def topk_route(logits: np.ndarray, topk: int, score_fn: int):
     # (patch:3015-3048 and fast/fp4moe_mar.cu:286-290); weights stay fp32 (fast/fp4moe_mar.cu:301)
     order = np.lexsort((np.broadcast_to(np.arange(lg.shape[-1]), lg.shape), -lg), axis=-1)
     ids = order[:, :topk].astype(np.int32)
-    if score_fn == 1:
-        v = 1.0 / (1.0 + np.exp(-np.take_along_axis(lg, ids, -1).astype(np.float64)))
-    else:
-        sel = np.take_along_axis(lg, ids, -1).astype(np.float64)
-        v = np.exp(sel - sel[:, :1])
-    return ids, (v / v.sum(-1, keepdims=True)).astype(np.float32)
+    return ids, route_weights(lg, ids, score_fn)
 
 
-def experts_up(xn: np.ndarray, ids: np.ndarray, w13, s13, g13) -> np.ndarray:
-    """-> act (bf16 values as fp32) [M*k, I], row m*k+s for expert ids[m, s]."""
+def experts_up(xn: np.ndarray, ids: np.ndarray, w13, s13, g13, dense=None) -> np.ndarray:
+    """-> act (bf16 values as fp32) [M*k, I], row m*k+s for expert ids[m, s].  dense: optional e -> dequantised
+    gate/up weight of expert e; the dots then run in that array's precision (float64 without it)."""
     M, k = ids.shape
     I = w13.shape[1] // 2
     act = np.zeros((M * k, I), dtype=np.float32)
@@ -73,10 +77,13 @@ def experts_up(xn: np.ndarray, ids: np.ndarray, w13, s13, g13) -> np.ndarray:
     for m in range(M):
         for s in range(k):
             e = int(ids[m, s])
-            if e not in cache:
-                cache[e] = dequantize_nvfp4(w13[e], s13[e]).astype(np.float64)
-            W = cache[e]
-            h = W @ xn[m].astype(np.float64)
+            if dense is not None:
+                W = dense(e)
+            else:
+                if e not in cache:
+                    cache[e] = dequantize_nvfp4(w13[e], s13[e]).astype(np.float64)
+                W = cache[e]
+            h = W @ xn[m].astype(W.dtype)
             g = (h[:I].astype(np.float32) * np.float32(g13[e])).astype(np.float32)
             u = (h[I:].astype(np.float32) * np.float32(g13[e])).astype(np.float32)
             silu = (g.astype(np.float64) / (1.0 + np.exp(-g.astype(np.float64)))).astype(np.float32)
@@ -84,8 +91,9 @@ def experts_up(xn: np.ndarray, ids: np.ndarray, w13, s13, g13) -> np.ndarray:
     return act
 
 
-def experts_down(act: np.ndarray, ids: np.ndarray, tw: np.ndarray, w2, s2, g2) -> np.ndarray:
-    """-> out (bf16 values as fp32) [M, H]."""
+def experts_down(act: np.ndarray, ids: np.ndarray, tw: np.ndarray, w2, s2, g2, dense=None) -> np.ndarray:
+    """-> out (bf16 values as fp32) [M, H].  dense: optional e -> dequantised down weight of expert e (as in
+    experts_up)."""
     M, k = ids.shape
     H = w2.shape[1]
     out = np.zeros((M, H), dtype=np.float32)
@@ -94,9 +102,13 @@ def experts_down(act: np.ndarray, ids: np.ndarray, tw: np.ndarray, w2, s2, g2) -
         acc = np.zeros(H, dtype=np.float64)
         for s in range(k):
             e = int(ids[m, s])
-            if e not in cache:
-                cache[e] = dequantize_nvfp4(w2[e], s2[e]).astype(np.float64)
-            y = bf16_round(((cache[e] @ act[m * k + s].astype(np.float64)).astype(np.float32) * np.float32(g2[e])))
+            if dense is not None:
+                W = dense(e)
+            else:
+                if e not in cache:
+                    cache[e] = dequantize_nvfp4(w2[e], s2[e]).astype(np.float64)
+                W = cache[e]
+            y = bf16_round(((W @ act[m * k + s].astype(W.dtype)).astype(np.float32) * np.float32(g2[e])))
             acc = (acc + np.float64(tw[m, s]) * y.astype(np.float64)).astype(np.float32).astype(np.float64)
         out[m] = bf16_round(acc.astype(np.float32))
     return out

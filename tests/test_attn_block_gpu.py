@@ -76,7 +76,7 @@ def check_against_oracle(I, out, res_out, q_out, attn, kv, sinks=None, window=0,
 @needs_cuda
 @pytest.mark.parametrize("ctx,window,use_sinks", [([40], 0, False), ([6057], 0, False), ([1], 0, True),
                                                   ([300, 4096, 33, 17], 0, True), ([5000], 513, True),
-                                                  ([0, 40], 0, False), ([32768], 0, False),
+                                                  ([0, 40], 0, False), ([32768], 0, False), ([262144], 0, False),
                                                   ([16, 17, 15, 1, 64, 100, 2000, 6057], 0, False)])
 def test_attn_block_vs_oracle(fb, ctx, window, use_sinks):
     rng = np.random.default_rng(sum(ctx) + 7 * window + len(ctx))
