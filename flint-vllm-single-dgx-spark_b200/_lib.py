@@ -77,6 +77,7 @@ SIGNATURES: dict[str, tuple] = {
     "flint_workspace_status_offset": (I64, [I32]),
     "flint_workspace_status": (I32, [P, I32, P, I32]),
     "flint_nvfp4_dequant": (I32, [P, P, I64, I64, P, I32, P, I32, P]),
+    "flint_marlin_nvfp4_unpack": (I32, [P, P, P, I64, I64, I64, P, P, P, P, I32, P]),
     "flint_decode_attention": (I32, [P, I64, P, I64, I64, I64, I64, P, I64, I64, P, P, I64, F32, I64, I64, P, I64, I64, P,
                                      I32, P]),
 }

@@ -7,9 +7,10 @@ Same entry points, argument order and outputs as the reference (fast/fp4moe_deco
 * ``moe_up(x, ti, w) -> (act bf16 [M*k, I], sact)``
 * ``moe_down(act, sact, ti, tw, w, trigger=0) -> out bf16 [M, H]``
 
-Differences, by design: the kernels read the ModelOpt NVFP4 tensors in place (``DecodeWeights``) instead of the
-Marlin repack the GB10 kernels need, run 1..8 tokens instead of 1, and take the expert count / top-k / score
-function from the weights instead of hard-coding Flint's 256 / 6 / sigmoid.  ``trigger`` is accepted for
+Differences, by design: the kernels read the ModelOpt NVFP4 layout (``DecodeWeights``, in place); the Marlin
+tensors the reference's caller passes to ``MarlinDecodeWeights`` are converted to it once on the GPU
+(``unpack_marlin``).  The kernels run 1..8 tokens instead of 1 and take the expert count / top-k / score function
+from the weights instead of hard-coding Flint's 256 / 6 / sigmoid.  ``trigger`` is accepted for
 signature compatibility (every launch is stream ordered).
 
 Flint's ungated shared expert (``DecodeWeights(..., shared=...)``): ``moe_up`` also returns its activation ``sact``
@@ -84,20 +85,58 @@ class DecodeWeights:
         return cls(w13, s13, g13, w2, s2, g2, topk=topk, score=score, shared=shared)
 
 
+def unpack_marlin(weight, weight_scale, global_scale):
+    """vLLM's Marlin-processed NVFP4 tensors of one projection -> ModelOpt (codes u8 [E, N, K/2], E4M3 scales u8
+    [E, N, K/16], global fp32 [E]), on the GPU (flint_marlin_nvfp4_unpack; layout fast/fp4moe_mar.cu:1-7).
+
+    weight int32 [E, K/16, 2N] (or [K/16, 2N] for one matrix, e.g. the shared expert), weight_scale [E, K/16, N]
+    processed scale bytes (any 1-byte dtype), global_scale the processed global scale per matrix ([E], [E, 2] -- the
+    first column is used, as fast/fp4moe_decode.py:41 does -- or a scalar).  The result reproduces the weights the
+    reference's kernels use bit for bit: e2m1 * e4m3 * gs == e2m1 * fp16(h << 7) * g * 2^-126.  Allocates the
+    ModelOpt copy (the Marlin tensors are not modified).  ValueError if a scale byte is not a processed scale."""
+    single = weight.dim() == 2
+    w = weight.unsqueeze(0) if single else weight
+    sc = weight_scale.unsqueeze(0) if single else weight_scale
+    if w.dtype != torch.int32 or w.dim() != 3:
+        raise ValueError(f"unpack_marlin: expected int32 Marlin tiles [E, K/16, 2N], got {weight.dtype} "
+                         f"{tuple(weight.shape)}")
+    E, KT, W2 = w.shape
+    N, K = W2 // 2, KT * 16
+    g = global_scale.float().reshape(E, -1)[:, 0].contiguous()
+    dev = w.device
+    P = torch.empty((E, N, K // 2), dtype=torch.uint8, device=dev)
+    S = torch.empty((E, N, K // 16), dtype=torch.uint8, device=dev)
+    gs = torch.empty((E,), dtype=torch.float32, device=dev)
+    bad = torch.zeros((1,), dtype=torch.int32, device=dev)
+    torch.ops.flint_b200.marlin_nvfp4_unpack(w.contiguous(), sc.contiguous().view(torch.uint8), g, P, S, gs, bad)
+    if int(bad.item()):
+        raise ValueError("unpack_marlin: a scale byte is not a processed NVFP4 scale (0, or 0x80..0xF6)")
+    return (P[0], S[0], gs[0]) if single else (P, S, gs)
+
+
 class MarlinDecodeWeights(DecodeWeights):
     """The reference's constructor and argument order (fast/fp4moe_decode.py:27-44, called at fast/model.py:277-282):
     the routed experts' six tensors, then the shared expert's gate_up and down as (weight, weight_scale, global
-    scale) tuples, with Flint's routing (top-6 sigmoid, or FLINT_MOE_TOPK / FLINT_MOE_SCORE).  These kernels read
-    the ModelOpt NVFP4 layout in place, so the tensors must be the ModelOpt ones (uint8 codes); the Marlin repack the
-    GB10 kernels read (int32 tiles) is refused with a ValueError."""
+    scale) tuples, with Flint's routing (top-6 sigmoid, or FLINT_MOE_TOPK / FLINT_MOE_SCORE).
+
+    Accepts what fast/model.py hands over -- vLLM's Marlin-processed tensors (int32 tiles, processed scales and
+    global scales; layout fast/fp4moe_mar.cu:1-7) -- and converts them once, on the GPU, to the ModelOpt layout these
+    kernels read (``unpack_marlin``; a second copy of the expert weights, while vLLM keeps its Marlin tensors for
+    prefill).  ModelOpt tensors (uint8 codes) are used in place."""
 
     def __init__(self, w13, s13, g13, w2, s2, g2, sh_gu, sh_dn):
-        if w13.dtype != torch.uint8 or w2.dtype != torch.uint8:
-            raise ValueError("MarlinDecodeWeights: these kernels read the ModelOpt NVFP4 layout (uint8 codes "
-                             f"[E, 2I, H/2]), got {w13.dtype} / {w2.dtype}: pass the layer's ModelOpt w13_weight / "
-                             "w2_weight (and scales), not the Marlin repack")
-        shared = (sh_gu[0], sh_gu[1], sh_gu[2].float().reshape(-1)[:1], sh_dn[0], sh_dn[1],
-                  sh_dn[2].float().reshape(-1)[:1])
+        if w13.dtype == torch.int32 and w2.dtype == torch.int32:
+            w13, s13, g13 = unpack_marlin(w13, s13, g13)
+            w2, s2, g2 = unpack_marlin(w2, s2, g2)
+            if sh_gu is not None:
+                sh_gu, sh_dn = unpack_marlin(*sh_gu), unpack_marlin(*sh_dn)
+        elif w13.dtype != torch.uint8 or w2.dtype != torch.uint8:
+            raise ValueError(f"MarlinDecodeWeights: expected Marlin int32 tiles or ModelOpt uint8 codes, got "
+                             f"{w13.dtype} / {w2.dtype}")
+        shared = None
+        if sh_gu is not None:
+            shared = (sh_gu[0], sh_gu[1], sh_gu[2].float().reshape(-1)[:1], sh_dn[0], sh_dn[1],
+                      sh_dn[2].float().reshape(-1)[:1])
         super().__init__(w13, s13, g13, w2, s2, g2, topk=TOPK, score=SCORE, shared=shared)
 
 

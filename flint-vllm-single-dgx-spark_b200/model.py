@@ -274,6 +274,7 @@ class Decoder:
         if c.shared_inter:
             self.sact, self.ys = e(M, c.shared_inter), e(M, c.hidden)
         self.route_trace = None          # trace_routing(): [layers, M, topk] int32, each MoE layer's chosen experts
+        self.route_trace_logits = None   # ... and [layers, M, E] fp32, its router logits
         self.dummy_f = e(1, 1, dt=torch.float32)
         self.dummy_b = e(0)
         self.splits = _ops.attention_splits(M, c.num_kv_heads)
@@ -290,13 +291,20 @@ class Decoder:
         self.launches_per_step = (3 if attn == "chain" else 1) * c.layers + mlp_launches + 2 + (1 if ep else 0)
 
     def trace_routing(self):
-        """Record every MoE layer's chosen experts of the current step in ``route_trace`` [layers, M, topk] (int32,
-        overwritten each step) -- the block launch writes them through its ids output, the chain and the fused
-        launch copy their routing buffer.  Call before capture(); single-GPU routed layers only."""
+        """Record every MoE layer's chosen experts and router logits of the current step in ``route_trace``
+        [layers, M, topk] (int32) and ``route_trace_logits`` [layers, M, E] (fp32), overwritten each step -- the
+        block launch writes them through its ids / logits outputs, the chain and the fused launch copy their routing
+        buffers.  Call before capture(); single-GPU routed layers only."""
         if self.m.world > 1:
             raise ValueError("routing traces are recorded on one GPU")
-        self.route_trace = torch.full((self.c.layers, self.M, self.c.topk), -1, dtype=torch.int32, device=self.m.dev)
+        c = self.c
+        self.route_trace = torch.full((c.layers, self.M, c.topk), -1, dtype=torch.int32, device=self.m.dev)
+        self.route_trace_logits = torch.zeros((c.layers, self.M, c.num_experts), dtype=torch.float32, device=self.m.dev)
         self.graphs.clear()
+
+    def _trace_copy(self, l):
+        self.route_trace[l].copy_(self.ti)
+        self.route_trace_logits[l].copy_(self.lg)
 
     # ---- one decode step as torch ops on persistent buffers ----
     def layer_ops(self, l: int) -> list[tuple[str, callable]]:
@@ -361,23 +369,24 @@ class Decoder:
             seq.append(("moe_block_ep", moe_ep))
         elif self.moe == "block":
             xn_out = self.xn if ew.shared is not None else None      # the shared expert reads the normalised input
-            ids_out = self.route_trace[l] if self.route_trace is not None else None
+            tr = self.route_trace is not None
+            ids_out, lg_out = (self.route_trace[l], self.route_trace_logits[l]) if tr else (None, None)
             seq.append(("moe_block", lambda: ops.moe_block(self.a, self.res_a, L["ln2"], c.rms_eps, L["gate"], c.topk,
                                                            ew.score_fn, ew.w13, ew.s13, ew.g13, ew.w2, ew.s2, ew.g2, self.h,
-                                                           self.res_b, xn_out, None, ids_out, None, pf)))
+                                                           self.res_b, xn_out, lg_out, ids_out, None, pf)))
         elif self.moe == "fused":
             seq.append(("moe_fused", lambda: ops.moe_fused(self.a, self.res_a, L["ln2"], c.rms_eps, L["gate"], c.topk,
                                                            ew.score_fn, ew.w13, ew.s13, ew.g13, ew.w2, ew.s2, ew.g2,
                                                            self.h, self.res_b, self.xn, self.lg, self.ti, self.tw,
                                                            ew.shared is not None)))
             if self.route_trace is not None:
-                seq.append(("route_trace", lambda: self.route_trace[l].copy_(self.ti)))
+                seq.append(("route_trace", lambda: self._trace_copy(l)))
         else:
             seq.append(("route", lambda: ops.moe_route(self.a, self.res_a, L["ln2"], c.rms_eps, L["gate"], c.topk,
                                                        ew.score_fn, self.lg, self.ti, self.tw, self.xn, self.res_b, True,
                                                        True)))
             if self.route_trace is not None:
-                seq.append(("route_trace", lambda: self.route_trace[l].copy_(self.ti)))
+                seq.append(("route_trace", lambda: self._trace_copy(l)))
             if m.world > 1:
                 # expert parallel: routing replicated; local routes' rows, an exact sum over ranks, slot-order combine
                 import torch.distributed as dist

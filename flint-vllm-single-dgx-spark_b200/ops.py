@@ -696,6 +696,35 @@ def _(blocks, n_cols, packed, scales, bad_blocks):
     return None
 
 
+@torch.library.custom_op(f"{NS}::marlin_nvfp4_unpack", mutates_args=("packed", "scales", "global_out", "bad"))
+def marlin_nvfp4_unpack(weight: torch.Tensor, weight_scale: torch.Tensor, global_scale: torch.Tensor,
+                        packed: torch.Tensor, scales: torch.Tensor, global_out: torch.Tensor, bad: torch.Tensor) -> None:
+    """Marlin-processed NVFP4 (int32 [E, K/16, 2N], processed scale bytes [E, K/16, N], processed global fp32 [E])
+    -> ModelOpt packed u8 [E, N, K/2], E4M3 bits u8 [E, N, K/16], global fp32 [E]; bad (int32 [1], zeroed by the
+    caller) counts CTAs that met a byte that is not a processed scale."""
+    _lib.require_cuda(weight, "marlin_nvfp4_unpack")
+    if weight.dtype != torch.int32 or weight.dim() != 3:
+        raise _lib.FlintError("marlin_nvfp4_unpack: weight must be int32 [E, K/16, 2N]")
+    E, KT, W2 = weight.shape
+    N, K = W2 // 2, KT * 16
+    if tuple(weight_scale.shape) != (E, KT, N) or tuple(packed.shape) != (E, N, K // 2) or \
+            tuple(scales.shape) != (E, N, K // 16) or global_scale.numel() != E or global_out.numel() != E:
+        raise _lib.FlintError("marlin_nvfp4_unpack: shapes do not match the weight")
+    for t in (weight, weight_scale, global_scale, packed, scales, global_out):
+        if not t.is_contiguous():
+            raise _lib.FlintError("marlin_nvfp4_unpack: tensors must be contiguous")
+    if global_scale.dtype != torch.float32 or global_out.dtype != torch.float32:
+        raise _lib.FlintError("marlin_nvfp4_unpack: global scales are fp32")
+    rc = lib().flint_marlin_nvfp4_unpack(ptr(weight), ptr(_u8(weight_scale)), ptr(global_scale), E, N, K, ptr(packed),
+                                         ptr(scales), ptr(global_out), ptr(bad), 0, stream_ptr(weight.device))
+    check(rc, "flint_marlin_nvfp4_unpack")
+
+
+@marlin_nvfp4_unpack.register_fake
+def _(weight, weight_scale, global_scale, packed, scales, global_out, bad):
+    return None
+
+
 @torch.library.custom_op(f"{NS}::nvfp4_dequant", mutates_args=("out",))
 def nvfp4_dequant(P: torch.Tensor, S: torch.Tensor, global_scale: torch.Tensor | None, out: torch.Tensor) -> None:
     """out [..., K] (fp32 or bf16) = e2m1(P) * e4m3(S) (* global_scale, one fp32 scalar on the device)."""

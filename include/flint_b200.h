@@ -394,6 +394,18 @@ int flint_gguf_nvfp4_repack(const void* blocks, int64_t rows, int64_t n_cols, vo
 int flint_nvfp4_dequant(const void* P, const void* S, int64_t rows, int64_t n_cols, const float* global_scale,
                         int out_f32, void* out, int pdl, void* stream);
 
+/* Marlin-processed NVFP4 (the tensors vLLM holds after its Marlin repack and that fast/model.py:271-282 hands to
+ * fp4moe_decode.MarlinDecodeWeights; layout fast/fp4moe_mar.cu:1-7) -> the ModelOpt layout of every kernel above.
+ * weight int32 [E][K/16][N/64][128 words] (4-byte aligned), weight_scale u8 [E][K/16][N] (processed S0E5M3 bytes,
+ * permuted inside each 64-column group), global_scale fp32 [E] (processed).  Writes packed u8 [E][N][K/2] (8-byte
+ * aligned), scales E4M3 bits u8 [E][N][K/16] (scale byte h -> h - 0x78, 0 stays 0) and global_out fp32 [E]
+ * (= global_scale * 2^-119), so e2m1 * e4m3 * gs equals the reference's e2m1 * fp16(h << 7) * g * 2^-126 exactly.
+ * A non-zero scale byte outside 0x80..0xF6 is not a processed scale: the CTAs that met one add 1 to *bad (device
+ * int32, zeroed by the caller) and write 0 for it.  N % 64 == 0, K % 16 == 0. */
+int flint_marlin_nvfp4_unpack(const void* weight, const void* weight_scale, const float* global_scale, int64_t E,
+                              int64_t N, int64_t K, void* packed, void* scales, float* global_out, int32_t* bad, int pdl,
+                              void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -15,9 +15,10 @@ dequantise-to-fp32 path, with the bf16 rounding points of the per-kernel oracles
 kernel's fixed summation order (moe.router_logits_mirror), so routing can be compared expert for expert.
 
 Routing of a token is a discrete choice on bf16 logits: when the model's hidden state differs from the GPU's by a bf16
-ulp somewhere, a k-th / (k+1)-th pair that is within an ulp or two may legitimately swap.  ``step`` therefore takes
-the GPU's own choice (``gpu_ids``) and adopts it when it is a top-k of this oracle's logits up to ``route_tol_ulps``
-bf16 ulps; a choice outside that bound raises ``RoutingMismatch``.  Adoptions are counted.
+ulp somewhere, two experts whose logits are within an ulp or two may legitimately swap.  ``step`` therefore takes the
+GPU's own choice (``gpu_ids``, with its router logits ``gpu_logits``) after checking it: the choice must be the exact
+top-k of the GPU's logits, and those must agree with this oracle's within ``route_tol_ulps`` bf16 ulps; anything
+else raises ``RoutingMismatch``.  Adoptions and the largest logit difference are recorded.
 """
 from __future__ import annotations
 
@@ -49,7 +50,7 @@ class DecodeOracle:
     k_norm [D], qkv (P, S, gs), o (P, S, gs), gate [E, H], w13, s13, g13, w2, s2, g2.  ``dense`` caches the
     dequantised fp32 weights; share one between oracles of the same model."""
 
-    def __init__(self, cfg, weights: dict, max_pos: int, dense: dict | None = None, route_tol_ulps: float = 2.0):
+    def __init__(self, cfg, weights: dict, max_pos: int, dense: dict | None = None, route_tol_ulps: float = 4.0):
         if cfg.shared_inter or cfg.mlp_only_layers or cfg.layer_types or cfg.attn_sinks or cfg.no_rope_layers:
             raise ValueError("DecodeOracle covers the BASELINE layer structure only")
         self.c, self.w = cfg, weights
@@ -61,6 +62,7 @@ class DecodeOracle:
         self.kv = [np.zeros((self.npages, nkv, PAGE, 2 * D), np.float32) for _ in range(cfg.layers)]
         self.adopted = 0                 # routing choices taken from the GPU within the tolerance
         self.route_checks = 0
+        self.max_logit_ulps = 0.0        # largest router-logit difference seen, in bf16 ulps of the row maximum
 
     # ---- dequantised weights, computed once per tensor ----
     def _dq(self, key, P, S) -> np.ndarray:
@@ -75,34 +77,57 @@ class DecodeOracle:
         return self._dq((l, which, e), P[e], S[e])
 
     # ---- routing ----
-    def route(self, logits: np.ndarray, gpu_ids: np.ndarray | None):
-        """-> (ids [1, k], weights [1, k]) for bf16 logits [1, E]: this oracle's top-k, or the GPU's choice when that
-        is a top-k of these logits within the tolerance (raises RoutingMismatch otherwise)."""
+    def route(self, logits: np.ndarray, gpu_ids: np.ndarray | None, gpu_logits: np.ndarray | None = None):
+        """-> (ids [1, k], weights [1, k]) for bf16 logits [1, E]: this oracle's top-k, or the GPU's choice.
+
+        With the GPU's own router logits: its ids must be exactly the top-k of those logits (the kernel's selection
+        rule), and those logits must agree with this oracle's within ``route_tol_ulps`` bf16 ulps of the row's
+        largest logit; the GPU's choice is then taken.  Without them: the GPU's ids must be a top-k of this oracle's
+        logits up to that many ulps at each compared logit.  Anything else raises RoutingMismatch."""
         k = self.c.topk
         ids, tw = topk_route(logits, k, self.score)
         if gpu_ids is None:
             return ids, tw
         self.route_checks += 1
         g = np.asarray(gpu_ids, np.int32).reshape(1, k)
+        v = logits[0].astype(np.float64)
+        if gpu_logits is not None:
+            gl = np.asarray(gpu_logits, np.float32).reshape(1, -1)
+            own, _ = topk_route(gl, k, self.score)
+            if not np.array_equal(own, g):
+                raise RoutingMismatch(f"GPU experts {g[0].tolist()} are not the top-{k} of the GPU's own router logits "
+                                      f"({own[0].tolist()})")
+            d = float(np.abs(gl[0].astype(np.float64) - v).max())
+            unit = bf16_ulp(np.abs(v).max())
+            self.max_logit_ulps = max(self.max_logit_ulps, d / unit)
+            if d > self.tol * unit:
+                raise RoutingMismatch(f"router logits differ from the oracle's by {d:.3g} (> {self.tol} bf16 ulps of "
+                                      f"{np.abs(v).max():.3g})")
+            if not np.array_equal(g, ids):
+                self.adopted += 1
+                return g, route_weights(logits, g, self.score)
+            return ids, tw
         if np.array_equal(g, ids):
             return ids, tw
-        v = logits[0].astype(np.float64)
-        tol = self.tol * bf16_ulp(v[ids[0, -1]])
         chosen = np.zeros(v.shape[0], bool)
         chosen[g[0]] = True
-        ok = (len(set(g[0].tolist())) == k and chosen.sum() == k
-              and v[chosen].min() >= v[~chosen].max() - tol                      # a top-k up to the tolerance
-              and np.all(np.diff(v[g[0]]) <= tol))                               # in descending order up to it
+        near = lambda a, b: self.tol * bf16_ulp(max(abs(a), abs(b)))
+        lo, hi = v[chosen].min(), v[~chosen].max()
+        sel = v[g[0]]
+        ok = (len(set(g[0].tolist())) == k and lo >= hi - near(lo, hi)
+              and all(sel[i] >= sel[i + 1] - near(sel[i], sel[i + 1]) for i in range(k - 1)))
         if not ok:
             raise RoutingMismatch(f"GPU experts {g[0].tolist()} are not a top-{k} of the oracle logits "
-                                  f"(oracle {ids[0].tolist()}, tolerance {tol:.3g})")
+                                  f"(oracle {ids[0].tolist()}, {self.tol} bf16 ulps)")
         self.adopted += 1
         return g, route_weights(logits, g, self.score)
 
     # ---- one position ----
-    def step(self, token: int, pos: int, gpu_ids: np.ndarray | None = None) -> np.ndarray:
-        """Run token at position pos through every layer (writing its K/V) and the head; gpu_ids [layers, k] is the
-        GPU's routing for this position (or None).  -> fp32 logits [V]."""
+    def step(self, token: int, pos: int, gpu_ids: np.ndarray | None = None,
+             gpu_logits: np.ndarray | None = None) -> np.ndarray:
+        """Run token at position pos through every layer (writing its K/V) and the head; gpu_ids [layers, k] and
+        gpu_logits [layers, E] are the GPU's routing and router logits for this position (or None).
+        -> fp32 logits [V]."""
         c, W = self.c, self.w
         nq, nkv, D, eps = c.num_heads, c.num_kv_heads, c.head_dim, c.rms_eps
         x, res = W["embed"][token][None, :], None
@@ -122,7 +147,8 @@ class DecodeOracle:
             a = gemv_nvfp4(att.reshape(1, -1), Po, So, go, W=self._dq((l, "o"), Po, So))
             xn, res_b = rmsnorm(a, res_a, L["ln2"], eps)
             lg = router_logits_mirror(xn, L["gate"])
-            ids, tw = self.route(lg, None if gpu_ids is None else gpu_ids[l])
+            ids, tw = self.route(lg, None if gpu_ids is None else gpu_ids[l],
+                                 None if gpu_logits is None else gpu_logits[l])
             act = experts_up(xn, ids, L["w13"], L["s13"], L["g13"], dense=lambda e: self._expert(l, "up", e))
             x = experts_down(act, ids, tw, L["w2"], L["s2"], L["g2"], dense=lambda e: self._expert(l, "down", e))
             res = res_b

@@ -5,9 +5,10 @@ three-launch chains, and two streams batched) against a CPU decode composed from
 The model: hidden 2048, 32 / 4 heads of 128, RoPE theta 1e6, 64 experts softmax top-8, I = 768, 4 layers, vocabulary
 16,384, seeded N(0, 0.02) NVFP4 weights.  A 64-token prompt runs through the decode kernels, then 32 greedy tokens.
 
-Per position the GPU's routing (every layer's chosen experts, recorded by the decoder's routing trace) must be a
-top-k of the oracle's router logits up to 2 bf16 ulps (the oracle takes the GPU's choice on such near-ties so both
-stay on one path); per generated token the GPU's fp32 logits must lie within 1e-2 of the logit scale of the
+Per position and layer the GPU's routing (chosen experts and router logits, recorded by the decoder's routing trace)
+must be exactly the top-k of the GPU's own logits, and those logits within 4 bf16 ulps (of the row's largest) of the
+oracle's; the oracle then takes the GPU's choice, so a near-tie swap cannot send the two down different experts.  Per
+generated token the GPU's fp32 logits must lie within 1e-2 of the logit scale of the
 oracle's and the GPU's token must be the oracle's argmax wherever the oracle's top-2 gap
 exceeds twice the logit difference measured at that step.  The oracle is teacher-forced with the GPU's tokens, so a
 near-tie in the argmax cannot desynchronise the two streams.  The same stream replayed through the captured decode
@@ -49,8 +50,9 @@ def setup(fb):
 
 
 def _gpu_stream(setup, batch, moe, attn):
-    """Eager decode with the routing trace and the head's logits: -> (tokens [M, NEW], routes [T, layers, M, k],
-    logits [NEW, M, V]); then the captured-graph stream of the same decoder configuration, -> tokens [M, NEW]."""
+    """Eager decode with the routing trace and the head's logits: -> (tokens [M, NEW], per position (ids [layers, M, k],
+    router logits [layers, M, E]), logits [NEW, M, V]); then the captured-graph stream of the same decoder
+    configuration, -> tokens [M, NEW]."""
     from flint_b200.model import Decoder
     model, cfg = setup["model"], setup["cfg"]
     prompts = setup["prompts"][:batch]
@@ -65,12 +67,12 @@ def _gpu_stream(setup, batch, moe, attn):
     for t in range(PROMPT - 1):                     # prompt positions 0 .. PROMPT-2 (as Decoder.prefill)
         dec._set_state(prompts[:, t], np.full(batch, t))
         dec._layers()
-        routes.append(_np(dec.route_trace).copy())
+        routes.append((_np(dec.route_trace).copy(), _np(dec.route_trace_logits).copy()))
     dec._set_state(prompts[:, PROMPT - 1], np.full(batch, PROMPT - 1))
     dec.step_ctr.zero_()
     for _ in range(NEW):
         dec._layers()
-        routes.append(_np(dec.route_trace).copy())
+        routes.append((_np(dec.route_trace).copy(), _np(dec.route_trace_logits).copy()))
         ops.lm_head_nv4(dec.h, P, S, gs, logits, tok, True, True, dec.res_b, model.final_norm, cfg.rms_eps)
         all_logits.append(_np(logits).copy())
         dec._head_and_advance()
@@ -85,7 +87,7 @@ def _gpu_stream(setup, batch, moe, attn):
     graph = _np(dec2.decode(NEW)).copy()
     dec.close()
     dec2.close()
-    return eager, np.stack(routes), np.stack(all_logits), graph
+    return eager, routes, np.stack(all_logits), graph
 
 
 def _check_stream(setup, b, tokens, routes, logits):
@@ -95,7 +97,7 @@ def _check_stream(setup, b, tokens, routes, logits):
     seq = list(setup["prompts"][b]) + list(tokens[b])
     min_gap, worst, checked = np.inf, 0.0, 0
     for t in range(PROMPT + NEW - 1):
-        ref = orc.step(int(seq[t]), t, routes[t][:, b])
+        ref = orc.step(int(seq[t]), t, routes[t][0][:, b], routes[t][1][:, b])
         if t < PROMPT - 1:
             continue
         i = t - (PROMPT - 1)                       # generated token i is predicted at position PROMPT - 1 + i
@@ -113,7 +115,7 @@ def _check_stream(setup, b, tokens, routes, logits):
                 f"|dlogit| {delta:.3g})")
             checked += 1
     return dict(min_gap=min_gap, worst_rel_dlogit=worst, argmax_checked=checked, adopted=orc.adopted,
-                route_checks=orc.route_checks)
+                route_checks=orc.route_checks, router_ulps=orc.max_logit_ulps)
 
 
 @needs_cuda
@@ -127,5 +129,8 @@ def test_greedy_stream_matches_oracle(setup, batch, moe, attn):
         r = _check_stream(setup, b, tokens, routes, logits)
         print(f"stream {b}: tokens {tokens[b, :8].tolist()}..., argmax checked {r['argmax_checked']}/{NEW}, "
               f"smallest top-2 gap {r['min_gap']:.3g}, worst |dlogit|/scale {r['worst_rel_dlogit']:.2e}, "
-              f"routing near-ties adopted {r['adopted']}/{r['route_checks']}")
-        assert r["argmax_checked"] >= NEW - 2          # near-ties of the argmax are rare; they are reported above
+              f"routing near-ties adopted {r['adopted']}/{r['route_checks']}, largest router-logit difference "
+              f"{r['router_ulps']:.2f} bf16 ulps")
+        # tokens whose oracle top-2 gap is within twice the measured logit difference are bf16 near-ties (reported
+        # above); most tokens must be decided clearly
+        assert r["argmax_checked"] >= NEW // 2

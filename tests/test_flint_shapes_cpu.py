@@ -213,7 +213,8 @@ def test_sharded_flint_layers_dispatch(rec, tmp_path):
 
 def test_marlin_decode_weights_name_takes_modelopt_tensors(fb):
     """The reference's MarlinDecodeWeights(w13, s13, g13, w2, s2, g2, sh_gu, sh_dn) call works unchanged with the
-    ModelOpt tensors (Flint's top-6 sigmoid routing + the shared expert) and refuses Marlin's int32 tiles."""
+    ModelOpt tensors (Flint's top-6 sigmoid routing + the shared expert); Marlin's int32 tiles go to the GPU
+    un-repack (no CPU path: it raises on the host), and other dtypes are refused."""
     from flint_b200 import fp4moe_decode as fm
     from flint_b200.nvfp4 import random_nvfp4
     g = torch.Generator().manual_seed(4)
@@ -223,6 +224,10 @@ def test_marlin_decode_weights_name_takes_modelopt_tensors(fb):
     w = fm.MarlinDecodeWeights(*routed, gu, dn)
     assert isinstance(w, fm.DecodeWeights) and (w.topk, w.score_fn) == (fm.TOPK, fm._SCORE_FN[fm.SCORE])
     assert w.shared is not None and w.shared.I == SI
-    marlin = (torch.zeros((E, 8, 16), dtype=torch.int32),) + routed[1:]
-    with pytest.raises(ValueError, match="ModelOpt"):
+    marlin = (torch.zeros((E, H // 16, 4 * I), dtype=torch.int32), torch.zeros((E, H // 16, 2 * I), dtype=torch.uint8),
+              torch.ones(E)) + (torch.zeros((E, I // 16, 2 * H), dtype=torch.int32),
+                                torch.zeros((E, I // 16, H), dtype=torch.uint8), torch.ones(E))
+    with pytest.raises(RuntimeError, match="CUDA|cuda"):
         fm.MarlinDecodeWeights(*marlin, gu, dn)
+    with pytest.raises(ValueError, match="Marlin int32 tiles or ModelOpt uint8"):
+        fm.MarlinDecodeWeights(routed[0].float(), *routed[1:], gu, dn)

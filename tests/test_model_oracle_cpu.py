@@ -75,3 +75,23 @@ def test_routing_adopts_only_near_ties():
     # a repeated expert
     with pytest.raises(RoutingMismatch):
         orc.route(lg, np.array([0, 0, 1], np.int32))
+
+
+def test_routing_with_the_gpu_logits():
+    c = Cfg()
+    c.topk, c.num_experts = 3, 8
+    orc = DecodeOracle(c, _weights(np.random.default_rng(1), Cfg()), max_pos=16)
+    lg = onv.bf16_round(np.array([[0.5, 0.25, 0.125, 0.12451171875, -1.0, -2.0, 0.0, 0.01]], np.float32))
+    gpu = lg.copy()
+    gpu[0, 3] = 0.125                                    # one ulp up: the GPU's top-3 is then 0, 1, 2 (lowest id)
+    g, _ = orc.route(lg, np.array([0, 1, 2], np.int32), gpu)
+    assert g.tolist() == [[0, 1, 2]] and orc.adopted == 0 and orc.max_logit_ulps > 0
+    gpu[0, 3] = 0.126953125                              # two ulps up: the GPU now picks expert 3
+    g, _ = orc.route(lg, np.array([0, 1, 3], np.int32), gpu)
+    assert g.tolist() == [[0, 1, 3]] and orc.adopted == 1
+    with pytest.raises(RoutingMismatch):                 # not the top-3 of the GPU's own logits
+        orc.route(lg, np.array([0, 1, 4], np.int32), gpu)
+    far = lg.copy()
+    far[0, 4] = 1.0                                      # a logit far from the oracle's
+    with pytest.raises(RoutingMismatch):
+        orc.route(lg, np.array([4, 0, 1], np.int32), far)
