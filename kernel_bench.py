@@ -15,7 +15,7 @@ also the small case used for full ncu captures of one kernel.
         [--cols 2048] [--reps 20]
 
 times the checkpoint-format kernels on one tensor of --rows x --cols values (default: the LM head, 174.6 MB of GGUF
-bytes, larger than L2) and the CPU oracle beside them on a bounded slice of the same tensor.
+bytes, larger than L2).
 """
 from __future__ import annotations
 
@@ -113,11 +113,7 @@ def time_kernel(name, args, dec, model, cfg, dev):
 def time_format_kernel(args):
     """GGUF -> ModelOpt repack (36 B read + 36 B written per 64 values) or the bf16 dequant (9 B read + 32 B written
     per 16 values) of one --rows x --cols tensor: CUDA events around one replay of a graph of --reps launches, after
-    3 warm-ups (the tensor is larger than L2, so back-to-back launches do not hit in it); the CPU oracle
-    on 4096 rows of the same tensor, scaled per byte."""
-    import time
-    sys.path.insert(0, ROOT)
-    from oracle import nvfp4 as onv
+    3 warm-ups (the tensor is larger than L2, so back-to-back launches do not hit in it)."""
     dev = torch.device("cuda", torch.cuda.current_device())
     ops = torch.ops.flint_b200
     R, C = args.rows, args.cols
@@ -154,13 +150,6 @@ def time_format_kernel(args):
     us = e0.elapsed_time(e1) * 1e3 / args.reps
     del graph
     assert int(bad.item()) == 0
-    rows = min(R, 4096)
-    hb = blocks[:rows].cpu().numpy()
-    t0 = time.perf_counter()
-    Po, So = onv.repack_gguf_nvfp4(hb, C)
-    if args.kernel == "nvfp4_dequant":
-        onv.bf16_bits(onv.dequantize_nvfp4(Po, So))
-    cpu_s = (time.perf_counter() - t0) * R / rows
     peak = None
     peaks = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(peaks):
@@ -168,9 +157,7 @@ def time_format_kernel(args):
     gbps = nbytes / us / 1e3
     print(json.dumps({"kernel": args.kernel, "rows": R, "cols": C, "launches": args.reps,
                       "us_per_launch": round(us, 2), "bytes_per_launch": nbytes, "GBps": round(gbps, 1),
-                      "frac_of_measured_hbm": round(gbps / peak, 3) if peak else None,
-                      "cpu_oracle_ms_per_tensor": round(cpu_s * 1e3, 1), "cpu_sample_rows": rows,
-                      "cpu_cores": 1}), flush=True)
+                      "frac_of_measured_hbm": round(gbps / peak, 3) if peak else None}), flush=True)
 
 
 if __name__ == "__main__":
