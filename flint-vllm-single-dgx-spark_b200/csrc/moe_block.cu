@@ -17,6 +17,14 @@
 // Routing, xn, res_out and the down step have the bits of flint_moe_route / flint_moe_down; the gate/up sums split
 // K across warps, so act (and hence out) agrees with the chain to fp32 rounding, not bit for bit.
 //
+// Shared expert (Flint's ungated shared MLP, SI = its intermediate size, flint_moe_block_shared): its gate/up rows are
+// extra up units after the routed ones (same 16 + 16-row units over all of H, so the work stays balanced over the
+// CTAs), its activation row is published beside the routed ones, and in phase D a spare warp (topk < 8) computes the
+// block's 16 shared output rows from its down block, loaded with the routed down blocks.  out = bf16(bf16(sum_s tw_s
+// y_s) + y_shared) with y_shared = bf16(act_sh . W2sh * gs2sh): the PR's combine rule (patch:3391-3397) and the
+// rounding of the chain (routed down, shared down, one bf16 add), replacing the GB10 kernels' shared groups inside
+// up_mar / down_mar (fast/fp4moe_mar.cu:67-152, 224-231) -- one launch instead of three.
+//
 // Expert-parallel mode (y_out given): this rank holds experts [e_lo, e_hi) only; the router and top-k run in full
 // (identical on every rank), only routed slots whose expert is local get up units and down rows, and instead of
 // the weighted sum the kernel writes y[slot][H] (bf16 y_s for local slots, zero rows otherwise) and the routing
@@ -43,13 +51,15 @@ constexpr int kXW = 8;                  // consumer warps
 constexpr int kXT = kXW * 32;
 constexpr int kXMaxUnits = 3;           // up units (16 gate + 16 up rows) per CTA
 constexpr int kXMaxSlots = 8;           // routed experts
+constexpr int kXMaxShared = 1024;       // shared expert intermediate size (its act row is staged by one warp)
 
 struct MoeBlockWs {
   GridSync sync;
   unsigned status;
   unsigned epoch;                       // launches so far: the tag of this launch's published words is epoch + 1
   unsigned pad[30];
-  // followed by: logits as tagged words [E] (data = fp32 bits), act as tagged words [8][I / 2] (data = bf16 pair)
+  // followed by: logits as tagged words [E] (data = fp32 bits), act as tagged words [8][I / 2] (data = bf16 pair),
+  // the shared expert's act as tagged words [kXMaxShared / 2]
 };
 
 struct MoeBlockArgs {
@@ -75,10 +85,14 @@ struct MoeBlockArgs {
   int peer_mode;                     // expert parallel with the fused peer exchange
   PeerSet peers;
   L2Prefetch pf;                     // the next op's bytes, pulled into L2 during phase D
+  int SI;                            // shared expert intermediate size (0: none)
+  const float* g13_sh;
+  const float* g2_sh;
+  uint32_t off_dn_sh, off_xa_sh;     // its down block and its staged act row in shared memory
 };
 
 static size_t moe_block_ws_bytes(int E, int I) {
-  return sizeof(MoeBlockWs) + (size_t)E * 8 + (size_t)kXMaxSlots * (I / 2) * 8 + 256;
+  return sizeof(MoeBlockWs) + (size_t)E * 8 + (size_t)kXMaxSlots * (I / 2) * 8 + (size_t)(kXMaxShared / 2) * 8 + 256;
 }
 
 __device__ __forceinline__ void xsync() { asm volatile("bar.sync 1, %0;" ::"r"(kXT) : "memory"); }
@@ -92,7 +106,10 @@ __device__ __forceinline__ bool xsync_and(bool pred) {
 template <int NV>   // H / 256
 __global__ void __launch_bounds__((kXW + 1) * 32, 1)
 moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant__ CUtensorMap up_s,
-                 const __grid_constant__ CUtensorMap dn_c, const __grid_constant__ CUtensorMap dn_s, const MoeBlockArgs a) {
+                 const __grid_constant__ CUtensorMap dn_c, const __grid_constant__ CUtensorMap dn_s,
+                 const __grid_constant__ CUtensorMap sh_up_c, const __grid_constant__ CUtensorMap sh_up_s,
+                 const __grid_constant__ CUtensorMap sh_dn_c, const __grid_constant__ CUtensorMap sh_dn_s,
+                 const MoeBlockArgs a) {
   constexpr int H = NV * 256;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -103,15 +120,18 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   __shared__ float red_n[kXW * 8 + 8];
   __shared__ float ybuf[kXMaxSlots][16];
   __shared__ int s_local[kXMaxSlots], s_nlocal;
+  __shared__ float ysh[16];
+  __shared__ int shift_sh;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nb = gridDim.x, cta = blockIdx.x;
-  const int E = a.E, I = a.I, topk = a.topk;
-  const int nks_u = H / kSliceK, nks_d = I / kSliceK, jpe = I / 16;
+  const int E = a.E, I = a.I, topk = a.topk, SI = a.SI;
+  const int nks_u = H / kSliceK, nks_d = I / kSliceK, jpe = I / 16, nks_sh = SI / kSliceK;
   const bool has_dn = cta < H / 16;
-  // up units follow the local routed slots (known after top-k): unit u -> slot s_local[u / jpe], rows 16 (u % jpe)
-  auto unit_range = [&](int& u0, int& nu) {        // 32-bit: U <= 8 slots x I / 16 units, cta < 2^16
-    const unsigned U = (unsigned)(s_nlocal * jpe);
+  // up units follow the local routed slots (known after top-k): unit u -> slot s_local[u / jpe], rows 16 (u % jpe);
+  // then the shared expert's SI / 16 units
+  auto unit_range = [&](int& u0, int& nu) {        // 32-bit: U <= 8 slots x I / 16 + SI / 16 units, cta < 2^16
+    const unsigned U = (unsigned)(s_nlocal * jpe + SI / 16);
     u0 = (int)((unsigned)cta * U / (unsigned)nb);
     nu = (int)((unsigned)(cta + 1) * U / (unsigned)nb) - u0;
   };
@@ -119,6 +139,7 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   unsigned* status = &ws->status;
   unsigned long long* lg = reinterpret_cast<unsigned long long*>(ws + 1);    // tagged logits
   unsigned long long* act_g = lg + E;                                         // tagged act pairs
+  unsigned long long* act_sh = act_g + kXMaxSlots * (I / 2);                  // the shared expert's
   uint8_t* up_base = smem;                              // [unit][gate codes | up codes | gate scales | up scales]
   uint8_t* dn_base = smem + a.off_dn;                   // [slot][codes | scales]
   bf16* xnb = reinterpret_cast<bf16*>(smem + a.off_xn);
@@ -152,27 +173,50 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
       tma_prefetch_desc(&up_s);
       tma_prefetch_desc(&dn_c);
       tma_prefetch_desc(&dn_s);
+      if (SI > 0) {
+        tma_prefetch_desc(&sh_up_c);
+        tma_prefetch_desc(&sh_up_s);
+        tma_prefetch_desc(&sh_dn_c);
+        tma_prefetch_desc(&sh_dn_s);
+      }
       if (!mbar_wait(&bar_plan, 0, status)) return;
       int u0, nu;
       unit_range(u0, nu);
+      const int routed_units = s_nlocal * jpe;
       for (int u = 0; u < nu; ++u) {
-        const int unit = u0 + u, s = s_local[unit / jpe], j = unit - (unit / jpe) * jpe;
-        const int rows_g = (s_ids[s] - a.e_lo) * 2 * I + j * 16, rows_u = rows_g + I;
+        const int unit = u0 + u;
+        const bool shared = unit >= routed_units;
+        int rows_g, rows_u;
+        if (shared) {                                   // shared expert: gate rows [0, SI), up rows [SI, 2 SI)
+          rows_g = (unit - routed_units) * 16;
+          rows_u = rows_g + SI;
+        } else {
+          const int s = s_local[unit / jpe], j = unit - (unit / jpe) * jpe;
+          rows_g = (s_ids[s] - a.e_lo) * 2 * I + j * 16;
+          rows_u = rows_g + I;
+        }
+        const CUtensorMap* mc = shared ? &sh_up_c : &up_c;
+        const CUtensorMap* ms = shared ? &sh_up_s : &up_s;
         uint8_t* b = up_base + u * a.unit_bytes;
         mbar_arrive_expect_tx(&bar_up[u], 2 * nks_u * (2048 + 256));
-        tma_load_3d(b, &up_c, 0, rows_g, 0, &bar_up[u]);
-        tma_load_3d(b + nks_u * 2048, &up_c, 0, rows_u, 0, &bar_up[u]);
-        tma_load_3d(b + 2 * nks_u * 2048, &up_s, 0, rows_g, 0, &bar_up[u]);
-        tma_load_3d(b + 2 * nks_u * 2048 + nks_u * 256, &up_s, 0, rows_u, 0, &bar_up[u]);
+        tma_load_3d(b, mc, 0, rows_g, 0, &bar_up[u]);
+        tma_load_3d(b + nks_u * 2048, mc, 0, rows_u, 0, &bar_up[u]);
+        tma_load_3d(b + 2 * nks_u * 2048, ms, 0, rows_g, 0, &bar_up[u]);
+        tma_load_3d(b + 2 * nks_u * 2048 + nks_u * 256, ms, 0, rows_u, 0, &bar_up[u]);
       }
-      if (has_dn && s_nlocal > 0) {
-        mbar_arrive_expect_tx(&bar_dn, s_nlocal * nks_d * (2048 + 256));
+      if (has_dn && (s_nlocal > 0 || SI > 0)) {
+        mbar_arrive_expect_tx(&bar_dn, (s_nlocal * nks_d + nks_sh) * (2048 + 256));
         for (int s = 0; s < topk; ++s) {
           if (s_ids[s] < a.e_lo || s_ids[s] >= a.e_hi) continue;
           const int rows = (s_ids[s] - a.e_lo) * H + cta * 16;
           uint8_t* b = dn_base + s * a.dslot_bytes;
           tma_load_3d(b, &dn_c, 0, rows, 0, &bar_dn);
           tma_load_3d(b + nks_d * 2048, &dn_s, 0, rows, 0, &bar_dn);
+        }
+        if (SI > 0) {                                   // the shared expert's 16 down rows of this block
+          uint8_t* b = smem + a.off_dn_sh;
+          tma_load_3d(b, &sh_dn_c, 0, cta * 16, 0, &bar_dn);
+          tma_load_3d(b + nks_sh * 2048, &sh_dn_s, 0, cta * 16, 0, &bar_dn);
         }
       }
     }
@@ -257,10 +301,16 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   const bool active = g == 0;
   int u0, nu;
   unit_range(u0, nu);
+  const int routed_units = s_nlocal * jpe;
   #pragma unroll 1
   for (int u = 0; u < nu; ++u) {
     if (!xsync_and(mbar_wait(&bar_up[u], 0, status))) break;
-    const int unit = u0 + u, s = s_local[unit / jpe], j = unit - (unit / jpe) * jpe, e = s_ids[s] - a.e_lo;
+    const int unit = u0 + u;
+    const bool shared = unit >= routed_units;
+    const int s = shared ? 0 : s_local[unit / jpe];
+    const int j = shared ? unit - routed_units : unit - (unit / jpe) * jpe;
+    const float g13u = shared ? a.g13_sh[0] : a.g13[s_ids[s] - a.e_lo];
+    unsigned long long* act_dst = shared ? act_sh : act_g + (int64_t)s * (I / 2);
     const uint8_t* b = up_base + u * a.unit_bytes;
     float acc_g[4][4], acc_u[4][4];
     zero_acc(acc_g);
@@ -288,12 +338,12 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
         gs += red[(0 * kXW + w) * 16 + tid];
         us += red[(1 * kXW + w) * 16 + tid];
       }
-      const float sc = ldexpf(a.g13[e], -shift_x[0]);
+      const float sc = ldexpf(g13u, -shift_x[0]);
       const float gv = gs * sc, uv = us * sc;
       const float silu = gv / (1.0f + expf(-gv));
       const unsigned vb = __bfloat16_as_ushort(__float2bfloat16_rn(silu * uv));
       const unsigned hi = __shfl_down_sync(0x0000ffffu, vb, 1);   // act pair (2i, 2i+1) -> one tagged word
-      if ((tid & 1) == 0) st_tagged(act_g + (int64_t)s * (I / 2) + (j * 16 + tid) / 2, ep, vb | (hi << 16));
+      if ((tid & 1) == 0) st_tagged(act_dst + (j * 16 + tid) / 2, ep, vb | (hi << 16));
     }
     xsync();
   }
@@ -327,6 +377,25 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
           const float sc = ldexpf(a.g2[e], -shift_a[s]);
           ybuf[s][r0] = bf16r(d[0] * sc);
           ybuf[s][r0 + 8] = bf16r(d[2] * sc);
+        }
+      } else if (SI > 0 && warp == topk) {
+        // the shared expert's 16 down rows of this block, from its act row (same accumulation as a routed slot)
+        __half* arow = reinterpret_cast<__half*>(smem + a.off_xa_sh);
+        stage_row_f16_tagged_warp(act_sh, SI, ep, arow, &shift_sh, lane, status);
+        const uint8_t* b = smem + a.off_dn_sh;
+        float acc[4][4];
+        zero_acc(acc);
+        if (__all_sync(0xffffffffu, mbar_wait(&bar_dn, 0, status))) {
+          #pragma unroll 1
+          for (int ks = 0; ks < nks_sh; ++ks) consume_stage(b + ks * 2048, b + nks_sh * 2048 + ks * 256, 0, g, t, ks, arow, g == 0, acc);
+        }
+        float d[4];
+        sum_acc(acc, d);
+        if (t == 0) {
+          const int r0 = tile_phi(g);
+          const float sc = ldexpf(a.g2_sh[0], -shift_sh);
+          ysh[r0] = bf16r(d[0] * sc);
+          ysh[r0 + 8] = bf16r(d[2] * sc);
         }
       }
       xsync();
@@ -367,7 +436,9 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
       } else if (tid < 16) {
         float acc = 0.f;
         for (int s = 0; s < topk; ++s) acc = fmaf(s_tw[s], ybuf[s][tid], acc);
-        a.out[cta * 16 + tid] = __float2bfloat16_rn(acc);
+        // with a shared expert: bf16(bf16(routed) + shared), as the chain's routed down + shared down + bf16 add
+        const float o = SI > 0 ? bf16r(acc) + ysh[tid] : acc;
+        a.out[cta * 16 + tid] = __float2bfloat16_rn(o);
       }
     }
   }
@@ -402,9 +473,17 @@ static int moe_block_launch(const void* x, int64_t ldx, const void* res, const v
                             const void* s13, const float* g13, const void* w2, const void* s2, const float* g2, int64_t I,
                             int64_t e_lo, int64_t n_local, void* out, void* y_out, void* res_out, void* xn_out,
                             float* logits_out, int32_t* topk_ids_out, float* topk_weights_out, void* workspace,
-                            const flint_l2_prefetch* next, int pdl, void* stream, const PeerSet* peers = nullptr) {
+                            const flint_l2_prefetch* next, int pdl, void* stream, const PeerSet* peers = nullptr,
+                            const void* sh_w13 = nullptr, const void* sh_s13 = nullptr, const float* sh_g13 = nullptr,
+                            const void* sh_w2 = nullptr, const void* sh_s2 = nullptr, const float* sh_g2 = nullptr,
+                            int64_t SI = 0) {
   if (!x || !norm_w || !gate_w || !w13 || !s13 || !g13 || !w2 || !s2 || !g2 || (!out && !y_out) || !workspace)
     return FLINT_ERR_ARGUMENT;
+  if (SI != 0) {                           // the shared expert: one-GPU weighted-sum mode only
+    if (!sh_w13 || !sh_s13 || !sh_g13 || !sh_w2 || !sh_s2 || !sh_g2 || !out || y_out || peers) return FLINT_ERR_ARGUMENT;
+    if (SI < kSliceK || SI % kSliceK != 0 || SI > kXMaxShared || topk >= kXW) return FLINT_ERR_SHAPE;
+    if (!aligned(sh_w13, 16) || !aligned(sh_s13, 16) || !aligned(sh_w2, 16) || !aligned(sh_s2, 16)) return FLINT_ERR_ALIGN;
+  }
   if (peers && (!out || y_out)) return FLINT_ERR_ARGUMENT;
   if (peers && (H / 16 != kPeerMoeBlocks || topk > kPeerSlots)) return FLINT_ERR_SHAPE;
   if (e_lo < 0 || n_local < 1 || e_lo + n_local > E || (y_out && !topk_weights_out)) return FLINT_ERR_ARGUMENT;
@@ -414,7 +493,7 @@ static int moe_block_launch(const void* x, int64_t ldx, const void* res, const v
       topk > kXMaxSlots || topk > E || I < kSliceK || I % kSliceK != 0 || ldx < H || score_fn < 0 || score_fn > 1 ||
       H / 16 > sms)
     return FLINT_ERR_SHAPE;
-  const int U = (int)(topk * (I / 16));
+  const int U = (int)(topk * (I / 16) + SI / 16);
   if ((U + sms - 1) / sms > kXMaxUnits) return FLINT_ERR_SHAPE;
   if (!aligned(x, 16) || ldx % 8 != 0 || (res && !aligned(res, 16)) || !aligned(norm_w, 16) || !aligned(gate_w, 16) ||
       !aligned(w13, 16) || !aligned(s13, 16) || !aligned(w2, 16) || !aligned(s2, 16) || (out && !aligned(out, 16)) ||
@@ -430,7 +509,9 @@ static int moe_block_launch(const void* x, int64_t ldx, const void* res, const v
   a.off_xn = a.off_dn + kXMaxSlots * a.dslot_bytes;
   a.off_xs = a.off_xn + (uint32_t)up((size_t)H * 2, 1024);
   a.off_xa = a.off_xs + (uint32_t)up((size_t)xs_stride((int)H) * 2, 1024);
-  a.off_red = a.off_xa + (uint32_t)up((size_t)kXMaxSlots * xs_stride((int)I) * 2, 1024);
+  a.off_dn_sh = a.off_xa + (uint32_t)up((size_t)kXMaxSlots * xs_stride((int)I) * 2, 1024);
+  a.off_xa_sh = a.off_dn_sh + (uint32_t)up((size_t)(SI / kSliceK) * (2048 + 256), 1024);
+  a.off_red = a.off_xa_sh + (uint32_t)up(SI > 0 ? (size_t)xs_stride((int)SI) * 2 : 0, 1024);
   const size_t smem = 1024 + a.off_red + 2 * kXW * 16 * 4;
   if (smem > 227 * 1024 - 2048) return FLINT_ERR_SHAPE;
 
@@ -448,6 +529,18 @@ static int moe_block_launch(const void* x, int64_t ldx, const void* res, const v
   if (!rc) rc = enc3(&dc, w2, 128, (uint64_t)n_local * H, I / 2, nks_d, true);
   if (!rc) rc = enc3(&ds, s2, 16, (uint64_t)n_local * H, I / 16, nks_d, false);
   if (rc) return rc;
+  CUtensorMap suc = uc, sus = us, sdc = dc, sds = ds;   // unused copies without a shared expert
+  if (SI > 0) {
+    const int nks_sh = (int)(SI / kSliceK);
+    rc = enc3(&suc, sh_w13, 128, (uint64_t)2 * SI, H / 2, nks_u, true);
+    if (!rc) rc = enc3(&sus, sh_s13, 16, (uint64_t)2 * SI, H / 16, nks_u, false);
+    if (!rc) rc = enc3(&sdc, sh_w2, 128, (uint64_t)H, SI / 2, nks_sh, true);
+    if (!rc) rc = enc3(&sds, sh_s2, 16, (uint64_t)H, SI / 16, nks_sh, false);
+    if (rc) return rc;
+  }
+  a.SI = (int)SI;
+  a.g13_sh = sh_g13;
+  a.g2_sh = sh_g2;
 
   a.x = (const bf16*)x; a.ldx = ldx; a.res = (const bf16*)res; a.nw = (const bf16*)norm_w; a.eps = eps;
   a.gate_w = (const bf16*)gate_w; a.E = (int)E; a.topk = (int)topk; a.score_fn = score_fn; a.H = (int)H; a.I = (int)I;
@@ -462,7 +555,8 @@ static int moe_block_launch(const void* x, int64_t ldx, const void* res, const v
   if (!l2_prefetch_pack(next, &a.pf)) return FLINT_ERR_ARGUMENT;
 
   // H = 2048: the single-pass norm keeps one 8-wide chunk per consumer thread
-  void (*kern)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, MoeBlockArgs) = moe_block_kernel<8>;
+  void (*kern)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap,
+               MoeBlockArgs) = moe_block_kernel<8>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return record_cuda(cudaGetLastError(), FLINT_ERR_LAUNCH);
   set_max_carveout(kern);
@@ -478,7 +572,7 @@ static int moe_block_launch(const void* x, int64_t ldx, const void* res, const v
   at[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 2 : 1;
-  return record_cuda(cudaLaunchKernelEx(&cfg, kern, uc, us, dc, ds, a), FLINT_ERR_LAUNCH);
+  return record_cuda(cudaLaunchKernelEx(&cfg, kern, uc, us, dc, ds, suc, sus, sdc, sds, a), FLINT_ERR_LAUNCH);
 }
 
 extern "C" int flint_moe_block(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, const void* gate_w,
@@ -490,6 +584,20 @@ extern "C" int flint_moe_block(const void* x, int64_t ldx, const void* res, cons
   return moe_block_launch(x, ldx, res, norm_w, eps, gate_w, H, E, topk, score_fn, w13, s13, g13, w2, s2, g2, I, 0, E, out,
                           nullptr, res_out, xn_out, logits_out, topk_ids_out, topk_weights_out, workspace, next, pdl,
                           stream);
+}
+
+extern "C" int flint_moe_block_shared(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps,
+                                      const void* gate_w, int64_t H, int64_t E, int64_t topk, int score_fn,
+                                      const void* w13, const void* s13, const float* g13, const void* w2, const void* s2,
+                                      const float* g2, int64_t I, const void* sh_w13, const void* sh_s13,
+                                      const float* sh_g13, const void* sh_w2, const void* sh_s2, const float* sh_g2,
+                                      int64_t SI, void* out, void* res_out, void* xn_out, float* logits_out,
+                                      int32_t* topk_ids_out, float* topk_weights_out, void* workspace,
+                                      const flint_l2_prefetch* next, int pdl, void* stream) {
+  if (SI < 1) return FLINT_ERR_SHAPE;
+  return moe_block_launch(x, ldx, res, norm_w, eps, gate_w, H, E, topk, score_fn, w13, s13, g13, w2, s2, g2, I, 0, E, out,
+                          nullptr, res_out, xn_out, logits_out, topk_ids_out, topk_weights_out, workspace, next, pdl,
+                          stream, nullptr, sh_w13, sh_s13, sh_g13, sh_w2, sh_s2, sh_g2, SI);
 }
 
 extern "C" int flint_moe_block_ep(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps,

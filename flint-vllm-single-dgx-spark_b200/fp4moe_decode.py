@@ -240,6 +240,20 @@ def moe_decode(x, res, nw, eps, gate_w, w: DecodeWeights, fused: bool = True, ex
     "block": one launch for one token with the down weights prefetched under the gate/up work (flint_moe_block).
     extras=True (fused / block) also returns (xn, logits, topk_ids, topk_weights)."""
     impl = impl or ("fused" if fused else "chain")
+    if (w.shared is not None and impl == "block" and not _routed_only and x.shape[0] == 1 and w.shared.I % 256 == 0
+            and w.shared.I <= 1024 and w.topk < 8):
+        # the shared expert inside the one-launch block (flint_moe_block_shared)
+        dev, M, H = x.device, x.shape[0], x.shape[1]
+        out = torch.empty((M, H), dtype=torch.bfloat16, device=dev)
+        res_out = torch.empty((M, H), dtype=torch.bfloat16, device=dev) if res is not None else None
+        ex = (None, torch.empty((M, w.E), dtype=torch.float32, device=dev),
+              torch.empty((M, w.topk), dtype=torch.int32, device=dev), torch.empty((M, w.topk), dtype=torch.float32, device=dev))
+        _, lg, ti, tw = ex if extras else (None, None, None, None)
+        sw = w.shared
+        torch.ops.flint_b200.moe_block_shared(x, res, nw, float(eps), gate_w, w.topk, w.score_fn, w.w13, w.s13, w.g13,
+                                              w.w2, w.s2, w.g2, sw.w13[0], sw.s13[0], sw.g13, sw.w2[0], sw.s2[0], sw.g2,
+                                              out, res_out, lg, ti, tw)
+        return (out, res_out, ex) if extras else (out, res_out)
     if w.shared is not None and impl != "chain" and not _routed_only:
         out, res_out, ex = moe_decode(x, res, nw, eps, gate_w, w, impl=impl, extras=True, _routed_only=True)
         sact = torch.empty((x.shape[0], w.shared.I), dtype=torch.bfloat16, device=x.device)

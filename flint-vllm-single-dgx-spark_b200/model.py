@@ -287,7 +287,10 @@ class Decoder:
         ep = model.world > 1
         moe_launches = (4 if ep else 3) if moe == "chain" else 2 if (ep and exchange == "nccl") else 1
         n_dense = len(c.mlp_only_layers)
-        mlp_launches = n_dense * 3 + (c.layers - n_dense) * (moe_launches + (2 if c.shared_inter else 0))
+        shared_fused = (c.shared_inter and model.world == 1 and moe == "block" and c.shared_inter % 256 == 0
+                        and c.shared_inter <= 1024 and c.topk < 8)
+        shared_launches = 0 if (not c.shared_inter or shared_fused) else 2
+        mlp_launches = n_dense * 3 + (c.layers - n_dense) * (moe_launches + shared_launches)
         self.launches_per_step = (3 if attn == "chain" else 1) * c.layers + mlp_launches + 2 + (1 if ep else 0)
 
     def trace_routing(self):
@@ -301,6 +304,13 @@ class Decoder:
         self.route_trace = torch.full((c.layers, self.M, c.topk), -1, dtype=torch.int32, device=self.m.dev)
         self.route_trace_logits = torch.zeros((c.layers, self.M, c.num_experts), dtype=torch.float32, device=self.m.dev)
         self.graphs.clear()
+
+    def shared_in_block(self, ew) -> bool:
+        """The one-launch MoE block takes the shared expert itself (flint_moe_block_shared) on one GPU when its
+        intermediate size is a multiple of 256 up to 1024 and a warp is free for it (top-k < 8)."""
+        sw = ew.shared
+        return (sw is not None and self.m.world == 1 and self.moe == "block" and sw.I % 256 == 0 and sw.I <= 1024
+                and ew.topk < 8)
 
     def _trace_copy(self, l):
         self.route_trace[l].copy_(self.ti)
@@ -367,6 +377,16 @@ class Decoder:
                 dist.all_reduce(self.y_slots, group=self.group)
                 ops.moe_combine(self.y_slots, self.tw, self.h)
             seq.append(("moe_block_ep", moe_ep))
+        elif self.moe == "block" and self.shared_in_block(ew):
+            # Flint's shared expert inside the one-launch block: out = bf16(bf16(routed) + shared)
+            sw = ew.shared
+            tr = self.route_trace is not None
+            ids_out, lg_out = (self.route_trace[l], self.route_trace_logits[l]) if tr else (None, None)
+            seq.append(("moe_block_shared", lambda: ops.moe_block_shared(
+                self.a, self.res_a, L["ln2"], c.rms_eps, L["gate"], c.topk, ew.score_fn, ew.w13, ew.s13, ew.g13,
+                ew.w2, ew.s2, ew.g2, sw.w13[0], sw.s13[0], sw.g13, sw.w2[0], sw.s2[0], sw.g2, self.h, self.res_b,
+                lg_out, ids_out, None)))
+            return seq
         elif self.moe == "block":
             xn_out = self.xn if ew.shared is not None else None      # the shared expert reads the normalised input
             tr = self.route_trace is not None

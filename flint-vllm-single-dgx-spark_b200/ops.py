@@ -362,6 +362,40 @@ def _(x, res, norm_w, eps, gate_w, topk, score_fn, w13, s13, g13, w2, s2, g2, ou
     return None
 
 
+@torch.library.custom_op(f"{NS}::moe_block_shared", mutates_args=("out", "res_out", "logits_out", "ids_out", "tw_out"))
+def moe_block_shared(x: torch.Tensor, res: torch.Tensor | None, norm_w: torch.Tensor, eps: float, gate_w: torch.Tensor,
+                     topk: int, score_fn: int, w13: torch.Tensor, s13: torch.Tensor, g13: torch.Tensor, w2: torch.Tensor,
+                     s2: torch.Tensor, g2: torch.Tensor, sw13: torch.Tensor, ss13: torch.Tensor, sg13: torch.Tensor,
+                     sw2: torch.Tensor, ss2: torch.Tensor, sg2: torch.Tensor, out: torch.Tensor,
+                     res_out: torch.Tensor | None, logits_out: torch.Tensor | None, ids_out: torch.Tensor | None,
+                     tw_out: torch.Tensor | None) -> None:
+    """moe_block with Flint's ungated shared expert in the same launch (flint_moe_block_shared): shared gate/up
+    sw13 u8 [2SI, H/2] + ss13 [2SI, H/16] + sg13 fp32 [1], down sw2 u8 [H, SI/2] + ss2 [H, SI/16] + sg2 fp32 [1];
+    out = bf16(bf16(routed) + shared)."""
+    _lib.require_cuda(x, "moe_block_shared")
+    _bf16_2d(x, "moe_block_shared x")
+    M, H = x.shape
+    E, I2, Hh = w13.shape
+    SI2 = sw13.shape[-2]
+    if M != 1 or Hh * 2 != H or gate_w.shape != (E, H) or out.shape != (1, H) or sw13.shape[-1] * 2 != H or \
+            sw2.shape[-2] != H or sw2.shape[-1] * 4 != SI2:
+        raise _lib.FlintError("moe_block_shared: one token, shapes must match the expert weights")
+    nbytes = lib().flint_moe_block_workspace_bytes(E, I2 // 2)
+    ws = _lib.workspace(x.device, f"moe_block_{E}_{I2 // 2}", nbytes)
+    rc = lib().flint_moe_block_shared(ptr(x), x.stride(0), ptr(res), ptr(norm_w), float(eps), ptr(gate_w), H, E, topk,
+                                      score_fn, ptr(_u8(w13)), ptr(_u8(s13)), ptr(g13), ptr(_u8(w2)), ptr(_u8(s2)),
+                                      ptr(g2), I2 // 2, ptr(_u8(sw13)), ptr(_u8(ss13)), ptr(sg13), ptr(_u8(sw2)),
+                                      ptr(_u8(ss2)), ptr(sg2), SI2 // 2, ptr(out), ptr(res_out), None, ptr(logits_out),
+                                      ptr(ids_out), ptr(tw_out), ptr(ws), None, PDL, stream_ptr(x.device))
+    check(rc, "flint_moe_block_shared")
+
+
+@moe_block_shared.register_fake
+def _(x, res, norm_w, eps, gate_w, topk, score_fn, w13, s13, g13, w2, s2, g2, sw13, ss13, sg13, sw2, ss2, sg2, out,
+      res_out, logits_out, ids_out, tw_out):
+    return None
+
+
 @torch.library.custom_op(f"{NS}::moe_block_ep", mutates_args=("y_out", "tw_out", "res_out"))
 def moe_block_ep(x: torch.Tensor, res: torch.Tensor | None, norm_w: torch.Tensor, eps: float, gate_w: torch.Tensor,
                  topk: int, score_fn: int, w13: torch.Tensor, s13: torch.Tensor, g13: torch.Tensor, w2: torch.Tensor,

@@ -222,6 +222,19 @@ int flint_moe_block(const void* x, int64_t ldx, const void* res, const void* nor
                     float* logits_out, int32_t* topk_ids_out, float* topk_weights_out, void* workspace,
                     const flint_l2_prefetch* next, int pdl, void* stream);
 
+/* flint_moe_block with Flint's ungated shared expert in the same launch (replaces the shared groups of the
+ * reference's up_mar / down_mar, fast/fp4moe_mar.cu:67-152, 224-231): shared gate/up sh_w13 u8 [2 SI, H/2] (gate rows
+ * first) + sh_s13 [2 SI, H/16] + sh_g13 fp32 [1], down sh_w2 u8 [H, SI/2] + sh_s2 [H, SI/16] + sh_g2 fp32 [1];
+ * out = bf16(bf16(sum_s tw_s y_s) + bf16(act_sh . W2sh * gs2sh)).  SI % 256 == 0, SI <= 1024, topk < 8; same
+ * workspace as flint_moe_block. */
+int flint_moe_block_shared(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, const void* gate_w,
+                           int64_t H, int64_t E, int64_t topk, int score_fn, const void* w13, const void* s13,
+                           const float* g13, const void* w2, const void* s2, const float* g2, int64_t I,
+                           const void* sh_w13, const void* sh_s13, const float* sh_g13, const void* sh_w2,
+                           const void* sh_s2, const float* sh_g2, int64_t SI, void* out, void* res_out, void* xn_out,
+                           float* logits_out, int32_t* topk_ids_out, float* topk_weights_out, void* workspace,
+                           const flint_l2_prefetch* next, int pdl, void* stream);
+
 /* Expert-parallel form of flint_moe_block (the MoE of a model whose experts are split over ranks): this rank's
  * weights hold experts expert_lo .. expert_lo + n_local - 1 (w13 / s13 / g13 / w2 / s2 / g2 indexed by local
  * expert); the router and top-k run in full.  Writes y_out bf16 [topk, H] (row s = y of routed slot s when its

@@ -95,6 +95,21 @@ def test_flint_layers_dispatch(rec, moe):
     assert dec.launches_per_step == 3 + 3 + 2 * (len(routed) + 2) + 2
 
 
+def test_shared_expert_inside_the_block(rec):
+    """A shared expert whose size the block takes (SI % 256 == 0, <= 1024, top-k < 8) runs inside the one-launch MoE
+    block: one launch per MoE layer, no shared up / down and no add."""
+    cfg = _small(layers=2, shared_inter=256, score="sigmoid")
+    m, dec = _model(cfg, batch=1, moe="block")
+    calls = _step_calls(rec, dec)
+    for l in range(2):
+        assert [n for n, _ in calls[l]] == ["attn_block", "moe_block_shared"]
+        a = calls[l][1][1]
+        sw = m.layers[l]["experts"].shared
+        assert a[13] is not None and torch.equal(a[13], sw.w13[0]) and torch.equal(a[16], sw.w2[0])
+        assert a[19] is dec.h and a[20] is dec.res_b
+    assert dec.launches_per_step == 2 * 2 + 2
+
+
 def test_flint_chain_attention_arguments(rec):
     cfg = _small(layers=2, layer_types=("sliding_attention", "full_attention"), sliding_window=5, no_rope_layers=(1,),
                  attn_sinks=True)

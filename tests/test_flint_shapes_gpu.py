@@ -73,6 +73,30 @@ def test_shared_expert_block_and_fused_match_chain(fb):
                           what=f"{impl} + shared vs chain")
 
 
+def test_shared_expert_inside_the_block_vs_oracle(fb):
+    """flint_moe_block_shared (one launch: routed experts + shared expert) against the oracle: the routing bit for bit
+    (the router mirror), the output within the activation tolerance of bf16(bf16(routed) + shared)."""
+    from flint_b200 import fp4moe_decode as fm
+    rng = np.random.default_rng(11)
+    R, S, w = _weights(rng)
+    x, res = bf16(rng, (1, H)), bf16(rng, (1, H))
+    nw_h = onv.bf16_round(1.0 + bf16(rng, (H,), 0.1))
+    gate_h = bf16(rng, (E, H), 0.02)
+    out, res_out, (_, lg, ti, tw) = fm.moe_decode(dev_bf16(x), dev_bf16(res), dev_bf16(nw_h), 1e-6, dev_bf16(gate_h), w,
+                                                  impl="block", extras=True)
+    torch.cuda.synchronize()
+    xn, res_ref = omoe.rmsnorm(x, res, nw_h, 1e-6)
+    np.testing.assert_array_equal(host(res_out), res_ref)
+    ids, tws = omoe.topk_route(omoe.router_logits_mirror(xn, gate_h), TOPK, 1)
+    np.testing.assert_array_equal(host(ti), ids)
+    act = omoe.experts_up(xn, ids, R["w13"], R["s13"], R["g13"])
+    routed = omoe.experts_down(act, ids, tws, R["w2"], R["s2"], R["g2"])
+    i0, w1 = _one(1)
+    sact = omoe.experts_up(xn, i0, S["w13"], S["s13"], S["g13"])
+    shared = omoe.experts_down(sact, i0, w1, S["w2"], S["s2"], S["g2"])
+    assert_bf16_close(host(out), onv.bf16_round(routed + shared), rel=2 ** -6, abs_frac=4e-3, what="block + shared")
+
+
 @pytest.mark.parametrize("M", [1, 4])
 def test_dense_mlp_vs_oracle(fb, M):
     from flint_b200 import fp4moe_decode as fm
