@@ -29,9 +29,15 @@
 #include "nvfp4_tile.cuh"
 #include "runtime.cuh"
 #include "tma.cuh"
+#include "timeline.cuh"
 
 #include <algorithm>
 #include <stdio.h>
+
+// phase stamps of development builds (-DFLINT_TIMELINE): 0 entry, 1 PDL wait done, 2 norm staged, 3 QKV rows
+// published, 4 page partition known, 5 first q heads fetched, 6 own pages done, 7 merges done, 8 O rows written;
+// producer: 10 resident weights landed, 11 last page requested
+FLINT_TL_BUFFER
 
 namespace flint {
 
@@ -191,6 +197,7 @@ __device__ __noinline__ void gemv_stream_o(const uint8_t* wc, const uint8_t* wsc
           atomicOr(status, STATUS_WAIT_TIMEOUT);
           break;
         }
+        poll_pause();
       }
       const uint4 v = make_uint4((uint32_t)w0.x, (uint32_t)w0.y, (uint32_t)w1.x, (uint32_t)w1.y);
       float f[8];
@@ -289,6 +296,7 @@ __device__ __forceinline__ void fetch_head(const unsigned long long* yrow, int h
       atomicOr(status, STATUS_WAIT_TIMEOUT);
       break;
     }
+    poll_pause();
   }
   v[0] = bf16_bits_to_f32((uint32_t)w0 & 0xFFFFu);
   v[1] = bf16_bits_to_f32(((uint32_t)w0) >> 16);
@@ -348,6 +356,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int G = gridDim.x, cta = blockIdx.x;
   const int M = MC > 0 ? MC : a.M;
+  if (threadIdx.x == 0) FLINT_TL(0);
   unsigned* status = &a.ws->status;
   uint8_t* ring = smem + a.off_ring;
   uint8_t* wq = smem;                                  // QKV weights (phase A), then warp partials (phase B)
@@ -394,6 +403,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
     }
   }
   pdl_wait();
+  if (threadIdx.x == 0) FLINT_TL(1);
   unsigned ep;                                         // this launch's tag (the last CTA to retire advances it)
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(ep) : "l"(&a.ws->epoch) : "memory");
   ep += 1u;
@@ -410,6 +420,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
     if ((int)threadIdx.x < M) s_seq[threadIdx.x] = my_seq;
   }
   __syncthreads();
+  if (threadIdx.x == 0) FLINT_TL(2);
   if (threadIdx.x == 0) {                              // page partition inputs
     int pre = 0;
     for (int b = 0; b < M; ++b) {
@@ -540,6 +551,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
     // (they are needed first; the pages then stream in under the QKV GEMV and the barrier) ----
     if (lane == 0) {
       if (ngq > 0 && !mbar_wait(&bar_wq, 0, status)) return;
+      FLINT_TL(10);
       int j = 0;
       for (int s = 0; s < S; ++s) {
         const int b = s / a.nkv, kvh = s - b * a.nkv;
@@ -554,6 +566,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
           tma_load_5d(ring + slot * kBPageBytes, &mkv, 0, 0, 0, kvh, blk, &full[slot]);
         }
       }
+      FLINT_TL(11);
     }
     return;
   }
@@ -565,7 +578,9 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
     cons_sync();
     gemv_finish_tagged(red, ngq, M, a.gs_qkv[0], shift, a.y_tag, a.Nqkv / 2, gq0 * 16, ep);
   }
+  if (threadIdx.x == 0) FLINT_TL(3);
   const bool have_tab = cons_sync_and(mbar_wait(&bar_tab, 0, status));   // segment tables from the producer warp
+  if (threadIdx.x == 0) FLINT_TL(4);
   const int lo = s_lo, hi = s_hi;
 
   // ---- B: attention ----
@@ -633,6 +648,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
       for (int i = 0; i < 4; ++i) q_tile[warp][pdim(lane, i)] = __float2bfloat16_rn(q[i]);
     }
     cons_sync();
+    if (threadIdx.x == 0 && j == 0) FLINT_TL(5);
     uint32_t qa[8][2];
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) {
@@ -795,6 +811,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
     }
   }
   cons_sync();
+  if (threadIdx.x == 0) FLINT_TL(6);
 
   // ---- B2: merge the partial records of each split segment without a grid barrier.  The CTAs holding the last
   // nm = min(n, Gq) of the segment's n tickets merge it, merger j taking q heads j, j + nm, ...; each waits until all
@@ -819,6 +836,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
             ok = 0;
             break;
           }
+          poll_pause();
         }
         __threadfence();
         s_go = ok;
@@ -906,6 +924,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
       cons_sync();                                                   // s_go is rewritten for the next ticket
     }
   }
+  if (threadIdx.x == 0) FLINT_TL(7);
   pdl_trigger();
 
   // ---- C: O projection from the resident weights, each warp's K slices staged as their heads arrive ----
@@ -919,6 +938,7 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
       gemv_finish(red, ngo, M, a.gs_o[0], shift, a.out, a.ldr, go0 * 16);
     }
   }
+  if (threadIdx.x == 0) FLINT_TL(8);
   grid_sync_retire(&a.ws->gs, G, &a.ws->epoch);
 }
 
@@ -1095,3 +1115,5 @@ extern "C" int flint_attn_block(const void* x, int64_t ldx, const int32_t* token
   cfg.numAttrs = pdl ? 2 : 1;
   return record_cuda(cudaLaunchKernelEx(&cfg, kern, mqc, mqs, moc, mos, mkv, a), FLINT_ERR_LAUNCH);
 }
+
+FLINT_TL_READER(flint_timeline_attn_block)

@@ -42,8 +42,13 @@
 #include "peer.cuh"
 #include "tagged.cuh"
 #include "runtime.cuh"
+#include "timeline.cuh"
 
 #include <algorithm>
+
+// phase stamps of development builds (-DFLINT_TIMELINE): 0 entry, 1 PDL wait done, 2 norm + router rows published,
+// 3 top-k known, 4 up units done, 5 down rows done, 6 output written; producer: 10 plan received, 11 loads issued
+FLINT_TL_BUFFER
 
 namespace flint {
 
@@ -126,6 +131,7 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nb = gridDim.x, cta = blockIdx.x;
   const int E = a.E, I = a.I, topk = a.topk, SI = a.SI;
+  if (tid == 0) FLINT_TL(0);
   const int nks_u = H / kSliceK, nks_d = I / kSliceK, jpe = I / 16, nks_sh = SI / kSliceK;
   const bool has_dn = cta < H / 16;
   // up units follow the local routed slots (known after top-k): unit u -> slot s_local[u / jpe], rows 16 (u % jpe);
@@ -164,7 +170,12 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
 #pragma unroll
     for (int i = 0; i < NV; ++i) wv[i] = ldg_stream_v4(wp + lane + 32 * i);
   }
+  // the next op's bytes (its weights, the KV pages it reads) into L2 while this kernel's routing runs: HBM is idle
+  // until the expert weights are requested.  Only bytes no pending kernel writes are named here (the next layer's
+  // weights and KV pages, block tables and sequence lengths are final before this step's first kernel).
+  if (warp == kXW && lane == 0) l2_prefetch_share(a.pf, cta, nb);
   pdl_wait();
+  if (tid == 0) FLINT_TL(1);
 
   if (warp == kXW) {
     // ---- producer: once the routing is known, this CTA's up units and down block ----
@@ -180,6 +191,7 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
         tma_prefetch_desc(&sh_dn_s);
       }
       if (!mbar_wait(&bar_plan, 0, status)) return;
+      FLINT_TL(10);
       int u0, nu;
       unit_range(u0, nu);
       const int routed_units = s_nlocal * jpe;
@@ -219,6 +231,7 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
           tma_load_3d(b + nks_sh * 2048, &sh_dn_s, 0, cta * 16, 0, &bar_dn);
         }
       }
+      FLINT_TL(11);
     }
     return;
   }
@@ -247,6 +260,7 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
     if (lane == 0) st_tagged(lg + my_row, ep, __float_as_uint(bf16r(acc)));
   }
   stage_rows_f16(xnb, H, 1, H, xs, shift_x, red_n, kXT, 1);
+  if (tid == 0) FLINT_TL(2);
 
   // ---- U: top-k once every CTA's router rows carry this launch's tag (no grid barrier), then the up units ----
   if (warp == 0) {
@@ -265,6 +279,7 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
         atomicOr(status, STATUS_WAIT_TIMEOUT);
         break;
       }
+      if (it > 0) poll_pause();
 #pragma unroll
       for (int j = 0; j < PER; ++j)
         if ((need & ~got) & (1u << j)) {
@@ -295,6 +310,7 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   if (cta == 0 && a.logits_out)                         // every tag was seen by warp 0 before the xsync
     for (int i = tid; i < E; i += kXT) a.logits_out[i] = __uint_as_float((uint32_t)ld_tagged(lg + i));
   if (tid == 0) mbar_arrive(&bar_plan);                 // release the producer
+  if (tid == 0) FLINT_TL(3);
 
   const int g = lane >> 2, t = lane & 3;
   const __half* xrow = xs;                              // token 0 (lanes g > 0 feed zero columns)
@@ -347,9 +363,8 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
     }
     xsync();
   }
+  if (tid == 0) FLINT_TL(4);
   pdl_trigger();
-  // the next op's bytes into L2: HBM is idle from here on (the down weights were requested with the up units)
-  if (tid == 32) l2_prefetch_share(a.pf, cta, nb);
 
   // ---- D: this CTA's 16 output rows over every routed expert, then the slot-order sum ----
   if (has_dn) {
@@ -399,6 +414,7 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
         }
       }
       xsync();
+      if (tid == 0) FLINT_TL(5);
       if (a.y_out) {
         for (int i = tid; i < topk * 16; i += kXT)
           a.y_out[(int64_t)(i >> 4) * H + cta * 16 + (i & 15)] = __float2bfloat16_rn(ybuf[i >> 4][i & 15]);
@@ -442,6 +458,7 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
       }
     }
   }
+  if (tid == 0) FLINT_TL(6);
   grid_sync_retire(&ws->sync, nb, &ws->epoch, a.peer_mode ? &peer_header(a.peers.base[a.peers.rank])->moe_epoch : nullptr);
 }
 
@@ -632,3 +649,5 @@ extern "C" int flint_moe_block_peer(const void* x, int64_t ldx, const void* res,
                           n_local, out, nullptr, res_out, nullptr, nullptr, nullptr, nullptr, workspace, next, pdl, stream,
                           &ps);
 }
+
+FLINT_TL_READER(flint_timeline_moe_block)

@@ -7,6 +7,7 @@
 // STATUS_WAIT_TIMEOUT and goes on with what it has.
 #pragma once
 #include "common.cuh"
+#include "timeline.cuh"
 #include "tma.cuh"
 
 namespace flint {
@@ -62,6 +63,7 @@ __device__ __forceinline__ void stage_row_f16_tagged_warp(const unsigned long lo
         }
       }
     }
+    if (got != need) poll_pause();
   }
   unsigned mxb = 0u;
 #pragma unroll

@@ -109,6 +109,13 @@ struct L2Prefetch {
   const uint8_t* ptr[8];
   unsigned long long n16[8];           // 16-byte units of each range
   int n;
+  // paged KV pages (kv != nullptr): see flint_l2_prefetch
+  const uint8_t* kv;
+  unsigned long long block_bytes, kv_blocks;
+  const int* bt;
+  long long bt_stride;
+  int bt_cols, streams, block_tokens, max_blocks;
+  const int* seq_lens;
 };
 
 // Host: validates and converts the ABI struct (NULL or n = 0: nothing); false on a bad range.
@@ -122,18 +129,56 @@ inline bool l2_prefetch_pack(const flint_l2_prefetch* in, L2Prefetch* out) {
     out->n16[r] = (unsigned long long)in->bytes[r] >> 4;
   }
   out->n = in->n;
+  if (in->kv) {
+    if (!in->block_tables || !in->seq_lens || in->streams < 1 || in->streams > 8 || in->block_tokens < 1 ||
+        in->block_bytes < 16 || (in->block_bytes & 15) || in->kv_blocks < 1 || in->bt_cols < 1 ||
+        in->bt_stride < in->bt_cols || in->max_blocks < 0 || (reinterpret_cast<uintptr_t>(in->kv) & 15))
+      return false;
+    out->kv = static_cast<const uint8_t*>(in->kv);
+    out->block_bytes = (unsigned long long)in->block_bytes;
+    out->kv_blocks = (unsigned long long)in->kv_blocks;
+    out->bt = in->block_tables;
+    out->bt_stride = in->bt_stride;
+    out->bt_cols = (int)(in->bt_cols < (1 << 30) ? in->bt_cols : (1 << 30));
+    out->seq_lens = in->seq_lens;
+    out->streams = in->streams;
+    out->block_tokens = in->block_tokens;
+    out->max_blocks = in->max_blocks;
+  }
   return true;
 }
 
-// One thread: this CTA's 1/nb share of every range, as bulk L2 prefetches of at most 32 KB.
+__device__ __forceinline__ void l2_prefetch_bulk(const uint8_t* p, unsigned long long bytes) {
+  for (unsigned long long u = 0; u < bytes; u += 32768) {
+    const unsigned long long k = bytes - u < 32768 ? bytes - u : 32768;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p + u), "r"((uint32_t)k) : "memory");
+  }
+}
+
+// One thread: this CTA's 1/nb share of every range, as bulk L2 prefetches of at most 32 KB, then its share of the
+// KV pages.  The page list reads seq_lens / block tables: the caller issues this only where they are final.
 __device__ __forceinline__ void l2_prefetch_share(const L2Prefetch& pf, int cta, int nb) {
   for (int r = 0; r < pf.n; ++r) {
     const unsigned long long lo = pf.n16[r] * cta / nb, hi = pf.n16[r] * (cta + 1) / nb;
-    for (unsigned long long u = lo; u < hi; u += 2048) {
-      const unsigned long long k = hi - u < 2048 ? hi - u : 2048;
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(pf.ptr[r] + u * 16), "r"((uint32_t)(k * 16))
-                   : "memory");
-    }
+    if (hi > lo) l2_prefetch_bulk(pf.ptr[r] + lo * 16, (hi - lo) * 16);
+  }
+  if (pf.kv == nullptr) return;
+  int npg[8], total = 0;
+  for (int b = 0; b < pf.streams; ++b) {
+    const int seq = pf.seq_lens[b];
+    int n = seq > 0 ? (seq + pf.block_tokens - 1) / pf.block_tokens : 0;
+    if (n > pf.bt_cols) n = pf.bt_cols;
+    npg[b] = n;
+    total += n;
+  }
+  if (total > pf.max_blocks) total = pf.max_blocks;
+  const int lo = (int)((long long)total * cta / nb), hi = (int)((long long)total * (cta + 1) / nb);
+  int b = 0, base = 0;
+  for (int i = lo; i < hi; ++i) {
+    while (b < pf.streams && i >= base + npg[b]) base += npg[b++];
+    if (b >= pf.streams) break;
+    const int blk = pf.bt[(long long)b * pf.bt_stride + (i - base)];
+    if (blk >= 0 && (unsigned long long)blk < pf.kv_blocks) l2_prefetch_bulk(pf.kv + (unsigned long long)blk * pf.block_bytes, pf.block_bytes);
   }
 }
 

@@ -363,6 +363,8 @@ class Decoder:
         if self.prefetch and l + 1 < c.layers:
             Ln = m.layers[l + 1]
             pf = _ops.prefetch_ranges(Ln["qkv"][0], Ln["qkv"][1], Ln["o"][0], Ln["o"][1])
+            if self.prefetch == "kv":     # and the pages its attention reads, up to a quarter of L2
+                pf += _ops.prefetch_kv(m.kv[l + 1], self.bt, self.seq_lens, (32 << 20) // (m.kv[l + 1].stride(0) * 2))
         if self.moe == "block" and m.world > 1 and self.peers is not None:
             pp = self.peers
             seq.append(("moe_block_peer", lambda: ops.moe_block_peer(

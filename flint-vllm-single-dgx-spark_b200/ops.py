@@ -445,20 +445,47 @@ def _(y, tw, out):
 
 class _L2Prefetch(ctypes.Structure):
     """flint_l2_prefetch (include/flint_b200.h)."""
-    _fields_ = [("ptr", ctypes.c_void_p * 8), ("bytes", ctypes.c_int64 * 8), ("n", ctypes.c_int32)]
+    _fields_ = [("ptr", ctypes.c_void_p * 8), ("bytes", ctypes.c_int64 * 8), ("n", ctypes.c_int32),
+                ("kv", ctypes.c_void_p), ("block_bytes", ctypes.c_int64), ("kv_blocks", ctypes.c_int64),
+                ("block_tables", ctypes.c_void_p), ("bt_stride", ctypes.c_int64), ("bt_cols", ctypes.c_int64),
+                ("seq_lens", ctypes.c_void_p), ("streams", ctypes.c_int32), ("block_tokens", ctypes.c_int32),
+                ("max_blocks", ctypes.c_int32)]
+
+
+_KV_TAG = -1          # starts the paged-KV part of a prefetch spec (prefetch_kv)
 
 
 def _prefetch_arg(spec: list[int] | None):
-    """[ptr0, bytes0, ptr1, bytes1, ...] -> (struct kept alive by the caller, pointer argument) or (None, None)."""
+    """[ptr0, bytes0, ptr1, bytes1, ...] (+ a prefetch_kv tail) -> (struct kept alive by the caller, pointer
+    argument) or (None, None)."""
     if not spec:
         return None, None
+    kv = None
+    if _KV_TAG in spec:
+        i = spec.index(_KV_TAG)
+        spec, kv = spec[:i], spec[i + 1:]
+        if len(kv) != 10:
+            raise _lib.FlintError("prefetch: malformed paged-KV part")
     if len(spec) % 2 or len(spec) > 16:
         raise _lib.FlintError("prefetch: up to 8 (pointer, bytes) pairs")
     pf = _L2Prefetch()
     pf.n = len(spec) // 2
     for i in range(pf.n):
         pf.ptr[i], pf.bytes[i] = spec[2 * i], spec[2 * i + 1]
+    if kv is not None:
+        (pf.kv, pf.block_bytes, pf.kv_blocks, pf.block_tables, pf.bt_stride, pf.bt_cols, pf.seq_lens, pf.streams,
+         pf.block_tokens, pf.max_blocks) = kv
     return pf, ctypes.cast(ctypes.pointer(pf), ctypes.c_void_p)
+
+
+def prefetch_kv(kv: torch.Tensor, block_tables: torch.Tensor, seq_lens: torch.Tensor, max_blocks: int) -> list[int]:
+    """The paged-KV part of a prefetch spec: the pages of kv (HND [blocks, kv_heads, block_tokens, 2 D], whole blocks)
+    that streams 0 .. len(seq_lens) - 1 will read, at most max_blocks blocks; append to prefetch_ranges(...)."""
+    if kv.dim() != 4 or not kv.is_contiguous() or block_tables.dtype != torch.int32 or seq_lens.dtype != torch.int32:
+        raise _lib.FlintError("prefetch_kv: contiguous HND cache, int32 block tables and sequence lengths")
+    blk = kv.stride(0) * kv.element_size()
+    return [_KV_TAG, kv.data_ptr(), blk, kv.shape[0], block_tables.data_ptr(), block_tables.stride(0),
+            block_tables.shape[1], seq_lens.data_ptr(), seq_lens.numel(), kv.shape[2], int(max_blocks)]
 
 
 def prefetch_ranges(*tensors: torch.Tensor) -> list[int]:

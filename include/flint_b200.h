@@ -41,11 +41,24 @@ enum {
 
 /* L2 prefetch hint: up to 8 device byte ranges (16-byte aligned; a tail below 16 bytes is skipped) that a kernel
  * taking one prefetches into L2 for the op that follows it -- in a decode step, the next layer's weights, whose
- * loads otherwise start only when the next kernel's blocks become resident.  Pure hint: no effect on results. */
+ * loads otherwise start only when the next kernel's blocks become resident -- plus, when kv is not NULL, the pages
+ * of a paged KV cache that the next attention will read: blocks block_tables[b * bt_stride + p] for
+ * p < min(ceil(seq_lens[b] / block_tokens), bt_cols), b < streams, each block_bytes long at kv + block * block_bytes
+ * (blocks outside [0, kv_blocks) are skipped), at most max_blocks blocks in all.  Pure hint: no effect on results. */
 typedef struct flint_l2_prefetch {
   const void* ptr[8];
   int64_t bytes[8];
   int32_t n;
+  const void* kv;
+  int64_t block_bytes;
+  int64_t kv_blocks;
+  const int32_t* block_tables;
+  int64_t bt_stride;
+  int64_t bt_cols;
+  const int32_t* seq_lens;
+  int32_t streams;
+  int32_t block_tokens;
+  int32_t max_blocks;
 } flint_l2_prefetch;
 
 /* Library version (major*10000 + minor*100 + patch). */
