@@ -14,10 +14,14 @@ roofline   the kernel with the largest share of the step: algorithmic bytes / CU
            its 48 per-layer launches) vs the measured HBM copy peak; roofline_kernels has every kernel
 cpu_baseline  the CPU oracle port of the reference's torch path on a bounded sample (rank 0, N = 1)
 
-With N > 1 (torchrun) the model is split over the N GPUs: expert parallelism for the MoE (each GPU holds E/N
-experts of every layer; per layer the local experts' slot rows are summed over the GPUs with NCCL and combined in
-slot order) and vocabulary sharding for the LM head (per-shard argmax keys, NCCL MAX); attention, router and norms
-are replicated.  One stream is decoded by all N GPUs together (strong scaling); results are bit-identical to 1 GPU.
+With N > 1 (torchrun) the model is split over the N GPUs and each GPU serves one stream (--multi dp, the default:
+weak scaling, value = the N streams' tokens per second): data-parallel attention (each GPU its own stream and KV
+cache, attention weights replicated), expert parallelism for the MoE (each GPU holds E/N experts of every layer; per
+layer the ranks all-gather their tokens, route all of them identically, compute their local experts' routes and
+reduce-scatter the per-route rows back to each token's rank) and vocabulary sharding for the LM head (every token
+through each rank's shard, argmax keys reduced with MAX).  Each stream is bit-identical to the one-GPU chain decode.
+--multi ep: one stream decoded by all N GPUs together (strong scaling), experts and vocabulary sharded, attention
+replicated.
 """
 from __future__ import annotations
 
@@ -122,7 +126,7 @@ def kernel_rooflines(model, dec, peak, peak_kind, ctx, step_us):
     L = model.cfg.layers
     st = torch.cuda.current_stream()
     out = {}
-    for name in [n for n, _ in dec.layer_ops(0)] + ["head"]:
+    for name in [n for n, _ in dec.layer_ops(0) if not n.startswith("dp_")] + ["head"]:
         fns = [dec.head_op()] * 20 if name == "head" else [dict(dec.layer_ops(l))[name] for l in range(L)]
         for fn in fns[:3]:
             fn()
@@ -162,14 +166,16 @@ def run_ours(args):
     steps, warm, plen = args.steps, args.warmup, args.prompt
     max_ctx = plen + warm + 2 * steps + 16
     M = args.streams
+    dp = world > 1 and args.multi == "dp"
     model = FlintModel(cfg, dev, seed=1234, max_ctx=max_ctx, max_batch=M, shard=(rank, world))
     sampling = (dict(temperature=1.0, top_k=20, top_p=0.95, seeds=[1000 + i for i in range(M)]) if args.sample
                 else None)
-    dec = Decoder(model, batch=M, moe=args.moe, attn=args.attn, group=dist.group.WORLD if dist else None,
-                  exchange=args.exchange, sampling=sampling)
+    dec = Decoder(model, batch=M, moe=None if dp else args.moe, attn=args.attn,
+                  group=dist.group.WORLD if dist else None, exchange=args.exchange, sampling=sampling, dp=dp)
     dec.reserve_history(warm + steps)
     dec.capture()
-    prompt = np.random.default_rng(7).integers(0, cfg.vocab, size=(M, plen))
+    # one prompt per stream; with --multi dp each rank decodes its own stream
+    prompt = np.random.default_rng(7 + (rank if dp else 0)).integers(0, cfg.vocab, size=(M, plen))
     fill = dec.prefill if args.prefill == "teacher" else dec.fill_kv_random
     t0 = time.time()
     fill(prompt)
@@ -212,14 +218,15 @@ def run_ours(args):
     if dist:
         t = torch.tensor([e2e_s], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_val = M * e2e_steps / float(t.item())
+        e2e_val = (M * world if dp else M) * e2e_steps / float(t.item())
 
     peak, peak_kind = measured_peak()
     mean_ctx = plen + warm + steps / 2
     # every rank times the kernels in lockstep (the sharded MoE and head contain collectives); rank 0 reports
     kernels = kernel_rooflines(model, dec, peak, peak_kind, int(mean_ctx), ms * 1e3 / steps)
     roof = max(kernels.values(), key=lambda r: r["share_of_step"]) if kernels else None
-    value = M * steps / (ms / 1e3)      # tokens of all streams, decoded by all the GPUs together
+    streams_total = M * world if dp else M
+    value = streams_total * steps / (ms / 1e3)      # tokens of all streams (every rank's under --multi dp)
     wbytes = cfg.weight_bytes_per_token()
     kv_bytes = cfg.layers * int(mean_ctx) * cfg.num_kv_heads * 2 * cfg.head_dim * 2
     total, active = cfg.param_counts()
@@ -240,24 +247,28 @@ def run_ours(args):
         line = {
             "metric": metric,
             "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warm,
-            "ms_per_step": round(ms / steps, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "ms_per_step": round(ms / steps, 4), "higher_is_better": True,
+            "scaling": "weak" if dp else "strong", "vs_baseline": None,
             "dtype": "nvfp4 weights (e2m1+e4m3), bf16 activations, fp32 accumulate", "data": "synthetic",
-            "config": {"workload": workload, "streams": M, "sampling": sampling and {k: v for k, v in sampling.items()
+            "config": {"workload": workload, "streams": streams_total, "sampling": sampling and {k: v for k, v in sampling.items()
                                                                                       if k != "seeds"},
                        "layers": cfg.layers, "hidden": cfg.hidden, "experts": cfg.num_experts, "topk": cfg.topk,
                        "moe_inter": cfg.moe_inter, "vocab": cfg.vocab, "prompt_tokens": plen,
                        "prefill": args.prefill, "moe_path": dec.moe, "attn_path": dec.attn_mode,
                        "params_total": total, "params_active": active, "weight_bytes_per_token": wbytes,
                        "kv_bytes_per_token_mean": kv_bytes,
-                       "parallelism": f"ep{world} + vocab{world} (attention replicated)" if world > 1 else "1 GPU",
-                       "exchange": (("in-kernel NVLink peer stores" if args.exchange == "peer" else "NCCL all-reduce")
-                                    if world > 1 else None),
+                       "parallelism": (f"dp{world} attention (one stream per GPU) + ep{world} experts + vocab{world} head"
+                                       if dp else f"ep{world} + vocab{world} (attention replicated)" if world > 1
+                                       else "1 GPU"),
+                       "exchange": ("NCCL all-gather of the tokens + reduce-scatter of the per-route rows per layer"
+                                    if dp else ("in-kernel NVLink peer stores" if args.exchange == "peer"
+                                                else "NCCL all-reduce") if world > 1 else None),
                        "l2": "no flush: 1.73 GB of weights streamed per step (> 126 MB L2)",
                        "prefill_s": round(prefill_s, 2)},
             "bound_tok_s": {"weights_only": round(peak * 1e9 / wbytes, 1),
                             "weights_plus_kv": round(peak * 1e9 / (wbytes + kv_bytes), 1), "peak_GBps": peak},
             "e2e": {"value": round(e2e_val, 2), "unit": "tok/s", "steps": e2e_steps,
-                    "h2d_bytes_per_step": M * (4 + 8 + 4 + 8), "d2h_bytes_per_step": M * 4},
+                    "h2d_bytes_per_step": streams_total * (4 + 8 + 4 + 8), "d2h_bytes_per_step": streams_total * 4},
             "gpu_launches": dec.launches_per_step * steps,
             "roofline": roof, "roofline_kernels": kernels, "cpu_baseline": cpu, "clocks": clk.summary(),
             "tokens_head": tokens[0, :8].tolist(),
@@ -330,6 +341,9 @@ def main():
     ap.add_argument("--prefill", default="teacher", choices=["teacher", "kv"],
                     help="teacher: prompt run through the decode kernels; kv: KV cache filled with seeded N(0,1) "
                          "(profiling runs)")
+    ap.add_argument("--multi", default="dp", choices=["dp", "ep"],
+                    help="N > 1: one stream per GPU (data-parallel attention + expert-parallel MoE, weak scaling) or "
+                         "one stream over all GPUs (expert parallel, attention replicated, strong scaling)")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="N > 1: MoE / head exchange fused into the kernels over NVLink peer memory, or NCCL calls")
     ap.add_argument("--streams", type=int, default=1, help="concurrent streams (1..8; BASELINE configs[4])")

@@ -204,21 +204,36 @@ class Decoder:
     """Batch-M (M <= 8) decode of a FlintModel: teacher-forced prompt processing and greedy generation."""
 
     def __init__(self, model: FlintModel, batch: int = 1, moe: str | None = None, attn: str = "block", group=None,
-                 exchange: str = "peer", prefetch: bool = False, sampling: dict | None = None):
+                 exchange: str = "peer", prefetch: bool = False, sampling: dict | None = None, dp: bool = False):
         """moe: "block" (one launch, one token; the default at batch 1), "chain" (route, up, down: three launches;
         the default for 2..8 tokens) or "fused" (one persistent launch for 1..8 tokens); attn: "block" (QKV +
         attention + O in one persistent launch) or "chain" (three launches).  sampling: None for greedy decode, or
         {"temperature", "top_k", "top_p", "seeds"} (one int64 seed per stream) for the seeded top-k -> top-p draw of
-        flint_lm_head_nv4_sample; the draw of step t uses the Philox counter (t, stream)."""
+        flint_lm_head_nv4_sample; the draw of step t uses the Philox counter (t, stream).
+
+        dp=True (a sharded model, one stream per GPU): data-parallel attention with expert-parallel MoE.  Each rank
+        decodes its own stream (its own KV cache, the attention weights replicated); per layer the ranks all-gather
+        their attention outputs and residuals, route all the ranks' tokens identically, compute the routes whose
+        expert is local (moe_up_ep / moe_down_ep), reduce-scatter the per-route rows (each element has one non-zero
+        term, so the sum is exact) and combine their own token's rows; the vocabulary-sharded head takes every rank's
+        hidden state and a MAX all-reduce of the argmax keys.  Each rank's stream equals the one-GPU chain decode of
+        that stream bit for bit."""
         # measured per layer at 6K context: one stream, the block; 2..5 streams, the chain (67.7 us at 4 against the
         # fused launch's 70.9); 6..8, the fused launch (118 us at 8 against the chain's 135).  Sharded: block or chain.
+        if dp:
+            if model.world < 2 or group is None or batch != 1:
+                raise ValueError("dp=True decodes one stream per GPU of a sharded model and needs its process group")
+            if sampling is not None or model.cfg.shared_inter or model.cfg.mlp_only_layers or attn != "block":
+                raise ValueError("dp=True: greedy decode of the BASELINE layer structure with the attention block")
+            moe = "dp"
+        self.dp = dp
         sharded_shared = model.world > 1 and model.cfg.shared_inter > 0
         moe = moe or ("block" if batch == 1 and not sharded_shared else
                       "chain" if batch <= 5 or model.world > 1 else "fused")
         if sharded_shared and moe != "chain":
             # the shared expert reads the normalised input, which the sharded block launches do not write out
             raise ValueError("a sharded model with a shared expert decodes with moe='chain'")
-        if moe not in ("block", "chain", "fused"):
+        if moe not in ("block", "chain", "fused", "dp"):
             raise ValueError(f"moe must be 'block', 'chain' or 'fused', got {moe!r}")
         if moe == "block" and batch != 1:
             raise ValueError("moe='block' decodes one token; use 'chain' or 'fused' for batches")
@@ -228,7 +243,7 @@ class Decoder:
             raise ValueError(f"exchange must be 'peer' or 'nccl', got {exchange!r}")
         self.group, self.exchange, self.prefetch = group, exchange, prefetch
         self.peers = None
-        if model.world > 1 and exchange == "peer":
+        if model.world > 1 and exchange == "peer" and not dp:
             from .peer import PeerBuffers
             self.peers = PeerBuffers(group, model.cfg.hidden)
         if attn not in ("block", "chain"):
@@ -273,6 +288,21 @@ class Decoder:
             self.dact = e(M, c.dense_inter)
         if c.shared_inter:
             self.sact, self.ys = e(M, c.shared_inter), e(M, c.hidden)
+        if dp:
+            # exchange buffers: the attention output and residual of this rank's token side by side, every rank's
+            # pair after the all-gather, then the routing, activations and per-route rows of all N tokens
+            N, r = model.world, model.rank
+            self.dp_send = e(2, c.hidden)
+            self.a, self.res_a = self.dp_send[0:1], self.dp_send[1:2]
+            self.dp_recv = e(N, 2, c.hidden)
+            self.dp_xn, self.dp_res = e(N, c.hidden), e(N, c.hidden)
+            self.dp_lg = e(N, c.num_experts, dt=torch.float32)
+            self.dp_ti, self.dp_tw = e(N, c.topk, dt=torch.int32), e(N, c.topk, dt=torch.float32)
+            self.dp_act, self.dp_y = e(N * c.topk, c.moe_inter), e(N * c.topk, c.hidden)
+            self.dp_mine = e(c.topk, c.hidden)
+            self.res_b = self.dp_res[r:r + 1]
+            self.dp_hsend, self.dp_hrecv = e(2, c.hidden), e(N, 2, c.hidden)
+            self.dp_keys = torch.zeros((N,), dtype=torch.int64, device=dev)
         self.route_trace = None          # trace_routing(): [layers, M, topk] int32, each MoE layer's chosen experts
         self.route_trace_logits = None   # ... and [layers, M, E] fp32, its router logits
         self.dummy_f = e(1, 1, dt=torch.float32)
@@ -285,7 +315,7 @@ class Decoder:
         # (peer exchange: the MoE block exchanges in-kernel; the head adds one exchange kernel)
         # dense layers: route + up + down; the shared expert: up + down (its bf16 add is a torch elementwise op)
         ep = model.world > 1
-        moe_launches = (4 if ep else 3) if moe == "chain" else 2 if (ep and exchange == "nccl") else 1
+        moe_launches = (4 if ep else 3) if moe == "chain" else 2 if (ep and exchange == "nccl") else 4 if moe == "dp" else 1
         n_dense = len(c.mlp_only_layers)
         shared_fused = (c.shared_inter and model.world == 1 and moe == "block" and c.shared_inter % 256 == 0
                         and c.shared_inter <= 1024 and c.topk < 8)
@@ -347,6 +377,22 @@ class Decoder:
                                                               self.seq_lens, sinks, window, self.scale, self.attn,
                                                               self.splits)),
                    ("o", lambda: ops.attn_o(self.attn.view(self.M, -1), Po, So, gso, self.a))]
+        if self.dp:
+            import torch.distributed as dist
+            N, r = m.world, m.rank
+            x_all, res_all = self.dp_recv[:, 0], self.dp_recv[:, 1]
+            seq += [("dp_gather", lambda: dist.all_gather_into_tensor(self.dp_recv.view(-1), self.dp_send.view(-1),
+                                                                       group=self.group)),
+                    ("route", lambda: ops.moe_route(x_all, res_all, L["ln2"], c.rms_eps, L["gate"], c.topk, ew.score_fn,
+                                                    self.dp_lg, self.dp_ti, self.dp_tw, self.dp_xn, self.dp_res, True,
+                                                    True)),
+                    ("up_ep", lambda: ops.moe_up_ep(self.dp_xn, self.dp_ti, ew.w13, ew.s13, ew.g13, c.num_experts,
+                                                    m.e_lo, self.dp_act)),
+                    ("down_ep", lambda: ops.moe_down_ep(self.dp_act, self.dp_ti, ew.w2, ew.s2, ew.g2, c.num_experts,
+                                                        m.e_lo, self.dp_y)),
+                    ("dp_scatter", lambda: dist.reduce_scatter_tensor(self.dp_mine, self.dp_y, group=self.group)),
+                    ("combine", lambda: ops.moe_combine(self.dp_mine, self.dp_tw[r:r + 1], self.h))]
+            return seq
         if c.is_dense(l):
             # dense SwiGLU: the route kernel's add + RMSNorm (an all-zero 32-way router sends every token to expert
             # 0 with weight 1), then the one-expert up and down
@@ -442,6 +488,21 @@ class Decoder:
     def head_op(self):
         P, S, gs = self.m.head
         ops = torch.ops.flint_b200
+        if self.dp:
+            import torch.distributed as dist
+            r = self.m.rank
+            x_all, res_all = self.dp_hrecv[:, 0], self.dp_hrecv[:, 1]
+
+            def head_dp():
+                # every rank's (h, res) pair, this rank's vocabulary shard for all of them, the MAX of the keys
+                self.dp_hsend[0].copy_(self.h[0])
+                self.dp_hsend[1].copy_(self.res_b[0])
+                dist.all_gather_into_tensor(self.dp_hrecv.view(-1), self.dp_hsend.view(-1), group=self.group)
+                ops.lm_head_shard(x_all, P, S, gs, self.m.v_lo, self.dp_keys, res_all, self.m.final_norm,
+                                  self.c.rms_eps)
+                dist.all_reduce(self.dp_keys, op=dist.ReduceOp.MAX, group=self.group)
+                ops.keys_to_tokens(self.dp_keys[r:r + 1], self.out_tok)
+            return head_dp
         if self.m.world > 1 and self.sampling is not None:
             import torch.distributed as dist
             sp, k, R = self.sampling, self.sampling["top_k"], self.m.world
@@ -489,8 +550,12 @@ class Decoder:
         """Bytes one launch of kernel `name` must move at batch M and context ctx (weights / KV read once,
         activations in and out): the roofline numerator."""
         c, M = self.c, self.M
+        if self.dp and name in ("route", "up_ep", "down_ep", "combine", "head"):
+            M = self.m.world                              # the MoE and the head work on every rank's token
         nv = lambda n, k: n * k // 2 + n * k // 16
         H, D = c.hidden, c.head_dim
+        if name == "combine":
+            return c.topk * H * 2 + c.topk * 4 + H * 2
         if name == "qkv":
             return nv(c.qkv_rows, H) + M * (3 * H * 2 + c.qkv_rows * 2 + c.num_heads * D * 2 + 2 * c.num_kv_heads * D * 2)
         if name == "attention":

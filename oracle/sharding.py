@@ -2,6 +2,9 @@
 
 TEST INFRASTRUCTURE ONLY: used by tests/ (gloo ranks on CPU) to check the exchange arithmetic the GPU path uses:
 
+* Data-parallel streams (one per rank): the ranks all-gather their tokens, route every token identically, each rank
+  produces the rows of the routes whose expert is local (zeros elsewhere) for all tokens, and a reduce-scatter sum
+  hands every rank its own token's rows -- exact for the same reason as below -- which it combines in slot order.
 * MoE: rank r holds experts [r*E/N, (r+1)*E/N); for one token it produces y_slots [topk, H] with the bf16 output of
   each routed slot whose expert is local and zeros elsewhere; the element-wise sum over ranks has exactly one
   non-zero term per element (exact), and out = bf16(sum_s tw[s] * y[s]) in slot order with fp32 FMAs -- the same

@@ -45,7 +45,8 @@ SAMPLING = dict(temperature=1.0, top_k=20, top_p=0.95)
 # (name, batch, moe path, exchange, sampled)
 CASES = [("b1_block_peer", 1, "block", "peer", False), ("b1_block_nccl", 1, "block", "nccl", False),
          ("b3_chain", 3, "chain", "peer", False), ("b3_chain_sampled", 3, "chain", "peer", True),
-         ("b1_block_sampled", 1, "block", "peer", True)]
+         ("b1_block_sampled", 1, "block", "peer", True),
+         ("dp_streams", 1, "dp", "nccl", False)]           # one stream per rank: data-parallel attention + EP MoE
 
 
 def decode(model, prompt, n, batch, moe, group=None, exchange="peer", sampled=False):
@@ -65,6 +66,22 @@ def decode(model, prompt, n, batch, moe, group=None, exchange="peer", sampled=Fa
     return toks, h, status
 
 
+def decode_dp(model, prompt, n, group, rank):
+    """This rank's stream (prompt row `rank`) through the data-parallel decode; -> (tokens [1, n], h [1, H])."""
+    from flint_b200.model import Decoder
+    dec = Decoder(model, batch=1, group=group, dp=True)
+    dec.reserve_history(n)
+    dec.capture()
+    dec.prefill(prompt[rank:rank + 1])
+    toks = dec.decode(n).clone()
+    h = dec.h.float().clone()
+    torch.cuda.synchronize()
+    dec.close()
+    del dec
+    gc.collect()
+    return toks, h
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--layers", type=int, default=4)
@@ -79,14 +96,22 @@ def main():
     from flint_b200.model import FlintConfig, FlintModel
     cfg = FlintConfig(layers=args.layers, vocab=256 * 8 * 16)
     dev = torch.device("cuda", torch.cuda.current_device())
-    prompt = np.random.default_rng(5).integers(0, cfg.vocab, size=(3, args.prompt))
+    prompt = np.random.default_rng(5).integers(0, cfg.vocab, size=(max(3, world), args.prompt))
     ctx = args.prompt + args.tokens + 16
     cases = [c for c in CASES if c[0] in args.cases.split(",")]
     model = FlintModel(cfg, dev, seed=11, max_ctx=ctx, max_batch=3, shard=(rank, world))
     runs = {}
     for name, batch, moe, exchange, sampled in cases:
-        runs[name] = decode(model, prompt, args.tokens, batch, moe, group=dist.group.WORLD, exchange=exchange,
-                            sampled=sampled)
+        if moe == "dp":                                 # every rank's stream, gathered to rank 0
+            toks, h = decode_dp(model, prompt, args.tokens, dist.group.WORLD, rank)
+            all_t = [torch.zeros_like(toks) for _ in range(world)]
+            all_h = [torch.zeros_like(h) for _ in range(world)]
+            dist.all_gather(all_t, toks)
+            dist.all_gather(all_h, h)
+            runs[name] = ([t.cpu().numpy() for t in all_t], [x.cpu().numpy() for x in all_h], 0)
+        else:
+            runs[name] = decode(model, prompt, args.tokens, batch, moe, group=dist.group.WORLD, exchange=exchange,
+                                sampled=sampled)
         dist.barrier()
     ok = True
     if rank == 0:
@@ -95,6 +120,16 @@ def main():
         single = FlintModel(cfg, dev, seed=11, max_ctx=ctx, max_batch=3)
         rep = {"world": world, "layers": cfg.layers}
         for name, batch, moe, exchange, sampled in cases:
+            if moe == "dp":                             # each rank's stream against that stream alone on one GPU
+                match, streams = True, []
+                for r in range(world):
+                    ref_toks, ref_h, _ = decode(single, prompt[r:r + 1], args.tokens, 1, "chain")
+                    ok_r = bool((runs[name][0][r] == ref_toks).all() and np.array_equal(runs[name][1][r], ref_h))
+                    streams.append({"rank": r, "match": ok_r, "tokens": runs[name][0][r][0, :8].tolist()})
+                    match = match and ok_r
+                rep[name] = {"match": match, "streams": streams}
+                ok = ok and match
+                continue
             ref_toks, ref_h, _ = decode(single, prompt, args.tokens, batch, moe, sampled=sampled)
             toks, h, status = runs[name]
             match = bool((toks == ref_toks).all() and np.array_equal(h, ref_h)) and status == 0

@@ -1,6 +1,8 @@
 """Multi-GPU exchange logic on CPU: world_size-2 and -4 gloo ranks run the sharded MoE sum + combine, the
 vocabulary-sharded argmax and the vocabulary-sharded sampled head (per-shard top-k candidates, all_gather, merge,
-draw) with the same arithmetic as the GPU path, against the single-process result."""
+draw) with the same arithmetic as the GPU path, against the single-process result; and the data-parallel decode of
+one stream per rank (tokens all-gathered, routed identically, local routes' rows reduce-scattered, combined per
+rank; every rank's token through each vocabulary shard) against each stream computed alone."""
 import os
 import socket
 
@@ -78,6 +80,87 @@ def test_sharded_exchange_gloo(world):
     for p in procs:
         p.start()
     out = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, res in out:
+        assert all(res.values()), (rank, res)
+
+
+def _dp_worker(rank, world, port, q):
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    from oracle import moe as om
+    from oracle import nvfp4 as onv
+    from oracle import sharding as sh
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        rng = np.random.default_rng(11)                     # the model: identical on every rank
+        E, k, H, I, V = 8, 2, 256, 64, 1024
+        bf = lambda *s_, sd=1.0: onv.bf16_round((rng.standard_normal(s_) * sd).astype(np.float32))
+
+        def stack(N, K):
+            parts = [onv.quantize_nvfp4((rng.standard_normal((N, K)) * 0.05).astype(np.float32)) for _ in range(E)]
+            return tuple(np.stack([p[i] for p in parts]) for i in range(3))
+        w13, s13, g13 = stack(2 * I, H)
+        w2, s2, g2 = stack(H, I)
+        gate, nw, fw = bf(E, H, sd=0.05), 1 + bf(H, sd=0.05), 1 + bf(H, sd=0.05)
+        Ph, Sh, gh = onv.quantize_nvfp4((rng.standard_normal((V, H)) * 0.05).astype(np.float32))
+        toks = [(bf(1, H), bf(1, H)) for _ in range(world)]          # each rank's (attention output, residual)
+        lo, hi = sh.expert_range(rank, world, E)
+        res = {}
+        # ---- MoE: all-gather the tokens, route all of them, local routes' rows, reduce-scatter, combine ----
+        send = torch.from_numpy(np.concatenate(toks[rank], 0))
+        recv = torch.zeros((world, 2, H))
+        dist.all_gather_into_tensor(recv.view(-1), send.view(-1))
+        x_all, r_all = recv[:, 0].numpy(), recv[:, 1].numpy()
+        xn, res_b = om.rmsnorm(x_all, r_all, nw, 1e-6)
+        ids, tw = om.topk_route(om.router_logits_mirror(xn, gate), k, 0)
+        act = om.experts_up(xn, ids, w13, s13, g13)
+        y = np.zeros((world * k, H), np.float32)
+        for m in range(world):                                      # each route's bf16 output row
+            for t in range(k):
+                y[m * k + t] = om.experts_down(act[m * k + t][None], ids[m:m + 1, t:t + 1], np.ones((1, 1), np.float32),
+                                               w2, s2, g2)[0]
+        mine = torch.from_numpy(sh.local_slot_rows(y, ids.reshape(-1), lo, hi))
+        out = torch.zeros((k, H))
+        dist.reduce_scatter_tensor(out, mine)                       # exact: one non-zero term per element
+        h = sh.combine(out.numpy(), tw[rank])
+        # alone: this rank's token through the whole MoE
+        xn1, rb1 = om.rmsnorm(toks[rank][0], toks[rank][1], nw, 1e-6)
+        i1, w1 = om.topk_route(om.router_logits_mirror(xn1, gate), k, 0)
+        a1 = om.experts_up(xn1, i1, w13, s13, g13)
+        y1 = np.stack([om.experts_down(a1[t][None], i1[:, t:t + 1], np.ones((1, 1), np.float32), w2, s2, g2)[0]
+                       for t in range(k)])
+        res["moe"] = bool(np.array_equal(h, sh.combine(y1, w1[0])) and np.array_equal(res_b[rank], rb1[0]))
+        # ---- head: every rank's (h, res) through this rank's vocabulary shard, MAX of the keys ----
+        hs = torch.from_numpy(np.concatenate([h[None], res_b[rank][None]], 0))
+        hrecv = torch.zeros((world, 2, H))
+        dist.all_gather_into_tensor(hrecv.view(-1), hs.view(-1))
+        xf, _ = om.rmsnorm(hrecv[:, 0].numpy(), hrecv[:, 1].numpy(), fw, 1e-6)
+        v0, v1 = sh.vocab_range(rank, world, V)
+        from oracle.lm_head import lm_head_logits
+        lg = lm_head_logits(xf, Ph[v0:v1], Sh[v0:v1], gh)
+        keys = torch.tensor([sh.shard_key(lg[m], v0) for m in range(world)], dtype=torch.int64)
+        dist.all_reduce(keys, op=dist.ReduceOp.MAX)
+        xf1, _ = om.rmsnorm(h[None], res_b[rank][None], fw, 1e-6)
+        full = lm_head_logits(xf1, Ph, Sh, gh)[0]
+        res["head"] = sh.key_token(int(keys[rank].item())) == int(np.flatnonzero(full == full.max())[0])
+        q.put((rank, res))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_data_parallel_streams_gloo(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dp_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=180) for _ in procs]
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
