@@ -35,8 +35,9 @@
 #include <stdio.h>
 
 // phase stamps of development builds (-DFLINT_TIMELINE): 0 entry, 1 PDL wait done, 2 norm staged, 3 QKV rows
-// published, 4 page partition known, 5 first q heads fetched, 6 own pages done, 7 merges done, 8 O rows written;
-// producer: 10 resident weights landed, 11 last page requested
+// published, 4 page partition known, 5 first q heads fetched, 6 own pages done, 7 merges done, 8 O rows written,
+// 12 norm computed (before the consumer barrier), 13 QKV weights resident, 14 QKV sums done;
+// producer: 10 first page requested, 11 last page requested
 FLINT_TL_BUFFER
 
 namespace flint {
@@ -407,48 +408,49 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
   unsigned ep;                                         // this launch's tag (the last CTA to retire advances it)
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(ep) : "l"(&a.ws->epoch) : "memory");
   ep += 1u;
-  // ---- A (first half): add + RMSNorm.  It runs before the page partition and before any page is requested, so its
-  // loads of x / res are not queued behind the KV stream; the sequence lengths load alongside. ----
-  const int my_seq = (int)threadIdx.x < M ? a.seq_lens[threadIdx.x] : 0;
-  if (warp < kBW) {
+  const int S = M * a.nkv;
+  if (warp == kBW) {
+    // ---- producer: the page partition inputs from the sequence lengths, right after the wait (the consumers run
+    // the norm meanwhile; they read these tables only once bar_tab has been released) ----
+    if (lane == 0) {
+      int pre = 0;
+      for (int b = 0; b < M; ++b) {
+        const int seq = a.seq_lens[b];
+        const int start = a.window > 0 ? max(0, seq - a.window) : 0;
+        const int pf = start / kBPage;
+        int pe = (seq + kBPage - 1) / kBPage;
+        if (pe > a.max_blocks) {
+          atomicOr(status, 4u);
+          pe = a.max_blocks;
+        }
+        s_seq[b] = seq;
+        s_start[b] = start;
+        s_pf[b] = pf;
+        s_npg[b] = max(0, pe - pf);
+        s_pre[b] = pre;
+        pre += s_npg[b];
+      }
+      s_pre[M] = pre;
+      s_P = a.nkv * pre;
+      s_ntk = 0;
+    }
+    __syncwarp();
+  } else {
+    // ---- A (first half), consumers: add + RMSNorm ----
     if (a.H / 8 <= kBCons)
       norm_stage_f16_1(a.x, a.ldx, a.tokens, a.res, a.ldr, a.nw, a.eps, M, a.H, xs, shift, red_n,
                        cta == 0 ? a.res_out : nullptr, kBCons, 1);
     else
       norm_stage_f16(a.x, a.ldx, a.tokens, a.res, a.ldr, a.nw, a.eps, M, a.H, xs, shift, red_n,
                      cta == 0 ? a.res_out : nullptr, kBCons, 1);
-    if ((int)threadIdx.x < M) s_seq[threadIdx.x] = my_seq;
+    if (threadIdx.x == 0) FLINT_TL(12);
+    cons_sync();
+    if (threadIdx.x == 0) FLINT_TL(2);
   }
-  __syncthreads();
-  if (threadIdx.x == 0) FLINT_TL(2);
-  if (threadIdx.x == 0) {                              // page partition inputs
-    int pre = 0;
-    for (int b = 0; b < M; ++b) {
-      const int seq = s_seq[b];
-      const int start = a.window > 0 ? max(0, seq - a.window) : 0;
-      const int pf = start / kBPage;
-      int pe = (seq + kBPage - 1) / kBPage;
-      if (pe > a.max_blocks) {
-        atomicOr(status, 4u);
-        pe = a.max_blocks;
-      }
-      s_seq[b] = seq;
-      s_start[b] = start;
-      s_pf[b] = pf;
-      s_npg[b] = max(0, pe - pf);
-      s_pre[b] = pre;
-      pre += s_npg[b];
-    }
-    s_pre[M] = pre;
-    s_P = a.nkv * pre;
-    s_ntk = 0;
-  }
-  __syncthreads();
-  const int S = M * a.nkv;
-  const int P = s_P;
 
   if (warp == kBW) {
-    // ---- producer, first: the partition, off the consumers' critical path (released to them through bar_tab).
+    const int P = s_P;
+    // ---- producer, next: the partition, off the consumers' critical path (released to them through bar_tab).
     // Each CTA works on ONE segment: segment s gets k_s CTAs in proportion to its n_s pages (floor of n_s G / P, at
     // least 1, at most n_s; spare CTAs to the largest remainders, ties to the lower segment), which split its pages
     // evenly in CTA order; CTA c0_s + i owns pages [A_s + i n_s / k_s, A_s + (i + 1) n_s / k_s) and writes record
@@ -547,10 +549,9 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
       if (lane == 0) mbar_arrive(&bar_tab);
     }
     const int lo = s_lo, hi = s_hi;
-    // ---- producer: this CTA's pages, in the order the consumers take them, once the resident weights have landed
-    // (they are needed first; the pages then stream in under the QKV GEMV and the barrier) ----
+    // ---- producer: this CTA's pages, in the order the consumers take them, from the start: the ring fills
+    // while the norm and the QKV GEMV run (the resident weights were requested before the wait) ----
     if (lane == 0) {
-      if (ngq > 0 && !mbar_wait(&bar_wq, 0, status)) return;
       FLINT_TL(10);
       int j = 0;
       for (int s = 0; s < S; ++s) {
@@ -574,8 +575,10 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
   // ================= consumers (256 threads) =================
   // ---- A (second half): QKV rows ----
   if (ngq > 0 && cons_sync_and(mbar_wait(&bar_wq, 0, status))) {
+    if (threadIdx.x == 0) FLINT_TL(13);
     gemv_resident(wq, wq + a.wq_scale_off, ngq, a.nks_q, xs, a.H, M, red, warp, lane);
     cons_sync();
+    if (threadIdx.x == 0) FLINT_TL(14);
     gemv_finish_tagged(red, ngq, M, a.gs_qkv[0], shift, a.y_tag, a.Nqkv / 2, gq0 * 16, ep);
   }
   if (threadIdx.x == 0) FLINT_TL(3);

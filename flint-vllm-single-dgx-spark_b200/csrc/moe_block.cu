@@ -47,7 +47,8 @@
 #include <algorithm>
 
 // phase stamps of development builds (-DFLINT_TIMELINE): 0 entry, 1 PDL wait done, 2 norm + router rows published,
-// 3 top-k known, 4 up units done, 5 down rows done, 6 output written; producer: 10 plan received, 11 loads issued
+// 3 top-k known, 4 up units done, 5 down rows done, 6 output written, 7 logits seen, 8 top-k computed (warp 0),
+// 9 first up unit landed; producer: 10 plan received, 11 loads issued
 FLINT_TL_BUFFER
 
 namespace flint {
@@ -290,9 +291,11 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
           }
         }
     }
+    if (lane == 0) FLINT_TL(7);
     int my_e;
     float my_w;
     warp_topk_regs<PER>(lv, per, topk, a.score_fn, lane, my_e, my_w);
+    if (lane == 0) FLINT_TL(8);
     if (lane < topk) {
       s_ids[lane] = my_e;
       s_tw[lane] = my_w;
@@ -321,6 +324,7 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   #pragma unroll 1
   for (int u = 0; u < nu; ++u) {
     if (!xsync_and(mbar_wait(&bar_up[u], 0, status))) break;
+    if (tid == 0 && u == 0) FLINT_TL(9);
     const int unit = u0 + u;
     const bool shared = unit >= routed_units;
     const int s = shared ? 0 : s_local[unit / jpe];
