@@ -41,6 +41,8 @@ SIGNATURES: dict[str, tuple] = {
     "flint_moe_fused_workspace_bytes": (I64, [I64, I64, I64]),
     "flint_moe_fused": (I32, [P, I64, P, P, F32, P, I64, I64, I64, I64, I32, P, P, P, P, P, P, I64, P, P, P, P, P, P, P, I32,
                               P]),
+    "flint_moe_fused_ep": (I32, [P, I64, P, P, F32, P, I64, I64, I64, I64, I32, P, P, P, P, P, P, I64, I64, I64, P, P, P, P,
+                                 P, P, I32, P]),
     "flint_moe_block_workspace_bytes": (I64, [I64, I64]),
     "flint_moe_block": (I32, [P, I64, P, P, F32, P, I64, I64, I64, I32, P, P, P, P, P, P, I64, P, P, P, P, P, P, P, P, I32,
                               P]),

@@ -14,6 +14,12 @@
 //
 // Numerics are those of the per-op kernels in moe.cu (same reduction orders), so routing is bit identical to them.
 // Up and down tiles are split over CTAs by a linear partition of their stage counts (balanced to within one tile).
+//
+// Expert-parallel mode (flint_moe_fused_ep, y_out given): the weights hold experts [e_lo, e_hi) only; the router and
+// top-k run in full (identical on every rank), only routes whose expert is local get tiles, and phase F writes
+// y_out[m * topk + s] = y of each local route (zero rows for the others) instead of the weighted sum: summed over the
+// ranks (one non-zero term per element) and combined in slot order they give the one-GPU output bit for bit, and the
+// rows equal flint_moe_down_ep's.
 #include "gridsync.cuh"
 #include "moe_common.cuh"
 #include "runtime.cuh"
@@ -47,6 +53,8 @@ struct MoeFusedArgs {
   int* ids_out;
   float* tw_out;
   MoeFusedWs* ws;
+  int e_lo, e_hi;                    // local experts (expert-parallel mode; 0 and kNotLocal otherwise)
+  bf16* y_out;                       // expert-parallel mode: per-route rows [M * topk][H]
 };
 
 __host__ __device__ inline size_t moe_fused_ws_bytes(int E, int H, int I) {
@@ -220,7 +228,7 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   if (blockIdx.x == 0 && a.logits_out)
     for (int i = tid; i < M * E; i += NT) a.logits_out[i] = __ldcg(lg + i);
   named_bar_sync(2, NT);
-  build_groups(ids_s, R, topk, E, G, sorted, ids_c, status, NT, 2);
+  build_groups(ids_s, R, topk, E, G, sorted, ids_c, status, NT, 2, a.e_lo, a.e_hi);
   const int U = G.n * tpu, Dn = G.n * tpd;
   const long total = (long)U * nks_up + (long)Dn * nks_dn;
   const long tau = (total + nb - 1) / nb;
@@ -300,9 +308,20 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   pdl_trigger();
   if (!grid_sync(&ws->sync, nb, 2, NT, 2, &s_ok, status)) return;
 
-  // ---------------- phase F: weighted sum in slot order ----------------
+  // ---------------- phase F: weighted sum in slot order (expert parallel: the local routes' rows) ----------------
   const int rows_per = (H + nb - 1) / nb;
   const int r0 = blockIdx.x * rows_per, r1 = min(H, r0 + rows_per);
+  if (a.y_out) {
+    for (int idx = tid; idx < (r1 - r0) * R; idx += NT) {
+      const int route = idx / (r1 - r0), r = r0 + idx - route * (r1 - r0);
+      const unsigned short b = ids_c[route] != kNotLocal
+                                   ? __ldcg(reinterpret_cast<const unsigned short*>(y_g + (int64_t)route * H + r))
+                                   : (unsigned short)0;
+      reinterpret_cast<unsigned short*>(a.y_out)[(int64_t)route * H + r] = b;
+    }
+    grid_sync_retire(&ws->sync, nb);
+    return;
+  }
   for (int idx = tid; idx < (r1 - r0) * M; idx += NT) {
     const int m = idx / (r1 - r0), r = r0 + idx - m * (r1 - r0);
     float acc = 0.f;
@@ -351,12 +370,15 @@ extern "C" int64_t flint_moe_fused_workspace_bytes(int64_t E, int64_t H, int64_t
   return (int64_t)moe_fused_ws_bytes((int)E, (int)H, (int)I);
 }
 
-extern "C" int flint_moe_fused(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, const void* gate_w,
-                               int64_t M, int64_t H, int64_t E, int64_t topk, int score_fn, const void* w13, const void* s13,
-                               const float* g13, const void* w2, const void* s2, const float* g2, int64_t I, void* out,
-                               void* res_out, void* xn_out, float* logits_out, int32_t* topk_ids_out,
-                               float* topk_weights_out, void* workspace, int pdl, void* stream) {
-  if (!x || !norm_w || !gate_w || !w13 || !s13 || !g13 || !w2 || !s2 || !g2 || !out || !workspace) return FLINT_ERR_ARGUMENT;
+static int moe_fused_launch(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, const void* gate_w,
+                            int64_t M, int64_t H, int64_t E, int64_t topk, int score_fn, const void* w13, const void* s13,
+                            const float* g13, const void* w2, const void* s2, const float* g2, int64_t I, int64_t e_lo,
+                            int64_t n_local, void* out, void* y_out, void* res_out, void* xn_out, float* logits_out,
+                            int32_t* topk_ids_out, float* topk_weights_out, void* workspace, int pdl, void* stream) {
+  if (!x || !norm_w || !gate_w || !w13 || !s13 || !g13 || !w2 || !s2 || !g2 || (!out && !y_out) || !workspace)
+    return FLINT_ERR_ARGUMENT;
+  if (e_lo < 0 || n_local < 1 || e_lo + n_local > E) return FLINT_ERR_ARGUMENT;
+  if (y_out && !aligned(y_out, 16)) return FLINT_ERR_ALIGN;
   const int sms = num_sms();
   if (sms <= 0) return FLINT_ERR_DEVICE;
   if (M < 1 || M > kMaxTokens || (H != 2048 && H != 4096) || E < 32 || E % 32 != 0 || E > 2 * sms || topk < 1 ||
@@ -364,15 +386,15 @@ extern "C" int flint_moe_fused(const void* x, int64_t ldx, const void* res, cons
       ldx % 8 != 0 || (score_fn != 0 && score_fn != 1))
     return FLINT_ERR_SHAPE;
   if (!aligned(x, 16) || (res && !aligned(res, 16)) || !aligned(norm_w, 16) || !aligned(gate_w, 16) || !aligned(w13, 16) ||
-      !aligned(s13, 16) || !aligned(w2, 16) || !aligned(s2, 16) || !aligned(out, 16) || (res_out && !aligned(res_out, 16)) ||
+      !aligned(s13, 16) || !aligned(w2, 16) || !aligned(s2, 16) || (out && !aligned(out, 16)) || (res_out && !aligned(res_out, 16)) ||
       (xn_out && !aligned(xn_out, 16)) || !aligned(workspace, 16))
     return FLINT_ERR_ALIGN;
   if (res_out && !res) return FLINT_ERR_ARGUMENT;
   CUtensorMap uc, us, dc, ds;
-  int rc = encode_u8_2d(&uc, w13, H / 2, E * 2 * I, H / 2, 128, kFBox, true);
-  if (!rc) rc = encode_u8_2d(&us, s13, H / 16, E * 2 * I, H / 16, 16, kFBox, false);
-  if (!rc) rc = encode_u8_2d(&dc, w2, I / 2, E * H, I / 2, 128, kFBox, true);
-  if (!rc) rc = encode_u8_2d(&ds, s2, I / 16, E * H, I / 16, 16, kFBox, false);
+  int rc = encode_u8_2d(&uc, w13, H / 2, n_local * 2 * I, H / 2, 128, kFBox, true);
+  if (!rc) rc = encode_u8_2d(&us, s13, H / 16, n_local * 2 * I, H / 16, 16, kFBox, false);
+  if (!rc) rc = encode_u8_2d(&dc, w2, I / 2, n_local * H, I / 2, 128, kFBox, true);
+  if (!rc) rc = encode_u8_2d(&ds, s2, I / 16, n_local * H, I / 16, 16, kFBox, false);
   if (rc) return rc;
   MoeFusedArgs a;
   a.x = (const bf16*)x; a.ldx = ldx; a.res = (const bf16*)res; a.nw = (const bf16*)norm_w; a.eps = eps;
@@ -380,10 +402,36 @@ extern "C" int flint_moe_fused(const void* x, int64_t ldx, const void* res, cons
   a.M = (int)M; a.H = (int)H; a.I = (int)I; a.out = (bf16*)out; a.res_out = (bf16*)res_out; a.xn_out = (bf16*)xn_out;
   a.logits_out = logits_out; a.ids_out = (int*)topk_ids_out; a.tw_out = topk_weights_out;
   a.ws = static_cast<MoeFusedWs*>(workspace);
+  a.y_out = (bf16*)y_out;
+  a.e_lo = (int)e_lo;
+  a.e_hi = y_out ? (int)(e_lo + n_local) : kNotLocal;
   if (H == 2048) {
     if (M <= 2) return launch_fused<6, 8>(sms, uc, us, dc, ds, a, pdl, stream);
     return launch_fused<4, 8>(sms, uc, us, dc, ds, a, pdl, stream);
   }
   if (M <= 2) return launch_fused<6, 16>(sms, uc, us, dc, ds, a, pdl, stream);
   return launch_fused<4, 16>(sms, uc, us, dc, ds, a, pdl, stream);
+}
+
+extern "C" int flint_moe_fused(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, const void* gate_w,
+                               int64_t M, int64_t H, int64_t E, int64_t topk, int score_fn, const void* w13, const void* s13,
+                               const float* g13, const void* w2, const void* s2, const float* g2, int64_t I, void* out,
+                               void* res_out, void* xn_out, float* logits_out, int32_t* topk_ids_out,
+                               float* topk_weights_out, void* workspace, int pdl, void* stream) {
+  if (!out) return FLINT_ERR_ARGUMENT;
+  return moe_fused_launch(x, ldx, res, norm_w, eps, gate_w, M, H, E, topk, score_fn, w13, s13, g13, w2, s2, g2, I, 0, E,
+                          out, nullptr, res_out, xn_out, logits_out, topk_ids_out, topk_weights_out, workspace, pdl,
+                          stream);
+}
+
+extern "C" int flint_moe_fused_ep(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps,
+                                  const void* gate_w, int64_t M, int64_t H, int64_t E, int64_t topk, int score_fn,
+                                  const void* w13, const void* s13, const float* g13, const void* w2, const void* s2,
+                                  const float* g2, int64_t I, int64_t expert_lo, int64_t n_local, void* y_out,
+                                  void* res_out, float* logits_out, int32_t* topk_ids_out, float* topk_weights_out,
+                                  void* workspace, int pdl, void* stream) {
+  if (!y_out) return FLINT_ERR_ARGUMENT;
+  return moe_fused_launch(x, ldx, res, norm_w, eps, gate_w, M, H, E, topk, score_fn, w13, s13, g13, w2, s2, g2, I,
+                          expert_lo, n_local, nullptr, y_out, res_out, nullptr, logits_out, topk_ids_out,
+                          topk_weights_out, workspace, pdl, stream);
 }

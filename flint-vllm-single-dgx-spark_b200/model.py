@@ -213,9 +213,9 @@ class Decoder:
 
         dp=True (a sharded model, one stream per GPU): data-parallel attention with expert-parallel MoE.  Each rank
         decodes its own stream (its own KV cache, the attention weights replicated); per layer the ranks all-gather
-        their attention outputs and residuals, route all the ranks' tokens identically, compute the routes whose
-        expert is local (moe_up_ep / moe_down_ep), reduce-scatter the per-route rows (each element has one non-zero
-        term, so the sum is exact) and combine their own token's rows; the vocabulary-sharded head takes every rank's
+        their attention outputs and residuals, route all the ranks' tokens identically and compute the routes whose
+        expert is local in one launch (moe_fused_ep), reduce-scatter the per-route rows (each element has one
+        non-zero term, so the sum is exact) and combine their own token's rows; the vocabulary-sharded head takes every rank's
         hidden state and a MAX all-reduce of the argmax keys.  Each rank's stream equals the one-GPU chain decode of
         that stream bit for bit."""
         # measured per layer at 6K context: one stream, the block; 2..5 streams, the chain (67.7 us at 4 against the
@@ -315,7 +315,7 @@ class Decoder:
         # (peer exchange: the MoE block exchanges in-kernel; the head adds one exchange kernel)
         # dense layers: route + up + down; the shared expert: up + down (its bf16 add is a torch elementwise op)
         ep = model.world > 1
-        moe_launches = (4 if ep else 3) if moe == "chain" else 2 if (ep and exchange == "nccl") else 4 if moe == "dp" else 1
+        moe_launches = (4 if ep else 3) if moe == "chain" else 2 if (ep and exchange == "nccl") else 2 if moe == "dp" else 1
         n_dense = len(c.mlp_only_layers)
         shared_fused = (c.shared_inter and model.world == 1 and moe == "block" and c.shared_inter % 256 == 0
                         and c.shared_inter <= 1024 and c.topk < 8)
@@ -383,13 +383,10 @@ class Decoder:
             x_all, res_all = self.dp_recv[:, 0], self.dp_recv[:, 1]
             seq += [("dp_gather", lambda: dist.all_gather_into_tensor(self.dp_recv.view(-1), self.dp_send.view(-1),
                                                                        group=self.group)),
-                    ("route", lambda: ops.moe_route(x_all, res_all, L["ln2"], c.rms_eps, L["gate"], c.topk, ew.score_fn,
-                                                    self.dp_lg, self.dp_ti, self.dp_tw, self.dp_xn, self.dp_res, True,
-                                                    True)),
-                    ("up_ep", lambda: ops.moe_up_ep(self.dp_xn, self.dp_ti, ew.w13, ew.s13, ew.g13, c.num_experts,
-                                                    m.e_lo, self.dp_act)),
-                    ("down_ep", lambda: ops.moe_down_ep(self.dp_act, self.dp_ti, ew.w2, ew.s2, ew.g2, c.num_experts,
-                                                        m.e_lo, self.dp_y)),
+                    ("moe_fused_ep", lambda: ops.moe_fused_ep(x_all, res_all, L["ln2"], c.rms_eps, L["gate"], c.topk,
+                                                              ew.score_fn, ew.w13, ew.s13, ew.g13, ew.w2, ew.s2, ew.g2,
+                                                              c.num_experts, m.e_lo, self.dp_y, self.dp_res, self.dp_ti,
+                                                              self.dp_tw)),
                     ("dp_scatter", lambda: dist.reduce_scatter_tensor(self.dp_mine, self.dp_y, group=self.group)),
                     ("combine", lambda: ops.moe_combine(self.dp_mine, self.dp_tw[r:r + 1], self.h))]
             return seq
@@ -550,7 +547,7 @@ class Decoder:
         """Bytes one launch of kernel `name` must move at batch M and context ctx (weights / KV read once,
         activations in and out): the roofline numerator."""
         c, M = self.c, self.M
-        if self.dp and name in ("route", "up_ep", "down_ep", "combine", "head"):
+        if self.dp and name in ("moe_fused_ep", "combine", "head"):
             M = self.m.world                              # the MoE and the head work on every rank's token
         nv = lambda n, k: n * k // 2 + n * k // 16
         H, D = c.hidden, c.head_dim
@@ -574,6 +571,9 @@ class Decoder:
         if name in ("moe_fused", "moe_block"):
             return (self.algorithmic_bytes("route", ctx) + self.algorithmic_bytes("up", ctx)
                     + self.algorithmic_bytes("down", ctx))
+        if name == "moe_fused_ep":                        # every rank's token routed; local experts' routes only
+            return (self.algorithmic_bytes("route", ctx) + (self.algorithmic_bytes("up", ctx)
+                                                            + self.algorithmic_bytes("down", ctx)) // self.m.world)
         if name in ("up_ep", "down_ep"):                  # local experts only: topk / world routes on average
             return self.algorithmic_bytes(name[:-3], ctx) // self.m.world
         if name in ("moe_block_ep", "moe_block_peer"):   # local experts only: topk / world routed slots on average

@@ -330,6 +330,36 @@ def _(x, res, norm_w, eps, gate_w, topk, score_fn, w13, s13, g13, w2, s2, g2, ou
     return None
 
 
+@torch.library.custom_op(f"{NS}::moe_fused_ep", mutates_args=("y_out", "res_out", "ids_out", "tw_out"))
+def moe_fused_ep(x: torch.Tensor, res: torch.Tensor | None, norm_w: torch.Tensor, eps: float, gate_w: torch.Tensor,
+                 topk: int, score_fn: int, w13: torch.Tensor, s13: torch.Tensor, g13: torch.Tensor, w2: torch.Tensor,
+                 s2: torch.Tensor, g2: torch.Tensor, num_experts: int, expert_lo: int, y_out: torch.Tensor,
+                 res_out: torch.Tensor | None, ids_out: torch.Tensor, tw_out: torch.Tensor) -> None:
+    """Expert-parallel fused MoE for 1..8 tokens (flint_moe_fused_ep): per-route rows of the local experts (zero rows
+    for the others), the routing of every token and the residual."""
+    _lib.require_cuda(x, "moe_fused_ep")
+    _bf16_2d(x, "moe_fused_ep x")
+    M, H = x.shape
+    n_local, I2, Hh = w13.shape
+    if Hh * 2 != H or gate_w.shape != (num_experts, H) or y_out.shape != (M * topk, H):
+        raise _lib.FlintError("moe_fused_ep: shapes must match the expert weights")
+    if res is not None and res.stride() != x.stride():
+        raise _lib.FlintError("moe_fused_ep: res must have x's row stride")
+    nbytes = lib().flint_moe_fused_workspace_bytes(num_experts, H, I2 // 2)
+    ws = _lib.workspace(x.device, f"moe_fused_{num_experts}_{H}_{I2 // 2}", nbytes)
+    rc = lib().flint_moe_fused_ep(ptr(x), x.stride(0), ptr(res), ptr(norm_w), float(eps), ptr(gate_w), M, H,
+                                  int(num_experts), topk, score_fn, ptr(_u8(w13)), ptr(_u8(s13)), ptr(g13), ptr(_u8(w2)),
+                                  ptr(_u8(s2)), ptr(g2), I2 // 2, int(expert_lo), n_local, ptr(y_out), ptr(res_out),
+                                  None, ptr(ids_out), ptr(tw_out), ptr(ws), PDL, stream_ptr(x.device))
+    check(rc, "flint_moe_fused_ep")
+
+
+@moe_fused_ep.register_fake
+def _(x, res, norm_w, eps, gate_w, topk, score_fn, w13, s13, g13, w2, s2, g2, num_experts, expert_lo, y_out, res_out,
+      ids_out, tw_out):
+    return None
+
+
 @torch.library.custom_op(f"{NS}::moe_block", mutates_args=("out", "res_out", "xn_out", "logits_out", "ids_out",
                                                              "tw_out"))
 def moe_block(x: torch.Tensor, res: torch.Tensor | None, norm_w: torch.Tensor, eps: float, gate_w: torch.Tensor, topk: int,

@@ -220,6 +220,18 @@ int flint_moe_fused(const void* x, int64_t ldx, const void* res, const void* nor
                     void* res_out, void* xn_out, float* logits_out, int32_t* topk_ids_out, float* topk_weights_out,
                     void* workspace, int pdl, void* stream);
 
+/* Expert-parallel flint_moe_fused (1..8 tokens in one launch): the weights hold experts expert_lo .. expert_lo +
+ * n_local - 1 (indexed by local expert); the router and top-k run in full (identical on every rank) and only routes
+ * whose expert is local get tiles.  Writes y_out bf16 [M * topk, H] (row m * topk + s = y of route (m, s) when its
+ * expert is local, zeros otherwise; the rows of flint_moe_down_ep), res_out, logits / ids / weights as
+ * flint_moe_fused.  A sum of y_out over the ranks (one non-zero term per element) and flint_moe_combine give the
+ * one-GPU output bit for bit.  Workspace: flint_moe_fused_workspace_bytes(E, H, I). */
+int flint_moe_fused_ep(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, const void* gate_w,
+                       int64_t M, int64_t H, int64_t E, int64_t topk, int score_fn, const void* w13, const void* s13,
+                       const float* g13, const void* w2, const void* s2, const float* g2, int64_t I, int64_t expert_lo,
+                       int64_t n_local, void* y_out, void* res_out, float* logits_out, int32_t* topk_ids_out,
+                       float* topk_weights_out, void* workspace, int pdl, void* stream);
+
 /* The decode MoE block for ONE token in one cooperative launch (router + top-k -> gate/up + SwiGLU -> down ->
  * weighted sum, two grid barriers): each CTA loads its share of the gate/up rows and its 16 output rows of every
  * routed expert's down matrix as soon as the routing is known, so the down weights stream in under the gate/up

@@ -200,3 +200,45 @@ def test_moe_block_graph_replay_deterministic(fb):
         g.replay()
     torch.cuda.synchronize()
     np.testing.assert_array_equal(host(out_g), ref)
+
+
+@needs_cuda
+@pytest.mark.parametrize("cfg,M,ranks", [(BASE, 2, 2), (BASE, 8, 8), (FLINT, 4, 4)])
+def test_fused_ep_rows_match_down_ep_and_sum_to_the_layer(fb, cfg, M, ranks):
+    """flint_moe_fused_ep on each expert range of `ranks` ranks (run here one after the other): its per-route rows
+    equal flint_moe_down_ep's bit for bit, and their sum over the ranks, combined in slot order, is the one-GPU
+    fused output (the data-parallel decode's MoE)."""
+    from flint_b200 import fp4moe_decode as fm
+    ops = torch.ops.flint_b200
+    rng = np.random.default_rng(300 + M + cfg["E"])
+    H, E, topk, I = cfg["H"], cfg["E"], cfg["topk"], cfg["I"]
+    L = make_layer(rng, **cfg)
+    w = dev_weights(L, topk, cfg["score"])
+    x, res = dev_bf16(bf16(rng, (M, H))), dev_bf16(bf16(rng, (M, H)))
+    nw, gate = dev_bf16(L["nw"]), dev_bf16(L["gate"])
+    ref_out, ref_res = fm.moe_decode(x, res, nw, 1e-6, gate, w, fused=True)
+    tw, ti, xn, _ = fm.route_norm(x, res, nw, 1e-6, gate, topk=topk, score=cfg["score"])
+    total = torch.zeros((M * topk, H), dtype=torch.float32, device="cuda")
+    for r in range(ranks):
+        lo, n = r * E // ranks, E // ranks
+        sl = lambda t: t[lo:lo + n].contiguous()
+        y = torch.empty((M * topk, H), dtype=torch.bfloat16, device="cuda")
+        res_o = torch.empty_like(res)
+        ids_o = torch.empty((M, topk), dtype=torch.int32, device="cuda")
+        tw_o = torch.empty((M, topk), dtype=torch.float32, device="cuda")
+        ops.moe_fused_ep(x, res, nw, 1e-6, gate, topk, w.score_fn, sl(w.w13), sl(w.s13), sl(w.g13), sl(w.w2), sl(w.s2),
+                         sl(w.g2), E, lo, y, res_o, ids_o, tw_o)
+        act = torch.empty((M * topk, I), dtype=torch.bfloat16, device="cuda")
+        ops.moe_up_ep(xn, ti, sl(w.w13), sl(w.s13), sl(w.g13), E, lo, act)
+        y_chain = torch.empty_like(y)
+        ops.moe_down_ep(act, ti, sl(w.w2), sl(w.s2), sl(w.g2), E, lo, y_chain)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(host(ids_o), host(ti))
+        np.testing.assert_array_equal(host(tw_o), host(tw))
+        np.testing.assert_array_equal(host(res_o), host(ref_res))
+        np.testing.assert_array_equal(host(y), host(y_chain))
+        total += y.float()
+    out = torch.empty_like(ref_out)
+    ops.moe_combine(total.to(torch.bfloat16), tw, out)        # exact: one non-zero term per element
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(host(out), host(ref_out))
