@@ -41,6 +41,80 @@ __global__ void keys_allmax_peer_kernel(const unsigned long long* __restrict__ k
   pdl_trigger();
 }
 
+// ---- data-parallel decode (one stream per rank, experts split over the ranks) ----
+//
+// Token gather, one CTA: this rank's two rows (attention output, residual: bf16 [2][H]) go into every rank's token
+// table at [parity][rank] with 16-byte stores, then its flag on every rank; once every rank's flag shows this
+// launch, the table is copied to `out` [world][2][H] (a fixed buffer, so captured graphs keep their pointers).
+__global__ void dp_gather_peer_kernel(const bf16* __restrict__ send, int H, const PeerSet ps, bf16* __restrict__ out) {
+  __shared__ int s_ok;
+  pdl_wait();
+  const int tid = threadIdx.x, W = ps.world, r = ps.rank;
+  PeerHeader* own = peer_header(ps.base[r]);
+  const unsigned ep = ld_relaxed_sys_u32(&own->dp_tok_epoch) + 1u, par = ep & 1u;
+  const int n16 = 2 * H / 8;                                       // 16-byte units of the two rows
+  const uint4* src = reinterpret_cast<const uint4*>(send);
+  for (int i = tid; i < n16 * W; i += blockDim.x) {
+    const int p = i / n16, u = i - p * n16;
+    reinterpret_cast<uint4*>(peer_dp_tokens(ps.base[p], par, H) + (size_t)r * 2 * H)[u] = src[u];
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (tid < W) st_release_sys_u32(reinterpret_cast<unsigned*>(ps.base[tid] + kPeerDpTokFlagsOff) + r, ep);
+  if (tid == 0) s_ok = 1;
+  __syncthreads();
+  if (tid < W && !peer_wait(reinterpret_cast<unsigned*>(ps.base[r] + kPeerDpTokFlagsOff) + tid, ep, own)) s_ok = 0;
+  __syncthreads();                                                 // orders the copy after the acquiring loads
+  const uint4* tab = reinterpret_cast<const uint4*>(peer_dp_tokens(ps.base[r], par, H));
+  for (int i = tid; i < n16 * W; i += blockDim.x) reinterpret_cast<uint4*>(out)[i] = s_ok ? __ldcg(tab + i) : make_uint4(0, 0, 0, 0);
+  __syncthreads();
+  if (tid == 0) own->dp_tok_epoch = ep;
+  pdl_trigger();
+}
+
+// Row scatter + combine, one CTA: y [world * topk][H] holds the rows of every token's routes whose expert is local
+// (zeros elsewhere); the rows of token m's local routes go to rank m's row table at [parity][this rank][slot], then
+// this rank's flag on every rank.  Once every flag shows this launch, out[h] = bf16(sum_s tw[s] * row_s[h]) in slot
+// order (fp32 FMA), row_s read from the rank that owns expert ids[rank * topk + s] (experts split in equal
+// contiguous ranges): the one-GPU weighted sum bit for bit.
+__global__ void dp_combine_peer_kernel(const bf16* __restrict__ y, const int* __restrict__ ids,
+                                       const float* __restrict__ tw, int topk, int E, int H, const PeerSet ps,
+                                       bf16* __restrict__ out) {
+  __shared__ int s_ok, s_src[kPeerSlots];
+  pdl_wait();
+  const int tid = threadIdx.x, W = ps.world, r = ps.rank, per = E / W;
+  PeerHeader* own = peer_header(ps.base[r]);
+  const unsigned ep = ld_relaxed_sys_u32(&own->dp_row_epoch) + 1u, par = ep & 1u;
+  const int n16 = H / 8;
+  for (int i = tid; i < W * topk * n16; i += blockDim.x) {        // push this rank's local routes of every token
+    const int route = i / n16, u = i - route * n16, m = route / topk, s = route - m * topk;
+    const int e = ids[route];
+    if (e < r * per || e >= (r + 1) * per) continue;
+    reinterpret_cast<uint4*>(peer_dp_rows(ps.base[m], par, H) + ((size_t)r * kPeerSlots + s) * H)[u] =
+        reinterpret_cast<const uint4*>(y + (size_t)route * H)[u];
+  }
+  if (tid < topk) {
+    const int e = ids[r * topk + tid];
+    s_src[tid] = min(max(e / per, 0), W - 1);
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (tid < W) st_release_sys_u32(reinterpret_cast<unsigned*>(ps.base[tid] + kPeerDpRowFlagsOff) + r, ep);
+  if (tid == 0) s_ok = 1;
+  __syncthreads();
+  if (tid < W && !peer_wait(reinterpret_cast<unsigned*>(ps.base[r] + kPeerDpRowFlagsOff) + tid, ep, own)) s_ok = 0;
+  __syncthreads();
+  const bf16* rows = peer_dp_rows(ps.base[r], par, H);
+  for (int h = tid; h < H; h += blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < topk; ++s) acc = fmaf(tw[r * topk + s], peer_ldcg_bf16(rows + ((size_t)s_src[s] * kPeerSlots + s) * H + h), acc);
+    out[h] = __float2bfloat16_rn(s_ok ? acc : 0.f);
+  }
+  __syncthreads();
+  if (tid == 0) own->dp_row_epoch = ep;
+  pdl_trigger();
+}
+
 int peer_set(const void* const* peers, int rank, int world, PeerSet* ps) {
   if (!peers) return FLINT_ERR_ARGUMENT;
   if (world < 2 || world > kPeerMax || rank < 0 || rank >= world) return FLINT_ERR_SHAPE;
@@ -117,4 +191,29 @@ extern "C" int flint_argmax_keys_allmax_peer(const uint64_t* keys, int64_t M, co
   if (rc) return rc;
   return launch(keys_allmax_peer_kernel, dim3(1), dim3(32), 0, stream, pdl,
                 reinterpret_cast<const unsigned long long*>(keys), (int)M, ps, (int*)tokens);
+}
+
+extern "C" int flint_dp_gather_peer(const void* send, int64_t H, const void* const* peers, int rank, int world, void* out,
+                                    int pdl, void* stream) {
+  if (!send || !out) return FLINT_ERR_ARGUMENT;
+  if (H < 8 || H % 8 != 0 || H > 65536) return FLINT_ERR_SHAPE;
+  if (!aligned(send, 16) || !aligned(out, 16)) return FLINT_ERR_ALIGN;
+  PeerSet ps;
+  const int rc = peer_set(peers, rank, world, &ps);
+  if (rc) return rc;
+  return launch(dp_gather_peer_kernel, dim3(1), dim3(512), 0, stream, pdl, (const bf16*)send, (int)H, ps, (bf16*)out);
+}
+
+extern "C" int flint_dp_combine_peer(const void* y, const int32_t* topk_ids, const float* topk_weights, int64_t topk,
+                                     int64_t E, int64_t H, const void* const* peers, int rank, int world, void* out,
+                                     int pdl, void* stream) {
+  if (!y || !topk_ids || !topk_weights || !out) return FLINT_ERR_ARGUMENT;
+  if (topk < 1 || topk > kPeerSlots || H < 8 || H % 8 != 0 || H > 65536 || E < world || E % world != 0)
+    return FLINT_ERR_SHAPE;
+  if (!aligned(y, 16)) return FLINT_ERR_ALIGN;
+  PeerSet ps;
+  const int rc = peer_set(peers, rank, world, &ps);
+  if (rc) return rc;
+  return launch(dp_combine_peer_kernel, dim3(1), dim3(512), 0, stream, pdl, (const bf16*)y, (const int*)topk_ids,
+                topk_weights, (int)topk, (int)E, (int)H, ps, (bf16*)out);
 }

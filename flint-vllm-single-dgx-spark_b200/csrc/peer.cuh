@@ -8,6 +8,11 @@
 //   [4352, 4384)        head flags u32 [8 source ranks]
 //   [4608, 5632)        head keys u64 [2 parities][8 source ranks][8 rows]
 //   [8192, 8192+32H)    MoE rows bf16 [2 parities][8 slots][H]
+//   [4384, 4416)        data-parallel token flags u32 [8 source ranks]
+//   [4416, 4448)        data-parallel row flags u32 [8 source ranks]
+//   [8192+32H, +64H)    data-parallel tokens bf16 [2 parities][8 source ranks][2 rows: attention output, residual][H]
+//   [8192+96H, +256H)   data-parallel rows bf16 [2 parities][8 source ranks][8 slots][H] (the routes of this rank's
+//                       token that the source rank computed)
 //
 // Protocol (both exchanges): the writer stores its data into every rank's buffer (its own included), fences at
 // system scope, then stores the launch epoch into its flag slot on every rank with a release store; the reader
@@ -30,18 +35,24 @@ constexpr size_t kPeerHeadFlagsOff = kPeerMoeFlagsOff + (size_t)kPeerMoeBlocks *
 constexpr size_t kPeerHeadKeysOff = 4608;
 constexpr size_t kPeerMoeRowsOff = 8192;
 constexpr int kPeerSlots = 8;
+constexpr size_t kPeerDpTokFlagsOff = 4384;
+constexpr size_t kPeerDpRowFlagsOff = 4416;
 constexpr int kPeerRowsMax = 8;                   // head rows (tokens) per exchange
 constexpr unsigned long long kPeerWaitNs = 10ull * 1000 * 1000 * 1000;   // 10 s
 enum : unsigned { STATUS_PEER_TIMEOUT = 4u };
 
 static_assert(kPeerHeadFlagsOff + kPeerMax * 4 <= kPeerHeadKeysOff, "peer layout");
 static_assert(kPeerHeadKeysOff + 2 * kPeerMax * kPeerRowsMax * 8 <= kPeerMoeRowsOff, "peer layout");
+static_assert(kPeerHeadFlagsOff + kPeerMax * 4 <= kPeerDpTokFlagsOff && kPeerDpRowFlagsOff + kPeerMax * 4 <= kPeerHeadKeysOff,
+              "peer layout");
 
 struct PeerHeader {
   unsigned moe_epoch;
   unsigned head_epoch;
   unsigned status;
-  unsigned pad[61];
+  unsigned dp_tok_epoch;                          // data-parallel token gather launches
+  unsigned dp_row_epoch;                          // data-parallel row scatter launches
+  unsigned pad[59];
 };
 
 struct PeerSet {
@@ -52,7 +63,11 @@ struct PeerSet {
 // Host: validates and packs the per-rank buffer pointers of one exchange (FLINT_OK or an error code).
 int peer_set(const void* const* peers, int rank, int world, PeerSet* ps);
 
-__host__ __device__ constexpr size_t peer_buffer_bytes(int H) { return kPeerMoeRowsOff + (size_t)2 * kPeerSlots * H * 2; }
+__host__ __device__ constexpr size_t peer_dp_tok_off(int H) { return kPeerMoeRowsOff + (size_t)2 * kPeerSlots * H * 2; }
+__host__ __device__ constexpr size_t peer_dp_row_off(int H) { return peer_dp_tok_off(H) + (size_t)2 * kPeerMax * 2 * H * 2; }
+__host__ __device__ constexpr size_t peer_buffer_bytes(int H) {
+  return peer_dp_row_off(H) + (size_t)2 * kPeerMax * kPeerSlots * H * 2;
+}
 
 __device__ __forceinline__ PeerHeader* peer_header(uint8_t* b) { return reinterpret_cast<PeerHeader*>(b); }
 __device__ __forceinline__ unsigned* peer_moe_flags(uint8_t* b) { return reinterpret_cast<unsigned*>(b + kPeerMoeFlagsOff); }
@@ -62,6 +77,12 @@ __device__ __forceinline__ unsigned long long* peer_head_keys(uint8_t* b, unsign
 }
 __device__ __forceinline__ bf16* peer_moe_rows(uint8_t* b, unsigned parity, int H) {
   return reinterpret_cast<bf16*>(b + kPeerMoeRowsOff) + (size_t)parity * kPeerSlots * H;
+}
+__device__ __forceinline__ bf16* peer_dp_tokens(uint8_t* b, unsigned parity, int H) {   // [8 src][2][H]
+  return reinterpret_cast<bf16*>(b + peer_dp_tok_off(H)) + (size_t)parity * kPeerMax * 2 * H;
+}
+__device__ __forceinline__ bf16* peer_dp_rows(uint8_t* b, unsigned parity, int H) {     // [8 src][8 slots][H]
+  return reinterpret_cast<bf16*>(b + peer_dp_row_off(H)) + (size_t)parity * kPeerMax * kPeerSlots * H;
 }
 
 __device__ __forceinline__ void st_release_sys_u32(unsigned* p, unsigned v) {

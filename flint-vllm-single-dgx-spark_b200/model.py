@@ -243,7 +243,7 @@ class Decoder:
             raise ValueError(f"exchange must be 'peer' or 'nccl', got {exchange!r}")
         self.group, self.exchange, self.prefetch = group, exchange, prefetch
         self.peers = None
-        if model.world > 1 and exchange == "peer" and not dp:
+        if model.world > 1 and exchange == "peer":
             from .peer import PeerBuffers
             self.peers = PeerBuffers(group, model.cfg.hidden)
         if attn not in ("block", "chain"):
@@ -315,7 +315,8 @@ class Decoder:
         # (peer exchange: the MoE block exchanges in-kernel; the head adds one exchange kernel)
         # dense layers: route + up + down; the shared expert: up + down (its bf16 add is a torch elementwise op)
         ep = model.world > 1
-        moe_launches = (4 if ep else 3) if moe == "chain" else 2 if (ep and exchange == "nccl") else 2 if moe == "dp" else 1
+        moe_launches = ((4 if ep else 3) if moe == "chain" else 2 if (ep and exchange == "nccl")
+                        else (3 if exchange == "peer" else 2) if moe == "dp" else 1)
         n_dense = len(c.mlp_only_layers)
         shared_fused = (c.shared_inter and model.world == 1 and moe == "block" and c.shared_inter % 256 == 0
                         and c.shared_inter <= 1024 and c.topk < 8)
@@ -381,14 +382,25 @@ class Decoder:
             import torch.distributed as dist
             N, r = m.world, m.rank
             x_all, res_all = self.dp_recv[:, 0], self.dp_recv[:, 1]
-            seq += [("dp_gather", lambda: dist.all_gather_into_tensor(self.dp_recv.view(-1), self.dp_send.view(-1),
-                                                                       group=self.group)),
+            pp = self.peers
+            if pp is not None:        # exchanges over NVLink peer memory inside our own launches
+                gather = ("dp_gather_peer", lambda: ops.dp_gather_peer(self.dp_send, pp.ptrs, pp.rank, self.dp_recv))
+                combine = ("dp_combine_peer", lambda: ops.dp_combine_peer(self.dp_y, self.dp_ti, self.dp_tw,
+                                                                          c.num_experts, pp.ptrs, pp.rank, self.h))
+            else:
+                gather = ("dp_gather", lambda: dist.all_gather_into_tensor(self.dp_recv.view(-1), self.dp_send.view(-1),
+                                                                           group=self.group))
+
+                def combine_nccl():
+                    dist.reduce_scatter_tensor(self.dp_mine, self.dp_y, group=self.group)
+                    ops.moe_combine(self.dp_mine, self.dp_tw[r:r + 1], self.h)
+                combine = ("dp_combine", combine_nccl)
+            seq += [gather,
                     ("moe_fused_ep", lambda: ops.moe_fused_ep(x_all, res_all, L["ln2"], c.rms_eps, L["gate"], c.topk,
                                                               ew.score_fn, ew.w13, ew.s13, ew.g13, ew.w2, ew.s2, ew.g2,
                                                               c.num_experts, m.e_lo, self.dp_y, self.dp_res, self.dp_ti,
                                                               self.dp_tw)),
-                    ("dp_scatter", lambda: dist.reduce_scatter_tensor(self.dp_mine, self.dp_y, group=self.group)),
-                    ("combine", lambda: ops.moe_combine(self.dp_mine, self.dp_tw[r:r + 1], self.h))]
+                    combine]
             return seq
         if c.is_dense(l):
             # dense SwiGLU: the route kernel's add + RMSNorm (an all-zero 32-way router sends every token to expert
@@ -547,12 +559,16 @@ class Decoder:
         """Bytes one launch of kernel `name` must move at batch M and context ctx (weights / KV read once,
         activations in and out): the roofline numerator."""
         c, M = self.c, self.M
-        if self.dp and name in ("moe_fused_ep", "combine", "head"):
+        if self.dp and name in ("moe_fused_ep", "combine", "head", "dp_gather_peer", "dp_combine_peer"):
             M = self.m.world                              # the MoE and the head work on every rank's token
         nv = lambda n, k: n * k // 2 + n * k // 16
         H, D = c.hidden, c.head_dim
         if name == "combine":
             return c.topk * H * 2 + c.topk * 4 + H * 2
+        if name == "dp_gather_peer":                       # this rank's rows to every rank, every rank's rows read
+            return 2 * (2 * H * 2) * self.m.world
+        if name == "dp_combine_peer":                      # local routes' rows pushed, this token's rows read
+            return 2 * c.topk * H * 2 + H * 2
         if name == "qkv":
             return nv(c.qkv_rows, H) + M * (3 * H * 2 + c.qkv_rows * 2 + c.num_heads * D * 2 + 2 * c.num_kv_heads * D * 2)
         if name == "attention":

@@ -560,6 +560,45 @@ def _(x, res, norm_w, eps, gate_w, topk, score_fn, w13, s13, g13, w2, s2, g2, ex
     return None
 
 
+@torch.library.custom_op(f"{NS}::dp_gather_peer", mutates_args=("out",))
+def dp_gather_peer(send: torch.Tensor, peers: list[int], rank: int, out: torch.Tensor) -> None:
+    """Every rank's two rows (bf16 [2, H]) into out [world, 2, H] over NVLink peer memory (flint_dp_gather_peer)."""
+    _lib.require_cuda(send, "dp_gather_peer")
+    H = send.shape[-1]
+    if send.dtype != torch.bfloat16 or send.numel() != 2 * H or out.numel() != len(peers) * 2 * H or \
+            not send.is_contiguous() or not out.is_contiguous():
+        raise _lib.FlintError("dp_gather_peer: send bf16 [2, H], out [world, 2, H], contiguous")
+    rc = lib().flint_dp_gather_peer(ptr(send), H, _peer_array(peers), int(rank), len(peers), ptr(out), PDL,
+                                    stream_ptr(send.device))
+    check(rc, "flint_dp_gather_peer")
+
+
+@dp_gather_peer.register_fake
+def _(send, peers, rank, out):
+    return None
+
+
+@torch.library.custom_op(f"{NS}::dp_combine_peer", mutates_args=("out",))
+def dp_combine_peer(y: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor, num_experts: int,
+                    peers: list[int], rank: int, out: torch.Tensor) -> None:
+    """Each route's row to its token's rank over NVLink peer memory, then this rank's token's slot-order weighted
+    sum (flint_dp_combine_peer)."""
+    _lib.require_cuda(y, "dp_combine_peer")
+    W = len(peers)
+    R, H = y.shape
+    topk = topk_ids.shape[-1]
+    if R != W * topk or topk_ids.numel() != R or topk_weights.numel() != R or out.numel() != H:
+        raise _lib.FlintError("dp_combine_peer: y [world * topk, H], ids / weights [world, topk], out [H]")
+    rc = lib().flint_dp_combine_peer(ptr(y), ptr(topk_ids), ptr(topk_weights), topk, int(num_experts), H,
+                                     _peer_array(peers), int(rank), W, ptr(out), PDL, stream_ptr(y.device))
+    check(rc, "flint_dp_combine_peer")
+
+
+@dp_combine_peer.register_fake
+def _(y, topk_ids, topk_weights, num_experts, peers, rank, out):
+    return None
+
+
 @torch.library.custom_op(f"{NS}::keys_allmax_peer", mutates_args=("tokens",))
 def keys_allmax_peer(keys: torch.Tensor, peers: list[int], rank: int, tokens: torch.Tensor) -> None:
     """Argmax over the vocabulary shards of all ranks (flint_argmax_keys_allmax_peer)."""

@@ -314,6 +314,18 @@ int flint_moe_block_peer(const void* x, int64_t ldx, const void* res, const void
                          const float* g13, const void* w2, const void* s2, const float* g2, int64_t I, int64_t expert_lo,
                          int64_t n_local, const void* const* peers, int rank, int world, void* out, void* res_out,
                          void* workspace, const flint_l2_prefetch* next, int pdl, void* stream);
+/* Data-parallel decode (one stream per rank, experts split in equal contiguous ranges), exchanges fused over NVLink
+ * peer memory (no collective library call; bounded waits, the peer-buffer status word records a time-out).
+ * flint_dp_gather_peer: this rank's two rows send bf16 [2][H] (attention output, residual) to every rank; out
+ * bf16 [world][2][H] = every rank's rows in rank order.
+ * flint_dp_combine_peer: y bf16 [world * topk][H] = the per-route rows of every rank's token (flint_moe_fused_ep: this
+ * rank's experts' routes, zeros elsewhere); each route's row goes to its token's rank, and out bf16 [H] =
+ * bf16(sum_s topk_weights[rank * topk + s] * row_s) in slot order for this rank's token (topk_ids / topk_weights
+ * [world][topk], identical on every rank).  E % world == 0, topk <= 8.  No counterpart in the reference (one GPU). */
+int flint_dp_gather_peer(const void* send, int64_t H, const void* const* peers, int rank, int world, void* out, int pdl,
+                         void* stream);
+int flint_dp_combine_peer(const void* y, const int32_t* topk_ids, const float* topk_weights, int64_t topk, int64_t E,
+                          int64_t H, const void* const* peers, int rank, int world, void* out, int pdl, void* stream);
 /* Vocabulary-shard argmax exchange: keys = this rank's M (<= 8) keys from flint_lm_head_nv4_shard; tokens int32 [M]
  * = the argmax over all ranks' shards (lowest id among the largest logits), -1 if a peer wait timed out. */
 int flint_argmax_keys_allmax_peer(const uint64_t* keys, int64_t M, const void* const* peers, int rank, int world,

@@ -166,3 +166,69 @@ def test_data_parallel_streams_gloo(world):
         assert p.exitcode == 0
     for rank, res in out:
         assert all(res.values()), (rank, res)
+
+
+def _dp_dispatch_worker(rank, world, port, q):
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "tests"))
+    from conftest import load_package
+    load_package()
+    calls = []
+
+    class Rec:
+        def __getattr__(self, name):
+            if name.startswith("__"):
+                raise AttributeError(name)
+            return lambda *a: calls.append((name, a))
+    torch.ops.flint_b200 = Rec()
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from flint_b200.model import Decoder, FlintConfig, FlintModel
+        cfg = FlintConfig(hidden=256, layers=2, num_heads=4, num_kv_heads=2, num_experts=32, topk=4, moe_inter=64,
+                          vocab=512 * world)
+        m = FlintModel(cfg, device="cpu", seed=3, max_ctx=64, max_batch=1, shard=(rank, world))
+        dec = Decoder(m, batch=1, group=dist.group.WORLD, exchange="nccl", dp=True)
+        dec.dp_send.copy_(torch.full_like(dec.dp_send, float(rank + 1)))
+        for _, fn in dec.layer_ops(0):
+            fn()
+        names = [n for n, _ in calls]
+        fe = dict(calls)["moe_fused_ep"]
+        comb = dict(calls)["moe_combine"]
+        res = {
+            "names": names == ["attn_block", "moe_fused_ep", "moe_combine"],
+            # the attention writes this rank's rows of the gathered pair
+            "attn_out": calls[0][1][24].data_ptr() == dec.dp_send[0:1].data_ptr()
+                        and calls[0][1][25].data_ptr() == dec.dp_send[1:2].data_ptr(),
+            # every rank's rows arrived, in rank order
+            "gathered": all(bool((dec.dp_recv[r] == r + 1).all()) for r in range(world)),
+            # the MoE runs every rank's token against this rank's experts
+            "moe_args": fe[0].shape == (world, 256) and fe[0].stride(0) == 512 and fe[13] == 32
+                        and fe[14] == rank * 32 // world and fe[7].shape[0] == 32 // world,
+            # this rank's token combines its own rows and weights
+            "combine": comb[0] is dec.dp_mine and comb[1].data_ptr() == dec.dp_tw[rank:rank + 1].data_ptr()
+                       and comb[2] is dec.h and dec.res_b.data_ptr() == dec.dp_res[rank:rank + 1].data_ptr(),
+            "launches": dec.launches_per_step == 2 * 1 + 2 * 2 + 3,
+        }
+        q.put((rank, res))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_data_parallel_decoder_dispatch_gloo():
+    """The data-parallel Decoder's per-layer sequence on two gloo ranks (kernel calls recorded, the collectives real):
+    the attention writes this rank's half of the exchanged pair, every rank's pair arrives in rank order, the fused
+    expert-parallel MoE runs all tokens against this rank's experts, and the combine takes this rank's token."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dp_dispatch_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=180) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, res in out:
+        assert all(res.values()), (rank, res)
