@@ -344,7 +344,7 @@ def main():
     ap.add_argument("--multi", default="dp", choices=["dp", "ep"],
                     help="N > 1: one stream per GPU (data-parallel attention + expert-parallel MoE, weak scaling) or "
                          "one stream over all GPUs (expert parallel, attention replicated, strong scaling)")
-    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+    ap.add_argument("--exchange", default=None, choices=["peer", "nccl"],
                     help="N > 1: MoE / head exchange fused into the kernels over NVLink peer memory, or NCCL calls")
     ap.add_argument("--streams", type=int, default=1, help="concurrent streams (1..8; BASELINE configs[4])")
     ap.add_argument("--sample", action="store_true", help="seeded T 1.0 / top-k 20 / top-p 0.95 sampling")
@@ -352,6 +352,8 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.exchange is None:       # measured on two B200s: NCCL for the data-parallel exchanges, peer stores for ep
+        args.exchange = "nccl" if args.multi == "dp" else "peer"
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -46,7 +46,8 @@ SAMPLING = dict(temperature=1.0, top_k=20, top_p=0.95)
 CASES = [("b1_block_peer", 1, "block", "peer", False), ("b1_block_nccl", 1, "block", "nccl", False),
          ("b3_chain", 3, "chain", "peer", False), ("b3_chain_sampled", 3, "chain", "peer", True),
          ("b1_block_sampled", 1, "block", "peer", True),
-         ("dp_streams", 1, "dp", "nccl", False)]           # one stream per rank: data-parallel attention + EP MoE
+         ("dp_streams", 1, "dp", "peer", False),           # one stream per rank: data-parallel attention + EP MoE
+         ("dp_streams_nccl", 1, "dp", "nccl", False)]
 
 
 def decode(model, prompt, n, batch, moe, group=None, exchange="peer", sampled=False):
@@ -66,10 +67,10 @@ def decode(model, prompt, n, batch, moe, group=None, exchange="peer", sampled=Fa
     return toks, h, status
 
 
-def decode_dp(model, prompt, n, group, rank):
+def decode_dp(model, prompt, n, group, rank, exchange="peer"):
     """This rank's stream (prompt row `rank`) through the data-parallel decode; -> (tokens [1, n], h [1, H])."""
     from flint_b200.model import Decoder
-    dec = Decoder(model, batch=1, group=group, dp=True)
+    dec = Decoder(model, batch=1, group=group, dp=True, exchange=exchange)
     dec.reserve_history(n)
     dec.capture()
     dec.prefill(prompt[rank:rank + 1])
@@ -103,7 +104,7 @@ def main():
     runs = {}
     for name, batch, moe, exchange, sampled in cases:
         if moe == "dp":                                 # every rank's stream, gathered to rank 0
-            toks, h = decode_dp(model, prompt, args.tokens, dist.group.WORLD, rank)
+            toks, h = decode_dp(model, prompt, args.tokens, dist.group.WORLD, rank, exchange)
             all_t = [torch.zeros_like(toks) for _ in range(world)]
             all_h = [torch.zeros_like(h) for _ in range(world)]
             dist.all_gather(all_t, toks)
