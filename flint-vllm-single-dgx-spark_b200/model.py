@@ -584,6 +584,9 @@ class Decoder:
         if name == "attn_block":
             return (self.algorithmic_bytes("qkv", ctx) + self.algorithmic_bytes("attention", ctx)
                     + self.algorithmic_bytes("o", ctx))
+        if name == "moe_block_shared":                    # + the shared expert's gate/up and down
+            SI = c.shared_inter
+            return self.algorithmic_bytes("moe_block", ctx) + nv(2 * SI, H) + nv(H, SI)
         if name in ("moe_fused", "moe_block"):
             return (self.algorithmic_bytes("route", ctx) + self.algorithmic_bytes("up", ctx)
                     + self.algorithmic_bytes("down", ctx))

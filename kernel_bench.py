@@ -53,6 +53,9 @@ def main(argv=None):
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--moe", default=None, choices=["block", "chain", "fused"])
     ap.add_argument("--attn", default="block", choices=["block", "chain"])
+    ap.add_argument("--config", default="baseline", choices=["baseline", "flint"],
+                    help="the BASELINE model's layer shapes, or Flint's own (256 experts sigmoid top-6, I 512, shared "
+                         "expert 1024: moe_block_shared)")
     ap.add_argument("--rows", type=int, default=151552)
     ap.add_argument("--cols", type=int, default=2048)
     args = ap.parse_args(argv)
@@ -61,9 +64,10 @@ def main(argv=None):
         return time_format_kernel(args)
     from flint_b200.model import Decoder, FlintConfig, FlintModel
 
-    cfg = FlintConfig(layers=args.layers)
+    cfg = FlintConfig(layers=args.layers) if args.config == "baseline" else FlintConfig.flint(layers=args.layers)
     dev = torch.device("cuda", torch.cuda.current_device())
-    model = FlintModel(cfg, dev, seed=5, max_ctx=args.ctx + 16, max_batch=args.batch)
+    model = FlintModel(cfg, dev, seed=5, max_ctx=args.ctx + 16, max_batch=args.batch,
+                       weights="quantized" if args.config == "baseline" else "codes")
     dec = Decoder(model, batch=args.batch, moe=args.moe, attn=args.attn)
     prompt = np.random.default_rng(3).integers(0, cfg.vocab, size=(args.batch, args.ctx))
     dec.fill_kv_random(prompt)
@@ -104,7 +108,7 @@ def time_kernel(name, args, dec, model, cfg, dev):
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / (args.reps * len(fns))
     nbytes = dec.algorithmic_bytes("head" if name.startswith("head") else name, args.ctx)
-    print(json.dumps({"kernel": name, "batch": args.batch, "moe": dec.moe, "ctx": args.ctx,
+    print(json.dumps({"kernel": name, "config": args.config, "batch": args.batch, "moe": dec.moe, "ctx": args.ctx,
                       "launches": args.reps * len(fns), "us_per_launch": round(us, 2), "bytes_per_launch": nbytes,
                       "GBps": round(nbytes / us / 1e3, 1)}), flush=True)
     del g
