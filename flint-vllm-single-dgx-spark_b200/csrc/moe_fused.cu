@@ -13,7 +13,9 @@
 //   F  out[m, r] = bf16(sum_s tw[m, s] * y[m*k + s, r]) in slot order for the CTA's rows
 //
 // Numerics are those of the per-op kernels in moe.cu (same reduction orders), so routing is bit identical to them.
-// Up and down tiles are split over CTAs by a linear partition of their stage counts (balanced to within one tile).
+// Up tiles are split evenly over all CTAs, and so are down tiles: every CTA works in both phases, its producer
+// streaming its down tiles into the ring behind its up tiles (they do not depend on the activations), so the down
+// weights are in flight while the grid waits at barrier 1.
 //
 // Expert-parallel mode (flint_moe_fused_ep, y_out given): the weights hold experts [e_lo, e_hi) only; the router and
 // top-k run in full (identical on every rank), only routes whose expert is local get tiles, and phase F writes
@@ -61,11 +63,6 @@ __host__ __device__ inline size_t moe_fused_ws_bytes(int E, int H, int I) {
   return sizeof(MoeFusedWs) + (size_t)kMaxTokens * E * 4 + (size_t)kMaxRoutes * I * 2 + (size_t)kMaxRoutes * H * 2;
 }
 
-// first tile whose stage prefix reaches `target` (prefix = nu * min(i, U) + nd * max(0, i - U), strictly increasing)
-__device__ __forceinline__ int tile_at(long target, int U, int nu, int nd) {
-  if (target <= (long)U * nu) return (int)((target + nu - 1) / nu);
-  return U + (int)((target - (long)U * nu + nd - 1) / nd);
-}
 
 template <int NS, int NV>
 __global__ void __launch_bounds__((kFW + 1) * 32, 1)
@@ -88,7 +85,7 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   __shared__ int shift_x[kMaxTokens], shift_a[kMaxRoutes];
   __shared__ float red[kFW * kMaxRoutes];
   __shared__ int s_ok;
-  __shared__ int tiles[4];                   // first / end tile of this CTA, U, total
+  __shared__ int tiles[4];                   // this CTA's up tiles [tiles[0], tiles[1]), down tiles [tiles[2], tiles[3])
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int M = a.M, H = a.H, I = a.I, E = a.E, topk = a.topk, R = M * topk;
@@ -133,11 +130,13 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
       }
       tma_prefetch_desc(&up_c);
       tma_prefetch_desc(&dn_c);
-      const int t0 = tiles[0], t1 = tiles[1], U = tiles[2];
+      const int u0 = tiles[0], u1 = tiles[1], d0 = tiles[2], d1 = tiles[3];
+      const int nup = u1 - u0, ntiles = nup + (d1 - d0);
       int slot = 0, s = 0;
       unsigned phase = 0;
-      for (int t = t0; t < t1; ++t) {
-        const bool up = t < U;
+      for (int i = 0; i < ntiles; ++i) {
+        const bool up = i < nup;
+        const int t = up ? u0 + i : d0 + (i - nup);             // up tile, or down tile (numbered from 0)
         const int nks = up ? nks_up : nks_dn;
         int y0, y1;
         if (up) {
@@ -145,7 +144,7 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
           y0 = e * 2 * I + j * kFBox;
           y1 = y0 + I;
         } else {
-          const int td = t - U, u = td / tpd, j = td - u * tpd;
+          const int u = t / tpd, j = t - u * tpd;
           y0 = G.exp[u] * H + j * 2 * kFBox;
           y1 = y0 + kFBox;
         }
@@ -230,14 +229,13 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   named_bar_sync(2, NT);
   build_groups(ids_s, R, topk, E, G, sorted, ids_c, status, NT, 2, a.e_lo, a.e_hi);
   const int U = G.n * tpu, Dn = G.n * tpd;
-  const long total = (long)U * nks_up + (long)Dn * nks_dn;
-  const long tau = (total + nb - 1) / nb;
-  const int t0 = min(tile_at((long)blockIdx.x * tau, U, nks_up, nks_dn), U + Dn);
-  const int t1 = min(tile_at((long)(blockIdx.x + 1) * tau, U, nks_up, nks_dn), U + Dn);
+  const int u0 = (int)((long)blockIdx.x * U / nb), u1 = (int)((long)(blockIdx.x + 1) * U / nb);
+  const int d0 = (int)((long)blockIdx.x * Dn / nb), d1 = (int)((long)(blockIdx.x + 1) * Dn / nb);
   if (tid == 0) {
-    tiles[0] = t0;
-    tiles[1] = t1;
-    tiles[2] = U;
+    tiles[0] = u0;
+    tiles[1] = u1;
+    tiles[2] = d0;
+    tiles[3] = d1;
     mbar_arrive(&plan_bar);                  // release the producer
   }
 
@@ -268,7 +266,7 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
     named_bar_sync(1, NT);
   };
 
-  for (int tt = t0; tt < min(t1, U); ++tt) {
+  for (int tt = u0; tt < u1; ++tt) {
     const int u = tt / tpu, j = tt - u * tpu, cnt = G.cnt[u], e = G.exp[u];
     const bool active = g < cnt;
     float d[4];
@@ -288,9 +286,9 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   if (!grid_sync(&ws->sync, nb, 1, NT, 2, &s_ok, status)) return;
 
   // ---------------- phase D: down tiles ----------------
-  if (t1 > U) stage_rows_f16(act_g, I, R, I, xa, shift_a, red, NT, 2, true);
-  for (int tt = max(t0, U); tt < t1; ++tt) {
-    const int td = tt - U, u = td / tpd, j = td - u * tpd, cnt = G.cnt[u], e = G.exp[u];
+  if (d1 > d0) stage_rows_f16(act_g, I, R, I, xa, shift_a, red, NT, 2, true);
+  for (int td = d0; td < d1; ++td) {
+    const int u = td / tpd, j = td - u * tpd, cnt = G.cnt[u], e = G.exp[u];
     const bool active = g < cnt;
     float d[4];
     run_tile(nks_dn, xa + (active ? G.route[u][g] : 0) * xs_stride(I), active, d);
