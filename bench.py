@@ -115,7 +115,7 @@ def dist_setup(n):
 
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of one ncu capture of each kernel at this
 # workload's shapes (batch 1, 6,057-token context); the captures are summarised in profiles/.
-NCU_TRAFFIC: dict[str, float | None] = {"attn_block": 23_159_808, "moe_block": 21_850_880, "head": 179_817_728}
+NCU_TRAFFIC: dict[str, float | None] = {"attn_block": 23_159_552, "moe_block": 21_850_880, "head": 179_817_728}
 
 
 def kernel_rooflines(model, dec, peak, peak_kind, ctx, step_us):

@@ -132,18 +132,34 @@ __device__ __forceinline__ float scale_pow2(float x, int s) {
   return (x * __int_as_float((127 + a) << 23)) * __int_as_float((127 + b) << 23);
 }
 
+// atomicMax of a non-negative float's bits into the shared word *p, reduced first across the calling lanes that name
+// the same word (one atomic per word and warp instead of one per lane contending on it).  Every lane of the calling
+// set must reach the call.
+__device__ __forceinline__ void smem_max_grouped(int* p, float v) {
+  const unsigned act = __activemask();
+  const unsigned grp = __match_any_sync(act, (unsigned long long)p);
+  const unsigned m = __reduce_max_sync(grp, __float_as_uint(v));
+  if ((int)(threadIdx.x & 31) == __ffs(grp) - 1) atomicMax(p, (int)m);
+}
+
 // Stage `rows` activation rows (src + r*ld, bf16, K columns, 16-byte aligned rows) as f16 into xs (row stride
 // xs_stride(K)) with a per-row power-of-two rescale shift[r].  Called by threads [0, nthreads) of the block (a multiple
 // of 32), which synchronise on named barrier `bar` (0 = __syncthreads when nthreads == blockDim.x).
-// One global pass: raw bf16 goes to its permuted place in xs while the row maxima accumulate (shared atomicMax on
-// the non-negative float bits), then each element is converted in place.  red: >= rows floats.
-__device__ __forceinline__ void stage_rows_f16(const bf16* __restrict__ src, int64_t ld, int rows, int K, __half* xs,
-                                               int* shift, float* red, int nthreads, int bar, bool cg = false) {
+// One global pass: raw bf16 goes to its permuted place in xs while the row maxima accumulate (one shared atomicMax
+// per row and warp on the non-negative float bits), then each element is converted in place.  red: >= rows floats.
+// stage_rows_f16_map stages only the rows row_of(0 .. rows-1) (entries < 0 are skipped), each at its own place r in
+// xs / shift / red (red: > the largest r floats); stage_rows_f16 is the identity map.
+template <class RowOf>
+__device__ __forceinline__ void stage_rows_f16_map(const bf16* __restrict__ src, int64_t ld, int rows, int K, __half* xs,
+                                                   int* shift, float* red, int nthreads, int bar, bool cg, RowOf row_of) {
   const int tid = threadIdx.x;
   const int K8 = K >> 3, n = rows * K8;
   auto sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthreads) : "memory"); };
   int* redi = reinterpret_cast<int*>(red);
-  for (int r = tid; r < rows; r += nthreads) redi[r] = 0;
+  for (int i = tid; i < rows; i += nthreads) {
+    const int r = row_of(i);
+    if (r >= 0) redi[r] = 0;
+  }
   sync();
   // up to kB 16-byte loads per thread are issued back to back (one memory round trip per kB * nthreads units)
   constexpr int kB = 4;
@@ -153,30 +169,35 @@ __device__ __forceinline__ void stage_rows_f16(const bf16* __restrict__ src, int
 #pragma unroll
     for (int i = 0; i < kB; ++i) {
       const int idx = base + i * nthreads + tid;
-      rr[i] = idx / K8;
-      kk[i] = idx - rr[i] * K8;
-      if (idx < n) {
+      const int ri = idx / K8;
+      kk[i] = idx - ri * K8;
+      rr[i] = idx < n ? row_of(ri) : -1;
+      if (rr[i] >= 0) {
         const uint4* vp = reinterpret_cast<const uint4*>(src + rr[i] * ld) + kk[i];
         v[i] = cg ? __ldcg(vp) : *vp;                 // cg: rows written by other CTAs of this kernel
       }
     }
 #pragma unroll
     for (int i = 0; i < kB; ++i) {
-      const int idx = base + i * nthreads + tid;
-      if (idx < n) {
-        const int r = rr[i], k8 = kk[i];
+      const int r = rr[i];
+      float mx = 0.f;
+      if (r >= 0) {
         float f[8];
         bf16x8_to_f32(v[i], f);
-        float mx = 0.f;
 #pragma unroll
         for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(f[j]));
-        atomicMax(&redi[r], __float_as_int(mx));
-        *reinterpret_cast<uint4*>(xs + r * xs_stride(K) + xs_perm(k8 * 8)) = v[i];   // 8 consecutive k: one 16-byte unit
+        *reinterpret_cast<uint4*>(xs + r * xs_stride(K) + xs_perm(kk[i] * 8)) = v[i];   // 8 consecutive k: one 16-byte unit
       }
+      // the lanes of a warp hold consecutive units (one to three rows): one atomic per row and warp
+      const unsigned grp = __match_any_sync(0xffffffffu, r);
+      const unsigned gmx = __reduce_max_sync(grp, __float_as_uint(mx));
+      if (r >= 0 && (tid & 31) == __ffs(grp) - 1) atomicMax(&redi[r], (int)gmx);
     }
   }
   sync();
-  for (int r = tid; r < rows; r += nthreads) {
+  for (int i = tid; i < rows; i += nthreads) {
+    const int r = row_of(i);
+    if (r < 0) continue;
     const float mx = __int_as_float(redi[r]);
     int s = 0;
     if (mx > 0.f && !(mx != mx) && mx <= 3.0e38f) s = 14 - ((int)((__float_as_uint(mx) >> 23) & 0xFF) - 127);
@@ -184,7 +205,9 @@ __device__ __forceinline__ void stage_rows_f16(const bf16* __restrict__ src, int
   }
   sync();
   for (int idx = tid; idx < n; idx += nthreads) {
-    const int r = idx / K8, k8 = idx - r * K8;
+    const int ri = idx / K8, k8 = idx - ri * K8;
+    const int r = row_of(ri);
+    if (r < 0) continue;
     uint4* p = reinterpret_cast<uint4*>(xs + r * xs_stride(K) + xs_perm(k8 * 8));
     float f[8];
     bf16x8_to_f32(*p, f);
@@ -198,6 +221,15 @@ __device__ __forceinline__ void stage_rows_f16(const bf16* __restrict__ src, int
     *p = make_uint4(h[0], h[1], h[2], h[3]);
   }
   sync();
+}
+
+struct RowIdentity {
+  __device__ __forceinline__ int operator()(int i) const { return i; }
+};
+
+__device__ __forceinline__ void stage_rows_f16(const bf16* __restrict__ src, int64_t ld, int rows, int K, __half* xs,
+                                               int* shift, float* red, int nthreads, int bar, bool cg = false) {
+  stage_rows_f16_map(src, ld, rows, K, xs, shift, red, nthreads, bar, cg, RowIdentity{});
 }
 
 // s = x (+ res) in fp32; res_out = bf16(s) (global, optional); xn = bf16(s * rsqrt(mean(s^2) + eps) * w) into shared
@@ -388,7 +420,7 @@ __device__ __forceinline__ void norm_stage_f16(const bf16* x, int64_t ldx, const
       mx = fmaxf(mx, fmaxf(fabsf(__low2float(n2)), fabsf(__high2float(n2))));
       pk[j] = *reinterpret_cast<uint32_t*>(&n2);
     }
-    atomicMax(&rmax[m], __float_as_int(mx));
+    smem_max_grouped(&rmax[m], mx);
     *reinterpret_cast<uint4*>(xs + m * xs_stride(H) + xs_perm(k8 * 8)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
   }
   sync();
@@ -476,7 +508,7 @@ __device__ __forceinline__ void norm_stage_f16_1w(const bf16* x, int64_t ldx, co
         mx = fmaxf(mx, fmaxf(fabsf(__low2float(n2)), fabsf(__high2float(n2))));
         pk[m][j] = *reinterpret_cast<uint32_t*>(&n2);
       }
-      atomicMax(&rmax[m], __float_as_int(mx));
+      smem_max_grouped(&rmax[m], mx);
     }
   }
   sync();
@@ -512,9 +544,10 @@ __device__ __forceinline__ void norm_stage_f16_1(const bf16* x, int64_t ldx, con
 // add_rmsnorm_2pass with ONE global pass, for H / 8 <= nthreads (one 8-wide chunk per thread and row, kept in
 // registers): the same per-thread chains, butterfly and warp order, so xn has the same bits.  xn: bf16 [M][H] in
 // shared memory; res_out / xn_out: optional global copies (rows H apart).  red: >= (nthreads/32) * 8 floats.
-__device__ __forceinline__ void add_rmsnorm_1pass(const bf16* x, int64_t ldx, const bf16* res, const bf16* __restrict__ w,
-                                                  float eps, int M, int H, bf16* xn, bf16* res_out, bf16* xn_out,
-                                                  float* red, int nthreads, int bar) {
+// (add_rmsnorm_1pass_w: the thread's 8 norm weights w[8 tid .. 8 tid + 7] passed in, e.g. loaded before a PDL wait.)
+__device__ __forceinline__ void add_rmsnorm_1pass_w(const bf16* x, int64_t ldx, const bf16* res, uint4 wchunk,
+                                                    float eps, int M, int H, bf16* xn, bf16* res_out, bf16* xn_out,
+                                                    float* red, int nthreads, int bar) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = nthreads >> 5, H8 = H >> 3;
   auto sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthreads) : "memory"); };
   const bool own = tid < H8;
@@ -543,7 +576,7 @@ __device__ __forceinline__ void add_rmsnorm_1pass(const bf16* x, int64_t ldx, co
   }
   sync();
   float wf[8];
-  if (own) bf16x8_to_f32(reinterpret_cast<const uint4*>(w)[tid], wf);
+  bf16x8_to_f32(wchunk, wf);
 #pragma unroll
   for (int m = 0; m < 8; ++m) {
     if (m < M && own) {
@@ -565,6 +598,13 @@ __device__ __forceinline__ void add_rmsnorm_1pass(const bf16* x, int64_t ldx, co
     }
   }
   sync();
+}
+
+__device__ __forceinline__ void add_rmsnorm_1pass(const bf16* x, int64_t ldx, const bf16* res, const bf16* __restrict__ w,
+                                                  float eps, int M, int H, bf16* xn, bf16* res_out, bf16* xn_out,
+                                                  float* red, int nthreads, int bar) {
+  const uint4 wc = (int)threadIdx.x < (H >> 3) ? reinterpret_cast<const uint4*>(w)[threadIdx.x] : make_uint4(0u, 0u, 0u, 0u);
+  add_rmsnorm_1pass_w(x, ldx, res, wc, eps, M, H, xn, res_out, xn_out, red, nthreads, bar);
 }
 
 // Whole-block variant (the LM head): all threads, __syncthreads.

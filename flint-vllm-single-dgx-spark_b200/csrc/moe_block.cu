@@ -175,6 +175,8 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   // until the expert weights are requested.  Only bytes no pending kernel writes are named here (the next layer's
   // weights and KV pages, block tables and sequence lengths are final before this step's first kernel).
   if (warp == kXW && lane == 0) l2_prefetch_share(a.pf, cta, nb);
+  // the norm weights (this thread's 8) do not depend on the previous kernel either
+  const uint4 nwc = tid < H / 8 ? reinterpret_cast<const uint4*>(a.nw)[tid] : make_uint4(0u, 0u, 0u, 0u);
   pdl_wait();
   if (tid == 0) FLINT_TL(1);
 
@@ -243,8 +245,8 @@ moe_block_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(ep) : "l"(&ws->epoch) : "memory");
   ep += 1u;
   // ---- R: norm, router rows ----
-  add_rmsnorm_1pass(a.x, a.ldx, a.res, a.nw, a.eps, 1, H, xnb, cta == 0 ? a.res_out : nullptr,
-                    cta == 0 ? a.xn_out : nullptr, red_n, kXT, 1);
+  add_rmsnorm_1pass_w(a.x, a.ldx, a.res, nwc, a.eps, 1, H, xnb, cta == 0 ? a.res_out : nullptr,
+                      cta == 0 ? a.xn_out : nullptr, red_n, kXT, 1);
   if (has_row) {
     const uint4* xp = reinterpret_cast<const uint4*>(xnb);
     float acc = 0.f;

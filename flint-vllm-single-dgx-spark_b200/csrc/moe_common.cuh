@@ -103,8 +103,12 @@ struct Groups {
 // Threads [0, nthreads) of the block call it and synchronise on named barrier `bar` (0 with nthreads == blockDim.x
 // is __syncthreads).  Expert parallel: only routes whose expert is in [e_lo, e_hi) are grouped, G.exp holds the
 // local expert index e - e_lo, and the other routes end with ids[r] = kNotLocal.
+// Groups are the routes of one expert in route order, experts ascending, at most 8 routes each (an expert with more
+// routes takes several consecutive groups).  Built in parallel, one thread per route: its place among its expert's
+// routes and the number of groups of the experts below it (two passes over the R <= 64 routes in shared memory).
+// scratch: int[kMaxRoutes] of shared memory.
 constexpr int kNotLocal = 0x7fffffff;
-__device__ __forceinline__ void build_groups(const int* ids_g, int R, int topk, int E, Groups& G, int* sorted, int* ids,
+__device__ __forceinline__ void build_groups(const int* ids_g, int R, int topk, int E, Groups& G, int* scratch, int* ids,
                                              unsigned* status, int nthreads, int bar, int e_lo = 0,
                                              int e_hi = kNotLocal) {
   const int tid = threadIdx.x;
@@ -116,33 +120,35 @@ __device__ __forceinline__ void build_groups(const int* ids_g, int R, int topk, 
     ids[tid] = ec >= e_lo && ec < e_hi ? ec : kNotLocal;
   }
   sync();
+  int e = kNotLocal, before = 0, total = 0;
   if (tid < R) {
-    const int e = ids[tid];
-    int rank = 0;
+    e = ids[tid];
+#pragma unroll 4
     for (int r = 0; r < R; ++r) {
       const int f = ids[r];
-      rank += (f < e) || (f == e && r < tid);
+      before += (f == e) & (r < tid);
+      total += f == e;
     }
-    sorted[rank] = tid;
+    // the expert's first route records how many groups the expert takes
+    scratch[tid] = before == 0 && e != kNotLocal ? (total + 7) >> 3 : 0;
   }
   sync();
-  if (tid == 0) {
-    int n = -1, prev = -1;
-    for (int i = 0; i < R; ++i) {
-      const int r = sorted[i];
-      const int e = ids[r];
-      if (e == kNotLocal) break;                      // the non-local routes sort last
-      if (e != prev || G.cnt[n] == 8) {
-        ++n;
-        G.exp[n] = e - e_lo;
-        G.cnt[n] = 0;
-        prev = e;
-      }
-      G.route[n][G.cnt[n]] = r;
-      G.tok[n][G.cnt[n]] = r / topk;
-      ++G.cnt[n];
+  if (tid < R && e != kNotLocal) {
+    int n = before >> 3;
+#pragma unroll 4
+    for (int r = 0; r < R; ++r) n += ids[r] < e ? scratch[r] : 0;
+    const int pos = before & 7;
+    G.route[n][pos] = tid;
+    G.tok[n][pos] = tid / topk;
+    if (pos == 0) {
+      G.exp[n] = e - e_lo;
+      G.cnt[n] = min(8, total - before);
     }
-    G.n = n + 1;
+  }
+  if (tid == 0) {
+    int ng = 0;
+    for (int r = 0; r < R; ++r) ng += scratch[r];
+    G.n = ng;
   }
   sync();
 }

@@ -25,6 +25,13 @@
 #include "gridsync.cuh"
 #include "moe_common.cuh"
 #include "runtime.cuh"
+#include "timeline.cuh"
+
+// Timeline stamps (-DFLINT_TIMELINE builds only): 0 entry, 1 PDL wait done, 2 norm + router rows + staging, 3 barrier 0,
+// 4 plan released, 5 first gate/up tile done, 6 gate/up tiles done, 7 barrier 1, 8 act rows staged, 9 down tiles done,
+// 10 barrier 2, 11 output written, 12 producer: first stage issued, 13 producer: last gate/up stage issued,
+// 14 producer: last stage issued, 15 norm done, 16 router rows written.
+FLINT_TL_BUFFER
 
 namespace flint {
 
@@ -107,6 +114,7 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
     fence_mbar_init();
   }
   __syncthreads();
+  if (tid == 0) FLINT_TL(0);
 
   // router rows of this CTA: e = blockIdx.x (+ gridDim.x), one warp each, prefetched before the wait
   const int my_row = blockIdx.x + warp * nb;
@@ -117,7 +125,10 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
 #pragma unroll
     for (int i = 0; i < NV; ++i) wv[i] = ldg_stream_v4(wp + lane + 32 * i);
   }
+  // the norm weights (this thread's 8) do not depend on the previous kernel either
+  const uint4 nwc = tid < H / 8 ? reinterpret_cast<const uint4*>(a.nw)[tid] : make_uint4(0u, 0u, 0u, 0u);
   pdl_wait();
+  if (tid == 0) FLINT_TL(1);
 
   if (warp == kFW) {
     // ---------------- producer: wait for the routing plan, then stream up tiles followed by down tiles ----------------
@@ -159,16 +170,27 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
           tma_load_2d(sdst, ms, ks * 16, y0, &bars[slot]);
           tma_load_2d(cdst + kFBox * 128, mc, ks * 128, y1, &bars[slot]);
           tma_load_2d(sdst + kFBox * 16, ms, ks * 16, y1, &bars[slot]);
+          if (s == 0) FLINT_TL(12);
           if (++slot == NS) { slot = 0; phase ^= 1u; }
         }
+        if (i + 1 == nup) FLINT_TL(13);
       }
+      FLINT_TL(14);
     }
     return;
   }
 
   // ---------------- phase R: norm, router rows ----------------
-  add_rmsnorm_2pass(a.x, a.ldx, a.res, a.nw, a.eps, M, H, xnb, red, NT, 2);
-  if (blockIdx.x == 0) {
+  // (one global pass with every token's chunk loaded at once when a thread owns one 8-wide chunk per row; the same
+  // per-thread chains, butterfly and warp order as the two-pass form, so xn has the same bits)
+  if (H / 8 <= NT) {
+    add_rmsnorm_1pass_w(a.x, a.ldx, a.res, nwc, a.eps, M, H, xnb, blockIdx.x == 0 ? a.res_out : nullptr,
+                        blockIdx.x == 0 ? a.xn_out : nullptr, red, NT, 2);
+  } else {
+    add_rmsnorm_2pass(a.x, a.ldx, a.res, a.nw, a.eps, M, H, xnb, red, NT, 2);
+  }
+  if (tid == 0) FLINT_TL(15);
+  if (blockIdx.x == 0 && H / 8 > NT) {
     for (int idx = tid; idx < M * (H / 8); idx += NT) {
       const int m = idx / (H / 8), k8 = idx - m * (H / 8);
       if (a.xn_out) reinterpret_cast<uint4*>(a.xn_out + (int64_t)m * H)[k8] = reinterpret_cast<const uint4*>(xnb + m * H)[k8];
@@ -191,24 +213,39 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
     }
   }
   if (has_row) {
-    for (int m = 0; m < M; ++m) {
-      const uint4* xp = reinterpret_cast<const uint4*>(xnb + m * H);
-      float acc = 0.f;
+    // every token's dot at once (independent chains; per token the same order: i, then j, then the butterfly)
+    float acc[kMaxTokens];
 #pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        float xf[8], wf[8];
-        bf16x8_to_f32(xp[lane + 32 * i], xf);
-        bf16x8_to_f32(wv[i], wf);
+    for (int m = 0; m < kMaxTokens; ++m) acc[m] = 0.f;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc = fmaf(wf[j], xf[j], acc);
+    for (int i = 0; i < NV; ++i) {
+      float wf[8];
+      bf16x8_to_f32(wv[i], wf);
+#pragma unroll
+      for (int m = 0; m < kMaxTokens; ++m) {
+        if (m < M) {
+          float xf[8];
+          bf16x8_to_f32(reinterpret_cast<const uint4*>(xnb + m * H)[lane + 32 * i], xf);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[m] = fmaf(wf[j], xf[j], acc[m]);
+        }
       }
+    }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-      if (lane == 0) __stcg(lg + m * E + my_row, bf16r(acc));
+    for (int m = 0; m < kMaxTokens; ++m) {
+      if (m < M) {
+        float v = acc[m];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) __stcg(lg + m * E + my_row, bf16r(v));
+      }
     }
   }
+  if (tid == 0) FLINT_TL(16);
   stage_rows_f16(xnb, H, M, H, xs, shift_x, red, NT, 2);
+  if (tid == 0) FLINT_TL(2);
   if (!grid_sync(&ws->sync, nb, 0, NT, 2, &s_ok, status)) return;
+  if (tid == 0) FLINT_TL(3);
 
   // ---------------- phase U: top-k, groups, plan, gate/up tiles ----------------
   if (warp < M) {
@@ -237,6 +274,7 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
     tiles[2] = d0;
     tiles[3] = d1;
     mbar_arrive(&plan_bar);                  // release the producer
+    FLINT_TL(4);
   }
 
   const int g = lane >> 2, t = lane & 3;
@@ -282,11 +320,23 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
              __bfloat16_as_ushort(__float2bfloat16_rn(silu * uv)));
     }
     named_bar_sync(1, NT);
+    if (tid == 0 && tt == u0) FLINT_TL(5);
   }
+  if (tid == 0) FLINT_TL(6);
   if (!grid_sync(&ws->sync, nb, 1, NT, 2, &s_ok, status)) return;
+  if (tid == 0) FLINT_TL(7);
 
   // ---------------- phase D: down tiles ----------------
-  if (d1 > d0) stage_rows_f16(act_g, I, R, I, xa, shift_a, red, NT, 2, true);
+  // stage the act rows of this CTA's down tiles only (the routes of groups d0 / tpd .. (d1 - 1) / tpd), each at its
+  // route's place
+  if (d1 > d0) {
+    const int ua = d0 / tpd, nslot = ((d1 - 1) / tpd - ua + 1) * 8;
+    stage_rows_f16_map(act_g, I, nslot, I, xa, shift_a, red, NT, 2, true, [&](int i) {
+      const int u = ua + (i >> 3), c = i & 7;
+      return c < G.cnt[u] ? G.route[u][c] : -1;
+    });
+  }
+  if (tid == 0) FLINT_TL(8);
   for (int td = d0; td < d1; ++td) {
     const int u = td / tpd, j = td - u * tpd, cnt = G.cnt[u], e = G.exp[u];
     const bool active = g < cnt;
@@ -303,8 +353,10 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
     }
     named_bar_sync(1, NT);
   }
+  if (tid == 0) FLINT_TL(9);
   pdl_trigger();
   if (!grid_sync(&ws->sync, nb, 2, NT, 2, &s_ok, status)) return;
+  if (tid == 0) FLINT_TL(10);
 
   // ---------------- phase F: weighted sum in slot order (expert parallel: the local routes' rows) ----------------
   const int rows_per = (H + nb - 1) / nb;
@@ -317,6 +369,7 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
                                    : (unsigned short)0;
       reinterpret_cast<unsigned short*>(a.y_out)[(int64_t)route * H + r] = b;
     }
+    if (tid == 0) FLINT_TL(11);
     grid_sync_retire(&ws->sync, nb);
     return;
   }
@@ -329,6 +382,7 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
     }
     a.out[(int64_t)m * H + r] = __float2bfloat16_rn(acc);
   }
+  if (tid == 0) FLINT_TL(11);
   grid_sync_retire(&ws->sync, nb);
 }
 
@@ -363,6 +417,8 @@ static int launch_fused(int sms, const CUtensorMap& uc, const CUtensorMap& us, c
 using namespace flint;
 
 int64_t flint::status_offset_moe_fused() { return (int64_t)offsetof(MoeFusedWs, status); }
+
+FLINT_TL_READER(flint_timeline_moe_fused)
 
 extern "C" int64_t flint_moe_fused_workspace_bytes(int64_t E, int64_t H, int64_t I) {
   return (int64_t)moe_fused_ws_bytes((int)E, (int)H, (int)I);

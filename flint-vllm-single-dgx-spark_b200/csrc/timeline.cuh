@@ -18,7 +18,7 @@ __device__ __forceinline__ void poll_pause() {
 #endif
 }
 
-constexpr int kTlSlots = 16;         // stamps per CTA
+constexpr int kTlSlots = 32;         // stamps per CTA
 constexpr int kTlCtas = 160;         // CTAs recorded (>= the SM count of a B200)
 
 }  // namespace flint
