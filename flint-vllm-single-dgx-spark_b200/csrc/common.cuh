@@ -448,6 +448,106 @@ __device__ __forceinline__ void norm_stage_f16(const bf16* x, int64_t ldx, const
   sync();
 }
 
+// add + RMSNorm of M <= 8 rows for H / 8 <= nthreads (one 8-wide chunk per thread and row) writing both the bf16
+// result xn (shared memory, rows H apart; optional global copies xn_out and res_out = bf16(x + res), rows H apart)
+// and its f16 staging in xs with the per-row power-of-two shift[m]: add_rmsnorm_1pass_w followed by
+// stage_rows_f16(xn, ...), with the same bits, in one pass -- every row's loads are issued before any arithmetic,
+// and the staging converts the registers instead of re-reading xn.  x and res rows are ldx apart; wchunk: this
+// thread's 8 norm weights.  red: >= (nthreads/32) * 8 + 8 floats.
+__device__ __forceinline__ void norm_xn_stage_f16(const bf16* x, int64_t ldx, const bf16* res, uint4 wchunk, float eps,
+                                                  int M, int H, bf16* xn, bf16* xn_out, bf16* res_out, __half* xs,
+                                                  int* shift, float* red, int nthreads, int bar) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = nthreads >> 5, H8 = H >> 3;
+  auto sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthreads) : "memory"); };
+  const bool own = tid < H8;
+  int* rmax = reinterpret_cast<int*>(red + nw * 8);
+  uint4 xv[8], rv[8];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    xv[m] = make_uint4(0u, 0u, 0u, 0u);
+    rv[m] = xv[m];
+    if (m < M && own) {
+      xv[m] = reinterpret_cast<const uint4*>(x + m * ldx)[tid];
+      if (res) rv[m] = reinterpret_cast<const uint4*>(res + m * ldx)[tid];
+    }
+  }
+  float a[8][8], ss[8];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    ss[m] = 0.f;
+    if (m < M && own) {
+      bf16x8_to_f32(xv[m], a[m]);
+      if (res) {
+        float b[8];
+        bf16x8_to_f32(rv[m], b);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a[m][j] += b[j];
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss[m] = fmaf(a[m][j], a[m][j], ss[m]);
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    float v = ss[m];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[warp * 8 + m] = v;
+  }
+  if (tid < 8) rmax[tid] = 0;
+  sync();
+  float wf[8], rsv[8];
+  bf16x8_to_f32(wchunk, wf);
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    float tot = 0.f;
+    for (int ww = 0; ww < nw; ++ww) tot += red[ww * 8 + m];
+    rsv[m] = rsqrtf(tot / (float)H + eps);
+  }
+  uint32_t pk[8][4];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    if (m < M && own) {
+      uint32_t pr[4];
+      float mx = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __nv_bfloat162 n2 = __floats2bfloat162_rn(a[m][2 * j] * rsv[m] * wf[2 * j], a[m][2 * j + 1] * rsv[m] * wf[2 * j + 1]);
+        mx = fmaxf(mx, fmaxf(fabsf(__low2float(n2)), fabsf(__high2float(n2))));
+        pk[m][j] = *reinterpret_cast<uint32_t*>(&n2);
+        __nv_bfloat162 r2 = __floats2bfloat162_rn(a[m][2 * j], a[m][2 * j + 1]);
+        pr[j] = *reinterpret_cast<uint32_t*>(&r2);
+      }
+      const uint4 nv = make_uint4(pk[m][0], pk[m][1], pk[m][2], pk[m][3]);
+      reinterpret_cast<uint4*>(xn + m * H)[tid] = nv;
+      if (xn_out) reinterpret_cast<uint4*>(xn_out + (int64_t)m * H)[tid] = nv;
+      if (res_out) reinterpret_cast<uint4*>(res_out + (int64_t)m * H)[tid] = make_uint4(pr[0], pr[1], pr[2], pr[3]);
+      smem_max_grouped(&rmax[m], mx);
+    }
+  }
+  sync();
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    if (m < M) {
+      const float mx = __int_as_float(rmax[m]);
+      int s = 0;
+      if (mx > 0.f && !(mx != mx) && mx <= 3.0e38f) s = 14 - ((int)((__float_as_uint(mx) >> 23) & 0xFF) - 127);
+      if (tid == 0) shift[m] = s;
+      if (own) {
+        uint32_t h[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          __half2 v = __floats2half2_rn(scale_pow2(bf16_bits_to_f32(pk[m][j] & 0xFFFFu), s),
+                                        scale_pow2(bf16_bits_to_f32(pk[m][j] >> 16), s));
+          h[j] = *reinterpret_cast<uint32_t*>(&v);
+        }
+        *reinterpret_cast<uint4*>(xs + m * xs_stride(H) + xs_perm(tid * 8)) = make_uint4(h[0], h[1], h[2], h[3]);
+      }
+    }
+  }
+  sync();
+}
+
 // norm_stage_f16 with ONE global pass, for H / 8 <= nthreads: each thread owns one 8-wide chunk of every row and keeps
 // x (+ res) in registers between the sum of squares and the normalisation (same fmaf chains, same bits).
 // (norm_stage_f16_1w: the thread's 8 norm weights, w[8 tid .. 8 tid + 7], are passed in, loaded before the PDL wait.)

@@ -117,11 +117,14 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   if (tid == 0) FLINT_TL(0);
 
   // router rows of this CTA: e = blockIdx.x (+ gridDim.x), one warp each, prefetched before the wait
-  const int my_row = blockIdx.x + warp * nb;
-  const bool has_row = warp < 2 && my_row < E;
+  // Router dots: this CTA's rows are blockIdx.x and blockIdx.x + nb (E <= 2 nb); (row, token) pair p is row
+  // blockIdx.x + (p / M) nb and token p % M, and consumer warp w takes pairs w, w + kFW, ...  A warp's first row is
+  // prefetched into registers before the PDL wait.
+  const int npairs = ((int)blockIdx.x < E ? M : 0) + ((int)(blockIdx.x + nb) < E ? M : 0);
+  int wv_rk = warp < kFW && warp < npairs ? warp / M : -1;   // row (0 or 1) held in wv
   uint4 wv[NV];
-  if (has_row) {
-    const uint4* wp = reinterpret_cast<const uint4*>(a.gate_w + (int64_t)my_row * H);
+  if (wv_rk >= 0) {
+    const uint4* wp = reinterpret_cast<const uint4*>(a.gate_w + (int64_t)(blockIdx.x + wv_rk * nb) * H);
 #pragma unroll
     for (int i = 0; i < NV; ++i) wv[i] = ldg_stream_v4(wp + lane + 32 * i);
   }
@@ -183,9 +186,11 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   // ---------------- phase R: norm, router rows ----------------
   // (one global pass with every token's chunk loaded at once when a thread owns one 8-wide chunk per row; the same
   // per-thread chains, butterfly and warp order as the two-pass form, so xn has the same bits)
+  // (H / 8 <= NT: one pass that also stages xn as f16 from registers; the same bits as the two-pass norm followed by
+  // stage_rows_f16, which the wider rows use)
   if (H / 8 <= NT) {
-    add_rmsnorm_1pass_w(a.x, a.ldx, a.res, nwc, a.eps, M, H, xnb, blockIdx.x == 0 ? a.res_out : nullptr,
-                        blockIdx.x == 0 ? a.xn_out : nullptr, red, NT, 2);
+    norm_xn_stage_f16(a.x, a.ldx, a.res, nwc, a.eps, M, H, xnb, blockIdx.x == 0 ? a.xn_out : nullptr,
+                      blockIdx.x == 0 ? a.res_out : nullptr, xs, shift_x, red, NT, 2);
   } else {
     add_rmsnorm_2pass(a.x, a.ldx, a.res, a.nw, a.eps, M, H, xnb, red, NT, 2);
   }
@@ -212,37 +217,32 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
       }
     }
   }
-  if (has_row) {
-    // every token's dot at once (independent chains; per token the same order: i, then j, then the butterfly)
-    float acc[kMaxTokens];
+  // one (row, token) dot per warp and pair: per lane the chain over i, then j, then the xor butterfly (the route
+  // kernel's order)
+  for (int p = warp; p < npairs; p += kFW) {
+    const int rk = p / M, m = p - rk * M, row = (int)blockIdx.x + rk * (int)nb;
+    if (rk != wv_rk) {                                    // a second row (E > nb and pairs beyond the first 8)
+      const uint4* wp = reinterpret_cast<const uint4*>(a.gate_w + (int64_t)row * H);
 #pragma unroll
-    for (int m = 0; m < kMaxTokens; ++m) acc[m] = 0.f;
+      for (int i = 0; i < NV; ++i) wv[i] = ldg_stream_v4(wp + lane + 32 * i);
+      wv_rk = rk;
+    }
+    const uint4* xp = reinterpret_cast<const uint4*>(xnb + m * H);
+    float acc = 0.f;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      float wf[8];
+      float xf[8], wf[8];
+      bf16x8_to_f32(xp[lane + 32 * i], xf);
       bf16x8_to_f32(wv[i], wf);
 #pragma unroll
-      for (int m = 0; m < kMaxTokens; ++m) {
-        if (m < M) {
-          float xf[8];
-          bf16x8_to_f32(reinterpret_cast<const uint4*>(xnb + m * H)[lane + 32 * i], xf);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) acc[m] = fmaf(wf[j], xf[j], acc[m]);
-        }
-      }
+      for (int j = 0; j < 8; ++j) acc = fmaf(wf[j], xf[j], acc);
     }
 #pragma unroll
-    for (int m = 0; m < kMaxTokens; ++m) {
-      if (m < M) {
-        float v = acc[m];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (lane == 0) __stcg(lg + m * E + my_row, bf16r(v));
-      }
-    }
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) __stcg(lg + m * E + row, bf16r(acc));
   }
   if (tid == 0) FLINT_TL(16);
-  stage_rows_f16(xnb, H, M, H, xs, shift_x, red, NT, 2);
+  if (H / 8 > NT) stage_rows_f16(xnb, H, M, H, xs, shift_x, red, NT, 2);
   if (tid == 0) FLINT_TL(2);
   if (!grid_sync(&ws->sync, nb, 0, NT, 2, &s_ok, status)) return;
   if (tid == 0) FLINT_TL(3);
