@@ -147,8 +147,8 @@ __device__ __forceinline__ void smem_max_grouped(int* p, float v) {
 // of 32), which synchronise on named barrier `bar` (0 = __syncthreads when nthreads == blockDim.x).
 // One global pass: raw bf16 goes to its permuted place in xs while the row maxima accumulate (one shared atomicMax
 // per row and warp on the non-negative float bits), then each element is converted in place.  red: >= rows floats.
-// stage_rows_f16_map stages only the rows row_of(0 .. rows-1) (entries < 0 are skipped), each at its own place r in
-// xs / shift / red (red: > the largest r floats); stage_rows_f16 is the identity map.
+// stage_rows_f16_map stages source row row_of(i) (i < rows; entries < 0 are skipped) into slot i of xs / shift;
+// stage_rows_f16 is the identity map.
 template <class RowOf>
 __device__ __forceinline__ void stage_rows_f16_map(const bf16* __restrict__ src, int64_t ld, int rows, int K, __half* xs,
                                                    int* shift, float* red, int nthreads, int bar, bool cg, RowOf row_of) {
@@ -156,24 +156,22 @@ __device__ __forceinline__ void stage_rows_f16_map(const bf16* __restrict__ src,
   const int K8 = K >> 3, n = rows * K8;
   auto sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthreads) : "memory"); };
   int* redi = reinterpret_cast<int*>(red);
-  for (int i = tid; i < rows; i += nthreads) {
-    const int r = row_of(i);
-    if (r >= 0) redi[r] = 0;
-  }
+  for (int i = tid; i < rows; i += nthreads) redi[i] = 0;
   sync();
   // up to kB 16-byte loads per thread are issued back to back (one memory round trip per kB * nthreads units)
   constexpr int kB = 4;
   for (int base = 0; base < n; base += kB * nthreads) {
     uint4 v[kB];
-    int rr[kB], kk[kB];
+    int rr[kB], kk[kB];                               // rr: the slot (-1: nothing to stage)
 #pragma unroll
     for (int i = 0; i < kB; ++i) {
       const int idx = base + i * nthreads + tid;
       const int ri = idx / K8;
       kk[i] = idx - ri * K8;
-      rr[i] = idx < n ? row_of(ri) : -1;
-      if (rr[i] >= 0) {
-        const uint4* vp = reinterpret_cast<const uint4*>(src + rr[i] * ld) + kk[i];
+      const int sr = idx < n ? row_of(ri) : -1;
+      rr[i] = sr >= 0 ? ri : -1;
+      if (sr >= 0) {
+        const uint4* vp = reinterpret_cast<const uint4*>(src + sr * ld) + kk[i];
         v[i] = cg ? __ldcg(vp) : *vp;                 // cg: rows written by other CTAs of this kernel
       }
     }
@@ -196,18 +194,16 @@ __device__ __forceinline__ void stage_rows_f16_map(const bf16* __restrict__ src,
   }
   sync();
   for (int i = tid; i < rows; i += nthreads) {
-    const int r = row_of(i);
-    if (r < 0) continue;
-    const float mx = __int_as_float(redi[r]);
+    if (row_of(i) < 0) continue;
+    const float mx = __int_as_float(redi[i]);
     int s = 0;
     if (mx > 0.f && !(mx != mx) && mx <= 3.0e38f) s = 14 - ((int)((__float_as_uint(mx) >> 23) & 0xFF) - 127);
-    shift[r] = s;
+    shift[i] = s;
   }
   sync();
   for (int idx = tid; idx < n; idx += nthreads) {
-    const int ri = idx / K8, k8 = idx - ri * K8;
-    const int r = row_of(ri);
-    if (r < 0) continue;
+    const int r = idx / K8, k8 = idx - r * K8;
+    if (row_of(r) < 0) continue;
     uint4* p = reinterpret_cast<uint4*>(xs + r * xs_stride(K) + xs_perm(k8 * 8));
     float f[8];
     bf16x8_to_f32(*p, f);

@@ -145,10 +145,10 @@ __device__ __forceinline__ void build_groups(const int* ids_g, int R, int topk, 
       G.cnt[n] = min(8, total - before);
     }
   }
-  if (tid == 0) {
-    int ng = 0;
-    for (int r = 0; r < R; ++r) ng += scratch[r];
-    G.n = ng;
+  if (tid < 32) {                                       // the group count: one warp sums the R <= 64 entries
+    const int v = (tid < R ? scratch[tid] : 0) + (tid + 32 < R ? scratch[tid + 32] : 0);
+    const int ng = __reduce_add_sync(0xffffffffu, v);
+    if (tid == 0) G.n = ng;
   }
   sync();
 }

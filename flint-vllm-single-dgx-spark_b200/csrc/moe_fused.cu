@@ -30,7 +30,7 @@
 // Timeline stamps (-DFLINT_TIMELINE builds only): 0 entry, 1 PDL wait done, 2 norm + router rows + staging, 3 barrier 0,
 // 4 plan released, 5 first gate/up tile done, 6 gate/up tiles done, 7 barrier 1, 8 act rows staged, 9 down tiles done,
 // 10 barrier 2, 11 output written, 12 producer: first stage issued, 13 producer: last gate/up stage issued,
-// 14 producer: last stage issued, 15 norm done, 16 router rows written.
+// 14 producer: last stage issued, 15 norm done, 16 router rows written, 17 top-k done.
 FLINT_TL_BUFFER
 
 namespace flint {
@@ -64,6 +64,7 @@ struct MoeFusedArgs {
   MoeFusedWs* ws;
   int e_lo, e_hi;                    // local experts (expert-parallel mode; 0 and kNotLocal otherwise)
   bf16* y_out;                       // expert-parallel mode: per-route rows [M * topk][H]
+  int nslot_cap;                     // act rows a CTA can stage (the routes of the groups its down tiles span)
 };
 
 __host__ __device__ inline size_t moe_fused_ws_bytes(int E, int H, int I) {
@@ -251,7 +252,16 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   if (warp < M) {
     int my_e;
     float my_w;
-    warp_topk(lg + warp * E, E, topk, a.score_fn, lane, my_e, my_w);
+    if (E <= 256) {                          // the logits in registers, each lane's keys sorted once (same bits)
+      constexpr int PER = 8;
+      const int per = E / 32;
+      float lv[PER];
+#pragma unroll
+      for (int j = 0; j < PER; ++j) lv[j] = j < per ? __ldcg(lg + warp * E + lane + 32 * j) : 0.f;
+      warp_topk_regs<PER>(lv, per, topk, a.score_fn, lane, my_e, my_w);
+    } else {
+      warp_topk(lg + warp * E, E, topk, a.score_fn, lane, my_e, my_w);
+    }
     if (lane < topk) {
       ids_s[warp * topk + lane] = my_e;
       tw_s[warp * topk + lane] = my_w;
@@ -264,6 +274,7 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   if (blockIdx.x == 0 && a.logits_out)
     for (int i = tid; i < M * E; i += NT) a.logits_out[i] = __ldcg(lg + i);
   named_bar_sync(2, NT);
+  if (tid == 0) FLINT_TL(17);
   build_groups(ids_s, R, topk, E, G, sorted, ids_c, status, NT, 2, a.e_lo, a.e_hi);
   const int U = G.n * tpu, Dn = G.n * tpd;
   const int u0 = (int)((long)blockIdx.x * U / nb), u1 = (int)((long)(blockIdx.x + 1) * U / nb);
@@ -327,10 +338,15 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   if (tid == 0) FLINT_TL(7);
 
   // ---------------- phase D: down tiles ----------------
-  // stage the act rows of this CTA's down tiles only (the routes of groups d0 / tpd .. (d1 - 1) / tpd), each at its
-  // route's place
+  // stage the act rows of this CTA's down tiles only: group u of d0 / tpd .. (d1 - 1) / tpd, route c of the group,
+  // goes to slot (u - ua) * 8 + c
+  const int ua = d0 / tpd;
   if (d1 > d0) {
-    const int ua = d0 / tpd, nslot = ((d1 - 1) / tpd - ua + 1) * 8;
+    int nslot = ((d1 - 1) / tpd - ua + 1) * 8;
+    if (nslot > a.nslot_cap) {                            // cannot happen within the launch's bound; never overrun
+      if (tid == 0) atomicOr(status, 2u);
+      nslot = a.nslot_cap;
+    }
     stage_rows_f16_map(act_g, I, nslot, I, xa, shift_a, red, NT, 2, true, [&](int i) {
       const int u = ua + (i >> 3), c = i & 7;
       return c < G.cnt[u] ? G.route[u][c] : -1;
@@ -338,16 +354,16 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   }
   if (tid == 0) FLINT_TL(8);
   for (int td = d0; td < d1; ++td) {
-    const int u = td / tpd, j = td - u * tpd, cnt = G.cnt[u], e = G.exp[u];
-    const bool active = g < cnt;
+    const int u = td / tpd, j = td - u * tpd, cnt = G.cnt[u], e = G.exp[u], slot0 = (u - ua) * 8;
+    const bool active = g < cnt && slot0 + g < a.nslot_cap;
     float d[4];
-    run_tile(nks_dn, xa + (active ? G.route[u][g] : 0) * xs_stride(I), active, d);
+    run_tile(nks_dn, xa + (slot0 + (active ? g : 0)) * xs_stride(I), active, d);
     store_dtile(d);
     for (int idx = tid; idx < 2 * kFBox * 8; idx += NT) {
       const int n = idx / (2 * kFBox), r = idx - n * (2 * kFBox);
-      if (n >= cnt) continue;
+      if (n >= cnt || slot0 + n >= a.nslot_cap) continue;
       const int route = G.route[u][n];
-      const float y = dtile[r * 8 + n] * ldexpf(a.g2[e], -shift_a[route]);
+      const float y = dtile[r * 8 + n] * ldexpf(a.g2[e], -shift_a[slot0 + n]);
       __stcg(reinterpret_cast<unsigned short*>(y_g + (int64_t)route * H + j * 2 * kFBox + r),
              __bfloat16_as_ushort(__float2bfloat16_rn(y)));
     }
@@ -386,14 +402,22 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   grid_sync_retire(&ws->sync, nb);
 }
 
+// dynamic shared memory: alignment slack, ring + dtile, the f16 token rows, and a region that holds the bf16 token rows
+// in phase R and the staged act rows in phase D
+static size_t moe_fused_smem(size_t ring_and_dtile, const MoeFusedArgs& a) {
+  const size_t region = std::max((size_t)a.nslot_cap * xs_stride(a.I) * 2, (size_t)a.M * a.H * 2);
+  return 1024 + ring_and_dtile + (size_t)a.M * xs_stride(a.H) * 2 + region;
+}
+
 template <int NS, int NV>
 static int launch_fused(int sms, const CUtensorMap& uc, const CUtensorMap& us, const CUtensorMap& dc, const CUtensorMap& ds,
                         const MoeFusedArgs& a, int pdl, void* stream) {
   using L = EngineSmem<kFW, NS, kFBox>;
-  const size_t region = std::max((size_t)a.M * a.topk * xs_stride(a.I) * 2, (size_t)a.M * a.H * 2);
-  const size_t smem = 1024 + L::ring_bytes + L::dtile_bytes + (size_t)a.M * xs_stride(a.H) * 2 + region;
-  if (smem > 227 * 1024) return FLINT_ERR_SHAPE;
+  const size_t smem = moe_fused_smem(L::ring_bytes + L::dtile_bytes, a);
   auto kern = moe_fused_kernel<NS, NV>;
+  cudaFuncAttributes fa{};
+  if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return FLINT_ERR_LAUNCH;
+  if (smem + fa.sharedSizeBytes > 227 * 1024) return FLINT_ERR_SHAPE;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return FLINT_ERR_LAUNCH;
   set_max_carveout(kern);
@@ -459,11 +483,18 @@ static int moe_fused_launch(const void* x, int64_t ldx, const void* res, const v
   a.y_out = (bf16*)y_out;
   a.e_lo = (int)e_lo;
   a.e_hi = y_out ? (int)(e_lo + n_local) : kNotLocal;
+  {
+    // a CTA's down tiles (at most ceil(R tpd / grid) of them) span at most ceil(that / tpd) + 1 groups of <= 8 routes
+    const long tpd = H / (2 * kFBox), tmax = (M * topk * tpd + sms - 1) / sms;
+    a.nslot_cap = (int)std::min<long>(kMaxRoutes, ((tmax + tpd - 1) / tpd + 1) * 8);
+  }
+  // the deepest weight ring that fits beside the rows (more stages in flight per SM: the stream is latency-bound)
   if (H == 2048) {
-    if (M <= 2) return launch_fused<6, 8>(sms, uc, us, dc, ds, a, pdl, stream);
+    using L8 = EngineSmem<kFW, 8, kFBox>;
+    if (moe_fused_smem(L8::ring_bytes + L8::dtile_bytes, a) + 12 * 1024 <= 227 * 1024)
+      return launch_fused<8, 8>(sms, uc, us, dc, ds, a, pdl, stream);
     return launch_fused<4, 8>(sms, uc, us, dc, ds, a, pdl, stream);
   }
-  if (M <= 2) return launch_fused<6, 16>(sms, uc, us, dc, ds, a, pdl, stream);
   return launch_fused<4, 16>(sms, uc, us, dc, ds, a, pdl, stream);
 }
 
