@@ -260,7 +260,12 @@ def run_ours(args):
                        "parallelism": (f"dp{world} attention (one stream per GPU) + ep{world} experts + vocab{world} head"
                                        if dp else f"ep{world} + vocab{world} (attention replicated)" if world > 1
                                        else "1 GPU"),
-                       "exchange": ("NCCL all-gather of the tokens + reduce-scatter of the per-route rows per layer"
+                       "exchange": (({"nccl": "NCCL all-gather of the tokens + reduce-scatter of the per-route rows per "
+                                              "layer",
+                                      "peer": "both exchanges inside the MoE launch over NVLink peer memory + a "
+                                              "receive-and-sum launch per layer",
+                                      "peer_split": "NVLink peer-memory gather and combine launches around the MoE "
+                                                    "launch"}[args.exchange])
                                     if dp else ("in-kernel NVLink peer stores" if args.exchange == "peer"
                                                 else "NCCL all-reduce") if world > 1 else None),
                        "l2": "no flush: 1.73 GB of weights streamed per step (> 126 MB L2)",
@@ -344,7 +349,7 @@ def main():
     ap.add_argument("--multi", default="dp", choices=["dp", "ep"],
                     help="N > 1: one stream per GPU (data-parallel attention + expert-parallel MoE, weak scaling) or "
                          "one stream over all GPUs (expert parallel, attention replicated, strong scaling)")
-    ap.add_argument("--exchange", default=None, choices=["peer", "nccl"],
+    ap.add_argument("--exchange", default=None, choices=["peer", "nccl", "peer_split"],
                     help="N > 1: MoE / head exchange fused into the kernels over NVLink peer memory, or NCCL calls")
     ap.add_argument("--streams", type=int, default=1, help="concurrent streams (1..8; BASELINE configs[4])")
     ap.add_argument("--sample", action="store_true", help="seeded T 1.0 / top-k 20 / top-p 0.95 sampling")

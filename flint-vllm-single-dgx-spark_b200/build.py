@@ -1,6 +1,7 @@
 """Build ``libflint_b200.so`` (all of ``csrc/*.cu``) for sm_100a with nvcc, in-tree.
 
     python flint-vllm-single-dgx-spark_b200/build.py [-v]
+    python flint-vllm-single-dgx-spark_b200/build.py --timeline DIR     (an instrumented copy, see build_timeline)
 
 The library is a plain C-ABI shared object (static CUDA runtime, no torch headers), so it loads with
 ctypes in any process.  Objects go to ``_build/``; the .so is written next to this file.
@@ -75,5 +76,26 @@ def build(verbose: bool = False, force: bool = False, ptxas_verbose: bool = Fals
     return LIB
 
 
+def build_timeline(out_dir: str) -> str:
+    """An instrumented copy of the library (-DFLINT_TIMELINE: per-CTA phase stamps in the block and fused kernels,
+    read back through flint_timeline_<kernel>) into out_dir; kernel_bench.py --lib <out_dir>/libflint_b200.so
+    --timeline prints them.  The default library is untouched."""
+    global BUILD, LIB, NVCC_FLAGS
+    saved = BUILD, LIB, NVCC_FLAGS
+    try:
+        os.makedirs(out_dir, exist_ok=True)
+        BUILD = os.path.join(out_dir, "obj")
+        LIB = os.path.join(out_dir, "libflint_b200.so")
+        NVCC_FLAGS = NVCC_FLAGS + ["-DFLINT_TIMELINE"]
+        lib = build(force=True)
+        shutil.rmtree(BUILD, ignore_errors=True)
+        return lib
+    finally:
+        BUILD, LIB, NVCC_FLAGS = saved
+
+
 if __name__ == "__main__":
-    build(verbose="-v" in sys.argv, force=True, ptxas_verbose="-v" in sys.argv)
+    if "--timeline" in sys.argv:
+        print(build_timeline(sys.argv[sys.argv.index("--timeline") + 1]))
+    else:
+        build(verbose="-v" in sys.argv, force=True, ptxas_verbose="-v" in sys.argv)

@@ -452,7 +452,7 @@ __device__ __forceinline__ void norm_stage_f16(const bf16* x, int64_t ldx, const
 // thread's 8 norm weights.  red: >= (nthreads/32) * 8 + 8 floats.
 __device__ __forceinline__ void norm_xn_stage_f16(const bf16* x, int64_t ldx, const bf16* res, uint4 wchunk, float eps,
                                                   int M, int H, bf16* xn, bf16* xn_out, bf16* res_out, __half* xs,
-                                                  int* shift, float* red, int nthreads, int bar) {
+                                                  int* shift, float* red, int nthreads, int bar, bool cg = false) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = nthreads >> 5, H8 = H >> 3;
   auto sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthreads) : "memory"); };
   const bool own = tid < H8;
@@ -462,9 +462,13 @@ __device__ __forceinline__ void norm_xn_stage_f16(const bf16* x, int64_t ldx, co
   for (int m = 0; m < 8; ++m) {
     xv[m] = make_uint4(0u, 0u, 0u, 0u);
     rv[m] = xv[m];
-    if (m < M && own) {
-      xv[m] = reinterpret_cast<const uint4*>(x + m * ldx)[tid];
-      if (res) rv[m] = reinterpret_cast<const uint4*>(res + m * ldx)[tid];
+    if (m < M && own) {                       // cg: rows another GPU stored into this one's memory
+      const uint4* xp = reinterpret_cast<const uint4*>(x + m * ldx) + tid;
+      xv[m] = cg ? __ldcg(xp) : *xp;
+      if (res) {
+        const uint4* rp = reinterpret_cast<const uint4*>(res + m * ldx) + tid;
+        rv[m] = cg ? __ldcg(rp) : *rp;
+      }
     }
   }
   float a[8][8], ss[8];

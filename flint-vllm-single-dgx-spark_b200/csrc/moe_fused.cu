@@ -22,10 +22,21 @@
 // y_out[m * topk + s] = y of each local route (zero rows for the others) instead of the weighted sum: summed over the
 // ranks (one non-zero term per element) and combined in slot order they give the one-GPU output bit for bit, and the
 // rows equal flint_moe_down_ep's.
+//
+// Data-parallel mode over NVLink peer memory (flint_moe_fused_dp_peer; one stream per GPU, expert-parallel MoE): the
+// launch is also the exchange.  In phase R, CTA 0 stores this rank's two rows (attention output, residual) into every
+// rank's token table and raises its flag there; every CTA waits for all ranks' flags and normalises the M = world
+// tokens from its own table.  In phase F each local route's rows go straight into the token owner's row table, and
+// the last CTA to finish raises this rank's row flag on every rank; flint_dp_combine_peer (rows already pushed) then
+// forms each rank's weighted sum.  The tables, flags and epochs are those of flint_dp_gather_peer /
+// flint_dp_combine_peer (peer.cuh); every wait is bounded in time.
 #include "gridsync.cuh"
 #include "moe_common.cuh"
+#include "peer.cuh"
 #include "runtime.cuh"
 #include "timeline.cuh"
+
+#include <string.h>
 
 // Timeline stamps (-DFLINT_TIMELINE builds only): 0 entry, 1 PDL wait done, 2 norm + router rows + staging, 3 barrier 0,
 // 4 plan released, 5 first gate/up tile done, 6 gate/up tiles done, 7 barrier 1, 8 act rows staged, 9 down tiles done,
@@ -65,6 +76,9 @@ struct MoeFusedArgs {
   int e_lo, e_hi;                    // local experts (expert-parallel mode; 0 and kNotLocal otherwise)
   bf16* y_out;                       // expert-parallel mode: per-route rows [M * topk][H]
   int nslot_cap;                     // act rows a CTA can stage (the routes of the groups its down tiles span)
+  int peer;                          // data-parallel peer mode (ps, send valid; M = world)
+  const bf16* send;                  // peer mode: this rank's rows [2][H] (attention output, residual)
+  PeerSet ps;
 };
 
 __host__ __device__ inline size_t moe_fused_ws_bytes(int E, int H, int I) {
@@ -189,11 +203,39 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   // per-thread chains, butterfly and warp order as the two-pass form, so xn has the same bits)
   // (H / 8 <= NT: one pass that also stages xn as f16 from registers; the same bits as the two-pass norm followed by
   // stage_rows_f16, which the wider rows use)
+  const bf16* xin = a.x;
+  const bf16* rin = a.res;
+  int64_t ldin = a.ldx;
+  unsigned ep_tok = 0, ep_row = 0;
+  if (a.peer) {
+    // every rank's (attention output, residual) rows into every rank's token table, this rank's flag there; then
+    // this CTA waits for every rank's flag and reads the M = world tokens from its own table
+    const int W = a.ps.world, rk = a.ps.rank, n16 = 2 * H / 8;
+    PeerHeader* own = peer_header(a.ps.base[rk]);
+    ep_tok = ld_relaxed_sys_u32(&own->dp_tok_epoch) + 1u;
+    ep_row = ld_relaxed_sys_u32(&own->dp_row_epoch) + 1u;
+    if (blockIdx.x == 0) {
+      const uint4* src = reinterpret_cast<const uint4*>(a.send);
+      for (int i = tid; i < n16 * W; i += NT) {
+        const int p = i / n16, u = i - p * n16;
+        reinterpret_cast<uint4*>(peer_dp_tokens(a.ps.base[p], ep_tok & 1u, H) + (size_t)rk * 2 * H)[u] = src[u];
+      }
+      __threadfence_system();
+      named_bar_sync(2, NT);
+      if (tid < W) st_release_sys_u32(reinterpret_cast<unsigned*>(a.ps.base[tid] + kPeerDpTokFlagsOff) + rk, ep_tok);
+    }
+    if (tid < W && !peer_wait(reinterpret_cast<unsigned*>(a.ps.base[rk] + kPeerDpTokFlagsOff) + tid, ep_tok, own))
+      atomicOr(status, STATUS_WAIT_TIMEOUT);
+    named_bar_sync(2, NT);                                  // orders the table reads after the acquiring polls
+    xin = peer_dp_tokens(a.ps.base[rk], ep_tok & 1u, H);
+    rin = xin + H;
+    ldin = 2 * H;
+  }
   if (H / 8 <= NT) {
-    norm_xn_stage_f16(a.x, a.ldx, a.res, nwc, a.eps, M, H, xnb, blockIdx.x == 0 ? a.xn_out : nullptr,
-                      blockIdx.x == 0 ? a.res_out : nullptr, xs, shift_x, red, NT, 2);
+    norm_xn_stage_f16(xin, ldin, rin, nwc, a.eps, M, H, xnb, blockIdx.x == 0 ? a.xn_out : nullptr,
+                      blockIdx.x == 0 ? a.res_out : nullptr, xs, shift_x, red, NT, 2, a.peer != 0);
   } else {
-    add_rmsnorm_2pass(a.x, a.ldx, a.res, a.nw, a.eps, M, H, xnb, red, NT, 2);
+    add_rmsnorm_2pass(xin, ldin, rin, a.nw, a.eps, M, H, xnb, red, NT, 2);
   }
   if (tid == 0) FLINT_TL(15);
   if (blockIdx.x == 0 && H / 8 > NT) {
@@ -202,9 +244,9 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
       if (a.xn_out) reinterpret_cast<uint4*>(a.xn_out + (int64_t)m * H)[k8] = reinterpret_cast<const uint4*>(xnb + m * H)[k8];
       if (a.res_out) {
         float f[8], g[8];
-        bf16x8_to_f32(reinterpret_cast<const uint4*>(a.x + m * a.ldx)[k8], f);
-        if (a.res) {
-          bf16x8_to_f32(reinterpret_cast<const uint4*>(a.res + m * a.ldx)[k8], g);
+        bf16x8_to_f32(__ldcg(reinterpret_cast<const uint4*>(xin + m * ldin) + k8), f);
+        if (rin) {
+          bf16x8_to_f32(__ldcg(reinterpret_cast<const uint4*>(rin + m * ldin) + k8), g);
 #pragma unroll
           for (int j = 0; j < 8; ++j) f[j] += g[j];
         }
@@ -377,6 +419,35 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   // ---------------- phase F: weighted sum in slot order (expert parallel: the local routes' rows) ----------------
   const int rows_per = (H + nb - 1) / nb;
   const int r0 = blockIdx.x * rows_per, r1 = min(H, r0 + rows_per);
+  if (a.peer) {
+    // each local route's rows into its token owner's row table at [this rank][slot]; the last CTA raises this rank's
+    // row flag on every rank (every CTA's stores fenced before it counts itself) and advances both epochs
+    const int W = a.ps.world, rk = a.ps.rank;
+    for (int idx = tid; idx < (r1 - r0) * R; idx += NT) {
+      const int route = idx / (r1 - r0), r = r0 + idx - route * (r1 - r0);
+      if (ids_c[route] == kNotLocal) continue;
+      const int m = route / topk, s = route - m * topk;
+      const unsigned short b = __ldcg(reinterpret_cast<const unsigned short*>(y_g + (int64_t)route * H + r));
+      reinterpret_cast<unsigned short*>(peer_dp_rows(a.ps.base[m], ep_row & 1u, H) +
+                                        ((size_t)rk * kPeerSlots + s) * H)[r] = b;
+    }
+    __threadfence_system();
+    named_bar_sync(2, NT);
+    if (tid == 0) {
+      FLINT_TL(11);
+      if (atomicAdd(&ws->sync.retired, 1u) == nb - 1) {
+        atomicExch(&ws->sync.count, 0u);
+        atomicExch(&ws->sync.retired, 0u);
+        __threadfence_system();
+        for (int w = 0; w < W; ++w)
+          st_release_sys_u32(reinterpret_cast<unsigned*>(a.ps.base[w] + kPeerDpRowFlagsOff) + rk, ep_row);
+        PeerHeader* own = peer_header(a.ps.base[rk]);
+        own->dp_tok_epoch = ep_tok;
+        own->dp_row_epoch = ep_row;                       // the receive-and-sum launch waits for this epoch
+      }
+    }
+    return;
+  }
   if (a.y_out) {
     for (int idx = tid; idx < (r1 - r0) * R; idx += NT) {
       const int route = idx / (r1 - r0), r = r0 + idx - route * (r1 - r0);
@@ -452,8 +523,9 @@ static int moe_fused_launch(const void* x, int64_t ldx, const void* res, const v
                             int64_t M, int64_t H, int64_t E, int64_t topk, int score_fn, const void* w13, const void* s13,
                             const float* g13, const void* w2, const void* s2, const float* g2, int64_t I, int64_t e_lo,
                             int64_t n_local, void* out, void* y_out, void* res_out, void* xn_out, float* logits_out,
-                            int32_t* topk_ids_out, float* topk_weights_out, void* workspace, int pdl, void* stream) {
-  if (!x || !norm_w || !gate_w || !w13 || !s13 || !g13 || !w2 || !s2 || !g2 || (!out && !y_out) || !workspace)
+                            int32_t* topk_ids_out, float* topk_weights_out, void* workspace, int pdl, void* stream,
+                            const PeerSet* ps = nullptr) {
+  if (!x || !norm_w || !gate_w || !w13 || !s13 || !g13 || !w2 || !s2 || !g2 || (!out && !y_out && !ps) || !workspace)
     return FLINT_ERR_ARGUMENT;
   if (e_lo < 0 || n_local < 1 || e_lo + n_local > E) return FLINT_ERR_ARGUMENT;
   if (y_out && !aligned(y_out, 16)) return FLINT_ERR_ALIGN;
@@ -482,7 +554,11 @@ static int moe_fused_launch(const void* x, int64_t ldx, const void* res, const v
   a.ws = static_cast<MoeFusedWs*>(workspace);
   a.y_out = (bf16*)y_out;
   a.e_lo = (int)e_lo;
-  a.e_hi = y_out ? (int)(e_lo + n_local) : kNotLocal;
+  a.e_hi = (y_out || ps) ? (int)(e_lo + n_local) : kNotLocal;
+  a.peer = ps != nullptr;
+  a.send = (const bf16*)x;
+  if (ps) a.ps = *ps;
+  else memset(&a.ps, 0, sizeof(a.ps));
   {
     // a CTA's down tiles (at most ceil(R tpd / grid) of them) span at most ceil(that / tpd) + 1 groups of <= 8 routes
     const long tpd = H / (2 * kFBox), tmax = (M * topk * tpd + sms - 1) / sms;
@@ -519,4 +595,21 @@ extern "C" int flint_moe_fused_ep(const void* x, int64_t ldx, const void* res, c
   return moe_fused_launch(x, ldx, res, norm_w, eps, gate_w, M, H, E, topk, score_fn, w13, s13, g13, w2, s2, g2, I,
                           expert_lo, n_local, nullptr, y_out, res_out, nullptr, logits_out, topk_ids_out,
                           topk_weights_out, workspace, pdl, stream);
+}
+
+extern "C" int flint_moe_fused_dp_peer(const void* send, const void* norm_w, float eps, const void* gate_w, int64_t H,
+                                       int64_t E, int64_t topk, int score_fn, const void* w13, const void* s13,
+                                       const float* g13, const void* w2, const void* s2, const float* g2, int64_t I,
+                                       int64_t expert_lo, int64_t n_local, const void* const* peers, int rank,
+                                       int world, void* res_out, float* logits_out, int32_t* topk_ids_out,
+                                       float* topk_weights_out, void* workspace, int pdl, void* stream) {
+  if (!send || !topk_ids_out || !topk_weights_out) return FLINT_ERR_ARGUMENT;
+  if (topk > kPeerSlots) return FLINT_ERR_SHAPE;
+  PeerSet ps;
+  const int rc = peer_set(peers, rank, world, &ps);
+  if (rc) return rc;
+  // the M = world tokens come from the token tables; send's two rows (H apart) pass the launch's argument checks
+  return moe_fused_launch(send, H, (const bf16*)send + H, norm_w, eps, gate_w, world, H, E, topk, score_fn, w13, s13,
+                          g13, w2, s2, g2, I, expert_lo, n_local, nullptr, nullptr, res_out, nullptr, logits_out,
+                          topk_ids_out, topk_weights_out, workspace, pdl, stream, &ps);
 }

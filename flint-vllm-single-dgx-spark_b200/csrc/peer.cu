@@ -76,7 +76,8 @@ __global__ void dp_gather_peer_kernel(const bf16* __restrict__ send, int H, cons
 // (zeros elsewhere); the rows of token m's local routes go to rank m's row table at [parity][this rank][slot], then
 // this rank's flag on every rank.  Once every flag shows this launch, out[h] = bf16(sum_s tw[s] * row_s[h]) in slot
 // order (fp32 FMA), row_s read from the rank that owns expert ids[rank * topk + s] (experts split in equal
-// contiguous ranges): the one-GPU weighted sum bit for bit.
+// contiguous ranges): the one-GPU weighted sum bit for bit.  y NULL: flint_moe_fused_dp_peer has already pushed the
+// rows and raised the flags, and this launch only waits and sums.
 __global__ void dp_combine_peer_kernel(const bf16* __restrict__ y, const int* __restrict__ ids,
                                        const float* __restrict__ tw, int topk, int E, int H, const PeerSet ps,
                                        bf16* __restrict__ out) {
@@ -84,9 +85,10 @@ __global__ void dp_combine_peer_kernel(const bf16* __restrict__ y, const int* __
   pdl_wait();
   const int tid = threadIdx.x, W = ps.world, r = ps.rank, per = E / W;
   PeerHeader* own = peer_header(ps.base[r]);
-  const unsigned ep = ld_relaxed_sys_u32(&own->dp_row_epoch) + 1u, par = ep & 1u;
+  // (y NULL: flint_moe_fused_dp_peer pushed the rows, raised the flags and advanced the epoch itself)
+  const unsigned ep = ld_relaxed_sys_u32(&own->dp_row_epoch) + (y ? 1u : 0u), par = ep & 1u;
   const int n16 = H / 8;
-  for (int i = tid; i < W * topk * n16; i += blockDim.x) {        // push this rank's local routes of every token
+  for (int i = tid; y && i < W * topk * n16; i += blockDim.x) {   // push this rank's local routes of every token
     const int route = i / n16, u = i - route * n16, m = route / topk, s = route - m * topk;
     const int e = ids[route];
     if (e < r * per || e >= (r + 1) * per) continue;
@@ -99,7 +101,7 @@ __global__ void dp_combine_peer_kernel(const bf16* __restrict__ y, const int* __
   }
   __threadfence_system();
   __syncthreads();
-  if (tid < W) st_release_sys_u32(reinterpret_cast<unsigned*>(ps.base[tid] + kPeerDpRowFlagsOff) + r, ep);
+  if (y && tid < W) st_release_sys_u32(reinterpret_cast<unsigned*>(ps.base[tid] + kPeerDpRowFlagsOff) + r, ep);
   if (tid == 0) s_ok = 1;
   __syncthreads();
   if (tid < W && !peer_wait(reinterpret_cast<unsigned*>(ps.base[r] + kPeerDpRowFlagsOff) + tid, ep, own)) s_ok = 0;
@@ -111,7 +113,7 @@ __global__ void dp_combine_peer_kernel(const bf16* __restrict__ y, const int* __
     out[h] = __float2bfloat16_rn(s_ok ? acc : 0.f);
   }
   __syncthreads();
-  if (tid == 0) own->dp_row_epoch = ep;
+  if (tid == 0 && y) own->dp_row_epoch = ep;
   pdl_trigger();
 }
 
@@ -207,10 +209,10 @@ extern "C" int flint_dp_gather_peer(const void* send, int64_t H, const void* con
 extern "C" int flint_dp_combine_peer(const void* y, const int32_t* topk_ids, const float* topk_weights, int64_t topk,
                                      int64_t E, int64_t H, const void* const* peers, int rank, int world, void* out,
                                      int pdl, void* stream) {
-  if (!y || !topk_ids || !topk_weights || !out) return FLINT_ERR_ARGUMENT;
+  if (!topk_ids || !topk_weights || !out) return FLINT_ERR_ARGUMENT;
   if (topk < 1 || topk > kPeerSlots || H < 8 || H % 8 != 0 || H > 65536 || E < world || E % world != 0)
     return FLINT_ERR_SHAPE;
-  if (!aligned(y, 16)) return FLINT_ERR_ALIGN;
+  if (y && !aligned(y, 16)) return FLINT_ERR_ALIGN;
   PeerSet ps;
   const int rc = peer_set(peers, rank, world, &ps);
   if (rc) return rc;

@@ -217,7 +217,9 @@ class Decoder:
         expert is local in one launch (moe_fused_ep), reduce-scatter the per-route rows (each element has one
         non-zero term, so the sum is exact) and combine their own token's rows; the vocabulary-sharded head takes every rank's
         hidden state and a MAX all-reduce of the argmax keys.  Each rank's stream equals the one-GPU chain decode of
-        that stream bit for bit."""
+        that stream bit for bit.  exchange (dp=True): "nccl" (all-gather, reduce-scatter), "peer" (both exchanges
+        inside the MoE launch over NVLink peer memory, moe_fused_dp_peer, then a receive-and-sum launch) or
+        "peer_split" (separate gather and combine launches over peer memory around moe_fused_ep)."""
         # measured per layer at 6K context: one stream, the block; 2..5 streams, the chain (67.7 us at 4 against the
         # fused launch's 70.9); 6..8, the fused launch (118 us at 8 against the chain's 135).  Sharded: block or chain.
         if dp:
@@ -239,11 +241,11 @@ class Decoder:
             raise ValueError("moe='block' decodes one token; use 'chain' or 'fused' for batches")
         if model.world > 1 and (moe == "fused" or group is None):
             raise ValueError("a sharded model decodes with moe='block' (one token) or 'chain' and needs its process group")
-        if exchange not in ("peer", "nccl"):
-            raise ValueError(f"exchange must be 'peer' or 'nccl', got {exchange!r}")
+        if exchange not in ("peer", "nccl") and not (dp and exchange == "peer_split"):
+            raise ValueError(f"exchange must be 'peer' or 'nccl' ('peer_split' with dp=True), got {exchange!r}")
         self.group, self.exchange, self.prefetch = group, exchange, prefetch
         self.peers = None
-        if model.world > 1 and exchange == "peer":
+        if model.world > 1 and exchange in ("peer", "peer_split"):
             from .peer import PeerBuffers
             self.peers = PeerBuffers(group, model.cfg.hidden)
         if attn not in ("block", "chain"):
@@ -316,7 +318,7 @@ class Decoder:
         # dense layers: route + up + down; the shared expert: up + down (its bf16 add is a torch elementwise op)
         ep = model.world > 1
         moe_launches = ((4 if ep else 3) if moe == "chain" else 2 if (ep and exchange == "nccl")
-                        else (3 if exchange == "peer" else 2) if moe == "dp" else 1)
+                        else (3 if exchange == "peer_split" else 2) if moe == "dp" else 1)
         n_dense = len(c.mlp_only_layers)
         shared_fused = (c.shared_inter and model.world == 1 and moe == "block" and c.shared_inter % 256 == 0
                         and c.shared_inter <= 1024 and c.topk < 8)
@@ -383,7 +385,16 @@ class Decoder:
             N, r = m.world, m.rank
             x_all, res_all = self.dp_recv[:, 0], self.dp_recv[:, 1]
             pp = self.peers
-            if pp is not None:        # exchanges over NVLink peer memory inside our own launches
+            if self.exchange == "peer":   # both exchanges inside the MoE launch, then this rank's receive-and-sum
+                return seq + [
+                    ("moe_fused_dp_peer", lambda: ops.moe_fused_dp_peer(self.dp_send, L["ln2"], c.rms_eps, L["gate"],
+                                                                        c.topk, ew.score_fn, ew.w13, ew.s13, ew.g13,
+                                                                        ew.w2, ew.s2, ew.g2, c.num_experts, m.e_lo,
+                                                                        pp.ptrs, pp.rank, self.dp_res, self.dp_ti,
+                                                                        self.dp_tw)),
+                    ("dp_combine_peer_recv", lambda: ops.dp_combine_peer_recv(self.dp_ti, self.dp_tw, c.num_experts,
+                                                                              pp.ptrs, pp.rank, self.h))]
+            if pp is not None:        # exchanges over NVLink peer memory in their own launches
                 gather = ("dp_gather_peer", lambda: ops.dp_gather_peer(self.dp_send, pp.ptrs, pp.rank, self.dp_recv))
                 combine = ("dp_combine_peer", lambda: ops.dp_combine_peer(self.dp_y, self.dp_ti, self.dp_tw,
                                                                           c.num_experts, pp.ptrs, pp.rank, self.h))
@@ -559,7 +570,8 @@ class Decoder:
         """Bytes one launch of kernel `name` must move at batch M and context ctx (weights / KV read once,
         activations in and out): the roofline numerator."""
         c, M = self.c, self.M
-        if self.dp and name in ("moe_fused_ep", "combine", "head", "dp_gather_peer", "dp_combine_peer"):
+        if self.dp and name in ("moe_fused_ep", "moe_fused_dp_peer", "combine", "head", "dp_gather_peer",
+                                "dp_combine_peer"):
             M = self.m.world                              # the MoE and the head work on every rank's token
         nv = lambda n, k: n * k // 2 + n * k // 16
         H, D = c.hidden, c.head_dim
@@ -569,6 +581,8 @@ class Decoder:
             return 2 * (2 * H * 2) * self.m.world
         if name == "dp_combine_peer":                      # local routes' rows pushed, this token's rows read
             return 2 * c.topk * H * 2 + H * 2
+        if name == "dp_combine_peer_recv":                 # this token's rows read, its output written
+            return c.topk * H * 2 + H * 2
         if name == "qkv":
             return nv(c.qkv_rows, H) + M * (3 * H * 2 + c.qkv_rows * 2 + c.num_heads * D * 2 + 2 * c.num_kv_heads * D * 2)
         if name == "attention":
@@ -593,6 +607,8 @@ class Decoder:
         if name == "moe_fused_ep":                        # every rank's token routed; local experts' routes only
             return (self.algorithmic_bytes("route", ctx) + (self.algorithmic_bytes("up", ctx)
                                                             + self.algorithmic_bytes("down", ctx)) // self.m.world)
+        if name == "moe_fused_dp_peer":                   # moe_fused_ep + this rank's rows to every rank
+            return self.algorithmic_bytes("moe_fused_ep", ctx) + self.algorithmic_bytes("dp_gather_peer", ctx)
         if name in ("up_ep", "down_ep"):                  # local experts only: topk / world routes on average
             return self.algorithmic_bytes(name[:-3], ctx) // self.m.world
         if name in ("moe_block_ep", "moe_block_peer"):   # local experts only: topk / world routed slots on average

@@ -599,6 +599,58 @@ def _(y, topk_ids, topk_weights, num_experts, peers, rank, out):
     return None
 
 
+@torch.library.custom_op(f"{NS}::dp_combine_peer_recv", mutates_args=("out",))
+def dp_combine_peer_recv(topk_ids: torch.Tensor, topk_weights: torch.Tensor, num_experts: int, peers: list[int],
+                         rank: int, out: torch.Tensor) -> None:
+    """This rank's token's slot-order weighted sum of the rows that flint_moe_fused_dp_peer pushed
+    (flint_dp_combine_peer with y NULL)."""
+    _lib.require_cuda(out, "dp_combine_peer_recv")
+    W, topk = topk_ids.shape
+    H = out.numel()
+    if W != len(peers) or topk_weights.shape != topk_ids.shape:
+        raise _lib.FlintError("dp_combine_peer_recv: ids / weights [world, topk], out [H]")
+    rc = lib().flint_dp_combine_peer(None, ptr(topk_ids), ptr(topk_weights), topk, int(num_experts), H,
+                                     _peer_array(peers), int(rank), W, ptr(out), PDL, stream_ptr(out.device))
+    check(rc, "flint_dp_combine_peer")
+
+
+@dp_combine_peer_recv.register_fake
+def _(topk_ids, topk_weights, num_experts, peers, rank, out):
+    return None
+
+
+@torch.library.custom_op(f"{NS}::moe_fused_dp_peer", mutates_args=("res_out", "ids_out", "tw_out"))
+def moe_fused_dp_peer(send: torch.Tensor, norm_w: torch.Tensor, eps: float, gate_w: torch.Tensor, topk: int,
+                      score_fn: int, w13: torch.Tensor, s13: torch.Tensor, g13: torch.Tensor, w2: torch.Tensor,
+                      s2: torch.Tensor, g2: torch.Tensor, num_experts: int, expert_lo: int, peers: list[int], rank: int,
+                      res_out: torch.Tensor, ids_out: torch.Tensor, tw_out: torch.Tensor) -> None:
+    """The data-parallel MoE layer with its exchanges inside the launch (flint_moe_fused_dp_peer): this rank's rows
+    send bf16 [2, H] in, every rank's residual res_out [world, H] and routing ids_out / tw_out [world, topk] out; the
+    local routes' rows go to their tokens' ranks for dp_combine_peer_recv."""
+    _lib.require_cuda(send, "moe_fused_dp_peer")
+    W = len(peers)
+    H = send.shape[-1]
+    n_local, I2, Hh = w13.shape
+    if send.dtype != torch.bfloat16 or send.numel() != 2 * H or not send.is_contiguous() or Hh * 2 != H or \
+            gate_w.shape != (num_experts, H) or res_out.shape != (W, H) or ids_out.shape != (W, topk) or \
+            tw_out.shape != (W, topk):
+        raise _lib.FlintError("moe_fused_dp_peer: send bf16 [2, H], res_out [world, H], ids / weights [world, topk]")
+    nbytes = lib().flint_moe_fused_workspace_bytes(num_experts, H, I2 // 2)
+    ws = _lib.workspace(send.device, f"moe_fused_{num_experts}_{H}_{I2 // 2}", nbytes)
+    rc = lib().flint_moe_fused_dp_peer(ptr(send), ptr(norm_w), float(eps), ptr(gate_w), H, int(num_experts), int(topk),
+                                       int(score_fn), ptr(_u8(w13)), ptr(_u8(s13)), ptr(g13), ptr(_u8(w2)),
+                                       ptr(_u8(s2)), ptr(g2), I2 // 2, int(expert_lo), n_local, _peer_array(peers),
+                                       int(rank), W, ptr(res_out), None, ptr(ids_out), ptr(tw_out), ptr(ws), PDL,
+                                       stream_ptr(send.device))
+    check(rc, "flint_moe_fused_dp_peer")
+
+
+@moe_fused_dp_peer.register_fake
+def _(send, norm_w, eps, gate_w, topk, score_fn, w13, s13, g13, w2, s2, g2, num_experts, expert_lo, peers, rank,
+      res_out, ids_out, tw_out):
+    return None
+
+
 @torch.library.custom_op(f"{NS}::keys_allmax_peer", mutates_args=("tokens",))
 def keys_allmax_peer(keys: torch.Tensor, peers: list[int], rank: int, tokens: torch.Tensor) -> None:
     """Argmax over the vocabulary shards of all ranks (flint_argmax_keys_allmax_peer)."""

@@ -321,11 +321,26 @@ int flint_moe_block_peer(const void* x, int64_t ldx, const void* res, const void
  * flint_dp_combine_peer: y bf16 [world * topk][H] = the per-route rows of every rank's token (flint_moe_fused_ep: this
  * rank's experts' routes, zeros elsewhere); each route's row goes to its token's rank, and out bf16 [H] =
  * bf16(sum_s topk_weights[rank * topk + s] * row_s) in slot order for this rank's token (topk_ids / topk_weights
- * [world][topk], identical on every rank).  E % world == 0, topk <= 8.  No counterpart in the reference (one GPU). */
+ * [world][topk], identical on every rank).  E % world == 0, topk <= 8.  y may be NULL when
+ * flint_moe_fused_dp_peer has pushed the rows itself: the launch then only waits for every rank's rows and sums.
+ * No counterpart in the reference (one GPU). */
 int flint_dp_gather_peer(const void* send, int64_t H, const void* const* peers, int rank, int world, void* out, int pdl,
                          void* stream);
 int flint_dp_combine_peer(const void* y, const int32_t* topk_ids, const float* topk_weights, int64_t topk, int64_t E,
                           int64_t H, const void* const* peers, int rank, int world, void* out, int pdl, void* stream);
+/* Data-parallel MoE layer with both exchanges inside the launch (no counterpart in the reference, which decodes on
+ * one GPU): flint_moe_fused_ep on the M = world tokens, where CTA 0 first stores this rank's two rows send bf16
+ * [2][H] (attention output, residual) into every rank's token table over NVLink and every CTA waits for all ranks'
+ * rows, and where each local route's output rows go straight into its token owner's row table (this rank's flag
+ * raised there by the last CTA).  Then flint_dp_combine_peer(NULL, ...) on every rank gives that rank's token's
+ * output.  res_out bf16 [world][H], topk_ids_out / topk_weights_out [world][topk] (required), logits_out optional.
+ * H = 2048 or 4096, topk <= 8, experts split in equal contiguous ranges; workspace as flint_moe_fused. */
+int flint_moe_fused_dp_peer(const void* send, const void* norm_w, float eps, const void* gate_w, int64_t H, int64_t E,
+                            int64_t topk, int score_fn, const void* w13, const void* s13, const float* g13,
+                            const void* w2, const void* s2, const float* g2, int64_t I, int64_t expert_lo,
+                            int64_t n_local, const void* const* peers, int rank, int world, void* res_out,
+                            float* logits_out, int32_t* topk_ids_out, float* topk_weights_out, void* workspace, int pdl,
+                            void* stream);
 /* Vocabulary-shard argmax exchange: keys = this rank's M (<= 8) keys from flint_lm_head_nv4_shard; tokens int32 [M]
  * = the argmax over all ranks' shards (lowest id among the largest logits), -1 if a peer wait timed out. */
 int flint_argmax_keys_allmax_peer(const uint64_t* keys, int64_t M, const void* const* peers, int rank, int world,

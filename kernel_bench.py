@@ -16,6 +16,12 @@ also the small case used for full ncu captures of one kernel.
 
 times the checkpoint-format kernels on one tensor of --rows x --cols values (default: the LM head, 174.6 MB of GGUF
 bytes, larger than L2).
+
+    python flint-vllm-single-dgx-spark_b200/build.py --timeline _build_tl
+    python kernel_bench.py --lib _build_tl/libflint_b200.so --timeline --kernel moe_fused --moe fused --batch 8
+
+runs the same timing on an instrumented library and then prints the phase stamps of the kernel's last launch (the
+last layer): per stamp the minimum, median and maximum over the CTAs, in microseconds from the first CTA's entry.
 """
 from __future__ import annotations
 
@@ -32,15 +38,68 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 PKG_DIR = os.path.join(ROOT, "flint-vllm-single-dgx-spark_b200")
 
 
-def _package():
+def _package(lib_path: str | None = None):
     if "flint_b200" in sys.modules:
         return sys.modules["flint_b200"]
     spec = importlib.util.spec_from_file_location("flint_b200", os.path.join(PKG_DIR, "__init__.py"),
                                                   submodule_search_locations=[PKG_DIR])
     mod = importlib.util.module_from_spec(spec)
     sys.modules["flint_b200"] = mod
+    if lib_path:                       # point the loader at another build before anything loads the library
+        lspec = importlib.util.spec_from_file_location("flint_b200._lib", os.path.join(PKG_DIR, "_lib.py"))
+        lmod = importlib.util.module_from_spec(lspec)
+        sys.modules["flint_b200._lib"] = lmod
+        lspec.loader.exec_module(lmod)
+        lmod.LIB_PATH = os.path.abspath(lib_path)
     spec.loader.exec_module(mod)
     return mod
+
+
+# Phase stamps of the instrumented kernels (the numbering of each kernel's FLINT_TL calls) and the library call that
+# reads them.
+TIMELINES = {
+    "attn_block": ("flint_timeline_attn_block", {
+        0: "entry", 1: "PDL wait done", 12: "norm computed", 13: "QKV weights resident", 14: "QKV sums done",
+        3: "QKV rows published", 5: "first q heads fetched", 6: "own pages done", 7: "split-K merges done",
+        8: "O rows written", 10: "producer: partition, first page", 11: "producer: last page requested"}),
+    "moe_block": ("flint_timeline_moe_block", {
+        0: "entry", 1: "PDL wait done", 2: "norm + router rows published", 7: "all router logits seen",
+        8: "top-k computed", 3: "plan released", 11: "producer: expert loads issued", 9: "first up unit landed",
+        4: "up units done", 5: "down rows done", 6: "output written"}),
+    "moe_fused": ("flint_timeline_moe_fused", {
+        0: "entry", 1: "PDL wait done", 15: "norm + f16 staging done", 16: "router rows written",
+        3: "barrier 0", 17: "top-k done", 4: "plan released", 12: "producer: first stage", 5: "first gate/up tile",
+        13: "producer: last gate/up stage", 6: "gate/up tiles done", 7: "barrier 1", 8: "act rows staged",
+        14: "producer: last stage", 9: "down tiles done", 10: "barrier 2", 11: "output written"}),
+}
+TIMELINES["moe_block_shared"] = TIMELINES["moe_block"]
+TIMELINES["moe_fused_ep"] = TIMELINES["moe_fused"]
+
+
+def print_timeline(name: str):
+    import ctypes
+    if name not in TIMELINES:
+        raise SystemExit(f"--timeline: no stamps in {name}")
+    fn, labels = TIMELINES[name]
+    lib = sys.modules["flint_b200._lib"].lib()
+    if not hasattr(lib, fn):
+        raise SystemExit(f"--timeline: {fn} missing -- build the library with build.py --timeline DIR, pass --lib")
+    slots, ctas = 32, 160
+    buf = (ctypes.c_uint64 * (ctas * slots))()
+    f = getattr(lib, fn)
+    f.argtypes, f.restype = [ctypes.c_void_p], ctypes.c_int
+    if f(ctypes.addressof(buf)) != 0:
+        raise SystemExit(f"{fn} failed")
+    nsm = torch.cuda.get_device_properties(0).multi_processor_count
+    t = np.frombuffer(buf, dtype=np.uint64).reshape(ctas, slots).astype(np.int64)[:nsm]
+    t0 = t[:, 0][t[:, 0] > 0].min()
+    rows = {}
+    for i, label in labels.items():
+        ok = t[:, i] > 0
+        if ok.any():
+            v = (t[ok, i] - t0) / 1e3
+            rows[f"{i} {label}"] = [round(float(v.min()), 2), round(float(np.median(v)), 2), round(float(v.max()), 2)]
+    print(json.dumps({"kernel": name, "timeline_us_min_median_max": rows}), flush=True)
 
 
 def main(argv=None):
@@ -58,8 +117,10 @@ def main(argv=None):
                          "expert 1024: moe_block_shared)")
     ap.add_argument("--rows", type=int, default=151552)
     ap.add_argument("--cols", type=int, default=2048)
+    ap.add_argument("--lib", default=None, help="load this build of libflint_b200.so (e.g. an instrumented one)")
+    ap.add_argument("--timeline", action="store_true", help="print the kernel's phase stamps (instrumented build)")
     args = ap.parse_args(argv)
-    _package()
+    _package(args.lib)
     if args.kernel in ("gguf_repack", "nvfp4_dequant"):
         return time_format_kernel(args)
     from flint_b200.model import Decoder, FlintConfig, FlintModel
@@ -111,6 +172,10 @@ def time_kernel(name, args, dec, model, cfg, dev):
     print(json.dumps({"kernel": name, "config": args.config, "batch": args.batch, "moe": dec.moe, "ctx": args.ctx,
                       "launches": args.reps * len(fns), "us_per_launch": round(us, 2), "bytes_per_launch": nbytes,
                       "GBps": round(nbytes / us / 1e3, 1)}), flush=True)
+    if args.timeline:
+        g.replay()
+        torch.cuda.synchronize()
+        print_timeline(name)
     del g
 
 

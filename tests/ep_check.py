@@ -47,7 +47,8 @@ CASES = [("b1_block_peer", 1, "block", "peer", False), ("b1_block_nccl", 1, "blo
          ("b3_chain", 3, "chain", "peer", False), ("b3_chain_sampled", 3, "chain", "peer", True),
          ("b1_block_sampled", 1, "block", "peer", True),
          ("dp_streams", 1, "dp", "peer", False),           # one stream per rank: data-parallel attention + EP MoE
-         ("dp_streams_nccl", 1, "dp", "nccl", False)]
+         ("dp_streams_nccl", 1, "dp", "nccl", False),
+         ("dp_streams_split", 1, "dp", "peer_split", False)]
 
 
 def decode(model, prompt, n, batch, moe, group=None, exchange="peer", sampled=False):
