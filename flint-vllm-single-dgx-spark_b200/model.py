@@ -206,7 +206,8 @@ class Decoder:
     def __init__(self, model: FlintModel, batch: int = 1, moe: str | None = None, attn: str = "block", group=None,
                  exchange: str = "peer", prefetch: bool = False, sampling: dict | None = None, dp: bool = False):
         """moe: "block" (one launch, one token; the default at batch 1), "chain" (route, up, down: three launches;
-        the default for 2..8 tokens) or "fused" (one persistent launch for 1..8 tokens); attn: "block" (QKV +
+        the default for a sharded model's batches) or "fused" (one persistent launch for 1..8 tokens; the default for
+        2..8 tokens on one GPU); attn: "block" (QKV +
         attention + O in one persistent launch) or "chain" (three launches).  sampling: None for greedy decode, or
         {"temperature", "top_k", "top_p", "seeds"} (one int64 seed per stream) for the seeded top-k -> top-p draw of
         flint_lm_head_nv4_sample; the draw of step t uses the Philox counter (t, stream).
@@ -220,8 +221,8 @@ class Decoder:
         that stream bit for bit.  exchange (dp=True): "nccl" (all-gather, reduce-scatter), "peer" (both exchanges
         inside the MoE launch over NVLink peer memory, moe_fused_dp_peer, then a receive-and-sum launch) or
         "peer_split" (separate gather and combine launches over peer memory around moe_fused_ep)."""
-        # measured per layer at 6K context: one stream, the block; 2..5 streams, the chain (67.7 us at 4 against the
-        # fused launch's 70.9); 6..8, the fused launch (118 us at 8 against the chain's 135).  Sharded: block or chain.
+        # measured per layer on a B200: one stream, the block; 2..8 streams, the fused launch (35.9 / 38.5 / 45.7 / 47.9
+        # us at 2 / 3 / 4 / 5 against the chain's 39.5 / 47.6 / 61.6 / 71.6; 59.3 at 8).  Sharded: block or chain.
         if dp:
             if model.world < 2 or group is None or batch != 1:
                 raise ValueError("dp=True decodes one stream per GPU of a sharded model and needs its process group")
@@ -230,8 +231,7 @@ class Decoder:
             moe = "dp"
         self.dp = dp
         sharded_shared = model.world > 1 and model.cfg.shared_inter > 0
-        moe = moe or ("block" if batch == 1 and not sharded_shared else
-                      "chain" if batch <= 5 or model.world > 1 else "fused")
+        moe = moe or ("block" if batch == 1 and not sharded_shared else "chain" if model.world > 1 else "fused")
         if sharded_shared and moe != "chain":
             # the shared expert reads the normalised input, which the sharded block launches do not write out
             raise ValueError("a sharded model with a shared expert decodes with moe='chain'")
