@@ -403,6 +403,9 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
       }
     }
   }
+  // the consumers' norm weights (8 per thread) do not depend on the previous kernel either
+  const uint4 nwc = warp < kBW && (int)threadIdx.x < (a.H >> 3) ? reinterpret_cast<const uint4*>(a.nw)[threadIdx.x]
+                                                                : make_uint4(0u, 0u, 0u, 0u);
   pdl_wait();
   if (threadIdx.x == 0) FLINT_TL(1);
   unsigned ep;                                         // this launch's tag (the last CTA to retire advances it)
@@ -438,8 +441,8 @@ attn_block_kernel(const __grid_constant__ CUtensorMap mqc, const __grid_constant
   } else {
     // ---- A (first half), consumers: add + RMSNorm ----
     if (a.H / 8 <= kBCons)
-      norm_stage_f16_1(a.x, a.ldx, a.tokens, a.res, a.ldr, a.nw, a.eps, M, a.H, xs, shift, red_n,
-                       cta == 0 ? a.res_out : nullptr, kBCons, 1);
+      norm_stage_f16_1w(a.x, a.ldx, a.tokens, a.res, a.ldr, nwc, a.eps, M, a.H, xs, shift, red_n,
+                        cta == 0 ? a.res_out : nullptr, kBCons, 1);
     else
       norm_stage_f16(a.x, a.ldx, a.tokens, a.res, a.ldr, a.nw, a.eps, M, a.H, xs, shift, red_n,
                      cta == 0 ? a.res_out : nullptr, kBCons, 1);
