@@ -548,6 +548,110 @@ __device__ __forceinline__ void norm_xn_stage_f16(const bf16* x, int64_t ldx, co
   sync();
 }
 
+// norm_xn_stage_f16 for nthreads = 2 (H / 8) (two halves of the block): thread t owns chunk c = t % (H / 8) of rows
+// 4 h .. 4 h + 3, h = t / (H / 8) -- half the registers of the one-half form.  Per row the same per-thread chains,
+// the same butterfly over the 32 chunks of a warp and the same order over the chunk warps, so the same bits.
+// H / 8 a multiple of 32; wchunk: the norm weights of chunk c.  red: >= (H / 256) * 8 + 8 floats.
+__device__ __forceinline__ void norm_xn_stage_f16_halves(const bf16* x, int64_t ldx, const bf16* res, uint4 wchunk,
+                                                         float eps, int M, int H, bf16* xn, bf16* xn_out,
+                                                         bf16* res_out, __half* xs, int* shift, float* red,
+                                                         int nthreads, int bar, bool cg) {
+  const int tid = threadIdx.x, lane = tid & 31, H8 = H >> 3, half = tid / H8, c = tid - half * H8;
+  const int cw = c >> 5, ncw = H8 >> 5;
+  auto sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthreads) : "memory"); };
+  int* rmax = reinterpret_cast<int*>(red + ncw * 8);
+  uint4 xv[4], rv[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int m = 4 * half + i;
+    xv[i] = make_uint4(0u, 0u, 0u, 0u);
+    rv[i] = xv[i];
+    if (m < M) {                              // cg: rows another GPU stored into this one's memory
+      const uint4* xp = reinterpret_cast<const uint4*>(x + m * ldx) + c;
+      xv[i] = cg ? __ldcg(xp) : *xp;
+      if (res) {
+        const uint4* rp = reinterpret_cast<const uint4*>(res + m * ldx) + c;
+        rv[i] = cg ? __ldcg(rp) : *rp;
+      }
+    }
+  }
+  float a[4][8], ss[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    ss[i] = 0.f;
+    if (4 * half + i < M) {
+      bf16x8_to_f32(xv[i], a[i]);
+      if (res) {
+        float b[8];
+        bf16x8_to_f32(rv[i], b);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a[i][j] += b[j];
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss[i] = fmaf(a[i][j], a[i][j], ss[i]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float v = ss[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[cw * 8 + 4 * half + i] = v;
+  }
+  if (tid < 8) rmax[tid] = 0;
+  sync();
+  float wf[8], rsv[4];
+  bf16x8_to_f32(wchunk, wf);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float tot = 0.f;
+    for (int ww = 0; ww < ncw; ++ww) tot += red[ww * 8 + 4 * half + i];
+    rsv[i] = rsqrtf(tot / (float)H + eps);
+  }
+  uint32_t pk[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int m = 4 * half + i;
+    if (m < M) {
+      uint32_t pr[4];
+      float mx = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __nv_bfloat162 n2 = __floats2bfloat162_rn(a[i][2 * j] * rsv[i] * wf[2 * j], a[i][2 * j + 1] * rsv[i] * wf[2 * j + 1]);
+        mx = fmaxf(mx, fmaxf(fabsf(__low2float(n2)), fabsf(__high2float(n2))));
+        pk[i][j] = *reinterpret_cast<uint32_t*>(&n2);
+        __nv_bfloat162 r2 = __floats2bfloat162_rn(a[i][2 * j], a[i][2 * j + 1]);
+        pr[j] = *reinterpret_cast<uint32_t*>(&r2);
+      }
+      const uint4 nv = make_uint4(pk[i][0], pk[i][1], pk[i][2], pk[i][3]);
+      reinterpret_cast<uint4*>(xn + m * H)[c] = nv;
+      if (xn_out) reinterpret_cast<uint4*>(xn_out + (int64_t)m * H)[c] = nv;
+      if (res_out) reinterpret_cast<uint4*>(res_out + (int64_t)m * H)[c] = make_uint4(pr[0], pr[1], pr[2], pr[3]);
+      smem_max_grouped(&rmax[m], mx);
+    }
+  }
+  sync();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int m = 4 * half + i;
+    if (m < M) {
+      const float mx = __int_as_float(rmax[m]);
+      int s = 0;
+      if (mx > 0.f && !(mx != mx) && mx <= 3.0e38f) s = 14 - ((int)((__float_as_uint(mx) >> 23) & 0xFF) - 127);
+      if (c == 0) shift[m] = s;
+      uint32_t h[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __half2 v = __floats2half2_rn(scale_pow2(bf16_bits_to_f32(pk[i][j] & 0xFFFFu), s),
+                                      scale_pow2(bf16_bits_to_f32(pk[i][j] >> 16), s));
+        h[j] = *reinterpret_cast<uint32_t*>(&v);
+      }
+      *reinterpret_cast<uint4*>(xs + m * xs_stride(H) + xs_perm(c * 8)) = make_uint4(h[0], h[1], h[2], h[3]);
+    }
+  }
+  sync();
+}
+
 // norm_stage_f16 with ONE global pass, for H / 8 <= nthreads: each thread owns one 8-wide chunk of every row and keeps
 // x (+ res) in registers between the sum of squares and the normalisation (same fmaf chains, same bits).
 // (norm_stage_f16_1w: the thread's 8 norm weights, w[8 tid .. 8 tid + 7], are passed in, loaded before the PDL wait.)

@@ -86,16 +86,20 @@ __host__ __device__ inline size_t moe_fused_ws_bytes(int E, int H, int I) {
 }
 
 
-template <int NS, int NV>
-__global__ void __launch_bounds__((kFW + 1) * 32, 1)
+// KG consumer groups of kFW warps: group g works on the CTA's tiles g, g + KG, ... of each phase, two tiles' stages
+// interleaved in the ring, each tile computed exactly as by one group (same warp / row mapping and sums), so KG
+// changes the speed only.  KG = 2 needs H = 2048 (its norm gives each thread half the rows of one chunk).
+template <int NS, int NV, int KG>
+__global__ void __launch_bounds__((KG * kFW + 1) * 32, 1)
 moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant__ CUtensorMap up_s,
                  const __grid_constant__ CUtensorMap dn_c, const __grid_constant__ CUtensorMap dn_s, const MoeFusedArgs a) {
   using L = EngineSmem<kFW, NS, kFBox>;
-  constexpr int NT = kFW * 32;              // consumer threads
+  constexpr int GT = kFW * 32;              // threads of one consumer group
+  constexpr int NT = KG * GT;               // consumer threads
+  constexpr int PW = KG * kFW;              // the producer warp
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* dtile = reinterpret_cast<float*>(smem + L::ring_bytes);
-  __half* xs = reinterpret_cast<__half*>(smem + L::ring_bytes + L::dtile_bytes);        // f16 [M][H+8]
+  __half* xs = reinterpret_cast<__half*>(smem + L::ring_bytes + KG * L::dtile_bytes);   // f16 [M][H+8]
   uint8_t* region = reinterpret_cast<uint8_t*>(xs + a.M * xs_stride(a.H));              // phase R: bf16 xn; D: f16 act
   bf16* xnb = reinterpret_cast<bf16*>(region);
   __half* xa = reinterpret_cast<__half*>(region);
@@ -136,7 +140,7 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   // blockIdx.x + (p / M) nb and token p % M, and consumer warp w takes pairs w, w + kFW, ...  A warp's first row is
   // prefetched into registers before the PDL wait.
   const int npairs = ((int)blockIdx.x < E ? M : 0) + ((int)(blockIdx.x + nb) < E ? M : 0);
-  int wv_rk = warp < kFW && warp < npairs ? warp / M : -1;   // row (0 or 1) held in wv
+  int wv_rk = warp < PW && warp < npairs ? warp / M : -1;    // row (0 or 1) held in wv
   uint4 wv[NV];
   if (wv_rk >= 0) {
     const uint4* wp = reinterpret_cast<const uint4*>(a.gate_w + (int64_t)(blockIdx.x + wv_rk * nb) * H);
@@ -144,12 +148,15 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
     for (int i = 0; i < NV; ++i) wv[i] = ldg_stream_v4(wp + lane + 32 * i);
   }
   // the norm weights (this thread's 8) do not depend on the previous kernel either
-  const uint4 nwc = tid < H / 8 ? reinterpret_cast<const uint4*>(a.nw)[tid] : make_uint4(0u, 0u, 0u, 0u);
+  const uint4 nwc = tid < NT && (KG > 1 || tid < H / 8) ? reinterpret_cast<const uint4*>(a.nw)[tid % (H / 8)]
+                                                        : make_uint4(0u, 0u, 0u, 0u);
   pdl_wait();
   if (tid == 0) FLINT_TL(1);
 
-  if (warp == kFW) {
+  if (warp == PW) {
     // ---------------- producer: wait for the routing plan, then stream up tiles followed by down tiles ----------------
+    // (per phase, the tiles of consumer groups 0 .. KG-1 go in rounds of KG tiles, their stages interleaved: stage k of
+    // round member j is stage number round_base + k * (members) + j of the phase)
     if (lane == 0) {
       bool ok = false;
       for (unsigned i = 0; i < FLINT_WAIT_LIMIT && !ok; ++i) ok = mbar_try_wait(&plan_bar, 0);
@@ -160,38 +167,42 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
       tma_prefetch_desc(&up_c);
       tma_prefetch_desc(&dn_c);
       const int u0 = tiles[0], u1 = tiles[1], d0 = tiles[2], d1 = tiles[3];
-      const int nup = u1 - u0, ntiles = nup + (d1 - d0);
       int slot = 0, s = 0;
       unsigned phase = 0;
-      for (int i = 0; i < ntiles; ++i) {
-        const bool up = i < nup;
-        const int t = up ? u0 + i : d0 + (i - nup);             // up tile, or down tile (numbered from 0)
-        const int nks = up ? nks_up : nks_dn;
-        int y0, y1;
-        if (up) {
-          const int u = t / tpu, j = t - u * tpu, e = G.exp[u];
-          y0 = e * 2 * I + j * kFBox;
-          y1 = y0 + I;
-        } else {
-          const int u = t / tpd, j = t - u * tpd;
-          y0 = G.exp[u] * H + j * 2 * kFBox;
-          y1 = y0 + kFBox;
-        }
+      for (int ph = 0; ph < 2; ++ph) {
+        const bool up = ph == 0;
+        const int t0 = up ? u0 : d0, n = up ? u1 - u0 : d1 - d0, nks = up ? nks_up : nks_dn;
         const CUtensorMap* mc = up ? &up_c : &dn_c;
         const CUtensorMap* ms = up ? &up_s : &dn_s;
-        for (int ks = 0; ks < nks; ++ks, ++s) {
-          if (s >= NS && !mbar_wait(&bars[NS + slot], phase ^ 1u, status)) return;
-          mbar_arrive_expect_tx(&bars[slot], L::code_bytes + L::scale_bytes);
-          uint8_t* cdst = smem + slot * L::code_bytes;
-          uint8_t* sdst = smem + NS * L::code_bytes + slot * L::scale_bytes;
-          tma_load_2d(cdst, mc, ks * 128, y0, &bars[slot]);
-          tma_load_2d(sdst, ms, ks * 16, y0, &bars[slot]);
-          tma_load_2d(cdst + kFBox * 128, mc, ks * 128, y1, &bars[slot]);
-          tma_load_2d(sdst + kFBox * 16, ms, ks * 16, y1, &bars[slot]);
-          if (s == 0) FLINT_TL(12);
-          if (++slot == NS) { slot = 0; phase ^= 1u; }
+        for (int rb = 0; rb < n; rb += KG) {
+          const int members = min(KG, n - rb);
+          for (int ks = 0; ks < nks; ++ks) {
+            for (int j = 0; j < members; ++j, ++s) {
+              const int t = t0 + rb + j;                        // up tile, or down tile (numbered from 0)
+              int y0, y1;
+              if (up) {
+                const int u = t / tpu, jj = t - u * tpu;
+                y0 = G.exp[u] * 2 * I + jj * kFBox;
+                y1 = y0 + I;
+              } else {
+                const int u = t / tpd, jj = t - u * tpd;
+                y0 = G.exp[u] * H + jj * 2 * kFBox;
+                y1 = y0 + kFBox;
+              }
+              if (s >= NS && !mbar_wait(&bars[NS + slot], phase ^ 1u, status)) return;
+              mbar_arrive_expect_tx(&bars[slot], L::code_bytes + L::scale_bytes);
+              uint8_t* cdst = smem + slot * L::code_bytes;
+              uint8_t* sdst = smem + NS * L::code_bytes + slot * L::scale_bytes;
+              tma_load_2d(cdst, mc, ks * 128, y0, &bars[slot]);
+              tma_load_2d(sdst, ms, ks * 16, y0, &bars[slot]);
+              tma_load_2d(cdst + kFBox * 128, mc, ks * 128, y1, &bars[slot]);
+              tma_load_2d(sdst + kFBox * 16, ms, ks * 16, y1, &bars[slot]);
+              if (s == 0) FLINT_TL(12);
+              if (++slot == NS) { slot = 0; phase ^= 1u; }
+            }
+          }
         }
-        if (i + 1 == nup) FLINT_TL(13);
+        if (up) FLINT_TL(13);
       }
       FLINT_TL(14);
     }
@@ -231,14 +242,18 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
     rin = xin + H;
     ldin = 2 * H;
   }
-  if (H / 8 <= NT) {
+  const bool one_pass = KG > 1 || H / 8 <= NT;
+  if (KG > 1) {
+    norm_xn_stage_f16_halves(xin, ldin, rin, nwc, a.eps, M, H, xnb, blockIdx.x == 0 ? a.xn_out : nullptr,
+                             blockIdx.x == 0 ? a.res_out : nullptr, xs, shift_x, red, NT, 2, a.peer != 0);
+  } else if (one_pass) {
     norm_xn_stage_f16(xin, ldin, rin, nwc, a.eps, M, H, xnb, blockIdx.x == 0 ? a.xn_out : nullptr,
                       blockIdx.x == 0 ? a.res_out : nullptr, xs, shift_x, red, NT, 2, a.peer != 0);
   } else {
     add_rmsnorm_2pass(xin, ldin, rin, a.nw, a.eps, M, H, xnb, red, NT, 2);
   }
   if (tid == 0) FLINT_TL(15);
-  if (blockIdx.x == 0 && H / 8 > NT) {
+  if (blockIdx.x == 0 && !one_pass) {
     for (int idx = tid; idx < M * (H / 8); idx += NT) {
       const int m = idx / (H / 8), k8 = idx - m * (H / 8);
       if (a.xn_out) reinterpret_cast<uint4*>(a.xn_out + (int64_t)m * H)[k8] = reinterpret_cast<const uint4*>(xnb + m * H)[k8];
@@ -262,7 +277,7 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
   }
   // one (row, token) dot per warp and pair: per lane the chain over i, then j, then the xor butterfly (the route
   // kernel's order)
-  for (int p = warp; p < npairs; p += kFW) {
+  for (int p = warp; p < npairs; p += PW) {
     const int rk = p / M, m = p - rk * M, row = (int)blockIdx.x + rk * (int)nb;
     if (rk != wv_rk) {                                    // a second row (E > nb and pairs beyond the first 8)
       const uint4* wp = reinterpret_cast<const uint4*>(a.gate_w + (int64_t)row * H);
@@ -285,7 +300,7 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
     if (lane == 0) __stcg(lg + m * E + row, bf16r(acc));
   }
   if (tid == 0) FLINT_TL(16);
-  if (H / 8 > NT) stage_rows_f16(xnb, H, M, H, xs, shift_x, red, NT, 2);
+  if (!one_pass) stage_rows_f16(xnb, H, M, H, xs, shift_x, red, NT, 2);
   if (tid == 0) FLINT_TL(2);
   if (!grid_sync(&ws->sync, nb, 0, NT, 2, &s_ok, status)) return;
   if (tid == 0) FLINT_TL(3);
@@ -330,22 +345,28 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
     FLINT_TL(4);
   }
 
+  // this thread's consumer group (its own dtile and named barrier), its warp and thread within the group
+  const int cg = warp / kFW, wg = warp - cg * kFW, gtid = tid - cg * GT, gbar = 1 + 2 * cg;   // barriers 1 and 3
+  float* dtile = reinterpret_cast<float*>(smem + L::ring_bytes + cg * L::dtile_bytes);
   const int g = lane >> 2, t = lane & 3;
-  const int prow = 16 * warp + tile_phi(g);
-  int slot = 0;
-  unsigned phase = 0;
+  const int prow = 16 * wg + tile_phi(g);
   bool ok = true;
-  auto run_tile = [&](int nks, const __half* xrow, bool active, float (&d)[4]) {
+  // stage k of the tile at position i of a phase with n tiles of nks stages each, numbered from `base`: rounds of KG
+  // tiles, a round's stages interleaved (the producer's order)
+  auto run_tile = [&](int nks, int base, int n, int i, const __half* xrow, bool active, float (&d)[4]) {
+    const int rb = i - i % KG, members = min(KG, n - rb);
+    const int s0 = base + rb * nks + (i - rb);
     float acc[4][4];
     zero_acc(acc);
     for (int ks = 0; ks < nks; ++ks) {
+      const int sidx = s0 + ks * members, slot = sidx % NS;
+      const unsigned phase = (unsigned)(sidx / NS) & 1u;
       if (ok && !mbar_wait(&bars[slot], phase, status)) ok = false;
       if (ok)
-        consume_stage(smem + slot * L::code_bytes, smem + NS * L::code_bytes + slot * L::scale_bytes, warp, g, t, ks, xrow,
+        consume_stage(smem + slot * L::code_bytes, smem + NS * L::code_bytes + slot * L::scale_bytes, wg, g, t, ks, xrow,
                       active, acc);
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[NS + slot]);
-      if (++slot == NS) { slot = 0; phase ^= 1u; }
     }
     sum_acc(acc, d);
   };
@@ -354,16 +375,17 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
     dtile[prow * 8 + 2 * t + 1] = d[1];
     dtile[(prow + 8) * 8 + 2 * t] = d[2];
     dtile[(prow + 8) * 8 + 2 * t + 1] = d[3];
-    named_bar_sync(1, NT);
+    named_bar_sync(gbar, GT);
   };
 
-  for (int tt = u0; tt < u1; ++tt) {
-    const int u = tt / tpu, j = tt - u * tpu, cnt = G.cnt[u], e = G.exp[u];
+  const int nup = u1 - u0;
+  for (int i = cg; i < nup; i += KG) {
+    const int tt = u0 + i, u = tt / tpu, j = tt - u * tpu, cnt = G.cnt[u], e = G.exp[u];
     const bool active = g < cnt;
     float d[4];
-    run_tile(nks_up, xs + (active ? G.tok[u][g] : 0) * xs_stride(H), active, d);
+    run_tile(nks_up, 0, nup, i, xs + (active ? G.tok[u][g] : 0) * xs_stride(H), active, d);
     store_dtile(d);
-    for (int idx = tid; idx < kFBox * 8; idx += NT) {
+    for (int idx = gtid; idx < kFBox * 8; idx += GT) {
       const int n = idx / kFBox, r = idx - n * kFBox;
       if (n >= cnt) continue;
       const float sc = ldexpf(a.g13[e], -shift_x[G.tok[u][n]]);
@@ -372,8 +394,8 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
       __stcg(reinterpret_cast<unsigned short*>(act_g + (int64_t)G.route[u][n] * I + j * kFBox + r),
              __bfloat16_as_ushort(__float2bfloat16_rn(silu * uv)));
     }
-    named_bar_sync(1, NT);
-    if (tid == 0 && tt == u0) FLINT_TL(5);
+    named_bar_sync(gbar, GT);
+    if (tid == 0 && i == 0) FLINT_TL(5);
   }
   if (tid == 0) FLINT_TL(6);
   if (!grid_sync(&ws->sync, nb, 1, NT, 2, &s_ok, status)) return;
@@ -395,13 +417,14 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
     });
   }
   if (tid == 0) FLINT_TL(8);
-  for (int td = d0; td < d1; ++td) {
-    const int u = td / tpd, j = td - u * tpd, cnt = G.cnt[u], e = G.exp[u], slot0 = (u - ua) * 8;
+  const int ndn = d1 - d0;
+  for (int i = cg; i < ndn; i += KG) {
+    const int td = d0 + i, u = td / tpd, j = td - u * tpd, cnt = G.cnt[u], e = G.exp[u], slot0 = (u - ua) * 8;
     const bool active = g < cnt && slot0 + g < a.nslot_cap;
     float d[4];
-    run_tile(nks_dn, xa + (slot0 + (active ? g : 0)) * xs_stride(I), active, d);
+    run_tile(nks_dn, nup * nks_up, ndn, i, xa + (slot0 + (active ? g : 0)) * xs_stride(I), active, d);
     store_dtile(d);
-    for (int idx = tid; idx < 2 * kFBox * 8; idx += NT) {
+    for (int idx = gtid; idx < 2 * kFBox * 8; idx += GT) {
       const int n = idx / (2 * kFBox), r = idx - n * (2 * kFBox);
       if (n >= cnt || slot0 + n >= a.nslot_cap) continue;
       const int route = G.route[u][n];
@@ -409,7 +432,7 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
       __stcg(reinterpret_cast<unsigned short*>(y_g + (int64_t)route * H + j * 2 * kFBox + r),
              __bfloat16_as_ushort(__float2bfloat16_rn(y)));
     }
-    named_bar_sync(1, NT);
+    named_bar_sync(gbar, GT);
   }
   if (tid == 0) FLINT_TL(9);
   pdl_trigger();
@@ -480,12 +503,12 @@ static size_t moe_fused_smem(size_t ring_and_dtile, const MoeFusedArgs& a) {
   return 1024 + ring_and_dtile + (size_t)a.M * xs_stride(a.H) * 2 + region;
 }
 
-template <int NS, int NV>
+template <int NS, int NV, int KG>
 static int launch_fused(int sms, const CUtensorMap& uc, const CUtensorMap& us, const CUtensorMap& dc, const CUtensorMap& ds,
                         const MoeFusedArgs& a, int pdl, void* stream) {
   using L = EngineSmem<kFW, NS, kFBox>;
-  const size_t smem = moe_fused_smem(L::ring_bytes + L::dtile_bytes, a);
-  auto kern = moe_fused_kernel<NS, NV>;
+  const size_t smem = moe_fused_smem(L::ring_bytes + KG * L::dtile_bytes, a);
+  auto kern = moe_fused_kernel<NS, NV, KG>;
   cudaFuncAttributes fa{};
   if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return FLINT_ERR_LAUNCH;
   if (smem + fa.sharedSizeBytes > 227 * 1024) return FLINT_ERR_SHAPE;
@@ -494,7 +517,7 @@ static int launch_fused(int sms, const CUtensorMap& uc, const CUtensorMap& us, c
   set_max_carveout(kern);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(sms);
-  cfg.blockDim = dim3((kFW + 1) * 32);
+  cfg.blockDim = dim3((KG * kFW + 1) * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = static_cast<cudaStream_t>(stream);
   cudaLaunchAttribute at[2];
@@ -564,14 +587,15 @@ static int moe_fused_launch(const void* x, int64_t ldx, const void* res, const v
     const long tpd = H / (2 * kFBox), tmax = (M * topk * tpd + sms - 1) / sms;
     a.nslot_cap = (int)std::min<long>(kMaxRoutes, ((tmax + tpd - 1) / tpd + 1) * 8);
   }
-  // the deepest weight ring that fits beside the rows (more stages in flight per SM: the stream is latency-bound)
+  // two consumer groups (16 consumer warps: the weight stream is consumer-bound with 8) and a 7-stage ring when they
+  // fit beside the rows; else one group and a 4-stage ring
   if (H == 2048) {
-    using L8 = EngineSmem<kFW, 8, kFBox>;
-    if (moe_fused_smem(L8::ring_bytes + L8::dtile_bytes, a) + 12 * 1024 <= 227 * 1024)
-      return launch_fused<8, 8>(sms, uc, us, dc, ds, a, pdl, stream);
-    return launch_fused<4, 8>(sms, uc, us, dc, ds, a, pdl, stream);
+    using L7 = EngineSmem<kFW, 7, kFBox>;
+    if (moe_fused_smem(L7::ring_bytes + 2 * L7::dtile_bytes, a) + 12 * 1024 <= 227 * 1024)
+      return launch_fused<7, 8, 2>(sms, uc, us, dc, ds, a, pdl, stream);
+    return launch_fused<4, 8, 1>(sms, uc, us, dc, ds, a, pdl, stream);
   }
-  return launch_fused<4, 16>(sms, uc, us, dc, ds, a, pdl, stream);
+  return launch_fused<4, 16, 1>(sms, uc, us, dc, ds, a, pdl, stream);
 }
 
 extern "C" int flint_moe_fused(const void* x, int64_t ldx, const void* res, const void* norm_w, float eps, const void* gate_w,
