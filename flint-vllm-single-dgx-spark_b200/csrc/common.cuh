@@ -142,6 +142,14 @@ __device__ __forceinline__ void smem_max_grouped(int* p, float v) {
   if ((int)(threadIdx.x & 31) == __ffs(grp) - 1) atomicMax(p, (int)m);
 }
 
+// smem_max_grouped for callers whose active lanes all name the same word (a norm's row loop): one warp reduction,
+// no lane matching.
+__device__ __forceinline__ void smem_max_warp(int* p, float v) {
+  const unsigned act = __activemask();
+  const unsigned m = __reduce_max_sync(act, __float_as_uint(v));
+  if ((int)(threadIdx.x & 31) == __ffs(act) - 1) atomicMax(p, (int)m);
+}
+
 // Stage `rows` activation rows (src + r*ld, bf16, K columns, 16-byte aligned rows) as f16 into xs (row stride
 // xs_stride(K)) with a per-row power-of-two rescale shift[r].  Called by threads [0, nthreads) of the block (a multiple
 // of 32), which synchronise on named barrier `bar` (0 = __syncthreads when nthreads == blockDim.x).
@@ -416,7 +424,7 @@ __device__ __forceinline__ void norm_stage_f16(const bf16* x, int64_t ldx, const
       mx = fmaxf(mx, fmaxf(fabsf(__low2float(n2)), fabsf(__high2float(n2))));
       pk[j] = *reinterpret_cast<uint32_t*>(&n2);
     }
-    smem_max_grouped(&rmax[m], mx);
+    smem_max_grouped(&rmax[m], mx);   // lanes may span rows here
     *reinterpret_cast<uint4*>(xs + m * xs_stride(H) + xs_perm(k8 * 8)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
   }
   sync();
@@ -522,7 +530,7 @@ __device__ __forceinline__ void norm_xn_stage_f16(const bf16* x, int64_t ldx, co
       reinterpret_cast<uint4*>(xn + m * H)[tid] = nv;
       if (xn_out) reinterpret_cast<uint4*>(xn_out + (int64_t)m * H)[tid] = nv;
       if (res_out) reinterpret_cast<uint4*>(res_out + (int64_t)m * H)[tid] = make_uint4(pr[0], pr[1], pr[2], pr[3]);
-      smem_max_grouped(&rmax[m], mx);
+      smem_max_warp(&rmax[m], mx);
     }
   }
   sync();
@@ -627,7 +635,7 @@ __device__ __forceinline__ void norm_xn_stage_f16_halves(const bf16* x, int64_t 
       reinterpret_cast<uint4*>(xn + m * H)[c] = nv;
       if (xn_out) reinterpret_cast<uint4*>(xn_out + (int64_t)m * H)[c] = nv;
       if (res_out) reinterpret_cast<uint4*>(res_out + (int64_t)m * H)[c] = make_uint4(pr[0], pr[1], pr[2], pr[3]);
-      smem_max_grouped(&rmax[m], mx);
+      smem_max_warp(&rmax[m], mx);
     }
   }
   sync();
@@ -648,6 +656,104 @@ __device__ __forceinline__ void norm_xn_stage_f16_halves(const bf16* x, int64_t 
       }
       *reinterpret_cast<uint4*>(xs + m * xs_stride(H) + xs_perm(c * 8)) = make_uint4(h[0], h[1], h[2], h[3]);
     }
+  }
+  sync();
+}
+
+// 16-byte global -> shared copy that does not wait (L2 only: also right for rows another GPU stored here).
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+               ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// norm_xn_stage_f16_halves with little code: the same arithmetic, bits and outputs, but every loop over the rows
+// is rolled (a kernel that runs this once per launch pays for each new instruction it fetches, so an unrolled
+// 4-row body costs more than the arithmetic).  All rows' x / res chunks are first copied into `scratch` (shared
+// memory, >= 2 M H bf16) with asynchronous copies issued back to back; x + res is recomputed from them where the
+// unrolled form kept it in registers.
+__device__ __forceinline__ void norm_xn_stage_f16_compact(const bf16* x, int64_t ldx, const bf16* res, uint4 wchunk,
+                                                          float eps, int M, int H, bf16* xn, bf16* xn_out,
+                                                          bf16* res_out, __half* xs, int* shift, float* red,
+                                                          int nthreads, int bar, bf16* scratch) {
+  const int tid = threadIdx.x, lane = tid & 31, H8 = H >> 3, half = tid / H8, c = tid - half * H8;
+  const int cw = c >> 5, ncw = H8 >> 5, m0 = 4 * half, m1 = min(M, m0 + 4);
+  auto sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthreads) : "memory"); };
+  int* rmax = reinterpret_cast<int*>(red + ncw * 8);
+  bf16* sx = scratch;                                       // [M][H]
+  bf16* sr = scratch + (size_t)M * H;                       // [M][H]
+#pragma unroll 1
+  for (int m = m0; m < m1; ++m) {
+    cp_async16(reinterpret_cast<uint4*>(sx + m * H) + c, reinterpret_cast<const uint4*>(x + m * ldx) + c);
+    if (res) cp_async16(reinterpret_cast<uint4*>(sr + m * H) + c, reinterpret_cast<const uint4*>(res + m * ldx) + c);
+  }
+  cp_async_wait_all();                                      // each thread reads back only its own chunks
+  auto load_s = [&](int m, float (&a)[8]) {                 // s = x (+ res) in fp32, the unrolled form's sums
+    bf16x8_to_f32(reinterpret_cast<const uint4*>(sx + m * H)[c], a);
+    if (res) {
+      float b[8];
+      bf16x8_to_f32(reinterpret_cast<const uint4*>(sr + m * H)[c], b);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) a[j] += b[j];
+    }
+  };
+#pragma unroll 1
+  for (int m = m0; m < m0 + 4; ++m) {
+    float v = 0.f;
+    if (m < M) {
+      float a[8];
+      load_s(m, a);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v = fmaf(a[j], a[j], v);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[cw * 8 + m] = v;
+  }
+  if (tid < 8) rmax[tid] = 0;
+  sync();
+  float wf[8];
+  bf16x8_to_f32(wchunk, wf);
+#pragma unroll 1
+  for (int m = m0; m < m1; ++m) {
+    float tot = 0.f;
+    for (int ww = 0; ww < ncw; ++ww) tot += red[ww * 8 + m];
+    const float rs = rsqrtf(tot / (float)H + eps);
+    float a[8];
+    load_s(m, a);
+    uint32_t pk[4], pr[4];
+    float mx = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __nv_bfloat162 n2 = __floats2bfloat162_rn(a[2 * j] * rs * wf[2 * j], a[2 * j + 1] * rs * wf[2 * j + 1]);
+      mx = fmaxf(mx, fmaxf(fabsf(__low2float(n2)), fabsf(__high2float(n2))));
+      pk[j] = *reinterpret_cast<uint32_t*>(&n2);
+      __nv_bfloat162 r2 = __floats2bfloat162_rn(a[2 * j], a[2 * j + 1]);
+      pr[j] = *reinterpret_cast<uint32_t*>(&r2);
+    }
+    const uint4 nv = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    reinterpret_cast<uint4*>(xn + m * H)[c] = nv;
+    if (xn_out) reinterpret_cast<uint4*>(xn_out + (int64_t)m * H)[c] = nv;
+    if (res_out) reinterpret_cast<uint4*>(res_out + (int64_t)m * H)[c] = make_uint4(pr[0], pr[1], pr[2], pr[3]);
+    smem_max_warp(&rmax[m], mx);
+  }
+  sync();
+#pragma unroll 1
+  for (int m = m0; m < m1; ++m) {
+    const float mx = __int_as_float(rmax[m]);
+    int s = 0;
+    if (mx > 0.f && !(mx != mx) && mx <= 3.0e38f) s = 14 - ((int)((__float_as_uint(mx) >> 23) & 0xFF) - 127);
+    if (c == 0) shift[m] = s;
+    const uint4 nv = reinterpret_cast<const uint4*>(xn + m * H)[c];
+    const uint32_t pk[4] = {nv.x, nv.y, nv.z, nv.w};
+    uint32_t h[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __half2 v = __floats2half2_rn(scale_pow2(bf16_bits_to_f32(pk[j] & 0xFFFFu), s),
+                                    scale_pow2(bf16_bits_to_f32(pk[j] >> 16), s));
+      h[j] = *reinterpret_cast<uint32_t*>(&v);
+    }
+    *reinterpret_cast<uint4*>(xs + m * xs_stride(H) + xs_perm(c * 8)) = make_uint4(h[0], h[1], h[2], h[3]);
   }
   sync();
 }
@@ -712,7 +818,7 @@ __device__ __forceinline__ void norm_stage_f16_1w(const bf16* x, int64_t ldx, co
         mx = fmaxf(mx, fmaxf(fabsf(__low2float(n2)), fabsf(__high2float(n2))));
         pk[m][j] = *reinterpret_cast<uint32_t*>(&n2);
       }
-      smem_max_grouped(&rmax[m], mx);
+      smem_max_warp(&rmax[m], mx);
     }
   }
   sync();

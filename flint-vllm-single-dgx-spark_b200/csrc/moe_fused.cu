@@ -243,9 +243,10 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap up_c, const __grid_constant
     ldin = 2 * H;
   }
   const bool one_pass = KG > 1 || H / 8 <= NT;
-  if (KG > 1) {
-    norm_xn_stage_f16_halves(xin, ldin, rin, nwc, a.eps, M, H, xnb, blockIdx.x == 0 ? a.xn_out : nullptr,
-                             blockIdx.x == 0 ? a.res_out : nullptr, xs, shift_x, red, NT, 2, a.peer != 0);
+  if (KG > 1) {                             // (the weight ring is free until the plan: the rows' copies go there)
+    norm_xn_stage_f16_compact(xin, ldin, rin, nwc, a.eps, M, H, xnb, blockIdx.x == 0 ? a.xn_out : nullptr,
+                              blockIdx.x == 0 ? a.res_out : nullptr, xs, shift_x, red, NT, 2,
+                              reinterpret_cast<bf16*>(smem));
   } else if (one_pass) {
     norm_xn_stage_f16(xin, ldin, rin, nwc, a.eps, M, H, xnb, blockIdx.x == 0 ? a.xn_out : nullptr,
                       blockIdx.x == 0 ? a.res_out : nullptr, xs, shift_x, red, NT, 2, a.peer != 0);
