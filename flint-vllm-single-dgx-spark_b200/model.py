@@ -221,8 +221,8 @@ class Decoder:
         that stream bit for bit.  exchange (dp=True): "nccl" (all-gather, reduce-scatter), "peer" (both exchanges
         inside the MoE launch over NVLink peer memory, moe_fused_dp_peer, then a receive-and-sum launch) or
         "peer_split" (separate gather and combine launches over peer memory around moe_fused_ep)."""
-        # measured per layer on a B200: one stream, the block; 2..8 streams, the fused launch (35.9 / 38.5 / 45.7 / 47.9
-        # us at 2 / 3 / 4 / 5 against the chain's 39.5 / 47.6 / 61.6 / 71.6; 59.3 at 8).  Sharded: block or chain.
+        # measured per layer on a B200: one stream, the block; 2..8 streams, the fused launch (30.6 / 41.6 / 53.8 us at
+        # 2 / 4 / 8; the chain took 39.5 / 61.6 at 2 / 4).  Sharded: block or chain.
         if dp:
             if model.world < 2 or group is None or batch != 1:
                 raise ValueError("dp=True decodes one stream per GPU of a sharded model and needs its process group")
