@@ -466,7 +466,7 @@ class Decoder:
             seq.append(("moe_fused", lambda: ops.moe_fused(self.a, self.res_a, L["ln2"], c.rms_eps, L["gate"], c.topk,
                                                            ew.score_fn, ew.w13, ew.s13, ew.g13, ew.w2, ew.s2, ew.g2,
                                                            self.h, self.res_b, self.xn, self.lg, self.ti, self.tw,
-                                                           ew.shared is not None)))
+                                                           ew.shared is not None or self.route_trace is not None)))
             if self.route_trace is not None:
                 seq.append(("route_trace", lambda: self._trace_copy(l)))
         else:
