@@ -114,6 +114,29 @@ def unpack_marlin(weight, weight_scale, global_scale):
     return (P[0], S[0], gs[0]) if single else (P, S, gs)
 
 
+def unpack_flashinfer(w1, w1_sf, w2, w2_sf):
+    """The Flint PR's FlashInfer W4A16 expert tensors (the outputs of prepare_weights,
+    vllm/models/flint/ops/moe_cute.py:29-59 / patch:4061-4091: gate/up rows interleaved, scales in the 6-D MMA
+    layout, returned as permuted views) -> ModelOpt (w13 u8 [E, 2I, H/2], s13 [E, 2I, H/16], w2 u8 [E, H, I/2],
+    s2 [E, H, I/16]) for the decode kernels, on the GPU (flint_flashinfer_nvfp4_unpack), bit for bit.  The scales
+    may be given as the PR's 6-D views ([32, 4, m, 4, k, E]) or as their stored arrays ([E, m, k, 32, 4, 4]).  The
+    global scales are not part of that layout and pass through unchanged."""
+    def stored(sf):
+        sf = sf.view(torch.uint8) if sf.dtype != torch.uint8 else sf
+        if sf.dim() == 6 and sf.shape[0] == 32 and sf.shape[1] == 4:         # the PR's logical view
+            sf = sf.permute(5, 2, 4, 0, 1, 3)
+        return sf.contiguous()
+    w1, w2 = w1.view(torch.uint8).contiguous(), w2.view(torch.uint8).contiguous()
+    E, R13, Hh = w1.shape
+    dev = w1.device
+    w13 = torch.empty((E, R13, Hh), dtype=torch.uint8, device=dev)
+    s13 = torch.empty((E, R13, Hh // 8), dtype=torch.uint8, device=dev)
+    w2o = torch.empty_like(w2)
+    s2 = torch.empty((E, w2.shape[1], w2.shape[2] // 8), dtype=torch.uint8, device=dev)
+    torch.ops.flint_b200.flashinfer_nvfp4_unpack(w1, stored(w1_sf), w2, stored(w2_sf), w13, s13, w2o, s2)
+    return w13, s13, w2o, s2
+
+
 class MarlinDecodeWeights(DecodeWeights):
     """The reference's constructor and argument order (fast/fp4moe_decode.py:27-44, called at fast/model.py:277-282):
     the routed experts' six tensors, then the shared expert's gate_up and down as (weight, weight_scale, global

@@ -907,6 +907,35 @@ def _(weight, weight_scale, global_scale, packed, scales, global_out, bad):
     return None
 
 
+@torch.library.custom_op(f"{NS}::flashinfer_nvfp4_unpack", mutates_args=("w13_out", "s13_out", "w2_out", "s2_out"))
+def flashinfer_nvfp4_unpack(w1: torch.Tensor, w1_sf: torch.Tensor, w2: torch.Tensor, w2_sf: torch.Tensor,
+                            w13_out: torch.Tensor, s13_out: torch.Tensor, w2_out: torch.Tensor,
+                            s2_out: torch.Tensor) -> None:
+    """FlashInfer W4A16 NVFP4 experts (w1 u8 [E, 2I, H/2] interleaved, w1_sf stored 6-D [E, 2I/128, H/64, 32, 4, 4],
+    w2 u8 [E, H, I/2], w2_sf [E, H/128, I/64, 32, 4, 4]) -> ModelOpt codes and scale bytes
+    (flint_flashinfer_nvfp4_unpack)."""
+    _lib.require_cuda(w1, "flashinfer_nvfp4_unpack")
+    E, R13, Hh = w1.shape
+    H, I = 2 * Hh, R13 // 2
+    if w1.dtype != torch.uint8 or w2.dtype != torch.uint8 or tuple(w2.shape) != (E, H, I // 2) or \
+            w1_sf.numel() != E * R13 * (H // 16) or w2_sf.numel() != E * H * (I // 16) or \
+            tuple(w13_out.shape) != (E, R13, Hh) or tuple(s13_out.shape) != (E, R13, H // 16) or \
+            tuple(w2_out.shape) != (E, H, I // 2) or tuple(s2_out.shape) != (E, H, I // 16):
+        raise _lib.FlintError("flashinfer_nvfp4_unpack: shapes do not match w1 [E, 2I, H/2]")
+    for t in (w1, w1_sf, w2, w2_sf, w13_out, s13_out, w2_out, s2_out):
+        if not t.is_contiguous():
+            raise _lib.FlintError("flashinfer_nvfp4_unpack: tensors must be contiguous (scales in their stored order)")
+    rc = lib().flint_flashinfer_nvfp4_unpack(ptr(w1), ptr(_u8(w1_sf)), ptr(w2), ptr(_u8(w2_sf)), E, H, I,
+                                             ptr(w13_out), ptr(s13_out), ptr(w2_out), ptr(s2_out), 0,
+                                             stream_ptr(w1.device))
+    check(rc, "flint_flashinfer_nvfp4_unpack")
+
+
+@flashinfer_nvfp4_unpack.register_fake
+def _(w1, w1_sf, w2, w2_sf, w13_out, s13_out, w2_out, s2_out):
+    return None
+
+
 @torch.library.custom_op(f"{NS}::nvfp4_dequant", mutates_args=("out",))
 def nvfp4_dequant(P: torch.Tensor, S: torch.Tensor, global_scale: torch.Tensor | None, out: torch.Tensor) -> None:
     """out [..., K] (fp32 or bf16) = e2m1(P) * e4m3(S) (* global_scale, one fp32 scalar on the device)."""

@@ -471,6 +471,17 @@ int flint_marlin_nvfp4_unpack(const void* weight, const void* weight_scale, cons
                               int64_t N, int64_t K, void* packed, void* scales, float* global_out, int32_t* bad, int pdl,
                               void* stream);
 
+/* FlashInfer W4A16 NVFP4 expert tensors (what the Flint PR's prepare_weights makes for its grouped MoE,
+ * vllm/models/flint/ops/moe_cute.py, patch:4061-4091) -> the ModelOpt layout of every kernel above.
+ * w1 u8 [E][2I][H/2] (gate/up rows interleaved: per 128-row block, 64 up rows then 64 gate rows), w1_sf the stored
+ * (contiguous) block scales of those rows [E][2I/128][H/64][32][4][4], w2 u8 [E][H][I/2], w2_sf [E][H/128][I/64][32]
+ * [4][4] (the PR returns the scales as permuted views of these arrays).  Writes w13_out [E][2I][H/2] ([gate; up]),
+ * s13_out [E][2I][H/16], w2_out [E][H][I/2], s2_out [E][H][I/16]: byte moves only, bit-exact.  H % 128 == 0,
+ * I % 64 == 0; code arrays 16-byte aligned. */
+int flint_flashinfer_nvfp4_unpack(const void* w1, const void* w1_sf, const void* w2, const void* w2_sf, int64_t E,
+                                  int64_t H, int64_t I, void* w13_out, void* s13_out, void* w2_out, void* s2_out,
+                                  int pdl, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
