@@ -637,7 +637,7 @@ extern "C" int flint_moe_block_ep(const void* x, int64_t ldx, const void* res, c
 extern "C" int flint_moe_combine(const void* y, const float* topk_weights, int64_t M, int64_t topk, int64_t H, void* out,
                                  int pdl, void* stream) {
   if (!y || !topk_weights || !out) return FLINT_ERR_ARGUMENT;
-  if (M < 1 || M > 8 || topk < 1 || topk > kXMaxSlots || H < 1 || H > (1 << 20)) return FLINT_ERR_SHAPE;
+  if (M < 1 || M > 65535 || topk < 1 || topk > kXMaxSlots || H < 1 || H > (1 << 20)) return FLINT_ERR_SHAPE;
   return launch(moe_combine_kernel, dim3((unsigned)((H + 255) / 256), (unsigned)M), dim3(256), 0, stream, pdl,
                 (const bf16*)y, topk_weights, (int)topk, (int)H, (bf16*)out);
 }

@@ -1,0 +1,244 @@
+// Prefill-side grouped MoE (replaces the Flint PR's FlashInfer grouped GEMMs for prompts, grouped_moe at
+// patch:4093-4212): the routes of a prompt, grouped by expert in blocks of 64 by the deterministic align
+// (flint_moe_align), run through the NVFP4 gate/up + SwiGLU and down projections with each decoded weight fragment
+// reused across the block's 64 routes (8 mma.sync n-groups per decoded A fragment; the decode kernels use it for
+// at most 8 tokens).
+//
+//   flint_rows_to_f16      any bf16 rows -> f16 rows scaled by the decode kernels' per-row power of two (exact)
+//   flint_moe_grouped_up   act[route] = bf16(silu(g) * u), g / u = (xh[token] . W13[e] rows) * g13[e] * 2^-shift
+//   flint_moe_grouped_down y[route]   = bf16((ah[route] . W2[e] rows) * g2[e] * 2^-shift)
+// then flint_moe_combine over the prompt's tokens gives out[t] = bf16(sum_s tw[t][s] y[t topk + s]) in slot order.
+//
+// CTA = (align block of 64 routes, 128 weight rows: 64 gate + 64 up rows of one 64-column slice of the
+// intermediate, or 128 down rows); 8 warps, each 16 weight rows x 64 routes.  K goes in stages of 256: the
+// stage's codes (128 B per row, 16-byte units swizzled by row as the decode kernels' TMA boxes are), scales and the
+// 64 routes' f16 activations are copied to shared memory, then each warp decodes its A fragments once per 16 k and
+// issues one m16n8k16 MMA per group of 8 routes.  Products are exact in f16 (e2m1 x e4m3 x the rescaled activation),
+// sums fp32 with one chain per route group, so results match the decode kernels within fp32 summation order.
+#include "common.cuh"
+#include "nvfp4_tile.cuh"
+#include "runtime.cuh"
+
+namespace flint {
+
+constexpr int kGB = 64;                     // routes per align block
+constexpr int kGW = 8;                      // warps
+constexpr int kGT = kGW * 32;
+constexpr int kGRows = kGW * 16;            // weight rows per CTA
+constexpr int kGXS = kSliceK + 8;           // f16 stride of a staged activation row (256 k)
+constexpr int kGSmem = kGRows * 128 + kGRows * 16 + kGB * kGXS * 2;   // codes + scales + activations (the
+                                                                      // activation region also takes the fp32
+                                                                      // results [128][64] at the end)
+static_assert(kGB * kGXS * 2 >= kGRows * kGB * 4, "result tile must fit over the activations");
+
+// one CTA per row: f16(x * 2^s), s from the row's largest |x| (the decode kernels' staging rule), unpermuted
+__global__ void __launch_bounds__(256) rows_to_f16_kernel(const bf16* __restrict__ src, int64_t ld, int K,
+                                                          __half* __restrict__ dst, int* __restrict__ shift) {
+  __shared__ float red[8];
+  pdl_wait();
+  const int r = blockIdx.x, tid = threadIdx.x;
+  const bf16* row = src + (int64_t)r * ld;
+  float mx = 0.f;
+  for (int k = tid; k < K; k += 256) mx = fmaxf(mx, fabsf(__bfloat162float(row[k])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((tid & 31) == 0) red[tid >> 5] = mx;
+  __syncthreads();
+  mx = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red[w]);
+  int s = 0;
+  if (mx > 0.f && !(mx != mx) && mx <= 3.0e38f) s = 14 - ((int)((__float_as_uint(mx) >> 23) & 0xFF) - 127);
+  if (tid == 0) shift[r] = s;
+  for (int k = tid; k < K; k += 256) dst[(int64_t)r * K + k] = __float2half_rn(scale_pow2(__bfloat162float(row[k]), s));
+  pdl_trigger();
+}
+
+struct GroupedArgs {
+  const __half* xh;          // f16 rows: the tokens [T][K] (up) or the routes [R][K] (down)
+  const int* shift;          // per row of xh
+  const int* sorted_ids;     // align: routes grouped by expert, blocks of 64, padding = numel
+  const int* expert_ids;     // align: expert of each block
+  const int* ntp;            // align: num_tokens_post_pad (device)
+  int numel, topk, E;
+  const uint8_t* W;          // codes [E][N][K/2]
+  const uint8_t* S;          // E4M3 scales [E][N][K/16]
+  const float* g;            // global scale [E]
+  int K, N, I;               // N = 2I (up) or H (down)
+  bf16* out;                 // act [R][I] (up) or y [R][H] (down)
+  int ldo;
+  unsigned* status;
+};
+
+template <bool UP>
+__global__ void __launch_bounds__(kGT) moe_grouped_kernel(const GroupedArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  uint8_t* codes = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* scales = codes + kGRows * 128;
+  __half* xa = reinterpret_cast<__half*>(scales + kGRows * 16);
+  float* res = reinterpret_cast<float*>(xa);                      // [128 rows][64 routes] after the last stage
+  __shared__ int s_route[kGB], s_row[kGB];
+
+  pdl_wait();
+  const int blk = blockIdx.x, tile = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (blk * kGB >= __ldg(a.ntp)) return;                            // past the padded routes
+  const int e = a.expert_ids[blk];
+  if (e < 0 || e >= a.E) {
+    if (tid == 0) atomicOr(a.status, 2u);
+    return;
+  }
+  if (tid < kGB) {
+    const int route = a.sorted_ids[blk * kGB + tid];
+    const bool ok = route >= 0 && route < a.numel;
+    s_route[tid] = ok ? route : -1;
+    s_row[tid] = ok ? (UP ? route / a.topk : route) : -1;
+  }
+  // weight row of CTA row r: up -- gate rows tile*64 + r (r < 64), up rows I + tile*64 + r - 64; down -- tile*128 + r
+  auto wrow = [&](int r) {
+    return UP ? (r < 64 ? tile * 64 + r : a.I + tile * 64 + (r - 64)) : tile * kGRows + r;
+  };
+  const int g = lane >> 2, t = lane & 3;
+  const int pr0 = 16 * warp + tile_phi(g), pr1 = pr0 + 8, key = pr0 & 7;
+  float acc[8][4];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[j][i] = 0.f;
+  const int nks = a.K / kSliceK, cb = a.K / 2, sb = a.K / 16;
+  const uint8_t* We = a.W + (int64_t)e * a.N * cb;
+  const uint8_t* Se = a.S + (int64_t)e * a.N * sb;
+
+#pragma unroll 1
+  for (int ks = 0; ks < nks; ++ks) {
+    __syncthreads();                                                // the previous stage is consumed
+    for (int i = tid; i < kGRows * 8; i += kGT) {                   // codes: 128 rows x 8 units of 16 B
+      const int r = i >> 3, u = i & 7;
+      *reinterpret_cast<uint4*>(codes + r * 128 + ((u ^ (r & 7)) << 4)) =
+          *reinterpret_cast<const uint4*>(We + (int64_t)wrow(r) * cb + ks * 128 + u * 16);
+    }
+    for (int r = tid; r < kGRows; r += kGT)                         // scales: 16 B per row
+      *reinterpret_cast<uint4*>(scales + r * 16) = *reinterpret_cast<const uint4*>(Se + (int64_t)wrow(r) * sb + ks * 16);
+    for (int i = tid; i < kGB * 32; i += kGT) {                     // activations: 64 rows x 32 units of 8 halves
+      const int rr = i >> 5, u = i & 31, row = s_row[rr];
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (row >= 0) v = *reinterpret_cast<const uint4*>(a.xh + (int64_t)row * a.K + ks * kSliceK + u * 8);
+      *reinterpret_cast<uint4*>(xa + rr * kGXS + xs_perm(u * 8)) = v;
+    }
+    __syncthreads();
+#pragma unroll 1
+    for (int c = 0; c < 2; ++c) {
+      const int phys = (4 * c + t) ^ key;
+      const uint4 qg = lds128(codes + pr0 * 128 + phys * 16);
+      const uint4 qg8 = lds128(codes + pr1 * 128 + phys * 16);
+      const uint32_t s2 = lds_u16(scales + pr0 * 16 + 8 * c + 2 * t) | (lds_u16(scales + pr1 * 16 + 8 * c + 2 * t) << 16);
+      const uint32_t sc_g = e4m3x2_to_f16x2(s2 & 0xFFFFu), sc_g8 = e4m3x2_to_f16x2(s2 >> 16);
+      const uint32_t wg[4] = {qg.x, qg.y, qg.z, qg.w}, wg8[4] = {qg8.x, qg8.y, qg8.z, qg8.w};
+      const int qswz = (t >> 1) << 1;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t dg[4], dg8[4];
+        e2m1x8_to_f16x2(wg[q], dg);
+        e2m1x8_to_f16x2(wg8[q], dg8);
+        const uint32_t s_g = q < 2 ? bcast_lo(sc_g) : bcast_hi(sc_g), s_g8 = q < 2 ? bcast_lo(sc_g8) : bcast_hi(sc_g8);
+        const uint32_t a0[4] = {hmul2(dg[0], s_g), hmul2(dg8[0], s_g8), hmul2(dg[1], s_g), hmul2(dg8[1], s_g8)};
+        const uint32_t a1[4] = {hmul2(dg[2], s_g), hmul2(dg8[2], s_g8), hmul2(dg[3], s_g), hmul2(dg8[3], s_g8)};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {                               // route group j: routes 8 j .. 8 j + 7
+          const uint4 b = lds128(xa + (8 * j + g) * kGXS + c * 128 + 32 * t + 8 * (q ^ qswz));
+          mma_f16(acc[j], a0, b.x, b.y);
+          mma_f16(acc[j], a1, b.z, b.w);
+        }
+      }
+    }
+  }
+  __syncthreads();                                                  // results go over the activations
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    res[pr0 * kGB + 8 * j + 2 * t] = acc[j][0];
+    res[pr0 * kGB + 8 * j + 2 * t + 1] = acc[j][1];
+    res[pr1 * kGB + 8 * j + 2 * t] = acc[j][2];
+    res[pr1 * kGB + 8 * j + 2 * t + 1] = acc[j][3];
+  }
+  __syncthreads();
+  const float ge = a.g[e];
+  if (UP) {
+    for (int idx = tid; idx < 64 * kGB; idx += kGT) {               // 64 columns x 64 routes
+      const int i = idx / 64, col = idx - i * 64, route = s_route[i];
+      if (route < 0) continue;
+      const float sc = ldexpf(ge, -a.shift[s_row[i]]);
+      const float gv = res[col * kGB + i] * sc, uv = res[(64 + col) * kGB + i] * sc;
+      const float silu = gv / (1.0f + expf(-gv));
+      a.out[(int64_t)route * a.ldo + tile * 64 + col] = __float2bfloat16_rn(silu * uv);
+    }
+  } else {
+    for (int idx = tid; idx < kGRows * kGB; idx += kGT) {           // 128 rows x 64 routes
+      const int i = idx / kGRows, r = idx - i * kGRows, route = s_route[i];
+      if (route < 0) continue;
+      a.out[(int64_t)route * a.ldo + tile * kGRows + r] =
+          __float2bfloat16_rn(res[r * kGB + i] * ldexpf(ge, -a.shift[route]));
+    }
+  }
+  pdl_trigger();
+}
+
+template <bool UP>
+static int grouped_launch(const GroupedArgs& a, int max_blocks, int tiles, int pdl, void* stream) {
+  auto kern = moe_grouped_kernel<UP>;
+  const int smem = kGSmem + 1024;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return FLINT_ERR_LAUNCH;
+  return launch(kern, dim3((unsigned)max_blocks, (unsigned)tiles), dim3(kGT), smem, stream, pdl, a);
+}
+
+}  // namespace flint
+
+using namespace flint;
+
+extern "C" int flint_rows_to_f16(const void* src, int64_t ld, int64_t rows, int64_t K, void* dst, int32_t* shift,
+                                 int pdl, void* stream) {
+  if (!src || !dst || !shift) return FLINT_ERR_ARGUMENT;
+  if (rows < 1 || rows > (1 << 30) || K < 1 || ld < K) return FLINT_ERR_SHAPE;
+  return launch(rows_to_f16_kernel, dim3((unsigned)rows), dim3(256), 0, stream, pdl, (const bf16*)src, ld, (int)K,
+                (__half*)dst, (int*)shift);
+}
+
+static int grouped_entry(bool up, const void* xh, const int32_t* shift, const int32_t* sorted_ids,
+                         const int32_t* expert_ids, const int32_t* num_tokens_post_pad, int64_t numel, int64_t topk,
+                         int64_t E, const void* W, const void* S, const float* g, int64_t H, int64_t I,
+                         int64_t max_blocks, void* out, void* workspace, int pdl, void* stream) {
+  if (!xh || !shift || !sorted_ids || !expert_ids || !num_tokens_post_pad || !W || !S || !g || !out || !workspace)
+    return FLINT_ERR_ARGUMENT;
+  if (numel < 1 || topk < 1 || topk > 32 || E < 1 || max_blocks < 1 || max_blocks > 65535 || H < kSliceK ||
+      H % kSliceK != 0 || I < kSliceK || I % kSliceK != 0)
+    return FLINT_ERR_SHAPE;
+  if (!aligned(xh, 16) || !aligned(W, 16) || !aligned(S, 16) || !aligned(workspace, 4)) return FLINT_ERR_ALIGN;
+  GroupedArgs a;
+  a.xh = (const __half*)xh; a.shift = shift; a.sorted_ids = sorted_ids; a.expert_ids = expert_ids;
+  a.ntp = num_tokens_post_pad; a.numel = (int)numel; a.topk = (int)topk; a.E = (int)E;
+  a.W = (const uint8_t*)W; a.S = (const uint8_t*)S; a.g = g; a.I = (int)I; a.out = (bf16*)out;
+  a.status = (unsigned*)workspace;
+  if (up) {
+    a.K = (int)H; a.N = (int)(2 * I); a.ldo = (int)I;
+    return grouped_launch<true>(a, (int)max_blocks, (int)(I / 64), pdl, stream);
+  }
+  a.K = (int)I; a.N = (int)H; a.ldo = (int)H;
+  return grouped_launch<false>(a, (int)max_blocks, (int)(H / kGRows), pdl, stream);
+}
+
+extern "C" int flint_moe_grouped_up(const void* xh, const int32_t* shift, const int32_t* sorted_ids,
+                                    const int32_t* expert_ids, const int32_t* num_tokens_post_pad, int64_t numel,
+                                    int64_t topk, int64_t E, const void* w13, const void* s13, const float* g13,
+                                    int64_t H, int64_t I, int64_t max_blocks, void* act, void* workspace, int pdl,
+                                    void* stream) {
+  return grouped_entry(true, xh, shift, sorted_ids, expert_ids, num_tokens_post_pad, numel, topk, E, w13, s13, g13,
+                       H, I, max_blocks, act, workspace, pdl, stream);
+}
+
+extern "C" int flint_moe_grouped_down(const void* ah, const int32_t* shift, const int32_t* sorted_ids,
+                                      const int32_t* expert_ids, const int32_t* num_tokens_post_pad, int64_t numel,
+                                      int64_t topk, int64_t E, const void* w2, const void* s2, const float* g2,
+                                      int64_t H, int64_t I, int64_t max_blocks, void* y, void* workspace, int pdl,
+                                      void* stream) {
+  return grouped_entry(false, ah, shift, sorted_ids, expert_ids, num_tokens_post_pad, numel, topk, E, w2, s2, g2, H,
+                       I, max_blocks, y, workspace, pdl, stream);
+}

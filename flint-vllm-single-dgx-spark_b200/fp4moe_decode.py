@@ -114,6 +114,39 @@ def unpack_marlin(weight, weight_scale, global_scale):
     return (P[0], S[0], gs[0]) if single else (P, S, gs)
 
 
+def grouped_moe(x, topk_ids, topk_weights, w: "DecodeWeights", block_size: int = 64):
+    """Prefill MoE of a prompt (the Flint PR's grouped_moe, patch:4093-4212, runs FlashInfer's grouped GEMMs; this
+    runs the library's NVFP4 tiles): x bf16 [T, H] (normalised), topk_ids [T, topk], topk_weights fp32 [T, topk] ->
+    out bf16 [T, H] = bf16(sum_s tw[t, s] * y[t, s]) in slot order, y the routed expert's output row.  The routes are
+    grouped by expert with the deterministic align (blocks of 64), each decoded weight fragment serves a block's 64
+    routes; gate/up, SwiGLU and down keep the decode kernels' rounding points (fp32 sums in another order).  The
+    routed experts only (a shared expert or dense layer is added by the caller, as for the decode path)."""
+    from .patch_align import align_sizes
+    ops = torch.ops.flint_b200
+    T, H = x.shape
+    k = topk_ids.shape[-1]
+    numel = T * k
+    dev = x.device
+    n_sorted, n_blocks = align_sizes(numel, w.E, block_size, pad_sorted_ids=True)
+    sorted_ids = torch.empty((n_sorted,), dtype=torch.int32, device=dev)
+    expert_ids = torch.empty((n_blocks,), dtype=torch.int32, device=dev)
+    ntp = torch.empty((1,), dtype=torch.int32, device=dev)
+    ops.moe_align(topk_ids.reshape(-1), w.E, block_size, sorted_ids, expert_ids, ntp)
+    xh = torch.empty((T, H), dtype=torch.float16, device=dev)
+    sx = torch.empty((T,), dtype=torch.int32, device=dev)
+    ops.rows_to_f16(x, xh, sx)
+    act = torch.empty((numel, w.I), dtype=torch.bfloat16, device=dev)
+    ops.moe_grouped_up(xh, sx, sorted_ids, expert_ids, ntp, numel, k, w.w13, w.s13, w.g13, act)
+    ah = torch.empty((numel, w.I), dtype=torch.float16, device=dev)
+    sa = torch.empty((numel,), dtype=torch.int32, device=dev)
+    ops.rows_to_f16(act, ah, sa)
+    y = torch.empty((numel, H), dtype=torch.bfloat16, device=dev)
+    ops.moe_grouped_down(ah, sa, sorted_ids, expert_ids, ntp, numel, k, w.w2, w.s2, w.g2, y)
+    out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    ops.moe_combine(y, topk_weights.float().contiguous(), out)
+    return out
+
+
 def unpack_flashinfer(w1, w1_sf, w2, w2_sf):
     """The Flint PR's FlashInfer W4A16 expert tensors (the outputs of prepare_weights,
     vllm/models/flint/ops/moe_cute.py:29-59 / patch:4061-4091: gate/up rows interleaved, scales in the 6-D MMA

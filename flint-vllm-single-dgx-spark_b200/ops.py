@@ -936,6 +936,69 @@ def _(w1, w1_sf, w2, w2_sf, w13_out, s13_out, w2_out, s2_out):
     return None
 
 
+@torch.library.custom_op(f"{NS}::rows_to_f16", mutates_args=("dst", "shift"))
+def rows_to_f16(src: torch.Tensor, dst: torch.Tensor, shift: torch.Tensor) -> None:
+    """bf16 rows [n, K] -> f16 rows x * 2^shift[row] with the decode kernels' per-row power of two
+    (flint_rows_to_f16)."""
+    _lib.require_cuda(src, "rows_to_f16")
+    _bf16_2d(src, "rows_to_f16 src")
+    n, K = src.shape
+    if dst.dtype != torch.float16 or tuple(dst.shape) != (n, K) or not dst.is_contiguous() or shift.numel() != n:
+        raise _lib.FlintError("rows_to_f16: dst f16 [n, K] contiguous, shift int32 [n]")
+    rc = lib().flint_rows_to_f16(ptr(src), src.stride(0), n, K, ptr(dst), ptr(shift), PDL, stream_ptr(src.device))
+    check(rc, "flint_rows_to_f16")
+
+
+@rows_to_f16.register_fake
+def _(src, dst, shift):
+    return None
+
+
+def _grouped(fn: str, xh, shift, sorted_ids, expert_ids, ntp, numel, topk, w, s, g, H, I, out):
+    _lib.require_cuda(xh, fn)
+    ws = _lib.workspace(xh.device, "moe_grouped_status", 4)
+    rc = getattr(lib(), f"flint_{fn}")(ptr(xh), ptr(shift), ptr(sorted_ids), ptr(expert_ids), ptr(ntp), int(numel),
+                                       int(topk), w.shape[0], ptr(_u8(w)), ptr(_u8(s)), ptr(g), int(H), int(I),
+                                       expert_ids.numel(), ptr(out), ptr(ws), PDL, stream_ptr(xh.device))
+    check(rc, f"flint_{fn}")
+
+
+@torch.library.custom_op(f"{NS}::moe_grouped_up", mutates_args=("act",))
+def moe_grouped_up(xh: torch.Tensor, shift: torch.Tensor, sorted_ids: torch.Tensor, expert_ids: torch.Tensor,
+                   num_tokens_post_pad: torch.Tensor, numel: int, topk: int, w13: torch.Tensor, s13: torch.Tensor,
+                   g13: torch.Tensor, act: torch.Tensor) -> None:
+    """Prefill gate/up + SwiGLU of the aligned routes (flint_moe_grouped_up): act bf16 [numel, I] per route."""
+    H = xh.shape[1]
+    I = w13.shape[1] // 2
+    if act.shape != (numel, I) or w13.shape[2] * 2 != H:
+        raise _lib.FlintError("moe_grouped_up: act [numel, I], w13 [E, 2I, H/2]")
+    _grouped("moe_grouped_up", xh, shift, sorted_ids, expert_ids, num_tokens_post_pad, numel, topk, w13, s13, g13, H,
+             I, act)
+
+
+@moe_grouped_up.register_fake
+def _(xh, shift, sorted_ids, expert_ids, num_tokens_post_pad, numel, topk, w13, s13, g13, act):
+    return None
+
+
+@torch.library.custom_op(f"{NS}::moe_grouped_down", mutates_args=("y",))
+def moe_grouped_down(ah: torch.Tensor, shift: torch.Tensor, sorted_ids: torch.Tensor, expert_ids: torch.Tensor,
+                     num_tokens_post_pad: torch.Tensor, numel: int, topk: int, w2: torch.Tensor, s2: torch.Tensor,
+                     g2: torch.Tensor, y: torch.Tensor) -> None:
+    """Prefill down projection of the aligned routes (flint_moe_grouped_down): y bf16 [numel, H] per route."""
+    I = ah.shape[1]
+    H = w2.shape[1]
+    if y.shape != (numel, H) or w2.shape[2] * 2 != I:
+        raise _lib.FlintError("moe_grouped_down: y [numel, H], w2 [E, H, I/2]")
+    _grouped("moe_grouped_down", ah, shift, sorted_ids, expert_ids, num_tokens_post_pad, numel, topk, w2, s2, g2, H, I,
+             y)
+
+
+@moe_grouped_down.register_fake
+def _(ah, shift, sorted_ids, expert_ids, num_tokens_post_pad, numel, topk, w2, s2, g2, y):
+    return None
+
+
 @torch.library.custom_op(f"{NS}::nvfp4_dequant", mutates_args=("out",))
 def nvfp4_dequant(P: torch.Tensor, S: torch.Tensor, global_scale: torch.Tensor | None, out: torch.Tensor) -> None:
     """out [..., K] (fp32 or bf16) = e2m1(P) * e4m3(S) (* global_scale, one fp32 scalar on the device)."""

@@ -482,6 +482,28 @@ int flint_flashinfer_nvfp4_unpack(const void* w1, const void* w1_sf, const void*
                                   int64_t H, int64_t I, void* w13_out, void* s13_out, void* w2_out, void* s2_out,
                                   int pdl, void* stream);
 
+/* Prefill-side grouped MoE (the Flint PR runs prompts through FlashInfer's grouped GEMMs, grouped_moe at
+ * patch:4093-4212; here with this library's NVFP4 tiles).  With the deterministic align of the prompt's routes
+ * (flint_moe_align, block size 64: sorted_ids [max_blocks * 64], expert_ids [max_blocks], num_tokens_post_pad [1]):
+ *   flint_rows_to_f16: rows bf16 [rows][ld >= K] -> dst f16 [rows][K] = x * 2^shift[row] (the per-row power of two of
+ *     the decode kernels, exact);
+ *   flint_moe_grouped_up: xh = the tokens' f16 rows [T][H] (and their shifts) -> act bf16 [numel][I] per route
+ *     (route = token * topk + slot): bf16(silu(g) * u) of the route's expert, g / u in fp32 (as flint_moe_up);
+ *   flint_moe_grouped_down: ah = the routes' f16 act rows [numel][I] -> y bf16 [numel][H] per route (as
+ *     flint_moe_down's per-route rows);
+ * then flint_moe_combine(y, topk_weights, T, topk, H, out) for the slot-order weighted sum.  Weights in the ModelOpt
+ * layout of the other MoE entry points; H and I multiples of 256; workspace: one status word (4 bytes, zeroed). */
+int flint_rows_to_f16(const void* src, int64_t ld, int64_t rows, int64_t K, void* dst, int32_t* shift, int pdl,
+                      void* stream);
+int flint_moe_grouped_up(const void* xh, const int32_t* shift, const int32_t* sorted_ids, const int32_t* expert_ids,
+                         const int32_t* num_tokens_post_pad, int64_t numel, int64_t topk, int64_t E, const void* w13,
+                         const void* s13, const float* g13, int64_t H, int64_t I, int64_t max_blocks, void* act,
+                         void* workspace, int pdl, void* stream);
+int flint_moe_grouped_down(const void* ah, const int32_t* shift, const int32_t* sorted_ids, const int32_t* expert_ids,
+                           const int32_t* num_tokens_post_pad, int64_t numel, int64_t topk, int64_t E, const void* w2,
+                           const void* s2, const float* g2, int64_t H, int64_t I, int64_t max_blocks, void* y,
+                           void* workspace, int pdl, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

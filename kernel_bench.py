@@ -117,12 +117,15 @@ def main(argv=None):
                          "expert 1024: moe_block_shared)")
     ap.add_argument("--rows", type=int, default=151552)
     ap.add_argument("--cols", type=int, default=2048)
+    ap.add_argument("--tokens", type=int, default=6057, help="grouped_moe: prompt tokens")
     ap.add_argument("--lib", default=None, help="load this build of libflint_b200.so (e.g. an instrumented one)")
     ap.add_argument("--timeline", action="store_true", help="print the kernel's phase stamps (instrumented build)")
     args = ap.parse_args(argv)
     _package(args.lib)
     if args.kernel in ("gguf_repack", "nvfp4_dequant"):
         return time_format_kernel(args)
+    if args.kernel == "grouped_moe":
+        return time_grouped_moe(args)
     from flint_b200.model import Decoder, FlintConfig, FlintModel
 
     cfg = FlintConfig(layers=args.layers) if args.config == "baseline" else FlintConfig.flint(layers=args.layers)
@@ -177,6 +180,44 @@ def time_kernel(name, args, dec, model, cfg, dev):
         torch.cuda.synchronize()
         print_timeline(name)
     del g
+
+
+def time_grouped_moe(args):
+    """The prefill MoE of one layer (BASELINE shapes: 128 experts top-8, I 768, hidden 2048; random NVFP4 codes and
+    random routing) for a --tokens prompt: fp4moe_decode.grouped_moe (align, staging, grouped gate/up, grouped down,
+    combine) against the decode kernels on 8-token chunks (moe_up + moe_down), CUDA events around --reps calls."""
+    from flint_b200 import fp4moe_decode as fm
+    dev = torch.device("cuda", torch.cuda.current_device())
+    T, H, E, k, I = args.tokens, 2048, 128, 8, 768
+    g = torch.Generator(device=dev).manual_seed(11)
+    rnd = lambda shape, hi: torch.randint(0, hi, shape, dtype=torch.uint8, device=dev, generator=g)
+    w = fm.DecodeWeights(rnd((E, 2 * I, H // 2), 256), rnd((E, 2 * I, H // 16), 0x30) + 0x28,
+                         torch.full((E,), 0.004, device=dev), rnd((E, H, I // 2), 256),
+                         rnd((E, H, I // 16), 0x30) + 0x28, torch.full((E,), 0.004, device=dev), topk=k,
+                         score="softmax")
+    x = (torch.randn((T, H), device=dev, generator=g) * 0.5).to(torch.bfloat16)
+    ids = torch.argsort(torch.rand((T, E), device=dev, generator=g), dim=1)[:, :k].to(torch.int32).contiguous()
+    tw = torch.softmax(torch.rand((T, k), device=dev, generator=g), dim=1).contiguous()
+
+    def chunks():
+        for t0 in range(0, T, 8):
+            a, _ = fm.moe_up(x[t0:t0 + 8], ids[t0:t0 + 8], w)
+            fm.moe_down(a, None, ids[t0:t0 + 8], tw[t0:t0 + 8], w)
+
+    res = {}
+    for name, fn in (("grouped_moe", lambda: fm.grouped_moe(x, ids, tw, w)), ("decode_kernels_8_token_chunks", chunks)):
+        fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        res[name] = round(e0.elapsed_time(e1) / args.reps, 3)
+    wbytes = E * (2 * I * H + H * I) * 9 // 16
+    print(json.dumps({"kernel": "grouped_moe", "tokens": T, "experts": E, "topk": k, "ms_per_layer": res,
+                      "expert_weight_bytes": wbytes}), flush=True)
 
 
 def time_format_kernel(args):
