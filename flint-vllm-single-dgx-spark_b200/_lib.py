@@ -66,8 +66,8 @@ SIGNATURES: dict[str, tuple] = {
     "flint_dp_combine_peer": (I32, [P, P, P, I64, I64, I64, P, I32, I32, P, I32, P]),
     "flint_flashinfer_nvfp4_unpack": (I32, [P, P, P, P, I64, I64, I64, P, P, P, P, I32, P]),
     "flint_rows_to_f16": (I32, [P, I64, I64, I64, P, P, I32, P]),
-    "flint_moe_grouped_up": (I32, [P, P, P, P, P, I64, I64, I64, P, P, P, I64, I64, I64, P, P, I32, P]),
-    "flint_moe_grouped_down": (I32, [P, P, P, P, P, I64, I64, I64, P, P, P, I64, I64, I64, P, P, I32, P]),
+    "flint_moe_grouped_up": (I32, [P, P, P, P, P, I64, I64, I64, P, P, P, I64, I64, I64, P, P, I32, I32, P]),
+    "flint_moe_grouped_down": (I32, [P, P, P, P, P, I64, I64, I64, P, P, P, I64, I64, I64, P, P, I32, I32, P]),
     "flint_moe_fused_dp_peer": (I32, [P, P, F32, P, I64, I64, I64, I32, P, P, P, P, P, P, I64, I64, I64, P, I32, I32, P,
                                       P, P, P, P, I32, P]),
     "flint_lm_head_nv4_shard": (I32, [P, I64, P, P, F32, I64, P, P, F32, I64, I64, I64, P, P, I32, P]),

@@ -181,10 +181,173 @@ __global__ void __launch_bounds__(kGT) moe_grouped_kernel(const GroupedArgs a) {
   pdl_trigger();
 }
 
+// ---- the same tile on the 5th-generation tensor cores (tcgen05, one CTA, accumulator in tensor memory) ----
+// Per K stage of 256 the warps decode the 128 weight rows into f16 in shared memory and copy the 64 routes' f16 rows
+// next to them, both in the K-major no-swizzle canonical layout of the MMA (8-row x 16-byte core matrices: row group
+// i at i * 4096 B, 16-k step s at s * 256 B, k half j at j * 128 B); one thread then issues the stage's 16
+// tcgen05.mma kind::f16 (M = 128 weight rows, N = 64 routes, K = 16) into a 128 x 64 fp32 accumulator in tensor
+// memory and commits them to an mbarrier that frees the stage.  The epilogue reads the accumulator with
+// tcgen05.ld (warp w: lanes 32 (w % 4) .., columns 32 (w / 4) ..).  Each product is exact; the tensor core's fp32
+// sums run in their own order (within the activation tolerance of the mma.sync tile and of the oracle).
+constexpr int kTcA = kGRows * kSliceK * 2;          // 64 KB decoded weights
+constexpr int kTcB = kGB * kSliceK * 2;             // 32 KB activations
+constexpr int kTcSmem = kGRows * 128 + kGRows * 16 + kTcA + kTcB;
+static_assert(kTcA >= kGRows * kGB * 4, "result tile must fit over the decoded weights");
+
+__device__ __forceinline__ uint64_t tc_desc(const void* p) {      // K-major, no swizzle, LBO 128 B, SBO 4096 B
+  return (uint64_t)((smem_u32(p) >> 4) & 0x3FFFu) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(4096 >> 4) << 32) |
+         (1ull << 46);
+}
+__device__ __forceinline__ void tc_mma_f16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 template <bool UP>
+__global__ void __launch_bounds__(kGT) moe_grouped_tc_kernel(const GroupedArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  uint8_t* codes = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* scales = codes + kGRows * 128;
+  uint8_t* As = scales + kGRows * 16;
+  uint8_t* Bs = As + kTcA;
+  float* res = reinterpret_cast<float*>(As);                      // [128 rows][64 routes] after the last stage
+  __shared__ int s_route[kGB], s_row[kGB];
+  __shared__ uint32_t s_taddr;
+  __shared__ __align__(8) uint64_t s_bar;
+
+  pdl_wait();
+  const int blk = blockIdx.x, tile = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (blk * kGB >= __ldg(a.ntp)) return;
+  const int e = a.expert_ids[blk];
+  if (e < 0 || e >= a.E) {
+    if (tid == 0) atomicOr(a.status, 2u);
+    return;
+  }
+  if (tid < kGB) {
+    const int route = a.sorted_ids[blk * kGB + tid];
+    const bool ok = route >= 0 && route < a.numel;
+    s_route[tid] = ok ? route : -1;
+    s_row[tid] = ok ? (UP ? route / a.topk : route) : -1;
+  }
+  if (tid == 0) {
+    mbar_init(&s_bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {                                                 // 64 tensor-memory columns: the accumulator
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_taddr)),
+                 "r"(64u)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  __syncthreads();
+  const uint32_t tmem = s_taddr;
+  auto wrow = [&](int r) {
+    return UP ? (r < 64 ? tile * 64 + r : a.I + tile * 64 + (r - 64)) : tile * kGRows + r;
+  };
+  const int nks = a.K / kSliceK, cb = a.K / 2, sb = a.K / 16;
+  const uint8_t* We = a.W + (int64_t)e * a.N * cb;
+  const uint8_t* Se = a.S + (int64_t)e * a.N * sb;
+  // kind::f16 instruction descriptor: fp32 accumulator, f16 A and B, both K-major, N = 64, M = 128
+  const uint32_t idesc = (1u << 4) | ((uint32_t)(kGB >> 3) << 17) | ((uint32_t)(kGRows >> 4) << 24);
+  bool ok = true;
+
+#pragma unroll 1
+  for (int ks = 0; ks < nks; ++ks) {
+    for (int i = tid; i < kGRows * 8; i += kGT) {                   // codes, swizzled as in the decode kernels
+      const int r = i >> 3, u = i & 7;
+      *reinterpret_cast<uint4*>(codes + r * 128 + ((u ^ (r & 7)) << 4)) =
+          *reinterpret_cast<const uint4*>(We + (int64_t)wrow(r) * cb + ks * 128 + u * 16);
+    }
+    for (int r = tid; r < kGRows; r += kGT)
+      *reinterpret_cast<uint4*>(scales + r * 16) = *reinterpret_cast<const uint4*>(Se + (int64_t)wrow(r) * sb + ks * 16);
+    for (int i = tid; i < kGB * 32; i += kGT) {                     // routes' f16 rows into the B tile
+      const int rr = i >> 5, v = i & 31, row = s_row[rr];
+      uint4 val = make_uint4(0u, 0u, 0u, 0u);
+      if (row >= 0) val = *reinterpret_cast<const uint4*>(a.xh + (int64_t)row * a.K + ks * kSliceK + v * 8);
+      *reinterpret_cast<uint4*>(Bs + (rr >> 3) * 4096 + (v >> 1) * 256 + (v & 1) * 128 + (rr & 7) * 16) = val;
+    }
+    __syncthreads();
+    for (int i = tid; i < kGRows * 32; i += kGT) {                  // decode: 128 rows x 32 units of 8 k
+      const int r = i >> 5, v = i & 31;
+      const uint32_t w = *reinterpret_cast<const uint32_t*>(codes + r * 128 + (((v >> 2) ^ (r & 7)) << 4) + (v & 3) * 4);
+      const uint32_t sc = bcast_lo(e4m3x2_to_f16x2(scales[r * 16 + (v >> 1)]));
+      uint32_t o[4];
+      e2m1x8_to_f16x2(w, o);
+      *reinterpret_cast<uint4*>(As + (r >> 3) * 4096 + (v >> 1) * 256 + (v & 1) * 128 + (r & 7) * 16) =
+          make_uint4(hmul2(o[0], sc), hmul2(o[1], sc), hmul2(o[2], sc), hmul2(o[3], sc));
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic-proxy stores -> the tensor core
+    __syncthreads();
+    if (tid == 0) {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll 1
+      for (int s16 = 0; s16 < kSliceK / 16; ++s16)
+        tc_mma_f16(tmem, tc_desc(As + s16 * 256), tc_desc(Bs + s16 * 256), idesc, (ks > 0 || s16 > 0) ? 1u : 0u);
+      tc_commit(&s_bar);
+    }
+    // the stage's MMAs are done before its shared memory is rewritten (bounded wait)
+    if (ok && !mbar_wait(&s_bar, (unsigned)(ks & 1), a.status)) ok = false;
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  }
+  __syncthreads();
+  // accumulator -> registers -> the result tile (over the decoded weights, which no MMA reads any more)
+  {
+    float v[32];
+    tc_ld32(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(32 * (warp >> 2)), v);
+    const int row = 32 * (warp & 3) + lane, col0 = 32 * (warp >> 2);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) res[row * kGB + col0 + i] = ok ? v[i] : 0.f;
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(64u) : "memory");
+  const float ge = a.g[e];
+  if (UP) {
+    for (int idx = tid; idx < 64 * kGB; idx += kGT) {
+      const int i = idx / 64, col = idx - i * 64, route = s_route[i];
+      if (route < 0) continue;
+      const float sc = ldexpf(ge, -a.shift[s_row[i]]);
+      const float gv = res[col * kGB + i] * sc, uv = res[(64 + col) * kGB + i] * sc;
+      const float silu = gv / (1.0f + expf(-gv));
+      a.out[(int64_t)route * a.ldo + tile * 64 + col] = __float2bfloat16_rn(silu * uv);
+    }
+  } else {
+    for (int idx = tid; idx < kGRows * kGB; idx += kGT) {
+      const int i = idx / kGRows, r = idx - i * kGRows, route = s_route[i];
+      if (route < 0) continue;
+      a.out[(int64_t)route * a.ldo + tile * kGRows + r] =
+          __float2bfloat16_rn(res[r * kGB + i] * ldexpf(ge, -a.shift[route]));
+    }
+  }
+  pdl_trigger();
+}
+
+template <bool UP, bool TC>
 static int grouped_launch(const GroupedArgs& a, int max_blocks, int tiles, int pdl, void* stream) {
-  auto kern = moe_grouped_kernel<UP>;
-  const int smem = kGSmem + 1024;
+  auto kern = TC ? moe_grouped_tc_kernel<UP> : moe_grouped_kernel<UP>;
+  const int smem = (TC ? kTcSmem : kGSmem) + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return FLINT_ERR_LAUNCH;
   return launch(kern, dim3((unsigned)max_blocks, (unsigned)tiles), dim3(kGT), smem, stream, pdl, a);
@@ -202,10 +365,11 @@ extern "C" int flint_rows_to_f16(const void* src, int64_t ld, int64_t rows, int6
                 (__half*)dst, (int*)shift);
 }
 
-static int grouped_entry(bool up, const void* xh, const int32_t* shift, const int32_t* sorted_ids,
+static int grouped_entry(bool up, int tc, const void* xh, const int32_t* shift, const int32_t* sorted_ids,
                          const int32_t* expert_ids, const int32_t* num_tokens_post_pad, int64_t numel, int64_t topk,
                          int64_t E, const void* W, const void* S, const float* g, int64_t H, int64_t I,
                          int64_t max_blocks, void* out, void* workspace, int pdl, void* stream) {
+  if (tc != 0 && tc != 1) return FLINT_ERR_ARGUMENT;
   if (!xh || !shift || !sorted_ids || !expert_ids || !num_tokens_post_pad || !W || !S || !g || !out || !workspace)
     return FLINT_ERR_ARGUMENT;
   if (numel < 1 || topk < 1 || topk > 32 || E < 1 || max_blocks < 1 || max_blocks > 65535 || H < kSliceK ||
@@ -219,26 +383,28 @@ static int grouped_entry(bool up, const void* xh, const int32_t* shift, const in
   a.status = (unsigned*)workspace;
   if (up) {
     a.K = (int)H; a.N = (int)(2 * I); a.ldo = (int)I;
-    return grouped_launch<true>(a, (int)max_blocks, (int)(I / 64), pdl, stream);
+    return tc ? grouped_launch<true, true>(a, (int)max_blocks, (int)(I / 64), pdl, stream)
+              : grouped_launch<true, false>(a, (int)max_blocks, (int)(I / 64), pdl, stream);
   }
   a.K = (int)I; a.N = (int)H; a.ldo = (int)H;
-  return grouped_launch<false>(a, (int)max_blocks, (int)(H / kGRows), pdl, stream);
+  return tc ? grouped_launch<false, true>(a, (int)max_blocks, (int)(H / kGRows), pdl, stream)
+            : grouped_launch<false, false>(a, (int)max_blocks, (int)(H / kGRows), pdl, stream);
 }
 
 extern "C" int flint_moe_grouped_up(const void* xh, const int32_t* shift, const int32_t* sorted_ids,
                                     const int32_t* expert_ids, const int32_t* num_tokens_post_pad, int64_t numel,
                                     int64_t topk, int64_t E, const void* w13, const void* s13, const float* g13,
-                                    int64_t H, int64_t I, int64_t max_blocks, void* act, void* workspace, int pdl,
-                                    void* stream) {
-  return grouped_entry(true, xh, shift, sorted_ids, expert_ids, num_tokens_post_pad, numel, topk, E, w13, s13, g13,
+                                    int64_t H, int64_t I, int64_t max_blocks, void* act, void* workspace,
+                                    int tensor_cores, int pdl, void* stream) {
+  return grouped_entry(true, tensor_cores, xh, shift, sorted_ids, expert_ids, num_tokens_post_pad, numel, topk, E, w13, s13, g13,
                        H, I, max_blocks, act, workspace, pdl, stream);
 }
 
 extern "C" int flint_moe_grouped_down(const void* ah, const int32_t* shift, const int32_t* sorted_ids,
                                       const int32_t* expert_ids, const int32_t* num_tokens_post_pad, int64_t numel,
                                       int64_t topk, int64_t E, const void* w2, const void* s2, const float* g2,
-                                      int64_t H, int64_t I, int64_t max_blocks, void* y, void* workspace, int pdl,
-                                      void* stream) {
-  return grouped_entry(false, ah, shift, sorted_ids, expert_ids, num_tokens_post_pad, numel, topk, E, w2, s2, g2, H,
+                                      int64_t H, int64_t I, int64_t max_blocks, void* y, void* workspace,
+                                      int tensor_cores, int pdl, void* stream) {
+  return grouped_entry(false, tensor_cores, ah, shift, sorted_ids, expert_ids, num_tokens_post_pad, numel, topk, E, w2, s2, g2, H,
                        I, max_blocks, y, workspace, pdl, stream);
 }

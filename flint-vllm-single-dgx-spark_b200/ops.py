@@ -954,48 +954,50 @@ def _(src, dst, shift):
     return None
 
 
-def _grouped(fn: str, xh, shift, sorted_ids, expert_ids, ntp, numel, topk, w, s, g, H, I, out):
+def _grouped(fn: str, xh, shift, sorted_ids, expert_ids, ntp, numel, topk, w, s, g, H, I, out, tc):
     _lib.require_cuda(xh, fn)
     ws = _lib.workspace(xh.device, "moe_grouped_status", 4)
     rc = getattr(lib(), f"flint_{fn}")(ptr(xh), ptr(shift), ptr(sorted_ids), ptr(expert_ids), ptr(ntp), int(numel),
                                        int(topk), w.shape[0], ptr(_u8(w)), ptr(_u8(s)), ptr(g), int(H), int(I),
-                                       expert_ids.numel(), ptr(out), ptr(ws), PDL, stream_ptr(xh.device))
+                                       expert_ids.numel(), ptr(out), ptr(ws), int(tc), PDL, stream_ptr(xh.device))
     check(rc, f"flint_{fn}")
 
 
 @torch.library.custom_op(f"{NS}::moe_grouped_up", mutates_args=("act",))
 def moe_grouped_up(xh: torch.Tensor, shift: torch.Tensor, sorted_ids: torch.Tensor, expert_ids: torch.Tensor,
                    num_tokens_post_pad: torch.Tensor, numel: int, topk: int, w13: torch.Tensor, s13: torch.Tensor,
-                   g13: torch.Tensor, act: torch.Tensor) -> None:
-    """Prefill gate/up + SwiGLU of the aligned routes (flint_moe_grouped_up): act bf16 [numel, I] per route."""
+                   g13: torch.Tensor, act: torch.Tensor, tensor_cores: int) -> None:
+    """Prefill gate/up + SwiGLU of the aligned routes (flint_moe_grouped_up): act bf16 [numel, I] per route;
+    tensor_cores 1: tcgen05, 0: mma.sync."""
     H = xh.shape[1]
     I = w13.shape[1] // 2
     if act.shape != (numel, I) or w13.shape[2] * 2 != H:
         raise _lib.FlintError("moe_grouped_up: act [numel, I], w13 [E, 2I, H/2]")
     _grouped("moe_grouped_up", xh, shift, sorted_ids, expert_ids, num_tokens_post_pad, numel, topk, w13, s13, g13, H,
-             I, act)
+             I, act, tensor_cores)
 
 
 @moe_grouped_up.register_fake
-def _(xh, shift, sorted_ids, expert_ids, num_tokens_post_pad, numel, topk, w13, s13, g13, act):
+def _(xh, shift, sorted_ids, expert_ids, num_tokens_post_pad, numel, topk, w13, s13, g13, act, tensor_cores):
     return None
 
 
 @torch.library.custom_op(f"{NS}::moe_grouped_down", mutates_args=("y",))
 def moe_grouped_down(ah: torch.Tensor, shift: torch.Tensor, sorted_ids: torch.Tensor, expert_ids: torch.Tensor,
                      num_tokens_post_pad: torch.Tensor, numel: int, topk: int, w2: torch.Tensor, s2: torch.Tensor,
-                     g2: torch.Tensor, y: torch.Tensor) -> None:
-    """Prefill down projection of the aligned routes (flint_moe_grouped_down): y bf16 [numel, H] per route."""
+                     g2: torch.Tensor, y: torch.Tensor, tensor_cores: int) -> None:
+    """Prefill down projection of the aligned routes (flint_moe_grouped_down): y bf16 [numel, H] per route;
+    tensor_cores 1: tcgen05, 0: mma.sync."""
     I = ah.shape[1]
     H = w2.shape[1]
     if y.shape != (numel, H) or w2.shape[2] * 2 != I:
         raise _lib.FlintError("moe_grouped_down: y [numel, H], w2 [E, H, I/2]")
     _grouped("moe_grouped_down", ah, shift, sorted_ids, expert_ids, num_tokens_post_pad, numel, topk, w2, s2, g2, H, I,
-             y)
+             y, tensor_cores)
 
 
 @moe_grouped_down.register_fake
-def _(ah, shift, sorted_ids, expert_ids, num_tokens_post_pad, numel, topk, w2, s2, g2, y):
+def _(ah, shift, sorted_ids, expert_ids, num_tokens_post_pad, numel, topk, w2, s2, g2, y, tensor_cores):
     return None
 
 

@@ -492,17 +492,19 @@ int flint_flashinfer_nvfp4_unpack(const void* w1, const void* w1_sf, const void*
  *   flint_moe_grouped_down: ah = the routes' f16 act rows [numel][I] -> y bf16 [numel][H] per route (as
  *     flint_moe_down's per-route rows);
  * then flint_moe_combine(y, topk_weights, T, topk, H, out) for the slot-order weighted sum.  Weights in the ModelOpt
- * layout of the other MoE entry points; H and I multiples of 256; workspace: one status word (4 bytes, zeroed). */
+ * layout of the other MoE entry points; H and I multiples of 256; workspace: one status word (4 bytes, zeroed).
+ * tensor_cores: 1 = tcgen05.mma with the accumulator in tensor memory, 0 = mma.sync (same tiles and rounding points;
+ * the fp32 sums differ in order). */
 int flint_rows_to_f16(const void* src, int64_t ld, int64_t rows, int64_t K, void* dst, int32_t* shift, int pdl,
                       void* stream);
 int flint_moe_grouped_up(const void* xh, const int32_t* shift, const int32_t* sorted_ids, const int32_t* expert_ids,
                          const int32_t* num_tokens_post_pad, int64_t numel, int64_t topk, int64_t E, const void* w13,
                          const void* s13, const float* g13, int64_t H, int64_t I, int64_t max_blocks, void* act,
-                         void* workspace, int pdl, void* stream);
+                         void* workspace, int tensor_cores, int pdl, void* stream);
 int flint_moe_grouped_down(const void* ah, const int32_t* shift, const int32_t* sorted_ids, const int32_t* expert_ids,
                            const int32_t* num_tokens_post_pad, int64_t numel, int64_t topk, int64_t E, const void* w2,
                            const void* s2, const float* g2, int64_t H, int64_t I, int64_t max_blocks, void* y,
-                           void* workspace, int pdl, void* stream);
+                           void* workspace, int tensor_cores, int pdl, void* stream);
 
 #ifdef __cplusplus
 }

@@ -205,7 +205,9 @@ def time_grouped_moe(args):
             fm.moe_down(a, None, ids[t0:t0 + 8], tw[t0:t0 + 8], w)
 
     res = {}
-    for name, fn in (("grouped_moe", lambda: fm.grouped_moe(x, ids, tw, w)), ("decode_kernels_8_token_chunks", chunks)):
+    for name, fn in (("grouped_moe", lambda: fm.grouped_moe(x, ids, tw, w)),
+                     ("grouped_moe_tcgen05", lambda: fm.grouped_moe(x, ids, tw, w, tensor_cores=True)),
+                     ("decode_kernels_8_token_chunks", chunks)):
         fn()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

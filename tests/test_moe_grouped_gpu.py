@@ -40,7 +40,7 @@ def _grouped_steps(x, ids, tw, w):
     sx = torch.empty((T,), dtype=torch.int32, device="cuda")
     ops.rows_to_f16(x, xh, sx)
     act = torch.full((numel, w.I), float("nan"), dtype=torch.bfloat16, device="cuda")
-    ops.moe_grouped_up(xh, sx, sorted_ids, expert_ids, ntp, numel, k, w.w13, w.s13, w.g13, act)
+    ops.moe_grouped_up(xh, sx, sorted_ids, expert_ids, ntp, numel, k, w.w13, w.s13, w.g13, act, 0)
     return act
 
 
@@ -76,3 +76,29 @@ def test_grouped_moe_vs_oracle_and_decode_kernels(fb, cfg, T, skew):
     out2 = fm.grouped_moe(x, ids_d, tw_d, w)
     torch.cuda.synchronize()
     np.testing.assert_array_equal(host(out2), host(out))
+
+
+@needs_cuda
+@pytest.mark.parametrize("cfg,T", [(BASE, 40), (FLINT, 130)], ids=["base_40", "flint_130"])
+def test_grouped_moe_tcgen05_matches_mma_sync_and_oracle(fb, cfg, T):
+    """The tcgen05 tiles (accumulator in tensor memory): same rounding points as the mma.sync tiles, fp32 sums in
+    the tensor core's order -- within the activation tolerance of them and of the oracle, and deterministic."""
+    from flint_b200 import fp4moe_decode as fm
+    rng = np.random.default_rng(5 + T)
+    H, E, topk, I = cfg["H"], 32, cfg["topk"], cfg["I"]
+    L = make_layer(rng, H=H, E=E, I=I)
+    w = dev_weights(L, topk, cfg["score"])
+    ids = _routes(rng, T, E, topk, False)
+    tw = rng.dirichlet(np.ones(topk), size=T).astype(np.float32)
+    xn = bf16(rng, (T, H))
+    x, ids_d, tw_d = dev_bf16(xn), to_dev(ids), to_dev(tw)
+    out_tc = fm.grouped_moe(x, ids_d, tw_d, w, tensor_cores=True)
+    out_ms = fm.grouped_moe(x, ids_d, tw_d, w, tensor_cores=False)
+    torch.cuda.synchronize()
+    assert_bf16_close(host(out_tc), host(out_ms), rel=2.0 ** -6, abs_frac=4e-3, what="tcgen05 vs mma.sync")
+    act_ref = omoe.experts_up(xn, ids, L["w13"], L["s13"], L["g13"])
+    assert_bf16_close(host(out_tc), omoe.experts_down(act_ref, ids, tw, L["w2"], L["s2"], L["g2"]), rel=2.0 ** -6,
+                      abs_frac=4e-3, what="tcgen05 vs oracle")
+    out_tc2 = fm.grouped_moe(x, ids_d, tw_d, w, tensor_cores=True)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(host(out_tc2), host(out_tc))
