@@ -181,21 +181,36 @@ __global__ void __launch_bounds__(kGT) moe_grouped_kernel(const GroupedArgs a) {
   pdl_trigger();
 }
 
-// ---- the same tile on the 5th-generation tensor cores (tcgen05, one CTA, accumulator in tensor memory) ----
-// Per K stage of 256 the warps decode the 128 weight rows into f16 in shared memory and copy the 64 routes' f16 rows
-// next to them, both in the K-major no-swizzle canonical layout of the MMA (8-row x 16-byte core matrices: row group
-// i at i * 4096 B, 16-k step s at s * 256 B, k half j at j * 128 B); one thread then issues the stage's 16
-// tcgen05.mma kind::f16 (M = 128 weight rows, N = 64 routes, K = 16) into a 128 x 64 fp32 accumulator in tensor
-// memory and commits them to an mbarrier that frees the stage.  The epilogue reads the accumulator with
-// tcgen05.ld (warp w: lanes 32 (w % 4) .., columns 32 (w / 4) ..).  Each product is exact; the tensor core's fp32
-// sums run in their own order (within the activation tolerance of the mma.sync tile and of the oracle).
-constexpr int kTcA = kGRows * kSliceK * 2;          // 64 KB decoded weights
-constexpr int kTcB = kGB * kSliceK * 2;             // 32 KB activations
-constexpr int kTcSmem = kGRows * 128 + kGRows * 16 + kTcA + kTcB;
-static_assert(kTcA >= kGRows * kGB * 4, "result tile must fit over the decoded weights");
+// ---- the same tile on the 5th-generation tensor cores (tcgen05, accumulator in tensor memory) ----
+// K goes in stages of 128.  Per stage every thread holds 2 chunks of 32 weight codes (16 B) with their two E4M3 scale
+// bytes and 4 units of 8 route activations (16 B) in registers, fetched one stage ahead; it decodes its codes into
+// f16 and stores them, and its activations, into one of two stage buffers in the K-major no-swizzle canonical layout
+// of the MMA (8-row x 16-byte core matrices: row group i at i * 2048 B, 16-k step s at s * 256 B, k half j at
+// j * 128 B).  Lane l of a warp takes row l % 8 of an 8-row group and k chunk l / 8, so each 8-lane phase of a
+// 16-byte store fills one whole 128-byte line of a core matrix (no bank conflicts) and each row's 64 bytes of the
+// stage are read by 4 lanes.
+// One thread then issues the stage's 8 tcgen05.mma kind::f16 (M = 128 weight rows, N = 64 routes, K = 16) into a
+// 128 x 64 fp32 accumulator in tensor memory and commits them to the buffer's mbarrier; the buffer is written again
+// two stages later, after that barrier (bounded wait).  So the MMAs of one stage run while the next is fetched and
+// decoded.  96 KB of shared memory: two CTAs per SM.  The epilogue reads the accumulator with tcgen05.ld (warp w:
+// lanes 32 (w % 4) .., columns 32 (w / 4) ..).  Each product is exact; the tensor core's fp32 sums run in their own
+// order (within the activation tolerance of the mma.sync tile and of the oracle).
+constexpr int kTcK = 128;                           // k per stage
+constexpr int kTcSbo = (kTcK / 16) * 256;           // bytes between 8-row groups
+constexpr int kTcA = kGRows * kTcK * 2;             // 32 KB decoded weights per buffer
+constexpr int kTcB = kGB * kTcK * 2;                // 16 KB activations per buffer
+constexpr int kTcSmem = 2 * (kTcA + kTcB);
+constexpr int kTcWU = kGRows * (kTcK / 32) / kGT;   // weight chunks of 32 k per thread per stage
+constexpr int kTcXU = kGB * (kTcK / 8) / kGT;       // activation units of 8 k per thread per stage
+constexpr int kTcRS = kGB + 1;                      // fp32 stride of a result row (conflict-free column walks)
+static_assert(2 * kTcA >= kGRows * kTcRS * 4, "result tile must fit over the decoded weights");
+static_assert(kTcWU * kGT == kGRows * (kTcK / 32) && kTcXU * kGT == kGB * (kTcK / 8), "whole units per thread");
+static_assert(kTcK / 32 == 4 && kGRows / 8 == kGW * kTcWU && kTcXU == 4 && kGW == 8, "lane map: 8 rows x 4 chunks");
 
-__device__ __forceinline__ uint64_t tc_desc(const void* p) {      // K-major, no swizzle, LBO 128 B, SBO 4096 B
-  return (uint64_t)((smem_u32(p) >> 4) & 0x3FFFu) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(4096 >> 4) << 32) |
+// canonical-layout byte offset of 8 k (16 B) at row r, unit v (of kTcK / 8) within a stage buffer
+__device__ __forceinline__ int tc_off(int r, int v) { return (r >> 3) * kTcSbo + (v >> 1) * 256 + (v & 1) * 128 + (r & 7) * 16; }
+__device__ __forceinline__ uint64_t tc_desc(const void* p) {      // K-major, no swizzle, LBO 128 B, SBO kTcSbo
+  return (uint64_t)((smem_u32(p) >> 4) & 0x3FFFu) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(kTcSbo >> 4) << 32) |
          (1ull << 46);
 }
 __device__ __forceinline__ void tc_mma_f16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
@@ -225,16 +240,14 @@ __device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
 }
 
 template <bool UP>
-__global__ void __launch_bounds__(kGT) moe_grouped_tc_kernel(const GroupedArgs a) {
+__global__ void __launch_bounds__(kGT, 2) moe_grouped_tc_kernel(const GroupedArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  uint8_t* codes = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* scales = codes + kGRows * 128;
-  uint8_t* As = scales + kGRows * 16;
-  uint8_t* Bs = As + kTcA;
-  float* res = reinterpret_cast<float*>(As);                      // [128 rows][64 routes] after the last stage
+  uint8_t* As = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* Bs = As + 2 * kTcA;                                    // buffer b: As + b kTcA, Bs + b kTcB
+  float* res = reinterpret_cast<float*>(As);                      // [128 rows][kTcRS] after the last stage
   __shared__ int s_route[kGB], s_row[kGB];
   __shared__ uint32_t s_taddr;
-  __shared__ __align__(8) uint64_t s_bar;
+  __shared__ __align__(8) uint64_t s_bar[2];
 
   pdl_wait();
   const int blk = blockIdx.x, tile = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -251,7 +264,8 @@ __global__ void __launch_bounds__(kGT) moe_grouped_tc_kernel(const GroupedArgs a
     s_row[tid] = ok ? (UP ? route / a.topk : route) : -1;
   }
   if (tid == 0) {
-    mbar_init(&s_bar, 1);
+    mbar_init(&s_bar[0], 1);
+    mbar_init(&s_bar[1], 1);
     fence_mbar_init();
   }
   if (warp == 0) {                                                 // 64 tensor-memory columns: the accumulator
@@ -265,51 +279,86 @@ __global__ void __launch_bounds__(kGT) moe_grouped_tc_kernel(const GroupedArgs a
   auto wrow = [&](int r) {
     return UP ? (r < 64 ? tile * 64 + r : a.I + tile * 64 + (r - 64)) : tile * kGRows + r;
   };
-  const int nks = a.K / kSliceK, cb = a.K / 2, sb = a.K / 16;
+  const int nks = a.K / kTcK, cb = a.K / 2, sb = a.K / 16;
   const uint8_t* We = a.W + (int64_t)e * a.N * cb;
   const uint8_t* Se = a.S + (int64_t)e * a.N * sb;
   // kind::f16 instruction descriptor: fp32 accumulator, f16 A and B, both K-major, N = 64, M = 128
   const uint32_t idesc = (1u << 4) | ((uint32_t)(kGB >> 3) << 17) | ((uint32_t)(kGRows >> 4) << 24);
   bool ok = true;
+  // this thread's pieces: weight chunk j (32 k) at row 8 (warp + 8 j) + lane % 8, chunk c = lane / 8 of the stage;
+  // activation unit j (8 k) at route 8 ((warp + 8 j) % 8) + lane % 8, unit 4 ((warp + 8 j) / 8) + lane / 8.
+  // (32-bit offsets within one expert's codes / scales: the entry bounds N K / 2 below 2^31)
+  const int l8 = lane & 7, c = lane >> 3;
+  int xrow[kTcXU];
+#pragma unroll
+  for (int j = 0; j < kTcXU; ++j) xrow[j] = s_row[8 * ((warp + 8 * j) & 7) + l8];
+  uint4 wc[kTcWU], xv[kTcXU];
+  uint32_t sc[kTcWU];
+  auto fetch = [&](int ks, uint4 (&w)[kTcWU], uint32_t (&s2)[kTcWU], uint4 (&x)[kTcXU]) {
+#pragma unroll
+    for (int j = 0; j < kTcWU; ++j) {
+      const int wr = wrow(8 * (warp + 8 * j) + l8);
+      w[j] = __ldg(reinterpret_cast<const uint4*>(We + (uint32_t)(wr * cb + ks * (kTcK / 2) + c * 16)));
+      s2[j] = __ldg(reinterpret_cast<const unsigned short*>(Se + (uint32_t)(wr * sb + ks * (kTcK / 16) + c * 2)));
+    }
+#pragma unroll
+    for (int j = 0; j < kTcXU; ++j) {
+      const int v = 4 * ((warp + 8 * j) >> 3) + c;
+      x[j] = xrow[j] >= 0 ? __ldg(reinterpret_cast<const uint4*>(a.xh + (int64_t)xrow[j] * a.K + ks * kTcK + v * 8))
+                          : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  fetch(0, wc, sc, xv);
 
 #pragma unroll 1
   for (int ks = 0; ks < nks; ++ks) {
-    for (int i = tid; i < kGRows * 8; i += kGT) {                   // codes, swizzled as in the decode kernels
-      const int r = i >> 3, u = i & 7;
-      *reinterpret_cast<uint4*>(codes + r * 128 + ((u ^ (r & 7)) << 4)) =
-          *reinterpret_cast<const uint4*>(We + (int64_t)wrow(r) * cb + ks * 128 + u * 16);
+    const int b = ks & 1;
+    uint4 wn[kTcWU], xn[kTcXU];
+    uint32_t sn[kTcWU];
+    if (ks + 1 < nks) fetch(ks + 1, wn, sn, xn);                   // the next stage's loads fly during this one
+    // buffer b was last read by the MMAs of stage ks - 2 (bounded wait on its barrier)
+    if (ks >= 2 && ok && !mbar_wait(&s_bar[b], (unsigned)(((ks >> 1) - 1) & 1), a.status)) ok = false;
+    uint8_t* Ab = As + b * kTcA;
+    uint8_t* Bb = Bs + b * kTcB;
+#pragma unroll
+    for (int j = 0; j < kTcWU; ++j) {
+      const int r = 8 * (warp + 8 * j) + l8;
+      const uint32_t sg = e4m3x2_to_f16x2(sc[j]);                  // scales of 16-k groups 2c, 2c + 1
+      const uint32_t wq[4] = {wc[j].x, wc[j].y, wc[j].z, wc[j].w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {                                // unit 4c + q: 8 k of group 2c + q / 2
+        const uint32_t s2 = q < 2 ? bcast_lo(sg) : bcast_hi(sg);
+        uint32_t o[4];
+        e2m1x8_to_f16x2(wq[q], o);
+        *reinterpret_cast<uint4*>(Ab + tc_off(r, 4 * c + q)) =
+            make_uint4(hmul2(o[0], s2), hmul2(o[1], s2), hmul2(o[2], s2), hmul2(o[3], s2));
+      }
     }
-    for (int r = tid; r < kGRows; r += kGT)
-      *reinterpret_cast<uint4*>(scales + r * 16) = *reinterpret_cast<const uint4*>(Se + (int64_t)wrow(r) * sb + ks * 16);
-    for (int i = tid; i < kGB * 32; i += kGT) {                     // routes' f16 rows into the B tile
-      const int rr = i >> 5, v = i & 31, row = s_row[rr];
-      uint4 val = make_uint4(0u, 0u, 0u, 0u);
-      if (row >= 0) val = *reinterpret_cast<const uint4*>(a.xh + (int64_t)row * a.K + ks * kSliceK + v * 8);
-      *reinterpret_cast<uint4*>(Bs + (rr >> 3) * 4096 + (v >> 1) * 256 + (v & 1) * 128 + (rr & 7) * 16) = val;
-    }
-    __syncthreads();
-    for (int i = tid; i < kGRows * 32; i += kGT) {                  // decode: 128 rows x 32 units of 8 k
-      const int r = i >> 5, v = i & 31;
-      const uint32_t w = *reinterpret_cast<const uint32_t*>(codes + r * 128 + (((v >> 2) ^ (r & 7)) << 4) + (v & 3) * 4);
-      const uint32_t sc = bcast_lo(e4m3x2_to_f16x2(scales[r * 16 + (v >> 1)]));
-      uint32_t o[4];
-      e2m1x8_to_f16x2(w, o);
-      *reinterpret_cast<uint4*>(As + (r >> 3) * 4096 + (v >> 1) * 256 + (v & 1) * 128 + (r & 7) * 16) =
-          make_uint4(hmul2(o[0], sc), hmul2(o[1], sc), hmul2(o[2], sc), hmul2(o[3], sc));
-    }
+#pragma unroll
+    for (int j = 0; j < kTcXU; ++j)
+      *reinterpret_cast<uint4*>(Bb + tc_off(8 * ((warp + 8 * j) & 7) + l8, 4 * ((warp + 8 * j) >> 3) + c)) = xv[j];
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic-proxy stores -> the tensor core
     __syncthreads();
     if (tid == 0) {
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll 1
-      for (int s16 = 0; s16 < kSliceK / 16; ++s16)
-        tc_mma_f16(tmem, tc_desc(As + s16 * 256), tc_desc(Bs + s16 * 256), idesc, (ks > 0 || s16 > 0) ? 1u : 0u);
-      tc_commit(&s_bar);
+      for (int s16 = 0; s16 < kTcK / 16; ++s16)
+        tc_mma_f16(tmem, tc_desc(Ab + s16 * 256), tc_desc(Bb + s16 * 256), idesc, (ks > 0 || s16 > 0) ? 1u : 0u);
+      tc_commit(&s_bar[b]);
     }
-    // the stage's MMAs are done before its shared memory is rewritten (bounded wait)
-    if (ok && !mbar_wait(&s_bar, (unsigned)(ks & 1), a.status)) ok = false;
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (ks + 1 < nks) {
+#pragma unroll
+      for (int j = 0; j < kTcWU; ++j) {
+        wc[j] = wn[j];
+        sc[j] = sn[j];
+      }
+#pragma unroll
+      for (int j = 0; j < kTcXU; ++j) xv[j] = xn[j];
+    }
   }
+  // the last commit covers every MMA of the tile (bounded wait)
+  if (ok && !mbar_wait(&s_bar[(nks - 1) & 1], (unsigned)(((nks - 1) >> 1) & 1), a.status)) ok = false;
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   __syncthreads();
   // accumulator -> registers -> the result tile (over the decoded weights, which no MMA reads any more)
   {
@@ -317,7 +366,7 @@ __global__ void __launch_bounds__(kGT) moe_grouped_tc_kernel(const GroupedArgs a
     tc_ld32(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(32 * (warp >> 2)), v);
     const int row = 32 * (warp & 3) + lane, col0 = 32 * (warp >> 2);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) res[row * kGB + col0 + i] = ok ? v[i] : 0.f;
+    for (int i = 0; i < 32; ++i) res[row * kTcRS + col0 + i] = ok ? v[i] : 0.f;
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
@@ -329,7 +378,7 @@ __global__ void __launch_bounds__(kGT) moe_grouped_tc_kernel(const GroupedArgs a
       const int i = idx / 64, col = idx - i * 64, route = s_route[i];
       if (route < 0) continue;
       const float sc = ldexpf(ge, -a.shift[s_row[i]]);
-      const float gv = res[col * kGB + i] * sc, uv = res[(64 + col) * kGB + i] * sc;
+      const float gv = res[col * kTcRS + i] * sc, uv = res[(64 + col) * kTcRS + i] * sc;
       const float silu = gv / (1.0f + expf(-gv));
       a.out[(int64_t)route * a.ldo + tile * 64 + col] = __float2bfloat16_rn(silu * uv);
     }
@@ -338,7 +387,7 @@ __global__ void __launch_bounds__(kGT) moe_grouped_tc_kernel(const GroupedArgs a
       const int i = idx / kGRows, r = idx - i * kGRows, route = s_route[i];
       if (route < 0) continue;
       a.out[(int64_t)route * a.ldo + tile * kGRows + r] =
-          __float2bfloat16_rn(res[r * kGB + i] * ldexpf(ge, -a.shift[route]));
+          __float2bfloat16_rn(res[r * kTcRS + i] * ldexpf(ge, -a.shift[route]));
     }
   }
   pdl_trigger();
@@ -373,8 +422,8 @@ static int grouped_entry(bool up, int tc, const void* xh, const int32_t* shift, 
   if (!xh || !shift || !sorted_ids || !expert_ids || !num_tokens_post_pad || !W || !S || !g || !out || !workspace)
     return FLINT_ERR_ARGUMENT;
   if (numel < 1 || topk < 1 || topk > 32 || E < 1 || max_blocks < 1 || max_blocks > 65535 || H < kSliceK ||
-      H % kSliceK != 0 || I < kSliceK || I % kSliceK != 0)
-    return FLINT_ERR_SHAPE;
+      H % kSliceK != 0 || I < kSliceK || I % kSliceK != 0 || I * H >= (int64_t(1) << 31))
+    return FLINT_ERR_SHAPE;                                         // one expert's 2I x H/2 code bytes in 32 bits
   if (!aligned(xh, 16) || !aligned(W, 16) || !aligned(S, 16) || !aligned(workspace, 4)) return FLINT_ERR_ALIGN;
   GroupedArgs a;
   a.xh = (const __half*)xh; a.shift = shift; a.sorted_ids = sorted_ids; a.expert_ids = expert_ids;

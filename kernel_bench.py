@@ -118,6 +118,8 @@ def main(argv=None):
     ap.add_argument("--rows", type=int, default=151552)
     ap.add_argument("--cols", type=int, default=2048)
     ap.add_argument("--tokens", type=int, default=6057, help="grouped_moe: prompt tokens")
+    ap.add_argument("--variants", default="grouped_moe,grouped_moe_tcgen05,decode_kernels_8_token_chunks",
+                    help="grouped_moe: comma-separated variants to time")
     ap.add_argument("--lib", default=None, help="load this build of libflint_b200.so (e.g. an instrumented one)")
     ap.add_argument("--timeline", action="store_true", help="print the kernel's phase stamps (instrumented build)")
     args = ap.parse_args(argv)
@@ -205,9 +207,11 @@ def time_grouped_moe(args):
             fm.moe_down(a, None, ids[t0:t0 + 8], tw[t0:t0 + 8], w)
 
     res = {}
-    for name, fn in (("grouped_moe", lambda: fm.grouped_moe(x, ids, tw, w)),
-                     ("grouped_moe_tcgen05", lambda: fm.grouped_moe(x, ids, tw, w, tensor_cores=True)),
-                     ("decode_kernels_8_token_chunks", chunks)):
+    variants = {"grouped_moe": lambda: fm.grouped_moe(x, ids, tw, w),
+                "grouped_moe_tcgen05": lambda: fm.grouped_moe(x, ids, tw, w, tensor_cores=True),
+                "decode_kernels_8_token_chunks": chunks}
+    for name in args.variants.split(","):
+        fn = variants[name]
         fn()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
