@@ -181,47 +181,70 @@ __global__ void __launch_bounds__(kGT) moe_grouped_kernel(const GroupedArgs a) {
   pdl_trigger();
 }
 
-// ---- the same tile on the 5th-generation tensor cores (tcgen05, accumulator in tensor memory) ----
-// K goes in stages of 128.  Per stage every thread holds 2 chunks of 32 weight codes (16 B) with their two E4M3 scale
-// bytes and 4 units of 8 route activations (16 B) in registers, fetched one stage ahead; it decodes its codes into
-// f16 and stores them, and its activations, into one of two stage buffers in the K-major no-swizzle canonical layout
-// of the MMA (8-row x 16-byte core matrices: row group i at i * 2048 B, 16-k step s at s * 256 B, k half j at
-// j * 128 B).  Lane l of a warp takes row l % 8 of an 8-row group and k chunk l / 8, so each 8-lane phase of a
-// 16-byte store fills one whole 128-byte line of a core matrix (no bank conflicts) and each row's 64 bytes of the
-// stage are read by 4 lanes.
-// One thread then issues the stage's 8 tcgen05.mma kind::f16 (M = 128 weight rows, N = 64 routes, K = 16) into a
-// 128 x 64 fp32 accumulator in tensor memory and commits them to the buffer's mbarrier; the buffer is written again
-// two stages later, after that barrier (bounded wait).  So the MMAs of one stage run while the next is fetched and
-// decoded.  96 KB of shared memory: two CTAs per SM.  The epilogue reads the accumulator with tcgen05.ld (warp w:
-// lanes 32 (w % 4) .., columns 32 (w / 4) ..).  Each product is exact; the tensor core's fp32 sums run in their own
-// order (within the activation tolerance of the mma.sync tile and of the oracle).
+// ---- the same tile on the 5th-generation tensor cores (tcgen05: decoded weights and accumulator in tensor memory) ----
+// 8 consumer warps and 1 producer warp; K goes in stages of 128.
+//   producer (warp 8, one lane): the stage's code bytes of the CTA's 128 weight rows, 2 TMA boxes of 64 rows x 64 B
+//     with the 64-byte swizzle, into a 4-slot ring (full / empty mbarriers, bounded waits);
+//   consumer thread (warp w, lane l): weight row r = 32 (w % 4) + l, k half h = w / 4 of the stage.  It reads its 32
+//     code bytes (conflict-free under the swizzle) and its 4 E4M3 scales (loaded once per CTA into a padded array),
+//     decodes them to 32 f16 pairs and writes them with one tcgen05.st into its own tensor-memory lane (warp w owns
+//     lanes 32 (w % 4) ..): the MMA's A operand, two stage buffers of 64 columns.  The 64 routes' f16 activations
+//     go through registers (fetched one stage ahead) into one of two shared-memory buffers in the K-major no-swizzle
+//     canonical layout (8-row x 16-byte core matrices: route group i at i * 2048 B, 16-k step s at s * 256 B, k half
+//     j at j * 128 B); lane l takes route l % 8 of an 8-route group, so each 8-lane store phase fills one 128-byte
+//     line;
+//   one thread then issues the stage's 8 tcgen05.mma kind::f16 (A from tensor memory, B from shared memory; M = 128
+//     weight rows, N = 64 routes, K = 16) into the 128 x 64 fp32 accumulator (tensor-memory columns 0..63) and
+//     commits them to the buffer's mbarrier; a buffer is written again two stages later, after that barrier.
+// 256 tensor-memory columns and ~80 KB of shared memory per CTA: two CTAs per SM.  The epilogue reads the
+// accumulator with tcgen05.ld.  Each product is exact; the tensor core's fp32 sums run in their own order (within
+// the activation tolerance of the mma.sync tile and of the oracle).
 constexpr int kTcK = 128;                           // k per stage
-constexpr int kTcSbo = (kTcK / 16) * 256;           // bytes between 8-row groups
-constexpr int kTcA = kGRows * kTcK * 2;             // 32 KB decoded weights per buffer
+constexpr int kTcSbo = (kTcK / 16) * 256;           // B: bytes between 8-route groups
 constexpr int kTcB = kGB * kTcK * 2;                // 16 KB activations per buffer
-constexpr int kTcSmem = 2 * (kTcA + kTcB);
-constexpr int kTcWU = kGRows * (kTcK / 32) / kGT;   // weight chunks of 32 k per thread per stage
+constexpr int kTcNS = 4;                            // code ring slots
+constexpr int kTcSlot = kGRows * (kTcK / 2);        // 8 KB of codes per slot (two 4 KB boxes)
 constexpr int kTcXU = kGB * (kTcK / 8) / kGT;       // activation units of 8 k per thread per stage
 constexpr int kTcRS = kGB + 1;                      // fp32 stride of a result row (conflict-free column walks)
-static_assert(2 * kTcA >= kGRows * kTcRS * 4, "result tile must fit over the decoded weights");
-static_assert(kTcWU * kGT == kGRows * (kTcK / 32) && kTcXU * kGT == kGB * (kTcK / 8), "whole units per thread");
-static_assert(kTcK / 32 == 4 && kGRows / 8 == kGW * kTcWU && kTcXU == 4 && kGW == 8, "lane map: 8 rows x 4 chunks");
+constexpr int kTcThreads = kGT + 32;                // + the producer warp
+constexpr int kTcCols = 256;                        // tensor memory: accumulator 0..63, A buffers at 64 and 128
+constexpr int kTcMinSmem = 80 * 1024;               // keeps a third CTA (and its tensor-memory request) off the SM
+static_assert(kTcXU == 4 && kGW == 8 && kGRows == 128, "lane maps: 8 routes x 4 units per warp, 2 threads per row");
+static_assert(kTcNS * kTcSlot + 2 * kTcB >= kGRows * kTcRS * 4, "result tile must fit over the ring and B buffers");
 
-// canonical-layout byte offset of 8 k (16 B) at row r, unit v (of kTcK / 8) within a stage buffer
+// scale bytes per row in shared memory: K/16 + 4 (an odd number of words, so 32 rows read in one wavefront)
+__host__ __device__ constexpr int tc_scale_stride(int K) { return K / 16 + 4; }
+static int tc_smem(int K) {
+  const int need = kTcNS * kTcSlot + 2 * kTcB + ((kGRows * tc_scale_stride(K) + 15) / 16) * 16;
+  return need > kTcMinSmem ? need : kTcMinSmem;
+}
+
+// canonical-layout byte offset of 8 k (16 B) at route r, unit v (of kTcK / 8) within a B buffer
 __device__ __forceinline__ int tc_off(int r, int v) { return (r >> 3) * kTcSbo + (v >> 1) * 256 + (v & 1) * 128 + (r & 7) * 16; }
 __device__ __forceinline__ uint64_t tc_desc(const void* p) {      // K-major, no swizzle, LBO 128 B, SBO kTcSbo
   return (uint64_t)((smem_u32(p) >> 4) & 0x3FFFu) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(kTcSbo >> 4) << 32) |
          (1ull << 46);
 }
-__device__ __forceinline__ void tc_mma_f16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+// D (tensor memory) += A (tensor memory) x B (shared memory descriptor)
+__device__ __forceinline__ void tc_mma_f16_ta(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}" ::"r"(d), "r"(a), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
 }
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
+}
+__device__ __forceinline__ void tc_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
 }
 __device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
@@ -238,16 +261,25 @@ __device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+// 2-D TMA tile load without an L2 hint: the weight rows are read again by the expert's other align blocks
+__device__ __forceinline__ void tc_tma_load(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
 
 template <bool UP>
-__global__ void __launch_bounds__(kGT, 2) moe_grouped_tc_kernel(const GroupedArgs a) {
+__global__ void __launch_bounds__(kTcThreads, 2)
+moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  uint8_t* As = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* Bs = As + 2 * kTcA;                                    // buffer b: As + b kTcA, Bs + b kTcB
-  float* res = reinterpret_cast<float*>(As);                      // [128 rows][kTcRS] after the last stage
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* Bs = ring + kTcNS * kTcSlot;                           // buffer b at Bs + b kTcB
+  uint8_t* scales = Bs + 2 * kTcB;                                // [128 rows][tc_scale_stride(K)]
+  float* res = reinterpret_cast<float*>(ring);                    // [128 rows][kTcRS] after the last stage
   __shared__ int s_route[kGB], s_row[kGB];
   __shared__ uint32_t s_taddr;
-  __shared__ __align__(8) uint64_t s_bar[2];
+  __shared__ __align__(8) uint64_t s_full[kTcNS], s_empty[kTcNS], s_mma[2];
 
   pdl_wait();
   const int blk = blockIdx.x, tile = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -264,104 +296,132 @@ __global__ void __launch_bounds__(kGT, 2) moe_grouped_tc_kernel(const GroupedArg
     s_row[tid] = ok ? (UP ? route / a.topk : route) : -1;
   }
   if (tid == 0) {
-    mbar_init(&s_bar[0], 1);
-    mbar_init(&s_bar[1], 1);
+    for (int i = 0; i < kTcNS; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], kGW);
+    }
+    mbar_init(&s_mma[0], 1);
+    mbar_init(&s_mma[1], 1);
     fence_mbar_init();
   }
-  if (warp == 0) {                                                 // 64 tensor-memory columns: the accumulator
+  if (warp == 0) {                                                 // accumulator + two A buffers
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_taddr)),
-                 "r"(64u)
+                 "r"((uint32_t)kTcCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  __syncthreads();
-  const uint32_t tmem = s_taddr;
   auto wrow = [&](int r) {
     return UP ? (r < 64 ? tile * 64 + r : a.I + tile * 64 + (r - 64)) : tile * kGRows + r;
   };
-  const int nks = a.K / kTcK, cb = a.K / 2, sb = a.K / 16;
-  const uint8_t* We = a.W + (int64_t)e * a.N * cb;
+  const int nks = a.K / kTcK, sb = a.K / 16, sst = tc_scale_stride(a.K);
   const uint8_t* Se = a.S + (int64_t)e * a.N * sb;
-  // kind::f16 instruction descriptor: fp32 accumulator, f16 A and B, both K-major, N = 64, M = 128
-  const uint32_t idesc = (1u << 4) | ((uint32_t)(kGB >> 3) << 17) | ((uint32_t)(kGRows >> 4) << 24);
-  bool ok = true;
-  // this thread's pieces: weight chunk j (32 k) at row 8 (warp + 8 j) + lane % 8, chunk c = lane / 8 of the stage;
-  // activation unit j (8 k) at route 8 ((warp + 8 j) % 8) + lane % 8, unit 4 ((warp + 8 j) / 8) + lane / 8.
-  // (32-bit offsets within one expert's codes / scales: the entry bounds N K / 2 below 2^31)
-  const int l8 = lane & 7, c = lane >> 3;
-  int xrow[kTcXU];
-#pragma unroll
-  for (int j = 0; j < kTcXU; ++j) xrow[j] = s_row[8 * ((warp + 8 * j) & 7) + l8];
-  uint4 wc[kTcWU], xv[kTcXU];
-  uint32_t sc[kTcWU];
-  auto fetch = [&](int ks, uint4 (&w)[kTcWU], uint32_t (&s2)[kTcWU], uint4 (&x)[kTcXU]) {
-#pragma unroll
-    for (int j = 0; j < kTcWU; ++j) {
-      const int wr = wrow(8 * (warp + 8 * j) + l8);
-      w[j] = __ldg(reinterpret_cast<const uint4*>(We + (uint32_t)(wr * cb + ks * (kTcK / 2) + c * 16)));
-      s2[j] = __ldg(reinterpret_cast<const unsigned short*>(Se + (uint32_t)(wr * sb + ks * (kTcK / 16) + c * 2)));
-    }
-#pragma unroll
-    for (int j = 0; j < kTcXU; ++j) {
-      const int v = 4 * ((warp + 8 * j) >> 3) + c;
-      x[j] = xrow[j] >= 0 ? __ldg(reinterpret_cast<const uint4*>(a.xh + (int64_t)xrow[j] * a.K + ks * kTcK + v * 8))
-                          : make_uint4(0u, 0u, 0u, 0u);
-    }
-  };
-  fetch(0, wc, sc, xv);
-
-#pragma unroll 1
-  for (int ks = 0; ks < nks; ++ks) {
-    const int b = ks & 1;
-    uint4 wn[kTcWU], xn[kTcXU];
-    uint32_t sn[kTcWU];
-    if (ks + 1 < nks) fetch(ks + 1, wn, sn, xn);                   // the next stage's loads fly during this one
-    // buffer b was last read by the MMAs of stage ks - 2 (bounded wait on its barrier)
-    if (ks >= 2 && ok && !mbar_wait(&s_bar[b], (unsigned)(((ks >> 1) - 1) & 1), a.status)) ok = false;
-    uint8_t* Ab = As + b * kTcA;
-    uint8_t* Bb = Bs + b * kTcB;
-#pragma unroll
-    for (int j = 0; j < kTcWU; ++j) {
-      const int r = 8 * (warp + 8 * j) + l8;
-      const uint32_t sg = e4m3x2_to_f16x2(sc[j]);                  // scales of 16-k groups 2c, 2c + 1
-      const uint32_t wq[4] = {wc[j].x, wc[j].y, wc[j].z, wc[j].w};
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {                                // unit 4c + q: 8 k of group 2c + q / 2
-        const uint32_t s2 = q < 2 ? bcast_lo(sg) : bcast_hi(sg);
-        uint32_t o[4];
-        e2m1x8_to_f16x2(wq[q], o);
-        *reinterpret_cast<uint4*>(Ab + tc_off(r, 4 * c + q)) =
-            make_uint4(hmul2(o[0], s2), hmul2(o[1], s2), hmul2(o[2], s2), hmul2(o[3], s2));
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < kTcXU; ++j)
-      *reinterpret_cast<uint4*>(Bb + tc_off(8 * ((warp + 8 * j) & 7) + l8, 4 * ((warp + 8 * j) >> 3) + c)) = xv[j];
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic-proxy stores -> the tensor core
-    __syncthreads();
-    if (tid == 0) {
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-#pragma unroll 1
-      for (int s16 = 0; s16 < kTcK / 16; ++s16)
-        tc_mma_f16(tmem, tc_desc(Ab + s16 * 256), tc_desc(Bb + s16 * 256), idesc, (ks > 0 || s16 > 0) ? 1u : 0u);
-      tc_commit(&s_bar[b]);
-    }
-    if (ks + 1 < nks) {
-#pragma unroll
-      for (int j = 0; j < kTcWU; ++j) {
-        wc[j] = wn[j];
-        sc[j] = sn[j];
-      }
-#pragma unroll
-      for (int j = 0; j < kTcXU; ++j) xv[j] = xn[j];
+  if (warp < kGW) {                                                // this CTA's scale rows, once
+    const int wpr = sb / 4;
+    for (int idx = tid; idx < kGRows * wpr; idx += kGT) {
+      const int r = idx / wpr, wd = idx - r * wpr;
+      *reinterpret_cast<uint32_t*>(scales + r * sst + wd * 4) =
+          __ldg(reinterpret_cast<const unsigned int*>(Se + (uint32_t)(wrow(r) * sb + wd * 4)));
     }
   }
-  // the last commit covers every MMA of the tile (bounded wait)
-  if (ok && !mbar_wait(&s_bar[(nks - 1) & 1], (unsigned)(((nks - 1) >> 1) & 1), a.status)) ok = false;
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
-  // accumulator -> registers -> the result tile (over the decoded weights, which no MMA reads any more)
-  {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = s_taddr;
+  bool ok = true;
+
+  if (warp == kGW) {
+    // ---- producer: code boxes into the ring ----
+    if (lane == 0) {
+      const int y0 = e * a.N + (UP ? tile * 64 : tile * kGRows), y1 = e * a.N + (UP ? a.I + tile * 64 : tile * kGRows + 64);
+#pragma unroll 1
+      for (int ks = 0; ks < nks; ++ks) {
+        const int slot = ks % kTcNS;
+        if (ks >= kTcNS && !mbar_wait(&s_empty[slot], (unsigned)(((ks / kTcNS) - 1) & 1), a.status)) break;
+        uint8_t* dst = ring + slot * kTcSlot;
+        mbar_arrive_expect_tx(&s_full[slot], (unsigned)kTcSlot);
+        tc_tma_load(dst, &mc, ks * (kTcK / 2), y0, &s_full[slot]);
+        tc_tma_load(dst + kTcSlot / 2, &mc, ks * (kTcK / 2), y1, &s_full[slot]);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---- consumers ----
+    // decode: row r = 32 (warp % 4) + lane, k half h = warp / 4; activations: unit j at route
+    // 8 ((warp + 8 j) % 8) + lane % 8, 8-k unit 4 ((warp + 8 j) / 8) + lane / 8
+    const int r = 32 * (warp & 3) + lane, h = warp >> 2, sw = (r >> 1) & 3;
+    const uint32_t a_lane = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+    const int l8 = lane & 7, c = lane >> 3;
+    const uint32_t idesc = (1u << 4) | ((uint32_t)(kGB >> 3) << 17) | ((uint32_t)(kGRows >> 4) << 24);
+    int xrow[kTcXU];
+#pragma unroll
+    for (int j = 0; j < kTcXU; ++j) xrow[j] = s_row[8 * ((warp + 8 * j) & 7) + l8];
+    uint4 xv[kTcXU];
+    auto fetch = [&](int ks, uint4 (&x)[kTcXU]) {
+#pragma unroll
+      for (int j = 0; j < kTcXU; ++j) {
+        const int v = 4 * ((warp + 8 * j) >> 3) + c;
+        x[j] = xrow[j] >= 0 ? __ldg(reinterpret_cast<const uint4*>(a.xh + (int64_t)xrow[j] * a.K + ks * kTcK + v * 8))
+                            : make_uint4(0u, 0u, 0u, 0u);
+      }
+    };
+    fetch(0, xv);
+#pragma unroll 1
+    for (int ks = 0; ks < nks; ++ks) {
+      const int slot = ks % kTcNS, b = ks & 1;
+      uint4 xn[kTcXU];
+      if (ks + 1 < nks) fetch(ks + 1, xn);                         // the next stage's rows fly during this one
+      if (ok && !mbar_wait(&s_full[slot], (unsigned)((ks / kTcNS) & 1), a.status)) ok = false;
+      const uint8_t* cs = ring + slot * kTcSlot + r * 64;
+      const uint4 q0 = *reinterpret_cast<const uint4*>(cs + (((2 * h) ^ sw) << 4));
+      const uint4 q1 = *reinterpret_cast<const uint4*>(cs + (((2 * h + 1) ^ sw) << 4));
+      const uint32_t s4 = *reinterpret_cast<const uint32_t*>(scales + r * sst + ks * (kTcK / 16) + 4 * h);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[slot]);                  // this warp is done with the slot
+      uint32_t d[32];
+      {
+        const uint32_t s01 = e4m3x2_to_f16x2(s4 & 0xFFFFu), s23 = e4m3x2_to_f16x2(s4 >> 16);
+        const uint32_t wq[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {                              // 8 k per word; 16-k scale group q / 2
+          const uint32_t sg = q < 2 ? bcast_lo(s01) : q < 4 ? bcast_hi(s01) : q < 6 ? bcast_lo(s23) : bcast_hi(s23);
+          uint32_t o[4];
+          e2m1x8_to_f16x2(wq[q], o);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) d[4 * q + i] = hmul2(o[i], sg);
+        }
+      }
+      // buffer b was last read by the MMAs of stage ks - 2 (bounded wait on its barrier)
+      if (ks >= 2 && ok && !mbar_wait(&s_mma[b], (unsigned)(((ks >> 1) - 1) & 1), a.status)) ok = false;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      tc_st32(a_lane + (uint32_t)(64 + 64 * b + 32 * h), d);
+      uint8_t* Bb = Bs + b * kTcB;
+#pragma unroll
+      for (int j = 0; j < kTcXU; ++j)
+        *reinterpret_cast<uint4*>(Bb + tc_off(8 * ((warp + 8 * j) & 7) + l8, 4 * ((warp + 8 * j) >> 3) + c)) = xv[j];
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); // generic-proxy stores -> the tensor core
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      asm volatile("bar.sync 1, %0;" ::"n"(kGT) : "memory");       // the consumers only
+      if (tid == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll 1
+        for (int s16 = 0; s16 < kTcK / 16; ++s16)
+          tc_mma_f16_ta(tmem, tmem + (uint32_t)(64 + 64 * b + 8 * s16), tc_desc(Bb + s16 * 256), idesc,
+                        (ks > 0 || s16 > 0) ? 1u : 0u);
+        tc_commit(&s_mma[b]);
+      }
+      if (ks + 1 < nks) {
+#pragma unroll
+        for (int j = 0; j < kTcXU; ++j) xv[j] = xn[j];
+      }
+    }
+    // the last commit covers every MMA of the tile (bounded wait)
+    if (ok && !mbar_wait(&s_mma[(nks - 1) & 1], (unsigned)(((nks - 1) >> 1) & 1), a.status)) ok = false;
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  }
+  __syncthreads();
+  // accumulator -> registers -> the result tile (over the ring and B buffers, which nothing reads any more)
+  if (warp < kGW) {
     float v[32];
     tc_ld32(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(32 * (warp >> 2)), v);
     const int row = 32 * (warp & 3) + lane, col0 = 32 * (warp >> 2);
@@ -371,35 +431,49 @@ __global__ void __launch_bounds__(kGT, 2) moe_grouped_tc_kernel(const GroupedArg
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(64u) : "memory");
-  const float ge = a.g[e];
-  if (UP) {
-    for (int idx = tid; idx < 64 * kGB; idx += kGT) {
-      const int i = idx / 64, col = idx - i * 64, route = s_route[i];
-      if (route < 0) continue;
-      const float sc = ldexpf(ge, -a.shift[s_row[i]]);
-      const float gv = res[col * kTcRS + i] * sc, uv = res[(64 + col) * kTcRS + i] * sc;
-      const float silu = gv / (1.0f + expf(-gv));
-      a.out[(int64_t)route * a.ldo + tile * 64 + col] = __float2bfloat16_rn(silu * uv);
-    }
-  } else {
-    for (int idx = tid; idx < kGRows * kGB; idx += kGT) {
-      const int i = idx / kGRows, r = idx - i * kGRows, route = s_route[i];
-      if (route < 0) continue;
-      a.out[(int64_t)route * a.ldo + tile * kGRows + r] =
-          __float2bfloat16_rn(res[r * kTcRS + i] * ldexpf(ge, -a.shift[route]));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)kTcCols) : "memory");
+  if (warp < kGW) {
+    const float ge = a.g[e];
+    if (UP) {
+      for (int idx = tid; idx < 64 * kGB; idx += kGT) {
+        const int i = idx / 64, col = idx - i * 64, route = s_route[i];
+        if (route < 0) continue;
+        const float sc = ldexpf(ge, -a.shift[s_row[i]]);
+        const float gv = res[col * kTcRS + i] * sc, uv = res[(64 + col) * kTcRS + i] * sc;
+        const float silu = gv / (1.0f + expf(-gv));
+        a.out[(int64_t)route * a.ldo + tile * 64 + col] = __float2bfloat16_rn(silu * uv);
+      }
+    } else {
+      for (int idx = tid; idx < kGRows * kGB; idx += kGT) {
+        const int i = idx / kGRows, rr = idx - i * kGRows, route = s_route[i];
+        if (route < 0) continue;
+        a.out[(int64_t)route * a.ldo + tile * kGRows + rr] =
+            __float2bfloat16_rn(res[rr * kTcRS + i] * ldexpf(ge, -a.shift[route]));
+      }
     }
   }
   pdl_trigger();
 }
 
-template <bool UP, bool TC>
-static int grouped_launch(const GroupedArgs& a, int max_blocks, int tiles, int pdl, void* stream) {
-  auto kern = TC ? moe_grouped_tc_kernel<UP> : moe_grouped_kernel<UP>;
-  const int smem = (TC ? kTcSmem : kGSmem) + 1024;
+template <bool UP>
+static int grouped_launch_mma(const GroupedArgs& a, int max_blocks, int tiles, int pdl, void* stream) {
+  auto kern = moe_grouped_kernel<UP>;
+  const int smem = kGSmem + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return FLINT_ERR_LAUNCH;
   return launch(kern, dim3((unsigned)max_blocks, (unsigned)tiles), dim3(kGT), smem, stream, pdl, a);
+}
+
+template <bool UP>
+static int grouped_launch_tc(const GroupedArgs& a, int max_blocks, int tiles, int pdl, void* stream) {
+  CUtensorMap mc;                                                  // codes [E N rows][K/2 B], boxes of 64 rows x 64 B
+  int rc = encode_u8_2d_sw64(&mc, a.W, (uint64_t)(a.K / 2), (uint64_t)a.E * a.N, (uint64_t)(a.K / 2), 64u);
+  if (rc) return rc;
+  auto kern = moe_grouped_tc_kernel<UP>;
+  const int smem = tc_smem(a.K) + 1024;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return FLINT_ERR_LAUNCH;
+  return launch(kern, dim3((unsigned)max_blocks, (unsigned)tiles), dim3(kTcThreads), smem, stream, pdl, mc, a);
 }
 
 }  // namespace flint
@@ -432,12 +506,12 @@ static int grouped_entry(bool up, int tc, const void* xh, const int32_t* shift, 
   a.status = (unsigned*)workspace;
   if (up) {
     a.K = (int)H; a.N = (int)(2 * I); a.ldo = (int)I;
-    return tc ? grouped_launch<true, true>(a, (int)max_blocks, (int)(I / 64), pdl, stream)
-              : grouped_launch<true, false>(a, (int)max_blocks, (int)(I / 64), pdl, stream);
+    return tc ? grouped_launch_tc<true>(a, (int)max_blocks, (int)(I / 64), pdl, stream)
+              : grouped_launch_mma<true>(a, (int)max_blocks, (int)(I / 64), pdl, stream);
   }
   a.K = (int)I; a.N = (int)H; a.ldo = (int)H;
-  return tc ? grouped_launch<false, true>(a, (int)max_blocks, (int)(H / kGRows), pdl, stream)
-            : grouped_launch<false, false>(a, (int)max_blocks, (int)(H / kGRows), pdl, stream);
+  return tc ? grouped_launch_tc<false>(a, (int)max_blocks, (int)(H / kGRows), pdl, stream)
+            : grouped_launch_mma<false>(a, (int)max_blocks, (int)(H / kGRows), pdl, stream);
 }
 
 extern "C" int flint_moe_grouped_up(const void* xh, const int32_t* shift, const int32_t* sorted_ids,

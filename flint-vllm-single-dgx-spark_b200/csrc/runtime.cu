@@ -55,6 +55,21 @@ int encode_u8_2d(CUtensorMap* map, const void* base, uint64_t cols_bytes, uint64
   return r == CUDA_SUCCESS ? FLINT_OK : FLINT_ERR_ALIGN;
 }
 
+int encode_u8_2d_sw64(CUtensorMap* map, const void* base, uint64_t cols_bytes, uint64_t rows, uint64_t row_stride_bytes,
+                      uint32_t box_rows) {
+  auto fn = get_encode_fn();
+  if (!fn) return FLINT_ERR_DEVICE;
+  if (!aligned(base, 16) || row_stride_bytes % 16 != 0) return FLINT_ERR_ALIGN;
+  cuuint64_t dims[2] = {cols_bytes, rows};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {64u, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? FLINT_OK : FLINT_ERR_ALIGN;
+}
+
 int encode_u8_3d(CUtensorMap* map, const void* base, const uint64_t dims[3], const uint64_t strides_bytes[2],
                  const uint32_t box[3], bool swizzle128) {
   auto fn = get_encode_fn();
