@@ -182,40 +182,44 @@ __global__ void __launch_bounds__(kGT) moe_grouped_kernel(const GroupedArgs a) {
 }
 
 // ---- the same tile on the 5th-generation tensor cores (tcgen05: decoded weights and accumulator in tensor memory) ----
-// 8 consumer warps and 1 producer warp; K goes in stages of 128.
+// 8 consumer warps, a TMA warp and an MMA warp; K goes in stages of 128.
 //   producer (warp 8, one lane): the stage's code bytes of the CTA's 128 weight rows, 2 TMA boxes of 64 rows x 64 B
 //     with the 64-byte swizzle, into a 4-slot ring (full / empty mbarriers, bounded waits);
 //   consumer thread (warp w, lane l): weight row r = 32 (w % 4) + l, k half h = w / 4 of the stage.  It reads its 32
 //     code bytes (conflict-free under the swizzle) and its 4 E4M3 scales (loaded once per CTA into a padded array),
 //     decodes them to 32 f16 pairs and writes them with one tcgen05.st into its own tensor-memory lane (warp w owns
-//     lanes 32 (w % 4) ..): the MMA's A operand, two stage buffers of 64 columns.  The 64 routes' f16 activations
-//     go through registers (fetched one stage ahead) into one of two shared-memory buffers in the K-major no-swizzle
+//     lanes 32 (w % 4) ..): the MMA's A operand, three stage buffers of 64 columns.  The 64 routes' f16 activations
+//     go through registers (fetched one stage ahead) into one of three shared-memory buffers in the K-major no-swizzle
 //     canonical layout (8-row x 16-byte core matrices: route group i at i * 2048 B, 16-k step s at s * 256 B, k half
 //     j at j * 128 B); lane l takes route l % 8 of an 8-route group, so each 8-lane store phase fills one 128-byte
 //     line;
-//   one thread then issues the stage's 8 tcgen05.mma kind::f16 (A from tensor memory, B from shared memory; M = 128
-//     weight rows, N = 64 routes, K = 16) into the 128 x 64 fp32 accumulator (tensor-memory columns 0..63) and
-//     commits them to the buffer's mbarrier; a buffer is written again two stages later, after that barrier.
-// 256 tensor-memory columns and ~80 KB of shared memory per CTA: two CTAs per SM.  The epilogue reads the
+//     each warp then arrives on the buffer's ready mbarrier (no CTA-wide barrier per stage);
+//   MMA warp (warp 9, one lane): waits for the buffer's 8 arrivals, issues the stage's 8 tcgen05.mma kind::f16 (A
+//     from tensor memory, B from shared memory; M = 128 weight rows, N = 64 routes, K = 16) into the 128 x 64 fp32
+//     accumulator (tensor-memory columns 0..63) and commits them to the buffer's done mbarrier; a buffer is written
+//     again three stages later, after that barrier.
+// 256 tensor-memory columns and ~97 KB of shared memory per CTA: two CTAs per SM.  The epilogue reads the
 // accumulator with tcgen05.ld.  Each product is exact; the tensor core's fp32 sums run in their own order (within
 // the activation tolerance of the mma.sync tile and of the oracle).
 constexpr int kTcK = 128;                           // k per stage
 constexpr int kTcSbo = (kTcK / 16) * 256;           // B: bytes between 8-route groups
 constexpr int kTcB = kGB * kTcK * 2;                // 16 KB activations per buffer
+constexpr int kTcNB = 3;                            // A (tensor memory) and B (shared memory) stage buffers
 constexpr int kTcNS = 4;                            // code ring slots
 constexpr int kTcSlot = kGRows * (kTcK / 2);        // 8 KB of codes per slot (two 4 KB boxes)
 constexpr int kTcXU = kGB * (kTcK / 8) / kGT;       // activation units of 8 k per thread per stage
 constexpr int kTcRS = kGB + 1;                      // fp32 stride of a result row (conflict-free column walks)
-constexpr int kTcThreads = kGT + 32;                // + the producer warp
-constexpr int kTcCols = 256;                        // tensor memory: accumulator 0..63, A buffers at 64 and 128
+constexpr int kTcThreads = kGT + 64;                // + the TMA warp and the MMA warp
+constexpr int kTcCols = 256;                        // tensor memory: accumulator 0..63, A buffers at 64, 128, 192
+static_assert(64 + 64 * kTcNB <= kTcCols, "A buffers fit the allocation");
 constexpr int kTcMinSmem = 80 * 1024;               // keeps a third CTA (and its tensor-memory request) off the SM
 static_assert(kTcXU == 4 && kGW == 8 && kGRows == 128, "lane maps: 8 routes x 4 units per warp, 2 threads per row");
-static_assert(kTcNS * kTcSlot + 2 * kTcB >= kGRows * kTcRS * 4, "result tile must fit over the ring and B buffers");
+static_assert(kTcNS * kTcSlot + kTcNB * kTcB >= kGRows * kTcRS * 4, "result tile must fit over the ring and B buffers");
 
 // scale bytes per row in shared memory: K/16 + 4 (an odd number of words, so 32 rows read in one wavefront)
 __host__ __device__ constexpr int tc_scale_stride(int K) { return K / 16 + 4; }
 static int tc_smem(int K) {
-  const int need = kTcNS * kTcSlot + 2 * kTcB + ((kGRows * tc_scale_stride(K) + 15) / 16) * 16;
+  const int need = kTcNS * kTcSlot + kTcNB * kTcB + ((kGRows * tc_scale_stride(K) + 15) / 16) * 16;
   return need > kTcMinSmem ? need : kTcMinSmem;
 }
 
@@ -275,11 +279,11 @@ moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs 
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* Bs = ring + kTcNS * kTcSlot;                           // buffer b at Bs + b kTcB
-  uint8_t* scales = Bs + 2 * kTcB;                                // [128 rows][tc_scale_stride(K)]
+  uint8_t* scales = Bs + kTcNB * kTcB;                            // [128 rows][tc_scale_stride(K)]
   float* res = reinterpret_cast<float*>(ring);                    // [128 rows][kTcRS] after the last stage
   __shared__ int s_route[kGB], s_row[kGB];
   __shared__ uint32_t s_taddr;
-  __shared__ __align__(8) uint64_t s_full[kTcNS], s_empty[kTcNS], s_mma[2];
+  __shared__ __align__(8) uint64_t s_full[kTcNS], s_empty[kTcNS], s_ready[kTcNB], s_mma[kTcNB];
 
   pdl_wait();
   const int blk = blockIdx.x, tile = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -300,8 +304,10 @@ moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs 
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], kGW);
     }
-    mbar_init(&s_mma[0], 1);
-    mbar_init(&s_mma[1], 1);
+    for (int i = 0; i < kTcNB; ++i) {
+      mbar_init(&s_ready[i], kGW);
+      mbar_init(&s_mma[i], 1);
+    }
     fence_mbar_init();
   }
   if (warp == 0) {                                                 // accumulator + two A buffers
@@ -344,6 +350,24 @@ moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs 
       }
     }
     __syncwarp();
+  } else if (warp == kGW + 1) {
+    // ---- MMA issue: one lane, each stage after its buffer's 8 consumer-warp arrivals ----
+    if (lane == 0) {
+      const uint32_t idesc = (1u << 4) | ((uint32_t)(kGB >> 3) << 17) | ((uint32_t)(kGRows >> 4) << 24);
+#pragma unroll 1
+      for (int ks = 0; ks < nks; ++ks) {
+        const int b = ks % kTcNB;
+        if (!mbar_wait(&s_ready[b], (unsigned)((ks / kTcNB) & 1), a.status)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint8_t* Bb = Bs + b * kTcB;
+#pragma unroll 1
+        for (int s16 = 0; s16 < kTcK / 16; ++s16)
+          tc_mma_f16_ta(tmem, tmem + (uint32_t)(64 + 64 * b + 8 * s16), tc_desc(Bb + s16 * 256), idesc,
+                        (ks > 0 || s16 > 0) ? 1u : 0u);
+        tc_commit(&s_mma[b]);
+      }
+    }
+    __syncwarp();
   } else {
     // ---- consumers ----
     // decode: row r = 32 (warp % 4) + lane, k half h = warp / 4; activations: unit j at route
@@ -351,7 +375,6 @@ moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs 
     const int r = 32 * (warp & 3) + lane, h = warp >> 2, sw = (r >> 1) & 3;
     const uint32_t a_lane = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
     const int l8 = lane & 7, c = lane >> 3;
-    const uint32_t idesc = (1u << 4) | ((uint32_t)(kGB >> 3) << 17) | ((uint32_t)(kGRows >> 4) << 24);
     int xrow[kTcXU];
 #pragma unroll
     for (int j = 0; j < kTcXU; ++j) xrow[j] = s_row[8 * ((warp + 8 * j) & 7) + l8];
@@ -367,7 +390,7 @@ moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs 
     fetch(0, xv);
 #pragma unroll 1
     for (int ks = 0; ks < nks; ++ks) {
-      const int slot = ks % kTcNS, b = ks & 1;
+      const int slot = ks % kTcNS, b = ks % kTcNB;
       uint4 xn[kTcXU];
       if (ks + 1 < nks) fetch(ks + 1, xn);                         // the next stage's rows fly during this one
       if (ok && !mbar_wait(&s_full[slot], (unsigned)((ks / kTcNS) & 1), a.status)) ok = false;
@@ -390,8 +413,8 @@ moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs 
           for (int i = 0; i < 4; ++i) d[4 * q + i] = hmul2(o[i], sg);
         }
       }
-      // buffer b was last read by the MMAs of stage ks - 2 (bounded wait on its barrier)
-      if (ks >= 2 && ok && !mbar_wait(&s_mma[b], (unsigned)(((ks >> 1) - 1) & 1), a.status)) ok = false;
+      // buffer b was last read by the MMAs of stage ks - kTcNB (bounded wait on its barrier)
+      if (ks >= kTcNB && ok && !mbar_wait(&s_mma[b], (unsigned)(((ks / kTcNB) - 1) & 1), a.status)) ok = false;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       tc_st32(a_lane + (uint32_t)(64 + 64 * b + 32 * h), d);
       uint8_t* Bb = Bs + b * kTcB;
@@ -401,22 +424,15 @@ moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs 
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); // generic-proxy stores -> the tensor core
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-      asm volatile("bar.sync 1, %0;" ::"n"(kGT) : "memory");       // the consumers only
-      if (tid == 0) {
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-#pragma unroll 1
-        for (int s16 = 0; s16 < kTcK / 16; ++s16)
-          tc_mma_f16_ta(tmem, tmem + (uint32_t)(64 + 64 * b + 8 * s16), tc_desc(Bb + s16 * 256), idesc,
-                        (ks > 0 || s16 > 0) ? 1u : 0u);
-        tc_commit(&s_mma[b]);
-      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_ready[b]);                     // this warp's share of the stage is in place
       if (ks + 1 < nks) {
 #pragma unroll
         for (int j = 0; j < kTcXU; ++j) xv[j] = xn[j];
       }
     }
     // the last commit covers every MMA of the tile (bounded wait)
-    if (ok && !mbar_wait(&s_mma[(nks - 1) & 1], (unsigned)(((nks - 1) >> 1) & 1), a.status)) ok = false;
+    if (ok && !mbar_wait(&s_mma[(nks - 1) % kTcNB], (unsigned)(((nks - 1) / kTcNB) & 1), a.status)) ok = false;
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   }
   __syncthreads();

@@ -114,14 +114,15 @@ def unpack_marlin(weight, weight_scale, global_scale):
     return (P[0], S[0], gs[0]) if single else (P, S, gs)
 
 
-def grouped_moe(x, topk_ids, topk_weights, w: "DecodeWeights", block_size: int = 64, tensor_cores: bool = False):
+def grouped_moe(x, topk_ids, topk_weights, w: "DecodeWeights", block_size: int = 64, tensor_cores: bool = True):
     """Prefill MoE of a prompt (the Flint PR's grouped_moe, patch:4093-4212, runs FlashInfer's grouped GEMMs; this
     runs the library's NVFP4 tiles): x bf16 [T, H] (normalised), topk_ids [T, topk], topk_weights fp32 [T, topk] ->
     out bf16 [T, H] = bf16(sum_s tw[t, s] * y[t, s]) in slot order, y the routed expert's output row.  The routes are
     grouped by expert with the deterministic align (blocks of 64), each decoded weight fragment serves a block's 64
     routes; gate/up, SwiGLU and down keep the decode kernels' rounding points (fp32 sums in another order).  The
     routed experts only (a shared expert or dense layer is added by the caller, as for the decode path).
-    tensor_cores: the tcgen05 tiles (accumulator in tensor memory) instead of mma.sync."""
+    tensor_cores: the tcgen05 tiles (decoded weights and accumulator in tensor memory; the default, the faster
+    form) or, with False, the mma.sync tiles."""
     from .patch_align import align_sizes
     ops = torch.ops.flint_b200
     T, H = x.shape

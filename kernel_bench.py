@@ -118,7 +118,7 @@ def main(argv=None):
     ap.add_argument("--rows", type=int, default=151552)
     ap.add_argument("--cols", type=int, default=2048)
     ap.add_argument("--tokens", type=int, default=6057, help="grouped_moe: prompt tokens")
-    ap.add_argument("--variants", default="grouped_moe,grouped_moe_tcgen05,decode_kernels_8_token_chunks",
+    ap.add_argument("--variants", default="grouped_moe_tcgen05,grouped_moe_mma_sync,decode_kernels_8_token_chunks",
                     help="grouped_moe: comma-separated variants to time")
     ap.add_argument("--lib", default=None, help="load this build of libflint_b200.so (e.g. an instrumented one)")
     ap.add_argument("--timeline", action="store_true", help="print the kernel's phase stamps (instrumented build)")
@@ -207,7 +207,7 @@ def time_grouped_moe(args):
             fm.moe_down(a, None, ids[t0:t0 + 8], tw[t0:t0 + 8], w)
 
     res = {}
-    variants = {"grouped_moe": lambda: fm.grouped_moe(x, ids, tw, w),
+    variants = {"grouped_moe_mma_sync": lambda: fm.grouped_moe(x, ids, tw, w, tensor_cores=False),
                 "grouped_moe_tcgen05": lambda: fm.grouped_moe(x, ids, tw, w, tensor_cores=True),
                 "decode_kernels_8_token_chunks": chunks}
     for name in args.variants.split(","):

@@ -24,7 +24,7 @@ def _routes(rng, T, E, topk, skew):
     return np.stack([rng.choice(E, topk, replace=False, p=p) for _ in range(T)]).astype(np.int32)
 
 
-def _grouped_steps(x, ids, tw, w):
+def _grouped_steps(x, ids, tw, w, tensor_cores):
     """The shim's steps, keeping the per-route activations for the check."""
     from flint_b200.patch_align import align_sizes
     ops = torch.ops.flint_b200
@@ -40,14 +40,15 @@ def _grouped_steps(x, ids, tw, w):
     sx = torch.empty((T,), dtype=torch.int32, device="cuda")
     ops.rows_to_f16(x, xh, sx)
     act = torch.full((numel, w.I), float("nan"), dtype=torch.bfloat16, device="cuda")
-    ops.moe_grouped_up(xh, sx, sorted_ids, expert_ids, ntp, numel, k, w.w13, w.s13, w.g13, act, 0)
+    ops.moe_grouped_up(xh, sx, sorted_ids, expert_ids, ntp, numel, k, w.w13, w.s13, w.g13, act, int(tensor_cores))
     return act
 
 
 @needs_cuda
+@pytest.mark.parametrize("tensor_cores", [True, False], ids=["tcgen05", "mma_sync"])
 @pytest.mark.parametrize("cfg,T,skew", [(BASE, 40, False), (BASE, 150, True), (FLINT, 70, False)],
                          ids=["base_40", "base_150_skewed", "flint_70"])
-def test_grouped_moe_vs_oracle_and_decode_kernels(fb, cfg, T, skew):
+def test_grouped_moe_vs_oracle_and_decode_kernels(fb, cfg, T, skew, tensor_cores):
     from flint_b200 import fp4moe_decode as fm
     rng = np.random.default_rng(4093 + T)
     H, E, topk, I = cfg["H"], 32, cfg["topk"], cfg["I"]
@@ -57,8 +58,8 @@ def test_grouped_moe_vs_oracle_and_decode_kernels(fb, cfg, T, skew):
     tw = rng.dirichlet(np.ones(topk), size=T).astype(np.float32)
     xn = bf16(rng, (T, H))
     x, ids_d, tw_d = dev_bf16(xn), to_dev(ids), to_dev(tw)
-    act = _grouped_steps(x, ids_d, tw_d, w)
-    out = fm.grouped_moe(x, ids_d, tw_d, w)
+    act = _grouped_steps(x, ids_d, tw_d, w, tensor_cores)
+    out = fm.grouped_moe(x, ids_d, tw_d, w, tensor_cores=tensor_cores)
     torch.cuda.synchronize()
     act_h = host(act)
     assert not np.isnan(act_h).any(), "a route's activation row was not written"
@@ -73,7 +74,7 @@ def test_grouped_moe_vs_oracle_and_decode_kernels(fb, cfg, T, skew):
     torch.cuda.synchronize()
     assert_bf16_close(host(out), host(torch.cat(ref)), rel=2.0 ** -6, abs_frac=4e-3, what="grouped vs decode kernels")
     # deterministic: the same prompt again gives the same bits
-    out2 = fm.grouped_moe(x, ids_d, tw_d, w)
+    out2 = fm.grouped_moe(x, ids_d, tw_d, w, tensor_cores=tensor_cores)
     torch.cuda.synchronize()
     np.testing.assert_array_equal(host(out2), host(out))
 
