@@ -299,7 +299,21 @@ moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs 
     s_route[tid] = ok ? route : -1;
     s_row[tid] = ok ? (UP ? route / a.topk : route) : -1;
   }
-  if (tid == 0) {
+  auto wrow = [&](int r) {
+    return UP ? (r < 64 ? tile * 64 + r : a.I + tile * 64 + (r - 64)) : tile * kGRows + r;
+  };
+  const int nks = a.K / kTcK, sb = a.K / 16, sst = tc_scale_stride(a.K);
+  const uint8_t* Se = a.S + (int64_t)e * a.N * sb;
+  const int y0 = e * a.N + (UP ? tile * 64 : tile * kGRows), y1 = e * a.N + (UP ? a.I + tile * 64 : tile * kGRows + 64);
+  const int npre = nks < kTcNS ? nks : kTcNS;
+  auto produce = [&](int ks) {                                     // one stage's two code boxes
+    const int slot = ks % kTcNS;
+    uint8_t* dst = ring + slot * kTcSlot;
+    mbar_arrive_expect_tx(&s_full[slot], (unsigned)kTcSlot);
+    tc_tma_load(dst, &mc, ks * (kTcK / 2), y0, &s_full[slot]);
+    tc_tma_load(dst + kTcSlot / 2, &mc, ks * (kTcK / 2), y1, &s_full[slot]);
+  };
+  if (warp == kGW && lane == 0) {                                  // barriers, then the first stages right away
     for (int i = 0; i < kTcNS; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], kGW);
@@ -309,19 +323,35 @@ moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs 
       mbar_init(&s_mma[i], 1);
     }
     fence_mbar_init();
+    for (int ks = 0; ks < npre; ++ks) produce(ks);
   }
-  if (warp == 0) {                                                 // accumulator + two A buffers
+  if (warp == 0) {                                                 // accumulator + three A buffers
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_taddr)),
                  "r"((uint32_t)kTcCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  auto wrow = [&](int r) {
-    return UP ? (r < 64 ? tile * 64 + r : a.I + tile * 64 + (r - 64)) : tile * kGRows + r;
+  // consumers' activation units: unit j at route 8 ((warp + 8 j) % 8) + lane % 8, 8-k unit 4 ((warp + 8 j) / 8) +
+  // lane / 8; the route rows come straight from the align output, so the first stage's loads start now
+  const int l8 = lane & 7, c = lane >> 3;
+  int xrow[kTcXU];
+  uint4 xv[kTcXU];
+  auto fetch = [&](int ks, uint4 (&x)[kTcXU]) {
+#pragma unroll
+    for (int j = 0; j < kTcXU; ++j) {
+      const int v = 4 * ((warp + 8 * j) >> 3) + c;
+      x[j] = xrow[j] >= 0 ? __ldg(reinterpret_cast<const uint4*>(a.xh + (int64_t)xrow[j] * a.K + ks * kTcK + v * 8))
+                          : make_uint4(0u, 0u, 0u, 0u);
+    }
   };
-  const int nks = a.K / kTcK, sb = a.K / 16, sst = tc_scale_stride(a.K);
-  const uint8_t* Se = a.S + (int64_t)e * a.N * sb;
-  if (warp < kGW) {                                                // this CTA's scale rows, once
+  if (warp < kGW) {
+#pragma unroll
+    for (int j = 0; j < kTcXU; ++j) {
+      const int route = __ldg(a.sorted_ids + blk * kGB + 8 * ((warp + 8 * j) & 7) + l8);
+      xrow[j] = route >= 0 && route < a.numel ? (UP ? route / a.topk : route) : -1;
+    }
+    fetch(0, xv);
+    // this CTA's scale rows, once
     const int wpr = sb / 4;
     for (int idx = tid; idx < kGRows * wpr; idx += kGT) {
       const int r = idx / wpr, wd = idx - r * wpr;
@@ -338,15 +368,10 @@ moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs 
   if (warp == kGW) {
     // ---- producer: code boxes into the ring ----
     if (lane == 0) {
-      const int y0 = e * a.N + (UP ? tile * 64 : tile * kGRows), y1 = e * a.N + (UP ? a.I + tile * 64 : tile * kGRows + 64);
 #pragma unroll 1
-      for (int ks = 0; ks < nks; ++ks) {
-        const int slot = ks % kTcNS;
-        if (ks >= kTcNS && !mbar_wait(&s_empty[slot], (unsigned)(((ks / kTcNS) - 1) & 1), a.status)) break;
-        uint8_t* dst = ring + slot * kTcSlot;
-        mbar_arrive_expect_tx(&s_full[slot], (unsigned)kTcSlot);
-        tc_tma_load(dst, &mc, ks * (kTcK / 2), y0, &s_full[slot]);
-        tc_tma_load(dst + kTcSlot / 2, &mc, ks * (kTcK / 2), y1, &s_full[slot]);
+      for (int ks = npre; ks < nks; ++ks) {
+        if (!mbar_wait(&s_empty[ks % kTcNS], (unsigned)(((ks / kTcNS) - 1) & 1), a.status)) break;
+        produce(ks);
       }
     }
     __syncwarp();
@@ -370,24 +395,9 @@ moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs 
     __syncwarp();
   } else {
     // ---- consumers ----
-    // decode: row r = 32 (warp % 4) + lane, k half h = warp / 4; activations: unit j at route
-    // 8 ((warp + 8 j) % 8) + lane % 8, 8-k unit 4 ((warp + 8 j) / 8) + lane / 8
+    // decode: row r = 32 (warp % 4) + lane, k half h = warp / 4
     const int r = 32 * (warp & 3) + lane, h = warp >> 2, sw = (r >> 1) & 3;
     const uint32_t a_lane = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
-    const int l8 = lane & 7, c = lane >> 3;
-    int xrow[kTcXU];
-#pragma unroll
-    for (int j = 0; j < kTcXU; ++j) xrow[j] = s_row[8 * ((warp + 8 * j) & 7) + l8];
-    uint4 xv[kTcXU];
-    auto fetch = [&](int ks, uint4 (&x)[kTcXU]) {
-#pragma unroll
-      for (int j = 0; j < kTcXU; ++j) {
-        const int v = 4 * ((warp + 8 * j) >> 3) + c;
-        x[j] = xrow[j] >= 0 ? __ldg(reinterpret_cast<const uint4*>(a.xh + (int64_t)xrow[j] * a.K + ks * kTcK + v * 8))
-                            : make_uint4(0u, 0u, 0u, 0u);
-      }
-    };
-    fetch(0, xv);
 #pragma unroll 1
     for (int ks = 0; ks < nks; ++ks) {
       const int slot = ks % kTcNS, b = ks % kTcNB;
@@ -436,20 +446,30 @@ moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs 
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   }
   __syncthreads();
-  // accumulator -> registers -> the result tile (over the ring and B buffers, which nothing reads any more)
+  // accumulator -> registers: thread (warp, lane) holds weight row 32 (warp % 4) + lane for routes 32 (warp / 4) ..
+  const float ge = a.g[e];
   if (warp < kGW) {
     float v[32];
     tc_ld32(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(32 * (warp >> 2)), v);
     const int row = 32 * (warp & 3) + lane, col0 = 32 * (warp >> 2);
+    if (UP) {                                                      // gate and up rows meet through shared memory
 #pragma unroll
-    for (int i = 0; i < 32; ++i) res[row * kTcRS + col0 + i] = ok ? v[i] : 0.f;
+      for (int i = 0; i < 32; ++i) res[row * kTcRS + col0 + i] = ok ? v[i] : 0.f;
+    } else {                                                       // down: straight out, 64 B per warp store
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int route = s_route[col0 + i];
+        if (route >= 0)
+          a.out[(int64_t)route * a.ldo + tile * kGRows + row] =
+              __float2bfloat16_rn((ok ? v[i] : 0.f) * ldexpf(ge, -a.shift[route]));
+      }
+    }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 0)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)kTcCols) : "memory");
   if (warp < kGW) {
-    const float ge = a.g[e];
     if (UP) {
       for (int idx = tid; idx < 64 * kGB; idx += kGT) {
         const int i = idx / 64, col = idx - i * 64, route = s_route[i];
@@ -458,13 +478,6 @@ moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs 
         const float gv = res[col * kTcRS + i] * sc, uv = res[(64 + col) * kTcRS + i] * sc;
         const float silu = gv / (1.0f + expf(-gv));
         a.out[(int64_t)route * a.ldo + tile * 64 + col] = __float2bfloat16_rn(silu * uv);
-      }
-    } else {
-      for (int idx = tid; idx < kGRows * kGB; idx += kGT) {
-        const int i = idx / kGRows, rr = idx - i * kGRows, route = s_route[i];
-        if (route < 0) continue;
-        a.out[(int64_t)route * a.ldo + tile * kGRows + rr] =
-            __float2bfloat16_rn(res[rr * kTcRS + i] * ldexpf(ge, -a.shift[route]));
       }
     }
   }
