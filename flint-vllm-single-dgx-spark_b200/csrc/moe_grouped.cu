@@ -286,7 +286,8 @@ moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs 
   __shared__ __align__(8) uint64_t s_full[kTcNS], s_empty[kTcNS], s_ready[kTcNB], s_mma[kTcNB];
 
   pdl_wait();
-  const int blk = blockIdx.x, tile = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // tiles fastest: the CTAs of one align block run together and share its route rows in L2
+  const int blk = blockIdx.y, tile = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (blk * kGB >= __ldg(a.ntp)) return;
   const int e = a.expert_ids[blk];
   if (e < 0 || e >= a.E) {
@@ -502,7 +503,7 @@ static int grouped_launch_tc(const GroupedArgs& a, int max_blocks, int tiles, in
   const int smem = tc_smem(a.K) + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return FLINT_ERR_LAUNCH;
-  return launch(kern, dim3((unsigned)max_blocks, (unsigned)tiles), dim3(kTcThreads), smem, stream, pdl, mc, a);
+  return launch(kern, dim3((unsigned)tiles, (unsigned)max_blocks), dim3(kTcThreads), smem, stream, pdl, mc, a);
 }
 
 }  // namespace flint
