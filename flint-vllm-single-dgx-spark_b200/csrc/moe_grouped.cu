@@ -189,7 +189,8 @@ __global__ void __launch_bounds__(kGT) moe_grouped_kernel(const GroupedArgs a) {
 //     code bytes (conflict-free under the swizzle) and its 4 E4M3 scales (loaded once per CTA into a padded array),
 //     decodes them to 32 f16 pairs and writes them with one tcgen05.st into its own tensor-memory lane (warp w owns
 //     lanes 32 (w % 4) ..): the MMA's A operand, three stage buffers of 64 columns.  The 64 routes' f16 activations
-//     go through registers (fetched one stage ahead) into one of three shared-memory buffers in the K-major no-swizzle
+//     are copied by cp.async (one stage ahead, zeros for padding routes) into one of three shared-memory buffers in
+//     the K-major no-swizzle
 //     canonical layout (8-row x 16-byte core matrices: route group i at i * 2048 B, 16-k step s at s * 256 B, k half
 //     j at j * 128 B); lane l takes route l % 8 of an 8-route group, so each 8-lane store phase fills one 128-byte
 //     line;
@@ -265,6 +266,14 @@ __device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+// 16-byte global -> shared copy that fills zeros when `valid` is false (src-size 0: nothing is read)
+__device__ __forceinline__ void tc_cp_async16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void tc_cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void tc_cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
 // 2-D TMA tile load without an L2 hint: the weight rows are read again by the expert's other align blocks
 __device__ __forceinline__ void tc_tma_load(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
@@ -336,14 +345,15 @@ moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs 
   // lane / 8; the route rows come straight from the align output, so the first stage's loads start now
   const int l8 = lane & 7, c = lane >> 3;
   int xrow[kTcXU];
-  uint4 xv[kTcXU];
-  auto fetch = [&](int ks, uint4 (&x)[kTcXU]) {
+  auto fetch = [&](int ks) {                                       // one cp.async group per stage
+    uint8_t* Bb = Bs + (ks % kTcNB) * kTcB;
 #pragma unroll
     for (int j = 0; j < kTcXU; ++j) {
       const int v = 4 * ((warp + 8 * j) >> 3) + c;
-      x[j] = xrow[j] >= 0 ? __ldg(reinterpret_cast<const uint4*>(a.xh + (int64_t)xrow[j] * a.K + ks * kTcK + v * 8))
-                          : make_uint4(0u, 0u, 0u, 0u);
+      const __half* src = a.xh + (xrow[j] >= 0 ? (int64_t)xrow[j] * a.K + ks * kTcK + v * 8 : 0);
+      tc_cp_async16(Bb + tc_off(8 * ((warp + 8 * j) & 7) + l8, v), src, xrow[j] >= 0);
     }
+    tc_cp_async_commit();
   };
   if (warp < kGW) {
 #pragma unroll
@@ -351,7 +361,7 @@ moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs 
       const int route = __ldg(a.sorted_ids + blk * kGB + 8 * ((warp + 8 * j) & 7) + l8);
       xrow[j] = route >= 0 && route < a.numel ? (UP ? route / a.topk : route) : -1;
     }
-    fetch(0, xv);
+    fetch(0);
     // this CTA's scale rows, once
     const int wpr = sb / 4;
     for (int idx = tid; idx < kGRows * wpr; idx += kGT) {
@@ -402,8 +412,12 @@ moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs 
 #pragma unroll 1
     for (int ks = 0; ks < nks; ++ks) {
       const int slot = ks % kTcNS, b = ks % kTcNB;
-      uint4 xn[kTcXU];
-      if (ks + 1 < nks) fetch(ks + 1, xn);                         // the next stage's rows fly during this one
+      // buffers: B of stage ks + 1 and A of stage ks were last read by the MMAs of stages ks - 2 and ks - 3; the
+      // commit of stage ks - 2 covers both (bounded wait)
+      if (ks >= 2 && ok && !mbar_wait(&s_mma[(ks - 2) % kTcNB], (unsigned)(((ks - 2) / kTcNB) & 1), a.status)) ok = false;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      if (ks + 1 < nks) fetch(ks + 1);                             // the next stage's rows fly during this one
+      else tc_cp_async_commit();                                   // (an empty group keeps the count uniform)
       if (ok && !mbar_wait(&s_full[slot], (unsigned)((ks / kTcNS) & 1), a.status)) ok = false;
       const uint8_t* cs = ring + slot * kTcSlot + r * 64;
       const uint4 q0 = *reinterpret_cast<const uint4*>(cs + (((2 * h) ^ sw) << 4));
@@ -424,23 +438,13 @@ moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs 
           for (int i = 0; i < 4; ++i) d[4 * q + i] = hmul2(o[i], sg);
         }
       }
-      // buffer b was last read by the MMAs of stage ks - kTcNB (bounded wait on its barrier)
-      if (ks >= kTcNB && ok && !mbar_wait(&s_mma[b], (unsigned)(((ks / kTcNB) - 1) & 1), a.status)) ok = false;
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       tc_st32(a_lane + (uint32_t)(64 + 64 * b + 32 * h), d);
-      uint8_t* Bb = Bs + b * kTcB;
-#pragma unroll
-      for (int j = 0; j < kTcXU; ++j)
-        *reinterpret_cast<uint4*>(Bb + tc_off(8 * ((warp + 8 * j) & 7) + l8, 4 * ((warp + 8 * j) >> 3) + c)) = xv[j];
+      tc_cp_async_wait1();                                         // this stage's rows are in place
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); // generic-proxy stores -> the tensor core
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_ready[b]);                     // this warp's share of the stage is in place
-      if (ks + 1 < nks) {
-#pragma unroll
-        for (int j = 0; j < kTcXU; ++j) xv[j] = xn[j];
-      }
     }
     // the last commit covers every MMA of the tile (bounded wait)
     if (ok && !mbar_wait(&s_mma[(nks - 1) % kTcNB], (unsigned)(((nks - 1) / kTcNB) & 1), a.status)) ok = false;
