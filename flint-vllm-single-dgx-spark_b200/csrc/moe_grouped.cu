@@ -80,7 +80,8 @@ __global__ void __launch_bounds__(kGT) moe_grouped_kernel(const GroupedArgs a) {
   __shared__ int s_route[kGB], s_row[kGB];
 
   pdl_wait();
-  const int blk = blockIdx.x, tile = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // tiles fastest: the CTAs of one align block run together and share its route rows in L2
+  const int blk = blockIdx.y, tile = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (blk * kGB >= __ldg(a.ntp)) return;                            // past the padded routes
   const int e = a.expert_ids[blk];
   if (e < 0 || e >= a.E) {
@@ -495,7 +496,7 @@ static int grouped_launch_mma(const GroupedArgs& a, int max_blocks, int tiles, i
   const int smem = kGSmem + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return FLINT_ERR_LAUNCH;
-  return launch(kern, dim3((unsigned)max_blocks, (unsigned)tiles), dim3(kGT), smem, stream, pdl, a);
+  return launch(kern, dim3((unsigned)tiles, (unsigned)max_blocks), dim3(kGT), smem, stream, pdl, a);
 }
 
 template <bool UP>
