@@ -183,46 +183,44 @@ __global__ void __launch_bounds__(kGT) moe_grouped_kernel(const GroupedArgs a) {
 }
 
 // ---- the same tile on the 5th-generation tensor cores (tcgen05: decoded weights and accumulator in tensor memory) ----
-// 8 consumer warps, a TMA warp and an MMA warp; K goes in stages of 128.
-//   producer (warp 8, one lane): the stage's code bytes of the CTA's 128 weight rows, 2 TMA boxes of 64 rows x 64 B
-//     with the 64-byte swizzle, into a 4-slot ring (full / empty mbarriers, bounded waits);
-//   consumer thread (warp w, lane l): weight row r = 32 (w % 4) + l, k half h = w / 4 of the stage.  It reads its 32
-//     code bytes (conflict-free under the swizzle) and its 4 E4M3 scales (loaded once per CTA into a padded array),
-//     decodes them to 32 f16 pairs and writes them with one tcgen05.st into its own tensor-memory lane (warp w owns
-//     lanes 32 (w % 4) ..): the MMA's A operand, three stage buffers of 64 columns.  The 64 routes' f16 activations
+// 8 consumer warps, a TMA warp and an MMA warp; K goes in stages of 64.
+//   TMA warp (one lane): the stage's code bytes of the CTA's 128 weight rows, 2 TMA boxes of 64 rows x 32 B with the
+//     32-byte swizzle, into a 4-slot ring (full / empty mbarriers, bounded waits);
+//   consumer thread (warp w, lane l): weight row r = 32 (w % 4) + l, k half h = w / 4 of the stage.  It reads its 16
+//     code bytes (conflict-free under the swizzle) and its 2 E4M3 scales (loaded once per CTA into a padded array),
+//     decodes them to 16 f16 pairs and writes them with one tcgen05.st into its own tensor-memory lane (warp w owns
+//     lanes 32 (w % 4) ..): the MMA's A operand, two stage buffers of 32 columns.  The 64 routes' f16 activations
 //     are copied by cp.async (one stage ahead, zeros for padding routes) into one of three shared-memory buffers in
-//     the K-major no-swizzle
-//     canonical layout (8-row x 16-byte core matrices: route group i at i * 2048 B, 16-k step s at s * 256 B, k half
-//     j at j * 128 B); lane l takes route l % 8 of an 8-route group, so each 8-lane store phase fills one 128-byte
-//     line;
-//     each warp then arrives on the buffer's ready mbarrier (no CTA-wide barrier per stage);
-//   MMA warp (warp 9, one lane): waits for the buffer's 8 arrivals, issues the stage's 8 tcgen05.mma kind::f16 (A
-//     from tensor memory, B from shared memory; M = 128 weight rows, N = 64 routes, K = 16) into the 128 x 64 fp32
-//     accumulator (tensor-memory columns 0..63) and commits them to the buffer's done mbarrier; a buffer is written
-//     again three stages later, after that barrier.
-// 256 tensor-memory columns and ~97 KB of shared memory per CTA: two CTAs per SM.  The epilogue reads the
-// accumulator with tcgen05.ld.  Each product is exact; the tensor core's fp32 sums run in their own order (within
-// the activation tolerance of the mma.sync tile and of the oracle).
-constexpr int kTcK = 128;                           // k per stage
+//     the K-major no-swizzle canonical layout (8-row x 16-byte core matrices: route group i at i * 1024 B, 16-k step
+//     s at s * 256 B, k half j at j * 128 B); lane l takes route l % 8 of an 8-route group, so each 8-lane phase of a
+//     16-byte copy fills one 128-byte line; each warp then arrives on the stage's ready mbarrier;
+//   MMA warp (one lane): waits for the stage's 8 arrivals, issues its 4 tcgen05.mma kind::f16 (A from tensor memory,
+//     B from shared memory; M = 128 weight rows, N = 64 routes, K = 16) into the 128 x 64 fp32 accumulator
+//     (tensor-memory columns 0..63) and commits them to the stage's done mbarrier.  One wait per stage, on the MMAs
+//     of two stages back, frees both the A buffer and the B buffer that the stage rewrites.
+// 128 tensor-memory columns, ~57 KB of shared memory and <= 64 registers per thread: three CTAs per SM.  The
+// epilogue reads the accumulator with tcgen05.ld.  Each product is exact; the tensor core's fp32 sums run in their
+// own order (within the activation tolerance of the mma.sync tile and of the oracle).
+constexpr int kTcK = 64;                            // k per stage
 constexpr int kTcSbo = (kTcK / 16) * 256;           // B: bytes between 8-route groups
-constexpr int kTcB = kGB * kTcK * 2;                // 16 KB activations per buffer
-constexpr int kTcNB = 3;                            // A (tensor memory) and B (shared memory) stage buffers
+constexpr int kTcB = kGB * kTcK * 2;                // 8 KB activations per buffer
+constexpr int kTcNB = 2;                            // A stage buffers (tensor memory); ready / done mbarriers
+constexpr int kTcNBB = 3;                           // B stage buffers (shared memory)
 constexpr int kTcNS = 4;                            // code ring slots
-constexpr int kTcSlot = kGRows * (kTcK / 2);        // 8 KB of codes per slot (two 4 KB boxes)
+constexpr int kTcSlot = kGRows * (kTcK / 2);        // 4 KB of codes per slot (two 2 KB boxes)
+constexpr int kTcACols = kTcK / 2;                  // tensor-memory columns of one A buffer (f16 pairs)
 constexpr int kTcXU = kGB * (kTcK / 8) / kGT;       // activation units of 8 k per thread per stage
 constexpr int kTcRS = kGB + 1;                      // fp32 stride of a result row (conflict-free column walks)
 constexpr int kTcThreads = kGT + 64;                // + the TMA warp and the MMA warp
-constexpr int kTcCols = 256;                        // tensor memory: accumulator 0..63, A buffers at 64, 128, 192
-static_assert(64 + 64 * kTcNB <= kTcCols, "A buffers fit the allocation");
-constexpr int kTcMinSmem = 80 * 1024;               // keeps a third CTA (and its tensor-memory request) off the SM
-static_assert(kTcXU == 4 && kGW == 8 && kGRows == 128, "lane maps: 8 routes x 4 units per warp, 2 threads per row");
-static_assert(kTcNS * kTcSlot + kTcNB * kTcB >= kGRows * kTcRS * 4, "result tile must fit over the ring and B buffers");
+constexpr int kTcCols = 128;                        // tensor memory: accumulator 0..63, A buffers at 64 and 96
+static_assert(64 + kTcACols * kTcNB <= kTcCols, "A buffers fit the allocation");
+static_assert(kTcXU == 2 && kGW == 8 && kGRows == 128, "lane maps: 8 routes x 4 units per warp, 2 threads per row");
+static_assert(kTcNS * kTcSlot + kTcNBB * kTcB >= kGRows * kTcRS * 4, "result tile must fit over the ring and B buffers");
 
 // scale bytes per row in shared memory: K/16 + 4 (an odd number of words, so 32 rows read in one wavefront)
 __host__ __device__ constexpr int tc_scale_stride(int K) { return K / 16 + 4; }
 static int tc_smem(int K) {
-  const int need = kTcNS * kTcSlot + kTcNB * kTcB + ((kGRows * tc_scale_stride(K) + 15) / 16) * 16;
-  return need > kTcMinSmem ? need : kTcMinSmem;
+  return kTcNS * kTcSlot + kTcNBB * kTcB + ((kGRows * tc_scale_stride(K) + 15) / 16) * 16;
 }
 
 // canonical-layout byte offset of 8 k (16 B) at route r, unit v (of kTcK / 8) within a B buffer
@@ -242,14 +240,11 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
 }
-__device__ __forceinline__ void tc_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+__device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
-      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
-      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
-      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
 }
 __device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
@@ -284,12 +279,12 @@ __device__ __forceinline__ void tc_tma_load(void* dst, const CUtensorMap* map, i
 }
 
 template <bool UP>
-__global__ void __launch_bounds__(kTcThreads, 2)
+__global__ void __launch_bounds__(kTcThreads, 3)
 moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* Bs = ring + kTcNS * kTcSlot;                           // buffer b at Bs + b kTcB
-  uint8_t* scales = Bs + kTcNB * kTcB;                            // [128 rows][tc_scale_stride(K)]
+  uint8_t* scales = Bs + kTcNBB * kTcB;                           // [128 rows][tc_scale_stride(K)]
   float* res = reinterpret_cast<float*>(ring);                    // [128 rows][kTcRS] after the last stage
   __shared__ int s_route[kGB], s_row[kGB];
   __shared__ uint32_t s_taddr;
@@ -336,7 +331,7 @@ moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs 
     fence_mbar_init();
     for (int ks = 0; ks < npre; ++ks) produce(ks);
   }
-  if (warp == 0) {                                                 // accumulator + three A buffers
+  if (warp == 0) {                                                 // accumulator + two A buffers
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_taddr)),
                  "r"((uint32_t)kTcCols)
                  : "memory");
@@ -347,7 +342,7 @@ moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs 
   const int l8 = lane & 7, c = lane >> 3;
   int xrow[kTcXU];
   auto fetch = [&](int ks) {                                       // one cp.async group per stage
-    uint8_t* Bb = Bs + (ks % kTcNB) * kTcB;
+    uint8_t* Bb = Bs + (ks % kTcNBB) * kTcB;
 #pragma unroll
     for (int j = 0; j < kTcXU; ++j) {
       const int v = 4 * ((warp + 8 * j) >> 3) + c;
@@ -396,10 +391,10 @@ moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs 
         const int b = ks % kTcNB;
         if (!mbar_wait(&s_ready[b], (unsigned)((ks / kTcNB) & 1), a.status)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint8_t* Bb = Bs + b * kTcB;
+        const uint8_t* Bb = Bs + (ks % kTcNBB) * kTcB;
 #pragma unroll 1
         for (int s16 = 0; s16 < kTcK / 16; ++s16)
-          tc_mma_f16_ta(tmem, tmem + (uint32_t)(64 + 64 * b + 8 * s16), tc_desc(Bb + s16 * 256), idesc,
+          tc_mma_f16_ta(tmem, tmem + (uint32_t)(64 + kTcACols * b + 8 * s16), tc_desc(Bb + s16 * 256), idesc,
                         (ks > 0 || s16 > 0) ? 1u : 0u);
         tc_commit(&s_mma[b]);
       }
@@ -408,7 +403,7 @@ moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs 
   } else {
     // ---- consumers ----
     // decode: row r = 32 (warp % 4) + lane, k half h = warp / 4
-    const int r = 32 * (warp & 3) + lane, h = warp >> 2, sw = (r >> 1) & 3;
+    const int r = 32 * (warp & 3) + lane, h = warp >> 2, sw = (r >> 2) & 1;
     const uint32_t a_lane = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
 #pragma unroll 1
     for (int ks = 0; ks < nks; ++ks) {
@@ -420,26 +415,25 @@ moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs 
       if (ks + 1 < nks) fetch(ks + 1);                             // the next stage's rows fly during this one
       else tc_cp_async_commit();                                   // (an empty group keeps the count uniform)
       if (ok && !mbar_wait(&s_full[slot], (unsigned)((ks / kTcNS) & 1), a.status)) ok = false;
-      const uint8_t* cs = ring + slot * kTcSlot + r * 64;
-      const uint4 q0 = *reinterpret_cast<const uint4*>(cs + (((2 * h) ^ sw) << 4));
-      const uint4 q1 = *reinterpret_cast<const uint4*>(cs + (((2 * h + 1) ^ sw) << 4));
-      const uint32_t s4 = *reinterpret_cast<const uint32_t*>(scales + r * sst + ks * (kTcK / 16) + 4 * h);
+      const uint8_t* cs = ring + slot * kTcSlot + r * 32;
+      const uint4 q0 = *reinterpret_cast<const uint4*>(cs + ((h ^ sw) << 4));
+      const uint32_t s2 = *reinterpret_cast<const unsigned short*>(scales + r * sst + ks * (kTcK / 16) + 2 * h);
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[slot]);                  // this warp is done with the slot
-      uint32_t d[32];
+      uint32_t d[16];
       {
-        const uint32_t s01 = e4m3x2_to_f16x2(s4 & 0xFFFFu), s23 = e4m3x2_to_f16x2(s4 >> 16);
-        const uint32_t wq[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        const uint32_t s01 = e4m3x2_to_f16x2(s2);
+        const uint32_t wq[4] = {q0.x, q0.y, q0.z, q0.w};
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {                              // 8 k per word; 16-k scale group q / 2
-          const uint32_t sg = q < 2 ? bcast_lo(s01) : q < 4 ? bcast_hi(s01) : q < 6 ? bcast_lo(s23) : bcast_hi(s23);
+        for (int q = 0; q < 4; ++q) {                              // 8 k per word; 16-k scale group q / 2
+          const uint32_t sg = q < 2 ? bcast_lo(s01) : bcast_hi(s01);
           uint32_t o[4];
           e2m1x8_to_f16x2(wq[q], o);
 #pragma unroll
           for (int i = 0; i < 4; ++i) d[4 * q + i] = hmul2(o[i], sg);
         }
       }
-      tc_st32(a_lane + (uint32_t)(64 + 64 * b + 32 * h), d);
+      tc_st16(a_lane + (uint32_t)(64 + kTcACols * b + 16 * h), d);
       tc_cp_async_wait1();                                         // this stage's rows are in place
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); // generic-proxy stores -> the tensor core
@@ -501,8 +495,8 @@ static int grouped_launch_mma(const GroupedArgs& a, int max_blocks, int tiles, i
 
 template <bool UP>
 static int grouped_launch_tc(const GroupedArgs& a, int max_blocks, int tiles, int pdl, void* stream) {
-  CUtensorMap mc;                                                  // codes [E N rows][K/2 B], boxes of 64 rows x 64 B
-  int rc = encode_u8_2d_sw64(&mc, a.W, (uint64_t)(a.K / 2), (uint64_t)a.E * a.N, (uint64_t)(a.K / 2), 64u);
+  CUtensorMap mc;                                                  // codes [E N rows][K/2 B], boxes of 64 rows x 32 B
+  int rc = encode_u8_2d_swz(&mc, a.W, (uint64_t)(a.K / 2), (uint64_t)a.E * a.N, (uint64_t)(a.K / 2), 64u, kTcK / 2);
   if (rc) return rc;
   auto kern = moe_grouped_tc_kernel<UP>;
   const int smem = tc_smem(a.K) + 1024;

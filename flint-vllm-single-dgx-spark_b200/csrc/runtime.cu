@@ -55,17 +55,22 @@ int encode_u8_2d(CUtensorMap* map, const void* base, uint64_t cols_bytes, uint64
   return r == CUDA_SUCCESS ? FLINT_OK : FLINT_ERR_ALIGN;
 }
 
-int encode_u8_2d_sw64(CUtensorMap* map, const void* base, uint64_t cols_bytes, uint64_t rows, uint64_t row_stride_bytes,
-                      uint32_t box_rows) {
+int encode_u8_2d_swz(CUtensorMap* map, const void* base, uint64_t cols_bytes, uint64_t rows, uint64_t row_stride_bytes,
+                     uint32_t box_rows, int swizzle_bytes) {
   auto fn = get_encode_fn();
   if (!fn) return FLINT_ERR_DEVICE;
   if (!aligned(base, 16) || row_stride_bytes % 16 != 0) return FLINT_ERR_ALIGN;
+  const CUtensorMapSwizzle swz = swizzle_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                 : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                 : swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                                        : CU_TENSOR_MAP_SWIZZLE_NONE;
+  if (swz == CU_TENSOR_MAP_SWIZZLE_NONE) return FLINT_ERR_ARGUMENT;
   cuuint64_t dims[2] = {cols_bytes, rows};
   cuuint64_t strides[1] = {row_stride_bytes};
-  cuuint32_t box[2] = {64u, box_rows};
+  cuuint32_t box[2] = {(cuuint32_t)swizzle_bytes, box_rows};
   cuuint32_t estr[2] = {1, 1};
   const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? FLINT_OK : FLINT_ERR_ALIGN;
 }

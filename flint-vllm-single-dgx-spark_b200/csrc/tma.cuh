@@ -185,10 +185,10 @@ __device__ __forceinline__ void l2_prefetch_share(const L2Prefetch& pf, int cta,
 // ---- host: tensor-map encoding through the driver entry point (no libcuda link needed) ----
 int encode_u8_2d(CUtensorMap* map, const void* base, uint64_t cols_bytes, uint64_t rows, uint64_t row_stride_bytes,
                  uint32_t box_cols, uint32_t box_rows, bool swizzle128);
-// u8 2-D map with the 64-byte swizzle (box rows of 64 B: 16-byte unit u of a row at byte address A lands at unit
-// u ^ ((A >> 7) & 3)).
-int encode_u8_2d_sw64(CUtensorMap* map, const void* base, uint64_t cols_bytes, uint64_t rows, uint64_t row_stride_bytes,
-                      uint32_t box_rows);
+// u8 2-D map, box rows of `swizzle_bytes` (32, 64 or 128) with that swizzle: 16-byte unit u of a row at byte
+// address A lands at unit u ^ ((A >> 7) & (swizzle_bytes / 16 - 1)).
+int encode_u8_2d_swz(CUtensorMap* map, const void* base, uint64_t cols_bytes, uint64_t rows, uint64_t row_stride_bytes,
+                     uint32_t box_rows, int swizzle_bytes);
 // bf16 4-D map (dims innermost first, strides in bytes for dims 1..3), 128-byte swizzle.
 int encode_bf16_4d(CUtensorMap* map, const void* base, const uint64_t dims[4], const uint64_t strides_bytes[3],
                    const uint32_t box[4]);
