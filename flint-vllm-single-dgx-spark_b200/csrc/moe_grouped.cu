@@ -198,7 +198,8 @@ __global__ void __launch_bounds__(kGT) moe_grouped_kernel(const GroupedArgs a) {
 //     B from shared memory; M = 128 weight rows, N = 64 routes, K = 16) into the 128 x 64 fp32 accumulator
 //     (tensor-memory columns 0..63) and commits them to the stage's done mbarrier.  One wait per stage, on the MMAs
 //     of two stages back, frees both the A buffer and the B buffer that the stage rewrites.
-// 128 tensor-memory columns, ~57 KB of shared memory and <= 64 registers per thread: three CTAs per SM.  The
+// 128 tensor-memory columns, ~57 KB of shared memory (gate/up; ~47 KB for down) and <= 64 (48) registers per
+// thread: three CTAs per SM (four for down).  The
 // epilogue reads the accumulator with tcgen05.ld.  Each product is exact; the tensor core's fp32 sums run in their
 // own order (within the activation tolerance of the mma.sync tile and of the oracle).
 constexpr int kTcK = 64;                            // k per stage
@@ -247,20 +248,17 @@ __device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t (&r)[16])
       "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
 }
-__device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
-      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr)
       : "memory");
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 // 16-byte global -> shared copy that fills zeros when `valid` is false (src-size 0: nothing is read)
 __device__ __forceinline__ void tc_cp_async16(void* dst, const void* src, bool valid) {
@@ -279,7 +277,7 @@ __device__ __forceinline__ void tc_tma_load(void* dst, const CUtensorMap* map, i
 }
 
 template <bool UP>
-__global__ void __launch_bounds__(kTcThreads, 3)
+__global__ void __launch_bounds__(kTcThreads, UP ? 3 : 4)      // down (K = I): 4 CTAs fit its smaller scale array
 moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -449,19 +447,23 @@ moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs 
   // accumulator -> registers: thread (warp, lane) holds weight row 32 (warp % 4) + lane for routes 32 (warp / 4) ..
   const float ge = a.g[e];
   if (warp < kGW) {
-    float v[32];
-    tc_ld32(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(32 * (warp >> 2)), v);
-    const int row = 32 * (warp & 3) + lane, col0 = 32 * (warp >> 2);
-    if (UP) {                                                      // gate and up rows meet through shared memory
+    const int row = 32 * (warp & 3) + lane;
+#pragma unroll 1
+    for (int half = 0; half < 2; ++half) {                         // 16 accumulator columns at a time
+      const int col0 = 32 * (warp >> 2) + 16 * half;
+      float v[16];
+      tc_ld16(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)col0, v);
+      if (UP) {                                                    // gate and up rows meet through shared memory
 #pragma unroll
-      for (int i = 0; i < 32; ++i) res[row * kTcRS + col0 + i] = ok ? v[i] : 0.f;
-    } else {                                                       // down: straight out, 64 B per warp store
+        for (int i = 0; i < 16; ++i) res[row * kTcRS + col0 + i] = ok ? v[i] : 0.f;
+      } else {                                                     // down: straight out, 64 B per warp store
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int route = s_route[col0 + i];
-        if (route >= 0)
-          a.out[(int64_t)route * a.ldo + tile * kGRows + row] =
-              __float2bfloat16_rn((ok ? v[i] : 0.f) * ldexpf(ge, -a.shift[route]));
+        for (int i = 0; i < 16; ++i) {
+          const int route = s_route[col0 + i];
+          if (route >= 0)
+            a.out[(int64_t)route * a.ldo + tile * kGRows + row] =
+                __float2bfloat16_rn((ok ? v[i] : 0.f) * ldexpf(ge, -a.shift[route]));
+        }
       }
     }
   }
