@@ -185,7 +185,7 @@ __global__ void __launch_bounds__(kGT) moe_grouped_kernel(const GroupedArgs a) {
 // ---- the same tile on the 5th-generation tensor cores (tcgen05: decoded weights and accumulator in tensor memory) ----
 // 8 consumer warps, a TMA warp and an MMA warp; K goes in stages of 64.
 //   TMA warp (one lane): the stage's code bytes of the CTA's 128 weight rows, 2 TMA boxes of 64 rows x 32 B with the
-//     32-byte swizzle, into a 4-slot ring (full / empty mbarriers, bounded waits);
+//     32-byte swizzle, into a 3-slot ring (full / empty mbarriers, bounded waits);
 //   consumer thread (warp w, lane l): weight row r = 32 (w % 4) + l, k half h = w / 4 of the stage.  It reads its 16
 //     code bytes (conflict-free under the swizzle) and its 2 E4M3 scales (loaded once per CTA into a padded array),
 //     decodes them to 16 f16 pairs and writes them with one tcgen05.st into its own tensor-memory lane (warp w owns
@@ -198,8 +198,8 @@ __global__ void __launch_bounds__(kGT) moe_grouped_kernel(const GroupedArgs a) {
 //     B from shared memory; M = 128 weight rows, N = 64 routes, K = 16) into the 128 x 64 fp32 accumulator
 //     (tensor-memory columns 0..63) and commits them to the stage's done mbarrier.  One wait per stage, on the MMAs
 //     of two stages back, frees both the A buffer and the B buffer that the stage rewrites.
-// 128 tensor-memory columns, ~57 KB of shared memory (gate/up; ~47 KB for down) and <= 64 (48) registers per
-// thread: three CTAs per SM (four for down).  The
+// 128 tensor-memory columns, <= 53 KB of shared memory (K <= 2048) and <= 48 registers per thread: four CTAs per
+// SM.  The
 // epilogue reads the accumulator with tcgen05.ld.  Each product is exact; the tensor core's fp32 sums run in their
 // own order (within the activation tolerance of the mma.sync tile and of the oracle).
 constexpr int kTcK = 64;                            // k per stage
@@ -207,7 +207,7 @@ constexpr int kTcSbo = (kTcK / 16) * 256;           // B: bytes between 8-route 
 constexpr int kTcB = kGB * kTcK * 2;                // 8 KB activations per buffer
 constexpr int kTcNB = 2;                            // A stage buffers (tensor memory); ready / done mbarriers
 constexpr int kTcNBB = 3;                           // B stage buffers (shared memory)
-constexpr int kTcNS = 4;                            // code ring slots
+constexpr int kTcNS = 3;                            // code ring slots
 constexpr int kTcSlot = kGRows * (kTcK / 2);        // 4 KB of codes per slot (two 2 KB boxes)
 constexpr int kTcACols = kTcK / 2;                  // tensor-memory columns of one A buffer (f16 pairs)
 constexpr int kTcXU = kGB * (kTcK / 8) / kGT;       // activation units of 8 k per thread per stage
@@ -277,7 +277,7 @@ __device__ __forceinline__ void tc_tma_load(void* dst, const CUtensorMap* map, i
 }
 
 template <bool UP>
-__global__ void __launch_bounds__(kTcThreads, UP ? 3 : 4)      // down (K = I): 4 CTAs fit its smaller scale array
+__global__ void __launch_bounds__(kTcThreads, 4)
 moe_grouped_tc_kernel(const __grid_constant__ CUtensorMap mc, const GroupedArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
