@@ -31,26 +31,53 @@ constexpr int kGSmem = kGRows * 128 + kGRows * 16 + kGB * kGXS * 2;   // codes +
                                                                       // results [128][64] at the end)
 static_assert(kGB * kGXS * 2 >= kGRows * kGB * 4, "result tile must fit over the activations");
 
-// one CTA per row: f16(x * 2^s), s from the row's largest |x| (the decode kernels' staging rule), unpermuted
-__global__ void __launch_bounds__(256) rows_to_f16_kernel(const bf16* __restrict__ src, int64_t ld, int K,
+// one warp per row: f16(x * 2^s), s from the row's largest |x| (the decode kernels' staging rule), unpermuted.
+// Two passes over the row (the second from L1 / L2), 16-byte accesses when the row and K allow them.
+__global__ void __launch_bounds__(256) rows_to_f16_kernel(const bf16* __restrict__ src, int64_t ld, int rows, int K,
                                                           __half* __restrict__ dst, int* __restrict__ shift) {
-  __shared__ float red[8];
   pdl_wait();
-  const int r = blockIdx.x, tid = threadIdx.x;
-  const bf16* row = src + (int64_t)r * ld;
-  float mx = 0.f;
-  for (int k = tid; k < K; k += 256) mx = fmaxf(mx, fabsf(__bfloat162float(row[k])));
+  const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (r < rows) {
+    const bf16* row = src + (int64_t)r * ld;
+    __half* out = dst + (int64_t)r * K;
+    const bool vec = (K % 8) == 0 && (reinterpret_cast<uintptr_t>(row) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+    float mx = 0.f;
+    if (vec) {
+      for (int k = lane * 8; k < K; k += 256) {
+        const uint4 u = *reinterpret_cast<const uint4*>(row + k);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if ((tid & 31) == 0) red[tid >> 5] = mx;
-  __syncthreads();
-  mx = red[0];
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+          mx = fmaxf(mx, fmaxf(fabsf(f.x), fabsf(f.y)));
+        }
+      }
+    } else {
+      for (int k = lane; k < K; k += 32) mx = fmaxf(mx, fabsf(__bfloat162float(row[k])));
+    }
 #pragma unroll
-  for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red[w]);
-  int s = 0;
-  if (mx > 0.f && !(mx != mx) && mx <= 3.0e38f) s = 14 - ((int)((__float_as_uint(mx) >> 23) & 0xFF) - 127);
-  if (tid == 0) shift[r] = s;
-  for (int k = tid; k < K; k += 256) dst[(int64_t)r * K + k] = __float2half_rn(scale_pow2(__bfloat162float(row[k]), s));
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    int s = 0;
+    if (mx > 0.f && !(mx != mx) && mx <= 3.0e38f) s = 14 - ((int)((__float_as_uint(mx) >> 23) & 0xFF) - 127);
+    if (lane == 0) shift[r] = s;
+    if (vec) {
+      for (int k = lane * 8; k < K; k += 256) {
+        const uint4 u = *reinterpret_cast<const uint4*>(row + k);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+        uint32_t h[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+          const __half2 v = __floats2half2_rn(scale_pow2(f.x, s), scale_pow2(f.y, s));
+          h[i] = *reinterpret_cast<const uint32_t*>(&v);
+        }
+        *reinterpret_cast<uint4*>(out + k) = make_uint4(h[0], h[1], h[2], h[3]);
+      }
+    } else {
+      for (int k = lane; k < K; k += 32) out[k] = __float2half_rn(scale_pow2(__bfloat162float(row[k]), s));
+    }
+  }
   pdl_trigger();
 }
 
@@ -515,8 +542,8 @@ extern "C" int flint_rows_to_f16(const void* src, int64_t ld, int64_t rows, int6
                                  int pdl, void* stream) {
   if (!src || !dst || !shift) return FLINT_ERR_ARGUMENT;
   if (rows < 1 || rows > (1 << 30) || K < 1 || ld < K) return FLINT_ERR_SHAPE;
-  return launch(rows_to_f16_kernel, dim3((unsigned)rows), dim3(256), 0, stream, pdl, (const bf16*)src, ld, (int)K,
-                (__half*)dst, (int*)shift);
+  return launch(rows_to_f16_kernel, dim3((unsigned)((rows + 7) / 8)), dim3(256), 0, stream, pdl, (const bf16*)src, ld,
+                (int)rows, (int)K, (__half*)dst, (int*)shift);
 }
 
 static int grouped_entry(bool up, int tc, const void* xh, const int32_t* shift, const int32_t* sorted_ids,

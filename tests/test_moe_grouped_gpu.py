@@ -103,3 +103,38 @@ def test_grouped_moe_tcgen05_matches_mma_sync_and_oracle(fb, cfg, T):
     out_tc2 = fm.grouped_moe(x, ids_d, tw_d, w, tensor_cores=True)
     torch.cuda.synchronize()
     np.testing.assert_array_equal(host(out_tc2), host(out_tc))
+
+
+def _rows_to_f16_ref(x):
+    """The staging rule restated: s = 14 - floor(log2(max |x|)), or 0 when the row's max |x| is 0 or above 3.0e38;
+    out = f16(x * 2^s) with one rounding (round to nearest even)."""
+    x = x.astype(np.float64)
+    mx = np.abs(x).max(axis=1)
+    _, e = np.frexp(mx)                                     # mx = m 2^e, m in [0.5, 1)
+    s = np.where((mx > 0) & (mx <= np.float64(np.float32(3.0e38))), 15 - e, 0).astype(np.int32)
+    with np.errstate(over="ignore"):
+        return (x * np.exp2(s)[:, None]).astype(np.float16), s
+
+
+@needs_cuda
+@pytest.mark.parametrize("K,ld_pad", [(768, 0), (2048, 0), (768, 8), (40, 0), (2048, 3)],
+                         ids=["768", "2048", "768_strided", "40_scalar", "2048_unaligned"])
+def test_rows_to_f16_is_the_exact_staging_rule(fb, K, ld_pad):
+    """flint_rows_to_f16 bit for bit against the rule, on rows of very different magnitudes (zero rows included),
+    through the 16-byte path and the scalar one (K not a multiple of 8, or rows off 16-byte alignment)."""
+    rng = np.random.default_rng(K + ld_pad)
+    n = 203
+    mags = np.exp2(rng.integers(-60, 60, size=n)).astype(np.float32)
+    x = bf16(rng, (n, K + ld_pad)) * mags[:, None]
+    x[7] = 0.0
+    x[11, :] = 0.0
+    x[11, K // 2] = -3.0e38 if K > 40 else 1.0
+    x = np.asarray(x, dtype=np.float32)
+    xd = dev_bf16(x)[:, :K]                                 # a strided view when ld_pad > 0
+    dst = torch.empty((n, K), dtype=torch.float16, device="cuda")
+    sh = torch.empty((n,), dtype=torch.int32, device="cuda")
+    torch.ops.flint_b200.rows_to_f16(xd, dst, sh)
+    torch.cuda.synchronize()
+    want, s = _rows_to_f16_ref(host(xd))
+    np.testing.assert_array_equal(sh.cpu().numpy(), s)
+    np.testing.assert_array_equal(dst.cpu().numpy().view(np.uint16), want.view(np.uint16))
