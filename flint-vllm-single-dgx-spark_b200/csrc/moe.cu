@@ -349,8 +349,11 @@ moe_down_kernel(const __grid_constant__ CUtensorMap mc, const __grid_constant__ 
 }
 
 // ------------------------------------------------------------------------------------------------------------
-// Deterministic moe_align_block_size (fast/patch_align.py:11-30): one CTA of 1024 threads, routes processed in
-// chunks of 1024; ranks inside a chunk come from warp match masks plus a per-warp, per-expert exclusive scan.
+// Deterministic moe_align_block_size (fast/patch_align.py:11-30): one CTA of 1024 threads.  Warp w owns the w-th
+// of 32 contiguous route segments: it counts its segment per expert (warp match masks), one exclusive scan over the
+// warps per expert gives each warp its start within every expert's run, and each warp then places its segment
+// 32 routes at a time with no block barrier.  A route's slot is its rank among the routes of its expert in index
+// order, as in the reference.
 // ------------------------------------------------------------------------------------------------------------
 constexpr int kAlignThreads = 1024;
 
@@ -360,18 +363,25 @@ moe_align_kernel(const int* __restrict__ topk_ids, int n, int E, int B, int* __r
   extern __shared__ int sm[];
   int* cnt = sm;                    // [E]
   int* pad_end = cnt + E;           // [E]
-  int* offset = pad_end + E;        // [E] running count placed so far
-  int* wc = offset + E;             // [32][E] per-warp counts of the current chunk (then exclusive prefix)
+  int* wc = pad_end + E;            // [32][E] per-warp counts of its segment (then its running start)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   pdl_wait();
-  for (int e = tid; e < E; e += kAlignThreads) { cnt[e] = 0; offset[e] = 0; }
+  for (int e = tid; e < E; e += kAlignThreads) cnt[e] = 0;
   for (int i = tid; i < 32 * E; i += kAlignThreads) wc[i] = 0;
   __syncthreads();
   int bad = 0;
-  for (int r = tid; r < n; r += kAlignThreads) {
-    const int e = topk_ids[r];
-    if (e < 0 || e >= E) { bad = 1; continue; }
-    atomicAdd(&cnt[e], 1);
+  for (int base = 0; base < n; base += 4 * kAlignThreads) {      // 4 loads in flight per thread
+    int ev[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int r = base + q * kAlignThreads + tid;
+      ev[q] = r < n ? topk_ids[r] : 0;
+      if (r < n && (ev[q] < 0 || ev[q] >= E)) { bad = 1; ev[q] = -1; }
+      if (r >= n) ev[q] = -1;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (ev[q] >= 0) atomicAdd(&cnt[ev[q]], 1);
   }
   if (bad) atomicOr(status, 1);
   __syncthreads();
@@ -394,33 +404,53 @@ moe_align_kernel(const int* __restrict__ topk_ids, int n, int E, int B, int* __r
     }
     expert_ids[blk] = lo >= E ? -1 : lo;
   }
-  for (int base = 0; base < n; base += kAlignThreads) {
-    const int r = base + tid;
-    int e = r < n ? topk_ids[r] : -1;
-    if (e >= E) e = -1;
-    const unsigned peers = __match_any_sync(0xffffffffu, e);
-    const int rank_w = __popc(peers & ((1u << lane) - 1u));
-    if (e >= 0 && rank_w == 0) wc[warp * E + e] = __popc(peers);
-    __syncthreads();
-    for (int ee = tid; ee < E; ee += kAlignThreads) {          // exclusive scan over warps, chunk total to offset
-      int acc = 0;
-      for (int w = 0; w < 32; ++w) {
-        const int c = wc[w * E + ee];
-        wc[w * E + ee] = acc;
-        acc += c;
+  const int seg = (n + 31) / 32, r0 = warp * seg, r1 = min(n, r0 + seg);
+  int* mine = wc + warp * E;                     // this warp's counts, then its running start per expert
+  auto load4 = [&](int base, int (&ev)[4]) {    // 4 x 32 routes of the segment, loads in flight together
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int r = base + 32 * q + lane;
+      ev[q] = r < r1 ? topk_ids[r] : -1;
+      if (ev[q] >= E) ev[q] = -1;
+    }
+  };
+  for (int base = r0; base < r1; base += 128) {  // pass 1: per-warp counts
+    int ev[4];
+    load4(base, ev);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int e = ev[q];
+      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      if (e >= 0 && __popc(peers & ((1u << lane) - 1u)) == 0) mine[e] += __popc(peers);
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  for (int ee = tid; ee < E; ee += kAlignThreads) {              // exclusive scan over the warps, per expert
+    int acc = ee == 0 ? 0 : pad_end[ee - 1];
+    for (int w = 0; w < 32; ++w) {
+      const int c = wc[w * E + ee];
+      wc[w * E + ee] = acc;
+      acc += c;
+    }
+  }
+  __syncthreads();
+  for (int base = r0; base < r1; base += 128) {  // pass 2: placement, in index order within the segment
+    int ev[4];
+    load4(base, ev);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int e = ev[q], r = base + 32 * q + lane;
+      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      const int rank = __popc(peers & ((1u << lane) - 1u));
+      if (e >= 0) {
+        const int pos = mine[e] + rank;
+        if (pos < n_sorted) sorted_ids[pos] = r; else atomicOr(status, 1);
       }
-      cnt[ee] = acc;                             // reuse: chunk total of expert ee
+      __syncwarp();
+      if (e >= 0 && rank == 0) mine[e] += __popc(peers);
+      __syncwarp();
     }
-    __syncthreads();
-    if (e >= 0) {
-      const int start = e == 0 ? 0 : pad_end[e - 1];
-      const int pos = start + offset[e] + wc[warp * E + e] + rank_w;
-      if (pos < n_sorted) sorted_ids[pos] = r; else atomicOr(status, 1);
-    }
-    __syncthreads();
-    for (int ee = tid; ee < E; ee += kAlignThreads) offset[ee] += cnt[ee];
-    for (int i = tid; i < 32 * E; i += kAlignThreads) wc[i] = 0;
-    __syncthreads();
   }
   pdl_trigger();
 }
@@ -559,7 +589,7 @@ extern "C" int flint_moe_align(const int32_t* topk_ids, int64_t numel, int64_t n
   int64_t need = numel + num_experts * (block_size - 1);
   if (numel < num_experts && numel * block_size < need) need = numel * block_size;
   if (n_sorted < need || n_blocks < (need + block_size - 1) / block_size) return FLINT_ERR_SHAPE;
-  const size_t smem = (size_t)(3 + 32) * num_experts * sizeof(int);
+  const size_t smem = (size_t)(2 + 32) * num_experts * sizeof(int);
   if (smem > 227 * 1024) return FLINT_ERR_SHAPE;
   if (cudaFuncSetAttribute(moe_align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return FLINT_ERR_LAUNCH;
