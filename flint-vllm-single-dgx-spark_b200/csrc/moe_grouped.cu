@@ -1,16 +1,17 @@
 // Prefill-side grouped MoE (replaces the Flint PR's FlashInfer grouped GEMMs for prompts, grouped_moe at
 // patch:4093-4212): the routes of a prompt, grouped by expert in blocks of 64 by the deterministic align
 // (flint_moe_align), run through the NVFP4 gate/up + SwiGLU and down projections with each decoded weight fragment
-// reused across the block's 64 routes (8 mma.sync n-groups per decoded A fragment; the decode kernels use it for
-// at most 8 tokens).
+// reused across the block's 64 routes (the decode kernels use it for at most 8 tokens).  Two tile forms, selected
+// by the entry points' tensor_cores argument: tcgen05 (decoded weights and accumulator in tensor memory, further
+// below; the faster one) and mma.sync (8 n-groups per decoded A fragment, described here).
 //
 //   flint_rows_to_f16      any bf16 rows -> f16 rows scaled by the decode kernels' per-row power of two (exact)
 //   flint_moe_grouped_up   act[route] = bf16(silu(g) * u), g / u = (xh[token] . W13[e] rows) * g13[e] * 2^-shift
 //   flint_moe_grouped_down y[route]   = bf16((ah[route] . W2[e] rows) * g2[e] * 2^-shift)
 // then flint_moe_combine over the prompt's tokens gives out[t] = bf16(sum_s tw[t][s] y[t topk + s]) in slot order.
 //
-// CTA = (align block of 64 routes, 128 weight rows: 64 gate + 64 up rows of one 64-column slice of the
-// intermediate, or 128 down rows); 8 warps, each 16 weight rows x 64 routes.  K goes in stages of 256: the
+// mma.sync form: CTA = (align block of 64 routes, 128 weight rows: 64 gate + 64 up rows of one 64-column slice of
+// the intermediate, or 128 down rows); 8 warps, each 16 weight rows x 64 routes.  K goes in stages of 256: the
 // stage's codes (128 B per row, 16-byte units swizzled by row as the decode kernels' TMA boxes are), scales and the
 // 64 routes' f16 activations are copied to shared memory, then each warp decodes its A fragments once per 16 k and
 // issues one m16n8k16 MMA per group of 8 routes.  Products are exact in f16 (e2m1 x e4m3 x the rescaled activation),
